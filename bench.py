@@ -1,0 +1,349 @@
+"""bench.py — the synthetic-encoder throughput of config 2 on 1..8 B200, plus the dominant kernel's
+roofline, the reference CPU path timed on this host's cores, and the reference arm.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl e2cuda|reference]
+    python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 bench.py --gpus N ...
+
+One step = one pass of the 24-layer synthetic encoder (hidden 768, 3 q heads /
+1 KV head of 256, FFN 1152, int8 token table [262144][768], dense 768->3072->768, L2) over a batch of
+64 sequences x 512 tokens per GPU (weak scaling: every rank embeds its own batch), followed, for
+N > 1, by the single NCCL all-gather of the pooled embeddings to every rank.
+Inputs are device-resident token ids ("value"); "e2e" drives the same pass through the C ABI's
+host-buffer entry point (pinned ids in, embeddings out, copies inside the timed region). Weights are
+random-init and seeded, token ids uniform in [2, 262144): there is no checkpoint or dataset.
+"""
+from __future__ import annotations
+
+import argparse
+import importlib.util
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+METRIC = "encoder embeddings/sec (config-2 synthetic encoder, W8A8 int8 GEMMs)"
+UNIT = "embeddings/s"
+BATCH, SEQ = 64, 512
+
+
+def load_pkg():
+    if "e2c_b200" in sys.modules:
+        return sys.modules["e2c_b200"]
+    pkg = ROOT / "e2.c_b200"
+    spec = importlib.util.spec_from_file_location("e2c_b200", pkg / "__init__.py", submodule_search_locations=[str(pkg)])
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules["e2c_b200"] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"], "src": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "src": "fallback"}
+
+
+# ------------------------------------------------------------------------------------ clocks
+class ClockSampler:
+    """nvidia-smi sampled every 200 ms while the timed region runs (read-only queries)."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ------------------------------------------------------------------------------------ distributed
+def dist_setup(n_gpus: int):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1 or n_gpus > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=None)
+        return dist, rank, world, local
+    return None, 0, 1, 0
+
+
+def max_over_ranks(dist, value: float, device) -> float:
+    if dist is None:
+        return value
+    import torch
+
+    t = torch.tensor([value], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ------------------------------------------------------------------------------------ reference arm
+def cpu_reference(seqs: int, seq_len: int, steps: int, warmup: int, weights, rng, budget_s: float | None = None):
+    """Times the reference's own CPU int8 path (the e2.c kernels built from source, driven by the
+    oracle's encoder composition over the reference thread pool) on `seqs` sequences per step.
+    Returns (embeddings/s, info)."""
+    sys.path.insert(0, str(ROOT))
+    from oracle import oracle_ffi as of
+
+    kind = "reference" if of.mux() is not None else "port"
+    nthreads = 0
+    if kind == "reference":
+        nthreads = of.mux().e2refmux_init(str(of.REF_DIR).encode(), 0)
+    ids = weights_ids = None
+    times = []
+    done = 0
+    t_start = time.perf_counter()
+    for i in range(warmup + steps):
+        weights_ids = rng.integers(2, weights.cfg.vocab, size=(seqs, seq_len), dtype=np.int32)
+        t0 = time.perf_counter()
+        of.encoder_forward(kind, weights, weights_ids)
+        dt = time.perf_counter() - t0
+        if i >= warmup:
+            times.append(dt)
+            done += seqs
+        if budget_s is not None and time.perf_counter() - t_start > budget_s and len(times) >= 1:
+            break
+    total = sum(times)
+    info = {"kind": kind, "cores": nthreads if kind == "reference" else 1,
+            "sample": f"{len(times)} x {seqs} sequences x {seq_len} tokens of the 24-layer encoder "
+                      f"({'reference e2.c AVX512-VNNI kernels + thread pool' if kind == 'reference' else 'plain-C port'}), "
+                      f"host {os.cpu_count()} logical CPUs"}
+    return done / total, info
+
+
+# ------------------------------------------------------------------------------------ main arm
+def main() -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="e2cuda", choices=["e2cuda", "reference"])
+    ap.add_argument("--layers", type=int, default=24, help=argparse.SUPPRESS)  # debugging only; headline uses 24
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+
+    import torch
+
+    dist, rank, world, local = dist_setup(args.gpus)
+    n = world
+    load_pkg()
+    import e2c_b200.synthetic as syn
+
+    cfg = syn.EncoderConfig(n_layers=args.layers, max_seq=SEQ)
+    config = {"workload": f"config 2: synthetic encoder, {cfg.n_layers} layers, hidden {cfg.hidden}, "
+                          f"{cfg.n_heads}q/{cfg.n_kv_heads}kv heads x {cfg.head_dim}, ffn {cfg.ffn}, int8 table "
+                          f"[{cfg.vocab}][{cfg.hidden}], head {cfg.hidden}->{cfg.dense_hidden}->{cfg.out_dim}",
+              "batch_per_gpu": BATCH, "seq_len": SEQ, "global_batch": BATCH * n, "act_scales": "per-token",
+              "parallelism": f"dp{n} (batch-sharded, weights replicated, one all-gather)",
+              "l2": "inputs larger than L2: each step streams ~0.1 GB of layer weights and ~0.5 GB of activations"}
+
+    if args.impl == "reference":
+        if rank != 0:
+            if dist:
+                dist.destroy_process_group()
+            return 0
+        w = syn.encoder_weights(cfg)
+        rng = np.random.default_rng(7)
+        seqs = 2
+        v, info = cpu_reference(seqs, SEQ, args.steps, args.warmup, w, rng)
+        line = {"metric": METRIC, "value": v, "unit": UNIT, "n_gpus": n, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": 1e3 * seqs / v, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "int8", "data": "synthetic (seeded random-init weights, uniform token ids)", "config": config,
+                "impl": "reference", "cpu_baseline": dict(info, value=v, unit=UNIT),
+                "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line))
+        if dist:
+            dist.destroy_process_group()
+        return 0
+
+    e2c = load_pkg()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    w = syn.encoder_weights(cfg)
+    desc, keep = syn.fill_desc(w, e2c.Q8W, e2c.EncoderDesc)
+    enc = e2c.Encoder(desc, keep, BATCH * SEQ)
+    rng = np.random.default_rng(1000 + rank)
+    ids_host = syn.token_batch(rng, BATCH, SEQ, cfg.vocab)
+    ids = torch.from_numpy(ids_host).to(dev)
+    out = torch.empty((BATCH, cfg.out_dim), dtype=torch.float32, device=dev)
+    gathered = torch.empty((n * BATCH, cfg.out_dim), dtype=torch.float32, device=dev) if dist else None
+    stream = torch.cuda.Stream(device=dev)
+
+    def step():
+        enc.embed_batch_device(ids, None, out, stream)
+        if dist:
+            with torch.cuda.stream(stream):
+                dist.all_gather_into_tensor(gathered, out)
+
+    with torch.cuda.stream(stream):
+        for _ in range(max(args.warmup, 3)):
+            step()
+    e2c.check(stream)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        with torch.cuda.stream(stream):
+            ev0.record(stream)
+            for _ in range(args.steps):
+                step()
+            ev1.record(stream)
+        torch.cuda.synchronize()
+    e2c.check(stream)
+    ms = ev0.elapsed_time(ev1)
+    ms = max_over_ranks(dist, ms, dev)
+    value = n * BATCH * args.steps / (ms / 1e3)
+    _, kernels, _ = enc.stats()
+
+    # e2e: the host-buffer C-ABI entry point, pinned ids in, embeddings out, copies in the region
+    ids_pin = torch.from_numpy(ids_host).pin_memory()
+    out_pin = torch.empty((BATCH, cfg.out_dim), dtype=torch.float32).pin_memory()
+    for _ in range(2):
+        enc.embed_batch_into(ids_pin, None, out_pin)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        enc.embed_batch_into(ids_pin, None, out_pin)
+    e2e_ms = (time.perf_counter() - t0) * 1e3
+    e2e_ms = max_over_ranks(dist, e2e_ms, dev)
+    e2e = n * BATCH * args.steps / (e2e_ms / 1e3)
+
+    # the dominant kernel in isolation: the gate|up GEMM of one layer (M = 32768, N = 2304, K = 768)
+    roof = None
+    if rank == 0:
+        roof = gate_up_roofline(e2c, syn, w, dev, stream)
+    cpu = None
+    if rank == 0 and not args.no_cpu_baseline:
+        try:
+            v, info = cpu_reference(2, SEQ, 3, 1, w, np.random.default_rng(9), budget_s=30.0)
+            cpu = dict(info, value=v, unit=UNIT)
+        except Exception as ex:  # the baseline is reported, not required
+            cpu = {"value": None, "unit": UNIT, "error": str(ex)[:200]}
+
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": n, "steps": args.steps,
+                "warmup": max(args.warmup, 3), "ms_per_step": ms / args.steps, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+                "data": "synthetic (seeded random-init int8 weights, uniform token ids)", "config": config,
+                "clocks": clk.summary(),
+                "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": int(ids_pin.numel() * 4),
+                        "d2h_bytes_per_step": int(out_pin.numel() * 4)},
+                "gpu_launches": int(kernels * args.steps), "roofline": roof, "cpu_baseline": cpu}
+        print(json.dumps(line))
+    enc.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def gate_up_roofline(e2c, syn, w, dev, stream) -> dict:
+    """CUDA-event timing of the gate|up GEMM with its GELU-gate epilogue at the encoder's shape,
+    against 2x the measured bf16 tensor peak (B200 dense int8 = 2x dense bf16)."""
+    import torch
+
+    M, D, I = BATCH * SEQ, w.cfg.hidden, w.cfg.ffn
+    lay = w.layers[0]
+    wi = np.empty((2 * I, D), np.int8)
+    si = np.empty(2 * I, np.float32)
+    for t in range(I // 128):
+        wi[256 * t:256 * t + 128], si[256 * t:256 * t + 128] = lay["wg"].q[128 * t:128 * t + 128], lay["wg"].scale[128 * t:128 * t + 128]
+        wi[256 * t + 128:256 * t + 256] = lay["wu"].q[128 * t:128 * t + 128]
+        si[256 * t + 128:256 * t + 256] = lay["wu"].scale[128 * t:128 * t + 128]
+    W = e2c.Weight(w=wi, scale=si)
+    g = torch.Generator(device=dev).manual_seed(5)
+    qa = torch.randint(-127, 128, (M, D), dtype=torch.int8, device=dev, generator=g)
+    qs = torch.rand((M, 1), device=dev, generator=g) * 0.05 + 1e-3
+    h = torch.empty((M, I), dtype=torch.float32, device=dev)
+    a = e2c.gemm_args(W, qa, qs, M)
+    a.epi, a.y, a.ldy = e2c.EPI_GELU, h.data_ptr(), I
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)  # 256 MB > L2
+    times = []
+    with torch.cuda.stream(stream):
+        for i in range(13):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            e2c.gemm_raw(a, stream)
+            e1.record(stream)
+            e1.synchronize()
+            if i >= 3:
+                times.append(e0.elapsed_time(e1))
+    e2c.check(stream)
+    avg_ms = sum(times) / len(times)
+    ops = 2.0 * M * (2 * I) * D
+    p = peaks()
+    peak = 2.0 * p["bf16_tflops"]
+    achieved = ops / (avg_ms / 1e3) / 1e12
+    traffic = None
+    tf = ROOT / "profiles" / "traffic.json"
+    if tf.exists():
+        traffic = json.loads(tf.read_text()).get("gate_up_gemm_M32768")
+    return {"kernel": "k_gemm_i8<256,4,per-row,GELU> gate|up 32768x2304x768", "bound": "tensor",
+            "achieved": achieved, "peak": peak, "unit": "TOPS (int8)", "frac": achieved / peak,
+            "peak_src": f"2 x {p['src']} bf16 {p['bf16_tflops']} TFLOP/s (dense int8 rate = 2x bf16)",
+            "avg_ms": avg_ms, "algorithmic_bytes": M * D + 4 * M + 2 * I * D + 8 * I + 4 * M * I,
+            "traffic": traffic}
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,475 @@
+/* encoder_host.c — the synthetic encoder (config 2) over the e2cuda kernels: weights uploaded once,
+ * one device pass per chunk of whole sequences, replayed from a CUDA graph per shape.
+ *
+ * Layer recipe: e2.c src/text.c:939-961 without the PLE block; head: masked mean pool -> dense ->
+ * dense -> L2 (the config-2 head). Per layer, 9 kernels:
+ *
+ *   [prev tail] norm_add + norm_split + quant      (layer 0: embed gather + norm + quant)
+ *   GEMM q|k|v  -> per-head RMSNorm + RoPE -> bf16 Q, K, V^T     (epilogue, gemm_i8.cu)
+ *   attention   -> ctx fp32                                       (attention.cu)
+ *   quant ctx ; GEMM o_proj -> tmp
+ *   norm_add(post_attn) + norm_split(pre_ffn) + quant
+ *   GEMM gate|up -> GELU(g)*u (epilogue) ; quant h ; GEMM down -> tmp
+ *   norm_add(post_ffn) + norm_split(next input_ln) + quant   (last layer: final norm)
+ */
+#include <math.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+#include <time.h>
+
+#include "internal.h"
+
+#define MAX_GRAPHS 16
+
+typedef struct {
+    int B, S, has_valid;
+    cudaGraphExec_t exec;
+    int kernels;
+} graph_slot;
+
+struct e2cuda_encoder {
+    int L, D, H, Dh, I, V, DH, DO, max_seq, ablk, max_tokens;
+    float eps, attn_scale, embed_scale;
+    e2cuda_w8 *wqkv, *wo, *wgu, *wd;
+    e2cuda_w8 dense1, dense2;
+    int8_t *table;
+    float *table_scale;
+    float *norms; /* per layer: input, post_attn, pre_ffn, post_ffn [D] + q_norm, k_norm [Dh]; then final [D] */
+    float *rope_cos, *rope_sin;
+    /* workspace */
+    int32_t *ids;
+    uint8_t *valid;
+    float *out, *res, *tmp, *ctx, *h, *pooled, *h1;
+    int8_t *qa, *pq;
+    float *qs, *ps;
+    void *Q, *K, *Vt;
+    size_t vt_bytes;
+    int *status;
+    cudaStream_t stream;
+    float *host_out;
+    graph_slot graphs[MAX_GRAPHS];
+    int ngraphs;
+    long calls, kernels_last;
+    double last_ms;
+};
+
+static size_t norm_stride(const e2cuda_encoder *e) { return (size_t)4 * e->D + 2 * (size_t)e->Dh; }
+static float *nrm(const e2cuda_encoder *e, int l, int which) {
+    float *b = e->norms + (size_t)l * norm_stride(e);
+    return which < 4 ? b + (size_t)which * e->D : b + 4 * (size_t)e->D + (size_t)(which - 4) * e->Dh;
+}
+static float *final_norm(const e2cuda_encoder *e) { return e->norms + (size_t)e->L * norm_stride(e); }
+
+/* concatenate projections (rows) into one device weight */
+static int upload_concat(const e2cuda_q8w *const *parts, int nparts, e2cuda_w8 *out) {
+    int N = 0;
+    const int K = parts[0]->K;
+    for (int i = 0; i < nparts; i++) {
+        if (parts[i]->K != K) {
+            e2cu_err("encoder: projections to concatenate differ in K");
+            return -1;
+        }
+        N += parts[i]->N;
+    }
+    int8_t *w = malloc((size_t)N * K);
+    float *s = malloc(sizeof(float) * (size_t)N);
+    if (!w || !s) {
+        free(w);
+        free(s);
+        e2cu_err("encoder: out of host memory");
+        return -1;
+    }
+    int off = 0;
+    for (int i = 0; i < nparts; i++) {
+        e2cu_unpack_q8w(parts[i], w + (size_t)off * K, K);
+        memcpy(s + off, parts[i]->scale, sizeof(float) * parts[i]->N);
+        off += parts[i]->N;
+    }
+    const int rc = e2cuda_w8_from_int8(w, s, N, K, out);
+    free(w);
+    free(s);
+    return rc;
+}
+
+void e2cuda_encoder_destroy(e2cuda_encoder *e) {
+    if (!e) return;
+    for (int i = 0; i < e->ngraphs; i++) cudaGraphExecDestroy(e->graphs[i].exec);
+    for (int l = 0; l < e->L; l++) {
+        if (e->wqkv) e2cuda_w8_free(&e->wqkv[l]);
+        if (e->wo) e2cuda_w8_free(&e->wo[l]);
+        if (e->wgu) e2cuda_w8_free(&e->wgu[l]);
+        if (e->wd) e2cuda_w8_free(&e->wd[l]);
+    }
+    free(e->wqkv);
+    free(e->wo);
+    free(e->wgu);
+    free(e->wd);
+    e2cuda_w8_free(&e->dense1);
+    e2cuda_w8_free(&e->dense2);
+    void *dev[] = { e->table, e->table_scale, e->norms, e->rope_cos, e->rope_sin, e->ids, e->valid, e->out, e->res,
+                    e->tmp, e->ctx, e->h, e->pooled, e->h1, e->qa, e->pq, e->qs, e->ps, e->Q, e->K, e->Vt };
+    for (size_t i = 0; i < sizeof dev / sizeof dev[0]; i++)
+        if (dev[i]) cudaFree(dev[i]);
+    if (e->host_out) cudaFreeHost(e->host_out);
+    if (e->stream) cudaStreamDestroy(e->stream);
+    free(e);
+}
+
+#define DALLOC(ptr, bytes) e2cu_cuda(cudaMalloc((void **)&(ptr), (bytes)), "encoder alloc " #ptr)
+
+e2cuda_encoder *e2cuda_encoder_create(const e2cuda_encoder_desc *d, int max_tokens) {
+    if (!d || d->n_layers <= 0 || d->head_dim != 256 || d->n_kv_heads != 1 || d->hidden % 128 || d->hidden > 1024 ||
+        d->n_heads <= 0 || d->ffn % 128 || d->vocab <= 0 || d->max_seq <= 0 || max_tokens <= 0 || !d->table ||
+        !d->table_scale || d->dense_hidden % 128 || d->out_dim <= 0) {
+        e2cu_err("encoder_create: unsupported geometry (needs head_dim 256, one KV head, hidden and ffn multiples "
+                 "of 128, hidden <= 1024)");
+        return NULL;
+    }
+    const int ablk = d->ablk ? d->ablk : d->hidden;
+    if (ablk != d->hidden && ablk != 128) {
+        e2cu_err("encoder_create: ablk must be hidden (per token) or 128");
+        return NULL;
+    }
+    e2cuda_encoder *e = calloc(1, sizeof *e);
+    if (!e) {
+        e2cu_err("encoder_create: out of host memory");
+        return NULL;
+    }
+    e->L = d->n_layers;
+    e->D = d->hidden;
+    e->H = d->n_heads;
+    e->Dh = d->head_dim;
+    e->I = d->ffn;
+    e->V = d->vocab;
+    e->DH = d->dense_hidden;
+    e->DO = d->out_dim;
+    e->max_seq = d->max_seq;
+    e->ablk = ablk;
+    e->max_tokens = max_tokens;
+    e->eps = d->eps;
+    e->attn_scale = d->attn_scale;
+    e->embed_scale = d->embed_scale;
+    const int L = e->L, D = e->D, GD = e->H * e->Dh;
+    const size_t M = (size_t)max_tokens;
+
+    e->wqkv = calloc((size_t)L, sizeof(e2cuda_w8));
+    e->wo = calloc((size_t)L, sizeof(e2cuda_w8));
+    e->wgu = calloc((size_t)L, sizeof(e2cuda_w8));
+    e->wd = calloc((size_t)L, sizeof(e2cuda_w8));
+    if (!e->wqkv || !e->wo || !e->wgu || !e->wd) {
+        e2cu_err("encoder_create: out of host memory");
+        goto fail;
+    }
+    for (int l = 0; l < L; l++) {
+        const e2cuda_q8w *parts[3] = { &d->wq[l], &d->wk[l], &d->wv[l] };
+        if (d->wq[l].N != GD || d->wk[l].N != e->Dh || d->wv[l].N != e->Dh || d->wq[l].K != D || d->wo[l].N != D ||
+            d->wo[l].K != GD || d->wg[l].N != e->I || d->wd[l].K != e->I || d->wd[l].N != D) {
+            e2cu_err("encoder_create: layer %d projection shapes do not match the geometry", l);
+            goto fail;
+        }
+        if (upload_concat(parts, 3, &e->wqkv[l]) || e2cuda_w8_from_q8w(&d->wo[l], &e->wo[l]) ||
+            e2cu_upload_gate_up(&d->wg[l], &d->wu[l], &e->wgu[l]) || e2cuda_w8_from_q8w(&d->wd[l], &e->wd[l]))
+            goto fail;
+    }
+    if (d->dense1->K != D || d->dense1->N != e->DH || d->dense2->K != e->DH || d->dense2->N != e->DO) {
+        e2cu_err("encoder_create: head shapes do not match");
+        goto fail;
+    }
+    if (e2cuda_w8_from_q8w(d->dense1, &e->dense1) || e2cuda_w8_from_q8w(d->dense2, &e->dense2)) goto fail;
+
+    /* token table, norms, RoPE tables */
+    if (DALLOC(e->table, (size_t)e->V * D) || DALLOC(e->table_scale, sizeof(float) * (size_t)e->V) ||
+        e2cu_cuda(cudaMemcpy(e->table, d->table, (size_t)e->V * D, cudaMemcpyHostToDevice), "table upload") ||
+        e2cu_cuda(cudaMemcpy(e->table_scale, d->table_scale, sizeof(float) * e->V, cudaMemcpyHostToDevice),
+                  "table upload"))
+        goto fail;
+    {
+        const size_t nn = (size_t)L * norm_stride(e) + D;
+        float *hn = malloc(sizeof(float) * nn);
+        if (!hn) {
+            e2cu_err("encoder_create: out of host memory");
+            goto fail;
+        }
+        for (int l = 0; l < L; l++) {
+            float *b = hn + (size_t)l * norm_stride(e);
+            memcpy(b, d->input_ln[l], sizeof(float) * D);
+            memcpy(b + D, d->post_attn_ln[l], sizeof(float) * D);
+            memcpy(b + 2 * D, d->pre_ffn_ln[l], sizeof(float) * D);
+            memcpy(b + 3 * D, d->post_ffn_ln[l], sizeof(float) * D);
+            memcpy(b + 4 * D, d->q_norm[l], sizeof(float) * e->Dh);
+            memcpy(b + 4 * D + e->Dh, d->k_norm[l], sizeof(float) * e->Dh);
+        }
+        memcpy(hn + (size_t)L * norm_stride(e), d->final_norm, sizeof(float) * D);
+        const int rc = DALLOC(e->norms, sizeof(float) * nn) ||
+                       e2cu_cuda(cudaMemcpy(e->norms, hn, sizeof(float) * nn, cudaMemcpyHostToDevice), "norm upload");
+        free(hn);
+        if (rc) goto fail;
+    }
+    {
+        /* e2.c src/text.c:483-506: inv = 1/theta^(2i/D), angle = pos * inv; halves duplicated there,
+         * stored once here ([pos][Dh/2]) */
+        const int half = e->Dh / 2;
+        float *c = malloc(sizeof(float) * (size_t)e->max_seq * half), *s = malloc(sizeof(float) * (size_t)e->max_seq * half);
+        if (!c || !s) {
+            free(c);
+            free(s);
+            e2cu_err("encoder_create: out of host memory");
+            goto fail;
+        }
+        for (int p = 0; p < e->max_seq; p++)
+            for (int i = 0; i < half; i++) {
+                const float inv = 1.0f / powf(d->rope_theta, (float)(2 * i) / (float)e->Dh);
+                const float f = (float)p * inv;
+                c[(size_t)p * half + i] = cosf(f);
+                s[(size_t)p * half + i] = sinf(f);
+            }
+        const size_t nb = sizeof(float) * (size_t)e->max_seq * half;
+        const int rc = DALLOC(e->rope_cos, nb) || DALLOC(e->rope_sin, nb) ||
+                       e2cu_cuda(cudaMemcpy(e->rope_cos, c, nb, cudaMemcpyHostToDevice), "rope upload") ||
+                       e2cu_cuda(cudaMemcpy(e->rope_sin, s, nb, cudaMemcpyHostToDevice), "rope upload");
+        free(c);
+        free(s);
+        if (rc) goto fail;
+    }
+    /* workspace; the widest activation row is max(D, GD, I) */
+    {
+        int KQ = D > GD ? D : GD;
+        if (e->I > KQ) KQ = e->I;
+        const size_t MB = M; /* at most one sequence per token */
+        if (DALLOC(e->ids, sizeof(int32_t) * M) || DALLOC(e->valid, M) || DALLOC(e->res, sizeof(float) * M * D) ||
+            DALLOC(e->tmp, sizeof(float) * M * D) || DALLOC(e->ctx, sizeof(float) * M * GD) ||
+            DALLOC(e->h, sizeof(float) * M * e->I) || DALLOC(e->qa, M * (size_t)KQ) ||
+            DALLOC(e->qs, sizeof(float) * M * (size_t)(KQ / 128 + 1)) || DALLOC(e->Q, 2 * M * GD) ||
+            DALLOC(e->K, 2 * M * e->Dh) || DALLOC(e->out, sizeof(float) * MB * e->DO) ||
+            DALLOC(e->pooled, sizeof(float) * MB * D) || DALLOC(e->h1, sizeof(float) * MB * e->DH) ||
+            DALLOC(e->pq, MB * (size_t)(e->DH > D ? e->DH : D)) ||
+            DALLOC(e->ps, sizeof(float) * MB * (size_t)((e->DH > D ? e->DH : D) / 128 + 1)))
+            goto fail;
+    }
+    e->status = e2cu_status();
+    if (!e->status || e2cu_cuda(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking), "stream")) goto fail;
+    return e;
+fail:
+    e2cuda_encoder_destroy(e);
+    return NULL;
+}
+
+static int round8(int x) { return (x + 7) & ~7; }
+
+/* queue one pass over B sequences of S tokens already in e->ids / e->valid; returns kernels queued */
+static int encode(e2cuda_encoder *e, int B, int S, int has_valid, cudaStream_t st) {
+    const int M = B * S, D = e->D, GD = e->H * e->Dh, I = e->I, L = e->L;
+    const int ab_d = e->ablk == D ? D : 128, ab_gd = e->ablk == D ? GD : 128, ab_i = e->ablk == D ? I : 128;
+    const int ldvt = round8(S);
+    const uint8_t *valid = has_valid ? e->valid : NULL;
+    int n = 0;
+    if (e2cu_launch(e2c_embed_norm_quant(e->ids, e->table, e->table_scale, e->embed_scale, nrm(e, 0, 0), e->eps, e->res,
+                                         e->qa, e->qs, M, D, ab_d, e->V, e->status, st),
+                    "encoder embed"))
+        return -1;
+    n++;
+    e2c_gemm_args a;
+    for (int l = 0; l < L; l++) {
+        /* q|k|v with per-head RMSNorm + RoPE */
+        e2cu_gemm_args(&a, &e->wqkv[l], e->qa, e->qs, M, ab_d);
+        a.epi = E2C_EPI_QKV;
+        a.nq = e->H;
+        a.q_out = e->Q;
+        a.k_out = e->K;
+        a.vt_out = e->Vt;
+        a.ldvt = ldvt;
+        a.seq_len = S;
+        a.q_gamma = nrm(e, l, 4);
+        a.k_gamma = nrm(e, l, 5);
+        a.rope_cos = e->rope_cos;
+        a.rope_sin = e->rope_sin;
+        a.eps = e->eps;
+        if (e2cu_launch(e2c_gemm(&a, st), "encoder qkv")) return -1;
+        if (e2cu_launch(e2c_attention(e->Q, e->K, e->Vt, ldvt, valid, e->ctx, B, S, e->H, e->attn_scale, e->status, st),
+                        "encoder attention"))
+            return -1;
+        if (e2cu_launch(e2c_quantize(e->ctx, GD, e->qa, GD, e->qs, M, GD, ab_gd, -INFINITY, INFINITY, 0, st),
+                        "encoder ctx quant"))
+            return -1;
+        e2cu_gemm_args(&a, &e->wo[l], e->qa, e->qs, M, ab_gd);
+        a.epi = E2C_EPI_F32;
+        a.y = e->tmp;
+        a.ldy = D;
+        if (e2cu_launch(e2c_gemm(&a, st), "encoder o_proj")) return -1;
+        if (e2cu_launch(e2c_norm_add_norm_quant(e->tmp, e->res, nrm(e, l, 1), nrm(e, l, 2), NULL, e->eps, e->qa, e->qs, M,
+                                                D, ab_d, st),
+                        "encoder post-attention norms"))
+            return -1;
+        e2cu_gemm_args(&a, &e->wgu[l], e->qa, e->qs, M, ab_d);
+        a.epi = E2C_EPI_GELU;
+        a.y = e->h;
+        a.ldy = I;
+        if (e2cu_launch(e2c_gemm(&a, st), "encoder gate|up")) return -1;
+        if (e2cu_launch(e2c_quantize(e->h, I, e->qa, I, e->qs, M, I, ab_i, -INFINITY, INFINITY, 0, st),
+                        "encoder h quant"))
+            return -1;
+        e2cu_gemm_args(&a, &e->wd[l], e->qa, e->qs, M, ab_i);
+        a.epi = E2C_EPI_F32;
+        a.y = e->tmp;
+        a.ldy = D;
+        if (e2cu_launch(e2c_gemm(&a, st), "encoder down")) return -1;
+        const int last = l + 1 == L;
+        if (e2cu_launch(e2c_norm_add_norm_quant(e->tmp, e->res, nrm(e, l, 3), last ? NULL : nrm(e, l + 1, 0),
+                                                last ? final_norm(e) : NULL, e->eps, e->qa, e->qs, M, D, ab_d, st),
+                        "encoder post-ffn norms"))
+            return -1;
+        n += 9;
+    }
+    /* head */
+    const int ab_dh = e->ablk == D ? e->DH : 128;
+    if (e2cu_launch(e2c_meanpool(e->res, valid, e->pooled, B, S, D, st), "encoder pool") ||
+        e2cu_launch(e2c_quantize(e->pooled, D, e->pq, D, e->ps, B, D, ab_d, -INFINITY, INFINITY, 0, st), "encoder head quant"))
+        return -1;
+    e2cu_gemm_args(&a, &e->dense1, e->pq, e->ps, B, ab_d);
+    a.y = e->h1;
+    a.ldy = e->DH;
+    if (e2cu_launch(e2c_gemm(&a, st), "encoder dense1") ||
+        e2cu_launch(e2c_quantize(e->h1, e->DH, e->pq, e->DH, e->ps, B, e->DH, ab_dh, -INFINITY, INFINITY, 0, st),
+                    "encoder head quant"))
+        return -1;
+    e2cu_gemm_args(&a, &e->dense2, e->pq, e->ps, B, ab_dh);
+    a.y = e->out;
+    a.ldy = e->DO;
+    if (e2cu_launch(e2c_gemm(&a, st), "encoder dense2") ||
+        e2cu_launch(e2c_l2norm_rows(e->out, valid, B, S, e->DO, st), "encoder l2"))
+        return -1;
+    return n + 6;
+}
+
+static int ensure_vt(e2cuda_encoder *e, int B, int S) {
+    const size_t need = (size_t)B * 256 * round8(S) * 2;
+    if (need <= e->vt_bytes) return 0;
+    /* captured graphs hold the old buffer */
+    for (int i = 0; i < e->ngraphs; i++) cudaGraphExecDestroy(e->graphs[i].exec);
+    e->ngraphs = 0;
+    if (e->Vt) cudaFree(e->Vt);
+    e->Vt = NULL;
+    e->vt_bytes = 0;
+    if (e2cu_cuda(cudaMalloc(&e->Vt, need), "encoder V^T alloc")) return -1;
+    e->vt_bytes = need;
+    return 0;
+}
+
+/* one pass, inputs already in e->ids / e->valid, result in e->out */
+static int pass(e2cuda_encoder *e, int B, int S, int has_valid, cudaStream_t st) {
+    if (ensure_vt(e, B, S)) return -1;
+    graph_slot *g = NULL;
+    for (int i = 0; i < e->ngraphs; i++)
+        if (e->graphs[i].B == B && e->graphs[i].S == S && e->graphs[i].has_valid == has_valid) g = &e->graphs[i];
+    if (g) {
+        e->kernels_last = g->kernels;
+        return e2cu_cuda(cudaGraphLaunch(g->exec, st), "encoder graph launch");
+    }
+    const int n = encode(e, B, S, has_valid, st);
+    if (n < 0) return -1;
+    e->kernels_last = n;
+    /* record the same sequence for the next call of this shape (not on the legacy stream) */
+    if (st && e->ngraphs < MAX_GRAPHS) {
+        cudaGraph_t graph = NULL;
+        if (cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal) == cudaSuccess) {
+            const int n2 = encode(e, B, S, has_valid, st);
+            const cudaError_t ce = cudaStreamEndCapture(st, &graph);
+            cudaGraphExec_t exec = NULL;
+            if (n2 >= 0 && ce == cudaSuccess && graph && cudaGraphInstantiate(&exec, graph, 0) == cudaSuccess) {
+                graph_slot *s = &e->graphs[e->ngraphs++];
+                s->B = B;
+                s->S = S;
+                s->has_valid = has_valid;
+                s->exec = exec;
+                s->kernels = n2;
+            }
+            if (graph) cudaGraphDestroy(graph);
+        }
+        cudaGetLastError(); /* a failed capture only means no graph for this shape */
+    }
+    return 0;
+}
+
+int e2cuda_encoder_embed_batch_device(e2cuda_encoder *e, const int32_t *d_ids, const uint8_t *d_valid, int batch,
+                                      int seq_len, float *d_out, void *stream) {
+    if (!e || !d_ids || !d_out || batch <= 0 || seq_len <= 0 || seq_len > e->max_seq) {
+        e2cu_err("encoder_embed_batch_device: bad arguments (seq_len %d, max %d)", seq_len, e ? e->max_seq : 0);
+        return -1;
+    }
+    cudaStream_t st = (cudaStream_t)stream;
+    const int per = e->max_tokens / seq_len;
+    if (per <= 0) {
+        e2cu_err("encoder_embed_batch_device: seq_len %d exceeds max_tokens %d", seq_len, e->max_tokens);
+        return -1;
+    }
+    for (int b0 = 0; b0 < batch; b0 += per) {
+        const int B = batch - b0 < per ? batch - b0 : per;
+        const size_t rows = (size_t)B * seq_len, off = (size_t)b0 * seq_len;
+        if (e2cu_cuda(cudaMemcpyAsync(e->ids, d_ids + off, sizeof(int32_t) * rows, cudaMemcpyDeviceToDevice, st), "ids") ||
+            (d_valid && e2cu_cuda(cudaMemcpyAsync(e->valid, d_valid + off, rows, cudaMemcpyDeviceToDevice, st), "valid")))
+            return -1;
+        if (pass(e, B, seq_len, d_valid != NULL, st)) return -1;
+        if (e2cu_cuda(cudaMemcpyAsync(d_out + (size_t)b0 * e->DO, e->out, sizeof(float) * (size_t)B * e->DO,
+                                      cudaMemcpyDeviceToDevice, st),
+                      "out"))
+            return -1;
+    }
+    e->calls++;
+    return 0;
+}
+
+static double now_ms(void) {
+    struct timespec ts;
+    clock_gettime(CLOCK_MONOTONIC, &ts);
+    return ts.tv_sec * 1e3 + ts.tv_nsec / 1e6;
+}
+
+int e2cuda_encoder_embed_batch(e2cuda_encoder *e, const int32_t *ids, const uint8_t *valid, int batch, int seq_len,
+                               float *out) {
+    const double t0 = now_ms();
+    if (!e || !ids || !out || batch <= 0 || seq_len <= 0 || seq_len > e->max_seq) {
+        e2cu_err("encoder_embed_batch: bad batch geometry");
+        return -1;
+    }
+    /* validate the whole request before touching the output (e2.c src/text.c:1005-1011) */
+    const size_t total = (size_t)batch * seq_len;
+    for (size_t i = 0; i < total; i++)
+        if (ids[i] < 0 || ids[i] >= e->V) {
+            e2cu_err("token id %d out of range", ids[i]);
+            return -1;
+        }
+    const int per = e->max_tokens / seq_len;
+    if (per <= 0) {
+        e2cu_err("encoder_embed_batch: seq_len %d exceeds max_tokens %d", seq_len, e->max_tokens);
+        return -1;
+    }
+    cudaStream_t st = e->stream;
+    for (int b0 = 0; b0 < batch; b0 += per) {
+        const int B = batch - b0 < per ? batch - b0 : per;
+        const size_t rows = (size_t)B * seq_len, off = (size_t)b0 * seq_len;
+        if (e2cu_cuda(cudaMemcpyAsync(e->ids, ids + off, sizeof(int32_t) * rows, cudaMemcpyHostToDevice, st), "ids") ||
+            (valid && e2cu_cuda(cudaMemcpyAsync(e->valid, valid + off, rows, cudaMemcpyHostToDevice, st), "valid")))
+            return -1;
+        if (pass(e, B, seq_len, valid != NULL, st)) return -1;
+        if (e2cu_cuda(cudaMemcpyAsync(out + (size_t)b0 * e->DO, e->out, sizeof(float) * (size_t)B * e->DO,
+                                      cudaMemcpyDeviceToHost, st),
+                      "out") ||
+            e2cuda_check(st))
+            return -1;
+    }
+    e->calls++;
+    e->last_ms = now_ms() - t0;
+    return 0;
+}
+
+int e2cuda_encoder_stats(e2cuda_encoder *e, long *calls, long *kernels_last, double *last_ms) {
+    if (!e) {
+        e2cu_err("encoder_stats: null encoder");
+        return -1;
+    }
+    if (calls) *calls = e->calls;
+    if (kernels_last) *kernels_last = e->kernels_last;
+    if (last_ms) *last_ms = e->last_ms;
+    return 0;
+}

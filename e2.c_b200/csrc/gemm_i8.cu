@@ -1,0 +1,542 @@
+// gemm_i8.cu — W8A8 GEMM on the sm_100a tensor cores (tcgen05.mma kind::i8).
+//
+//   y[m, n] = sum over activation blocks b of  float(dot_b(m, n)) * (as[m, b] * ws[n])
+//
+// dot_b is the exact int32 dot of the signed int8 activation row and weight row over block b; the
+// fold is f = fma(float(dot_b), as*ws, f), blocks in order, as in the reference's AVX512-VNNI kernel
+// (src/kernels_i8_avx512_vnni.c:113-119,276-307), so per-row (one block = K) and per-block outputs
+// are bit-identical to it. With per-row scales the whole K accumulates in TMEM and the epilogue
+// runs once per tile; with per-block scales the accumulator is drained after every block into a
+// register-resident fp32 fold while the tensor core fills the other TMEM buffer.
+//
+// Structure (one CTA per SM, persistent over 128 x BN output tiles):
+//   warp 0      TMA producer: A [128 x 128] and B [BN x 128] int8 tiles, 128-byte swizzle,
+//               a ring of shared-memory stages guarded by full/empty mbarriers;
+//   warp 1      TMEM owner and MMA issuer: 4 x tcgen05.mma (K = 32) per stage into one of two
+//               TMEM accumulators (2 x BN columns of int32), tcgen05.commit frees stages;
+//   warps 2..5  epilogue: tcgen05.ld of their 32 TMEM lanes, dequant and the fused tail
+//               (residual, clamp, GELU-gate, per-head RMSNorm + RoPE), direct stores.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdint.h>
+#include <stdio.h>
+
+#include "launch.h"
+#include "ptx.cuh"
+#include "tmap.h"
+
+namespace {
+
+constexpr int BM = 128;   // tile rows (tokens) = TMEM lanes
+constexpr int BK = 128;   // bytes of K per stage = one 128-byte swizzle row
+constexpr int NTHREADS = 192;
+
+template <int BN, int STAGES>
+struct GemmSmem {
+    static constexpr int A_BYTES = BM * BK;
+    static constexpr int B_BYTES = BN * BK;
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int BAR_OFF = STAGES * STAGE_BYTES;
+    // full[S], empty[S], tfull[2], tempty[2], tmem slot
+    static constexpr int BYTES = BAR_OFF + (2 * STAGES + 4) * 8 + 16;
+    static constexpr int ALLOC = BYTES + 1024;  // slack for 1024-byte alignment
+};
+
+// ---------------------------------------------------------------------------------- epilogue math
+// The reference's AVX-512 exp (src/kernels_avx512.c:19-44): two-constant range reduction, degree-5
+// polynomial, exponent-field scaling.
+__device__ __forceinline__ float exp_poly(float x) {
+    x = fminf(fmaxf(x, -87.0f), 88.0f);
+    const float t = __fmul_rn(x, 1.4426950408889634f);
+    const float n = rintf(t);
+    float r = __fmaf_rn(-n, 0.6931471805599453f, x);
+    r = __fmaf_rn(-n, -1.904654299957768e-9f, r);
+    float p = 1.9875691500e-4f;
+    p = __fmaf_rn(p, r, 1.3981999507e-3f);
+    p = __fmaf_rn(p, r, 8.3334519073e-3f);
+    p = __fmaf_rn(p, r, 4.1665795894e-2f);
+    p = __fmaf_rn(p, r, 1.6666665459e-1f);
+    p = __fmaf_rn(p, r, 5.0000001201e-1f);
+    p = __fmaf_rn(p, __fmul_rn(r, r), r);
+    p = __fadd_rn(p, 1.0f);
+    const int ni = __float2int_rn(n);
+    return __fmul_rn(p, __int_as_float((ni + 127) << 23));
+}
+// GELU-tanh of the reference (src/kernels_avx512.c:46-55,186-203).
+__device__ __forceinline__ float gelu_tanh(float v) {
+    const float v3 = __fmul_rn(__fmul_rn(v, v), v);
+    const float inner = __fmul_rn(0.7978845608028654f, __fmaf_rn(0.044715f, v3, v));
+    const float a = fabsf(inner);
+    const float e = exp_poly(__fadd_rn(a, a));
+    float th = __fsub_rn(1.0f, __fdiv_rn(2.0f, __fadd_rn(e, 1.0f)));
+    if (a > 15.0f) th = 1.0f;
+    th = copysignf(th, inner);
+    return __fmul_rn(__fmul_rn(0.5f, v), __fadd_rn(1.0f, th));
+}
+
+__device__ __forceinline__ float dq(uint32_t acc, float s) { return __fmul_rn(__int2float_rn((int)acc), s); }
+
+__device__ __forceinline__ void store_bf16x32(__nv_bfloat16 *dst, const float (&v)[32]) {
+    uint4 *d4 = reinterpret_cast<uint4 *>(dst);
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        uint32_t w[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const __nv_bfloat162 h = __floats2bfloat162_rn(v[8 * i + 2 * j], v[8 * i + 2 * j + 1]);
+            w[j] = *reinterpret_cast<const uint32_t *>(&h);
+        }
+        d4[i] = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+}
+
+// ---------------------------------------------------------------------------------- kernel
+template <int BN, int STAGES, bool PERBLOCK, int EPI>
+__global__ void __launch_bounds__(NTHREADS, 1)
+    k_gemm_i8(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const e2c_gemm_args p) {
+    using L = GemmSmem<BN, STAGES>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    const uint32_t sbase = smem_u32(smem);
+    const uint32_t bar0 = sbase + L::BAR_OFF;
+    auto full_bar = [&](int s) { return bar0 + 8u * s; };
+    auto empty_bar = [&](int s) { return bar0 + 8u * (STAGES + s); };
+    auto tfull_bar = [&](int a) { return bar0 + 8u * (2 * STAGES + a); };
+    auto tempty_bar = [&](int a) { return bar0 + 8u * (2 * STAGES + 2 + a); };
+    volatile uint32_t *tmem_slot = reinterpret_cast<volatile uint32_t *>(smem + L::BAR_OFF + (2 * STAGES + 4) * 8);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int M = p.M, K = p.K;
+    const int ncols = p.n1 - p.n0;
+    const int tiles_m = (M + BM - 1) / BM, tiles_n = (ncols + BN - 1) / BN;
+    const int ntiles = tiles_m * tiles_n;
+    const int nk = (K + BK - 1) / BK;                    // stages per tile
+    const int kpu = PERBLOCK ? p.ablk / BK : nk;         // stages per accumulation unit
+    const int nunits = PERBLOCK ? K / p.ablk : 1;
+    const int nb = K / p.ablk;                           // scale blocks per row
+    constexpr uint32_t TMEM_COLS = 2 * BN;
+
+    if (warp == 0 && lane == 0) {
+        for (int s = 0; s < STAGES; s++) {
+            mbar_init(full_bar(s), 1);
+            mbar_init(empty_bar(s), 1);
+        }
+        for (int a = 0; a < 2; a++) {
+            mbar_init(tfull_bar(a), 1);
+            mbar_init(tempty_bar(a), 128);
+        }
+        fence_mbar_init();
+        tma_prefetch_desc(&tmA);
+        tma_prefetch_desc(&tmB);
+    }
+    if (warp == 1) {
+        tmem_alloc(sbase + L::BAR_OFF + (2 * STAGES + 4) * 8, TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------------ TMA producer
+        if (elect_one()) {
+            int stage = 0;
+            uint32_t phase = 0;
+            int issued = 0;  // loads in flight that nobody consumed (drained on failure)
+            bool ok = true;
+            for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+                const int m0 = (t / tiles_n) * BM, c0 = p.n0 + (t % tiles_n) * BN;
+                for (int kb = 0; kb < nk; kb++) {
+                    if (!mbar_wait(empty_bar(stage), phase ^ 1u, p.status, E2C_ERR_WAIT_PRODUCER)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t sa = sbase + stage * L::STAGE_BYTES, sb = sa + L::A_BYTES;
+                    mbar_arrive_expect_tx(full_bar(stage), L::STAGE_BYTES);
+                    tma_load_2d(sa, &tmA, kb * BK, m0, full_bar(stage));
+                    tma_load_2d(sb, &tmB, kb * BK, c0, full_bar(stage));
+                    issued++;
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+            }
+            if (!ok) {
+                // let the copies this thread started land before the CTA's shared memory goes away
+                int s = stage, ph = phase;
+                for (int i = 0; i < (issued < STAGES ? issued : STAGES); i++) {
+                    if (--s < 0) {
+                        s = STAGES - 1;
+                        ph ^= 1;
+                    }
+                    mbar_wait(full_bar(s), (uint32_t)ph, nullptr, E2C_ERR_WAIT_DRAIN);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------------ MMA issuer
+        if (elect_one()) {
+            constexpr uint32_t idesc = idesc_i8(BN);
+            int stage = 0;
+            uint32_t phase = 0;
+            int acc = 0;
+            uint32_t acc_phase = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+                for (int u = 0; u < nunits && ok; u++) {
+                    if (!mbar_wait(tempty_bar(acc), acc_phase ^ 1u, p.status, E2C_ERR_WAIT_MMA)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t d = tmem_base + (uint32_t)(acc * BN);
+                    for (int kk = 0; kk < kpu; kk++) {
+                        if (!mbar_wait(full_bar(stage), phase, p.status, E2C_ERR_WAIT_MMA)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        const uint32_t sa = sbase + stage * L::STAGE_BYTES, sb = sa + L::A_BYTES;
+#pragma unroll
+                        for (int k = 0; k < BK / 32; k++)
+                            mma_i8(d, smem_desc_sw128(sa + 32 * k), smem_desc_sw128(sb + 32 * k), idesc,
+                                   (kk | k) != 0);
+                        mma_commit(empty_bar(stage));
+                        if (++stage == STAGES) {
+                            stage = 0;
+                            phase ^= 1u;
+                        }
+                    }
+                    mma_commit(tfull_bar(acc));
+                    if (++acc == 2) {
+                        acc = 0;
+                        acc_phase ^= 1u;
+                    }
+                }
+            }
+            if (!ok) {
+                // every MMA issued so far must finish before the accumulator is released
+                const uint32_t drain = tfull_bar(acc);
+                mma_commit(drain);
+                mbar_wait(drain, acc_phase, nullptr, E2C_ERR_WAIT_DRAIN);
+            }
+        }
+    } else {
+        // ------------------------------------------------------------------ epilogue
+        const int q = warp & 3;          // TMEM lane quadrant this warp may access
+        const int row = q * 32 + lane;   // row of the tile = TMEM lane
+        const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        bool ok = true;
+        for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+            const int m = (t / tiles_n) * BM + row;
+            const int c0 = p.n0 + (t % tiles_n) * BN;
+            const bool mrow = m < M;
+            if constexpr (PERBLOCK) {
+                float f[BN];
+#pragma unroll
+                for (int j = 0; j < BN; j++) f[j] = 0.f;
+                for (int u = 0; u < nunits; u++) {
+                    // warp-uniform outcome: tcgen05.ld below is .sync.aligned
+                    if (!__all_sync(0xffffffffu, mbar_wait(tfull_bar(acc), acc_phase, p.status, E2C_ERR_WAIT_EPI))) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const float as = mrow ? __ldg(p.a_scale + (size_t)m * nb + u) : 0.f;
+#pragma unroll
+                    for (int c = 0; c < BN / 32; c++) {
+                        uint32_t r[32];
+                        tmem_ld32(tmem_base + lane_addr + (uint32_t)(acc * BN + c * 32), r);
+                        tmem_wait_ld();
+                        if constexpr (EPI == E2C_EPI_I32) {
+                            if (mrow)
+                                for (int j = 0; j < 32; j++) {
+                                    const int n = c0 + c * 32 + j;
+                                    if (n < p.n1) p.dots[((size_t)m * p.ldd + n) * nb + u] = (int32_t)r[j];
+                                }
+                        } else {
+#pragma unroll
+                            for (int j = 0; j < 32; j++) {
+                                const int n = c0 + c * 32 + j;
+                                const float ws = n < p.n1 ? __ldg(p.w_scale + n) : 0.f;
+                                f[c * 32 + j] = __fmaf_rn(__int2float_rn((int)r[j]), __fmul_rn(as, ws), f[c * 32 + j]);
+                            }
+                        }
+                    }
+                    tc_fence_before();
+                    mbar_arrive(tempty_bar(acc));
+                    if (++acc == 2) {
+                        acc = 0;
+                        acc_phase ^= 1u;
+                    }
+                }
+                if (!ok) break;
+                if constexpr (EPI != E2C_EPI_I32) {
+                    if (mrow) {
+#pragma unroll
+                        for (int j = 0; j < BN; j++) {
+                            const int n = c0 + j;
+                            if (n < p.n1) {
+                                float v = fminf(fmaxf(f[j], p.out_min), p.out_max);
+                                if constexpr (EPI == E2C_EPI_RESID) v = __fadd_rn(v, p.resid[(size_t)m * p.ldr + n]);
+                                p.y[(size_t)m * p.ldy + n] = v;
+                            }
+                        }
+                    }
+                }
+            } else {
+                if (!__all_sync(0xffffffffu, mbar_wait(tfull_bar(acc), acc_phase, p.status, E2C_ERR_WAIT_EPI))) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const float as = mrow ? __ldg(p.a_scale + (size_t)m * nb) : 0.f;
+                const uint32_t tbase = tmem_base + lane_addr + (uint32_t)(acc * BN);
+                if constexpr (EPI == E2C_EPI_F32 || EPI == E2C_EPI_RESID || EPI == E2C_EPI_I32) {
+#pragma unroll 1
+                    for (int c = 0; c < BN / 32; c++) {
+                        uint32_t r[32];
+                        tmem_ld32(tbase + c * 32, r);
+                        tmem_wait_ld();
+                        const int nbase = c0 + c * 32;
+                        if (!mrow || nbase >= p.n1) continue;
+                        if constexpr (EPI == E2C_EPI_I32) {
+                            for (int j = 0; j < 32; j++)
+                                if (nbase + j < p.n1) p.dots[(size_t)m * p.ldd + nbase + j] = (int32_t)r[j];
+                        } else {
+                            float v[32];
+#pragma unroll
+                            for (int j = 0; j < 32; j++) {
+                                const int n = nbase + j;
+                                const float ws = n < p.n1 ? __ldg(p.w_scale + n) : 0.f;
+                                v[j] = fminf(fmaxf(dq(r[j], __fmul_rn(as, ws)), p.out_min), p.out_max);
+                            }
+                            float *yr = p.y + (size_t)m * p.ldy + nbase;
+                            if constexpr (EPI == E2C_EPI_RESID) {
+                                const float *rr = p.resid + (size_t)m * p.ldr + nbase;
+                                for (int j = 0; j < 32; j++)
+                                    if (nbase + j < p.n1) v[j] = __fadd_rn(v[j], rr[j]);
+                            }
+                            const bool vec = nbase + 32 <= p.n1 && ((reinterpret_cast<uintptr_t>(yr) & 15) == 0);
+                            if (vec) {
+                                float4 *y4 = reinterpret_cast<float4 *>(yr);
+#pragma unroll
+                                for (int j = 0; j < 8; j++) y4[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+                            } else {
+                                for (int j = 0; j < 32; j++)
+                                    if (nbase + j < p.n1) yr[j] = v[j];
+                            }
+                        }
+                    }
+                } else if constexpr (EPI == E2C_EPI_GELU) {
+                    // weight rows are interleaved per 128: [gate c0/2 .. +128 | up c0/2 .. +128]
+                    const int h0 = (c0 - p.n0) / 2;
+#pragma unroll 1
+                    for (int c = 0; c < 4; c++) {
+                        uint32_t rg[32], ru[32];
+                        tmem_ld32(tbase + c * 32, rg);
+                        tmem_ld32(tbase + 128 + c * 32, ru);
+                        tmem_wait_ld();
+                        if (!mrow) continue;
+                        float h[32];
+#pragma unroll
+                        for (int j = 0; j < 32; j++) {
+                            const int ng = c0 + c * 32 + j, nu = ng + 128;
+                            const float g = dq(rg[j], __fmul_rn(as, __ldg(p.w_scale + ng)));
+                            const float u = dq(ru[j], __fmul_rn(as, __ldg(p.w_scale + nu)));
+                            h[j] = __fmul_rn(gelu_tanh(g), u);
+                        }
+                        float4 *y4 = reinterpret_cast<float4 *>(p.y + (size_t)m * p.ldy + h0 + c * 32);
+#pragma unroll
+                        for (int j = 0; j < 8; j++) y4[j] = make_float4(h[4 * j], h[4 * j + 1], h[4 * j + 2], h[4 * j + 3]);
+                    }
+                } else if constexpr (EPI == E2C_EPI_QKV) {
+                    // one 256-column tile = one head: q heads, then k, then v
+                    const int head = (c0 - p.n0) / 256;
+                    const bool is_k = head == p.nq, is_v = head == p.nq + 1;
+                    const float *gamma = is_v ? nullptr : (is_k ? p.k_gamma : p.q_gamma);
+                    float ss = 0.f;
+#pragma unroll 1
+                    for (int c = 0; c < 8; c++) {
+                        uint32_t r[32];
+                        tmem_ld32(tbase + c * 32, r);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int j = 0; j < 32; j++) {
+                            const float v = dq(r[j], __fmul_rn(as, __ldg(p.w_scale + c0 + c * 32 + j)));
+                            ss = __fmaf_rn(v, v, ss);
+                        }
+                    }
+                    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, 256.0f), p.eps)));
+                    const int pos = mrow ? m % p.seq_len : 0;
+#pragma unroll 1
+                    for (int c = 0; c < 4; c++) {
+                        uint32_t ra[32], rb[32];
+                        tmem_ld32(tbase + c * 32, ra);
+                        tmem_ld32(tbase + 128 + c * 32, rb);
+                        tmem_wait_ld();
+                        if (!mrow) continue;
+                        float va[32], vb[32];
+#pragma unroll
+                        for (int j = 0; j < 32; j++) {
+                            const int i = c * 32 + j;
+                            float a = __fmul_rn(dq(ra[j], __fmul_rn(as, __ldg(p.w_scale + c0 + i))), inv);
+                            float b = __fmul_rn(dq(rb[j], __fmul_rn(as, __ldg(p.w_scale + c0 + 128 + i))), inv);
+                            if (gamma) {
+                                a = __fmul_rn(a, __ldg(gamma + i));
+                                b = __fmul_rn(b, __ldg(gamma + 128 + i));
+                            }
+                            if (!is_v) {
+                                const float cs = __ldg(p.rope_cos + (size_t)pos * 128 + i);
+                                const float sn = __ldg(p.rope_sin + (size_t)pos * 128 + i);
+                                const float oa = __fmaf_rn(a, cs, -__fmul_rn(b, sn));
+                                const float ob = __fmaf_rn(a, sn, __fmul_rn(b, cs));
+                                a = oa;
+                                b = ob;
+                            }
+                            va[j] = a;
+                            vb[j] = b;
+                        }
+                        if (is_v) {
+                            __nv_bfloat16 *vt = reinterpret_cast<__nv_bfloat16 *>(p.vt_out) +
+                                                (size_t)(m / p.seq_len) * 256 * p.ldvt + pos;
+#pragma unroll
+                            for (int j = 0; j < 32; j++) {
+                                vt[(size_t)(c * 32 + j) * p.ldvt] = __float2bfloat16_rn(va[j]);
+                                vt[(size_t)(128 + c * 32 + j) * p.ldvt] = __float2bfloat16_rn(vb[j]);
+                            }
+                        } else {
+                            __nv_bfloat16 *dst = is_k ? reinterpret_cast<__nv_bfloat16 *>(p.k_out) + (size_t)m * 256
+                                                      : reinterpret_cast<__nv_bfloat16 *>(p.q_out) +
+                                                            (size_t)m * (256 * p.nq) + head * 256;
+                            store_bf16x32(dst + c * 32, va);
+                            store_bf16x32(dst + 128 + c * 32, vb);
+                        }
+                    }
+                }
+                tc_fence_before();
+                mbar_arrive(tempty_bar(acc));
+                if (++acc == 2) {
+                    acc = 0;
+                    acc_phase ^= 1u;
+                }
+            }
+        }
+        (void)ok;
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, TMEM_COLS);
+    }
+}
+
+int g_num_sms = 0;
+
+template <int BN, int STAGES, bool PERBLOCK, int EPI>
+int launch(const e2c_gemm_args *a, cudaStream_t st) {
+    using L = GemmSmem<BN, STAGES>;
+    auto kern = k_gemm_i8<BN, STAGES, PERBLOCK, EPI>;
+    static bool attr_set = false;
+    if (!attr_set) {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC) != cudaSuccess) {
+            e2c_set_msg("gemm: cannot reserve %d bytes of shared memory", L::ALLOC);
+            return -2;
+        }
+        attr_set = true;
+    }
+    CUtensorMap ta, tb;
+    if (e2c_tmap_2d(&ta, a->a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)a->K, (uint64_t)a->M, (uint64_t)a->lda,
+                    BK, BM) ||
+        e2c_tmap_2d(&tb, a->w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)a->K, (uint64_t)a->wrows,
+                    (uint64_t)a->ldw, BK, BN))
+        return -3;
+    const int tiles = ((a->M + BM - 1) / BM) * ((a->n1 - a->n0 + BN - 1) / BN);
+    const int grid = tiles < g_num_sms ? tiles : g_num_sms;
+    kern<<<grid, NTHREADS, L::ALLOC, st>>>(ta, tb, *a);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        e2c_set_msg("gemm launch: %s", cudaGetErrorString(e));
+        return -2;
+    }
+    return 0;
+}
+
+int pick_bn(const e2c_gemm_args *a) {
+    if (a->ablk != a->K) return 128;                         // per-block fold keeps BN floats per thread
+    if (a->epi == E2C_EPI_GELU || a->epi == E2C_EPI_QKV) return 256;
+    const int ncols = a->n1 - a->n0;
+    const int t256 = ((a->M + BM - 1) / BM) * ((ncols + 255) / 256);
+    return t256 * 2 <= g_num_sms ? 128 : 256;                // small problems: more, narrower tiles
+}
+
+}  // namespace
+
+extern "C" void e2c_gemm_tile(const e2c_gemm_args *a, int *bm, int *bn) {
+    if (!g_num_sms) cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, 0);
+    *bm = BM;
+    *bn = pick_bn(a);
+}
+
+extern "C" int e2c_gemm(const e2c_gemm_args *a, void *stream) {
+    if (!g_num_sms) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        if (cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || g_num_sms <= 0) {
+            e2c_set_msg("gemm: no CUDA device");
+            return -2;
+        }
+    }
+    if (a->M < 0 || a->K <= 0 || a->K % 16 || a->lda % 16 || a->ldw % 16 || a->n0 < 0 || a->n1 > a->wrows ||
+        a->n0 > a->n1) {
+        e2c_set_msg("gemm: bad geometry (M=%d K=%d lda=%d ldw=%d n0=%d n1=%d wrows=%d): K and strides must be multiples of 16",
+                    a->M, a->K, a->lda, a->ldw, a->n0, a->n1, a->wrows);
+        return -1;
+    }
+    if (a->ablk <= 0 || a->K % a->ablk || (a->ablk != a->K && a->ablk % BK)) {
+        e2c_set_msg("gemm: activation block %d must be K (per-row) or a multiple of 128 dividing K=%d", a->ablk, a->K);
+        return -1;
+    }
+    if (((uintptr_t)a->a | (uintptr_t)a->w) & 15) {
+        e2c_set_msg("gemm: operands must be 16-byte aligned");
+        return -1;
+    }
+    if (a->M == 0 || a->n1 == a->n0) return 0;
+    cudaStream_t st = (cudaStream_t)stream;
+    const bool perblock = a->ablk != a->K;
+    const int bn = pick_bn(a);
+    switch (a->epi) {
+    case E2C_EPI_F32:
+        if (perblock) return launch<128, 6, true, E2C_EPI_F32>(a, st);
+        return bn == 128 ? launch<128, 6, false, E2C_EPI_F32>(a, st) : launch<256, 4, false, E2C_EPI_F32>(a, st);
+    case E2C_EPI_RESID:
+        if (perblock) return launch<128, 6, true, E2C_EPI_RESID>(a, st);
+        return bn == 128 ? launch<128, 6, false, E2C_EPI_RESID>(a, st) : launch<256, 4, false, E2C_EPI_RESID>(a, st);
+    case E2C_EPI_I32:
+        if (perblock) return launch<128, 6, true, E2C_EPI_I32>(a, st);
+        return bn == 128 ? launch<128, 6, false, E2C_EPI_I32>(a, st) : launch<256, 4, false, E2C_EPI_I32>(a, st);
+    case E2C_EPI_GELU:
+        if (perblock || (a->n1 - a->n0) % 256 || a->ldy % 4) {
+            e2c_set_msg("gemm: the GELU-gate epilogue needs per-row scales and 256-column (gate|up) groups");
+            return -1;
+        }
+        return launch<256, 4, false, E2C_EPI_GELU>(a, st);
+    case E2C_EPI_QKV:
+        if (perblock || a->n0 != 0 || a->n1 != 256 * (a->nq + 2) || a->seq_len <= 0 || a->M % a->seq_len) {
+            e2c_set_msg("gemm: the QKV epilogue needs per-row scales, whole heads of 256 and M a multiple of seq_len");
+            return -1;
+        }
+        return launch<256, 4, false, E2C_EPI_QKV>(a, st);
+    default:
+        e2c_set_msg("gemm: unknown epilogue %d", a->epi);
+        return -1;
+    }
+}

@@ -1,0 +1,101 @@
+/* launch.h — the C-callable kernel launchers behind the e2cuda C ABI.
+ *
+ * The host side of e2cuda (e2cuda.c, encoder.c) is C11; every function here is implemented in a
+ * .cu file and exported with C linkage. All pointers are device pointers unless named otherwise;
+ * `stream` is a cudaStream_t. Launchers check arguments they can check cheaply and return 0, or a
+ * negative code with a message in e2c_msg.
+ */
+#ifndef E2C_LAUNCH_H
+#define E2C_LAUNCH_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* last launcher error message (thread-local) */
+const char *e2c_msg(void);
+void e2c_set_msg(const char *fmt, ...);
+
+/* Activation quantiser (src/int8.c:178-209 semantics, SURVEY F3 forms): x fp32 [M][K] (row stride
+ * ldx floats) -> q int8 [M][K] (row stride ldq bytes), scales [M][K/ablk]. biased != 0 stores q+128
+ * (the reference's byte convention), else signed q. ablk = K for per-row, else a divisor of K that
+ * is a multiple of 16. */
+int e2c_quantize(const float *x, int ldx, int8_t *q, int ldq, float *scales, int M, int K, int ablk,
+                 float lo, float hi, int biased, void *stream);
+
+/* bytes ^= 0x80: converts between the reference's biased q+128 and signed q, in place */
+int e2c_flip_bias(int8_t *q, size_t n, void *stream);
+
+/* int8 GEMM epilogues */
+enum {
+    E2C_EPI_F32 = 0,   /* y = dequant (clamped)                                            */
+    E2C_EPI_RESID = 1, /* y = dequant (clamped) + resid                                    */
+    E2C_EPI_I32 = 2,   /* dots[m][n][b] = raw int32 block dots (debug; bit-exact check)      */
+    E2C_EPI_GELU = 3,  /* weight rows interleaved per 128: h = gelu(g) * u, fp32 [M][N/2]  */
+    E2C_EPI_QKV = 4    /* per-head RMSNorm (+gamma) + RoPE -> bf16 Q, K, V^T               */
+};
+
+typedef struct {
+    /* operands */
+    const int8_t *a;       /* [M][K] signed, row stride lda bytes (multiple of 16)          */
+    int lda;
+    const float *a_scale;  /* [M][K/ablk]                                                  */
+    const int8_t *w;       /* [wrows][K] K-major, row stride ldw bytes (multiple of 16)     */
+    int ldw, wrows;
+    const float *w_scale;  /* [wrows]                                                      */
+    int M, K, ablk;
+    int n0, n1;            /* columns (= weight rows) to compute                            */
+    int epi;
+    /* outputs */
+    float *y;              /* F32 / RESID / GELU output, row stride ldy floats              */
+    int ldy;
+    const float *resid;    /* RESID: row stride ldr floats                                  */
+    int ldr;
+    int32_t *dots;         /* I32: [M][ldd][K/ablk]                                         */
+    int ldd;
+    float out_min, out_max;
+    /* QKV epilogue: columns [0, 256*nq) are q heads, then one k head, then one v head */
+    int nq;
+    void *q_out, *k_out, *vt_out; /* bf16: Q [M][256*nq], K [M][256], V^T [B][256][ldvt]  */
+    int ldvt, seq_len;     /* position of row m = m % seq_len; V^T row block = m / seq_len  */
+    const float *q_gamma, *k_gamma; /* [256] */
+    const float *rope_cos, *rope_sin; /* [seq_len][128] */
+    float eps;
+    int *status;
+} e2c_gemm_args;
+
+int e2c_gemm(const e2c_gemm_args *a, void *stream);
+/* the tile the GEMM picks for these arguments, for traffic accounting: *bm x *bn */
+void e2c_gemm_tile(const e2c_gemm_args *a, int *bm, int *bn);
+
+/* ---- row kernels of the encoder (one warp per token row, D = hidden, a multiple of 128;
+ * ablk is 128 or D) */
+/* x = table[id] * table_scale[id] * embed_scale; res = x; quantise(rmsnorm(x) * gamma) per row.
+ * An id outside [0, vocab) reads row 0 and records status 0x106. */
+int e2c_embed_norm_quant(const int32_t *ids, const int8_t *table, const float *table_scale,
+                         float embed_scale, const float *gamma, float eps, float *res, int8_t *q,
+                         float *qs, int M, int D, int ablk, int vocab, int *status, void *stream);
+/* x = rmsnorm(t) * g1 + res; then res = x and quantise(rmsnorm(x) * g2) per row. With g2 NULL:
+ * out = rmsnorm(x) * gfinal written to `res` instead (the last layer's final norm), no quantise. */
+int e2c_norm_add_norm_quant(const float *t, float *res, const float *g1, const float *g2,
+                            const float *gfinal, float eps, int8_t *q, float *qs, int M, int D,
+                            int ablk, void *stream);
+/* quantise(rmsnorm(x) * gamma) per row (config-1 FFN prologue; the residual is x itself) */
+int e2c_norm_quant(const float *x, const float *gamma, float eps, int8_t *q, float *qs, int M, int D,
+                   int ablk, void *stream);
+/* pooled[b][d] = mean over valid rows of x[b*S + s][d] (all-invalid -> 0) */
+int e2c_meanpool(const float *x, const uint8_t *valid, float *pooled, int B, int S, int D, void *stream);
+/* rows of y [B][D] L2-normalised in place; rows whose sequence has no valid token become 0 */
+int e2c_l2norm_rows(float *y, const uint8_t *valid, int B, int S, int D, void *stream);
+
+/* ---- attention: bf16 Q [B*S][H*256], K [B*S][256], V^T [B][256][ldvt] -> ctx fp32 [B*S][H*256] */
+int e2c_attention(const void *q, const void *k, const void *vt, int ldvt, const uint8_t *valid,
+                  float *ctx, int B, int S, int H, float scale, int *status, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

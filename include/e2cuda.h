@@ -1,0 +1,169 @@
+/* e2cuda.h — e2.c's int8 hot path on an NVIDIA B200 (sm_100a), as a C ABI.
+ *
+ * The CUDA sibling of the engine's GPU backends (include/e2gpu.h, include/e2hip.h in e2.c): the same
+ * W8A8 recipe — int8 weights with one fp32 scale per output row (the q8cache's e2_q8w), activations
+ * quantised dynamically per token (or per 128-element block) — on the Blackwell tensor cores:
+ *
+ *   - activation quantiser          replaces e2_i8_quantize      (e2.c src/kernels.h:72)
+ *   - W8A8 GEMM + fused epilogues   replaces e2_i8_gemm          (e2.c src/int8.h:96-97)
+ *   - bf16 flash attention          replaces attention_blocked   (e2.c src/text.c:780-815)
+ *   - the synthetic encoder         the text tower's layer recipe (e2.c src/text.c:924-984) over
+ *                                   the kernels above, batch API shaped like e2_hip_text_embed_batch
+ *                                   (e2.c include/e2hip.h:44-50)
+ *
+ * Conventions (those of e2gpu.h/e2hip.h): calls return 0 on success and -1 on failure, with the
+ * reason in e2cuda_last_error() (thread-local). Input validation failures leave outputs untouched.
+ * Functions taking a `stream` (a cudaStream_t, passed as void*) work on DEVICE pointers and are
+ * stream-ordered: they return once the work is queued. A kernel that stops making progress records
+ * a status code instead of hanging (every wait in the kernels is bounded to ~2 s); e2cuda_check()
+ * synchronises a stream and reports such a failure. Host-buffer entry points (`_host`, the encoder's
+ * embed_batch) synchronise and check before returning.
+ *
+ * Signed int8 activations: the device path stores q, not the reference's q+128 (V_DOT4-style, like
+ * e2hip.h), so the +128 zero-point correction (e2_q8w.bsq) never exists on the device. Bytes are
+ * the reference's with the top bit flipped; the `_host` entry points convert at the boundary.
+ *
+ * No TMA multicast and no peer-memory access anywhere: each GPU reads only its own memory.
+ */
+#ifndef E2CUDA_H
+#define E2CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define E2CUDA_ABI_VERSION 1
+
+/* Byte-for-byte the reference's e2_q8w (e2.c src/int8.h:79-92): quad-interleaved int8 weights
+ * [Npad/8][K/4][8][4], per-block sums [nblocks][Npad], per-row scales [Npad], optional output clamp.
+ * e2.c passes its `const e2_q8w *` cast to this type. */
+typedef struct e2cuda_q8w {
+    int8_t *w;
+    int32_t *bsq;
+    float *scale;
+    int N, K, nblocks, Npad;
+    float out_min, out_max;
+    int borrowed;
+} e2cuda_q8w;
+
+/* A device-resident int8 weight in the layout the TMA engine streams: row-major [rows][ld] (K
+ * contiguous, ld = K rounded up to 16 bytes, rows = N rounded up to 16), fp32 scale per row. */
+typedef struct e2cuda_w8 {
+    int8_t *w;
+    float *scale;
+    int N, K, rows, ld;
+    float out_min, out_max; /* the e2_q8w clamp, applied at the GEMM's store */
+} e2cuda_w8;
+
+/* ------------------------------------------------------------------ library */
+const char *e2cuda_last_error(void);
+/* Name of the current CUDA device ("" if none); e2_hip_device's counterpart (e2hip.h:41). */
+const char *e2cuda_device(void);
+/* Synchronise `stream` and report (then clear) a device-side failure recorded by any e2cuda kernel
+ * on the current device since the last check. 0 = clean. */
+int e2cuda_check(void *stream);
+
+/* ------------------------------------------------------------------ weights (A2, A11) */
+/* Repack a reference e2_q8w (quad-interleaved, host) into a device e2cuda_w8. The int8 values and
+ * scales are copied, never re-quantised, so device weights are bit-identical to the q8cache's.
+ * Replaces the HIP backend's upload (e2.c src/gpu/hip/forward.c:28-64). */
+int e2cuda_w8_from_q8w(const e2cuda_q8w *q, e2cuda_w8 *out);
+/* The same from a plain row-major int8 [N][K] host matrix and its N row scales. */
+int e2cuda_w8_from_int8(const int8_t *w, const float *scale, int N, int K, e2cuda_w8 *out);
+void e2cuda_w8_free(e2cuda_w8 *w);
+
+/* ------------------------------------------------------------------ op API (device pointers) */
+/* Activation quantiser (A1), e2.c src/int8.c:178-209 / src/kernels_i8_avx512_vnni.c:312-366:
+ * per block of `ablk` elements (ablk = K: per-token scales), amax of the input clamped to [lo, hi]
+ * (-INFINITY/INFINITY: no clamp), scale = amax/127 (1 for an all-zero block), q = round(x*127/amax).
+ * x [M][K] fp32 -> q [M][K] signed int8, scales [M][K/ablk]. K and ablk multiples of 16. */
+int e2cuda_quantize_rows(const float *x, int8_t *q, float *scales, int M, int K, int ablk, float lo,
+                         float hi, void *stream);
+
+/* Optional epilogue of e2cuda_i8_gemm. */
+typedef struct e2cuda_epilogue {
+    const float *residual; /* y = gemm + residual[m * ld_residual + n] (NULL: none)              */
+    int ld_residual;
+    int32_t *dots;         /* debug: raw int32 block dots [M][N][K/ablk] instead of y (NULL: off) */
+} e2cuda_epilogue;
+
+/* W8A8 GEMM (A3), e2.c src/kernels_i8_avx512_vnni.c:276-307: for n in [n0, n1),
+ *   y[m * ldy + n] = clamp(sum_b fma-fold float(dot_b(qa[m], w[n])) * (a_scales[m][b] * w.scale[n]))
+ * bit-identical to the reference kernel. ablk = K (per-token scales, the fast path) or a multiple of
+ * 128 dividing K. */
+int e2cuda_i8_gemm(const e2cuda_w8 *w, const int8_t *qa, const float *a_scales, int M, int ablk,
+                   int n0, int n1, const e2cuda_epilogue *ep, float *y, int ldy, void *stream);
+
+/* bf16 attention (A8), full bidirectional over the valid keys of each sequence, GQA with one KV
+ * head: q [B*S][H*256], k [B*S][256], vt [B][256][ldvt] (V transposed, ldvt >= S, multiple of 8),
+ * valid [B*S] or NULL -> ctx fp32 [B*S][H*256]. scale multiplies the logits. */
+int e2cuda_attention(const void *q, const void *k, const void *vt, int ldvt, const uint8_t *valid,
+                     float *ctx, int B, int S, int H, float scale, void *stream);
+
+/* ------------------------------------------------------------------ fused FFN block (config 1) */
+typedef struct e2cuda_ffn e2cuda_ffn;
+/* y = down(quant(GELU_tanh(gate(q)) * up(q))) + x with q = quant(rmsnorm(x) * gamma), e2.c
+ * src/text.c:893-903 + gate_quant :424-468, per-token activation scales. gate/up [I][D], down
+ * [D][I] host e2_q8w; gamma [D] host. */
+e2cuda_ffn *e2cuda_ffn_create(const e2cuda_q8w *gate, const e2cuda_q8w *up, const e2cuda_q8w *down,
+                              const float *gamma, float eps, int max_tokens);
+void e2cuda_ffn_destroy(e2cuda_ffn *f);
+/* x, y device fp32 [M][D] (M <= max_tokens). */
+int e2cuda_ffn_forward(e2cuda_ffn *f, const float *x, int M, float *y, void *stream);
+
+/* ------------------------------------------------------------------ drop-ins on host buffers */
+/* Exactly the reference's op signatures (e2_i8_gemm_fn, e2_i8_quantize), biased q+128 bytes, so
+ * e2.c can install them in its kernel registry (e2.c src/kernels.c:438-459). Each call copies its
+ * operands to the device and its result back; weights are uploaded once per distinct e2_q8w and
+ * cached. ablk for the quantiser is e2cuda_set_act_block's (default 128, like E2_I8_BLOCK); the
+ * GEMM infers it from w->K / w->nblocks. Failures are reported through e2cuda_last_error(). */
+void e2cuda_set_act_block(int ablk);
+void e2cuda_i8_quantize_host(int8_t *out, float *scales, const float *x, int M, int K, float lo,
+                             float hi);
+void e2cuda_i8_gemm_host(float *y, const int8_t *qa, const float *a_scales, const e2cuda_q8w *w,
+                         int M, int N, int n0, int n1);
+/* Drop every cached weight upload (call before freeing the e2_q8w arrays they mirror). */
+void e2cuda_host_cache_clear(void);
+
+/* ------------------------------------------------------------------ the synthetic encoder (config 2) */
+typedef struct e2cuda_encoder e2cuda_encoder;
+
+typedef struct e2cuda_encoder_desc {
+    int n_layers, hidden, n_heads, n_kv_heads, head_dim, ffn, vocab, dense_hidden, out_dim;
+    int max_seq;        /* longest sequence a call may pass (RoPE table size)                        */
+    int ablk;           /* activation block: hidden (per token, default when 0) or 128                */
+    float rope_theta, eps, attn_scale, embed_scale;
+    /* host arrays, copied at create time */
+    const int8_t *table;          /* [vocab][hidden] int8 token table (F7)                           */
+    const float *table_scale;     /* [vocab]                                                          */
+    const e2cuda_q8w *wq, *wk, *wv, *wo, *wg, *wu, *wd; /* [n_layers] each                           */
+    const float *const *input_ln, *const *post_attn_ln, *const *pre_ffn_ln, *const *post_ffn_ln;
+    const float *const *q_norm, *const *k_norm;         /* [n_layers] pointers to [head_dim]          */
+    const float *final_norm;
+    const e2cuda_q8w *dense1, *dense2;                  /* hidden -> dense_hidden -> out_dim           */
+} e2cuda_encoder_desc;
+
+/* Uploads everything once. max_tokens bounds batch * seq_len of one device pass (larger batches
+ * are chunked by whole sequences). Returns NULL on failure. Restrictions of this build: head_dim
+ * 256, one KV head, hidden a multiple of 128 up to 1024. */
+e2cuda_encoder *e2cuda_encoder_create(const e2cuda_encoder_desc *d, int max_tokens);
+void e2cuda_encoder_destroy(e2cuda_encoder *e);
+/* Host buffers, e2_hip_text_embed_batch's contract (e2.c include/e2hip.h:44-50): ids [batch][seq_len],
+ * valid NULL or [batch][seq_len] (nonzero keeps a token), out [batch][out_dim] unit vectors; a
+ * sequence with no valid token yields exact zeros. Positions restart per sequence. */
+int e2cuda_encoder_embed_batch(e2cuda_encoder *e, const int32_t *ids, const uint8_t *valid,
+                               int batch, int seq_len, float *out);
+/* The same on device buffers, stream-ordered (call e2cuda_check before reading d_out). The first
+ * call for a (batch, seq_len) shape runs eagerly; later calls replay a captured CUDA graph. */
+int e2cuda_encoder_embed_batch_device(e2cuda_encoder *e, const int32_t *d_ids, const uint8_t *d_valid,
+                                      int batch, int seq_len, float *d_out, void *stream);
+/* Calls served, kernels in the last pass, wall time of the last host call (e2hip.h:62-64). */
+int e2cuda_encoder_stats(e2cuda_encoder *e, long *calls, long *kernels_last, double *last_ms);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,343 @@
+"""Parity of the e2cuda kernels with the reference's CPU int8 path (through the C ABI, on a B200).
+
+Bars: quantised bytes, scales, int32 dots and per-row-mode fp32 GEMM
+outputs are bit-exact; fp32 epilogues that run after an RMSNorm are compared teacher-forced with
+the reference's own tie rule; bf16 attention by cosine / relative error.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import math
+
+import numpy as np
+import pytest
+
+from conftest import cosine_rows, tie_tolerant_bytes
+
+pytestmark = pytest.mark.gpu
+
+
+def dev(torch, a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def f32_bits_equal(a: np.ndarray, b: np.ndarray) -> bool:
+    return np.array_equal(np.ascontiguousarray(a, np.float32).view(np.int32), np.ascontiguousarray(b, np.float32).view(np.int32))
+
+
+# ------------------------------------------------------------------------------------------ A1 quantiser
+QUANT_CASES = [(1, 768, 768), (7, 768, 768), (512, 768, 768), (333, 1152, 1152), (5, 8192, 8192), (17, 2048, 2048),
+               (9, 208, 208), (3, 3072, 3072), (64, 768, 128), (31, 1152, 128), (8, 512, 32), (8, 512, 64),
+               (8, 1024, 256), (8, 1024, 512), (0, 768, 768)]
+
+
+@pytest.mark.parametrize("M,K,ablk", QUANT_CASES)
+def test_quantize_bitexact(e2c, of, syn, torch_cuda, M, K, ablk):
+    rng = np.random.default_rng(M * 131 + K + ablk)
+    x = syn.activations(rng, max(M, 1), K)[:M] * rng.uniform(1e-3, 10.0, (M, 1)).astype(np.float32)
+    x = np.ascontiguousarray(x, np.float32)
+    if M > 0:
+        x[0] = 0.0                      # all-zero row: scale 1, bytes 0
+    if M > 2:
+        x[2, :ablk] = 0.0               # one all-zero block
+    q, s = e2c.quantize_rows(dev(torch_cuda, x), ablk)
+    eq, es = of.quantize_signed(x, ablk) if M else (np.zeros((0, K), np.int8), np.zeros((0, K // ablk), np.float32))
+    assert np.array_equal(q.cpu().numpy(), eq)
+    assert f32_bits_equal(s.cpu().numpy(), es)
+
+
+def test_quantize_clamp_and_host_dropin(e2c, of, syn, torch_cuda):
+    rng = np.random.default_rng(3)
+    x = syn.activations(rng, 40, 512)
+    lo, hi = -0.75, 0.5
+    q, s = e2c.quantize_rows(dev(torch_cuda, x), 128, lo, hi)
+    eb, es = of.quantize_biased(x, 128, lo, hi)
+    assert np.array_equal(q.cpu().numpy().view(np.uint8) ^ 0x80, eb)
+    assert f32_bits_equal(s.cpu().numpy(), es)
+    # the reference-signature drop-in: host buffers, biased bytes, block from e2cuda_set_act_block
+    lib = e2c.lib()
+    lib.e2cuda_set_act_block(128)
+    out = np.empty((40, 512), np.int8)
+    sc = np.empty((40, 4), np.float32)
+    lib.e2cuda_i8_quantize_host(out.ctypes.data_as(e2c.i8p), sc.ctypes.data_as(e2c.f32p), x.ctypes.data_as(e2c.f32p),
+                                40, 512, -math.inf, math.inf)
+    assert e2c.last_error() == ""
+    eb2, es2 = of.quantize_biased(x, 128)
+    assert np.array_equal(out.view(np.uint8), eb2) and f32_bits_equal(sc, es2)
+
+
+# ------------------------------------------------------------------------------------------ A3 GEMM
+GEMM_CASES = [
+    (512, 1152, 768, 768),     # config 0
+    (1, 256, 768, 768), (7, 40, 768, 768), (129, 300, 768, 768), (200, 1152, 1152, 1152),
+    (64, 64, 2048, 2048), (33, 96, 208, 208), (300, 2304, 768, 768), (16, 512, 8192, 8192),
+    (8, 64, 512, 128), (130, 256, 1024, 128), (17, 48, 384, 128), (256, 384, 2048, 256),
+]
+
+
+def _gemm_inputs(rng, M, N, K, ablk):
+    nb = K // ablk
+    qa = rng.integers(-127, 128, size=(M, K), dtype=np.int8)
+    a_s = rng.uniform(1e-3, 0.05, size=(M, nb)).astype(np.float32)
+    w = rng.integers(-127, 128, size=(N, K), dtype=np.int8)
+    ws = rng.uniform(1e-4, 0.02, size=N).astype(np.float32)
+    return qa, a_s, w, ws
+
+
+@pytest.mark.parametrize("M,N,K,ablk", GEMM_CASES)
+def test_gemm_bitexact(e2c, of, torch_cuda, M, N, K, ablk):
+    rng = np.random.default_rng(M + 7 * N + K + ablk)
+    qa, a_s, w, ws = _gemm_inputs(rng, M, N, K, ablk)
+    W = e2c.Weight(w=w, scale=ws)
+    qd, sd = dev(torch_cuda, qa), dev(torch_cuda, a_s)
+    y = e2c.i8_gemm(W, qd, sd, ablk).cpu().numpy()
+    dots = e2c.i8_gemm(W, qd, sd, ablk, dots=True).cpu().numpy()
+    e2c.check()
+    ey, ed = of.gemm_plain(qa, a_s, w, ws, ablk, want_dots=True)
+    assert np.array_equal(dots, ed), "int32 block dots differ"
+    assert f32_bits_equal(y, ey), f"fp32 outputs differ: max abs {np.abs(y - ey).max()}"
+
+
+def test_gemm_column_range_residual(e2c, of, torch_cuda):
+    rng = np.random.default_rng(11)
+    M, N, K = 45, 40, 768
+    qa, a_s, w, ws = _gemm_inputs(rng, M, N, K, K)
+    W = e2c.Weight(w=w, scale=ws)
+    y0 = np.full((M, N), -777.0, np.float32)
+    y = dev(torch_cuda, y0)
+    res = rng.standard_normal((M, N)).astype(np.float32)
+    e2c.i8_gemm(W, dev(torch_cuda, qa), dev(torch_cuda, a_s), K, n0=3, n1=29, residual=dev(torch_cuda, res), y=y)
+    got = y.cpu().numpy()
+    ey = of.gemm_plain(qa, a_s, w, ws, K)
+    assert np.all(got[:, :3] == -777.0) and np.all(got[:, 29:] == -777.0), "columns outside [n0, n1) were written"
+    assert f32_bits_equal(got[:, 3:29], ey[:, 3:29] + res[:, 3:29])
+
+
+def test_gemm_host_dropin_matches_reference_kernel(e2c, of, syn, torch_cuda):
+    """e2cuda_i8_gemm_host has e2_i8_gemm_fn's signature: biased bytes, packed e2_q8w, row stride N,
+    columns [n0, n1). Both modes, against the port of src/kernels_i8_avx512_vnni.c."""
+    rng = np.random.default_rng(5)
+    for ablk, M, N, K in ((768, 37, 200, 768), (128, 20, 96, 512)):
+        x = syn.activations(rng, M, K)
+        pw = syn.packed_weight(rng, N, K, 0.02, ablk)
+        qb, qs = of.quantize_biased(x, ablk)
+        q8 = of.Q8W()
+        pw.fill(q8)
+        want = np.full((M, N), -5.0, np.float32)
+        of.port().e2o_i8_gemm(want.ctypes.data_as(of.f32p), qb.view(np.int8).ctypes.data_as(of.i8p),
+                              qs.ctypes.data_as(of.f32p), C.byref(q8), M, N, 8, N - 5, ablk)
+        got = np.full((M, N), -5.0, np.float32)
+        q8e = e2c.Q8W()
+        pw.fill(q8e)
+        e2c.lib().e2cuda_i8_gemm_host(got.ctypes.data_as(e2c.f32p), qb.view(np.int8).ctypes.data_as(e2c.i8p),
+                                      qs.ctypes.data_as(e2c.f32p), C.byref(q8e), M, N, 8, N - 5)
+        assert e2c.last_error() == "", e2c.last_error()
+        assert f32_bits_equal(got, want)
+    e2c.lib().e2cuda_host_cache_clear()
+
+
+def test_gemm_clamp_from_q8w(e2c, of, syn, torch_cuda):
+    rng = np.random.default_rng(9)
+    M, N, K = 30, 64, 256
+    pw = syn.packed_weight(rng, N, K, 0.05, K)
+    q8 = e2c.Q8W()
+    pw.fill(q8)
+    q8.out_min, q8.out_max = -0.5, 0.5  # the audio tower's clipped linears (e2.c src/int8.h:84-88)
+    W = e2c.Weight(q8w=q8)
+    x = syn.activations(rng, M, K)
+    qa, a_s = of.quantize_signed(x, K)
+    y = e2c.i8_gemm(W, dev(torch_cuda, qa), dev(torch_cuda, a_s), K).cpu().numpy()
+    ey = of.gemm_plain(qa, a_s, pw.q, pw.scale, K, out_min=-0.5, out_max=0.5)
+    assert f32_bits_equal(y, ey) and y.max() <= 0.5 and y.min() >= -0.5
+
+
+# ------------------------------------------------------------------------------------------ fused epilogues
+class GemmArgs(C.Structure):
+    """Mirror of e2c_gemm_args (e2.c_b200/csrc/launch.h): the fused epilogues have no public entry
+    point of their own, so their parity tests drive the launcher directly."""
+
+    _fields_ = [("a", C.c_void_p), ("lda", C.c_int), ("a_scale", C.c_void_p), ("w", C.c_void_p), ("ldw", C.c_int),
+                ("wrows", C.c_int), ("w_scale", C.c_void_p), ("M", C.c_int), ("K", C.c_int), ("ablk", C.c_int),
+                ("n0", C.c_int), ("n1", C.c_int), ("epi", C.c_int), ("y", C.c_void_p), ("ldy", C.c_int),
+                ("resid", C.c_void_p), ("ldr", C.c_int), ("dots", C.c_void_p), ("ldd", C.c_int),
+                ("out_min", C.c_float), ("out_max", C.c_float), ("nq", C.c_int), ("q_out", C.c_void_p),
+                ("k_out", C.c_void_p), ("vt_out", C.c_void_p), ("ldvt", C.c_int), ("seq_len", C.c_int),
+                ("q_gamma", C.c_void_p), ("k_gamma", C.c_void_p), ("rope_cos", C.c_void_p),
+                ("rope_sin", C.c_void_p), ("eps", C.c_float), ("status", C.c_void_p)]
+
+
+def _launch(e2c, args, torch):
+    lib = e2c.lib()
+    lib.e2c_gemm.argtypes = [C.POINTER(GemmArgs), C.c_void_p]
+    lib.e2c_msg.restype = C.c_char_p
+    rc = lib.e2c_gemm(C.byref(args), torch.cuda.current_stream().cuda_stream)
+    assert rc == 0, lib.e2c_msg().decode()
+    e2c.check()
+
+
+def _args_for(W, qd, sd, M, K):
+    a = GemmArgs()
+    a.a, a.lda, a.a_scale = qd.data_ptr(), W.w8.ld, sd.data_ptr()
+    a.w, a.ldw, a.wrows, a.w_scale = C.cast(W.w8.w, C.c_void_p), W.w8.ld, W.w8.rows, C.cast(W.w8.scale, C.c_void_p)
+    a.M, a.K, a.ablk, a.n0, a.n1 = M, K, K, 0, W.N
+    a.out_min, a.out_max = -1e31, 1e31
+    return a
+
+
+def test_gelu_gate_epilogue_bitexact(e2c, of, torch_cuda):
+    """gate|up GEMM with GELU-tanh(g)*u in the epilogue (e2.c src/text.c:424-447 +
+    src/kernels_avx512.c:186-203) against the port of the same polynomial."""
+    torch = torch_cuda
+    rng = np.random.default_rng(21)
+    M, D, I = 150, 768, 1152
+    qa, a_s, wg, sg = _gemm_inputs(rng, M, I, D, D)
+    _, _, wu, su = _gemm_inputs(rng, M, I, D, D)
+    wi = np.empty((2 * I, D), np.int8)
+    si = np.empty(2 * I, np.float32)
+    for t in range(I // 128):
+        wi[256 * t:256 * t + 128], si[256 * t:256 * t + 128] = wg[128 * t:128 * t + 128], sg[128 * t:128 * t + 128]
+        wi[256 * t + 128:256 * t + 256], si[256 * t + 128:256 * t + 256] = wu[128 * t:128 * t + 128], su[128 * t:128 * t + 128]
+    W = e2c.Weight(w=wi, scale=si)
+    qd, sd = dev(torch, qa), dev(torch, a_s)
+    h = torch.zeros((M, I), dtype=torch.float32, device="cuda")
+    a = _args_for(W, qd, sd, M, D)
+    a.epi, a.y, a.ldy = 3, h.data_ptr(), I
+    _launch(e2c, a, torch)
+    g = of.gemm_plain(qa, a_s, wg, sg, D)
+    u = of.gemm_plain(qa, a_s, wu, su, D)
+    gg = np.ascontiguousarray(g.copy())
+    of.port().e2o_gelu_tanh(gg.ctypes.data_as(of.f32p), gg.size)
+    want = (gg * u).astype(np.float32)
+    got = h.cpu().numpy()
+    assert f32_bits_equal(got, want), f"max abs {np.abs(got - want).max()}"
+
+
+def test_qkv_epilogue_norm_rope(e2c, of, torch_cuda):
+    """q|k|v GEMM with per-head RMSNorm (+gamma) and RoPE in the epilogue (e2.c src/text.c:836-854),
+    bf16 outputs, V transposed. fp32 differs from the port only by the sum order of the norm."""
+    torch = torch_cuda
+    rng = np.random.default_rng(31)
+    B, S, D, H, Dh = 2, 200, 768, 3, 256
+    M, N = B * S, (H + 2) * Dh
+    qa, a_s, w, ws = _gemm_inputs(rng, M, N, D, D)
+    qg = (1 + 0.1 * rng.standard_normal(Dh)).astype(np.float32)
+    kg = (1 + 0.1 * rng.standard_normal(Dh)).astype(np.float32)
+    cs = np.empty((S, Dh), np.float32)
+    sn = np.empty((S, Dh), np.float32)
+    of.port().e2o_rope_tables(cs.ctypes.data_as(of.f32p), sn.ctypes.data_as(of.f32p), S, Dh, 10000.0)
+    W = e2c.Weight(w=w, scale=ws)
+    qd, sd = dev(torch, qa), dev(torch, a_s)
+    ldvt = (S + 7) // 8 * 8
+    Q = torch.zeros((M, H * Dh), dtype=torch.bfloat16, device="cuda")
+    K = torch.zeros((M, Dh), dtype=torch.bfloat16, device="cuda")
+    Vt = torch.zeros((B, Dh, ldvt), dtype=torch.bfloat16, device="cuda")
+    gq, gk = dev(torch, qg), dev(torch, kg)
+    cd, sdn = dev(torch, np.ascontiguousarray(cs[:, :128])), dev(torch, np.ascontiguousarray(sn[:, :128]))
+    a = _args_for(W, qd, sd, M, D)
+    a.epi, a.nq = 4, H
+    a.q_out, a.k_out, a.vt_out, a.ldvt, a.seq_len = Q.data_ptr(), K.data_ptr(), Vt.data_ptr(), ldvt, S
+    a.q_gamma, a.k_gamma, a.rope_cos, a.rope_sin, a.eps = gq.data_ptr(), gk.data_ptr(), cd.data_ptr(), sdn.data_ptr(), 1e-6
+    _launch(e2c, a, torch)
+    y = of.gemm_plain(qa, a_s, w, ws, D).reshape(M, H + 2, Dh)
+    port = of.port()
+    exp = np.empty_like(y)
+    for hd in range(H + 2):
+        blk = np.ascontiguousarray(y[:, hd])
+        gamma = qg if hd < H else (kg if hd == H else None)
+        port.e2o_rmsnorm(blk.ctypes.data_as(of.f32p), M, Dh, None if gamma is None else gamma.ctypes.data_as(of.f32p), 1e-6)
+        if hd <= H:
+            port.e2o_rope_rows(blk.ctypes.data_as(of.f32p), 0, M, 1, Dh, Dh,
+                               np.ascontiguousarray(np.tile(cs, (B, 1))).ctypes.data_as(of.f32p),
+                               np.ascontiguousarray(np.tile(sn, (B, 1))).ctypes.data_as(of.f32p))
+        exp[:, hd] = blk
+    to_bf = lambda t: t.float().cpu().numpy()
+    got = np.concatenate([to_bf(Q).reshape(M, H, Dh), to_bf(K).reshape(M, 1, Dh),
+                          to_bf(Vt)[:, :, :S].transpose(0, 2, 1).reshape(M, 1, Dh)], axis=1)
+    want = torch.from_numpy(exp).to(torch.bfloat16).float().numpy()
+    diff = np.abs(got - want)
+    ulp = np.abs(want) * 2.0 ** -7 + 1e-30
+    assert np.all(diff <= ulp), f"beyond one bf16 ulp: {int((diff > ulp).sum())}"
+    assert (diff == 0).mean() > 0.99
+
+
+def test_norm_quant_teacher_forced(e2c, of, torch_cuda):
+    """The config-1 prologue (rmsnorm * gamma -> per-row quantise): bytes within the tie rule."""
+    torch = torch_cuda
+    rng = np.random.default_rng(41)
+    M, D = 300, 768
+    x = rng.standard_normal((M, D)).astype(np.float32) * 3
+    g = (1 + 0.1 * rng.standard_normal(D)).astype(np.float32)
+    q = torch.zeros((M, D), dtype=torch.int8, device="cuda")
+    s = torch.zeros((M, 1), dtype=torch.float32, device="cuda")
+    lib = e2c.lib()
+    lib.e2c_norm_quant.argtypes = [C.c_void_p, C.c_void_p, C.c_float, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p]
+    xd, gd = dev(torch, x), dev(torch, g)
+    assert lib.e2c_norm_quant(xd.data_ptr(), gd.data_ptr(), 1e-6, q.data_ptr(), s.data_ptr(), M, D, D,
+                              torch.cuda.current_stream().cuda_stream) == 0
+    e2c.check()
+    xn = x.copy()
+    of.port().e2o_rmsnorm(xn.ctypes.data_as(of.f32p), M, D, g.ctypes.data_as(of.f32p), 1e-6)
+    eq, es = of.quantize_signed(xn, D)
+    np.testing.assert_allclose(s.cpu().numpy(), es, rtol=4e-7)
+    pre = xn * (np.float32(127.0) / np.abs(xn).max(axis=1, keepdims=True))
+    tie_tolerant_bytes(q.cpu().numpy(), eq, pre)
+
+
+# ------------------------------------------------------------------------------------------ A8 attention
+def _attn_ref(q, k, v, valid, B, S, H, scale):
+    """fp64 attention over the valid keys of each sequence; invalid query rows are 0."""
+    Dh = 256
+    out = np.zeros((B * S, H * Dh), np.float64)
+    for b in range(B):
+        keys = np.arange(S) if valid is None else np.nonzero(valid[b])[0]
+        kb = k[b * S + keys].astype(np.float64)
+        vb = v[b * S + keys].astype(np.float64)
+        for h in range(H):
+            qh = q[b * S:(b + 1) * S, h * Dh:(h + 1) * Dh].astype(np.float64)
+            if len(keys) == 0:
+                continue
+            lg = qh @ kb.T * scale
+            lg -= lg.max(axis=1, keepdims=True)
+            p = np.exp(lg)
+            p /= p.sum(axis=1, keepdims=True)
+            o = p @ vb
+            if valid is not None:
+                o[valid[b] == 0] = 0
+            out[b * S:(b + 1) * S, h * Dh:(h + 1) * Dh] = o
+    return out
+
+
+@pytest.mark.parametrize("B,S,H,scale,masked", [(2, 300, 3, 1 / 16, True), (3, 512, 3, 1 / 16, False),
+                                                (1, 64, 3, 1 / 16, False), (2, 1, 3, 1 / 16, False),
+                                                (2, 700, 3, 1.0, True), (1, 130, 1, 1 / 16, False)])
+def test_attention_vs_fp64(e2c, torch_cuda, B, S, H, scale, masked):
+    torch = torch_cuda
+    rng = np.random.default_rng(S * 10 + B)
+    Dh = 256
+    qf = torch.from_numpy(rng.standard_normal((B * S, H * Dh)).astype(np.float32)).to(torch.bfloat16)
+    kf = torch.from_numpy(rng.standard_normal((B * S, Dh)).astype(np.float32)).to(torch.bfloat16)
+    vf = torch.from_numpy(rng.standard_normal((B * S, Dh)).astype(np.float32)).to(torch.bfloat16)
+    valid = None
+    if masked:
+        valid = np.ones((B, S), np.uint8)
+        valid[-1, S - S // 6:] = 0
+        valid[0, 5:9] = 0
+    ldvt = (S + 7) // 8 * 8
+    vt = torch.zeros((B, Dh, ldvt), dtype=torch.bfloat16)
+    vt[:, :, :S] = vf.reshape(B, S, Dh).transpose(1, 2)
+    vd = None if valid is None else dev(torch, valid.reshape(-1))
+    ctx = e2c.attention(qf.cuda(), kf.cuda(), vt.cuda(), vd, B, S, H, scale)
+    e2c.check()
+    got = ctx.cpu().numpy()
+    want = _attn_ref(qf.float().numpy(), kf.float().numpy(), vf.float().numpy(), valid, B, S, H, scale)
+    for b in range(B):
+        for h in range(H):
+            rows = slice(b * S, (b + 1) * S)
+            g = got[rows, h * Dh:(h + 1) * Dh]
+            w = want[rows, h * Dh:(h + 1) * Dh]
+            live = np.linalg.norm(w, axis=1) > 0
+            if valid is not None:
+                assert np.all(g[valid[b] == 0] == 0)
+            err = np.linalg.norm(g[live] - w[live], axis=1) / np.linalg.norm(w[live], axis=1)
+            assert err.max() < 1e-2, f"b={b} h={h} worst row rel err {err.max()}"
+            assert cosine_rows(g[live], w[live]).min() > 0.9999
