@@ -212,23 +212,27 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 break;
             }
             tc_fence_after();
+            // Each row (thread) decides whether its running max moves; the O rescale itself is a
+            // warp-collective TMEM round trip (tcgen05.ld/st are .sync.aligned), so the warp runs it
+            // whenever any of its rows needs it, rows that do not with alpha = 1.
+            float alpha = 1.f;
             if (mx > m_used + kRescaleLog2 || (m_used == -INFINITY && mx > -INFINITY)) {
-                const float alpha = m_used == -INFINITY ? 0.f : exp2f(m_used - mx);
+                alpha = m_used == -INFINITY ? 0.f : exp2f(m_used - mx);
                 l *= alpha;
-                if (j > 0) {
-#pragma unroll 1
-                    for (int c = 0; c < HD / 32; c++) {
-                        uint32_t o[32];
-                        const uint32_t ta = tmem + lane_addr + (uint32_t)(2 * TKV + c * 32);
-                        tmem_ld32(ta, o);
-                        tmem_wait_ld();
-#pragma unroll
-                        for (int i = 0; i < 32; i++) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-                        tmem_st32(ta, o);
-                    }
-                    tmem_wait_st();
-                }
                 m_used = mx;
+            }
+            if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+#pragma unroll 1
+                for (int c = 0; c < HD / 32; c++) {
+                    uint32_t o[32];
+                    const uint32_t ta = tmem + lane_addr + (uint32_t)(2 * TKV + c * 32);
+                    tmem_ld32(ta, o);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int i = 0; i < 32; i++) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+                    tmem_st32(ta, o);
+                }
+                tmem_wait_st();
             }
             // probabilities -> bf16 P row (two 128-byte swizzled sub-tiles of 64 keys)
             float lsum = 0.f;

@@ -34,8 +34,12 @@ def test_ffn_block_config1_shape(e2c, of, syn, torch_cuda):
     e2c.check()
     got = y.cpu().numpy()
     want = of.ffn_block(_which(of), x, g, 1e-6, wg, wu, wd, ablk=0)
+    # Rows whose requantised bytes all agree match to rounding; a row where the fp32 RMSNorm or GELU
+    # moved one pre-round value across a .5 tie carries a one-step difference in one byte
     err = np.linalg.norm(got - want, axis=1) / np.linalg.norm(want, axis=1)
-    assert err.max() < 1e-3, f"worst row {err.max()}"
+    assert np.mean(err < 1e-5) > 0.9, f"only {np.mean(err < 1e-5):.3f} of rows agree to rounding"
+    assert err.max() < 5e-3, f"worst row {err.max()}"
+    assert cosine_rows(got, want).min() > 0.99999
     # the FFN's own contribution (y - x), where requantisation differences live
     d_err = np.linalg.norm((got - x) - (want - x)) / np.linalg.norm(want - x)
     assert d_err < 1e-2, d_err

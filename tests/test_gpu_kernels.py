@@ -278,7 +278,7 @@ def test_norm_quant_teacher_forced(e2c, of, torch_cuda):
     xn = x.copy()
     of.port().e2o_rmsnorm(xn.ctypes.data_as(of.f32p), M, D, g.ctypes.data_as(of.f32p), 1e-6)
     eq, es = of.quantize_signed(xn, D)
-    np.testing.assert_allclose(s.cpu().numpy(), es, rtol=4e-7)
+    np.testing.assert_allclose(s.cpu().numpy(), es, rtol=2e-6)  # normed values differ by a few ulp (sum order)
     pre = xn * (np.float32(127.0) / np.abs(xn).max(axis=1, keepdims=True))
     tie_tolerant_bytes(q.cpu().numpy(), eq, pre)
 
