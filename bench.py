@@ -69,7 +69,7 @@ class ClockSampler:
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
@@ -171,12 +171,17 @@ def cpu_reference(seqs: int, seq_len: int, steps: int, warmup: int, weights, rng
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="e2cuda", choices=["e2cuda", "reference"])
     ap.add_argument("--layers", type=int, default=24, help=argparse.SUPPRESS)  # debugging only; headline uses 24
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--kernel", default=None, choices=["gate_up", "qkv", "down", "attention", "quantize"],
+                    help="run one encoder kernel --steps times at the encoder's shapes (for ncu captures)")
+    ap.add_argument("--tokens", type=int, default=BATCH * SEQ, help="tokens for --kernel (a multiple of 512)")
     args = ap.parse_args()
+    if args.kernel:
+        return kernel_only(args)
 
     import torch
 
@@ -343,6 +348,71 @@ def gate_up_roofline(e2c, syn, w, dev, stream) -> dict:
             "peak_src": f"2 x {p['src']} bf16 {p['bf16_tflops']} TFLOP/s (dense int8 rate = 2x bf16)",
             "avg_ms": avg_ms, "algorithmic_bytes": M * D + 4 * M + 2 * I * D + 8 * I + 4 * M * I,
             "traffic": traffic}
+
+
+def kernel_only(args) -> int:
+    """One encoder kernel in isolation (the ncu capture target): prints its CUDA-event average."""
+    import torch
+
+    e2c = load_pkg()
+    import e2c_b200.synthetic as syn
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    M, D, I, Dh, H = args.tokens, 768, 1152, 256, 3
+    g = torch.Generator(device=dev).manual_seed(5)
+    rng = np.random.default_rng(5)
+    stream = torch.cuda.Stream(device=dev)
+
+    def qin(K):
+        return (torch.randint(-127, 128, (M, K), dtype=torch.int8, device=dev, generator=g),
+                torch.rand((M, 1), device=dev, generator=g) * 0.05 + 1e-3)
+
+    if args.kernel in ("gate_up", "qkv", "down"):
+        N, K = {"gate_up": (2 * I, D), "qkv": ((H + 2) * Dh, D), "down": (D, I)}[args.kernel]
+        W = e2c.Weight(w=rng.integers(-127, 128, (N, K), dtype=np.int8), scale=rng.uniform(1e-4, 0.02, N).astype(np.float32))
+        qa, qs = qin(K)
+        a = e2c.gemm_args(W, qa, qs, M)
+        keep = []
+        if args.kernel == "gate_up":
+            y = torch.empty((M, I), dtype=torch.float32, device=dev)
+            a.epi, a.y, a.ldy = e2c.EPI_GELU, y.data_ptr(), I
+        elif args.kernel == "down":
+            y = torch.empty((M, D), dtype=torch.float32, device=dev)
+            a.epi, a.y, a.ldy = e2c.EPI_F32, y.data_ptr(), D
+        else:
+            Q = torch.empty((M, H * Dh), dtype=torch.bfloat16, device=dev)
+            Kt = torch.empty((M, Dh), dtype=torch.bfloat16, device=dev)
+            Vt = torch.empty((M // SEQ, Dh, SEQ), dtype=torch.bfloat16, device=dev)
+            gam = torch.ones(Dh, device=dev)
+            cs = torch.rand((SEQ, Dh // 2), device=dev)
+            keep = [Q, Kt, Vt, gam, cs]
+            a.epi, a.nq, a.q_out, a.k_out, a.vt_out, a.ldvt, a.seq_len = e2c.EPI_QKV, H, Q.data_ptr(), Kt.data_ptr(), Vt.data_ptr(), SEQ, SEQ
+            a.q_gamma = a.k_gamma = gam.data_ptr()
+            a.rope_cos = a.rope_sin = cs.data_ptr()
+            a.eps = 1e-6
+        run = lambda: e2c.gemm_raw(a, stream)
+    elif args.kernel == "attention":
+        B = M // SEQ
+        q = torch.randn((M, H * Dh), device=dev, generator=g).to(torch.bfloat16)
+        k = torch.randn((M, Dh), device=dev, generator=g).to(torch.bfloat16)
+        vt = torch.randn((B, Dh, SEQ), device=dev, generator=g).to(torch.bfloat16)
+        run = lambda: e2c.attention(q, k, vt, None, B, SEQ, H, 1.0 / 16, stream)
+    else:
+        x = torch.randn((M, I), device=dev, generator=g)
+        run = lambda: e2c.quantize_rows(x, I, stream=stream)
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            run()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            run()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    e2c.check(stream)
+    print(json.dumps({"kernel": args.kernel, "tokens": M, "avg_ms": e0.elapsed_time(e1) / max(args.steps, 1)}))
+    return 0
 
 
 if __name__ == "__main__":
