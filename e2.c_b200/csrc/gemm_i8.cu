@@ -14,8 +14,10 @@
 //               a ring of shared-memory stages guarded by full/empty mbarriers;
 //   warp 1      TMEM owner and MMA issuer: 4 x tcgen05.mma (K = 32) per stage into one of two
 //               TMEM accumulators (2 x BN columns of int32), tcgen05.commit frees stages;
-//   warps 2..5  epilogue: tcgen05.ld of their 32 TMEM lanes, dequant and the fused tail
-//               (residual, clamp, GELU-gate, per-head RMSNorm + RoPE), direct stores.
+//   warps 2..9  epilogue, two warps per TMEM lane quadrant, each owning half of the tile's
+//               columns: tcgen05.ld, dequant (weight scales broadcast by warp shuffle) and the fused
+//               tail (residual, clamp, GELU-gate, per-head RMSNorm + RoPE), results staged in a
+//               per-warp swizzled shared-memory tile and written by TMA stores.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -31,24 +33,32 @@ namespace {
 
 constexpr int BM = 128;   // tile rows (tokens) = TMEM lanes
 constexpr int BK = 128;   // bytes of K per stage = one 128-byte swizzle row
-constexpr int NTHREADS = 192;
+constexpr int EPI_WARPS = 8;
+constexpr int NTHREADS = 64 + 32 * EPI_WARPS;
+constexpr int STG_WARP = 4096;  // staging bytes per epilogue warp (32 rows x 128 bytes)
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, int EPI>
 struct GemmSmem {
     static constexpr int A_BYTES = BM * BK;
     static constexpr int B_BYTES = BN * BK;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-    static constexpr int BAR_OFF = STAGES * STAGE_BYTES;
-    // full[S], empty[S], tfull[2], tempty[2], tmem slot
-    static constexpr int BYTES = BAR_OFF + (2 * STAGES + 4) * 8 + 16;
+    static constexpr int STG_PER_WARP = EPI == E2C_EPI_QKV ? 2 * STG_WARP : STG_WARP;
+    static constexpr int STG_OFF = STAGES * STAGE_BYTES;
+    static constexpr int SSQ_OFF = STG_OFF + EPI_WARPS * STG_PER_WARP;
+    static constexpr int SSQ_BYTES = EPI == E2C_EPI_QKV ? 2 * 2 * BM * 4 : 0;  // [acc][half][row]
+    static constexpr int BAR_OFF = SSQ_OFF + SSQ_BYTES;
+    // full[S], empty[S], tfull[2], tempty[2], pair[2][4] (QKV row-norm exchange), tmem slot
+    static constexpr int NBAR = 2 * STAGES + 4 + 8;
+    static constexpr int BYTES = BAR_OFF + NBAR * 8 + 16;
     static constexpr int ALLOC = BYTES + 1024;  // slack for 1024-byte alignment
+    static_assert(ALLOC <= 232448, "shared memory");
 };
 
 // ---------------------------------------------------------------------------------- epilogue math
 // The reference's AVX-512 exp (src/kernels_avx512.c:19-44): two-constant range reduction, degree-5
-// polynomial, exponent-field scaling.
-__device__ __forceinline__ float exp_poly(float x) {
-    x = fminf(fmaxf(x, -87.0f), 88.0f);
+// polynomial, exponent-field scaling. Callers pass x in [0, 32], where the reference's clamp to
+// [-87, 88] is the identity, so it is omitted.
+__device__ __forceinline__ float exp_poly_0_32(float x) {
     const float t = __fmul_rn(x, 1.4426950408889634f);
     const float n = rintf(t);
     float r = __fmaf_rn(-n, 0.6931471805599453f, x);
@@ -64,12 +74,15 @@ __device__ __forceinline__ float exp_poly(float x) {
     const int ni = __float2int_rn(n);
     return __fmul_rn(p, __int_as_float((ni + 127) << 23));
 }
-// GELU-tanh of the reference (src/kernels_avx512.c:46-55,186-203).
+// GELU-tanh of the reference (src/kernels_avx512.c:46-55,186-203): tanh(z) = 1 - 2/(exp(2|z|)+1)
+// with the sign of z, 1 beyond |z| > 15. Past 15 the exp argument is held at 32 (its result is
+// discarded there), which keeps the IEEE division out of its denormal slow path.
 __device__ __forceinline__ float gelu_tanh(float v) {
     const float v3 = __fmul_rn(__fmul_rn(v, v), v);
     const float inner = __fmul_rn(0.7978845608028654f, __fmaf_rn(0.044715f, v3, v));
     const float a = fabsf(inner);
-    const float e = exp_poly(__fadd_rn(a, a));
+    const float ah = fminf(a, 16.0f);
+    const float e = exp_poly_0_32(__fadd_rn(ah, ah));
     float th = __fsub_rn(1.0f, __fdiv_rn(2.0f, __fadd_rn(e, 1.0f)));
     if (a > 15.0f) th = 1.0f;
     th = copysignf(th, inner);
@@ -78,25 +91,51 @@ __device__ __forceinline__ float gelu_tanh(float v) {
 
 __device__ __forceinline__ float dq(uint32_t acc, float s) { return __fmul_rn(__int2float_rn((int)acc), s); }
 
-__device__ __forceinline__ void store_bf16x32(__nv_bfloat16 *dst, const float (&v)[32]) {
-    uint4 *d4 = reinterpret_cast<uint4 *>(dst);
+// Row `lane` of a 32-row x 128-byte staging tile in the TMA 128-byte-swizzle layout: 16-byte chunk c
+// of the row lives at chunk (c ^ (row & 7)).
+__device__ __forceinline__ void stage_row_f32(uint8_t *buf, int lane, const float (&v)[32]) {
+    uint8_t *row = buf + lane * 128;
 #pragma unroll
-    for (int i = 0; i < 4; i++) {
+    for (int c = 0; c < 8; c++)
+        *reinterpret_cast<float4 *>(row + ((c ^ (lane & 7)) << 4)) =
+            make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+}
+// 32 bf16 values into 16-byte chunks [c0, c0 + 4) of the row
+__device__ __forceinline__ void stage_row_bf16(uint8_t *buf, int lane, int c0, const float (&v)[32]) {
+    uint8_t *row = buf + lane * 128;
+#pragma unroll
+    for (int c = 0; c < 4; c++) {
         uint32_t w[4];
 #pragma unroll
         for (int j = 0; j < 4; j++) {
-            const __nv_bfloat162 h = __floats2bfloat162_rn(v[8 * i + 2 * j], v[8 * i + 2 * j + 1]);
+            const __nv_bfloat162 h = __floats2bfloat162_rn(v[8 * c + 2 * j], v[8 * c + 2 * j + 1]);
             w[j] = *reinterpret_cast<const uint32_t *>(&h);
         }
-        d4[i] = make_uint4(w[0], w[1], w[2], w[3]);
+        *reinterpret_cast<uint4 *>(row + (((c0 + c) ^ (lane & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
     }
+}
+// hand a staged tile to the TMA engine (one lane), after every lane's writes are visible to it
+__device__ __forceinline__ void stage_store(const CUtensorMap *m, uint8_t *buf, int x, int y, int lane) {
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+        tma_store_2d(m, smem_u32(buf), x, y);
+        bulk_commit();
+    }
+}
+// before rewriting a staging tile: its previous store has read it
+__device__ __forceinline__ void stage_reuse(int lane) {
+    if (lane == 0) bulk_wait_read0();
+    __syncwarp();
 }
 
 // ---------------------------------------------------------------------------------- kernel
 template <int BN, int STAGES, bool PERBLOCK, int EPI>
 __global__ void __launch_bounds__(NTHREADS, 1)
-    k_gemm_i8(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const e2c_gemm_args p) {
-    using L = GemmSmem<BN, STAGES>;
+    k_gemm_i8(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+              const __grid_constant__ CUtensorMap tmO0, const __grid_constant__ CUtensorMap tmO1, const e2c_gemm_args p,
+              const int tma_out) {
+    using L = GemmSmem<BN, STAGES, EPI>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     const uint32_t sbase = smem_u32(smem);
@@ -105,7 +144,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     auto empty_bar = [&](int s) { return bar0 + 8u * (STAGES + s); };
     auto tfull_bar = [&](int a) { return bar0 + 8u * (2 * STAGES + a); };
     auto tempty_bar = [&](int a) { return bar0 + 8u * (2 * STAGES + 2 + a); };
-    volatile uint32_t *tmem_slot = reinterpret_cast<volatile uint32_t *>(smem + L::BAR_OFF + (2 * STAGES + 4) * 8);
+    auto pair_bar = [&](int a, int q) { return bar0 + 8u * (2 * STAGES + 4 + 4 * a + q); };
+    volatile uint32_t *tmem_slot = reinterpret_cast<volatile uint32_t *>(smem + L::BAR_OFF + L::NBAR * 8);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int M = p.M, K = p.K;
@@ -125,14 +165,15 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         }
         for (int a = 0; a < 2; a++) {
             mbar_init(tfull_bar(a), 1);
-            mbar_init(tempty_bar(a), 128);
+            mbar_init(tempty_bar(a), 32 * EPI_WARPS);
+            for (int q = 0; q < 4; q++) mbar_init(pair_bar(a, q), 64);
         }
         fence_mbar_init();
         tma_prefetch_desc(&tmA);
         tma_prefetch_desc(&tmB);
     }
     if (warp == 1) {
-        tmem_alloc(sbase + L::BAR_OFF + (2 * STAGES + 4) * 8, TMEM_COLS);
+        tmem_alloc(sbase + L::BAR_OFF + L::NBAR * 8, TMEM_COLS);
         tmem_relinquish();
     }
     tc_fence_before();
@@ -227,20 +268,26 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         }
     } else {
         // ------------------------------------------------------------------ epilogue
-        const int q = warp & 3;          // TMEM lane quadrant this warp may access
-        const int row = q * 32 + lane;   // row of the tile = TMEM lane
+        const int q = warp & 3;                  // TMEM lane quadrant this warp may access
+        const int hf = (warp - 2) >> 2;          // which half of the tile's columns it owns
+        const int row = q * 32 + lane;           // row of the tile = TMEM lane
         const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
+        uint8_t *stg = smem + L::STG_OFF + (warp - 2) * L::STG_PER_WARP;
         int acc = 0;
         uint32_t acc_phase = 0;
         bool ok = true;
+        bool pending = false;  // a TMA store of this warp may still be reading its staging tile
         for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
-            const int m = (t / tiles_n) * BM + row;
+            const int mt = (t / tiles_n) * BM;
+            const int m = mt + row;
             const int c0 = p.n0 + (t % tiles_n) * BN;
             const bool mrow = m < M;
+            const int y0 = mt + q * 32;  // first row of this warp's 32
             if constexpr (PERBLOCK) {
-                float f[BN];
+                constexpr int HALF = BN / 2;
+                float f[HALF];
 #pragma unroll
-                for (int j = 0; j < BN; j++) f[j] = 0.f;
+                for (int j = 0; j < HALF; j++) f[j] = 0.f;
                 for (int u = 0; u < nunits; u++) {
                     // warp-uniform outcome: tcgen05.ld below is .sync.aligned
                     if (!__all_sync(0xffffffffu, mbar_wait(tfull_bar(acc), acc_phase, p.status, E2C_ERR_WAIT_EPI))) {
@@ -250,21 +297,23 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     tc_fence_after();
                     const float as = mrow ? __ldg(p.a_scale + (size_t)m * nb + u) : 0.f;
 #pragma unroll
-                    for (int c = 0; c < BN / 32; c++) {
+                    for (int c = 0; c < HALF / 32; c++) {
+                        const int col = hf * HALF + c * 32;
                         uint32_t r[32];
-                        tmem_ld32(tmem_base + lane_addr + (uint32_t)(acc * BN + c * 32), r);
+                        tmem_ld32(tmem_base + lane_addr + (uint32_t)(acc * BN + col), r);
                         tmem_wait_ld();
                         if constexpr (EPI == E2C_EPI_I32) {
                             if (mrow)
                                 for (int j = 0; j < 32; j++) {
-                                    const int n = c0 + c * 32 + j;
+                                    const int n = c0 + col + j;
                                     if (n < p.n1) p.dots[((size_t)m * p.ldd + n) * nb + u] = (int32_t)r[j];
                                 }
                         } else {
+                            const int nl = c0 + col + lane;
+                            const float wsl = nl < p.n1 ? __ldg(p.w_scale + nl) : 0.f;
 #pragma unroll
                             for (int j = 0; j < 32; j++) {
-                                const int n = c0 + c * 32 + j;
-                                const float ws = n < p.n1 ? __ldg(p.w_scale + n) : 0.f;
+                                const float ws = __shfl_sync(0xffffffffu, wsl, j);
                                 f[c * 32 + j] = __fmaf_rn(__int2float_rn((int)r[j]), __fmul_rn(as, ws), f[c * 32 + j]);
                             }
                         }
@@ -278,15 +327,24 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 }
                 if (!ok) break;
                 if constexpr (EPI != E2C_EPI_I32) {
-                    if (mrow) {
 #pragma unroll
-                        for (int j = 0; j < BN; j++) {
-                            const int n = c0 + j;
-                            if (n < p.n1) {
-                                float v = fminf(fmaxf(f[j], p.out_min), p.out_max);
-                                if constexpr (EPI == E2C_EPI_RESID) v = __fadd_rn(v, p.resid[(size_t)m * p.ldr + n]);
-                                p.y[(size_t)m * p.ldy + n] = v;
-                            }
+                    for (int c = 0; c < HALF / 32; c++) {
+                        const int nbase = c0 + hf * HALF + c * 32;
+                        float v[32];
+#pragma unroll
+                        for (int j = 0; j < 32; j++) {
+                            v[j] = fminf(fmaxf(f[c * 32 + j], p.out_min), p.out_max);
+                            if constexpr (EPI == E2C_EPI_RESID)
+                                if (mrow && nbase + j < p.n1) v[j] = __fadd_rn(v[j], p.resid[(size_t)m * p.ldr + nbase + j]);
+                        }
+                        if (tma_out) {
+                            if (pending) stage_reuse(lane);
+                            stage_row_f32(stg, lane, v);
+                            stage_store(&tmO0, stg, nbase - p.n0, y0, lane);
+                            pending = true;
+                        } else if (mrow) {
+                            for (int j = 0; j < 32; j++)
+                                if (nbase + j < p.n1) p.y[(size_t)m * p.ldy + nbase + j] = v[j];
                         }
                     }
                 }
@@ -299,104 +357,135 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 const float as = mrow ? __ldg(p.a_scale + (size_t)m * nb) : 0.f;
                 const uint32_t tbase = tmem_base + lane_addr + (uint32_t)(acc * BN);
                 if constexpr (EPI == E2C_EPI_F32 || EPI == E2C_EPI_RESID || EPI == E2C_EPI_I32) {
+                    constexpr int HALF = BN / 2;
 #pragma unroll 1
-                    for (int c = 0; c < BN / 32; c++) {
+                    for (int c = 0; c < HALF / 32; c++) {
+                        const int col = hf * HALF + c * 32;
                         uint32_t r[32];
-                        tmem_ld32(tbase + c * 32, r);
+                        tmem_ld32(tbase + col, r);
                         tmem_wait_ld();
-                        const int nbase = c0 + c * 32;
-                        if (!mrow || nbase >= p.n1) continue;
+                        const int nbase = c0 + col;
                         if constexpr (EPI == E2C_EPI_I32) {
-                            for (int j = 0; j < 32; j++)
-                                if (nbase + j < p.n1) p.dots[(size_t)m * p.ldd + nbase + j] = (int32_t)r[j];
+                            if (mrow)
+                                for (int j = 0; j < 32; j++)
+                                    if (nbase + j < p.n1) p.dots[(size_t)m * p.ldd + nbase + j] = (int32_t)r[j];
                         } else {
+                            const float wsl = nbase + lane < p.n1 ? __ldg(p.w_scale + nbase + lane) : 0.f;
                             float v[32];
 #pragma unroll
                             for (int j = 0; j < 32; j++) {
-                                const int n = nbase + j;
-                                const float ws = n < p.n1 ? __ldg(p.w_scale + n) : 0.f;
+                                const float ws = __shfl_sync(0xffffffffu, wsl, j);
                                 v[j] = fminf(fmaxf(dq(r[j], __fmul_rn(as, ws)), p.out_min), p.out_max);
                             }
-                            float *yr = p.y + (size_t)m * p.ldy + nbase;
                             if constexpr (EPI == E2C_EPI_RESID) {
-                                const float *rr = p.resid + (size_t)m * p.ldr + nbase;
-                                for (int j = 0; j < 32; j++)
-                                    if (nbase + j < p.n1) v[j] = __fadd_rn(v[j], rr[j]);
+                                if (mrow) {
+                                    const float *rr = p.resid + (size_t)m * p.ldr + nbase;
+                                    for (int j = 0; j < 32; j++)
+                                        if (nbase + j < p.n1) v[j] = __fadd_rn(v[j], rr[j]);
+                                }
                             }
-                            const bool vec = nbase + 32 <= p.n1 && ((reinterpret_cast<uintptr_t>(yr) & 15) == 0);
-                            if (vec) {
-                                float4 *y4 = reinterpret_cast<float4 *>(yr);
-#pragma unroll
-                                for (int j = 0; j < 8; j++) y4[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-                            } else {
+                            if (tma_out) {
+                                if (pending) stage_reuse(lane);
+                                stage_row_f32(stg, lane, v);
+                                stage_store(&tmO0, stg, nbase - p.n0, y0, lane);
+                                pending = true;
+                            } else if (mrow && nbase < p.n1) {
+                                float *yr = p.y + (size_t)m * p.ldy + nbase;
                                 for (int j = 0; j < 32; j++)
                                     if (nbase + j < p.n1) yr[j] = v[j];
                             }
                         }
                     }
                 } else if constexpr (EPI == E2C_EPI_GELU) {
-                    // weight rows are interleaved per 128: [gate c0/2 .. +128 | up c0/2 .. +128]
+                    // weight rows are interleaved per 128: [gate c0/2 .. +128 | up c0/2 .. +128];
+                    // this warp produces outputs [64 hf, 64 hf + 64) of the tile's 128
                     const int h0 = (c0 - p.n0) / 2;
 #pragma unroll 1
-                    for (int c = 0; c < 4; c++) {
+                    for (int c = 0; c < 2; c++) {
+                        const int oc = 64 * hf + 32 * c;
                         uint32_t rg[32], ru[32];
-                        tmem_ld32(tbase + c * 32, rg);
-                        tmem_ld32(tbase + 128 + c * 32, ru);
+                        tmem_ld32(tbase + oc, rg);
+                        tmem_ld32(tbase + 128 + oc, ru);
                         tmem_wait_ld();
-                        if (!mrow) continue;
+                        const float wgl = __ldg(p.w_scale + c0 + oc + lane);
+                        const float wul = __ldg(p.w_scale + c0 + 128 + oc + lane);
                         float h[32];
 #pragma unroll
                         for (int j = 0; j < 32; j++) {
-                            const int ng = c0 + c * 32 + j, nu = ng + 128;
-                            const float g = dq(rg[j], __fmul_rn(as, __ldg(p.w_scale + ng)));
-                            const float u = dq(ru[j], __fmul_rn(as, __ldg(p.w_scale + nu)));
+                            const float g = dq(rg[j], __fmul_rn(as, __shfl_sync(0xffffffffu, wgl, j)));
+                            const float u = dq(ru[j], __fmul_rn(as, __shfl_sync(0xffffffffu, wul, j)));
                             h[j] = __fmul_rn(gelu_tanh(g), u);
                         }
-                        float4 *y4 = reinterpret_cast<float4 *>(p.y + (size_t)m * p.ldy + h0 + c * 32);
+                        if (tma_out) {
+                            if (pending) stage_reuse(lane);
+                            stage_row_f32(stg, lane, h);
+                            stage_store(&tmO0, stg, h0 + oc, y0, lane);
+                            pending = true;
+                        } else if (mrow) {
+                            float4 *y4 = reinterpret_cast<float4 *>(p.y + (size_t)m * p.ldy + h0 + oc);
 #pragma unroll
-                        for (int j = 0; j < 8; j++) y4[j] = make_float4(h[4 * j], h[4 * j + 1], h[4 * j + 2], h[4 * j + 3]);
+                            for (int j = 0; j < 8; j++) y4[j] = make_float4(h[4 * j], h[4 * j + 1], h[4 * j + 2], h[4 * j + 3]);
+                        }
                     }
                 } else if constexpr (EPI == E2C_EPI_QKV) {
-                    // one 256-column tile = one head: q heads, then k, then v
+                    // one 256-column tile = one head (q heads, then k, then v). This warp owns
+                    // rotate-half pairs i in [64 hf, 64 hf + 64) with their partners i + 128.
                     const int head = (c0 - p.n0) / 256;
                     const bool is_k = head == p.nq, is_v = head == p.nq + 1;
                     const float *gamma = is_v ? nullptr : (is_k ? p.k_gamma : p.q_gamma);
                     float ss = 0.f;
 #pragma unroll 1
-                    for (int c = 0; c < 8; c++) {
+                    for (int c = 0; c < 4; c++) {
+                        const int col = (c & 1) * 32 + 64 * hf + (c >> 1) * 128;
                         uint32_t r[32];
-                        tmem_ld32(tbase + c * 32, r);
+                        tmem_ld32(tbase + col, r);
                         tmem_wait_ld();
+                        const float wsl = __ldg(p.w_scale + c0 + col + lane);
 #pragma unroll
                         for (int j = 0; j < 32; j++) {
-                            const float v = dq(r[j], __fmul_rn(as, __ldg(p.w_scale + c0 + c * 32 + j)));
+                            const float v = dq(r[j], __fmul_rn(as, __shfl_sync(0xffffffffu, wsl, j)));
                             ss = __fmaf_rn(v, v, ss);
                         }
                     }
-                    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, 256.0f), p.eps)));
+                    // the row's sum of squares: this warp's half plus its partner's (same rows)
+                    float *ssq = reinterpret_cast<float *>(smem + L::SSQ_OFF) + acc * 2 * BM;
+                    ssq[hf * BM + row] = ss;
+                    mbar_arrive(pair_bar(acc, q));  // release: the partial is visible to the partner
+                    if (!__all_sync(0xffffffffu, mbar_wait(pair_bar(acc, q), acc_phase, p.status, E2C_ERR_WAIT_EPI))) {
+                        ok = false;
+                        break;
+                    }
+                    const float sst = __fadd_rn(ssq[row], ssq[BM + row]);
+                    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sst, 256.0f), p.eps)));
                     const int pos = mrow ? m % p.seq_len : 0;
+                    if (!is_v && tma_out && pending) stage_reuse(lane);
 #pragma unroll 1
-                    for (int c = 0; c < 4; c++) {
+                    for (int c = 0; c < 2; c++) {
+                        const int ia = 64 * hf + 32 * c;  // rotate-half index of this chunk
                         uint32_t ra[32], rb[32];
-                        tmem_ld32(tbase + c * 32, ra);
-                        tmem_ld32(tbase + 128 + c * 32, rb);
+                        tmem_ld32(tbase + ia, ra);
+                        tmem_ld32(tbase + 128 + ia, rb);
                         tmem_wait_ld();
-                        if (!mrow) continue;
+                        const float wal = __ldg(p.w_scale + c0 + ia + lane);
+                        const float wbl = __ldg(p.w_scale + c0 + 128 + ia + lane);
+                        const float gal = gamma ? __ldg(gamma + ia + lane) : 1.f;
+                        const float gbl = gamma ? __ldg(gamma + 128 + ia + lane) : 1.f;
+                        const float *cs = p.rope_cos + (size_t)pos * 128 + ia;
+                        const float *sn = p.rope_sin + (size_t)pos * 128 + ia;
                         float va[32], vb[32];
 #pragma unroll
                         for (int j = 0; j < 32; j++) {
-                            const int i = c * 32 + j;
-                            float a = __fmul_rn(dq(ra[j], __fmul_rn(as, __ldg(p.w_scale + c0 + i))), inv);
-                            float b = __fmul_rn(dq(rb[j], __fmul_rn(as, __ldg(p.w_scale + c0 + 128 + i))), inv);
+                            float a = __fmul_rn(dq(ra[j], __fmul_rn(as, __shfl_sync(0xffffffffu, wal, j))), inv);
+                            float b = __fmul_rn(dq(rb[j], __fmul_rn(as, __shfl_sync(0xffffffffu, wbl, j))), inv);
+                            const float ga = __shfl_sync(0xffffffffu, gal, j), gb = __shfl_sync(0xffffffffu, gbl, j);
                             if (gamma) {
-                                a = __fmul_rn(a, __ldg(gamma + i));
-                                b = __fmul_rn(b, __ldg(gamma + 128 + i));
+                                a = __fmul_rn(a, ga);
+                                b = __fmul_rn(b, gb);
                             }
                             if (!is_v) {
-                                const float cs = __ldg(p.rope_cos + (size_t)pos * 128 + i);
-                                const float sn = __ldg(p.rope_sin + (size_t)pos * 128 + i);
-                                const float oa = __fmaf_rn(a, cs, -__fmul_rn(b, sn));
-                                const float ob = __fmaf_rn(a, sn, __fmul_rn(b, cs));
+                                const float c_ = __ldg(cs + j), s_ = __ldg(sn + j);
+                                const float oa = __fmaf_rn(a, c_, -__fmul_rn(b, s_));
+                                const float ob = __fmaf_rn(a, s_, __fmul_rn(b, c_));
                                 a = oa;
                                 b = ob;
                             }
@@ -404,20 +493,39 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                             vb[j] = b;
                         }
                         if (is_v) {
-                            __nv_bfloat16 *vt = reinterpret_cast<__nv_bfloat16 *>(p.vt_out) +
-                                                (size_t)(m / p.seq_len) * 256 * p.ldvt + pos;
+                            if (mrow) {
+                                __nv_bfloat16 *vt = reinterpret_cast<__nv_bfloat16 *>(p.vt_out) +
+                                                    (size_t)(m / p.seq_len) * 256 * p.ldvt + pos;
 #pragma unroll
-                            for (int j = 0; j < 32; j++) {
-                                vt[(size_t)(c * 32 + j) * p.ldvt] = __float2bfloat16_rn(va[j]);
-                                vt[(size_t)(128 + c * 32 + j) * p.ldvt] = __float2bfloat16_rn(vb[j]);
+                                for (int j = 0; j < 32; j++) {
+                                    vt[(size_t)(ia + j) * p.ldvt] = __float2bfloat16_rn(va[j]);
+                                    vt[(size_t)(128 + ia + j) * p.ldvt] = __float2bfloat16_rn(vb[j]);
+                                }
                             }
-                        } else {
+                        } else if (tma_out) {
+                            stage_row_bf16(stg, lane, 4 * c, va);
+                            stage_row_bf16(stg + STG_WARP, lane, 4 * c, vb);
+                        } else if (mrow) {
                             __nv_bfloat16 *dst = is_k ? reinterpret_cast<__nv_bfloat16 *>(p.k_out) + (size_t)m * 256
                                                       : reinterpret_cast<__nv_bfloat16 *>(p.q_out) +
                                                             (size_t)m * (256 * p.nq) + head * 256;
-                            store_bf16x32(dst + c * 32, va);
-                            store_bf16x32(dst + 128 + c * 32, vb);
+                            for (int j = 0; j < 32; j++) {
+                                dst[ia + j] = __float2bfloat16_rn(va[j]);
+                                dst[128 + ia + j] = __float2bfloat16_rn(vb[j]);
+                            }
                         }
+                    }
+                    if (!is_v && tma_out) {
+                        const CUtensorMap *tm = is_k ? &tmO1 : &tmO0;
+                        const int xb = is_k ? 0 : head * 256;
+                        fence_proxy_async_smem();
+                        __syncwarp();
+                        if (lane == 0) {
+                            tma_store_2d(tm, smem_u32(stg), xb + 64 * hf, y0);
+                            tma_store_2d(tm, smem_u32(stg + STG_WARP), xb + 128 + 64 * hf, y0);
+                            bulk_commit();
+                        }
+                        pending = true;
                     }
                 }
                 tc_fence_before();
@@ -428,7 +536,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 }
             }
         }
-        (void)ok;
+        // the global writes of every store this warp issued complete before the kernel ends
+        if (lane == 0) bulk_wait0();
+        __syncwarp();
     }
 
     tc_fence_before();
@@ -443,7 +553,7 @@ int g_num_sms = 0;
 
 template <int BN, int STAGES, bool PERBLOCK, int EPI>
 int launch(const e2c_gemm_args *a, cudaStream_t st) {
-    using L = GemmSmem<BN, STAGES>;
+    using L = GemmSmem<BN, STAGES, EPI>;
     auto kern = k_gemm_i8<BN, STAGES, PERBLOCK, EPI>;
     static bool attr_set = false;
     if (!attr_set) {
@@ -453,15 +563,35 @@ int launch(const e2c_gemm_args *a, cudaStream_t st) {
         }
         attr_set = true;
     }
-    CUtensorMap ta, tb;
+    CUtensorMap ta, tb, t0, t1;
     if (e2c_tmap_2d(&ta, a->a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)a->K, (uint64_t)a->M, (uint64_t)a->lda,
                     BK, BM) ||
         e2c_tmap_2d(&tb, a->w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)a->K, (uint64_t)a->wrows,
                     (uint64_t)a->ldw, BK, BN))
         return -3;
+    memset(&t0, 0, sizeof t0);
+    memset(&t1, 0, sizeof t1);
+    int tma_out = 0;
+    if (EPI == E2C_EPI_F32 || EPI == E2C_EPI_RESID) {
+        // TMA stores need 16-byte aligned rows and column starts; the tensor ends at n1 so nothing
+        // right of the requested range is written
+        if (a->ldy % 4 == 0 && a->n0 % 4 == 0 && ((uintptr_t)a->y & 15) == 0)
+            tma_out = !e2c_tmap_2d(&t0, a->y + a->n0, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)(a->n1 - a->n0),
+                                   (uint64_t)a->M, (uint64_t)a->ldy * 4, 32, 32);
+    } else if (EPI == E2C_EPI_GELU) {
+        const int width = (a->n1 - a->n0) / 2;
+        if (a->ldy % 4 == 0 && ((uintptr_t)a->y & 15) == 0)
+            tma_out = !e2c_tmap_2d(&t0, a->y, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)width, (uint64_t)a->M,
+                                   (uint64_t)a->ldy * 4, 32, 32);
+    } else if (EPI == E2C_EPI_QKV) {
+        if ((((uintptr_t)a->q_out | (uintptr_t)a->k_out) & 15) == 0)
+            tma_out = !e2c_tmap_2d(&t0, a->q_out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)256 * a->nq,
+                                   (uint64_t)a->M, (uint64_t)512 * a->nq, 64, 32) &&
+                      !e2c_tmap_2d(&t1, a->k_out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 256, (uint64_t)a->M, 512, 64, 32);
+    }
     const int tiles = ((a->M + BM - 1) / BM) * ((a->n1 - a->n0 + BN - 1) / BN);
     const int grid = tiles < g_num_sms ? tiles : g_num_sms;
-    kern<<<grid, NTHREADS, L::ALLOC, st>>>(ta, tb, *a);
+    kern<<<grid, NTHREADS, L::ALLOC, st>>>(ta, tb, t0, t1, *a, tma_out);
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
         e2c_set_msg("gemm launch: %s", cudaGetErrorString(e));
@@ -471,7 +601,7 @@ int launch(const e2c_gemm_args *a, cudaStream_t st) {
 }
 
 int pick_bn(const e2c_gemm_args *a) {
-    if (a->ablk != a->K) return 128;                         // per-block fold keeps BN floats per thread
+    if (a->ablk != a->K) return 128;                         // per-block fold keeps BN/2 floats per thread
     if (a->epi == E2C_EPI_GELU || a->epi == E2C_EPI_QKV) return 256;
     const int ncols = a->n1 - a->n0;
     const int t256 = ((a->M + BM - 1) / BM) * ((ncols + 255) / 256);
@@ -524,7 +654,7 @@ extern "C" int e2c_gemm(const e2c_gemm_args *a, void *stream) {
         if (perblock) return launch<128, 6, true, E2C_EPI_I32>(a, st);
         return bn == 128 ? launch<128, 6, false, E2C_EPI_I32>(a, st) : launch<256, 4, false, E2C_EPI_I32>(a, st);
     case E2C_EPI_GELU:
-        if (perblock || (a->n1 - a->n0) % 256 || a->ldy % 4) {
+        if (perblock || (a->n1 - a->n0) % 256 || a->n0 % 256 || a->ldy % 4) {
             e2c_set_msg("gemm: the GELU-gate epilogue needs per-row scales and 256-column (gate|up) groups");
             return -1;
         }
@@ -534,7 +664,7 @@ extern "C" int e2c_gemm(const e2c_gemm_args *a, void *stream) {
             e2c_set_msg("gemm: the QKV epilogue needs per-row scales, whole heads of 256 and M a multiple of seq_len");
             return -1;
         }
-        return launch<256, 4, false, E2C_EPI_QKV>(a, st);
+        return launch<256, 3, false, E2C_EPI_QKV>(a, st);
     default:
         e2c_set_msg("gemm: unknown epilogue %d", a->epi);
         return -1;

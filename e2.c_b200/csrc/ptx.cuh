@@ -91,6 +91,21 @@ E2C_DEV void tma_load_2d(uint32_t dst, const CUtensorMap *m, int x, int y, uint3
         "l"(reinterpret_cast<uint64_t>(m)), "r"(x), "r"(y), "r"(bar)
         : "memory");
 }
+// 2D tile store from this CTA's shared memory (bulk-group completion). Rows / columns outside the
+// tensor are not written.
+E2C_DEV void tma_store_2d(const CUtensorMap *m, uint32_t src, int x, int y) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                     reinterpret_cast<uint64_t>(m)),
+                 "r"(x), "r"(y), "r"(src)
+                 : "memory");
+}
+E2C_DEV void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// the shared-memory sources of every committed store have been read (the buffer may be rewritten)
+E2C_DEV void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// every committed store has completed
+E2C_DEV void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+E2C_DEV void named_barrier(int id, int nthreads) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory"); }
+
 // generic-proxy shared-memory writes become visible to the async proxy (tcgen05.mma operands)
 E2C_DEV void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
