@@ -3,10 +3,10 @@
 // One CTA per (sequence, query head, 128-query tile). Per 128-key tile j:
 //   S_j = Q K_j^T        bf16 x bf16 -> fp32 in TMEM (two S buffers, so QK of tile j+1 overlaps the
 //                        softmax of tile j)
-//   P_j = exp2(S_j * scale * log2e - m)   online softmax in registers, one thread per query row,
-//                        the running max only moved when it grows by more than 2^8 (then O is
-//                        rescaled in TMEM), P written to shared memory as bf16 in the MMA's
-//                        swizzled K-major layout
+//   P_j = exp2(S_j * scale * log2e - m)   online softmax in registers; the running max m moves only
+//                        when a row's max grows by more than 2^8 (then its O row is rescaled in
+//                        TMEM). P is written back as bf16 into the S buffer it came from, and the PV
+//                        product reads its A operand from tensor memory: no shared-memory round trip.
 //   O  += P_j V_j        fp32 accumulator in TMEM (256 columns)
 // and at the end ctx = O / rowsum in fp32. Keys past the sequence end or with valid == 0 get
 // probability 0; query rows with valid == 0 get ctx 0 (the reference's masking, src/text.c:661-701).
@@ -14,8 +14,9 @@
 // Operands: Q [B*S][H*256] and K [B*S][256] bf16 row-major (head dim contiguous, K-major for QK^T),
 // V^T [B][256][ldvt] bf16 (keys contiguous, K-major for PV) — the QKV GEMM epilogue writes them so.
 //
-// Warps: 0 = TMA for Q and K, 1 = TMA for V^T, 2 = MMA issuer (+TMEM owner), 3..6 = softmax,
-// rescale and epilogue (warp w owns TMEM lanes 32*(w%4) .. +31).
+// Warps: 0 = TMA for Q and K, 1 = TMA for V^T, 2 = MMA issuer (+TMEM owner), 3..10 = softmax,
+// rescale and epilogue: warp w owns TMEM lanes 32*(w%4) .. +31 and, with its partner of the same
+// quadrant, half of every key tile (keys 64*kh .. +63) and half of the output columns.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -31,16 +32,18 @@ namespace {
 constexpr int HD = 256;        // head dim
 constexpr int TQ = 128;        // queries per CTA
 constexpr int TKV = 128;       // keys per tile
-constexpr int NTHREADS = 224;  // 7 warps
+constexpr int SM_WARPS = 8;    // softmax warps
+constexpr int NTHREADS = 96 + 32 * SM_WARPS;
 constexpr float kRescaleLog2 = 8.0f;
 
 // shared memory map (bytes, from a 1024-aligned base)
 constexpr int Q_OFF = 0;                       // 4 x [128 q][64 d]   (16 KB each)
 constexpr int K_OFF = Q_OFF + TQ * HD * 2;     // 4 x [128 k][64 d]
 constexpr int V_OFF = K_OFF + TKV * HD * 2;    // 2 x [256 d][64 k]   (32 KB each)
-constexpr int P_OFF = V_OFF + HD * TKV * 2;    // 2 x [128 q][64 k]   (16 KB each)
-constexpr int BAR_OFF = P_OFF + TQ * TKV * 2;
-enum { B_Q, B_KF, B_KE, B_VF, B_PV, B_SF0, B_SF1, B_SE0, B_SE1, B_PF, B_NUM };
+constexpr int X_OFF = V_OFF + HD * TKV * 2;    // row-max / row-sum exchange [2][2][128] floats
+constexpr int BAR_OFF = X_OFF + 2 * 2 * TQ * 4;
+// Q, K full, K empty, V full, PV done, S full x2, P full, pair x [2][4], final pair x [4]
+enum { B_Q, B_KF, B_KE, B_VF, B_PV, B_SF0, B_SF1, B_PF, B_PAIR, B_FIN = B_PAIR + 8, B_NUM = B_FIN + 4 };
 constexpr int SMEM_BYTES = BAR_OFF + B_NUM * 8 + 16;
 constexpr int SMEM_ALLOC = SMEM_BYTES + 1024;
 
@@ -51,6 +54,12 @@ struct AttnArgs {
     float scale_log2;
     int *status;
 };
+
+E2C_DEV float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
 
 __global__ void __launch_bounds__(NTHREADS, 1)
     k_attention(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -75,9 +84,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         mbar_init(bar(B_PV), 1);
         mbar_init(bar(B_SF0), 1);
         mbar_init(bar(B_SF1), 1);
-        mbar_init(bar(B_SE0), 128);
-        mbar_init(bar(B_SE1), 128);
-        mbar_init(bar(B_PF), 128);
+        mbar_init(bar(B_PF), 32 * SM_WARPS);
+        for (int i = 0; i < 8; i++) mbar_init(bar(B_PAIR + i), 64);
+        for (int i = 0; i < 4; i++) mbar_init(bar(B_FIN + i), 64);
         fence_mbar_init();
         tma_prefetch_desc(&tmQ);
         tma_prefetch_desc(&tmK);
@@ -115,7 +124,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         if (elect_one()) {
             int issued = 0;
             for (int j = 0; j < nkt; j++) {
-                // V buffer is free once PV of tile j-1 completed
+                // the V buffer is free once PV of tile j-1 completed
                 if (j > 0 && !mbar_wait(bar(B_PV), (uint32_t)((j - 1) & 1), p.status, E2C_ERR_WAIT_PRODUCER)) break;
                 mbar_arrive_expect_tx(bar(B_VF), HD * TKV * 2);
                 for (int i = 0; i < 2; i++)
@@ -126,14 +135,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         }
     } else if (warp == 2) {
         // ---------------------------------------------------------------- MMA issuer
+        // Issue order QK0, QK1, PV0, QK2, PV1, QK3, ...: tcgen05.mma from one thread runs in order,
+        // so QK(j+2) overwrites S buffer j%2 only after PV(j) has read P(j) out of it.
         if (elect_one()) {
             constexpr uint32_t id_s = idesc_bf16(TKV), id_o = idesc_bf16(HD);
             bool ok = mbar_wait(bar(B_Q), 0, p.status, E2C_ERR_WAIT_MMA);
             auto issue_qk = [&](int j) -> bool {
                 const int sb = j & 1;
                 if (!mbar_wait(bar(B_KF), (uint32_t)(j & 1), p.status, E2C_ERR_WAIT_MMA)) return false;
-                if (!mbar_wait(bar(sb ? B_SE1 : B_SE0), (uint32_t)(((j >> 1) & 1) ^ 1), p.status, E2C_ERR_WAIT_MMA))
-                    return false;
                 tc_fence_after();
                 const uint32_t d = tmem + (uint32_t)(sb * TKV);
 #pragma unroll
@@ -146,35 +155,38 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 return true;
             };
             if (ok) ok = issue_qk(0);
+            if (ok && nkt > 1) ok = issue_qk(1);
             for (int j = 0; j < nkt && ok; j++) {
-                if (j + 1 < nkt && !(ok = issue_qk(j + 1))) break;
                 if (!mbar_wait(bar(B_PF), (uint32_t)(j & 1), p.status, E2C_ERR_WAIT_MMA) ||
                     !mbar_wait(bar(B_VF), (uint32_t)(j & 1), p.status, E2C_ERR_WAIT_MMA)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
+                const uint32_t pa = tmem + (uint32_t)((j & 1) * TKV);  // P(j): 64 columns of bf16 pairs
 #pragma unroll
                 for (int k = 0; k < TKV / 16; k++) {
-                    const uint32_t pa = sbase + P_OFF + (uint32_t)((k >> 2) * (TQ * 128) + (k & 3) * 32);
                     const uint32_t vb = sbase + V_OFF + (uint32_t)((k >> 2) * (HD * 128) + (k & 3) * 32);
-                    mma_bf16(tmem + 2 * TKV, smem_desc_sw128(pa), smem_desc_sw128(vb), id_o, (j | k) != 0);
+                    mma_bf16_ts(tmem + 2 * TKV, pa + 8 * k, smem_desc_sw128(vb), id_o, (j | k) != 0);
                 }
                 mma_commit(bar(B_PV));
+                if (j + 2 < nkt && !(ok = issue_qk(j + 2))) break;
             }
             if (!ok) {
                 // drain whatever was issued before TMEM is released
-                mma_commit(bar(B_SE0));
-                mbar_wait(bar(B_SE0), 0, nullptr, E2C_ERR_WAIT_DRAIN);
+                mma_commit(bar(B_SF0));
+                mbar_wait(bar(B_SF0), 0, nullptr, E2C_ERR_WAIT_DRAIN);
             }
         }
     } else {
         // ---------------------------------------------------------------- softmax / epilogue
         const int quad = warp & 3;
-        const int r = quad * 32 + lane;  // query row within the tile = TMEM lane
+        const int kh = (warp - 3) >> 2;   // key half of every tile (and output-column half) this warp owns
+        const int r = quad * 32 + lane;   // query row within the tile = TMEM lane
         const uint32_t lane_addr = (uint32_t)(quad * 32) << 16;
         const int qrow = q0 + r;
         const bool row_in = qrow < S;
+        float *xch = reinterpret_cast<float *>(smem + X_OFF);  // [2][2][TQ]
         float m_used = -INFINITY, l = 0.f;
         bool ok = true;
         for (int j = 0; j < nkt; j++) {
@@ -185,36 +197,39 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 break;
             }
             tc_fence_after();
-            float s[TKV];
+            const uint32_t sbuf = tmem + lane_addr + (uint32_t)(sb * TKV);
+            float s[64];
 #pragma unroll
-            for (int c = 0; c < TKV / 32; c++) {
+            for (int c = 0; c < 2; c++) {
                 uint32_t rr[32];
-                tmem_ld32(tmem + lane_addr + (uint32_t)(sb * TKV + c * 32), rr);
+                tmem_ld32(sbuf + 64 * kh + 32 * c, rr);
                 tmem_wait_ld();
 #pragma unroll
                 for (int i = 0; i < 32; i++) s[c * 32 + i] = __uint_as_float(rr[i]);
             }
-            tc_fence_before();
-            mbar_arrive(bar(sb ? B_SE1 : B_SE0));  // S buffer may be overwritten by QK of tile j+2
-            // key mask and scaled logits (log2 units)
-            const int k0 = j * TKV;
+            // masking only where a tile runs past the sequence or a valid mask is given
+            const int k0 = j * TKV + 64 * kh;
+            if (p.valid || k0 + 64 > S) {
+#pragma unroll
+                for (int i = 0; i < 64; i++) {
+                    const int key = k0 + i;
+                    if (!(key < S && (!p.valid || p.valid[row0 + key]))) s[i] = -INFINITY;
+                }
+            }
             float mx = -INFINITY;
 #pragma unroll
-            for (int i = 0; i < TKV; i++) {
-                const int key = k0 + i;
-                const bool kv = key < S && (!p.valid || p.valid[row0 + key]);
-                s[i] = kv ? s[i] * p.scale_log2 : -INFINITY;
-                mx = fmaxf(mx, s[i]);
-            }
-            // P and O may be touched only after PV of tile j-1 finished
-            if (j > 0 && !__all_sync(0xffffffffu, mbar_wait(bar(B_PV), (uint32_t)((j - 1) & 1), p.status, E2C_ERR_WAIT_ATTN))) {
+            for (int i = 0; i < 64; i++) mx = fmaxf(mx, s[i]);
+            // the row max over both key halves, through the partner warp
+            xch[(sb * 2 + kh) * TQ + r] = mx;
+            mbar_arrive(bar(B_PAIR + sb * 4 + quad));
+            if (!__all_sync(0xffffffffu, mbar_wait(bar(B_PAIR + sb * 4 + quad), (uint32_t)((j >> 1) & 1), p.status,
+                                                   E2C_ERR_WAIT_ATTN))) {
                 ok = false;
                 break;
             }
-            tc_fence_after();
-            // Each row (thread) decides whether its running max moves; the O rescale itself is a
-            // warp-collective TMEM round trip (tcgen05.ld/st are .sync.aligned), so the warp runs it
-            // whenever any of its rows needs it, rows that do not with alpha = 1.
+            mx = fmaxf(xch[(sb * 2) * TQ + r], xch[(sb * 2 + 1) * TQ + r]) * p.scale_log2;
+            // Each row decides whether its running max moves; the O rescale is a warp-collective TMEM
+            // round trip (tcgen05.ld/st are .sync.aligned), run when any row of the warp needs it.
             float alpha = 1.f;
             if (mx > m_used + kRescaleLog2 || (m_used == -INFINITY && mx > -INFINITY)) {
                 alpha = m_used == -INFINITY ? 0.f : exp2f(m_used - mx);
@@ -222,10 +237,16 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 m_used = mx;
             }
             if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+                // O may be touched only once PV of tile j-1 completed
+                if (!__all_sync(0xffffffffu, mbar_wait(bar(B_PV), (uint32_t)((j - 1) & 1), p.status, E2C_ERR_WAIT_ATTN))) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
 #pragma unroll 1
-                for (int c = 0; c < HD / 32; c++) {
+                for (int c = 0; c < 4; c++) {
                     uint32_t o[32];
-                    const uint32_t ta = tmem + lane_addr + (uint32_t)(2 * TKV + c * 32);
+                    const uint32_t ta = tmem + lane_addr + (uint32_t)(2 * TKV + 128 * kh + c * 32);
                     tmem_ld32(ta, o);
                     tmem_wait_ld();
 #pragma unroll
@@ -234,50 +255,49 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 }
                 tmem_wait_st();
             }
-            // probabilities -> bf16 P row (two 128-byte swizzled sub-tiles of 64 keys)
+            // probabilities -> bf16 pairs, written over this warp's 64 columns' worth of S: P(j)
+            // occupies columns [32 kh, 32 kh + 32) of the buffer (both halves already read S)
+            const float c = p.scale_log2, mneg = -m_used;
+            const bool live = m_used != -INFINITY;
+            uint32_t pk[32];
             float lsum = 0.f;
-            uint8_t *prow = smem + P_OFF + r * 128;
 #pragma unroll
-            for (int c = 0; c < TKV / 8; c++) {
-                float e[8];
-#pragma unroll
-                for (int i = 0; i < 8; i++) {
-                    const float v = s[c * 8 + i];
-                    e[i] = (v == -INFINITY || m_used == -INFINITY) ? 0.f : exp2f(v - m_used);
-                }
-                uint32_t w[4];
-#pragma unroll
-                for (int i = 0; i < 4; i++) {
-                    const __nv_bfloat162 hv = __floats2bfloat162_rn(e[2 * i], e[2 * i + 1]);
-                    w[i] = *reinterpret_cast<const uint32_t *>(&hv);
-                    const float2 back = __bfloat1622float2(hv);
-                    lsum += back.x + back.y;  // the sum of what the MMA will actually weigh
-                }
-                const int sub = c >> 3, chunk = c & 7;
-                *reinterpret_cast<uint4 *>(prow + sub * (TQ * 128) + ((chunk ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+            for (int i = 0; i < 32; i++) {
+                const float e0 = live ? ex2_approx(__fmaf_rn(s[2 * i], c, mneg)) : 0.f;
+                const float e1 = live ? ex2_approx(__fmaf_rn(s[2 * i + 1], c, mneg)) : 0.f;
+                lsum += e0 + e1;
+                const __nv_bfloat162 hv = __floats2bfloat162_rn(e0, e1);
+                pk[i] = *reinterpret_cast<const uint32_t *>(&hv);
             }
             l += lsum;
-            fence_proxy_async_smem();
+            tmem_st32(tmem + lane_addr + (uint32_t)(sb * TKV + 32 * kh), pk);
+            tmem_wait_st();
             tc_fence_before();
             mbar_arrive(bar(B_PF));
         }
         // ---------------------------------------------------------------- epilogue
         if (ok && __all_sync(0xffffffffu, mbar_wait(bar(B_PV), (uint32_t)((nkt - 1) & 1), p.status, E2C_ERR_WAIT_ATTN))) {
             tc_fence_after();
-            const bool keep = row_in && (!p.valid || p.valid[row0 + qrow]) && l > 0.f;
-            const float inv = keep ? __fdiv_rn(1.0f, l) : 0.f;
-            float *out = p.ctx + ((size_t)row0 + qrow) * (size_t)(p.H * HD) + h * HD;
+            // the row sum over both key halves
+            xch[kh * TQ + r] = l;  // buffer 0; its last use (the row max of an earlier tile) is fenced by B_PV
+            mbar_arrive(bar(B_FIN + quad));
+            if (__all_sync(0xffffffffu, mbar_wait(bar(B_FIN + quad), 0, p.status, E2C_ERR_WAIT_ATTN))) {
+                const float lt = xch[r] + xch[TQ + r];
+                const bool keep = row_in && (!p.valid || p.valid[row0 + qrow]) && lt > 0.f;
+                const float inv = keep ? __fdiv_rn(1.0f, lt) : 0.f;
+                float *out = p.ctx + ((size_t)row0 + qrow) * (size_t)(p.H * HD) + h * HD + 128 * kh;
 #pragma unroll 1
-            for (int c = 0; c < HD / 32; c++) {
-                uint32_t o[32];
-                tmem_ld32(tmem + lane_addr + (uint32_t)(2 * TKV + c * 32), o);
-                tmem_wait_ld();
-                if (row_in) {
-                    float4 *o4 = reinterpret_cast<float4 *>(out + c * 32);
+                for (int c = 0; c < 4; c++) {
+                    uint32_t o[32];
+                    tmem_ld32(tmem + lane_addr + (uint32_t)(2 * TKV + 128 * kh + c * 32), o);
+                    tmem_wait_ld();
+                    if (row_in) {
+                        float4 *o4 = reinterpret_cast<float4 *>(out + c * 32);
 #pragma unroll
-                    for (int i = 0; i < 8; i++)
-                        o4[i] = make_float4(__uint_as_float(o[4 * i]) * inv, __uint_as_float(o[4 * i + 1]) * inv,
-                                            __uint_as_float(o[4 * i + 2]) * inv, __uint_as_float(o[4 * i + 3]) * inv);
+                        for (int i = 0; i < 8; i++)
+                            o4[i] = make_float4(__uint_as_float(o[4 * i]) * inv, __uint_as_float(o[4 * i + 1]) * inv,
+                                                __uint_as_float(o[4 * i + 2]) * inv, __uint_as_float(o[4 * i + 3]) * inv);
+                    }
                 }
             }
         }

@@ -470,8 +470,18 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                         const float wbl = __ldg(p.w_scale + c0 + 128 + ia + lane);
                         const float gal = gamma ? __ldg(gamma + ia + lane) : 1.f;
                         const float gbl = gamma ? __ldg(gamma + 128 + ia + lane) : 1.f;
-                        const float *cs = p.rope_cos + (size_t)pos * 128 + ia;
-                        const float *sn = p.rope_sin + (size_t)pos * 128 + ia;
+                        // this row's 32 table entries as 16-byte loads (each lane reads its own position)
+                        float csv[32], snv[32];
+                        if (!is_v) {
+                            const float4 *cs4 = reinterpret_cast<const float4 *>(p.rope_cos + (size_t)pos * 128 + ia);
+                            const float4 *sn4 = reinterpret_cast<const float4 *>(p.rope_sin + (size_t)pos * 128 + ia);
+#pragma unroll
+                            for (int j = 0; j < 8; j++) {
+                                const float4 c4 = __ldg(cs4 + j), s4 = __ldg(sn4 + j);
+                                csv[4 * j] = c4.x, csv[4 * j + 1] = c4.y, csv[4 * j + 2] = c4.z, csv[4 * j + 3] = c4.w;
+                                snv[4 * j] = s4.x, snv[4 * j + 1] = s4.y, snv[4 * j + 2] = s4.z, snv[4 * j + 3] = s4.w;
+                            }
+                        }
                         float va[32], vb[32];
 #pragma unroll
                         for (int j = 0; j < 32; j++) {
@@ -483,7 +493,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                                 b = __fmul_rn(b, gb);
                             }
                             if (!is_v) {
-                                const float c_ = __ldg(cs + j), s_ = __ldg(sn + j);
+                                const float c_ = csv[j], s_ = snv[j];
                                 const float oa = __fmaf_rn(a, c_, -__fmul_rn(b, s_));
                                 const float ob = __fmaf_rn(a, s_, __fmul_rn(b, c_));
                                 a = oa;
