@@ -63,7 +63,7 @@ E2C_DEV float ex2_approx(float x) {
 
 __global__ void __launch_bounds__(NTHREADS, 1)
     k_attention(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                const __grid_constant__ CUtensorMap tmV, const AttnArgs p) {
+                const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO, const AttnArgs p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     const uint32_t sbase = smem_u32(smem);
@@ -199,13 +199,15 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             tc_fence_after();
             const uint32_t sbuf = tmem + lane_addr + (uint32_t)(sb * TKV);
             float s[64];
-#pragma unroll
-            for (int c = 0; c < 2; c++) {
-                uint32_t rr[32];
-                tmem_ld32(sbuf + 64 * kh + 32 * c, rr);
+            {
+                uint32_t rr[2][32];
+                tmem_ld32(sbuf + 64 * kh, rr[0]);
+                tmem_ld32(sbuf + 64 * kh + 32, rr[1]);
                 tmem_wait_ld();
 #pragma unroll
-                for (int i = 0; i < 32; i++) s[c * 32 + i] = __uint_as_float(rr[i]);
+                for (int c = 0; c < 2; c++)
+#pragma unroll
+                    for (int i = 0; i < 32; i++) s[c * 32 + i] = __uint_as_float(rr[c][i]);
             }
             // masking only where a tile runs past the sequence or a valid mask is given
             const int k0 = j * TKV + 64 * kh;
@@ -286,19 +288,48 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 const bool keep = row_in && (!p.valid || p.valid[row0 + qrow]) && lt > 0.f;
                 const float inv = keep ? __fdiv_rn(1.0f, lt) : 0.f;
                 float *out = p.ctx + ((size_t)row0 + qrow) * (size_t)(p.H * HD) + h * HD + 128 * kh;
-#pragma unroll 1
-                for (int c = 0; c < 4; c++) {
-                    uint32_t o[32];
-                    tmem_ld32(tmem + lane_addr + (uint32_t)(2 * TKV + 128 * kh + c * 32), o);
-                    tmem_wait_ld();
-                    if (row_in) {
-                        float4 *o4 = reinterpret_cast<float4 *>(out + c * 32);
+                // Whole 32-row groups inside the sequence leave through a TMA store staged in the Q
+                // tile (free: every QK product completed before the last PV); a group running past
+                // the sequence end stores row by row so the next sequence's rows stay untouched.
+                const bool tma = q0 + quad * 32 + 32 <= S;
+                uint8_t *stg = smem + Q_OFF + (warp - 3) * 4096;
 #pragma unroll
-                        for (int i = 0; i < 8; i++)
-                            o4[i] = make_float4(__uint_as_float(o[4 * i]) * inv, __uint_as_float(o[4 * i + 1]) * inv,
-                                                __uint_as_float(o[4 * i + 2]) * inv, __uint_as_float(o[4 * i + 3]) * inv);
+                for (int cp = 0; cp < 2; cp++) {
+                    uint32_t o[2][32];
+                    tmem_ld32(tmem + lane_addr + (uint32_t)(2 * TKV + 128 * kh + 64 * cp), o[0]);
+                    tmem_ld32(tmem + lane_addr + (uint32_t)(2 * TKV + 128 * kh + 64 * cp + 32), o[1]);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int h2 = 0; h2 < 2; h2++) {
+                        float v[32];
+#pragma unroll
+                        for (int i = 0; i < 32; i++) v[i] = __uint_as_float(o[h2][i]) * inv;
+                        const int col = 64 * cp + 32 * h2;
+                        if (tma) {
+                            if (cp | h2) {
+                                if (lane == 0) bulk_wait_read0();
+                                __syncwarp();
+                            }
+                            uint8_t *rowp = stg + lane * 128;
+#pragma unroll
+                            for (int c = 0; c < 8; c++)
+                                *reinterpret_cast<float4 *>(rowp + ((c ^ (lane & 7)) << 4)) =
+                                    make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+                            fence_proxy_async_smem();
+                            __syncwarp();
+                            if (lane == 0) {
+                                tma_store_2d(&tmO, smem_u32(stg), h * HD + 128 * kh + col, row0 + q0 + quad * 32);
+                                bulk_commit();
+                            }
+                        } else if (row_in) {
+                            float4 *o4 = reinterpret_cast<float4 *>(out + col);
+#pragma unroll
+                            for (int i = 0; i < 8; i++) o4[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+                        }
                     }
                 }
+                if (lane == 0) bulk_wait0();
+                __syncwarp();
             }
         }
     }
@@ -328,11 +359,16 @@ extern "C" int e2c_attention(const void *q, const void *k, const void *vt, int l
         }
         attr = true;
     }
-    CUtensorMap tq, tk, tv;
+    if ((uintptr_t)ctx & 15) {
+        e2c_set_msg("attention: ctx must be 16-byte aligned");
+        return -1;
+    }
+    CUtensorMap tq, tk, tv, to;
     const uint64_t rows = (uint64_t)B * S;
     if (e2c_tmap_2d(&tq, q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)H * HD, rows, (uint64_t)H * HD * 2, 64, TQ) ||
         e2c_tmap_2d(&tk, k, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, HD, rows, HD * 2, 64, TKV) ||
-        e2c_tmap_2d(&tv, vt, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)S, (uint64_t)B * HD, (uint64_t)ldvt * 2, 64, HD))
+        e2c_tmap_2d(&tv, vt, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)S, (uint64_t)B * HD, (uint64_t)ldvt * 2, 64, HD) ||
+        e2c_tmap_2d(&to, ctx, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)H * HD, rows, (uint64_t)H * HD * 4, 32, 32))
         return -3;
     AttnArgs a;
     a.valid = valid;
@@ -343,7 +379,7 @@ extern "C" int e2c_attention(const void *q, const void *k, const void *vt, int l
     a.scale_log2 = scale * 1.4426950408889634f;
     a.status = status;
     const dim3 grid((S + TQ - 1) / TQ, H, B);
-    k_attention<<<grid, NTHREADS, SMEM_ALLOC, (cudaStream_t)stream>>>(tq, tk, tv, a);
+    k_attention<<<grid, NTHREADS, SMEM_ALLOC, (cudaStream_t)stream>>>(tq, tk, tv, to, a);
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
         e2c_set_msg("attention launch: %s", cudaGetErrorString(e));

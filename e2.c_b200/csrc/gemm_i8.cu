@@ -349,14 +349,33 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     }
                 }
             } else {
+                // values that do not depend on the accumulator are fetched while the MMA still runs:
+                // the row's activation scale and this lane's weight scale of each of the warp's chunks
+                const float as = mrow ? __ldg(p.a_scale + (size_t)m * nb) : 0.f;
+                float wpre[4] = {0.f, 0.f, 0.f, 0.f};
+                if constexpr (EPI == E2C_EPI_F32 || EPI == E2C_EPI_RESID) {
+#pragma unroll
+                    for (int c = 0; c < BN / 64; c++) {
+                        const int n = c0 + hf * (BN / 2) + 32 * c + lane;
+                        wpre[c] = n < p.n1 ? __ldg(p.w_scale + n) : 0.f;
+                    }
+                } else if constexpr (EPI == E2C_EPI_GELU) {
+#pragma unroll
+                    for (int c = 0; c < 2; c++) {
+                        wpre[c] = __ldg(p.w_scale + c0 + 64 * hf + 32 * c + lane);
+                        wpre[2 + c] = __ldg(p.w_scale + c0 + 128 + 64 * hf + 32 * c + lane);
+                    }
+                } else if constexpr (EPI == E2C_EPI_QKV) {
+#pragma unroll
+                    for (int c = 0; c < 4; c++) wpre[c] = __ldg(p.w_scale + c0 + (c & 1) * 32 + 64 * hf + (c >> 1) * 128 + lane);
+                }
                 if (!__all_sync(0xffffffffu, mbar_wait(tfull_bar(acc), acc_phase, p.status, E2C_ERR_WAIT_EPI))) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
-                const float as = mrow ? __ldg(p.a_scale + (size_t)m * nb) : 0.f;
                 const uint32_t tbase = tmem_base + lane_addr + (uint32_t)(acc * BN);
-                if constexpr (EPI == E2C_EPI_F32 || EPI == E2C_EPI_RESID || EPI == E2C_EPI_I32) {
+                if constexpr (EPI == E2C_EPI_I32) {
                     constexpr int HALF = BN / 2;
 #pragma unroll 1
                     for (int c = 0; c < HALF / 32; c++) {
@@ -365,17 +384,27 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                         tmem_ld32(tbase + col, r);
                         tmem_wait_ld();
                         const int nbase = c0 + col;
-                        if constexpr (EPI == E2C_EPI_I32) {
-                            if (mrow)
-                                for (int j = 0; j < 32; j++)
-                                    if (nbase + j < p.n1) p.dots[(size_t)m * p.ldd + nbase + j] = (int32_t)r[j];
-                        } else {
-                            const float wsl = nbase + lane < p.n1 ? __ldg(p.w_scale + nbase + lane) : 0.f;
+                        if (mrow)
+                            for (int j = 0; j < 32; j++)
+                                if (nbase + j < p.n1) p.dots[(size_t)m * p.ldd + nbase + j] = (int32_t)r[j];
+                    }
+                } else if constexpr (EPI == E2C_EPI_F32 || EPI == E2C_EPI_RESID) {
+                    constexpr int HALF = BN / 2;
+                    // two 32-column chunks per TMEM round trip
+#pragma unroll
+                    for (int cp = 0; cp < HALF / 64; cp++) {
+                        uint32_t r2[2][32];
+                        tmem_ld32(tbase + hf * HALF + 64 * cp, r2[0]);
+                        tmem_ld32(tbase + hf * HALF + 64 * cp + 32, r2[1]);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int h2 = 0; h2 < 2; h2++) {
+                            const int nbase = c0 + hf * HALF + 64 * cp + 32 * h2;
                             float v[32];
 #pragma unroll
                             for (int j = 0; j < 32; j++) {
-                                const float ws = __shfl_sync(0xffffffffu, wsl, j);
-                                v[j] = fminf(fmaxf(dq(r[j], __fmul_rn(as, ws)), p.out_min), p.out_max);
+                                const float ws = __shfl_sync(0xffffffffu, wpre[2 * cp + h2], j);
+                                v[j] = fminf(fmaxf(dq(r2[h2][j], __fmul_rn(as, ws)), p.out_min), p.out_max);
                             }
                             if constexpr (EPI == E2C_EPI_RESID) {
                                 if (mrow) {
@@ -400,20 +429,18 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     // weight rows are interleaved per 128: [gate c0/2 .. +128 | up c0/2 .. +128];
                     // this warp produces outputs [64 hf, 64 hf + 64) of the tile's 128
                     const int h0 = (c0 - p.n0) / 2;
-#pragma unroll 1
+#pragma unroll
                     for (int c = 0; c < 2; c++) {
                         const int oc = 64 * hf + 32 * c;
                         uint32_t rg[32], ru[32];
                         tmem_ld32(tbase + oc, rg);
                         tmem_ld32(tbase + 128 + oc, ru);
                         tmem_wait_ld();
-                        const float wgl = __ldg(p.w_scale + c0 + oc + lane);
-                        const float wul = __ldg(p.w_scale + c0 + 128 + oc + lane);
                         float h[32];
 #pragma unroll
                         for (int j = 0; j < 32; j++) {
-                            const float g = dq(rg[j], __fmul_rn(as, __shfl_sync(0xffffffffu, wgl, j)));
-                            const float u = dq(ru[j], __fmul_rn(as, __shfl_sync(0xffffffffu, wul, j)));
+                            const float g = dq(rg[j], __fmul_rn(as, __shfl_sync(0xffffffffu, wpre[c], j)));
+                            const float u = dq(ru[j], __fmul_rn(as, __shfl_sync(0xffffffffu, wpre[2 + c], j)));
                             h[j] = __fmul_rn(gelu_tanh(g), u);
                         }
                         if (tma_out) {
@@ -433,19 +460,25 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     const int head = (c0 - p.n0) / 256;
                     const bool is_k = head == p.nq, is_v = head == p.nq + 1;
                     const float *gamma = is_v ? nullptr : (is_k ? p.k_gamma : p.q_gamma);
-                    float ss = 0.f;
-#pragma unroll 1
-                    for (int c = 0; c < 4; c++) {
-                        const int col = (c & 1) * 32 + 64 * hf + (c >> 1) * 128;
-                        uint32_t r[32];
-                        tmem_ld32(tbase + col, r);
-                        tmem_wait_ld();
-                        const float wsl = __ldg(p.w_scale + c0 + col + lane);
+                    float gpre[4] = {1.f, 1.f, 1.f, 1.f};  // gamma of the chunks (none for v)
+                    if (gamma) {
 #pragma unroll
-                        for (int j = 0; j < 32; j++) {
-                            const float v = dq(r[j], __fmul_rn(as, __shfl_sync(0xffffffffu, wsl, j)));
-                            ss = __fmaf_rn(v, v, ss);
-                        }
+                        for (int c = 0; c < 4; c++) gpre[c] = __ldg(gamma + (c & 1) * 32 + 64 * hf + (c >> 1) * 128 + lane);
+                    }
+                    float ss = 0.f;
+#pragma unroll
+                    for (int c2 = 0; c2 < 2; c2++) {
+                        uint32_t r2[2][32];
+                        tmem_ld32(tbase + 64 * hf + 32 * c2, r2[0]);
+                        tmem_ld32(tbase + 128 + 64 * hf + 32 * c2, r2[1]);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int h2 = 0; h2 < 2; h2++)
+#pragma unroll
+                            for (int j = 0; j < 32; j++) {
+                                const float v = dq(r2[h2][j], __fmul_rn(as, __shfl_sync(0xffffffffu, wpre[2 * h2 + c2], j)));
+                                ss = __fmaf_rn(v, v, ss);
+                            }
                     }
                     // the row's sum of squares: this warp's half plus its partner's (same rows)
                     float *ssq = reinterpret_cast<float *>(smem + L::SSQ_OFF) + acc * 2 * BM;
@@ -459,17 +492,15 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sst, 256.0f), p.eps)));
                     const int pos = mrow ? m % p.seq_len : 0;
                     if (!is_v && tma_out && pending) stage_reuse(lane);
-#pragma unroll 1
+#pragma unroll
                     for (int c = 0; c < 2; c++) {
                         const int ia = 64 * hf + 32 * c;  // rotate-half index of this chunk
                         uint32_t ra[32], rb[32];
                         tmem_ld32(tbase + ia, ra);
                         tmem_ld32(tbase + 128 + ia, rb);
                         tmem_wait_ld();
-                        const float wal = __ldg(p.w_scale + c0 + ia + lane);
-                        const float wbl = __ldg(p.w_scale + c0 + 128 + ia + lane);
-                        const float gal = gamma ? __ldg(gamma + ia + lane) : 1.f;
-                        const float gbl = gamma ? __ldg(gamma + 128 + ia + lane) : 1.f;
+                        const float wal = wpre[c], wbl = wpre[2 + c];
+                        const float gal = gpre[c], gbl = gpre[2 + c];
                         // this row's 32 table entries as 16-byte loads (each lane reads its own position)
                         float csv[32], snv[32];
                         if (!is_v) {

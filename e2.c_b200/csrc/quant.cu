@@ -18,10 +18,8 @@ constexpr float kInv127 = 0x1.020408p-7f;  // fl(1/127)
 __device__ __forceinline__ float clampv(float v, float lo, float hi, bool clamp) {
     return clamp ? (v < lo ? lo : (v > hi ? hi : v)) : v;
 }
-__device__ __forceinline__ int qround(float v, float inv) {
-    int r = __float2int_rn(__fmul_rn(v, inv));
-    return r > 127 ? 127 : (r < -127 ? -127 : r);
-}
+// |v| <= amax, so |v * fl(127/amax)| <= 127 (to within a rounding that rint absorbs): no saturation
+__device__ __forceinline__ int qround(float v, float inv) { return __float2int_rn(__fmul_rn(v, inv)); }
 __device__ __forceinline__ uint32_t pack4(int a, int b, int c, int d, uint32_t bias) {
     return ((((uint32_t)a & 0xffu) | (((uint32_t)b & 0xffu) << 8) | (((uint32_t)c & 0xffu) << 16) |
              (((uint32_t)d & 0xffu) << 24)) ^
@@ -84,12 +82,13 @@ __global__ void __launch_bounds__(256) k_quant_small(const float *__restrict__ x
 }
 
 // Blocks of any multiple of 16 elements (per-row mode: the block is the whole row). Groups of 16
-// are strided over the lanes; up to REG groups per lane stay in registers, beyond that the second
-// pass re-reads (L1-resident).
-template <int REG>
+// are strided over the lanes; a lane holds at most REG groups (REG = ceil(groups / 32), so the whole
+// block stays in registers and x is read once). |x * 127/amax| <= 127 for every x of the block, so
+// the conversion needs no saturation.
+template <int REG, bool CLAMP>
 __global__ void __launch_bounds__(256) k_quant_wide(const float *__restrict__ x, int ldx, int8_t *__restrict__ q,
                                                     int ldq, float *__restrict__ scales, int M, int K, int ablk,
-                                                    float lo, float hi, int clamp, uint32_t bias) {
+                                                    float lo, float hi, uint32_t bias) {
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (warp >= M) return;
     const float *xr = x + (size_t)warp * ldx;
@@ -102,11 +101,7 @@ __global__ void __launch_bounds__(256) k_quant_wide(const float *__restrict__ x,
 #pragma unroll
         for (int i = 0; i < REG; i++) {
             const int g = lane + 32 * i;
-            if (g < ng) load16(xr + kb + 16 * g, v[i], lo, hi, clamp != 0, amax);
-        }
-        for (int g = lane + 32 * REG; g < ng; g += 32) {
-            float t[16];
-            load16(xr + kb + 16 * g, t, lo, hi, clamp != 0, amax);
+            if (g < ng) load16(xr + kb + 16 * g, v[i], lo, hi, CLAMP, amax);
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
@@ -115,12 +110,6 @@ __global__ void __launch_bounds__(256) k_quant_wide(const float *__restrict__ x,
         for (int i = 0; i < REG; i++) {
             const int g = lane + 32 * i;
             if (g < ng) quant16(v[i], inv, qr + kb + 16 * g, bias);
-        }
-        for (int g = lane + 32 * REG; g < ng; g += 32) {
-            float t[16];
-            float dummy = 0.f;
-            load16(xr + kb + 16 * g, t, lo, hi, clamp != 0, dummy);
-            quant16(t, inv, qr + kb + 16 * g, bias);
         }
         if (lane == 0) scales[(size_t)warp * nb + b] = amax > 0.f ? __fmul_rn(amax, kInv127) : 1.0f;
     }
@@ -175,10 +164,26 @@ extern "C" int e2c_quantize(const float *x, int ldx, int8_t *q, int ldq, float *
         case 16: k_quant_small<16><<<grid, block, 0, st>>>(x, ldx, q, ldq, scales, M, K, lo, hi, clamp, bias); break;
         default: k_quant_small<32><<<grid, block, 0, st>>>(x, ldx, q, ldq, scales, M, K, lo, hi, clamp, bias); break;
         }
-    } else if (ablk <= 2048) {
-        k_quant_wide<4><<<grid, block, 0, st>>>(x, ldx, q, ldq, scales, M, K, ablk, lo, hi, clamp, bias);
     } else {
-        k_quant_wide<2><<<grid, block, 0, st>>>(x, ldx, q, ldq, scales, M, K, ablk, lo, hi, clamp, bias);
+        const int reg = (ablk / 16 + 31) / 32;  // groups of 16 per lane
+        if (reg > 16) {
+            e2c_set_msg("quantize: blocks longer than 8192 elements are not supported");
+            return -1;
+        }
+#define E2C_QW(R)                                                                                            \
+    (clamp ? k_quant_wide<R, true><<<grid, block, 0, st>>>(x, ldx, q, ldq, scales, M, K, ablk, lo, hi, bias)   \
+           : k_quant_wide<R, false><<<grid, block, 0, st>>>(x, ldx, q, ldq, scales, M, K, ablk, lo, hi, bias))
+        switch (reg) {
+        case 1: E2C_QW(1); break;
+        case 2: E2C_QW(2); break;
+        case 3: E2C_QW(3); break;
+        case 4: E2C_QW(4); break;
+        case 5: case 6: E2C_QW(6); break;
+        case 7: case 8: E2C_QW(8); break;
+        case 9: case 10: case 11: case 12: E2C_QW(12); break;
+        default: E2C_QW(16); break;  // up to 8192 per block
+        }
+#undef E2C_QW
     }
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
