@@ -14,10 +14,10 @@
 //               a ring of shared-memory stages guarded by full/empty mbarriers;
 //   warp 1      TMEM owner and MMA issuer: 4 x tcgen05.mma (K = 32) per stage into one of two
 //               TMEM accumulators (2 x BN columns of int32), tcgen05.commit frees stages;
-//   warps 2..9  epilogue, two warps per TMEM lane quadrant, each owning half of the tile's
+//   warps 2..17 epilogue, four warps per TMEM lane quadrant, each owning a quarter of the tile's
 //               columns: tcgen05.ld, dequant (weight scales broadcast by warp shuffle) and the fused
 //               tail (residual, clamp, GELU-gate, per-head RMSNorm + RoPE), results staged in a
-//               per-warp swizzled shared-memory tile and written by TMA stores.
+//               per-warp 64-byte-swizzled shared-memory tile and written by TMA stores.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -33,9 +33,9 @@ namespace {
 
 constexpr int BM = 128;   // tile rows (tokens) = TMEM lanes
 constexpr int BK = 128;   // bytes of K per stage = one 128-byte swizzle row
-constexpr int EPI_WARPS = 8;
+constexpr int EPI_WARPS = 16;
 constexpr int NTHREADS = 64 + 32 * EPI_WARPS;
-constexpr int STG_WARP = 4096;  // staging bytes per epilogue warp (32 rows x 128 bytes)
+constexpr int STG_WARP = 2048;  // staging bytes per epilogue warp and store (32 rows x 64 bytes)
 
 template <int BN, int STAGES, int EPI>
 struct GemmSmem {
@@ -45,7 +45,7 @@ struct GemmSmem {
     static constexpr int STG_PER_WARP = EPI == E2C_EPI_QKV ? 2 * STG_WARP : STG_WARP;
     static constexpr int STG_OFF = STAGES * STAGE_BYTES;
     static constexpr int SSQ_OFF = STG_OFF + EPI_WARPS * STG_PER_WARP;
-    static constexpr int SSQ_BYTES = EPI == E2C_EPI_QKV ? 2 * 2 * BM * 4 : 0;  // [acc][half][row]
+    static constexpr int SSQ_BYTES = EPI == E2C_EPI_QKV ? 2 * 4 * BM * 4 : 0;  // [acc][part][row]
     static constexpr int BAR_OFF = SSQ_OFF + SSQ_BYTES;
     // full[S], empty[S], tfull[2], tempty[2], pair[2][4] (QKV row-norm exchange), tmem slot
     static constexpr int NBAR = 2 * STAGES + 4 + 8;
@@ -59,8 +59,11 @@ struct GemmSmem {
 // polynomial, exponent-field scaling. Callers pass x in [0, 32], where the reference's clamp to
 // [-87, 88] is the identity, so it is omitted.
 __device__ __forceinline__ float exp_poly_0_32(float x) {
+    // n = rint(t) and its integer by the 1.5 * 2^23 rounding constant (exact for 0 <= t < 2^22): the
+    // same values as rintf / float-to-int, on the FMA and integer pipes instead of the XU
     const float t = __fmul_rn(x, 1.4426950408889634f);
-    const float n = rintf(t);
+    const float tm = __fadd_rn(t, 12582912.0f);
+    const float n = __fsub_rn(tm, 12582912.0f);
     float r = __fmaf_rn(-n, 0.6931471805599453f, x);
     r = __fmaf_rn(-n, -1.904654299957768e-9f, r);
     float p = 1.9875691500e-4f;
@@ -71,7 +74,7 @@ __device__ __forceinline__ float exp_poly_0_32(float x) {
     p = __fmaf_rn(p, r, 5.0000001201e-1f);
     p = __fmaf_rn(p, __fmul_rn(r, r), r);
     p = __fadd_rn(p, 1.0f);
-    const int ni = __float2int_rn(n);
+    const int ni = __float_as_int(tm) - 0x4B400000;
     return __fmul_rn(p, __int_as_float((ni + 127) << 23));
 }
 // GELU-tanh of the reference (src/kernels_avx512.c:46-55,186-203): tanh(z) = 1 - 2/(exp(2|z|)+1)
@@ -91,27 +94,27 @@ __device__ __forceinline__ float gelu_tanh(float v) {
 
 __device__ __forceinline__ float dq(uint32_t acc, float s) { return __fmul_rn(__int2float_rn((int)acc), s); }
 
-// Row `lane` of a 32-row x 128-byte staging tile in the TMA 128-byte-swizzle layout: 16-byte chunk c
-// of the row lives at chunk (c ^ (row & 7)).
-__device__ __forceinline__ void stage_row_f32(uint8_t *buf, int lane, const float (&v)[32]) {
-    uint8_t *row = buf + lane * 128;
+// Staging tiles are 32 rows x 64 bytes in the TMA 64-byte-swizzle layout (512-byte aligned): the
+// 16-byte chunk c of row r lives at chunk c ^ ((r >> 1) & 3). Row `lane` = the thread's TMEM lane.
+__device__ __forceinline__ void stage_f32x16(uint8_t *buf, int lane, const float (&v)[16]) {
+    uint8_t *row = buf + lane * 64;
 #pragma unroll
-    for (int c = 0; c < 8; c++)
-        *reinterpret_cast<float4 *>(row + ((c ^ (lane & 7)) << 4)) =
+    for (int c = 0; c < 4; c++)
+        *reinterpret_cast<float4 *>(row + ((c ^ ((lane >> 1) & 3)) << 4)) =
             make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
 }
-// 32 bf16 values into 16-byte chunks [c0, c0 + 4) of the row
-__device__ __forceinline__ void stage_row_bf16(uint8_t *buf, int lane, int c0, const float (&v)[32]) {
-    uint8_t *row = buf + lane * 128;
+// 16 bf16 values into chunks [c0, c0 + 2) of the row
+__device__ __forceinline__ void stage_bf16x16(uint8_t *buf, int lane, int c0, const float (&v)[16]) {
+    uint8_t *row = buf + lane * 64;
 #pragma unroll
-    for (int c = 0; c < 4; c++) {
+    for (int c = 0; c < 2; c++) {
         uint32_t w[4];
 #pragma unroll
         for (int j = 0; j < 4; j++) {
             const __nv_bfloat162 h = __floats2bfloat162_rn(v[8 * c + 2 * j], v[8 * c + 2 * j + 1]);
             w[j] = *reinterpret_cast<const uint32_t *>(&h);
         }
-        *reinterpret_cast<uint4 *>(row + (((c0 + c) ^ (lane & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+        *reinterpret_cast<uint4 *>(row + (((c0 + c) ^ ((lane >> 1) & 3)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
     }
 }
 // hand a staged tile to the TMA engine (one lane), after every lane's writes are visible to it
@@ -166,7 +169,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         for (int a = 0; a < 2; a++) {
             mbar_init(tfull_bar(a), 1);
             mbar_init(tempty_bar(a), 32 * EPI_WARPS);
-            for (int q = 0; q < 4; q++) mbar_init(pair_bar(a, q), 64);
+            for (int q = 0; q < 4; q++) mbar_init(pair_bar(a, q), 128);
         }
         fence_mbar_init();
         tma_prefetch_desc(&tmA);
@@ -269,57 +272,57 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     } else {
         // ------------------------------------------------------------------ epilogue
         const int q = warp & 3;                  // TMEM lane quadrant this warp may access
-        const int hf = (warp - 2) >> 2;          // which half of the tile's columns it owns
+        const int part = (warp - 2) >> 2;        // which quarter of the tile's columns it owns
         const int row = q * 32 + lane;           // row of the tile = TMEM lane
         const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
         uint8_t *stg = smem + L::STG_OFF + (warp - 2) * L::STG_PER_WARP;
+        constexpr int QCOLS = BN / 4;            // columns per warp
         int acc = 0;
         uint32_t acc_phase = 0;
         bool ok = true;
         bool pending = false;  // a TMA store of this warp may still be reading its staging tile
+        // stage 16 fp32 columns of this warp's 32 rows and store them at (x, y0)
+        auto put16 = [&](const float (&v)[16], int x, int y0) {
+            if (pending) stage_reuse(lane);
+            stage_f32x16(stg, lane, v);
+            stage_store(&tmO0, stg, x, y0, lane);
+            pending = true;
+        };
         for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
             const int mt = (t / tiles_n) * BM;
             const int m = mt + row;
             const int c0 = p.n0 + (t % tiles_n) * BN;
             const bool mrow = m < M;
             const int y0 = mt + q * 32;  // first row of this warp's 32
+            const int cw = c0 + part * QCOLS;  // first column of this warp (F32 / I32 / per-block)
             if constexpr (PERBLOCK) {
-                constexpr int HALF = BN / 2;
-                float f[HALF];
+                float f[QCOLS];
 #pragma unroll
-                for (int j = 0; j < HALF; j++) f[j] = 0.f;
+                for (int j = 0; j < QCOLS; j++) f[j] = 0.f;
+                const int nl = cw + lane;
+                const float wsl = (EPI != E2C_EPI_I32 && nl < p.n1) ? __ldg(p.w_scale + nl) : 0.f;
                 for (int u = 0; u < nunits; u++) {
+                    const float as = mrow ? __ldg(p.a_scale + (size_t)m * nb + u) : 0.f;
                     // warp-uniform outcome: tcgen05.ld below is .sync.aligned
                     if (!__all_sync(0xffffffffu, mbar_wait(tfull_bar(acc), acc_phase, p.status, E2C_ERR_WAIT_EPI))) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const float as = mrow ? __ldg(p.a_scale + (size_t)m * nb + u) : 0.f;
-#pragma unroll
-                    for (int c = 0; c < HALF / 32; c++) {
-                        const int col = hf * HALF + c * 32;
-                        uint32_t r[32];
-                        tmem_ld32(tmem_base + lane_addr + (uint32_t)(acc * BN + col), r);
-                        tmem_wait_ld();
-                        if constexpr (EPI == E2C_EPI_I32) {
-                            if (mrow)
-                                for (int j = 0; j < 32; j++) {
-                                    const int n = c0 + col + j;
-                                    if (n < p.n1) p.dots[((size_t)m * p.ldd + n) * nb + u] = (int32_t)r[j];
-                                }
-                        } else {
-                            const int nl = c0 + col + lane;
-                            const float wsl = nl < p.n1 ? __ldg(p.w_scale + nl) : 0.f;
-#pragma unroll
-                            for (int j = 0; j < 32; j++) {
-                                const float ws = __shfl_sync(0xffffffffu, wsl, j);
-                                f[c * 32 + j] = __fmaf_rn(__int2float_rn((int)r[j]), __fmul_rn(as, ws), f[c * 32 + j]);
-                            }
-                        }
-                    }
+                    uint32_t r[32];
+                    tmem_ld32(tmem_base + lane_addr + (uint32_t)(acc * BN + part * QCOLS), r);
+                    tmem_wait_ld();
                     tc_fence_before();
                     mbar_arrive(tempty_bar(acc));
+                    if constexpr (EPI == E2C_EPI_I32) {
+                        if (mrow)
+                            for (int j = 0; j < 32; j++)
+                                if (cw + j < p.n1) p.dots[((size_t)m * p.ldd + cw + j) * nb + u] = (int32_t)r[j];
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 32; j++)
+                            f[j] = __fmaf_rn(__int2float_rn((int)r[j]), __fmul_rn(as, __shfl_sync(0xffffffffu, wsl, j)), f[j]);
+                    }
                     if (++acc == 2) {
                         acc = 0;
                         acc_phase ^= 1u;
@@ -328,46 +331,38 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 if (!ok) break;
                 if constexpr (EPI != E2C_EPI_I32) {
 #pragma unroll
-                    for (int c = 0; c < HALF / 32; c++) {
-                        const int nbase = c0 + hf * HALF + c * 32;
-                        float v[32];
+                    for (int h2 = 0; h2 < 2; h2++) {
+                        float v[16];
 #pragma unroll
-                        for (int j = 0; j < 32; j++) {
-                            v[j] = fminf(fmaxf(f[c * 32 + j], p.out_min), p.out_max);
+                        for (int j = 0; j < 16; j++) {
+                            const int n = cw + 16 * h2 + j;
+                            v[j] = fminf(fmaxf(f[16 * h2 + j], p.out_min), p.out_max);
                             if constexpr (EPI == E2C_EPI_RESID)
-                                if (mrow && nbase + j < p.n1) v[j] = __fadd_rn(v[j], p.resid[(size_t)m * p.ldr + nbase + j]);
+                                if (mrow && n < p.n1) v[j] = __fadd_rn(v[j], p.resid[(size_t)m * p.ldr + n]);
                         }
                         if (tma_out) {
-                            if (pending) stage_reuse(lane);
-                            stage_row_f32(stg, lane, v);
-                            stage_store(&tmO0, stg, nbase - p.n0, y0, lane);
-                            pending = true;
+                            put16(v, cw + 16 * h2 - p.n0, y0);
                         } else if (mrow) {
-                            for (int j = 0; j < 32; j++)
-                                if (nbase + j < p.n1) p.y[(size_t)m * p.ldy + nbase + j] = v[j];
+                            for (int j = 0; j < 16; j++)
+                                if (cw + 16 * h2 + j < p.n1) p.y[(size_t)m * p.ldy + cw + 16 * h2 + j] = v[j];
                         }
                     }
                 }
             } else {
                 // values that do not depend on the accumulator are fetched while the MMA still runs:
-                // the row's activation scale and this lane's weight scale of each of the warp's chunks
+                // the row's activation scale and this lane's weight scales for the warp's columns
                 const float as = mrow ? __ldg(p.a_scale + (size_t)m * nb) : 0.f;
-                float wpre[4] = {0.f, 0.f, 0.f, 0.f};
+                float wpre[2] = {0.f, 0.f};
                 if constexpr (EPI == E2C_EPI_F32 || EPI == E2C_EPI_RESID) {
 #pragma unroll
-                    for (int c = 0; c < BN / 64; c++) {
-                        const int n = c0 + hf * (BN / 2) + 32 * c + lane;
+                    for (int c = 0; c < QCOLS / 32; c++) {
+                        const int n = cw + 32 * c + lane;
                         wpre[c] = n < p.n1 ? __ldg(p.w_scale + n) : 0.f;
                     }
-                } else if constexpr (EPI == E2C_EPI_GELU) {
-#pragma unroll
-                    for (int c = 0; c < 2; c++) {
-                        wpre[c] = __ldg(p.w_scale + c0 + 64 * hf + 32 * c + lane);
-                        wpre[2 + c] = __ldg(p.w_scale + c0 + 128 + 64 * hf + 32 * c + lane);
-                    }
-                } else if constexpr (EPI == E2C_EPI_QKV) {
-#pragma unroll
-                    for (int c = 0; c < 4; c++) wpre[c] = __ldg(p.w_scale + c0 + (c & 1) * 32 + 64 * hf + (c >> 1) * 128 + lane);
+                } else if constexpr (EPI == E2C_EPI_GELU || EPI == E2C_EPI_QKV) {
+                    // gate | up (GELU) or the rotate-half pair i, i + 128 (QKV) of this warp's 32 columns
+                    wpre[0] = __ldg(p.w_scale + c0 + 32 * part + lane);
+                    wpre[1] = __ldg(p.w_scale + c0 + 128 + 32 * part + lane);
                 }
                 if (!__all_sync(0xffffffffu, mbar_wait(tfull_bar(acc), acc_phase, p.status, E2C_ERR_WAIT_EPI))) {
                     ok = false;
@@ -376,157 +371,139 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 tc_fence_after();
                 const uint32_t tbase = tmem_base + lane_addr + (uint32_t)(acc * BN);
                 if constexpr (EPI == E2C_EPI_I32) {
-                    constexpr int HALF = BN / 2;
 #pragma unroll 1
-                    for (int c = 0; c < HALF / 32; c++) {
-                        const int col = hf * HALF + c * 32;
+                    for (int c = 0; c < QCOLS / 32; c++) {
                         uint32_t r[32];
-                        tmem_ld32(tbase + col, r);
+                        tmem_ld32(tbase + part * QCOLS + 32 * c, r);
                         tmem_wait_ld();
-                        const int nbase = c0 + col;
+                        const int nbase = cw + 32 * c;
                         if (mrow)
                             for (int j = 0; j < 32; j++)
                                 if (nbase + j < p.n1) p.dots[(size_t)m * p.ldd + nbase + j] = (int32_t)r[j];
                     }
                 } else if constexpr (EPI == E2C_EPI_F32 || EPI == E2C_EPI_RESID) {
-                    constexpr int HALF = BN / 2;
-                    // two 32-column chunks per TMEM round trip
 #pragma unroll
-                    for (int cp = 0; cp < HALF / 64; cp++) {
-                        uint32_t r2[2][32];
-                        tmem_ld32(tbase + hf * HALF + 64 * cp, r2[0]);
-                        tmem_ld32(tbase + hf * HALF + 64 * cp + 32, r2[1]);
+                    for (int c = 0; c < QCOLS / 32; c++) {
+                        uint32_t r[32];
+                        tmem_ld32(tbase + part * QCOLS + 32 * c, r);
                         tmem_wait_ld();
 #pragma unroll
                         for (int h2 = 0; h2 < 2; h2++) {
-                            const int nbase = c0 + hf * HALF + 64 * cp + 32 * h2;
-                            float v[32];
+                            const int nbase = cw + 32 * c + 16 * h2;
+                            float v[16];
 #pragma unroll
-                            for (int j = 0; j < 32; j++) {
-                                const float ws = __shfl_sync(0xffffffffu, wpre[2 * cp + h2], j);
-                                v[j] = fminf(fmaxf(dq(r2[h2][j], __fmul_rn(as, ws)), p.out_min), p.out_max);
+                            for (int j = 0; j < 16; j++) {
+                                const float ws = __shfl_sync(0xffffffffu, wpre[c], 16 * h2 + j);
+                                v[j] = fminf(fmaxf(dq(r[16 * h2 + j], __fmul_rn(as, ws)), p.out_min), p.out_max);
                             }
                             if constexpr (EPI == E2C_EPI_RESID) {
                                 if (mrow) {
                                     const float *rr = p.resid + (size_t)m * p.ldr + nbase;
-                                    for (int j = 0; j < 32; j++)
+                                    for (int j = 0; j < 16; j++)
                                         if (nbase + j < p.n1) v[j] = __fadd_rn(v[j], rr[j]);
                                 }
                             }
                             if (tma_out) {
-                                if (pending) stage_reuse(lane);
-                                stage_row_f32(stg, lane, v);
-                                stage_store(&tmO0, stg, nbase - p.n0, y0, lane);
-                                pending = true;
+                                put16(v, nbase - p.n0, y0);
                             } else if (mrow && nbase < p.n1) {
                                 float *yr = p.y + (size_t)m * p.ldy + nbase;
-                                for (int j = 0; j < 32; j++)
+                                for (int j = 0; j < 16; j++)
                                     if (nbase + j < p.n1) yr[j] = v[j];
                             }
                         }
                     }
                 } else if constexpr (EPI == E2C_EPI_GELU) {
                     // weight rows are interleaved per 128: [gate c0/2 .. +128 | up c0/2 .. +128];
-                    // this warp produces outputs [64 hf, 64 hf + 64) of the tile's 128
+                    // this warp produces outputs [32 part, 32 part + 32) of the tile's 128, 16 at a time
                     const int h0 = (c0 - p.n0) / 2;
 #pragma unroll
-                    for (int c = 0; c < 2; c++) {
-                        const int oc = 64 * hf + 32 * c;
-                        uint32_t rg[32], ru[32];
-                        tmem_ld32(tbase + oc, rg);
-                        tmem_ld32(tbase + 128 + oc, ru);
+                    for (int h2 = 0; h2 < 2; h2++) {
+                        const int oc = 32 * part + 16 * h2;
+                        uint32_t rg[16], ru[16];
+                        tmem_ld16(tbase + oc, rg);
+                        tmem_ld16(tbase + 128 + oc, ru);
                         tmem_wait_ld();
-                        float h[32];
+                        float h[16];
 #pragma unroll
-                        for (int j = 0; j < 32; j++) {
-                            const float g = dq(rg[j], __fmul_rn(as, __shfl_sync(0xffffffffu, wpre[c], j)));
-                            const float u = dq(ru[j], __fmul_rn(as, __shfl_sync(0xffffffffu, wpre[2 + c], j)));
+                        for (int j = 0; j < 16; j++) {
+                            const float g = dq(rg[j], __fmul_rn(as, __shfl_sync(0xffffffffu, wpre[0], 16 * h2 + j)));
+                            const float u = dq(ru[j], __fmul_rn(as, __shfl_sync(0xffffffffu, wpre[1], 16 * h2 + j)));
                             h[j] = __fmul_rn(gelu_tanh(g), u);
                         }
                         if (tma_out) {
-                            if (pending) stage_reuse(lane);
-                            stage_row_f32(stg, lane, h);
-                            stage_store(&tmO0, stg, h0 + oc, y0, lane);
-                            pending = true;
+                            put16(h, h0 + oc, y0);
                         } else if (mrow) {
                             float4 *y4 = reinterpret_cast<float4 *>(p.y + (size_t)m * p.ldy + h0 + oc);
 #pragma unroll
-                            for (int j = 0; j < 8; j++) y4[j] = make_float4(h[4 * j], h[4 * j + 1], h[4 * j + 2], h[4 * j + 3]);
+                            for (int j = 0; j < 4; j++) y4[j] = make_float4(h[4 * j], h[4 * j + 1], h[4 * j + 2], h[4 * j + 3]);
                         }
                     }
                 } else if constexpr (EPI == E2C_EPI_QKV) {
                     // one 256-column tile = one head (q heads, then k, then v). This warp owns
-                    // rotate-half pairs i in [64 hf, 64 hf + 64) with their partners i + 128.
+                    // rotate-half pairs i in [32 part, 32 part + 32) with their partners i + 128.
                     const int head = (c0 - p.n0) / 256;
                     const bool is_k = head == p.nq, is_v = head == p.nq + 1;
                     const float *gamma = is_v ? nullptr : (is_k ? p.k_gamma : p.q_gamma);
-                    float gpre[4] = {1.f, 1.f, 1.f, 1.f};  // gamma of the chunks (none for v)
-                    if (gamma) {
-#pragma unroll
-                        for (int c = 0; c < 4; c++) gpre[c] = __ldg(gamma + (c & 1) * 32 + 64 * hf + (c >> 1) * 128 + lane);
-                    }
+                    const float gal = gamma ? __ldg(gamma + 32 * part + lane) : 1.f;
+                    const float gbl = gamma ? __ldg(gamma + 128 + 32 * part + lane) : 1.f;
                     float ss = 0.f;
 #pragma unroll
-                    for (int c2 = 0; c2 < 2; c2++) {
-                        uint32_t r2[2][32];
-                        tmem_ld32(tbase + 64 * hf + 32 * c2, r2[0]);
-                        tmem_ld32(tbase + 128 + 64 * hf + 32 * c2, r2[1]);
+                    for (int h2 = 0; h2 < 2; h2++) {
+                        uint32_t ra[16], rb[16];
+                        tmem_ld16(tbase + 32 * part + 16 * h2, ra);
+                        tmem_ld16(tbase + 128 + 32 * part + 16 * h2, rb);
                         tmem_wait_ld();
 #pragma unroll
-                        for (int h2 = 0; h2 < 2; h2++)
-#pragma unroll
-                            for (int j = 0; j < 32; j++) {
-                                const float v = dq(r2[h2][j], __fmul_rn(as, __shfl_sync(0xffffffffu, wpre[2 * h2 + c2], j)));
-                                ss = __fmaf_rn(v, v, ss);
-                            }
+                        for (int j = 0; j < 16; j++) {
+                            const float a = dq(ra[j], __fmul_rn(as, __shfl_sync(0xffffffffu, wpre[0], 16 * h2 + j)));
+                            const float b = dq(rb[j], __fmul_rn(as, __shfl_sync(0xffffffffu, wpre[1], 16 * h2 + j)));
+                            ss = __fmaf_rn(b, b, __fmaf_rn(a, a, ss));
+                        }
                     }
-                    // the row's sum of squares: this warp's half plus its partner's (same rows)
-                    float *ssq = reinterpret_cast<float *>(smem + L::SSQ_OFF) + acc * 2 * BM;
-                    ssq[hf * BM + row] = ss;
-                    mbar_arrive(pair_bar(acc, q));  // release: the partial is visible to the partner
+                    // the row's sum of squares over the four warps of this quadrant (same rows)
+                    float *ssq = reinterpret_cast<float *>(smem + L::SSQ_OFF) + acc * 4 * BM;
+                    ssq[part * BM + row] = ss;
+                    mbar_arrive(pair_bar(acc, q));  // release: the partial is visible to the others
                     if (!__all_sync(0xffffffffu, mbar_wait(pair_bar(acc, q), acc_phase, p.status, E2C_ERR_WAIT_EPI))) {
                         ok = false;
                         break;
                     }
-                    const float sst = __fadd_rn(ssq[row], ssq[BM + row]);
+                    const float sst = __fadd_rn(__fadd_rn(ssq[row], ssq[BM + row]), __fadd_rn(ssq[2 * BM + row], ssq[3 * BM + row]));
                     const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sst, 256.0f), p.eps)));
                     const int pos = mrow ? m % p.seq_len : 0;
                     if (!is_v && tma_out && pending) stage_reuse(lane);
 #pragma unroll
-                    for (int c = 0; c < 2; c++) {
-                        const int ia = 64 * hf + 32 * c;  // rotate-half index of this chunk
-                        uint32_t ra[32], rb[32];
-                        tmem_ld32(tbase + ia, ra);
-                        tmem_ld32(tbase + 128 + ia, rb);
+                    for (int h2 = 0; h2 < 2; h2++) {
+                        const int ia = 32 * part + 16 * h2;  // rotate-half index of these 16 pairs
+                        uint32_t ra[16], rb[16];
+                        tmem_ld16(tbase + ia, ra);
+                        tmem_ld16(tbase + 128 + ia, rb);
                         tmem_wait_ld();
-                        const float wal = wpre[c], wbl = wpre[2 + c];
-                        const float gal = gpre[c], gbl = gpre[2 + c];
-                        // this row's 32 table entries as 16-byte loads (each lane reads its own position)
-                        float csv[32], snv[32];
+                        float csv[16], snv[16];
                         if (!is_v) {
                             const float4 *cs4 = reinterpret_cast<const float4 *>(p.rope_cos + (size_t)pos * 128 + ia);
                             const float4 *sn4 = reinterpret_cast<const float4 *>(p.rope_sin + (size_t)pos * 128 + ia);
 #pragma unroll
-                            for (int j = 0; j < 8; j++) {
+                            for (int j = 0; j < 4; j++) {
                                 const float4 c4 = __ldg(cs4 + j), s4 = __ldg(sn4 + j);
                                 csv[4 * j] = c4.x, csv[4 * j + 1] = c4.y, csv[4 * j + 2] = c4.z, csv[4 * j + 3] = c4.w;
                                 snv[4 * j] = s4.x, snv[4 * j + 1] = s4.y, snv[4 * j + 2] = s4.z, snv[4 * j + 3] = s4.w;
                             }
                         }
-                        float va[32], vb[32];
+                        float va[16], vb[16];
 #pragma unroll
-                        for (int j = 0; j < 32; j++) {
-                            float a = __fmul_rn(dq(ra[j], __fmul_rn(as, __shfl_sync(0xffffffffu, wal, j))), inv);
-                            float b = __fmul_rn(dq(rb[j], __fmul_rn(as, __shfl_sync(0xffffffffu, wbl, j))), inv);
-                            const float ga = __shfl_sync(0xffffffffu, gal, j), gb = __shfl_sync(0xffffffffu, gbl, j);
+                        for (int j = 0; j < 16; j++) {
+                            const int jj = 16 * h2 + j;
+                            float a = __fmul_rn(dq(ra[j], __fmul_rn(as, __shfl_sync(0xffffffffu, wpre[0], jj))), inv);
+                            float b = __fmul_rn(dq(rb[j], __fmul_rn(as, __shfl_sync(0xffffffffu, wpre[1], jj))), inv);
+                            const float ga = __shfl_sync(0xffffffffu, gal, jj), gb = __shfl_sync(0xffffffffu, gbl, jj);
                             if (gamma) {
                                 a = __fmul_rn(a, ga);
                                 b = __fmul_rn(b, gb);
                             }
                             if (!is_v) {
-                                const float c_ = csv[j], s_ = snv[j];
-                                const float oa = __fmaf_rn(a, c_, -__fmul_rn(b, s_));
-                                const float ob = __fmaf_rn(a, s_, __fmul_rn(b, c_));
+                                const float oa = __fmaf_rn(a, csv[j], -__fmul_rn(b, snv[j]));
+                                const float ob = __fmaf_rn(a, snv[j], __fmul_rn(b, csv[j]));
                                 a = oa;
                                 b = ob;
                             }
@@ -538,19 +515,19 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                                 __nv_bfloat16 *vt = reinterpret_cast<__nv_bfloat16 *>(p.vt_out) +
                                                     (size_t)(m / p.seq_len) * 256 * p.ldvt + pos;
 #pragma unroll
-                                for (int j = 0; j < 32; j++) {
+                                for (int j = 0; j < 16; j++) {
                                     vt[(size_t)(ia + j) * p.ldvt] = __float2bfloat16_rn(va[j]);
                                     vt[(size_t)(128 + ia + j) * p.ldvt] = __float2bfloat16_rn(vb[j]);
                                 }
                             }
                         } else if (tma_out) {
-                            stage_row_bf16(stg, lane, 4 * c, va);
-                            stage_row_bf16(stg + STG_WARP, lane, 4 * c, vb);
+                            stage_bf16x16(stg, lane, 2 * h2, va);
+                            stage_bf16x16(stg + STG_WARP, lane, 2 * h2, vb);
                         } else if (mrow) {
                             __nv_bfloat16 *dst = is_k ? reinterpret_cast<__nv_bfloat16 *>(p.k_out) + (size_t)m * 256
                                                       : reinterpret_cast<__nv_bfloat16 *>(p.q_out) +
                                                             (size_t)m * (256 * p.nq) + head * 256;
-                            for (int j = 0; j < 32; j++) {
+                            for (int j = 0; j < 16; j++) {
                                 dst[ia + j] = __float2bfloat16_rn(va[j]);
                                 dst[128 + ia + j] = __float2bfloat16_rn(vb[j]);
                             }
@@ -562,8 +539,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                         fence_proxy_async_smem();
                         __syncwarp();
                         if (lane == 0) {
-                            tma_store_2d(tm, smem_u32(stg), xb + 64 * hf, y0);
-                            tma_store_2d(tm, smem_u32(stg + STG_WARP), xb + 128 + 64 * hf, y0);
+                            tma_store_2d(tm, smem_u32(stg), xb + 32 * part, y0);
+                            tma_store_2d(tm, smem_u32(stg + STG_WARP), xb + 128 + 32 * part, y0);
                             bulk_commit();
                         }
                         pending = true;
@@ -617,18 +594,18 @@ int launch(const e2c_gemm_args *a, cudaStream_t st) {
         // TMA stores need 16-byte aligned rows and column starts; the tensor ends at n1 so nothing
         // right of the requested range is written
         if (a->ldy % 4 == 0 && a->n0 % 4 == 0 && ((uintptr_t)a->y & 15) == 0)
-            tma_out = !e2c_tmap_2d(&t0, a->y + a->n0, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)(a->n1 - a->n0),
-                                   (uint64_t)a->M, (uint64_t)a->ldy * 4, 32, 32);
+            tma_out = !e2c_tmap_2d_sw64(&t0, a->y + a->n0, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)(a->n1 - a->n0),
+                                        (uint64_t)a->M, (uint64_t)a->ldy * 4, 16, 32);
     } else if (EPI == E2C_EPI_GELU) {
         const int width = (a->n1 - a->n0) / 2;
         if (a->ldy % 4 == 0 && ((uintptr_t)a->y & 15) == 0)
-            tma_out = !e2c_tmap_2d(&t0, a->y, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)width, (uint64_t)a->M,
-                                   (uint64_t)a->ldy * 4, 32, 32);
+            tma_out = !e2c_tmap_2d_sw64(&t0, a->y, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)width, (uint64_t)a->M,
+                                        (uint64_t)a->ldy * 4, 16, 32);
     } else if (EPI == E2C_EPI_QKV) {
         if ((((uintptr_t)a->q_out | (uintptr_t)a->k_out) & 15) == 0)
-            tma_out = !e2c_tmap_2d(&t0, a->q_out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)256 * a->nq,
-                                   (uint64_t)a->M, (uint64_t)512 * a->nq, 64, 32) &&
-                      !e2c_tmap_2d(&t1, a->k_out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 256, (uint64_t)a->M, 512, 64, 32);
+            tma_out = !e2c_tmap_2d_sw64(&t0, a->q_out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)256 * a->nq,
+                                        (uint64_t)a->M, (uint64_t)512 * a->nq, 32, 32) &&
+                      !e2c_tmap_2d_sw64(&t1, a->k_out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 256, (uint64_t)a->M, 512, 32, 32);
     }
     const int tiles = ((a->M + BM - 1) / BM) * ((a->n1 - a->n0 + BN - 1) / BN);
     const int grid = tiles < g_num_sms ? tiles : g_num_sms;
@@ -642,7 +619,7 @@ int launch(const e2c_gemm_args *a, cudaStream_t st) {
 }
 
 int pick_bn(const e2c_gemm_args *a) {
-    if (a->ablk != a->K) return 128;                         // per-block fold keeps BN/2 floats per thread
+    if (a->ablk != a->K) return 128;                         // per-block fold keeps BN/4 floats per thread
     if (a->epi == E2C_EPI_GELU || a->epi == E2C_EPI_QKV) return 256;
     const int ncols = a->n1 - a->n0;
     const int t256 = ((a->M + BM - 1) / BM) * ((ncols + 255) / 256);

@@ -12,6 +12,9 @@ extern "C" {
 // be 128 bytes) and zero fill outside the tensor. Returns 0, or -1 with a message in e2c_msg().
 int e2c_tmap_2d(CUtensorMap *m, const void *base, CUtensorMapDataType dt, int elem_bytes, uint64_t inner,
                 uint64_t outer, uint64_t row_stride, uint32_t box_inner, uint32_t box_outer);
+// The same with the 64-byte swizzle (box_inner * elem must be 64 bytes).
+int e2c_tmap_2d_sw64(CUtensorMap *m, const void *base, CUtensorMapDataType dt, int elem_bytes, uint64_t inner,
+                     uint64_t outer, uint64_t row_stride, uint32_t box_inner, uint32_t box_outer);
 
 #ifdef __cplusplus
 }
