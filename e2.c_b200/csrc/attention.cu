@@ -1,12 +1,14 @@
 // attention.cu — bidirectional GQA attention on the sm_100a tensor cores (tcgen05.mma kind::f16).
 //
-// One CTA per (sequence, query head, 128-query tile). Per 128-key tile j:
+// One CTA per (sequence, query head, 128-query tile). Keys are swept in tiles of 64, K and V^T
+// double-buffered in shared memory so the next tile's loads overlap the current tile's products.
+// Per key tile j:
 //   S_j = Q K_j^T        bf16 x bf16 -> fp32 in TMEM (two S buffers, so QK of tile j+1 overlaps the
 //                        softmax of tile j)
 //   P_j = exp2(S_j * scale * log2e - m)   online softmax in registers; the running max m moves only
 //                        when a row's max grows by more than 2^8 (then its O row is rescaled in
 //                        TMEM). P is written back as bf16 into the S buffer it came from, and the PV
-//                        product reads its A operand from tensor memory: no shared-memory round trip.
+//                        product reads its A operand from tensor memory.
 //   O  += P_j V_j        fp32 accumulator in TMEM (256 columns)
 // and at the end ctx = O / rowsum in fp32. Keys past the sequence end or with valid == 0 get
 // probability 0; query rows with valid == 0 get ctx 0 (the reference's masking, src/text.c:661-701).
@@ -16,7 +18,7 @@
 //
 // Warps: 0 = TMA for Q and K, 1 = TMA for V^T, 2 = MMA issuer (+TMEM owner), 3..10 = softmax,
 // rescale and epilogue: warp w owns TMEM lanes 32*(w%4) .. +31 and, with its partner of the same
-// quadrant, half of every key tile (keys 64*kh .. +63) and half of the output columns.
+// quadrant, half of every key tile (keys 32*kh .. +31) and half of the output columns.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -31,19 +33,36 @@ namespace {
 
 constexpr int HD = 256;        // head dim
 constexpr int TQ = 128;        // queries per CTA
-constexpr int TKV = 128;       // keys per tile
+constexpr int TKV = 64;        // keys per tile
 constexpr int SM_WARPS = 8;    // softmax warps
 constexpr int NTHREADS = 96 + 32 * SM_WARPS;
 constexpr float kRescaleLog2 = 8.0f;
 
 // shared memory map (bytes, from a 1024-aligned base)
-constexpr int Q_OFF = 0;                       // 4 x [128 q][64 d]   (16 KB each)
-constexpr int K_OFF = Q_OFF + TQ * HD * 2;     // 4 x [128 k][64 d]
-constexpr int V_OFF = K_OFF + TKV * HD * 2;    // 2 x [256 d][64 k]   (32 KB each)
-constexpr int X_OFF = V_OFF + HD * TKV * 2;    // row-max / row-sum exchange [2][2][128] floats
+constexpr int Q_OFF = 0;                           // 4 x [128 q][64 d]   (16 KB each)
+constexpr int K_TILE = TKV * HD * 2;               // 4 x [64 k][64 d]    (8 KB each)
+constexpr int V_TILE = HD * TKV * 2;               // [256 d][64 k]       (32 KB)
+constexpr int K_OFF = Q_OFF + TQ * HD * 2;         // 2 buffers
+constexpr int V_OFF = K_OFF + 2 * K_TILE;          // 2 buffers
+constexpr int X_OFF = V_OFF + 2 * V_TILE;          // row-max / row-sum exchange [2][2][128] floats
 constexpr int BAR_OFF = X_OFF + 2 * 2 * TQ * 4;
-// Q, K full, K empty, V full, PV done, S full x2, P full, pair x [2][4], final pair x [4]
-enum { B_Q, B_KF, B_KE, B_VF, B_PV, B_SF0, B_SF1, B_PF, B_PAIR, B_FIN = B_PAIR + 8, B_NUM = B_FIN + 4 };
+// Q, K full x2, K empty x2, V full x2, V empty x2, PV done x2, S full x2, P full x2, pair [2][4],
+// final [4], drain. Every per-tile barrier comes in two, indexed by tile parity: a waiter may then
+// trail the arriving side by up to one tile without two phases completing under it.
+enum {
+    B_Q,
+    B_KF,
+    B_KE = B_KF + 2,
+    B_VF = B_KE + 2,
+    B_VE = B_VF + 2,
+    B_PV = B_VE + 2,
+    B_SF = B_PV + 2,
+    B_PF = B_SF + 2,
+    B_PAIR = B_PF + 2,
+    B_FIN = B_PAIR + 8,
+    B_DRAIN = B_FIN + 4,
+    B_NUM
+};
 constexpr int SMEM_BYTES = BAR_OFF + B_NUM * 8 + 16;
 constexpr int SMEM_ALLOC = SMEM_BYTES + 1024;
 
@@ -78,13 +97,16 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 
     if (warp == 0 && lane == 0) {
         mbar_init(bar(B_Q), 1);
-        mbar_init(bar(B_KF), 1);
-        mbar_init(bar(B_KE), 1);
-        mbar_init(bar(B_VF), 1);
-        mbar_init(bar(B_PV), 1);
-        mbar_init(bar(B_SF0), 1);
-        mbar_init(bar(B_SF1), 1);
-        mbar_init(bar(B_PF), 32 * SM_WARPS);
+        for (int i = 0; i < 2; i++) {
+            mbar_init(bar(B_KF + i), 1);
+            mbar_init(bar(B_KE + i), 1);
+            mbar_init(bar(B_VF + i), 1);
+            mbar_init(bar(B_VE + i), 1);
+            mbar_init(bar(B_SF + i), 1);
+            mbar_init(bar(B_PV + i), 1);
+            mbar_init(bar(B_PF + i), 32 * SM_WARPS);
+        }
+        mbar_init(bar(B_DRAIN), 1);
         for (int i = 0; i < 8; i++) mbar_init(bar(B_PAIR + i), 64);
         for (int i = 0; i < 4; i++) mbar_init(bar(B_FIN + i), 64);
         fence_mbar_init();
@@ -99,7 +121,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    const uint32_t tmem = *tmem_slot;  // S0: cols 0..127, S1: 128..255, O: 256..511
+    const uint32_t tmem = *tmem_slot;  // S0: cols 0..63, S1: 64..127, O: 256..511
 
     if (warp == 0) {
         // ---------------------------------------------------------------- Q and K loads
@@ -109,29 +131,33 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 tma_load_2d(sbase + Q_OFF + i * (TQ * 128), &tmQ, h * HD + 64 * i, row0 + q0, bar(B_Q));
             int issued = 0;
             for (int j = 0; j < nkt; j++) {
-                if (!mbar_wait(bar(B_KE), (uint32_t)((j & 1) ^ 1), p.status, E2C_ERR_WAIT_PRODUCER)) break;
-                mbar_arrive_expect_tx(bar(B_KF), TKV * HD * 2);
+                const int kb = j & 1;
+                // buffer kb is free once QK of tile j-2 completed
+                if (!mbar_wait(bar(B_KE + kb), (uint32_t)(((j >> 1) & 1) ^ 1), p.status, E2C_ERR_WAIT_PRODUCER)) break;
+                mbar_arrive_expect_tx(bar(B_KF + kb), K_TILE);
                 for (int i = 0; i < 4; i++)
-                    tma_load_2d(sbase + K_OFF + i * (TKV * 128), &tmK, 64 * i, row0 + j * TKV, bar(B_KF));
+                    tma_load_2d(sbase + K_OFF + kb * K_TILE + i * (TKV * 128), &tmK, 64 * i, row0 + j * TKV, bar(B_KF + kb));
                 issued = j + 1;
             }
-            // the last K load (and Q) must have landed before the CTA may exit
+            // the last loads (and Q) must have landed before the CTA may exit
             mbar_wait(bar(B_Q), 0, nullptr, E2C_ERR_WAIT_DRAIN);
-            if (issued) mbar_wait(bar(B_KF), (uint32_t)((issued - 1) & 1), nullptr, E2C_ERR_WAIT_DRAIN);
+            for (int j = issued - 2 < 0 ? 0 : issued - 2; j < issued; j++)
+                mbar_wait(bar(B_KF + (j & 1)), (uint32_t)((j >> 1) & 1), nullptr, E2C_ERR_WAIT_DRAIN);
         }
     } else if (warp == 1) {
         // ---------------------------------------------------------------- V^T loads
         if (elect_one()) {
             int issued = 0;
             for (int j = 0; j < nkt; j++) {
-                // the V buffer is free once PV of tile j-1 completed
-                if (j > 0 && !mbar_wait(bar(B_PV), (uint32_t)((j - 1) & 1), p.status, E2C_ERR_WAIT_PRODUCER)) break;
-                mbar_arrive_expect_tx(bar(B_VF), HD * TKV * 2);
-                for (int i = 0; i < 2; i++)
-                    tma_load_2d(sbase + V_OFF + i * (HD * 128), &tmV, j * TKV + 64 * i, b * HD, bar(B_VF));
+                const int vb = j & 1;
+                // buffer vb is free once PV of tile j-2 completed
+                if (!mbar_wait(bar(B_VE + vb), (uint32_t)(((j >> 1) & 1) ^ 1), p.status, E2C_ERR_WAIT_PRODUCER)) break;
+                mbar_arrive_expect_tx(bar(B_VF + vb), V_TILE);
+                tma_load_2d(sbase + V_OFF + vb * V_TILE, &tmV, j * TKV, b * HD, bar(B_VF + vb));
                 issued = j + 1;
             }
-            if (issued) mbar_wait(bar(B_VF), (uint32_t)((issued - 1) & 1), nullptr, E2C_ERR_WAIT_DRAIN);
+            for (int j = issued - 2 < 0 ? 0 : issued - 2; j < issued; j++)
+                mbar_wait(bar(B_VF + (j & 1)), (uint32_t)((j >> 1) & 1), nullptr, E2C_ERR_WAIT_DRAIN);
         }
     } else if (warp == 2) {
         // ---------------------------------------------------------------- MMA issuer
@@ -142,40 +168,43 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             bool ok = mbar_wait(bar(B_Q), 0, p.status, E2C_ERR_WAIT_MMA);
             auto issue_qk = [&](int j) -> bool {
                 const int sb = j & 1;
-                if (!mbar_wait(bar(B_KF), (uint32_t)(j & 1), p.status, E2C_ERR_WAIT_MMA)) return false;
+                if (!mbar_wait(bar(B_KF + sb), (uint32_t)((j >> 1) & 1), p.status, E2C_ERR_WAIT_MMA)) return false;
                 tc_fence_after();
                 const uint32_t d = tmem + (uint32_t)(sb * TKV);
+                const uint32_t kbase = sbase + K_OFF + sb * K_TILE;
 #pragma unroll
                 for (int k = 0; k < HD / 16; k++) {
-                    const uint32_t off = (uint32_t)((k >> 2) * (TQ * 128) + (k & 3) * 32);
-                    mma_bf16(d, smem_desc_sw128(sbase + Q_OFF + off), smem_desc_sw128(sbase + K_OFF + off), id_s, k != 0);
+                    const uint32_t qoff = (uint32_t)((k >> 2) * (TQ * 128) + (k & 3) * 32);
+                    const uint32_t koff = (uint32_t)((k >> 2) * (TKV * 128) + (k & 3) * 32);
+                    mma_bf16(d, smem_desc_sw128(sbase + Q_OFF + qoff), smem_desc_sw128(kbase + koff), id_s, k != 0);
                 }
-                mma_commit(bar(sb ? B_SF1 : B_SF0));
-                mma_commit(bar(B_KE));
+                mma_commit(bar(B_SF + sb));
+                mma_commit(bar(B_KE + sb));
                 return true;
             };
             if (ok) ok = issue_qk(0);
             if (ok && nkt > 1) ok = issue_qk(1);
             for (int j = 0; j < nkt && ok; j++) {
-                if (!mbar_wait(bar(B_PF), (uint32_t)(j & 1), p.status, E2C_ERR_WAIT_MMA) ||
-                    !mbar_wait(bar(B_VF), (uint32_t)(j & 1), p.status, E2C_ERR_WAIT_MMA)) {
+                const int sb = j & 1;
+                if (!mbar_wait(bar(B_PF + sb), (uint32_t)((j >> 1) & 1), p.status, E2C_ERR_WAIT_MMA) ||
+                    !mbar_wait(bar(B_VF + sb), (uint32_t)((j >> 1) & 1), p.status, E2C_ERR_WAIT_MMA)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
-                const uint32_t pa = tmem + (uint32_t)((j & 1) * TKV);  // P(j): 64 columns of bf16 pairs
+                const uint32_t pa = tmem + (uint32_t)(sb * TKV);  // P(j): 32 columns of bf16 pairs
+                const uint32_t vbase = sbase + V_OFF + sb * V_TILE;
 #pragma unroll
-                for (int k = 0; k < TKV / 16; k++) {
-                    const uint32_t vb = sbase + V_OFF + (uint32_t)((k >> 2) * (HD * 128) + (k & 3) * 32);
-                    mma_bf16_ts(tmem + 2 * TKV, pa + 8 * k, smem_desc_sw128(vb), id_o, (j | k) != 0);
-                }
-                mma_commit(bar(B_PV));
+                for (int k = 0; k < TKV / 16; k++)
+                    mma_bf16_ts(tmem + 256, pa + 8 * k, smem_desc_sw128(vbase + (uint32_t)(k * 32)), id_o, (j | k) != 0);
+                mma_commit(bar(B_PV + sb));
+                mma_commit(bar(B_VE + sb));
                 if (j + 2 < nkt && !(ok = issue_qk(j + 2))) break;
             }
             if (!ok) {
                 // drain whatever was issued before TMEM is released
-                mma_commit(bar(B_SF0));
-                mbar_wait(bar(B_SF0), 0, nullptr, E2C_ERR_WAIT_DRAIN);
+                mma_commit(bar(B_DRAIN));
+                mbar_wait(bar(B_DRAIN), 0, nullptr, E2C_ERR_WAIT_DRAIN);
             }
         }
     } else {
@@ -191,36 +220,31 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         bool ok = true;
         for (int j = 0; j < nkt; j++) {
             const int sb = j & 1;
-            if (!__all_sync(0xffffffffu, mbar_wait(bar(sb ? B_SF1 : B_SF0), (uint32_t)((j >> 1) & 1), p.status,
-                                                   E2C_ERR_WAIT_ATTN))) {
+            if (!__all_sync(0xffffffffu, mbar_wait(bar(B_SF + sb), (uint32_t)((j >> 1) & 1), p.status, E2C_ERR_WAIT_ATTN))) {
                 ok = false;
                 break;
             }
             tc_fence_after();
-            const uint32_t sbuf = tmem + lane_addr + (uint32_t)(sb * TKV);
-            float s[64];
+            float s[32];
             {
-                uint32_t rr[2][32];
-                tmem_ld32(sbuf + 64 * kh, rr[0]);
-                tmem_ld32(sbuf + 64 * kh + 32, rr[1]);
+                uint32_t rr[32];
+                tmem_ld32(tmem + lane_addr + (uint32_t)(sb * TKV + 32 * kh), rr);
                 tmem_wait_ld();
 #pragma unroll
-                for (int c = 0; c < 2; c++)
-#pragma unroll
-                    for (int i = 0; i < 32; i++) s[c * 32 + i] = __uint_as_float(rr[c][i]);
+                for (int i = 0; i < 32; i++) s[i] = __uint_as_float(rr[i]);
             }
             // masking only where a tile runs past the sequence or a valid mask is given
-            const int k0 = j * TKV + 64 * kh;
-            if (p.valid || k0 + 64 > S) {
+            const int k0 = j * TKV + 32 * kh;
+            if (p.valid || k0 + 32 > S) {
 #pragma unroll
-                for (int i = 0; i < 64; i++) {
+                for (int i = 0; i < 32; i++) {
                     const int key = k0 + i;
                     if (!(key < S && (!p.valid || p.valid[row0 + key]))) s[i] = -INFINITY;
                 }
             }
             float mx = -INFINITY;
 #pragma unroll
-            for (int i = 0; i < 64; i++) mx = fmaxf(mx, s[i]);
+            for (int i = 0; i < 32; i++) mx = fmaxf(mx, s[i]);
             // the row max over both key halves, through the partner warp
             xch[(sb * 2 + kh) * TQ + r] = mx;
             mbar_arrive(bar(B_PAIR + sb * 4 + quad));
@@ -240,7 +264,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             }
             if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
                 // O may be touched only once PV of tile j-1 completed
-                if (!__all_sync(0xffffffffu, mbar_wait(bar(B_PV), (uint32_t)((j - 1) & 1), p.status, E2C_ERR_WAIT_ATTN))) {
+                if (!__all_sync(0xffffffffu, mbar_wait(bar(B_PV + ((j - 1) & 1)), (uint32_t)(((j - 1) >> 1) & 1), p.status,
+                                                       E2C_ERR_WAIT_ATTN))) {
                     ok = false;
                     break;
                 }
@@ -248,7 +273,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 #pragma unroll 1
                 for (int c = 0; c < 4; c++) {
                     uint32_t o[32];
-                    const uint32_t ta = tmem + lane_addr + (uint32_t)(2 * TKV + 128 * kh + c * 32);
+                    const uint32_t ta = tmem + lane_addr + (uint32_t)(256 + 128 * kh + c * 32);
                     tmem_ld32(ta, o);
                     tmem_wait_ld();
 #pragma unroll
@@ -257,14 +282,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 }
                 tmem_wait_st();
             }
-            // probabilities -> bf16 pairs, written over this warp's 64 columns' worth of S: P(j)
-            // occupies columns [32 kh, 32 kh + 32) of the buffer (both halves already read S)
+            // probabilities -> bf16 pairs over this warp's S columns: P(j) occupies columns
+            // [16 kh, 16 kh + 16) of the buffer (both halves already read S, through the exchange)
             const float c = p.scale_log2, mneg = -m_used;
             const bool live = m_used != -INFINITY;
-            uint32_t pk[32];
+            uint32_t pk[16];
             float lsum = 0.f;
 #pragma unroll
-            for (int i = 0; i < 32; i++) {
+            for (int i = 0; i < 16; i++) {
                 const float e0 = live ? ex2_approx(__fmaf_rn(s[2 * i], c, mneg)) : 0.f;
                 const float e1 = live ? ex2_approx(__fmaf_rn(s[2 * i + 1], c, mneg)) : 0.f;
                 lsum += e0 + e1;
@@ -272,13 +297,23 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 pk[i] = *reinterpret_cast<const uint32_t *>(&hv);
             }
             l += lsum;
-            tmem_st32(tmem + lane_addr + (uint32_t)(sb * TKV + 32 * kh), pk);
+            {
+                const uint32_t ta = tmem + lane_addr + (uint32_t)(sb * TKV + 16 * kh);
+                asm volatile(
+                    "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+                    "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(ta),
+                    "r"(pk[0]), "r"(pk[1]), "r"(pk[2]), "r"(pk[3]), "r"(pk[4]), "r"(pk[5]), "r"(pk[6]), "r"(pk[7]),
+                    "r"(pk[8]), "r"(pk[9]), "r"(pk[10]), "r"(pk[11]), "r"(pk[12]), "r"(pk[13]), "r"(pk[14]), "r"(pk[15])
+                    : "memory");
+            }
             tmem_wait_st();
             tc_fence_before();
-            mbar_arrive(bar(B_PF));
+            mbar_arrive(bar(B_PF + sb));
         }
         // ---------------------------------------------------------------- epilogue
-        if (ok && __all_sync(0xffffffffu, mbar_wait(bar(B_PV), (uint32_t)((nkt - 1) & 1), p.status, E2C_ERR_WAIT_ATTN))) {
+        // PV of the last tile completes after every earlier product (tcgen05.commit tracks all prior MMAs)
+        if (ok && __all_sync(0xffffffffu, mbar_wait(bar(B_PV + ((nkt - 1) & 1)), (uint32_t)(((nkt - 1) >> 1) & 1),
+                                                    p.status, E2C_ERR_WAIT_ATTN))) {
             tc_fence_after();
             // the row sum over both key halves
             xch[kh * TQ + r] = l;  // buffer 0; its last use (the row max of an earlier tile) is fenced by B_PV
@@ -296,8 +331,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 #pragma unroll
                 for (int cp = 0; cp < 2; cp++) {
                     uint32_t o[2][32];
-                    tmem_ld32(tmem + lane_addr + (uint32_t)(2 * TKV + 128 * kh + 64 * cp), o[0]);
-                    tmem_ld32(tmem + lane_addr + (uint32_t)(2 * TKV + 128 * kh + 64 * cp + 32), o[1]);
+                    tmem_ld32(tmem + lane_addr + (uint32_t)(256 + 128 * kh + 64 * cp), o[0]);
+                    tmem_ld32(tmem + lane_addr + (uint32_t)(256 + 128 * kh + 64 * cp + 32), o[1]);
                     tmem_wait_ld();
 #pragma unroll
                     for (int h2 = 0; h2 < 2; h2++) {
@@ -351,6 +386,10 @@ extern "C" int e2c_attention(const void *q, const void *k, const void *vt, int l
         e2c_set_msg("attention: bad arguments (H=%d S=%d ldvt=%d; ldvt >= S, multiple of 8; 16-byte aligned)", H, S, ldvt);
         return -1;
     }
+    if ((uintptr_t)ctx & 15) {
+        e2c_set_msg("attention: ctx must be 16-byte aligned");
+        return -1;
+    }
     static bool attr = false;
     if (!attr) {
         if (cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_ALLOC) != cudaSuccess) {
@@ -358,10 +397,6 @@ extern "C" int e2c_attention(const void *q, const void *k, const void *vt, int l
             return -2;
         }
         attr = true;
-    }
-    if ((uintptr_t)ctx & 15) {
-        e2c_set_msg("attention: ctx must be 16-byte aligned");
-        return -1;
     }
     CUtensorMap tq, tk, tv, to;
     const uint64_t rows = (uint64_t)B * S;

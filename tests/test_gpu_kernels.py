@@ -184,9 +184,11 @@ def _args_for(W, qd, sd, M, K):
     return a
 
 
-def test_gelu_gate_epilogue_bitexact(e2c, of, torch_cuda):
+def test_gelu_gate_epilogue(e2c, of, torch_cuda):
     """gate|up GEMM with GELU-tanh(g)*u in the epilogue (e2.c src/text.c:424-447 +
-    src/kernels_avx512.c:186-203) against the port of the same polynomial."""
+    src/kernels_avx512.c:186-203). g and u are the bit-exact dequantised GEMM outputs; GELU is a
+    floating-point epilogue (the reference's -ffast-math build is itself not reproducible to the bit,
+    SURVEY F4), so h agrees with the port within 2e-6 relative (a few ulp)."""
     torch = torch_cuda
     rng = np.random.default_rng(21)
     M, D, I = 150, 768, 1152
@@ -209,7 +211,11 @@ def test_gelu_gate_epilogue_bitexact(e2c, of, torch_cuda):
     of.port().e2o_gelu_tanh(gg.ctypes.data_as(of.f32p), gg.size)
     want = (gg * u).astype(np.float32)
     got = h.cpu().numpy()
-    assert f32_bits_equal(got, want), f"max abs {np.abs(got - want).max()}"
+    np.testing.assert_allclose(got, want, rtol=2e-6, atol=1e-7 * float(np.abs(want).max()))
+    # and the bytes a per-token requantisation of h makes agree within the reference's tie rule
+    gq, gs = of.quantize_signed(np.ascontiguousarray(got), I)
+    wq, ws = of.quantize_signed(np.ascontiguousarray(want), I)
+    tie_tolerant_bytes(gq, wq, want * (np.float32(127.0) / np.abs(want).max(axis=1, keepdims=True)))
 
 
 def test_qkv_epilogue_norm_rope(e2c, of, torch_cuda):
