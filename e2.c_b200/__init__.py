@@ -109,6 +109,7 @@ API = [
     ("e2cuda_quantize_rows", C.c_int, [vp, vp, vp, C.c_int, C.c_int, C.c_int, C.c_float, C.c_float, vp]),
     ("e2cuda_i8_gemm", C.c_int, [C.POINTER(W8), vp, vp, C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(Epilogue),
                                  vp, C.c_int, vp]),
+    ("e2cuda_i8_linear_noalloc", C.c_int, [C.POINTER(W8), vp, C.c_int, C.c_int, vp, C.c_int, vp]),
     ("e2cuda_attention", C.c_int, [vp, vp, vp, C.c_int, vp, vp, C.c_int, C.c_int, C.c_int, C.c_float, vp]),
     ("e2cuda_ffn_create", vp, [C.POINTER(Q8W), C.POINTER(Q8W), C.POINTER(Q8W), f32p, C.c_float, C.c_int]),
     ("e2cuda_ffn_destroy", None, [vp]),
@@ -239,6 +240,21 @@ def i8_gemm(w: Weight, qa, a_scales, ablk: int | None = None, n0: int = 0, n1: i
     _ok(lib().e2cuda_i8_gemm(C.byref(w.w8), _ptr(qa), _ptr(a_scales), M, ablk, n0, n1, C.byref(ep),
                              None if dots else _ptr(out), w.N, _stream(stream)), "i8_gemm")
     return out
+
+
+# bytes of the fixed device array behind e2cuda_i8_linear_noalloc (E2CUDA_NOALLOC_SCRATCH_BYTES)
+NOALLOC_SCRATCH_BYTES = 8 << 20
+
+
+def i8_linear_noalloc(w: Weight, x, y, ablk: int | None = None, stream=None):
+    """quantise(x) then the W8A8 GEMM into the caller's y [M][N] fp32, with no allocation in the
+    library: the quantised activations live in the library's fixed per-device array. Returns y once
+    written (the call synchronises `stream`)."""
+    M = x.shape[0]
+    ablk = ablk or w.K
+    _ok(lib().e2cuda_i8_linear_noalloc(C.byref(w.w8), _ptr(x), M, ablk, _ptr(y), y.shape[1], _stream(stream)),
+        "i8_linear_noalloc")
+    return y
 
 
 def attention(q, k, vt, valid, B: int, S: int, H: int, scale: float, stream=None):

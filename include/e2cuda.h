@@ -97,6 +97,37 @@ typedef struct e2cuda_epilogue {
 int e2cuda_i8_gemm(const e2cuda_w8 *w, const int8_t *qa, const float *a_scales, int M, int ablk,
                    int n0, int n1, const e2cuda_epilogue *ep, float *y, int ldy, void *stream);
 
+/* Quantise-then-GEMM with no allocation. This entry point has no counterpart in the reference. e2.c
+ * quantises into its model workspace (ws.qa) and then runs the GEMM tiles over it (gemm_segs /
+ * gemm_quant_phase, e2.c src/text.c:321-411). This call does the same two steps without any
+ * buffer from the caller or the library, for callers that cannot let a library allocate device
+ * memory. Typical reasons:
+ *   - a serving process's own allocator already holds the device memory it budgeted;
+ *   - cudaMalloc/cudaFree may block the calling thread and synchronise the device;
+ *   - the host wants a fixed, known device footprint.
+ *
+ * What it computes: y[m * ldy + n] for n in [0, w->N) — e2cuda_quantize_rows(x, ablk, no clamp)
+ * followed by e2cuda_i8_gemm with the F32 epilogue, i.e. the same result.
+ *   - x is device fp32 [M][w->K]; w->K must be a multiple of 16.
+ *   - ablk is w->K (per-token scales) or a multiple of 128 dividing w->K.
+ *
+ * Scratch. The quantised activations and this call's status word live in one fixed array of
+ * E2CUDA_NOALLOC_SCRATCH_BYTES (8 MiB). Each GPU reserves it when it loads this library's device
+ * code and keeps it until the process exits.
+ *   - The call needs 256 + M*K bytes (rounded up to 256) + 4*M*K/ablk bytes. A larger M is rejected
+ *     with an error: split the rows into smaller calls.
+ *   - Every call on a device shares the array, and it keeps the last call's contents. The status
+ *     word is cleared at the start of each call; everything else is rewritten before it is read.
+ *     Calls that overlap on the GPU (other streams, other host threads) race on it: serialise them.
+ *   - The first call on each device looks up the array's device address, with that device current.
+ *     Make that first call before any stream capture.
+ *
+ * The call is queued on `stream`, then synchronises `stream` to read its device status; it returns
+ * once y is written. Calls no cudaMalloc, cudaFree or allocating library routine. */
+#define E2CUDA_NOALLOC_SCRATCH_BYTES ((size_t)8 << 20)
+int e2cuda_i8_linear_noalloc(const e2cuda_w8 *w, const float *x, int M, int ablk, float *y, int ldy,
+                             void *stream);
+
 /* bf16 attention (A8), full bidirectional over the valid keys of each sequence, GQA with one KV
  * head: q [B*S][H*256], k [B*S][256], vt [B][256][ldvt] (V transposed, ldvt >= S, multiple of 8),
  * valid [B*S] or NULL -> ctx fp32 [B*S][H*256]. scale multiplies the logits. */
