@@ -4,10 +4,10 @@ roofline, the reference CPU path timed on this host's cores, and the reference a
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl e2cuda|reference]
     python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 bench.py --gpus N ...
 
-One step = one pass of the 24-layer synthetic encoder (hidden 768, 3 q heads /
+One step = one pass of the 24-layer synthetic encoder (benchmark config 2: hidden 768, 3 q heads /
 1 KV head of 256, FFN 1152, int8 token table [262144][768], dense 768->3072->768, L2) over a batch of
 64 sequences x 512 tokens per GPU (weak scaling: every rank embeds its own batch), followed, for
-N > 1, by the single NCCL all-gather of the pooled embeddings to every rank (BASELINE.json north_star).
+N > 1, by the single NCCL all-gather of the pooled embeddings to every rank.
 Inputs are device-resident token ids ("value"); "e2e" drives the same pass through the C ABI's
 host-buffer entry point (pinned ids in, embeddings out, copies inside the timed region). Weights are
 random-init and seeded, token ids uniform in [2, 262144): there is no checkpoint or dataset.

@@ -19,7 +19,7 @@ extern "C" {
 const char *e2c_msg(void);
 void e2c_set_msg(const char *fmt, ...);
 
-/* Activation quantiser (src/int8.c:178-209 semantics, SURVEY F3 forms): x fp32 [M][K] (row stride
+/* Activation quantiser (src/int8.c:178-209 semantics in the forms the -ffast-math build computes): x fp32 [M][K] (row stride
  * ldx floats) -> q int8 [M][K] (row stride ldq bytes), scales [M][K/ablk]. biased != 0 stores q+128
  * (the reference's byte convention), else signed q. ablk = K for per-row, else a divisor of K that
  * is a multiple of 16. */

@@ -1,8 +1,8 @@
-"""Seeded synthetic inputs and random-init int8 models for the BASELINE configs.
+"""Seeded synthetic inputs and random-init int8 models for the benchmark configs 0-4.
 
 No dataset or checkpoint exists for these configs (the synthetic encoder of config 2 is not a model
 the reference can load), so every config is generated here from a fixed seed with the shapes and
-distributions BASELINE.json names. Weights are quantised exactly as the reference's model loader
+distributions the benchmark configs name. Weights are quantised exactly as the reference's model loader
 does (e2.c src/int8.c:19-66, the per-row weight quantiser with its -ffast-math scale forms), and packed
 into the reference's quad-interleaved e2_q8w layout, so the device path consumes what a q8cache would
 hold.
@@ -110,7 +110,7 @@ class EncoderConfig:
     out_dim: int = 768
     rope_theta: float = 10000.0
     eps: float = 1e-6
-    attn_scale: float = 1.0 / 16.0      # 1/sqrt(head_dim): the config leaves it open
+    attn_scale: float = 1.0 / 16.0      # 1/sqrt(head_dim); the config leaves the scale open
     embed_scale: float | None = None    # sqrt(hidden), as the reference's loader (e2.c src/e2.c:298)
     weight_std: float = 0.02
     norm_std: float = 0.1

@@ -179,7 +179,7 @@ void e2o_i8_gemm_plain(float *y, int32_t *dots, const int8_t *qa, const float *a
 /* ------------------------------------------------------------------ fp32 row ops
  * src/kernels.c:76-87 (rmsnorm), :144-171 (norm_split / norm_add): inv = 1/sqrt(mean(x^2) + eps),
  * x*inv*gamma. The reference's -ffast-math AVX-512 build sums in 16 lanes and may use an
- * rsqrt+Newton step (SURVEY F4): these agree with it to a few ulp, and tests gate them by tolerance. */
+ * rsqrt+Newton step: these agree with it to a few ulp, and tests gate them by tolerance. */
 static float row_inv(const float *x, int D, float eps) {
     float ss = 0.f;
     for (int d = 0; d < D; d++) ss += x[d] * x[d];

@@ -70,7 +70,7 @@ def cosine_rows(a: np.ndarray, b: np.ndarray) -> np.ndarray:
 
 
 def tie_tolerant_bytes(got: np.ndarray, want: np.ndarray, pre_round: np.ndarray, band: float = 2e-3) -> None:
-    """Quantised bytes after an fp32 epilogue (SURVEY F4, the reference's own rule in
+    """Quantised bytes after an fp32 epilogue (the reference's own rule in
     tests/test_gpu_ffn.c:112-118): equal, or one step apart where the pre-round value is within
     `band` of a .5 tie."""
     d = np.abs(got.astype(np.int32) - want.astype(np.int32))

@@ -54,7 +54,7 @@ def test_ffn_fixture(of, syn, gold):
     wu = syn.PackedWeight(gold["ffn_wu_q"], gold["ffn_wu_s"], 128)
     wd = syn.PackedWeight(gold["ffn_wd_q"], gold["ffn_wd_s"], 256)
     y, st = of.ffn_block("port", gold["ffn_x"], gold["ffn_g"], 1e-6, wg, wu, wd, ablk=0, stages=True)
-    # the port's RMSNorm is IEEE; the reference's is -ffast-math (SURVEY F4): bytes may differ by
+    # the port's RMSNorm is IEEE; the reference's is -ffast-math: bytes may differ by
     # one step at a tie, outputs by a few ulp
     d = np.abs(st["xq"].astype(int) - gold["ffn_xq"].astype(int))
     assert d.max() <= 1 and (d == 0).mean() > 0.999

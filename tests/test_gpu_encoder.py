@@ -2,7 +2,7 @@
 reference's CPU int8 path (the reference build when present, else the port), through the C ABI.
 
 Bars: FFN output within 1e-3 of the output norm (requantised activations may flip by one step at a
-tie); pooled embeddings cosine >= 0.9999 per sequence.
+tie after an fp32 epilogue); pooled embeddings cosine >= 0.9999 per sequence.
 """
 from __future__ import annotations
 
@@ -35,7 +35,7 @@ def test_ffn_block_config1_shape(e2c, of, syn, torch_cuda):
     got = y.cpu().numpy()
     want = of.ffn_block(_which(of), x, g, 1e-6, wg, wu, wd, ablk=0)
     # Rows whose requantised bytes all agree match to rounding; a row where the fp32 RMSNorm or GELU
-    # moved one pre-round value across a .5 tie carries a one-step difference in one byte (SURVEY F4)
+    # moved one pre-round value across a .5 tie carries a one-step difference in one byte
     err = np.linalg.norm(got - want, axis=1) / np.linalg.norm(want, axis=1)
     assert np.mean(err < 1e-5) > 0.9, f"only {np.mean(err < 1e-5):.3f} of rows agree to rounding"
     assert err.max() < 5e-3, f"worst row {err.max()}"

@@ -122,8 +122,8 @@ def test_gemm_clamped_output(of, syn):
 
 
 def test_fp32_vtable_close_to_reference(of, syn):
-    """RMSNorm / softmax / GELU-tanh agree to a few ulp. The reference is built -ffast-math
-    (SURVEY F4): GCC turns GELU's 2/(e+1) into rcp14 + one Newton step and reassociates the final
+    """RMSNorm / softmax / GELU-tanh agree to a few ulp. The reference is built -ffast-math:
+    GCC turns GELU's 2/(e+1) into rcp14 + one Newton step and reassociates the final
     products, and sums norms in 16 lanes, so bit-exactness is not defined for these."""
     rng = np.random.default_rng(12)
     k = C.cast(of.mux().e2refmux_kernels(128), C.POINTER(C.c_void_p))
