@@ -182,9 +182,12 @@ def main() -> int:
     ap.add_argument("--tokens", type=int, default=BATCH * SEQ, help="tokens for --kernel (a multiple of 512)")
     ap.add_argument("--chunk", type=int, default=CHUNK,
                     help="tokens per device pass (whole sequences); intermediates of a pass stay L2-resident")
+    ap.add_argument("--sweep", action="store_true", help="benchmark config 3: the GEMM over M x (K, N)")
     args = ap.parse_args()
     if args.kernel:
         return kernel_only(args)
+    if args.sweep:
+        return gemm_sweep(args)
 
     import torch
 
@@ -327,20 +330,8 @@ def gate_up_roofline(e2c, syn, w, dev, stream) -> dict:
     h = torch.empty((M, I), dtype=torch.float32, device=dev)
     a = e2c.gemm_args(W, qa, qs, M)
     a.epi, a.y, a.ldy = e2c.EPI_GELU, h.data_ptr(), I
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)  # 256 MB > L2
-    times = []
-    with torch.cuda.stream(stream):
-        for i in range(13):
-            flush.zero_()
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record(stream)
-            e2c.gemm_raw(a, stream)
-            e1.record(stream)
-            e1.synchronize()
-            if i >= 3:
-                times.append(e0.elapsed_time(e1))
+    avg_ms = timed_launches(lambda: e2c.gemm_raw(a, stream), stream, 3, 10)
     e2c.check(stream)
-    avg_ms = sum(times) / len(times)
     ops = 2.0 * M * (2 * I) * D
     p = peaks()
     peak = 2.0 * p["bf16_tflops"]
@@ -408,17 +399,77 @@ def kernel_only(args) -> int:
     else:
         x = torch.randn((M, I), device=dev, generator=g)
         run = lambda: e2c.quantize_rows(x, I, stream=stream)
-    with torch.cuda.stream(stream):
-        for _ in range(args.warmup):
-            run()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for _ in range(args.steps):
-            run()
-        e1.record(stream)
-    torch.cuda.synchronize()
+    avg_ms = timed_launches(run, stream, args.warmup, args.steps)
     e2c.check(stream)
-    print(json.dumps({"kernel": args.kernel, "tokens": M, "avg_ms": e0.elapsed_time(e1) / max(args.steps, 1)}))
+    print(json.dumps({"kernel": args.kernel, "tokens": M, "avg_ms": avg_ms, "l2": "flushed between launches"}))
+    return 0
+
+
+def timed_launches(run, stream, warmup: int, steps: int) -> float:
+    """Average CUDA-event time of `run` on `stream`, a 256 MB buffer (> L2) rewritten before every
+    launch so each one starts from a cold L2."""
+    import torch
+
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=torch.cuda.current_device())
+    times = []
+    with torch.cuda.stream(stream):
+        for i in range(warmup + steps):
+            flush.zero_()
+            # keep the stream busy while the host records the event and enqueues the launch, so
+            # host-side launch latency never shows up between the two events
+            torch.cuda._sleep(100_000)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            run()
+            e1.record(stream)
+            if i >= warmup:
+                times.append((e0, e1))
+    torch.cuda.synchronize()
+    return sum(a.elapsed_time(b) for a, b in times) / max(len(times), 1)
+
+
+SWEEP_M = (1, 16, 128, 1024, 8192)
+SWEEP_KN = ((2048, 8192), (8192, 2048), (2048, 2048), (768, 262144))
+
+
+def gemm_sweep(args) -> int:
+    """Benchmark config 3: the W8A8 GEMM (per-token activation scales, fp32 output) over
+    M x (K, N), one JSON line per point with its time against the roofline that bounds it: int8
+    tensor throughput (2 x measured bf16) or HBM bandwidth over the algorithmic bytes
+    M*K + 4*M (activations) + N*K + 4*N (weights) + 4*M*N (output)."""
+    import torch
+
+    e2c = load_pkg()
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    stream = torch.cuda.Stream(device=dev)
+    p = peaks()
+    int8_peak, hbm = 2.0 * p["bf16_tflops"] * 1e12, p["hbm_gbs"] * 1e9
+    g = torch.Generator(device=dev).manual_seed(3)
+    rng = np.random.default_rng(3)
+    for K, N in SWEEP_KN:
+        W = e2c.Weight(w=rng.integers(-127, 128, size=(N, K), dtype=np.int8),
+                       scale=rng.uniform(1e-4, 0.02, size=N).astype(np.float32))
+        for M in SWEEP_M:
+            qa = torch.randint(-127, 128, (M, K), dtype=torch.int8, device=dev, generator=g)
+            qs = torch.rand((M, 1), device=dev, generator=g) * 0.05 + 1e-3
+            y = torch.empty((M, N), dtype=torch.float32, device=dev)
+            a = e2c.gemm_args(W, qa, qs, M)
+            a.epi, a.y, a.ldy = e2c.EPI_F32, y.data_ptr(), N
+            run = lambda: e2c.gemm_raw(a, stream)
+            ms = timed_launches(run, stream, args.warmup, args.steps)
+            e2c.check(stream)
+            ops = 2.0 * M * N * K
+            nbytes = M * K + 4 * M + N * K + 4 * N + 4 * M * N
+            t_tc, t_hbm = ops / int8_peak, nbytes / hbm
+            t = ms / 1e3
+            print(json.dumps({"sweep": "config 3", "M": M, "K": K, "N": N, "us": round(ms * 1e3, 2),
+                              "tops": round(ops / t / 1e12, 1), "gbs": round(nbytes / t / 1e9, 1),
+                              "bound": "tensor" if t_tc > t_hbm else "hbm",
+                              "frac_of_roofline": round(max(t_tc, t_hbm) / t, 3),
+                              "peak_src": p["src"]}), flush=True)
+            del qa, qs, y
+        W.free()
     return 0
 
 

@@ -5,6 +5,7 @@
 
 #include <cuda_runtime.h>
 #include <math.h>
+#include <pthread.h>
 #include <stdarg.h>
 #include <stdio.h>
 #include <stdlib.h>
@@ -361,6 +362,10 @@ int e2cuda_ffn_forward(e2cuda_ffn *f, const float *x, int M, float *y, void *str
 }
 
 /* ------------------------------------------------------------------ host drop-ins */
+/* The drop-ins share one weight cache and three scratch buffers. e2.c calls its GEMM from every
+ * pool worker at once, each on its own column range (src/text.c:301-318), so every drop-in call
+ * holds this lock: concurrent calls are safe and run one after another on the device. */
+static pthread_mutex_t g_host_mu = PTHREAD_MUTEX_INITIALIZER;
 static int g_act_block = 128;
 
 void e2cuda_set_act_block(int ablk) { g_act_block = ablk > 0 ? ablk : 128; }
@@ -414,14 +419,16 @@ static const e2cuda_w8 *cached_weight(const e2cuda_q8w *q) {
 }
 
 void e2cuda_host_cache_clear(void) {
+    pthread_mutex_lock(&g_host_mu);
     for (int i = 0; i < E2CU_CACHE; i++)
         if (g_cache[i].key) {
             e2cuda_w8_free(&g_cache[i].w);
             g_cache[i].key = NULL;
         }
+    pthread_mutex_unlock(&g_host_mu);
 }
 
-void e2cuda_i8_quantize_host(int8_t *out, float *scales, const float *x, int M, int K, float lo, float hi) {
+static void quantize_host_locked(int8_t *out, float *scales, const float *x, int M, int K, float lo, float hi) {
     const int ablk = g_act_block < K ? g_act_block : K;
     if (!out || !scales || !x || M <= 0 || K % ablk || K % 16) {
         e2cu_err("i8_quantize_host: bad arguments (M=%d K=%d block %d)", M, K, ablk);
@@ -444,8 +451,14 @@ void e2cuda_i8_quantize_host(int8_t *out, float *scales, const float *x, int M, 
     g_err[0] = 0;
 }
 
-void e2cuda_i8_gemm_host(float *y, const int8_t *qa, const float *a_scales, const e2cuda_q8w *w, int M, int N,
-                         int n0, int n1) {
+void e2cuda_i8_quantize_host(int8_t *out, float *scales, const float *x, int M, int K, float lo, float hi) {
+    pthread_mutex_lock(&g_host_mu);
+    quantize_host_locked(out, scales, x, M, K, lo, hi);
+    pthread_mutex_unlock(&g_host_mu);
+}
+
+static void gemm_host_locked(float *y, const int8_t *qa, const float *a_scales, const e2cuda_q8w *w, int M, int N,
+                             int n0, int n1) {
     if (!y || !qa || !a_scales || !w || M <= 0 || n0 < 0 || n1 > w->N || n0 >= n1 || w->K % 16 || w->nblocks <= 0 ||
         w->K % w->nblocks) {
         e2cu_err("i8_gemm_host: bad arguments");
@@ -479,4 +492,11 @@ void e2cuda_i8_gemm_host(float *y, const int8_t *qa, const float *a_scales, cons
                   "download"))
         return;
     g_err[0] = 0;
+}
+
+void e2cuda_i8_gemm_host(float *y, const int8_t *qa, const float *a_scales, const e2cuda_q8w *w, int M, int N,
+                         int n0, int n1) {
+    pthread_mutex_lock(&g_host_mu);
+    gemm_host_locked(y, qa, a_scales, w, M, N, n0, n1);
+    pthread_mutex_unlock(&g_host_mu);
 }

@@ -15,9 +15,13 @@
 //   warp 1      TMEM owner and MMA issuer: 4 x tcgen05.mma (K = 32) per stage into one of two
 //               TMEM accumulators (2 x BN columns of int32), tcgen05.commit frees stages;
 //   warps 2..17 epilogue, four warps per TMEM lane quadrant, each owning a quarter of the tile's
-//               columns: tcgen05.ld, dequant (weight scales broadcast by warp shuffle) and the fused
-//               tail (residual, clamp, GELU-gate, per-head RMSNorm + RoPE), results staged in a
-//               per-warp 64-byte-swizzled shared-memory tile and written by TMA stores.
+//               columns: tcgen05.ld, dequant (the columns' weight scales, fetched a tile ahead, read
+//               back from shared memory by broadcast loads) and the fused tail (residual, clamp,
+//               GELU-gate, per-head RMSNorm + RoPE), results staged in per-warp 64-byte-swizzled
+//               shared-memory tiles (two, alternating) and written by TMA stores.
+// Tile widths BN = 256, 192 or 128: the launcher picks the one whose waves of tiles over the SMs
+// cost least (N = 768 takes 192: 4 column tiles, so 7 nearly full waves of 148 instead of 6 with
+// the last one at a fifth).
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -37,14 +41,20 @@ constexpr int EPI_WARPS = 16;
 constexpr int NTHREADS = 64 + 32 * EPI_WARPS;
 constexpr int STG_WARP = 2048;  // staging bytes per epilogue warp and store (32 rows x 64 bytes)
 
-template <int BN, int STAGES, int EPI>
+template <int BN, int STAGES, bool PERBLOCK, int EPI, int CG>
 struct GemmSmem {
     static constexpr int A_BYTES = BM * BK;
-    static constexpr int B_BYTES = BN * BK;
+    static constexpr int B_BYTES = (BN / CG) * BK;  // a CTA pair splits B's rows between its CTAs
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-    static constexpr int STG_PER_WARP = EPI == E2C_EPI_QKV ? 2 * STG_WARP : STG_WARP;
+    // staging tiles per epilogue warp: QKV stages the two halves of a head; the other epilogues
+    // without the per-block fold alternate between two, so a store overlaps the next chunk's math
+    static constexpr int STG_BUFS = (EPI == E2C_EPI_QKV || (!PERBLOCK && EPI != E2C_EPI_I32 && CG == 1)) ? 2 : 1;
+    static constexpr int STG_PER_WARP = STG_BUFS * STG_WARP;
     static constexpr int STG_OFF = STAGES * STAGE_BYTES;
-    static constexpr int SSQ_OFF = STG_OFF + EPI_WARPS * STG_PER_WARP;
+    // per-warp column constants (weight scales, norm gains): 128 floats
+    static constexpr int CST_OFF = STG_OFF + EPI_WARPS * STG_PER_WARP;
+    static constexpr int CST_BYTES = (PERBLOCK || EPI == E2C_EPI_I32) ? 0 : EPI_WARPS * 128 * 4;
+    static constexpr int SSQ_OFF = CST_OFF + CST_BYTES;
     static constexpr int SSQ_BYTES = EPI == E2C_EPI_QKV ? 2 * 4 * BM * 4 : 0;  // [acc][part][row]
     static constexpr int BAR_OFF = SSQ_OFF + SSQ_BYTES;
     // full[S], empty[S], tfull[2], tempty[2], pair[2][4] (QKV row-norm exchange), tmem slot
@@ -55,12 +65,14 @@ struct GemmSmem {
 };
 
 // ---------------------------------------------------------------------------------- epilogue math
-// GELU-tanh with the reference's formulation (src/kernels_avx512.c:46-55,186-203):
-//   0.5 v (1 + tanh(c (v + 0.044715 v^3))),  tanh(z) = sign(z) (1 - 2 / (exp(2|z|) + 1)),
-//   tanh = 1 past |z| > 15.
-// exp and the reciprocal use the SFU approximations (ex2.approx: <= 2 ulp; rcp.approx: <= 1 ulp),
-// so a GELU value is within ~1e-7 relative of the reference's, whose own -ffast-math build divides
-// with rcp14 plus a Newton step: the same order of agreement, at a third of the instructions.
+// GELU-tanh, the reference's function (src/kernels_avx512.c:46-55,186-203):
+//   0.5 v (1 + tanh(c (v + 0.044715 v^3))),  c = sqrt(2/pi).
+// Evaluated through the identity 0.5 (1 + tanh z) = 1 / (1 + exp(-2z)):
+//   gelu(v) = v / (1 + 2^(k v (1 + 0.044715 v^2))),  k = -2 c log2(e),
+// with the SFU's ex2.approx (<= 2 ulp) and rcp.approx (<= 1 ulp): about 8 instructions, no range
+// clamps (ex2 saturates to 0 or +inf, and v / inf = -0 matches tanh = -1 exactly), and no
+// cancellation in 1 + tanh for negative v. Within ~1e-7 relative of the reference, whose own
+// -ffast-math build divides with rcp14 plus a Newton step.
 __device__ __forceinline__ float ex2_fast(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -72,14 +84,9 @@ __device__ __forceinline__ float rcp_fast(float x) {
     return y;
 }
 __device__ __forceinline__ float gelu_tanh(float v) {
-    const float v3 = __fmul_rn(__fmul_rn(v, v), v);
-    const float inner = __fmul_rn(0.7978845608028654f, __fmaf_rn(0.044715f, v3, v));
-    const float a = fminf(fabsf(inner), 15.5f);                    // exp(31) stays finite
-    const float e = ex2_fast(__fmul_rn(a, 2.8853900817779268f));   // exp(2a) = 2^(2a log2 e)
-    float th = __fmaf_rn(-2.0f, rcp_fast(__fadd_rn(e, 1.0f)), 1.0f);
-    if (a > 15.0f) th = 1.0f;
-    th = copysignf(th, inner);
-    return __fmul_rn(__fmul_rn(0.5f, v), __fadd_rn(1.0f, th));
+    const float t = __fmaf_rn(0.044715f, __fmul_rn(v, v), 1.0f);
+    const float e = ex2_fast(__fmul_rn(__fmul_rn(-2.302208198144325f, v), t));
+    return __fmul_rn(v, rcp_fast(__fadd_rn(1.0f, e)));
 }
 
 __device__ __forceinline__ float dq(uint32_t acc, float s) { return __fmul_rn(__int2float_rn((int)acc), s); }
@@ -116,19 +123,13 @@ __device__ __forceinline__ void stage_store(const CUtensorMap *m, uint8_t *buf, 
         bulk_commit();
     }
 }
-// before rewriting a staging tile: its previous store has read it
-__device__ __forceinline__ void stage_reuse(int lane) {
-    if (lane == 0) bulk_wait_read0();
-    __syncwarp();
-}
-
 // ---------------------------------------------------------------------------------- kernel
-template <int BN, int STAGES, bool PERBLOCK, int EPI>
+template <int BN, int STAGES, bool PERBLOCK, int EPI, int CG>
 __global__ void __launch_bounds__(NTHREADS, 1)
     k_gemm_i8(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
               const __grid_constant__ CUtensorMap tmO0, const __grid_constant__ CUtensorMap tmO1, const e2c_gemm_args p,
               const int tma_out) {
-    using L = GemmSmem<BN, STAGES, EPI>;
+    using L = GemmSmem<BN, STAGES, PERBLOCK, EPI, CG>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     const uint32_t sbase = smem_u32(smem);
@@ -143,13 +144,17 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int M = p.M, K = p.K;
     const int ncols = p.n1 - p.n0;
-    const int tiles_m = (M + BM - 1) / BM, tiles_n = (ncols + BN - 1) / BN;
+    // A CTA pair (CG = 2, a cluster of two) shares 256-row tiles: rank r owns rows 128 r .. +127.
+    const uint32_t rank = CG == 2 ? cluster_ctarank() : 0u;
+    const int tfirst = CG == 2 ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+    const int tstride = CG == 2 ? (int)(gridDim.x >> 1) : (int)gridDim.x;
+    const int tiles_m = (M + BM * CG - 1) / (BM * CG), tiles_n = (ncols + BN - 1) / BN;
     const int ntiles = tiles_m * tiles_n;
     const int nk = (K + BK - 1) / BK;                    // stages per tile
     const int kpu = PERBLOCK ? p.ablk / BK : nk;         // stages per accumulation unit
     const int nunits = PERBLOCK ? K / p.ablk : 1;
     const int nb = K / p.ablk;                           // scale blocks per row
-    constexpr uint32_t TMEM_COLS = 2 * BN;
+    constexpr uint32_t TMEM_COLS = BN == 192 ? 512 : 2 * BN;  // a power of two, two accumulators
 
     if (warp == 0 && lane == 0) {
         for (int s = 0; s < STAGES; s++) {
@@ -158,7 +163,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         }
         for (int a = 0; a < 2; a++) {
             mbar_init(tfull_bar(a), 1);
-            mbar_init(tempty_bar(a), 32 * EPI_WARPS);
+            mbar_init(tempty_bar(a), EPI_WARPS * CG);  // one arrival per epilogue warp of the pair
             for (int q = 0; q < 4; q++) mbar_init(pair_bar(a, q), 128);
         }
         fence_mbar_init();
@@ -166,13 +171,30 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         tma_prefetch_desc(&tmB);
     }
     if (warp == 1) {
-        tmem_alloc(sbase + L::BAR_OFF + L::NBAR * 8, TMEM_COLS);
-        tmem_relinquish();
+        __syncwarp();
+        if constexpr (CG == 2) {
+            tmem_alloc_pair(sbase + L::BAR_OFF + L::NBAR * 8, TMEM_COLS);
+            tmem_relinquish_pair();
+        } else {
+            tmem_alloc(sbase + L::BAR_OFF + L::NBAR * 8, TMEM_COLS);
+            tmem_relinquish();
+        }
     }
     tc_fence_before();
-    __syncthreads();
+    // a pair: the leader's barriers are initialised before the other CTA signals them
+    if constexpr (CG == 2) cluster_sync();
+    else __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    // the accumulator is free again: one arrival per warp on the leader's barrier
+    auto release_acc = [&](int a) {
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+            if constexpr (CG == 2) mbar_arrive_cluster(mapa_shared(tempty_bar(a), 0));
+            else mbar_arrive(tempty_bar(a));
+        }
+    };
 
     if (warp == 0) {
         // ------------------------------------------------------------------ TMA producer
@@ -181,17 +203,25 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             uint32_t phase = 0;
             int issued = 0;  // loads in flight that nobody consumed (drained on failure)
             bool ok = true;
-            for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
-                const int m0 = (t / tiles_n) * BM, c0 = p.n0 + (t % tiles_n) * BN;
+            for (int t = tfirst; t < ntiles && ok; t += tstride) {
+                const int m0 = (t / tiles_n) * (BM * CG) + (int)rank * BM, c0 = p.n0 + (t % tiles_n) * BN;
                 for (int kb = 0; kb < nk; kb++) {
                     if (!mbar_wait(empty_bar(stage), phase ^ 1u, p.status, E2C_ERR_WAIT_PRODUCER)) {
                         ok = false;
                         break;
                     }
                     const uint32_t sa = sbase + stage * L::STAGE_BYTES, sb = sa + L::A_BYTES;
-                    mbar_arrive_expect_tx(full_bar(stage), L::STAGE_BYTES);
-                    tma_load_2d(sa, &tmA, kb * BK, m0, full_bar(stage));
-                    tma_load_2d(sb, &tmB, kb * BK, c0, full_bar(stage));
+                    if constexpr (CG == 2) {
+                        // both halves complete on the leader's full barrier, which expects both
+                        const uint32_t fb = mapa_shared(full_bar(stage), 0);
+                        if (rank == 0) mbar_arrive_expect_tx(full_bar(stage), 2 * L::STAGE_BYTES);
+                        tma_load_2d_pair(sa, &tmA, kb * BK, m0, fb);
+                        tma_load_2d_pair(sb, &tmB, kb * BK, c0 + (int)rank * (BN / 2), fb);
+                    } else {
+                        mbar_arrive_expect_tx(full_bar(stage), L::STAGE_BYTES);
+                        tma_load_2d(sa, &tmA, kb * BK, m0, full_bar(stage));
+                        tma_load_2d(sb, &tmB, kb * BK, c0, full_bar(stage));
+                    }
                     issued++;
                     if (++stage == STAGES) {
                         stage = 0;
@@ -199,8 +229,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     }
                 }
             }
-            if (!ok) {
+            if (!ok && rank == 0) {
                 // let the copies this thread started land before the CTA's shared memory goes away
+                // (a pair's second CTA cannot observe its copies: they complete on the leader)
                 int s = stage, ph = phase;
                 for (int i = 0; i < (issued < STAGES ? issued : STAGES); i++) {
                     if (--s < 0) {
@@ -213,14 +244,23 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         }
     } else if (warp == 1) {
         // ------------------------------------------------------------------ MMA issuer
-        if (elect_one()) {
-            constexpr uint32_t idesc = idesc_i8(BN);
+        // commits arrive on a barrier of this CTA, or for a pair on that barrier in both CTAs
+        auto commit = [&](uint32_t bar) {
+            if constexpr (CG == 2) {
+                mma_commit_pair(mapa_shared(bar, 0));
+                mma_commit_pair(mapa_shared(bar, 1));
+            } else {
+                mma_commit(bar);
+            }
+        };
+        if (rank == 0 && elect_one()) {
+            constexpr uint32_t idesc = idesc_i8(BN, BM * CG);
             int stage = 0;
             uint32_t phase = 0;
             int acc = 0;
             uint32_t acc_phase = 0;
             bool ok = true;
-            for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+            for (int t = tfirst; t < ntiles && ok; t += tstride) {
                 for (int u = 0; u < nunits && ok; u++) {
                     if (!mbar_wait(tempty_bar(acc), acc_phase ^ 1u, p.status, E2C_ERR_WAIT_MMA)) {
                         ok = false;
@@ -236,16 +276,21 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                         tc_fence_after();
                         const uint32_t sa = sbase + stage * L::STAGE_BYTES, sb = sa + L::A_BYTES;
 #pragma unroll
-                        for (int k = 0; k < BK / 32; k++)
-                            mma_i8(d, smem_desc_sw128(sa + 32 * k), smem_desc_sw128(sb + 32 * k), idesc,
-                                   (kk | k) != 0);
-                        mma_commit(empty_bar(stage));
+                        for (int k = 0; k < BK / 32; k++) {
+                            if constexpr (CG == 2)
+                                mma_i8_pair(d, smem_desc_sw128(sa + 32 * k), smem_desc_sw128(sb + 32 * k), idesc,
+                                            (kk | k) != 0);
+                            else
+                                mma_i8(d, smem_desc_sw128(sa + 32 * k), smem_desc_sw128(sb + 32 * k), idesc,
+                                       (kk | k) != 0);
+                        }
+                        commit(empty_bar(stage));
                         if (++stage == STAGES) {
                             stage = 0;
                             phase ^= 1u;
                         }
                     }
-                    mma_commit(tfull_bar(acc));
+                    commit(tfull_bar(acc));
                     if (++acc == 2) {
                         acc = 0;
                         acc_phase ^= 1u;
@@ -255,7 +300,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             if (!ok) {
                 // every MMA issued so far must finish before the accumulator is released
                 const uint32_t drain = tfull_bar(acc);
-                mma_commit(drain);
+                if constexpr (CG == 2) mma_commit_pair(mapa_shared(drain, 0));
+                else mma_commit(drain);
                 mbar_wait(drain, acc_phase, nullptr, E2C_ERR_WAIT_DRAIN);
             }
         }
@@ -270,16 +316,70 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         int acc = 0;
         uint32_t acc_phase = 0;
         bool ok = true;
-        bool pending = false;  // a TMA store of this warp may still be reading its staging tile
+        int nst = 0;  // store groups this warp committed
+        // the staging tile for the next fp32 store: tiles alternate, and the store that last read
+        // the chosen one must have finished reading it
+        auto stg_next = [&]() -> uint8_t * {
+            uint8_t *buf = stg + (nst % L::STG_BUFS) * STG_WARP;
+            if (nst >= L::STG_BUFS) {
+                if (lane == 0) {
+                    if constexpr (L::STG_BUFS == 2) bulk_wait_read1();
+                    else bulk_wait_read0();
+                }
+                __syncwarp();
+            }
+            return buf;
+        };
         // stage 16 fp32 columns of this warp's 32 rows and store them at (x, y0)
         auto put16 = [&](const float (&v)[16], int x, int y0) {
-            if (pending) stage_reuse(lane);
-            stage_f32x16(stg, lane, v);
-            stage_store(&tmO0, stg, x, y0, lane);
-            pending = true;
+            uint8_t *buf = stg_next();
+            stage_f32x16(buf, lane, v);
+            stage_store(&tmO0, buf, x, y0, lane);
+            ++nst;
         };
-        for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
-            const int mt = (t / tiles_n) * BM;
+        // Per-tile values that do not depend on the accumulator, fetched one tile ahead: the row's
+        // activation scale, and per lane the weight scales (and for QKV the norm gains) of the
+        // columns this warp owns. They reach the math through a per-warp shared array (`cst`) read
+        // back by broadcast loads, four columns per instruction.
+        struct Pre {
+            float w0, w1, g0, g1, as;
+        };
+        auto fetch = [&](int t) -> Pre {
+            Pre r{0.f, 0.f, 1.f, 1.f, 0.f};
+            if (PERBLOCK || t >= ntiles) return r;
+            const int m = (t / tiles_n) * (BM * CG) + (int)rank * BM + row, c0 = p.n0 + (t % tiles_n) * BN;
+            if (m < M) r.as = __ldg(p.a_scale + (size_t)m * nb);
+            if constexpr (EPI == E2C_EPI_F32 || EPI == E2C_EPI_RESID) {
+                const int cw = c0 + part * QCOLS;
+                if (lane < QCOLS && cw + lane < p.n1) r.w0 = __ldg(p.w_scale + cw + lane);
+                if (32 + lane < QCOLS && cw + 32 + lane < p.n1) r.w1 = __ldg(p.w_scale + cw + 32 + lane);
+            } else if constexpr (EPI == E2C_EPI_GELU || EPI == E2C_EPI_QKV) {
+                // gate | up (GELU) or the rotate-half pair i, i + 128 (QKV) of this warp's 32 columns
+                r.w0 = __ldg(p.w_scale + c0 + 32 * part + lane);
+                r.w1 = __ldg(p.w_scale + c0 + 128 + 32 * part + lane);
+                if constexpr (EPI == E2C_EPI_QKV) {
+                    const int head = (c0 - p.n0) / 256;
+                    const float *gamma = head == p.nq + 1 ? nullptr : (head == p.nq ? p.k_gamma : p.q_gamma);
+                    if (gamma) {
+                        r.g0 = __ldg(gamma + 32 * part + lane);
+                        r.g1 = __ldg(gamma + 128 + 32 * part + lane);
+                    }
+                }
+            }
+            return r;
+        };
+        float *cst = reinterpret_cast<float *>(smem + L::CST_OFF) + (warp - 2) * 128;
+        // 16 consecutive floats of cst from `off` (a broadcast: every lane reads the same address)
+        auto cst16 = [&](int off, float (&o)[16]) {
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                const float4 w = *reinterpret_cast<const float4 *>(cst + off + 4 * k);
+                o[4 * k] = w.x, o[4 * k + 1] = w.y, o[4 * k + 2] = w.z, o[4 * k + 3] = w.w;
+            }
+        };
+        Pre pre = fetch(tfirst);
+        for (int t = tfirst; t < ntiles && ok; t += tstride) {
+            const int mt = (t / tiles_n) * (BM * CG) + (int)rank * BM;
             const int m = mt + row;
             const int c0 = p.n0 + (t % tiles_n) * BN;
             const bool mrow = m < M;
@@ -302,8 +402,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     uint32_t r[32];
                     tmem_ld32(tmem_base + lane_addr + (uint32_t)(acc * BN + part * QCOLS), r);
                     tmem_wait_ld();
-                    tc_fence_before();
-                    mbar_arrive(tempty_bar(acc));
+                    release_acc(acc);
                     if constexpr (EPI == E2C_EPI_I32) {
                         if (mrow)
                             for (int j = 0; j < 32; j++)
@@ -339,21 +438,23 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     }
                 }
             } else {
-                // values that do not depend on the accumulator are fetched while the MMA still runs:
-                // the row's activation scale and this lane's weight scales for the warp's columns
-                const float as = mrow ? __ldg(p.a_scale + (size_t)m * nb) : 0.f;
-                float wpre[2] = {0.f, 0.f};
+                const Pre cur = pre;
+                pre = fetch(t + tstride);
+                const float as = cur.as;
+                __syncwarp();  // every lane is done reading the previous tile's cst
                 if constexpr (EPI == E2C_EPI_F32 || EPI == E2C_EPI_RESID) {
-#pragma unroll
-                    for (int c = 0; c < QCOLS / 32; c++) {
-                        const int n = cw + 32 * c + lane;
-                        wpre[c] = n < p.n1 ? __ldg(p.w_scale + n) : 0.f;
-                    }
-                } else if constexpr (EPI == E2C_EPI_GELU || EPI == E2C_EPI_QKV) {
-                    // gate | up (GELU) or the rotate-half pair i, i + 128 (QKV) of this warp's 32 columns
-                    wpre[0] = __ldg(p.w_scale + c0 + 32 * part + lane);
-                    wpre[1] = __ldg(p.w_scale + c0 + 128 + 32 * part + lane);
+                    if (lane < QCOLS) cst[lane] = cur.w0;
+                    if (32 + lane < QCOLS) cst[32 + lane] = cur.w1;
+                } else if constexpr (EPI == E2C_EPI_GELU) {
+                    cst[lane] = cur.w0;
+                    cst[32 + lane] = cur.w1;
+                } else if constexpr (EPI == E2C_EPI_QKV) {
+                    cst[lane] = cur.w0;
+                    cst[32 + lane] = cur.w1;
+                    cst[64 + lane] = __fmul_rn(cur.w0, cur.g0);
+                    cst[96 + lane] = __fmul_rn(cur.w1, cur.g1);
                 }
+                __syncwarp();
                 if (!__all_sync(0xffffffffu, mbar_wait(tfull_bar(acc), acc_phase, p.status, E2C_ERR_WAIT_EPI))) {
                     ok = false;
                     break;
@@ -362,43 +463,51 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 const uint32_t tbase = tmem_base + lane_addr + (uint32_t)(acc * BN);
                 if constexpr (EPI == E2C_EPI_I32) {
 #pragma unroll 1
-                    for (int c = 0; c < QCOLS / 32; c++) {
-                        uint32_t r[32];
-                        tmem_ld32(tbase + part * QCOLS + 32 * c, r);
+                    for (int c = 0; c < QCOLS / 16; c++) {
+                        uint32_t r[16];
+                        tmem_ld16(tbase + part * QCOLS + 16 * c, r);
                         tmem_wait_ld();
-                        const int nbase = cw + 32 * c;
+                        const int nbase = cw + 16 * c;
                         if (mrow)
-                            for (int j = 0; j < 32; j++)
+                            for (int j = 0; j < 16; j++)
                                 if (nbase + j < p.n1) p.dots[(size_t)m * p.ldd + nbase + j] = (int32_t)r[j];
                     }
                 } else if constexpr (EPI == E2C_EPI_F32 || EPI == E2C_EPI_RESID) {
+                    // y = float(acc) * (as * ws), the reference's single-block fold; the clamp only
+                    // when the weight carries one (the defaults +-1e31 bound no finite output)
+                    constexpr int NCH = QCOLS / 16;
+                    const bool clamp = p.out_min > -1e30f || p.out_max < 1e30f;
 #pragma unroll
-                    for (int c = 0; c < QCOLS / 32; c++) {
-                        uint32_t r[32];
-                        tmem_ld32(tbase + part * QCOLS + 32 * c, r);
+                    for (int c2 = 0; c2 < NCH; c2 += 2) {
+                        uint32_t r[2][16];
+                        tmem_ld16(tbase + part * QCOLS + 16 * c2, r[0]);
+                        if (c2 + 1 < NCH) tmem_ld16(tbase + part * QCOLS + 16 * (c2 + 1), r[1]);
                         tmem_wait_ld();
 #pragma unroll
-                        for (int h2 = 0; h2 < 2; h2++) {
-                            const int nbase = cw + 32 * c + 16 * h2;
-                            float v[16];
+                        for (int h = 0; h < 2; h++) {
+                            if (c2 + h < NCH) {
+                                const int nbase = cw + 16 * (c2 + h);
+                                float w[16], v[16];
+                                cst16(16 * (c2 + h), w);
 #pragma unroll
-                            for (int j = 0; j < 16; j++) {
-                                const float ws = __shfl_sync(0xffffffffu, wpre[c], 16 * h2 + j);
-                                v[j] = fminf(fmaxf(dq(r[16 * h2 + j], __fmul_rn(as, ws)), p.out_min), p.out_max);
-                            }
-                            if constexpr (EPI == E2C_EPI_RESID) {
-                                if (mrow) {
-                                    const float *rr = p.resid + (size_t)m * p.ldr + nbase;
-                                    for (int j = 0; j < 16; j++)
-                                        if (nbase + j < p.n1) v[j] = __fadd_rn(v[j], rr[j]);
+                                for (int j = 0; j < 16; j++) v[j] = dq(r[h][j], __fmul_rn(as, w[j]));
+                                if (clamp)
+#pragma unroll
+                                    for (int j = 0; j < 16; j++) v[j] = fminf(fmaxf(v[j], p.out_min), p.out_max);
+                                if constexpr (EPI == E2C_EPI_RESID) {
+                                    if (mrow) {
+                                        const float *rr = p.resid + (size_t)m * p.ldr + nbase;
+                                        for (int j = 0; j < 16; j++)
+                                            if (nbase + j < p.n1) v[j] = __fadd_rn(v[j], rr[j]);
+                                    }
                                 }
-                            }
-                            if (tma_out) {
-                                put16(v, nbase - p.n0, y0);
-                            } else if (mrow && nbase < p.n1) {
-                                float *yr = p.y + (size_t)m * p.ldy + nbase;
-                                for (int j = 0; j < 16; j++)
-                                    if (nbase + j < p.n1) yr[j] = v[j];
+                                if (tma_out) {
+                                    put16(v, nbase - p.n0, y0);
+                                } else if (mrow && nbase < p.n1) {
+                                    float *yr = p.y + (size_t)m * p.ldy + nbase;
+                                    for (int j = 0; j < 16; j++)
+                                        if (nbase + j < p.n1) yr[j] = v[j];
+                                }
                             }
                         }
                     }
@@ -413,11 +522,13 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                         tmem_ld16(tbase + oc, rg);
                         tmem_ld16(tbase + 128 + oc, ru);
                         tmem_wait_ld();
-                        float h[16];
+                        float wg[16], wu[16], h[16];
+                        cst16(16 * h2, wg);
+                        cst16(32 + 16 * h2, wu);
 #pragma unroll
                         for (int j = 0; j < 16; j++) {
-                            const float g = dq(rg[j], __fmul_rn(as, __shfl_sync(0xffffffffu, wpre[0], 16 * h2 + j)));
-                            const float u = dq(ru[j], __fmul_rn(as, __shfl_sync(0xffffffffu, wpre[1], 16 * h2 + j)));
+                            const float g = dq(rg[j], __fmul_rn(as, wg[j]));
+                            const float u = dq(ru[j], __fmul_rn(as, wu[j]));
                             h[j] = __fmul_rn(gelu_tanh(g), u);
                         }
                         if (tma_out) {
@@ -431,11 +542,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 } else if constexpr (EPI == E2C_EPI_QKV) {
                     // one 256-column tile = one head (q heads, then k, then v). This warp owns
                     // rotate-half pairs i in [32 part, 32 part + 32) with their partners i + 128.
+                    // x = float(acc) * as * ws;  y = x * inv * gamma with inv = 1/sqrt(mean(x^2) + eps)
+                    // (v: no gamma), computed as float(acc) * (ws * gamma) * (as * inv); then RoPE.
                     const int head = (c0 - p.n0) / 256;
                     const bool is_k = head == p.nq, is_v = head == p.nq + 1;
-                    const float *gamma = is_v ? nullptr : (is_k ? p.k_gamma : p.q_gamma);
-                    const float gal = gamma ? __ldg(gamma + 32 * part + lane) : 1.f;
-                    const float gbl = gamma ? __ldg(gamma + 128 + 32 * part + lane) : 1.f;
+                    const int pos = mrow ? m % p.seq_len : 0;
+                    // pass 1: sum over this warp's 64 columns of (float(acc) * ws)^2
                     float ss = 0.f;
 #pragma unroll
                     for (int h2 = 0; h2 < 2; h2++) {
@@ -443,13 +555,29 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                         tmem_ld16(tbase + 32 * part + 16 * h2, ra);
                         tmem_ld16(tbase + 128 + 32 * part + 16 * h2, rb);
                         tmem_wait_ld();
+                        float wa[16], wb[16];
+                        cst16(16 * h2, wa);
+                        cst16(32 + 16 * h2, wb);
 #pragma unroll
                         for (int j = 0; j < 16; j++) {
-                            const float a = dq(ra[j], __fmul_rn(as, __shfl_sync(0xffffffffu, wpre[0], 16 * h2 + j)));
-                            const float b = dq(rb[j], __fmul_rn(as, __shfl_sync(0xffffffffu, wpre[1], 16 * h2 + j)));
+                            const float a = __fmul_rn(__int2float_rn((int)ra[j]), wa[j]);
+                            const float b = __fmul_rn(__int2float_rn((int)rb[j]), wb[j]);
                             ss = __fmaf_rn(b, b, __fmaf_rn(a, a, ss));
                         }
                     }
+                    // RoPE coefficients of the first 16 pairs load while the row norms are exchanged
+                    float csv[16], snv[16];
+                    auto rope_load = [&](int ia) {
+                        const float4 *cs4 = reinterpret_cast<const float4 *>(p.rope_cos + (size_t)pos * 128 + ia);
+                        const float4 *sn4 = reinterpret_cast<const float4 *>(p.rope_sin + (size_t)pos * 128 + ia);
+#pragma unroll
+                        for (int j = 0; j < 4; j++) {
+                            const float4 c4 = __ldg(cs4 + j), s4 = __ldg(sn4 + j);
+                            csv[4 * j] = c4.x, csv[4 * j + 1] = c4.y, csv[4 * j + 2] = c4.z, csv[4 * j + 3] = c4.w;
+                            snv[4 * j] = s4.x, snv[4 * j + 1] = s4.y, snv[4 * j + 2] = s4.z, snv[4 * j + 3] = s4.w;
+                        }
+                    };
+                    if (!is_v) rope_load(32 * part);
                     // the row's sum of squares over the four warps of this quadrant (same rows)
                     float *ssq = reinterpret_cast<float *>(smem + L::SSQ_OFF) + acc * 4 * BM;
                     ssq[part * BM + row] = ss;
@@ -459,46 +587,36 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                         break;
                     }
                     const float sst = __fadd_rn(__fadd_rn(ssq[row], ssq[BM + row]), __fadd_rn(ssq[2 * BM + row], ssq[3 * BM + row]));
-                    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sst, 256.0f), p.eps)));
-                    const int pos = mrow ? m % p.seq_len : 0;
-                    if (!is_v && tma_out && pending) stage_reuse(lane);
+                    const float ms = __fmul_rn(__fmul_rn(as, as), __fdiv_rn(sst, 256.0f));
+                    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, p.eps)));
+                    const float rs = __fmul_rn(as, inv);
+                    if (!is_v && tma_out && nst > 0) {
+                        // the previous tile's stores have read both staging halves
+                        if (lane == 0) bulk_wait_read0();
+                        __syncwarp();
+                    }
 #pragma unroll
                     for (int h2 = 0; h2 < 2; h2++) {
                         const int ia = 32 * part + 16 * h2;  // rotate-half index of these 16 pairs
                         uint32_t ra[16], rb[16];
                         tmem_ld16(tbase + ia, ra);
                         tmem_ld16(tbase + 128 + ia, rb);
+                        if (h2 == 1 && !is_v) rope_load(ia);
                         tmem_wait_ld();
-                        float csv[16], snv[16];
-                        if (!is_v) {
-                            const float4 *cs4 = reinterpret_cast<const float4 *>(p.rope_cos + (size_t)pos * 128 + ia);
-                            const float4 *sn4 = reinterpret_cast<const float4 *>(p.rope_sin + (size_t)pos * 128 + ia);
-#pragma unroll
-                            for (int j = 0; j < 4; j++) {
-                                const float4 c4 = __ldg(cs4 + j), s4 = __ldg(sn4 + j);
-                                csv[4 * j] = c4.x, csv[4 * j + 1] = c4.y, csv[4 * j + 2] = c4.z, csv[4 * j + 3] = c4.w;
-                                snv[4 * j] = s4.x, snv[4 * j + 1] = s4.y, snv[4 * j + 2] = s4.z, snv[4 * j + 3] = s4.w;
-                            }
-                        }
-                        float va[16], vb[16];
+                        float ca[16], cb[16], va[16], vb[16];
+                        cst16(64 + 16 * h2, ca);
+                        cst16(96 + 16 * h2, cb);
 #pragma unroll
                         for (int j = 0; j < 16; j++) {
-                            const int jj = 16 * h2 + j;
-                            float a = __fmul_rn(dq(ra[j], __fmul_rn(as, __shfl_sync(0xffffffffu, wpre[0], jj))), inv);
-                            float b = __fmul_rn(dq(rb[j], __fmul_rn(as, __shfl_sync(0xffffffffu, wpre[1], jj))), inv);
-                            const float ga = __shfl_sync(0xffffffffu, gal, jj), gb = __shfl_sync(0xffffffffu, gbl, jj);
-                            if (gamma) {
-                                a = __fmul_rn(a, ga);
-                                b = __fmul_rn(b, gb);
-                            }
+                            const float a = __fmul_rn(__fmul_rn(__int2float_rn((int)ra[j]), ca[j]), rs);
+                            const float b = __fmul_rn(__fmul_rn(__int2float_rn((int)rb[j]), cb[j]), rs);
                             if (!is_v) {
-                                const float oa = __fmaf_rn(a, csv[j], -__fmul_rn(b, snv[j]));
-                                const float ob = __fmaf_rn(a, snv[j], __fmul_rn(b, csv[j]));
-                                a = oa;
-                                b = ob;
+                                va[j] = __fmaf_rn(a, csv[j], -__fmul_rn(b, snv[j]));
+                                vb[j] = __fmaf_rn(a, snv[j], __fmul_rn(b, csv[j]));
+                            } else {
+                                va[j] = a;
+                                vb[j] = b;
                             }
-                            va[j] = a;
-                            vb[j] = b;
                         }
                         if (is_v) {
                             if (mrow) {
@@ -533,11 +651,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                             tma_store_2d(tm, smem_u32(stg + STG_WARP), xb + 128 + 32 * part, y0);
                             bulk_commit();
                         }
-                        pending = true;
+                        ++nst;
                     }
                 }
-                tc_fence_before();
-                mbar_arrive(tempty_bar(acc));
+                release_acc(acc);
                 if (++acc == 2) {
                     acc = 0;
                     acc_phase ^= 1u;
@@ -550,20 +667,25 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
 
     tc_fence_before();
-    __syncthreads();
+    // a pair: neither CTA leaves while the other may still signal its barriers
+    if constexpr (CG == 2) cluster_sync();
+    else __syncthreads();
     if (warp == 1) {
+        __syncwarp();
         tc_fence_after();
-        tmem_dealloc(tmem_base, TMEM_COLS);
+        if constexpr (CG == 2) tmem_dealloc_pair(tmem_base, TMEM_COLS);
+        else tmem_dealloc(tmem_base, TMEM_COLS);
     }
 }
 
 int g_num_sms = 0;
 
-template <int BN, int STAGES, bool PERBLOCK, int EPI>
+template <int BN, int STAGES, bool PERBLOCK, int EPI, int CG>
 int launch(const e2c_gemm_args *a, cudaStream_t st) {
-    using L = GemmSmem<BN, STAGES, EPI>;
-    auto kern = k_gemm_i8<BN, STAGES, PERBLOCK, EPI>;
+    using L = GemmSmem<BN, STAGES, PERBLOCK, EPI, CG>;
+    auto kern = k_gemm_i8<BN, STAGES, PERBLOCK, EPI, CG>;
     static bool attr_set = false;
+    static int max_pairs = 0;  // CTA pairs the device holds at once (CG = 2)
     if (!attr_set) {
         if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC) != cudaSuccess) {
             e2c_set_msg("gemm: cannot reserve %d bytes of shared memory", L::ALLOC);
@@ -575,7 +697,7 @@ int launch(const e2c_gemm_args *a, cudaStream_t st) {
     if (e2c_tmap_2d(&ta, a->a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)a->K, (uint64_t)a->M, (uint64_t)a->lda,
                     BK, BM) ||
         e2c_tmap_2d(&tb, a->w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)a->K, (uint64_t)a->wrows,
-                    (uint64_t)a->ldw, BK, BN))
+                    (uint64_t)a->ldw, BK, BN / CG))
         return -3;
     memset(&t0, 0, sizeof t0);
     memset(&t1, 0, sizeof t1);
@@ -597,10 +719,37 @@ int launch(const e2c_gemm_args *a, cudaStream_t st) {
                                         (uint64_t)a->M, (uint64_t)512 * a->nq, 32, 32) &&
                       !e2c_tmap_2d_sw64(&t1, a->k_out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 256, (uint64_t)a->M, 512, 32, 32);
     }
-    const int tiles = ((a->M + BM - 1) / BM) * ((a->n1 - a->n0 + BN - 1) / BN);
-    const int grid = tiles < g_num_sms ? tiles : g_num_sms;
-    kern<<<grid, NTHREADS, L::ALLOC, st>>>(ta, tb, t0, t1, *a, tma_out);
-    const cudaError_t e = cudaGetLastError();
+    const int tiles = ((a->M + BM * CG - 1) / (BM * CG)) * ((a->n1 - a->n0 + BN - 1) / BN);
+    cudaError_t e;
+    if constexpr (CG == 1) {
+        const int grid = tiles < g_num_sms ? tiles : g_num_sms;
+        kern<<<grid, NTHREADS, L::ALLOC, st>>>(ta, tb, t0, t1, *a, tma_out);
+        e = cudaGetLastError();
+    } else {
+        cudaLaunchConfig_t cfg;
+        memset(&cfg, 0, sizeof cfg);
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.blockDim = dim3(NTHREADS);
+        cfg.dynamicSmemBytes = L::ALLOC;
+        cfg.stream = st;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        if (!max_pairs) {
+            cfg.gridDim = dim3(2 * (g_num_sms / 2));
+            if (cudaOccupancyMaxActiveClusters(&max_pairs, kern, &cfg) != cudaSuccess || max_pairs <= 0) {
+                cudaGetLastError();
+                max_pairs = 0;
+                e2c_set_msg("gemm: the device cannot hold a pair of GEMM CTAs");
+                return -2;
+            }
+        }
+        cfg.gridDim = dim3(2 * (tiles < max_pairs ? tiles : max_pairs));
+        e = cudaLaunchKernelEx(&cfg, kern, ta, tb, t0, t1, *a, tma_out);
+    }
     if (e != cudaSuccess) {
         e2c_set_msg("gemm launch: %s", cudaGetErrorString(e));
         return -2;
@@ -608,20 +757,43 @@ int launch(const e2c_gemm_args *a, cudaStream_t st) {
     return 0;
 }
 
-int pick_bn(const e2c_gemm_args *a) {
-    if (a->ablk != a->K) return 128;                         // per-block fold keeps BN/4 floats per thread
-    if (a->epi == E2C_EPI_GELU || a->epi == E2C_EPI_QKV) return 256;
+// Tile plan: width BN and whether CTA pairs (M = 256 per pair, each SM loading half of the weight
+// tile: a third less operand traffic per MAC) share tiles.
+struct Plan {
+    int bn, cg;
+};
+
+Plan pick_plan(const e2c_gemm_args *a) {
+    if (a->ablk != a->K) return {128, 1};                    // per-block fold keeps BN/4 floats per thread
     const int ncols = a->n1 - a->n0;
-    const int t256 = ((a->M + BM - 1) / BM) * ((ncols + 255) / 256);
-    return t256 * 2 <= g_num_sms ? 128 : 256;                // small problems: more, narrower tiles
+    const long pairs256 = (long)((a->M + 2 * BM - 1) / (2 * BM)) * ((ncols + 255) / 256);
+    // pairs pay off once they fill the device (a full wave of 256-row tiles) and both CTAs of a
+    // pair have rows of their own: with M <= 256 the second one would only multiply zeros
+    const int cg = (pairs256 >= g_num_sms / 2 && a->M > 2 * BM) ? 2 : 1;
+    if (a->epi == E2C_EPI_GELU || a->epi == E2C_EPI_QKV) return {256, cg};
+    // the width whose waves of persistent tiles cost least: a tile's time ~ BN + a fixed 32
+    const int slots = cg == 2 ? g_num_sms / 2 : g_num_sms;
+    const long tm = (a->M + BM * cg - 1) / (BM * cg);
+    int best = 256;
+    long best_cost = -1;
+    for (int bn : {256, 192, 128}) {
+        const long units = tm * ((ncols + bn - 1) / bn);
+        const long cost = (units + slots - 1) / slots * (bn + 32);
+        if (best_cost < 0 || cost < best_cost) {
+            best = bn;
+            best_cost = cost;
+        }
+    }
+    return {best, cg};
 }
 
 }  // namespace
 
 extern "C" void e2c_gemm_tile(const e2c_gemm_args *a, int *bm, int *bn) {
     if (!g_num_sms) cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, 0);
-    *bm = BM;
-    *bn = pick_bn(a);
+    const Plan pl = pick_plan(a);
+    *bm = BM * pl.cg;
+    *bn = pl.bn;
 }
 
 extern "C" int e2c_gemm(const e2c_gemm_args *a, void *stream) {
@@ -650,29 +822,48 @@ extern "C" int e2c_gemm(const e2c_gemm_args *a, void *stream) {
     if (a->M == 0 || a->n1 == a->n0) return 0;
     cudaStream_t st = (cudaStream_t)stream;
     const bool perblock = a->ablk != a->K;
-    const int bn = pick_bn(a);
+    const Plan pl = pick_plan(a);
+    const bool pair = pl.cg == 2;
     switch (a->epi) {
     case E2C_EPI_F32:
-        if (perblock) return launch<128, 6, true, E2C_EPI_F32>(a, st);
-        return bn == 128 ? launch<128, 6, false, E2C_EPI_F32>(a, st) : launch<256, 4, false, E2C_EPI_F32>(a, st);
+        if (perblock) return launch<128, 6, true, E2C_EPI_F32, 1>(a, st);
+        if (pair)
+            return pl.bn == 128   ? launch<128, 6, false, E2C_EPI_F32, 2>(a, st)
+                   : pl.bn == 192 ? launch<192, 6, false, E2C_EPI_F32, 2>(a, st)
+                                  : launch<256, 5, false, E2C_EPI_F32, 2>(a, st);
+        return pl.bn == 128   ? launch<128, 4, false, E2C_EPI_F32, 1>(a, st)
+               : pl.bn == 192 ? launch<192, 3, false, E2C_EPI_F32, 1>(a, st)
+                              : launch<256, 3, false, E2C_EPI_F32, 1>(a, st);
     case E2C_EPI_RESID:
-        if (perblock) return launch<128, 6, true, E2C_EPI_RESID>(a, st);
-        return bn == 128 ? launch<128, 6, false, E2C_EPI_RESID>(a, st) : launch<256, 4, false, E2C_EPI_RESID>(a, st);
+        if (perblock) return launch<128, 6, true, E2C_EPI_RESID, 1>(a, st);
+        if (pair)
+            return pl.bn == 128   ? launch<128, 6, false, E2C_EPI_RESID, 2>(a, st)
+                   : pl.bn == 192 ? launch<192, 6, false, E2C_EPI_RESID, 2>(a, st)
+                                  : launch<256, 5, false, E2C_EPI_RESID, 2>(a, st);
+        return pl.bn == 128   ? launch<128, 4, false, E2C_EPI_RESID, 1>(a, st)
+               : pl.bn == 192 ? launch<192, 3, false, E2C_EPI_RESID, 1>(a, st)
+                              : launch<256, 3, false, E2C_EPI_RESID, 1>(a, st);
     case E2C_EPI_I32:
-        if (perblock) return launch<128, 6, true, E2C_EPI_I32>(a, st);
-        return bn == 128 ? launch<128, 6, false, E2C_EPI_I32>(a, st) : launch<256, 4, false, E2C_EPI_I32>(a, st);
+        if (perblock) return launch<128, 6, true, E2C_EPI_I32, 1>(a, st);
+        if (pair)
+            return pl.bn == 128   ? launch<128, 6, false, E2C_EPI_I32, 2>(a, st)
+                   : pl.bn == 192 ? launch<192, 6, false, E2C_EPI_I32, 2>(a, st)
+                                  : launch<256, 6, false, E2C_EPI_I32, 2>(a, st);
+        return pl.bn == 128   ? launch<128, 6, false, E2C_EPI_I32, 1>(a, st)
+               : pl.bn == 192 ? launch<192, 4, false, E2C_EPI_I32, 1>(a, st)
+                              : launch<256, 4, false, E2C_EPI_I32, 1>(a, st);
     case E2C_EPI_GELU:
         if (perblock || (a->n1 - a->n0) % 256 || a->n0 % 256 || a->ldy % 4) {
             e2c_set_msg("gemm: the GELU-gate epilogue needs per-row scales and 256-column (gate|up) groups");
             return -1;
         }
-        return launch<256, 4, false, E2C_EPI_GELU>(a, st);
+        return pair ? launch<256, 5, false, E2C_EPI_GELU, 2>(a, st) : launch<256, 3, false, E2C_EPI_GELU, 1>(a, st);
     case E2C_EPI_QKV:
         if (perblock || a->n0 != 0 || a->n1 != 256 * (a->nq + 2) || a->seq_len <= 0 || a->M % a->seq_len) {
             e2c_set_msg("gemm: the QKV epilogue needs per-row scales, whole heads of 256 and M a multiple of seq_len");
             return -1;
         }
-        return launch<256, 3, false, E2C_EPI_QKV>(a, st);
+        return pair ? launch<256, 4, false, E2C_EPI_QKV, 2>(a, st) : launch<256, 3, false, E2C_EPI_QKV, 1>(a, st);
     default:
         e2c_set_msg("gemm: unknown epilogue %d", a->epi);
         return -1;

@@ -102,6 +102,8 @@ E2C_DEV void tma_store_2d(const CUtensorMap *m, uint32_t src, int x, int y) {
 E2C_DEV void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // the shared-memory sources of every committed store have been read (the buffer may be rewritten)
 E2C_DEV void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// the same for all but the most recently committed group
+E2C_DEV void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
 // every committed store has completed
 E2C_DEV void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 E2C_DEV void named_barrier(int id, int nthreads) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory"); }
@@ -117,6 +119,16 @@ E2C_DEV void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
 E2C_DEV void tmem_relinquish() { asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory"); }
 E2C_DEV void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+// The same for a CTA pair (cta_group::2): issued by the same warp in both CTAs of the cluster, which
+// then hold the same TMEM address.
+E2C_DEV void tmem_alloc_pair(uint32_t dst_smem, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(ncols)
+                 : "memory");
+}
+E2C_DEV void tmem_relinquish_pair() { asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory"); }
+E2C_DEV void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
 }
 E2C_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 E2C_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
@@ -155,6 +167,57 @@ E2C_DEV void mma_commit(uint32_t bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
 }
 
+// ------------------------------------------------------------------------------- CTA pairs
+// A pair of CTAs (a cluster of two) runs one M = 256 product: each CTA holds 128 rows of A and half
+// of B's N rows in its shared memory, and 128 rows x N of the accumulator in its TMEM. The MMA and
+// its commits are issued by the CTA of rank 0 (the leader) only.
+E2C_DEV uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// the shared::cluster address of the variable at shared::cta address `addr` in the CTA of `rank`
+E2C_DEV uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+    return r;
+}
+// every thread of both CTAs (release / acquire at cluster scope); the non-.aligned forms, so that
+// warps whose lanes arrive at different times (one elected lane did the role's work) are fine
+E2C_DEV void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+// arrive on an mbarrier given by its shared::cluster address (possibly in the other CTA), with
+// the default semantics (release at CTA scope); cluster-scope release made every arrival wait for
+// the thread's earlier writes and stalled the epilogue between tiles
+E2C_DEV void mbar_arrive_cluster(uint32_t bar_cluster) {
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
+}
+// 2D tiled TMA load into this CTA's shared memory whose completed bytes are counted on the
+// mbarrier `bar_cluster` (a shared::cluster address: the leader's barrier). No multicast.
+E2C_DEV void tma_load_2d_pair(uint32_t dst, const CUtensorMap *m, int x, int y, uint32_t bar_cluster) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+        "l"(m), "r"(x), "r"(y), "r"(bar_cluster)
+        : "memory");
+}
+// M = 256 int8 product over the pair: A and B descriptors address the leader's shared memory; the
+// same offsets in the other CTA hold its rows of A and its half of B.
+E2C_DEV void mma_i8_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// Arrive once on the mbarrier at shared::cluster address `bar_cluster` when every pair MMA this
+// thread issued so far has completed.
+E2C_DEV void mma_commit_pair(uint32_t bar_cluster) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar_cluster)
+                 : "memory");
+}
+
 // K-major operand tile in shared memory with the 128-byte swizzle: rows of 128 bytes, 8-row
 // groups 1024 bytes apart (SBO), the leading offset unused. Base must be 1024-byte aligned; a
 // k-step inside the 128-byte row advances the start address.
@@ -168,11 +231,11 @@ E2C_DEV uint64_t smem_desc_sw128(uint32_t addr) {
 }
 
 // Instruction descriptors (M = 128, K-major A and B, dense).
-__host__ __device__ constexpr uint32_t idesc_i8(int n) {
+__host__ __device__ constexpr uint32_t idesc_i8(int n, int m = 128) {
     return (2u << 4)            // D = s32
            | (1u << 7)          // A = s8
            | (1u << 10)         // B = s8
-           | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+           | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
 }
 __host__ __device__ constexpr uint32_t idesc_bf16(int n) {
     return (1u << 4)            // D = f32
