@@ -822,6 +822,18 @@ extern "C" int e2c_gemm(const e2c_gemm_args *a, void *stream) {
     if (a->M == 0 || a->n1 == a->n0) return 0;
     cudaStream_t st = (cudaStream_t)stream;
     const bool perblock = a->ablk != a->K;
+    {
+        // short activation matrices: when the persistent kernel would leave most SMs idle, split K
+        // over a cluster so every SM streams a slice of the weight
+        int sbn = 0, S = 1;
+        const int split_ctas = e2c_gemm_splitk_plan(a, g_num_sms, &sbn, &S);
+        if (split_ctas) {
+            const Plan pp = pick_plan(a);
+            const long ptiles = (long)((a->M + BM * pp.cg - 1) / (BM * pp.cg)) * ((a->n1 - a->n0 + pp.bn - 1) / pp.bn);
+            const long pctas = (ptiles < g_num_sms / pp.cg ? ptiles : g_num_sms / pp.cg) * pp.cg;
+            if (split_ctas >= 2 * pctas) return e2c_gemm_splitk(a, sbn, S, stream);
+        }
+    }
     const Plan pl = pick_plan(a);
     const bool pair = pl.cg == 2;
     switch (a->epi) {

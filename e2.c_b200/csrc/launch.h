@@ -68,6 +68,14 @@ typedef struct {
 } e2c_gemm_args;
 
 int e2c_gemm(const e2c_gemm_args *a, void *stream);
+/* The same GEMM with K split over a cluster of S CTAs per 128 x bn output tile (S a power of two,
+ * 2..16; bn 128 or 256), partial sums reduced in distributed shared memory: the launcher e2c_gemm
+ * picks it for short activation matrices (few output tiles). Per-row scales, F32 or residual
+ * epilogue only. */
+int e2c_gemm_splitk(const e2c_gemm_args *a, int bn, int S, void *stream);
+/* the split that puts most CTAs to work with every cluster resident at once: returns the CTA count
+ * (0 when the split kernel does not apply) and sets *bn, *S */
+int e2c_gemm_splitk_plan(const e2c_gemm_args *a, int num_sms, int *bn, int *S);
 /* the tile the GEMM picks for these arguments, for traffic accounting: *bm x *bn */
 void e2c_gemm_tile(const e2c_gemm_args *a, int *bm, int *bn);
 
