@@ -20,7 +20,7 @@
 
 #include "internal.h"
 
-#define MAX_GRAPHS 16
+#define MAX_GRAPHS 128
 
 typedef struct {
     int B, S, has_valid;
