@@ -65,6 +65,7 @@ static const char *status_name(int s) {
     case 0x104: return "attention softmax timed out";
     case 0x105: return "drain of in-flight copies timed out";
     case 0x106: return "token id outside the embedding table";
+    case 0x107: return "dynamic shared memory not 1024-byte aligned (kernel skipped)";
     default: return "unknown device failure";
     }
 }

@@ -21,7 +21,8 @@ enum {
     E2C_ERR_WAIT_EPI = 0x103,       // epilogue gave up waiting for an accumulator
     E2C_ERR_WAIT_ATTN = 0x104,      // attention softmax / correction gave up
     E2C_ERR_WAIT_DRAIN = 0x105,     // teardown gave up draining in-flight copies
-    E2C_ERR_BAD_TOKEN = 0x106       // a token id outside the table (row 0 used instead)
+    E2C_ERR_BAD_TOKEN = 0x106,      // a token id outside the table (row 0 used instead)
+    E2C_ERR_SMEM_ALIGN = 0x107      // dynamic shared memory not 1024-byte aligned: the kernel did nothing
 };
 
 E2C_DEV uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }

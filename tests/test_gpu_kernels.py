@@ -371,7 +371,11 @@ def _attn_ref(q, k, v, valid, B, S, H, scale):
 
 @pytest.mark.parametrize("B,S,H,scale,masked", [(2, 300, 3, 1 / 16, True), (3, 512, 3, 1 / 16, False),
                                                 (1, 64, 3, 1 / 16, False), (2, 1, 3, 1 / 16, False),
-                                                (2, 700, 3, 1.0, True), (1, 130, 1, 1 / 16, False)])
+                                                (2, 700, 3, 1.0, True), (1, 130, 1, 1 / 16, False),
+                                                # more units (sequence, head, query tile) than SMs: the
+                                                # persistent CTAs carry state from one unit to the next
+                                                (16, 512, 3, 1 / 16, False), (24, 300, 3, 1 / 16, True),
+                                                (150, 64, 1, 1 / 16, True)])
 def test_attention_vs_fp64(e2c, torch_cuda, B, S, H, scale, masked):
     torch = torch_cuda
     rng = np.random.default_rng(S * 10 + B)
