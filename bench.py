@@ -177,7 +177,7 @@ def main() -> int:
     ap.add_argument("--impl", default="e2cuda", choices=["e2cuda", "reference"])
     ap.add_argument("--layers", type=int, default=24, help=argparse.SUPPRESS)  # debugging only; headline uses 24
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--kernel", default=None, choices=["gate_up", "qkv", "down", "attention", "quantize"],
+    ap.add_argument("--kernel", default=None, choices=list(KERNELS),
                     help="run one encoder kernel --steps times at the encoder's shapes (for ncu captures)")
     ap.add_argument("--tokens", type=int, default=BATCH * SEQ, help="tokens for --kernel (a multiple of 512)")
     ap.add_argument("--chunk", type=int, default=CHUNK,
@@ -286,10 +286,11 @@ def main() -> int:
     e2e_ms = max_over_ranks(dist, e2e_ms, dev)
     e2e = n * BATCH * args.steps / (e2e_ms / 1e3)
 
-    # the dominant kernel in isolation: the gate|up GEMM of one layer (M = 32768, N = 2304, K = 768)
-    roof = None
+    # every kernel of a layer in isolation; the roofline object is the dominant one's
+    roof, table = None, None
     if rank == 0:
-        roof = gate_up_roofline(e2c, syn, w, dev, stream)
+        table = kernel_table(dev, stream)
+        roof = dominant_roofline(table)
     cpu = None
     if rank == 0 and not args.no_cpu_baseline:
         try:
@@ -306,7 +307,10 @@ def main() -> int:
                 "clocks": clk.summary(),
                 "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": int(ids_pin.numel() * 4),
                         "d2h_bytes_per_step": int(out_pin.numel() * 4)},
-                "gpu_launches": int(kernels * passes * args.steps), "roofline": roof, "cpu_baseline": cpu}
+                "gpu_launches": int(kernels * passes * args.steps), "roofline": roof,
+                "kernels": {k: {kk: v[kk] for kk in ("bound", "achieved", "unit", "frac", "avg_ms", "traffic")}
+                            for k, v in (table or {}).items()},
+                "cpu_baseline": cpu}
         print(json.dumps(line))
     enc.close()
     if dist:
@@ -393,41 +397,144 @@ def config4(args) -> int:
     return 0
 
 
-def gate_up_roofline(e2c, syn, w, dev, stream) -> dict:
-    """CUDA-event timing of the gate|up GEMM with its GELU-gate epilogue at the encoder's shape,
-    against 2x the measured bf16 tensor peak (B200 dense int8 = 2x dense bf16)."""
+# One layer's kernels at the encoder's shape (M = 64 x 512 tokens, hidden 768, FFN 1152, 3 q heads and
+# one KV head of 256), the per-launch algorithmic work each is measured against, and the launches of
+# each per layer. Weights are quantised N(0, 0.02), activations per-token quantised N(0, 1).
+KERNELS = ("gate_up", "qkv", "o_proj", "down", "attention", "quantize", "quantize_ctx", "norm_add")
+
+
+def kernel_work(name: str, M: int) -> dict:
+    D, I, H, Dh = 768, 1152, 3, 256
+    if name in ("gate_up", "qkv", "o_proj", "down"):
+        N, K = {"gate_up": (2 * I, D), "qkv": ((H + 2) * Dh, D), "o_proj": (D, D), "down": (D, I)}[name]
+        out_bytes = {"gate_up": 4 * M * I, "qkv": 2 * M * N, "o_proj": 4 * M * D, "down": 4 * M * D}[name]
+        return {"bound": "tensor", "ops": 2.0 * M * N * K, "bytes": M * K + 4 * M + N * K + 4 * N + out_bytes,
+                "per_layer": 1}
+    if name == "attention":
+        return {"bound": "tensor", "ops": 4.0 * M * SEQ * Dh * H, "bytes": M * (H + 2) * Dh * 2 + 4 * M * H * Dh,
+                "per_layer": 1}
+    if name in ("quantize", "quantize_ctx"):
+        K = I if name == "quantize" else D
+        return {"bound": "hbm", "ops": 0.0, "bytes": M * (4 * K + K + 4), "per_layer": 1}
+    return {"bound": "hbm", "ops": 0.0, "bytes": M * (3 * 4 * D + D + 4), "per_layer": 2}  # norm_add
+
+
+def kernel_runner(name: str, M: int, dev, stream):
+    """A closure launching one encoder kernel at token count M (multiple of 512) on `stream`, plus the
+    buffers it keeps alive."""
+    import ctypes as C
+
     import torch
 
-    M, D, I = BATCH * SEQ, w.cfg.hidden, w.cfg.ffn
-    lay = w.layers[0]
-    wi = np.empty((2 * I, D), np.int8)
-    si = np.empty(2 * I, np.float32)
-    for t in range(I // 128):
-        wi[256 * t:256 * t + 128], si[256 * t:256 * t + 128] = lay["wg"].q[128 * t:128 * t + 128], lay["wg"].scale[128 * t:128 * t + 128]
-        wi[256 * t + 128:256 * t + 256] = lay["wu"].q[128 * t:128 * t + 128]
-        si[256 * t + 128:256 * t + 256] = lay["wu"].scale[128 * t:128 * t + 128]
-    W = e2c.Weight(w=wi, scale=si)
+    e2c = load_pkg()
+    import e2c_b200.synthetic as syn
+
+    D, I, Dh, H = 768, 1152, 256, 3
     g = torch.Generator(device=dev).manual_seed(5)
-    qa = torch.randint(-127, 128, (M, D), dtype=torch.int8, device=dev, generator=g)
-    qs = torch.rand((M, 1), device=dev, generator=g) * 0.05 + 1e-3
-    h = torch.empty((M, I), dtype=torch.float32, device=dev)
-    a = e2c.gemm_args(W, qa, qs, M)
-    a.epi, a.y, a.ldy = e2c.EPI_GELU, h.data_ptr(), I
-    avg_ms = timed_launches(lambda: e2c.gemm_raw(a, stream), stream, 3, 10)
-    e2c.check(stream)
-    ops = 2.0 * M * (2 * I) * D
+    rng = np.random.default_rng(5)
+
+    def qin(K):
+        return e2c.quantize_rows(torch.randn((M, K), device=dev, generator=g), K)
+
+    keep = []
+    if name in ("gate_up", "qkv", "o_proj", "down"):
+        N, K = {"gate_up": (2 * I, D), "qkv": ((H + 2) * Dh, D), "o_proj": (D, D), "down": (D, I)}[name]
+        wq, ws = syn.quantize_weight_rows((rng.standard_normal((N, K)) * 0.02).astype(np.float32))
+        W = e2c.Weight(w=wq, scale=ws)
+        qa, qs = qin(K)
+        a = e2c.gemm_args(W, qa, qs, M)
+        keep = [W, qa, qs]
+        if name == "gate_up":
+            y = torch.empty((M, I), dtype=torch.float32, device=dev)
+            a.epi, a.y, a.ldy = e2c.EPI_GELU, y.data_ptr(), I
+            keep.append(y)
+        elif name in ("down", "o_proj"):
+            y = torch.empty((M, D), dtype=torch.float32, device=dev)
+            a.epi, a.y, a.ldy = e2c.EPI_F32, y.data_ptr(), D
+            keep.append(y)
+        else:
+            Q = torch.empty((M, H * Dh), dtype=torch.bfloat16, device=dev)
+            Kt = torch.empty((M, Dh), dtype=torch.bfloat16, device=dev)
+            Vt = torch.empty((M // SEQ, Dh, SEQ), dtype=torch.bfloat16, device=dev)
+            gam = torch.ones(Dh, device=dev)
+            cs = torch.rand((SEQ, Dh // 2), device=dev)
+            keep += [Q, Kt, Vt, gam, cs]
+            a.epi, a.nq, a.q_out, a.k_out, a.vt_out, a.ldvt, a.seq_len = e2c.EPI_QKV, H, Q.data_ptr(), Kt.data_ptr(), Vt.data_ptr(), SEQ, SEQ
+            a.q_gamma = a.k_gamma = gam.data_ptr()
+            a.rope_cos = a.rope_sin = cs.data_ptr()
+            a.eps = 1e-6
+        return (lambda: e2c.gemm_raw(a, stream)), keep
+    if name == "attention":
+        B = M // SEQ
+        q = torch.randn((M, H * Dh), device=dev, generator=g).to(torch.bfloat16)
+        k = torch.randn((M, Dh), device=dev, generator=g).to(torch.bfloat16)
+        vt = torch.randn((B, Dh, SEQ), device=dev, generator=g).to(torch.bfloat16)
+        return (lambda: e2c.attention(q, k, vt, None, B, SEQ, H, 1.0 / 16, stream)), [q, k, vt]
+    if name in ("quantize", "quantize_ctx"):
+        K = I if name == "quantize" else D
+        x = torch.randn((M, K), device=dev, generator=g)
+        q = torch.empty((M, K), dtype=torch.int8, device=dev)
+        s_ = torch.empty((M, 1), dtype=torch.float32, device=dev)
+        lib = e2c.lib()
+        return (lambda: e2c._ok(lib.e2cuda_quantize_rows(x.data_ptr(), q.data_ptr(), s_.data_ptr(), M, K, K,
+                                                        -math.inf, math.inf, e2c._stream(stream)), "quantize")), [x, q, s_]
+    # norm_add: x = rmsnorm(t) * g1 + res; res = x; q = quantise(rmsnorm(x) * g2), per token
+    lib = e2c.lib()
+    fn = lib.e2c_norm_add_norm_quant
+    fn.restype = C.c_int
+    fn.argtypes = [C.c_void_p] * 5 + [C.c_float, C.c_void_p, C.c_void_p] + [C.c_int] * 3 + [C.c_void_p]
+    t = torch.randn((M, D), device=dev, generator=g)
+    res = torch.randn((M, D), device=dev, generator=g)
+    g1 = torch.ones(D, device=dev)
+    g2 = torch.ones(D, device=dev)
+    q = torch.empty((M, D), dtype=torch.int8, device=dev)
+    s_ = torch.empty((M, 1), dtype=torch.float32, device=dev)
+    run = lambda: e2c._ok(fn(t.data_ptr(), res.data_ptr(), g1.data_ptr(), g2.data_ptr(), None, 1e-6, q.data_ptr(),
+                             s_.data_ptr(), M, D, D, e2c._stream(stream)), "norm_add_norm_quant")
+    return run, [t, res, g1, g2, q, s_]
+
+
+def kernel_table(dev, stream, M: int = BATCH * SEQ, steps: int = 10) -> dict:
+    """CUDA-event time of every encoder kernel at the encoder's shape (L2 flushed before each launch)
+    with its roofline fraction against the measured peaks."""
+    e2c = load_pkg()
     p = peaks()
-    peak = 2.0 * p["bf16_tflops"]
-    achieved = ops / (avg_ms / 1e3) / 1e12
-    traffic = None
+    int8_peak, bf16_peak, hbm = 2.0 * p["bf16_tflops"], p["bf16_tflops"], p["hbm_gbs"]
+    traffic = {}
     tf = ROOT / "profiles" / "traffic.json"
     if tf.exists():
-        traffic = json.loads(tf.read_text()).get("gate_up_gemm_M32768")
-    return {"kernel": "k_gemm_i8<256,4,per-row,GELU> gate|up 32768x2304x768", "bound": "tensor",
-            "achieved": achieved, "peak": peak, "unit": "TOPS (int8)", "frac": achieved / peak,
-            "peak_src": f"2 x {p['src']} bf16 {p['bf16_tflops']} TFLOP/s (dense int8 rate = 2x bf16)",
-            "avg_ms": avg_ms, "algorithmic_bytes": M * D + 4 * M + 2 * I * D + 8 * I + 4 * M * I,
-            "traffic": traffic}
+        traffic = json.loads(tf.read_text())
+    table = {}
+    for name in KERNELS:
+        run, keep = kernel_runner(name, M, dev, stream)
+        ms = timed_launches(run, stream, 3, steps)
+        e2c.check(stream)
+        wk = kernel_work(name, M)
+        if wk["bound"] == "tensor":
+            peak = bf16_peak if name == "attention" else int8_peak
+            achieved, unit = wk["ops"] / (ms / 1e3) / 1e12, "TFLOP/s"
+        else:
+            peak, achieved, unit = hbm, wk["bytes"] / (ms / 1e3) / 1e9, "GB/s"
+        table[name] = {"bound": wk["bound"], "achieved": achieved, "peak": peak, "unit": unit, "frac": achieved / peak,
+                       "avg_ms": ms, "launches_per_layer": wk["per_layer"], "algorithmic_bytes": wk["bytes"],
+                       "traffic": traffic.get(name)}
+        del run, keep
+    return table
+
+
+def dominant_roofline(table: dict) -> dict:
+    """The roofline of the kernel with the largest share of a layer's time (time x launches per layer)."""
+    name = max(table, key=lambda k: table[k]["avg_ms"] * table[k]["launches_per_layer"])
+    p = peaks()
+    r = dict(table[name])
+    r["kernel"] = name
+    if r["bound"] == "hbm":
+        r["peak_src"] = f"{p['src']} HBM copy {p['hbm_gbs']} GB/s"
+    elif name == "attention":
+        r["peak_src"] = f"{p['src']} bf16 {p['bf16_tflops']} TFLOP/s"
+    else:
+        r["peak_src"] = f"2 x {p['src']} bf16 {p['bf16_tflops']} TFLOP/s (dense int8 = 2 x dense bf16; int8 ops counted as FLOP)"
+    return r
 
 
 def kernel_only(args) -> int:
@@ -435,56 +542,13 @@ def kernel_only(args) -> int:
     import torch
 
     e2c = load_pkg()
-    import e2c_b200.synthetic as syn
-
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
-    M, D, I, Dh, H = args.tokens, 768, 1152, 256, 3
-    g = torch.Generator(device=dev).manual_seed(5)
-    rng = np.random.default_rng(5)
     stream = torch.cuda.Stream(device=dev)
-
-    def qin(K):
-        # per-token quantised N(0,1) activations, as the encoder's row kernels produce them
-        return e2c.quantize_rows(torch.randn((M, K), device=dev, generator=g), K)
-
-    if args.kernel in ("gate_up", "qkv", "down"):
-        N, K = {"gate_up": (2 * I, D), "qkv": ((H + 2) * Dh, D), "down": (D, I)}[args.kernel]
-        wq, ws = syn.quantize_weight_rows((rng.standard_normal((N, K)) * 0.02).astype(np.float32))
-        W = e2c.Weight(w=wq, scale=ws)
-        qa, qs = qin(K)
-        a = e2c.gemm_args(W, qa, qs, M)
-        keep = []
-        if args.kernel == "gate_up":
-            y = torch.empty((M, I), dtype=torch.float32, device=dev)
-            a.epi, a.y, a.ldy = e2c.EPI_GELU, y.data_ptr(), I
-        elif args.kernel == "down":
-            y = torch.empty((M, D), dtype=torch.float32, device=dev)
-            a.epi, a.y, a.ldy = e2c.EPI_F32, y.data_ptr(), D
-        else:
-            Q = torch.empty((M, H * Dh), dtype=torch.bfloat16, device=dev)
-            Kt = torch.empty((M, Dh), dtype=torch.bfloat16, device=dev)
-            Vt = torch.empty((M // SEQ, Dh, SEQ), dtype=torch.bfloat16, device=dev)
-            gam = torch.ones(Dh, device=dev)
-            cs = torch.rand((SEQ, Dh // 2), device=dev)
-            keep = [Q, Kt, Vt, gam, cs]
-            a.epi, a.nq, a.q_out, a.k_out, a.vt_out, a.ldvt, a.seq_len = e2c.EPI_QKV, H, Q.data_ptr(), Kt.data_ptr(), Vt.data_ptr(), SEQ, SEQ
-            a.q_gamma = a.k_gamma = gam.data_ptr()
-            a.rope_cos = a.rope_sin = cs.data_ptr()
-            a.eps = 1e-6
-        run = lambda: e2c.gemm_raw(a, stream)
-    elif args.kernel == "attention":
-        B = M // SEQ
-        q = torch.randn((M, H * Dh), device=dev, generator=g).to(torch.bfloat16)
-        k = torch.randn((M, Dh), device=dev, generator=g).to(torch.bfloat16)
-        vt = torch.randn((B, Dh, SEQ), device=dev, generator=g).to(torch.bfloat16)
-        run = lambda: e2c.attention(q, k, vt, None, B, SEQ, H, 1.0 / 16, stream)
-    else:
-        x = torch.randn((M, I), device=dev, generator=g)
-        run = lambda: e2c.quantize_rows(x, I, stream=stream)
+    run, keep = kernel_runner(args.kernel, args.tokens, dev, stream)
     avg_ms = timed_launches(run, stream, args.warmup, args.steps)
     e2c.check(stream)
-    print(json.dumps({"kernel": args.kernel, "tokens": M, "avg_ms": avg_ms, "l2": "flushed between launches"}))
+    print(json.dumps({"kernel": args.kernel, "tokens": args.tokens, "avg_ms": avg_ms, "l2": "flushed between launches"}))
     return 0
 
 
