@@ -400,14 +400,23 @@ def config4(args) -> int:
 # One layer's kernels at the encoder's shape (M = 64 x 512 tokens, hidden 768, FFN 1152, 3 q heads and
 # one KV head of 256), the per-launch algorithmic work each is measured against, and the launches of
 # each per layer. Weights are quantised N(0, 0.02), activations per-token quantised N(0, 1).
-KERNELS = ("gate_up", "qkv", "o_proj", "down", "attention", "quantize", "quantize_ctx", "norm_add")
+KERNELS = ("gate_up", "qkv", "o_proj", "down", "o_proj_norm", "down_norm", "attention", "quantize", "quantize_ctx",
+           "norm_add")
+# the kernels an encoder layer runs (hidden 768, per-token scales; the residual norms run as their own
+# row kernel after o_proj and down unless E2C_FUSED_NORM=1 fuses them into those GEMMs)
+LAYER_KERNELS = ("gate_up", "qkv", "o_proj", "down", "attention", "quantize", "quantize_ctx", "norm_add")
+if os.environ.get("E2C_FUSED_NORM") == "1":
+    LAYER_KERNELS = ("gate_up", "qkv", "o_proj_norm", "down_norm", "attention", "quantize", "quantize_ctx")
 
 
 def kernel_work(name: str, M: int) -> dict:
     D, I, H, Dh = 768, 1152, 3, 256
-    if name in ("gate_up", "qkv", "o_proj", "down"):
-        N, K = {"gate_up": (2 * I, D), "qkv": ((H + 2) * Dh, D), "o_proj": (D, D), "down": (D, I)}[name]
-        out_bytes = {"gate_up": 4 * M * I, "qkv": 2 * M * N, "o_proj": 4 * M * D, "down": 4 * M * D}[name]
+    if name in ("gate_up", "qkv", "o_proj", "down", "o_proj_norm", "down_norm"):
+        N, K = {"gate_up": (2 * I, D), "qkv": ((H + 2) * Dh, D), "o_proj": (D, D), "down": (D, I),
+                "o_proj_norm": (D, D), "down_norm": (D, I)}[name]
+        # the fused norm epilogue reads and writes the fp32 residual and writes int8 rows + scales
+        out_bytes = {"gate_up": 4 * M * I, "qkv": 2 * M * N, "o_proj": 4 * M * D, "down": 4 * M * D,
+                     "o_proj_norm": 8 * M * D + M * D + 4 * M, "down_norm": 8 * M * D + M * D + 4 * M}[name]
         return {"bound": "tensor", "ops": 2.0 * M * N * K, "bytes": M * K + 4 * M + N * K + 4 * N + out_bytes,
                 "per_layer": 1}
     if name == "attention":
@@ -437,8 +446,9 @@ def kernel_runner(name: str, M: int, dev, stream):
         return e2c.quantize_rows(torch.randn((M, K), device=dev, generator=g), K)
 
     keep = []
-    if name in ("gate_up", "qkv", "o_proj", "down"):
-        N, K = {"gate_up": (2 * I, D), "qkv": ((H + 2) * Dh, D), "o_proj": (D, D), "down": (D, I)}[name]
+    if name in ("gate_up", "qkv", "o_proj", "down", "o_proj_norm", "down_norm"):
+        N, K = {"gate_up": (2 * I, D), "qkv": ((H + 2) * Dh, D), "o_proj": (D, D), "down": (D, I),
+                "o_proj_norm": (D, D), "down_norm": (D, I)}[name]
         wq, ws = syn.quantize_weight_rows((rng.standard_normal((N, K)) * 0.02).astype(np.float32))
         W = e2c.Weight(w=wq, scale=ws)
         qa, qs = qin(K)
@@ -452,6 +462,15 @@ def kernel_runner(name: str, M: int, dev, stream):
             y = torch.empty((M, D), dtype=torch.float32, device=dev)
             a.epi, a.y, a.ldy = e2c.EPI_F32, y.data_ptr(), D
             keep.append(y)
+        elif name in ("down_norm", "o_proj_norm"):
+            res = torch.randn((M, D), device=dev, generator=g)
+            g1 = torch.ones(D, device=dev)
+            q8 = torch.empty((M, D), dtype=torch.int8, device=dev)
+            q8s = torch.empty((M,), dtype=torch.float32, device=dev)
+            keep += [res, g1, q8, q8s]
+            a.epi, a.eps, a.res, a.ldres = e2c.EPI_NORMADD, 1e-6, res.data_ptr(), D
+            a.norm_g1 = a.norm_g2 = g1.data_ptr()
+            a.q8, a.ldq, a.q8_scale = q8.data_ptr(), D, q8s.data_ptr()
         else:
             Q = torch.empty((M, H * Dh), dtype=torch.bfloat16, device=dev)
             Kt = torch.empty((M, Dh), dtype=torch.bfloat16, device=dev)
@@ -505,7 +524,7 @@ def kernel_table(dev, stream, M: int = BATCH * SEQ, steps: int = 10) -> dict:
     if tf.exists():
         traffic = json.loads(tf.read_text())
     table = {}
-    for name in KERNELS:
+    for name in LAYER_KERNELS:
         run, keep = kernel_runner(name, M, dev, stream)
         ms = timed_launches(run, stream, 3, steps)
         e2c.check(stream)

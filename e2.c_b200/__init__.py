@@ -67,7 +67,7 @@ class EncoderDesc(C.Structure):
 
 class GemmArgs(C.Structure):
     """Mirror of e2c_gemm_args (csrc/launch.h), the launcher under e2cuda_i8_gemm: the fused
-    epilogues (GELU-gate, per-head norm + RoPE) are reached only through it. Used by the parity
+    epilogues (GELU-gate, per-head norm + RoPE, residual norm + quantise) are reached only through it. Used by the parity
     tests and by bench.py to time one encoder GEMM in isolation."""
 
     _fields_ = [("a", C.c_void_p), ("lda", C.c_int), ("a_scale", C.c_void_p), ("w", C.c_void_p), ("ldw", C.c_int),
@@ -77,10 +77,12 @@ class GemmArgs(C.Structure):
                 ("out_min", C.c_float), ("out_max", C.c_float), ("nq", C.c_int), ("q_out", C.c_void_p),
                 ("k_out", C.c_void_p), ("vt_out", C.c_void_p), ("ldvt", C.c_int), ("seq_len", C.c_int),
                 ("q_gamma", C.c_void_p), ("k_gamma", C.c_void_p), ("rope_cos", C.c_void_p),
-                ("rope_sin", C.c_void_p), ("eps", C.c_float), ("status", C.c_void_p)]
+                ("rope_sin", C.c_void_p), ("eps", C.c_float), ("res", C.c_void_p), ("ldres", C.c_int),
+                ("norm_g1", C.c_void_p), ("norm_g2", C.c_void_p), ("norm_gf", C.c_void_p), ("q8", C.c_void_p),
+                ("ldq", C.c_int), ("q8_scale", C.c_void_p), ("status", C.c_void_p)]
 
 
-EPI_F32, EPI_RESID, EPI_I32, EPI_GELU, EPI_QKV = 0, 1, 2, 3, 4
+EPI_F32, EPI_RESID, EPI_I32, EPI_GELU, EPI_QKV, EPI_NORMADD = 0, 1, 2, 3, 4, 5
 
 
 def gemm_args(w: "Weight", qa, a_scales, M: int) -> GemmArgs:

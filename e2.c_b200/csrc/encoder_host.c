@@ -2,15 +2,22 @@
  * one device pass per chunk of whole sequences, replayed from a CUDA graph per shape.
  *
  * Layer recipe: e2.c src/text.c:939-961 without the PLE block; head: masked mean pool -> dense ->
- * dense -> L2 (the config-2 head). Per layer, 9 kernels:
+ * dense -> L2 (the config-2 head). Per layer:
  *
  *   [prev tail] norm_add + norm_split + quant      (layer 0: embed gather + norm + quant)
  *   GEMM q|k|v  -> per-head RMSNorm + RoPE -> bf16 Q, K, V^T     (epilogue, gemm_i8.cu)
  *   attention   -> ctx fp32                                       (attention.cu)
- *   quant ctx ; GEMM o_proj -> tmp
- *   norm_add(post_attn) + norm_split(pre_ffn) + quant
- *   GEMM gate|up -> GELU(g)*u (epilogue) ; quant h ; GEMM down -> tmp
- *   norm_add(post_ffn) + norm_split(next input_ln) + quant   (last layer: final norm)
+ *   quant ctx ; GEMM o_proj + norm_add(post_attn) + norm_split(pre_ffn) + quant
+ *   GEMM gate|up -> GELU(g)*u (epilogue) ; quant h
+ *   GEMM down + norm_add(post_ffn) + norm_split(next input_ln) + quant   (last layer: final norm)
+ *
+ * With per-token scales and a hidden size of 192 x (1..4) the residual norms run in the o_proj and
+ * down GEMMs' epilogue (whole rows per cluster of CTAs; 7 kernels per layer); otherwise the GEMM
+ * writes fp32 and a row kernel applies them (9 kernels per layer).
+ *
+ * int8 activations alternate between two buffers: the layer's input (and the fused tails' output)
+ * in qb, the quantised ctx and h in qa. A fused tail writes int8 rows of its output while other CTAs
+ * still read the GEMM's input rows, so the two must never be the same buffer.
  */
 #include <math.h>
 #include <stdio.h>
@@ -41,8 +48,9 @@ struct e2cuda_encoder {
     int32_t *ids;
     uint8_t *valid;
     float *out, *res, *tmp, *ctx, *h, *pooled, *h1;
-    int8_t *qa, *pq;
-    float *qs, *ps;
+    int8_t *qa, *qb, *pq;
+    float *qs, *qsb, *ps;
+    int fused_norm;
     void *Q, *K, *Vt;
     size_t vt_bytes;
     int *status;
@@ -108,7 +116,8 @@ void e2cuda_encoder_destroy(e2cuda_encoder *e) {
     e2cuda_w8_free(&e->dense1);
     e2cuda_w8_free(&e->dense2);
     void *dev[] = { e->table, e->table_scale, e->norms, e->rope_cos, e->rope_sin, e->ids, e->valid, e->out, e->res,
-                    e->tmp, e->ctx, e->h, e->pooled, e->h1, e->qa, e->pq, e->qs, e->ps, e->Q, e->K, e->Vt };
+                    e->tmp, e->ctx, e->h, e->pooled, e->h1, e->qa, e->qb, e->pq, e->qs, e->qsb, e->ps, e->Q, e->K,
+                    e->Vt };
     for (size_t i = 0; i < sizeof dev / sizeof dev[0]; i++)
         if (dev[i]) cudaFree(dev[i]);
     if (e->host_out) cudaFreeHost(e->host_out);
@@ -240,12 +249,19 @@ e2cuda_encoder *e2cuda_encoder_create(const e2cuda_encoder_desc *d, int max_toke
         if (DALLOC(e->ids, sizeof(int32_t) * M) || DALLOC(e->valid, M) || DALLOC(e->res, sizeof(float) * M * D) ||
             DALLOC(e->tmp, sizeof(float) * M * D) || DALLOC(e->ctx, sizeof(float) * M * GD) ||
             DALLOC(e->h, sizeof(float) * M * e->I) || DALLOC(e->qa, M * (size_t)KQ) ||
-            DALLOC(e->qs, sizeof(float) * M * (size_t)(KQ / 128 + 1)) || DALLOC(e->Q, 2 * M * GD) ||
+            DALLOC(e->qs, sizeof(float) * M * (size_t)(KQ / 128 + 1)) || DALLOC(e->qb, M * (size_t)D) ||
+            DALLOC(e->qsb, sizeof(float) * M * (size_t)(D / 128 + 1)) || DALLOC(e->Q, 2 * M * GD) ||
             DALLOC(e->K, 2 * M * e->Dh) || DALLOC(e->out, sizeof(float) * MB * e->DO) ||
             DALLOC(e->pooled, sizeof(float) * MB * D) || DALLOC(e->h1, sizeof(float) * MB * e->DH) ||
             DALLOC(e->pq, MB * (size_t)(e->DH > D ? e->DH : D)) ||
             DALLOC(e->ps, sizeof(float) * MB * (size_t)((e->DH > D ? e->DH : D) / 128 + 1)))
             goto fail;
+    }
+    /* The GEMM with the residual norms in its epilogue (one launch instead of two) is opt-in by
+     * E2C_FUSED_NORM=1 until it beats the GEMM + row-kernel pair at the encoder's shapes. */
+    {
+        const char *fz = getenv("E2C_FUSED_NORM");
+        e->fused_norm = fz && fz[0] == '1' && e->ablk == D && D % 192 == 0 && D / 192 <= 4;
     }
     e->status = e2cu_status();
     if (!e->status || e2cu_cuda(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking), "stream")) goto fail;
@@ -257,6 +273,38 @@ fail:
 
 static int round8(int x) { return (x + 7) & ~7; }
 
+/* o_proj / down and the residual norms after them: res = rmsnorm(gemm) * g1 + res, then qb / qsb =
+ * quantise(rmsnorm(res) * g2), or (g2 NULL, after the last layer) res = rmsnorm(res) * gf. Adds the
+ * kernels queued to *n. */
+static int gemm_norms(e2cuda_encoder *e, const e2cuda_w8 *w, int M, int ablk, const float *g1, const float *g2,
+                      const float *gf, int *n, cudaStream_t st, const char *what) {
+    const int D = e->D;
+    e2c_gemm_args a;
+    e2cu_gemm_args(&a, w, e->qa, e->qs, M, ablk);
+    if (e->fused_norm) {
+        a.epi = E2C_EPI_NORMADD;
+        a.res = e->res;
+        a.ldres = D;
+        a.norm_g1 = g1;
+        a.norm_g2 = g2;
+        a.norm_gf = gf;
+        a.q8 = g2 ? e->qb : NULL;
+        a.ldq = D;
+        a.q8_scale = g2 ? e->qsb : NULL;
+        a.eps = e->eps;
+        *n += 1;
+        return e2cu_launch(e2c_gemm(&a, st), what);
+    }
+    a.epi = E2C_EPI_F32;
+    a.y = e->tmp;
+    a.ldy = D;
+    *n += 2;
+    return e2cu_launch(e2c_gemm(&a, st), what) ||
+           e2cu_launch(e2c_norm_add_norm_quant(e->tmp, e->res, g1, g2, gf, e->eps, e->qb, e->qsb, M, D,
+                                               e->ablk == D ? D : 128, st),
+                       what);
+}
+
 /* queue one pass over B sequences of S tokens already in e->ids / e->valid; returns kernels queued */
 static int encode(e2cuda_encoder *e, int B, int S, int has_valid, cudaStream_t st) {
     const int M = B * S, D = e->D, GD = e->H * e->Dh, I = e->I, L = e->L;
@@ -265,14 +313,14 @@ static int encode(e2cuda_encoder *e, int B, int S, int has_valid, cudaStream_t s
     const uint8_t *valid = has_valid ? e->valid : NULL;
     int n = 0;
     if (e2cu_launch(e2c_embed_norm_quant(e->ids, e->table, e->table_scale, e->embed_scale, nrm(e, 0, 0), e->eps, e->res,
-                                         e->qa, e->qs, M, D, ab_d, e->V, e->status, st),
+                                         e->qb, e->qsb, M, D, ab_d, e->V, e->status, st),
                     "encoder embed"))
         return -1;
     n++;
     e2c_gemm_args a;
     for (int l = 0; l < L; l++) {
         /* q|k|v with per-head RMSNorm + RoPE */
-        e2cu_gemm_args(&a, &e->wqkv[l], e->qa, e->qs, M, ab_d);
+        e2cu_gemm_args(&a, &e->wqkv[l], e->qb, e->qsb, M, ab_d);
         a.epi = E2C_EPI_QKV;
         a.nq = e->H;
         a.q_out = e->Q;
@@ -292,16 +340,8 @@ static int encode(e2cuda_encoder *e, int B, int S, int has_valid, cudaStream_t s
         if (e2cu_launch(e2c_quantize(e->ctx, GD, e->qa, GD, e->qs, M, GD, ab_gd, -INFINITY, INFINITY, 0, st),
                         "encoder ctx quant"))
             return -1;
-        e2cu_gemm_args(&a, &e->wo[l], e->qa, e->qs, M, ab_gd);
-        a.epi = E2C_EPI_F32;
-        a.y = e->tmp;
-        a.ldy = D;
-        if (e2cu_launch(e2c_gemm(&a, st), "encoder o_proj")) return -1;
-        if (e2cu_launch(e2c_norm_add_norm_quant(e->tmp, e->res, nrm(e, l, 1), nrm(e, l, 2), NULL, e->eps, e->qa, e->qs, M,
-                                                D, ab_d, st),
-                        "encoder post-attention norms"))
-            return -1;
-        e2cu_gemm_args(&a, &e->wgu[l], e->qa, e->qs, M, ab_d);
+        if (gemm_norms(e, &e->wo[l], M, ab_gd, nrm(e, l, 1), nrm(e, l, 2), NULL, &n, st, "encoder o_proj + norms")) return -1;
+        e2cu_gemm_args(&a, &e->wgu[l], e->qb, e->qsb, M, ab_d);
         a.epi = E2C_EPI_GELU;
         a.y = e->h;
         a.ldy = I;
@@ -309,17 +349,11 @@ static int encode(e2cuda_encoder *e, int B, int S, int has_valid, cudaStream_t s
         if (e2cu_launch(e2c_quantize(e->h, I, e->qa, I, e->qs, M, I, ab_i, -INFINITY, INFINITY, 0, st),
                         "encoder h quant"))
             return -1;
-        e2cu_gemm_args(&a, &e->wd[l], e->qa, e->qs, M, ab_i);
-        a.epi = E2C_EPI_F32;
-        a.y = e->tmp;
-        a.ldy = D;
-        if (e2cu_launch(e2c_gemm(&a, st), "encoder down")) return -1;
         const int last = l + 1 == L;
-        if (e2cu_launch(e2c_norm_add_norm_quant(e->tmp, e->res, nrm(e, l, 3), last ? NULL : nrm(e, l + 1, 0),
-                                                last ? final_norm(e) : NULL, e->eps, e->qa, e->qs, M, D, ab_d, st),
-                        "encoder post-ffn norms"))
+        if (gemm_norms(e, &e->wd[l], M, ab_i, nrm(e, l, 3), last ? NULL : nrm(e, l + 1, 0), last ? final_norm(e) : NULL,
+                       &n, st, "encoder down + norms"))
             return -1;
-        n += 9;
+        n += 5;
     }
     /* head */
     const int ab_dh = e->ablk == D ? e->DH : 128;

@@ -51,14 +51,21 @@ struct GemmSmem {
     static constexpr int STG_BUFS = (EPI == E2C_EPI_QKV || (!PERBLOCK && EPI != E2C_EPI_I32 && CG == 1)) ? 2 : 1;
     static constexpr int STG_PER_WARP = STG_BUFS * STG_WARP;
     static constexpr int STG_OFF = STAGES * STAGE_BYTES;
-    // per-warp column constants (weight scales, norm gains): 128 floats
+    // per-warp column constants (weight scales, norm gains): 128 floats (NORMADD: 192)
+    static constexpr int CST_FLOATS = EPI == E2C_EPI_NORMADD ? 192 : 128;
     static constexpr int CST_OFF = STG_OFF + EPI_WARPS * STG_PER_WARP;
-    static constexpr int CST_BYTES = (PERBLOCK || EPI == E2C_EPI_I32) ? 0 : EPI_WARPS * 128 * 4;
+    static constexpr int CST_BYTES = (PERBLOCK || EPI == E2C_EPI_I32) ? 0 : EPI_WARPS * CST_FLOATS * 4;
     static constexpr int SSQ_OFF = CST_OFF + CST_BYTES;
     static constexpr int SSQ_BYTES = EPI == E2C_EPI_QKV ? 2 * 4 * BM * 4 : 0;  // [acc][part][row]
-    static constexpr int BAR_OFF = SSQ_OFF + SSQ_BYTES;
-    // full[S], empty[S], tfull[2], tempty[2], pair[2][4] (QKV row-norm exchange), tmem slot
-    static constexpr int NBAR = 2 * STAGES + 4 + 8;
+    // NORMADD row exchanges: local partials [4 parts][128 rows] (round 0: float, round 1: float2),
+    // then one partial per CTA of the cluster [NCL][128] (float, float2)
+    static constexpr int NCL = 4;
+    static constexpr int NRM_OFF = SSQ_OFF + SSQ_BYTES;
+    static constexpr int NRM_BYTES = EPI == E2C_EPI_NORMADD ? (4 * BM * 12 + NCL * BM * 12) : 0;
+    static constexpr int BAR_OFF = NRM_OFF + NRM_BYTES;
+    // full[S], empty[S], tfull[2], tempty[2], pair[2][4] (QKV row-norm exchange), NORMADD lbar[2][4]
+    // and xbar[2][4], tmem slot
+    static constexpr int NBAR = 2 * STAGES + 4 + 8 + (EPI == E2C_EPI_NORMADD ? 16 : 0);
     static constexpr int BYTES = BAR_OFF + NBAR * 8 + 16;
     static constexpr int ALLOC = BYTES + 1024;  // slack for 1024-byte alignment
     static_assert(ALLOC <= 232448, "shared memory");
@@ -139,6 +146,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     auto tfull_bar = [&](int a) { return bar0 + 8u * (2 * STAGES + a); };
     auto tempty_bar = [&](int a) { return bar0 + 8u * (2 * STAGES + 2 + a); };
     auto pair_bar = [&](int a, int q) { return bar0 + 8u * (2 * STAGES + 4 + 4 * a + q); };
+    auto lbar = [&](int r, int q) { return bar0 + 8u * (2 * STAGES + 12 + 4 * r + q); };
+    auto xbar = [&](int r, int q) { return bar0 + 8u * (2 * STAGES + 20 + 4 * r + q); };
     volatile uint32_t *tmem_slot = reinterpret_cast<volatile uint32_t *>(smem + L::BAR_OFF + L::NBAR * 8);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -166,6 +175,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             mbar_init(tempty_bar(a), EPI_WARPS * CG);  // one arrival per epilogue warp of the pair
             for (int q = 0; q < 4; q++) mbar_init(pair_bar(a, q), 128);
         }
+        if constexpr (EPI == E2C_EPI_NORMADD)
+            for (int r = 0; r < 2; r++)
+                for (int q = 0; q < 4; q++) {
+                    mbar_init(lbar(r, q), 128);             // the 4 warps of a lane quadrant
+                    mbar_init(xbar(r, q), 1);               // this CTA's expect_tx; the bytes come by st.async
+                }
         fence_mbar_init();
         tma_prefetch_desc(&tmA);
         tma_prefetch_desc(&tmB);
@@ -181,8 +196,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         }
     }
     tc_fence_before();
-    // a pair: the leader's barriers are initialised before the other CTA signals them
-    if constexpr (CG == 2) cluster_sync();
+    // a pair (or a NORMADD cluster): every CTA's barriers are initialised before another signals them
+    if constexpr (CG == 2 || EPI == E2C_EPI_NORMADD) cluster_sync();
     else __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
@@ -349,7 +364,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             if (PERBLOCK || t >= ntiles) return r;
             const int m = (t / tiles_n) * (BM * CG) + (int)rank * BM + row, c0 = p.n0 + (t % tiles_n) * BN;
             if (m < M) r.as = __ldg(p.a_scale + (size_t)m * nb);
-            if constexpr (EPI == E2C_EPI_F32 || EPI == E2C_EPI_RESID) {
+            if constexpr (EPI == E2C_EPI_F32 || EPI == E2C_EPI_RESID || EPI == E2C_EPI_NORMADD) {
                 const int cw = c0 + part * QCOLS;
                 if (lane < QCOLS && cw + lane < p.n1) r.w0 = __ldg(p.w_scale + cw + lane);
                 if (32 + lane < QCOLS && cw + 32 + lane < p.n1) r.w1 = __ldg(p.w_scale + cw + 32 + lane);
@@ -368,7 +383,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             }
             return r;
         };
-        float *cst = reinterpret_cast<float *>(smem + L::CST_OFF) + (warp - 2) * 128;
+        float *cst = reinterpret_cast<float *>(smem + L::CST_OFF) + (warp - 2) * L::CST_FLOATS;
+        int ntile = 0;  // tiles this warp finished (NORMADD exchange parity)
         // 16 consecutive floats of cst from `off` (a broadcast: every lane reads the same address)
         auto cst16 = [&](int off, float (&o)[16]) {
 #pragma unroll
@@ -445,6 +461,20 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 if constexpr (EPI == E2C_EPI_F32 || EPI == E2C_EPI_RESID) {
                     if (lane < QCOLS) cst[lane] = cur.w0;
                     if (32 + lane < QCOLS) cst[32 + lane] = cur.w1;
+                } else if constexpr (EPI == E2C_EPI_NORMADD) {
+                    // [0, 64) weight scales, [64, 128) first norm gain, [128, 192) second (or final) gain
+                    const float *gb = p.norm_g2 ? p.norm_g2 : p.norm_gf;
+                    const int cl = part * QCOLS - p.n0 + c0;  // this warp's first column within the row
+                    if (lane < QCOLS) {
+                        cst[lane] = cur.w0;
+                        cst[64 + lane] = __ldg(p.norm_g1 + cl + lane);
+                        cst[128 + lane] = __ldg(gb + cl + lane);
+                    }
+                    if (32 + lane < QCOLS) {
+                        cst[32 + lane] = cur.w1;
+                        cst[96 + lane] = __ldg(p.norm_g1 + cl + 32 + lane);
+                        cst[160 + lane] = __ldg(gb + cl + 32 + lane);
+                    }
                 } else if constexpr (EPI == E2C_EPI_GELU) {
                     cst[lane] = cur.w0;
                     cst[32 + lane] = cur.w1;
@@ -510,6 +540,169 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                                 }
                             }
                         }
+                    }
+                } else if constexpr (EPI == E2C_EPI_NORMADD) {
+                    // The GEMM output t of this tile never leaves the SM. Per row (768 columns over
+                    // the cluster's CTAs): inv1 = 1/sqrt(mean t^2 + eps); x = t inv1 g1 + res;
+                    // inv2 = 1/sqrt(mean x^2 + eps); res = x and q = quantise(x inv2 g2) per token,
+                    // or res = x inv2 gf (the final norm). Row sums and maxima are exchanged in two
+                    // rounds: the quadrant's 4 warps combine their columns in shared memory, one warp
+                    // sends the CTA's partial to every CTA of the cluster, all wait for all of them.
+                    constexpr int NCH = QCOLS / 16;
+                    const int ncl = tiles_n;  // CTAs of the cluster = column blocks of a row
+                    const int D = p.n1 - p.n0;
+                    const int cw0 = c0 + part * QCOLS;  // first (absolute) column of this warp
+                    const uint32_t par = (uint32_t)(ntile & 1);
+                    float *xl0 = reinterpret_cast<float *>(smem + L::NRM_OFF);                 // [4][BM]
+                    float2 *xl1 = reinterpret_cast<float2 *>(smem + L::NRM_OFF + 4 * BM * 4);  // [4][BM]
+                    const uint32_t xr0 = sbase + L::NRM_OFF + 4 * BM * 12;                    // [NCL][BM] float
+                    const uint32_t xr1 = xr0 + L::NCL * BM * 4;                               // [NCL][BM] float2
+                    const int myblk = (c0 - p.n0) / BN;                                       // = cluster rank
+                    bool xok = true;
+                    // round r: combine this warp's partial (sum in .x, max in .y) over the row's columns
+                    auto exchange = [&](int r, float2 v) -> float2 {
+                        if (r == 0) xl0[part * BM + row] = v.x;
+                        else xl1[part * BM + row] = v;
+                        mbar_arrive(lbar(r, q));
+                        if (part == 0) {
+                            xok = xok && __all_sync(0xffffffffu, mbar_wait(lbar(r, q), par, p.status, E2C_ERR_WAIT_EPI));
+                            float2 c = make_float2(0.f, 0.f);
+                            if (xok) {
+#pragma unroll
+                                for (int w = 0; w < 4; w++) {
+                                    if (r == 0) {
+                                        c.x = __fadd_rn(c.x, xl0[w * BM + row]);
+                                    } else {
+                                        const float2 o = xl1[w * BM + row];
+                                        c.x = __fadd_rn(c.x, o.x);
+                                        c.y = fmaxf(c.y, o.y);
+                                    }
+                                }
+                            }
+                            // this CTA expects one partial per row of the quadrant from every CTA
+                            if (lane == 0) mbar_arrive_expect_tx(xbar(r, q), (uint32_t)(ncl * 32 * (r == 0 ? 4 : 8)));
+                            for (int d = 0; d < ncl; d++) {
+                                const uint32_t slot = (r == 0 ? xr0 + (uint32_t)((myblk * BM + row) * 4)
+                                                              : xr1 + (uint32_t)((myblk * BM + row) * 8));
+                                const uint32_t rb = mapa_shared(xbar(r, q), (uint32_t)d);
+                                if (r == 0) st_async_f32(mapa_shared(slot, (uint32_t)d), c.x, rb);
+                                else st_async_f32x2(mapa_shared(slot, (uint32_t)d), c.x, c.y, rb);
+                            }
+                        }
+                        xok = xok && __all_sync(0xffffffffu, mbar_wait(xbar(r, q), par, p.status, E2C_ERR_WAIT_EPI));
+                        float2 tot = make_float2(0.f, 0.f);
+                        for (int d = 0; d < ncl; d++) {
+                            if (r == 0) {
+                                tot.x = __fadd_rn(tot.x, *reinterpret_cast<const float *>(smem + (xr0 - sbase) + (d * BM + row) * 4));
+                            } else {
+                                const float2 o = *reinterpret_cast<const float2 *>(smem + (xr1 - sbase) + (d * BM + row) * 8);
+                                tot.x = __fadd_rn(tot.x, o.x);
+                                tot.y = fmaxf(tot.y, o.y);
+                            }
+                        }
+                        return tot;
+                    };
+                    // t for 16 columns of chunk c: the reference's single-block fold
+                    auto tval = [&](int c, float (&t)[16]) {
+                        uint32_t r[16];
+                        tmem_ld16(tbase + part * QCOLS + 16 * c, r);
+                        tmem_wait_ld();
+                        float w[16];
+                        cst16(16 * c, w);
+#pragma unroll
+                        for (int j = 0; j < 16; j++) t[j] = dq(r[j], __fmul_rn(as, w[j]));
+                    };
+                    // x = (t inv1) g1 + res for 16 columns of chunk c (0 past the last row)
+                    auto xval = [&](int c, float inv1, float (&x)[16]) {
+                        float t[16], g[16];
+                        tval(c, t);
+                        cst16(64 + 16 * c, g);
+                        float rv[16];
+                        if (mrow) {
+                            const float4 *r4 = reinterpret_cast<const float4 *>(p.res + (size_t)m * p.ldres + cw0 + 16 * c);
+#pragma unroll
+                            for (int k = 0; k < 4; k++) {
+                                const float4 v4 = r4[k];
+                                rv[4 * k] = v4.x, rv[4 * k + 1] = v4.y, rv[4 * k + 2] = v4.z, rv[4 * k + 3] = v4.w;
+                            }
+                        } else {
+#pragma unroll
+                            for (int j = 0; j < 16; j++) rv[j] = 0.f;
+                        }
+#pragma unroll
+                        for (int j = 0; j < 16; j++) x[j] = __fadd_rn(__fmul_rn(__fmul_rn(t[j], inv1), g[j]), rv[j]);
+                    };
+                    // pass 1: sum of t^2
+                    float ss = 0.f;
+#pragma unroll
+                    for (int c = 0; c < NCH; c++) {
+                        float t[16];
+                        tval(c, t);
+#pragma unroll
+                        for (int j = 0; j < 16; j++) ss = __fmaf_rn(t[j], t[j], ss);
+                    }
+                    const float inv1 = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(exchange(0, make_float2(ss, 0.f)).x, (float)D), p.eps)));
+                    // pass 2: sum of x^2 and max |x g2|
+                    const bool quant = p.norm_g2 != nullptr;
+                    float ss2 = 0.f, mx = 0.f;
+#pragma unroll
+                    for (int c = 0; c < NCH; c++) {
+                        float x[16], g[16];
+                        xval(c, inv1, x);
+                        cst16(128 + 16 * c, g);
+#pragma unroll
+                        for (int j = 0; j < 16; j++) {
+                            ss2 = __fmaf_rn(x[j], x[j], ss2);
+                            mx = fmaxf(mx, fabsf(__fmul_rn(x[j], g[j])));
+                        }
+                    }
+                    const float2 t2 = exchange(1, make_float2(ss2, mx));
+                    const float inv2 = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t2.x, (float)D), p.eps)));
+                    // the quantiser of src/int8.c:178-209 on z = x inv2 g2: amax = max |z| (taken as
+                    // inv2 max |x g2|), scale = amax / 127, q = rint(z 127 / amax)
+                    const float amax = __fmul_rn(t2.y, inv2);
+                    const float qinv = amax > 0.f ? __fdiv_rn(127.0f, amax) : 1.0f;
+                    if (quant && myblk == 0 && part == 0 && mrow) p.q8_scale[m] = amax > 0.f ? __fmul_rn(amax, 0x1.020408p-7f) : 1.0f;
+                    // pass 3: outputs
+#pragma unroll
+                    for (int c = 0; c < NCH; c++) {
+                        float x[16], g[16], o[16];
+                        xval(c, inv1, x);
+                        cst16(128 + 16 * c, g);
+                        if (quant) {
+                            uint32_t pk[4];
+#pragma unroll
+                            for (int k = 0; k < 4; k++) {
+                                uint32_t wv = 0;
+#pragma unroll
+                                for (int e = 0; e < 4; e++) {
+                                    const float z = __fmul_rn(__fmul_rn(x[4 * k + e], inv2), g[4 * k + e]);
+                                    int qi = __float2int_rn(__fmul_rn(z, qinv));
+                                    qi = qi > 127 ? 127 : (qi < -127 ? -127 : qi);
+                                    wv |= ((uint32_t)qi & 0xffu) << (8 * e);
+                                }
+                                pk[k] = wv;
+                            }
+                            if (mrow)
+                                *reinterpret_cast<uint4 *>(p.q8 + (size_t)m * p.ldq + cw0 + 16 * c) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+#pragma unroll
+                            for (int j = 0; j < 16; j++) o[j] = x[j];
+                        } else {
+#pragma unroll
+                            for (int j = 0; j < 16; j++) o[j] = __fmul_rn(__fmul_rn(x[j], inv2), g[j]);
+                        }
+                        if (tma_out) {
+                            put16(o, cw0 + 16 * c, y0);
+                        } else if (mrow) {
+                            float4 *y4 = reinterpret_cast<float4 *>(p.res + (size_t)m * p.ldres + cw0 + 16 * c);
+#pragma unroll
+                            for (int k = 0; k < 4; k++) y4[k] = make_float4(o[4 * k], o[4 * k + 1], o[4 * k + 2], o[4 * k + 3]);
+                        }
+                    }
+                    ntile++;
+                    if (!xok) {
+                        ok = false;
+                        break;
                     }
                 } else if constexpr (EPI == E2C_EPI_GELU) {
                     // weight rows are interleaved per 128: [gate c0/2 .. +128 | up c0/2 .. +128];
@@ -667,8 +860,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
 
     tc_fence_before();
-    // a pair: neither CTA leaves while the other may still signal its barriers
-    if constexpr (CG == 2) cluster_sync();
+    // a pair (or a NORMADD cluster): no CTA leaves while another may still signal its barriers or
+    // write its shared memory
+    if constexpr (CG == 2 || EPI == E2C_EPI_NORMADD) cluster_sync();
     else __syncthreads();
     if (warp == 1) {
         __syncwarp();
@@ -685,7 +879,7 @@ int launch(const e2c_gemm_args *a, cudaStream_t st) {
     using L = GemmSmem<BN, STAGES, PERBLOCK, EPI, CG>;
     auto kern = k_gemm_i8<BN, STAGES, PERBLOCK, EPI, CG>;
     static bool attr_set = false;
-    static int max_pairs = 0;  // CTA pairs the device holds at once (CG = 2)
+    static int max_clusters[9] = {0};  // clusters of 2..8 CTAs the device holds at once
     if (!attr_set) {
         if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC) != cudaSuccess) {
             e2c_set_msg("gemm: cannot reserve %d bytes of shared memory", L::ALLOC);
@@ -713,15 +907,22 @@ int launch(const e2c_gemm_args *a, cudaStream_t st) {
         if (a->ldy % 4 == 0 && ((uintptr_t)a->y & 15) == 0)
             tma_out = !e2c_tmap_2d_sw64(&t0, a->y, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)width, (uint64_t)a->M,
                                         (uint64_t)a->ldy * 4, 16, 32);
+    } else if (EPI == E2C_EPI_NORMADD) {
+        if (a->ldres % 4 == 0 && ((uintptr_t)a->res & 15) == 0)
+            tma_out = !e2c_tmap_2d_sw64(&t0, a->res, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)(a->n1 - a->n0),
+                                        (uint64_t)a->M, (uint64_t)a->ldres * 4, 16, 32);
     } else if (EPI == E2C_EPI_QKV) {
         if ((((uintptr_t)a->q_out | (uintptr_t)a->k_out) & 15) == 0)
             tma_out = !e2c_tmap_2d_sw64(&t0, a->q_out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)256 * a->nq,
                                         (uint64_t)a->M, (uint64_t)512 * a->nq, 32, 32) &&
                       !e2c_tmap_2d_sw64(&t1, a->k_out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 256, (uint64_t)a->M, 512, 32, 32);
     }
-    const int tiles = ((a->M + BM * CG - 1) / (BM * CG)) * ((a->n1 - a->n0 + BN - 1) / BN);
+    const int tiles_n = (a->n1 - a->n0 + BN - 1) / BN;
+    const int tiles = ((a->M + BM * CG - 1) / (BM * CG)) * tiles_n;
+    // CTA pairs share 256-row tiles; a NORMADD cluster holds the column blocks of whole rows
+    const int csize = CG == 2 ? 2 : (EPI == E2C_EPI_NORMADD ? tiles_n : 1);
     cudaError_t e;
-    if constexpr (CG == 1) {
+    if (csize == 1) {
         const int grid = tiles < g_num_sms ? tiles : g_num_sms;
         kern<<<grid, NTHREADS, L::ALLOC, st>>>(ta, tb, t0, t1, *a, tma_out);
         e = cudaGetLastError();
@@ -730,7 +931,7 @@ int launch(const e2c_gemm_args *a, cudaStream_t st) {
         memset(&cfg, 0, sizeof cfg);
         cudaLaunchAttribute attr[1];
         attr[0].id = cudaLaunchAttributeClusterDimension;
-        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.x = (unsigned)csize;
         attr[0].val.clusterDim.y = 1;
         attr[0].val.clusterDim.z = 1;
         cfg.blockDim = dim3(NTHREADS);
@@ -738,16 +939,19 @@ int launch(const e2c_gemm_args *a, cudaStream_t st) {
         cfg.stream = st;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
-        if (!max_pairs) {
-            cfg.gridDim = dim3(2 * (g_num_sms / 2));
-            if (cudaOccupancyMaxActiveClusters(&max_pairs, kern, &cfg) != cudaSuccess || max_pairs <= 0) {
+        int &maxc = max_clusters[csize];
+        if (!maxc) {
+            cfg.gridDim = dim3((unsigned)(csize * (g_num_sms / csize)));
+            if (cudaOccupancyMaxActiveClusters(&maxc, kern, &cfg) != cudaSuccess || maxc <= 0) {
                 cudaGetLastError();
-                max_pairs = 0;
-                e2c_set_msg("gemm: the device cannot hold a pair of GEMM CTAs");
+                maxc = 0;
+                e2c_set_msg("gemm: the device cannot hold a cluster of %d GEMM CTAs", csize);
                 return -2;
             }
         }
-        cfg.gridDim = dim3(2 * (tiles < max_pairs ? tiles : max_pairs));
+        // units of work = clusters' worth of tiles (a pair's 256-row tile, a NORMADD row block)
+        const int units = CG == 2 ? tiles : tiles / csize;
+        cfg.gridDim = dim3((unsigned)(csize * (units < maxc ? units : maxc)));
         e = cudaLaunchKernelEx(&cfg, kern, ta, tb, t0, t1, *a, tma_out);
     }
     if (e != cudaSuccess) {
@@ -876,8 +1080,21 @@ extern "C" int e2c_gemm(const e2c_gemm_args *a, void *stream) {
             return -1;
         }
         return pair ? launch<256, 4, false, E2C_EPI_QKV, 2>(a, st) : launch<256, 3, false, E2C_EPI_QKV, 1>(a, st);
+    case E2C_EPI_NORMADD: {
+        const int ncols = a->n1 - a->n0;
+        if (perblock || a->n0 != 0 || ncols % 192 || ncols / 192 > 4 || !a->res || !a->norm_g1 ||
+            (!a->norm_g2 && !a->norm_gf) || (a->norm_g2 && (!a->q8 || !a->q8_scale || a->ldq % 16)) || a->ldres % 4) {
+            e2c_set_msg("gemm: the norm epilogue needs per-row scales, whole rows of 192 x (1..4) columns, res, the "
+                        "norm gains and (with a second gain) 16-byte aligned int8 rows and their scales");
+            return -1;
+        }
+        return launch<192, 3, false, E2C_EPI_NORMADD, 1>(a, st);
+    }
     default:
         e2c_set_msg("gemm: unknown epilogue %d", a->epi);
         return -1;
     }
 }
+
+// sizeof(e2c_gemm_args), for the bindings' layout check
+extern "C" int e2c_gemm_args_size(void) { return (int)sizeof(e2c_gemm_args); }

@@ -35,7 +35,10 @@ enum {
     E2C_EPI_RESID = 1, /* y = dequant (clamped) + resid                                    */
     E2C_EPI_I32 = 2,   /* dots[m][n][b] = raw int32 block dots (debug; bit-exact check)      */
     E2C_EPI_GELU = 3,  /* weight rows interleaved per 128: h = gelu(g) * u, fp32 [M][N/2]  */
-    E2C_EPI_QKV = 4    /* per-head RMSNorm (+gamma) + RoPE -> bf16 Q, K, V^T               */
+    E2C_EPI_QKV = 4,   /* per-head RMSNorm (+gamma) + RoPE -> bf16 Q, K, V^T               */
+    E2C_EPI_NORMADD = 5 /* y = gemm (never stored); x = rmsnorm(y) * g1 + res; res = x;
+                          q = quantise(rmsnorm(x) * g2) per token (g2 NULL: res = rmsnorm(x) * gf).
+                          Whole rows per cluster of CTAs (N = 768: 4 x 192 columns) */
 };
 
 typedef struct {
@@ -64,6 +67,15 @@ typedef struct {
     const float *q_gamma, *k_gamma; /* [256] */
     const float *rope_cos, *rope_sin; /* [seq_len][128] */
     float eps;
+    /* NORMADD epilogue: the residual stream res [M][ldres] (read and written), the two norm gains,
+     * the final norm's gain (used when norm_g2 is NULL), the quantised rows q8 [M][ldq] and their
+     * per-token scales q8_scale [M] */
+    float *res;
+    int ldres;
+    const float *norm_g1, *norm_g2, *norm_gf;
+    int8_t *q8;
+    int ldq;
+    float *q8_scale;
     int *status;
 } e2c_gemm_args;
 

@@ -194,6 +194,56 @@ E2C_DEV void cluster_sync() {
 E2C_DEV void mbar_arrive_cluster(uint32_t bar_cluster) {
     asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
 }
+// the same with release semantics at cluster scope: the arriving thread's earlier writes (to this
+// CTA's or another's shared memory) are visible to a thread that then waits with acquire.cluster
+E2C_DEV void mbar_arrive_cluster_release(uint32_t bar_cluster) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
+}
+E2C_DEV bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// bounded wait with acquire at cluster scope (pairs with mbar_arrive_cluster_release)
+E2C_DEV bool mbar_wait_cluster(uint32_t bar, uint32_t parity, int *status, int code) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    const uint64_t t0 = globaltimer();
+    for (uint32_t it = 0;; ++it) {
+        if (mbar_try_wait_cluster(bar, parity)) return true;
+        if ((it & 63) == 63) {
+            if (globaltimer() - t0 > E2C_WAIT_NS) {
+                record_status(status, code);
+                return false;
+            }
+            if (status && *(volatile int *)status != 0) return false;
+        }
+    }
+}
+// Asynchronous stores into another CTA's shared memory whose bytes complete on an mbarrier of that
+// CTA (like a TMA load's): the receiver expects the bytes with mbar_arrive_expect_tx and waits on
+// the barrier; no release fence on the sender's side.
+E2C_DEV void st_async_f32(uint32_t cluster_addr, float v, uint32_t cluster_bar) {
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.f32 [%0], %1, [%2];" ::"r"(cluster_addr), "f"(v),
+                 "r"(cluster_bar)
+                 : "memory");
+}
+E2C_DEV void st_async_f32x2(uint32_t cluster_addr, float a, float b, uint32_t cluster_bar) {
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.f32 [%0], {%1, %2}, [%3];" ::"r"(cluster_addr),
+                 "f"(a), "f"(b), "r"(cluster_bar)
+                 : "memory");
+}
+E2C_DEV void st_dsmem_f32(uint32_t cluster_addr, float v) {
+    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(cluster_addr), "f"(v) : "memory");
+}
+E2C_DEV void st_dsmem_f32x2(uint32_t cluster_addr, float a, float b) {
+    asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" ::"r"(cluster_addr), "f"(a), "f"(b) : "memory");
+}
 // 2D tiled TMA load into this CTA's shared memory whose completed bytes are counted on the
 // mbarrier `bar_cluster` (a shared::cluster address: the leader's barrier). No multicast.
 E2C_DEV void tma_load_2d_pair(uint32_t dst, const CUtensorMap *m, int x, int y, uint32_t bar_cluster) {

@@ -47,3 +47,10 @@ def test_error_reporting_without_device(e2c):
     # argument validation happens before any device work: a bad call fails with a message
     assert lib.e2cuda_ffn_create(None, None, None, None, 1e-6, 16) is None
     assert "ffn_create" in e2c.last_error()
+
+
+def test_gemm_args_layout_matches_the_library(e2c):
+    """The launcher's argument struct (csrc/launch.h) and its ctypes mirror have the same size."""
+    lib = C.CDLL(str(e2c.LIB_PATH))
+    lib.e2c_gemm_args_size.restype = C.c_int
+    assert lib.e2c_gemm_args_size() == C.sizeof(e2c.GemmArgs)

@@ -203,23 +203,8 @@ def test_gemm_clamp_from_q8w(e2c, of, syn, torch_cuda):
 
 
 # ------------------------------------------------------------------------------------------ fused epilogues
-class GemmArgs(C.Structure):
-    """Mirror of e2c_gemm_args (e2.c_b200/csrc/launch.h): the fused epilogues have no public entry
-    point of their own, so their parity tests drive the launcher directly."""
-
-    _fields_ = [("a", C.c_void_p), ("lda", C.c_int), ("a_scale", C.c_void_p), ("w", C.c_void_p), ("ldw", C.c_int),
-                ("wrows", C.c_int), ("w_scale", C.c_void_p), ("M", C.c_int), ("K", C.c_int), ("ablk", C.c_int),
-                ("n0", C.c_int), ("n1", C.c_int), ("epi", C.c_int), ("y", C.c_void_p), ("ldy", C.c_int),
-                ("resid", C.c_void_p), ("ldr", C.c_int), ("dots", C.c_void_p), ("ldd", C.c_int),
-                ("out_min", C.c_float), ("out_max", C.c_float), ("nq", C.c_int), ("q_out", C.c_void_p),
-                ("k_out", C.c_void_p), ("vt_out", C.c_void_p), ("ldvt", C.c_int), ("seq_len", C.c_int),
-                ("q_gamma", C.c_void_p), ("k_gamma", C.c_void_p), ("rope_cos", C.c_void_p),
-                ("rope_sin", C.c_void_p), ("eps", C.c_float), ("status", C.c_void_p)]
-
-
 def _launch(e2c, args, torch):
     lib = e2c.lib()
-    lib.e2c_gemm.argtypes = [C.POINTER(GemmArgs), C.c_void_p]
     lib.e2c_msg.restype = C.c_char_p
     rc = lib.e2c_gemm(C.byref(args), torch.cuda.current_stream().cuda_stream)
     assert rc == 0, lib.e2c_msg().decode()
@@ -227,7 +212,9 @@ def _launch(e2c, args, torch):
 
 
 def _args_for(W, qd, sd, M, K):
-    a = GemmArgs()
+    from conftest import load_e2c
+
+    a = load_e2c().GemmArgs()
     a.a, a.lda, a.a_scale = qd.data_ptr(), W.w8.ld, sd.data_ptr()
     a.w, a.ldw, a.wrows, a.w_scale = C.cast(W.w8.w, C.c_void_p), W.w8.ld, W.w8.rows, C.cast(W.w8.scale, C.c_void_p)
     a.M, a.K, a.ablk, a.n0, a.n1 = M, K, K, 0, W.N
@@ -320,6 +307,50 @@ def test_qkv_epilogue_norm_rope(e2c, of, torch_cuda, B, S):
     tol = np.abs(want) * 2.0 ** -7 + 4e-6
     assert np.all(diff <= tol), f"beyond one bf16 ulp: {int((diff > tol).sum())}, worst {diff.max()}"
     assert (diff == 0).mean() > 0.99
+
+
+@pytest.mark.parametrize("M,final", [(300, False), (16384, False), (1000, True)])
+def test_gemm_norm_add_epilogue(e2c, of, torch_cuda, M, final):
+    """o_proj / down with the residual norm fused (e2.c src/text.c:947,950 + :321-339): the GEMM's fp32
+    output t stays on chip; x = rmsnorm(t) * g1 + res becomes the residual and the next layer's input
+    rmsnorm(x) * g2 is quantised per token (or, after the last layer, rmsnorm(x) * gf is written).
+    Rows span a cluster of four CTAs of 192 columns. Against fp64 of the same formula on the
+    bit-exact t; 16384 rows give every CTA several tiles."""
+    torch = torch_cuda
+    rng = np.random.default_rng(61 + M)
+    N = K = 768
+    qa, a_s, w, ws = _gemm_inputs(rng, M, N, K, K)
+    res0 = rng.standard_normal((M, N)).astype(np.float32)
+    g1 = (1 + 0.1 * rng.standard_normal(N)).astype(np.float32)
+    g2 = (1 + 0.1 * rng.standard_normal(N)).astype(np.float32)
+    eps = 1e-6
+    W = e2c.Weight(w=w, scale=ws)
+    res = dev(torch, res0)
+    q = torch.zeros((M, N), dtype=torch.int8, device="cuda")
+    qs = torch.zeros((M,), dtype=torch.float32, device="cuda")
+    gd1, gd2 = dev(torch, g1), dev(torch, g2)
+    a = _args_for(W, dev(torch, qa), dev(torch, a_s), M, K)
+    a.epi, a.eps = e2c.EPI_NORMADD, eps
+    a.res, a.ldres, a.norm_g1 = res.data_ptr(), N, gd1.data_ptr()
+    if final:
+        a.norm_gf = gd2.data_ptr()
+    else:
+        a.norm_g2, a.q8, a.ldq, a.q8_scale = gd2.data_ptr(), q.data_ptr(), N, qs.data_ptr()
+    _launch(e2c, a, torch)
+    t = of.gemm_plain(qa, a_s, w, ws, K).astype(np.float64)
+    inv1 = 1.0 / np.sqrt((t * t).mean(axis=1, keepdims=True) + eps)
+    x = t * inv1 * g1 + res0
+    inv2 = 1.0 / np.sqrt((x * x).mean(axis=1, keepdims=True) + eps)
+    z = x * inv2 * g2
+    got = res.cpu().numpy()
+    want = z if final else x
+    err = np.abs(got - want).max(axis=1) / np.abs(want).max(axis=1)
+    assert err.max() < 1e-5, f"residual off by {err.max()}"
+    if not final:
+        amax = np.abs(z).max(axis=1, keepdims=True)
+        np.testing.assert_allclose(qs.cpu().numpy(), amax[:, 0] / 127.0, rtol=1e-5)
+        pre = z * (127.0 / amax)
+        tie_tolerant_bytes(q.cpu().numpy(), np.clip(np.rint(pre), -127, 127).astype(np.int8), pre)
 
 
 def test_norm_quant_teacher_forced(e2c, of, torch_cuda):
