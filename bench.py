@@ -402,11 +402,11 @@ def config4(args) -> int:
 # each per layer. Weights are quantised N(0, 0.02), activations per-token quantised N(0, 1).
 KERNELS = ("gate_up", "qkv", "o_proj", "down", "o_proj_norm", "down_norm", "attention", "quantize", "quantize_ctx",
            "norm_add")
-# the kernels an encoder layer runs (hidden 768, per-token scales; the residual norms run as their own
-# row kernel after o_proj and down unless E2C_FUSED_NORM=1 fuses them into those GEMMs)
-LAYER_KERNELS = ("gate_up", "qkv", "o_proj", "down", "attention", "quantize", "quantize_ctx", "norm_add")
-if os.environ.get("E2C_FUSED_NORM") == "1":
-    LAYER_KERNELS = ("gate_up", "qkv", "o_proj_norm", "down_norm", "attention", "quantize", "quantize_ctx")
+# the kernels an encoder layer runs (hidden 768, per-token scales: the residual norms fused into o_proj
+# and down, or with E2C_FUSED_NORM=0 their own row kernel after each)
+LAYER_KERNELS = ("gate_up", "qkv", "o_proj_norm", "down_norm", "attention", "quantize", "quantize_ctx")
+if os.environ.get("E2C_FUSED_NORM") == "0":
+    LAYER_KERNELS = ("gate_up", "qkv", "o_proj", "down", "attention", "quantize", "quantize_ctx", "norm_add")
 
 
 def kernel_work(name: str, M: int) -> dict:

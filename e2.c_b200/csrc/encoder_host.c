@@ -257,11 +257,12 @@ e2cuda_encoder *e2cuda_encoder_create(const e2cuda_encoder_desc *d, int max_toke
             DALLOC(e->ps, sizeof(float) * MB * (size_t)((e->DH > D ? e->DH : D) / 128 + 1)))
             goto fail;
     }
-    /* The GEMM with the residual norms in its epilogue (one launch instead of two) is opt-in by
-     * E2C_FUSED_NORM=1 until it beats the GEMM + row-kernel pair at the encoder's shapes. */
+    /* o_proj / down run with the residual norms in their epilogue (one launch instead of two, the
+     * GEMM output never written) where the shape allows; E2C_FUSED_NORM=0 selects the GEMM + row
+     * kernel pair instead. */
     {
         const char *fz = getenv("E2C_FUSED_NORM");
-        e->fused_norm = fz && fz[0] == '1' && e->ablk == D && D % 192 == 0 && D / 192 <= 4;
+        e->fused_norm = !(fz && fz[0] == '0') && e->ablk == D && D % 192 == 0 && D / 192 <= 4;
     }
     e->status = e2cu_status();
     if (!e->status || e2cu_cuda(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking), "stream")) goto fail;

@@ -107,6 +107,13 @@ E2C_DEV void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;"
 E2C_DEV void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
 // every committed store has completed
 E2C_DEV void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// 4 bytes global -> shared without a register round trip; src_bytes 0 writes a zero and reads
+// nothing. Visible to the issuing thread after cp_async_wait_all().
+E2C_DEV void cp_async_4(uint32_t dst, const void *src, uint32_t src_bytes) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+E2C_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+E2C_DEV void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 E2C_DEV void named_barrier(int id, int nthreads) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory"); }
 
 // generic-proxy shared-memory writes become visible to the async proxy (tcgen05.mma operands)
