@@ -11,7 +11,7 @@
  *   GEMM gate|up -> GELU(g)*u (epilogue) ; quant h
  *   GEMM down + norm_add(post_ffn) + norm_split(next input_ln) + quant   (last layer: final norm)
  *
- * With per-token scales and a hidden size of 192 x (1..4) the residual norms run in the o_proj and
+ * With per-token scales and a hidden size of 128 x (1..8) the residual norms run in the o_proj and
  * down GEMMs' epilogue (whole rows per cluster of CTAs; 7 kernels per layer); otherwise the GEMM
  * writes fp32 and a row kernel applies them (9 kernels per layer).
  *
@@ -262,7 +262,7 @@ e2cuda_encoder *e2cuda_encoder_create(const e2cuda_encoder_desc *d, int max_toke
      * kernel pair instead. */
     {
         const char *fz = getenv("E2C_FUSED_NORM");
-        e->fused_norm = !(fz && fz[0] == '0') && e->ablk == D && D % 192 == 0 && D / 192 <= 4;
+        e->fused_norm = !(fz && fz[0] == '0') && e->ablk == D && D % 128 == 0 && D / 128 <= 8;
     }
     e->status = e2cu_status();
     if (!e->status || e2cu_cuda(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking), "stream")) goto fail;

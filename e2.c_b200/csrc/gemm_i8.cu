@@ -47,29 +47,18 @@ struct GemmSmem {
     static constexpr int B_BYTES = (BN / CG) * BK;  // a CTA pair splits B's rows between its CTAs
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     // staging tiles per epilogue warp: QKV stages the two halves of a head; the other epilogues
-    // without the per-block fold alternate between two, so a store overlaps the next chunk's math;
-    // NORMADD keeps the warp's whole residual block (32 rows x 48 columns = three tiles) on chip
-    static constexpr int STG_BUFS = EPI == E2C_EPI_NORMADD ? 3
-                                    : (EPI == E2C_EPI_QKV || (!PERBLOCK && EPI != E2C_EPI_I32 && CG == 1)) ? 2
-                                                                                                             : 1;
+    // without the per-block fold alternate between two, so a store overlaps the next chunk's math
+    static constexpr int STG_BUFS = (EPI == E2C_EPI_QKV || (!PERBLOCK && EPI != E2C_EPI_I32 && CG == 1)) ? 2 : 1;
     static constexpr int STG_PER_WARP = STG_BUFS * STG_WARP;
     static constexpr int STG_OFF = STAGES * STAGE_BYTES;
-    // per-warp column constants (weight scales, norm gains): 128 floats (NORMADD: 256, with the
-    // rows' activation scales)
-    static constexpr int CST_FLOATS = EPI == E2C_EPI_NORMADD ? 256 : 128;
+    // per-warp column constants (weight scales, norm gains): 128 floats
     static constexpr int CST_OFF = STG_OFF + EPI_WARPS * STG_PER_WARP;
-    static constexpr int CST_BYTES = (PERBLOCK || EPI == E2C_EPI_I32) ? 0 : EPI_WARPS * CST_FLOATS * 4;
+    static constexpr int CST_BYTES = (PERBLOCK || EPI == E2C_EPI_I32) ? 0 : EPI_WARPS * 128 * 4;
     static constexpr int SSQ_OFF = CST_OFF + CST_BYTES;
     static constexpr int SSQ_BYTES = EPI == E2C_EPI_QKV ? 2 * 4 * BM * 4 : 0;  // [acc][part][row]
-    // NORMADD row exchanges: local partials [4 parts][128 rows] (round 0: float, round 1: float2),
-    // then one partial per CTA of the cluster [NCL][128] (float, float2)
-    static constexpr int NCL = 4;
-    static constexpr int NRM_OFF = SSQ_OFF + SSQ_BYTES;
-    static constexpr int NRM_BYTES = EPI == E2C_EPI_NORMADD ? (4 * BM * 12 + NCL * BM * 12) : 0;
-    static constexpr int BAR_OFF = NRM_OFF + NRM_BYTES;
-    // full[S], empty[S], tfull[2], tempty[2], pair[2][4] (QKV row-norm exchange), NORMADD lbar[2][4],
-    // xbar[2][4] and rbar[16] (a warp's residual block landed), tmem slot
-    static constexpr int NBAR = 2 * STAGES + 4 + 8 + (EPI == E2C_EPI_NORMADD ? 16 + EPI_WARPS : 0);
+    static constexpr int BAR_OFF = SSQ_OFF + SSQ_BYTES;
+    // full[S], empty[S], tfull[2], tempty[2], pair[2][4] (QKV row-norm exchange), tmem slot
+    static constexpr int NBAR = 2 * STAGES + 4 + 8;
     static constexpr int BYTES = BAR_OFF + NBAR * 8 + 16;
     static constexpr int ALLOC = BYTES + 1024;  // slack for 1024-byte alignment
     static_assert(ALLOC <= 232448, "shared memory");
@@ -150,9 +139,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     auto tfull_bar = [&](int a) { return bar0 + 8u * (2 * STAGES + a); };
     auto tempty_bar = [&](int a) { return bar0 + 8u * (2 * STAGES + 2 + a); };
     auto pair_bar = [&](int a, int q) { return bar0 + 8u * (2 * STAGES + 4 + 4 * a + q); };
-    auto lbar = [&](int r, int q) { return bar0 + 8u * (2 * STAGES + 12 + 4 * r + q); };
-    auto xbar = [&](int r, int q) { return bar0 + 8u * (2 * STAGES + 20 + 4 * r + q); };
-    auto rbar = [&](int w) { return bar0 + 8u * (2 * STAGES + 28 + w); };
     volatile uint32_t *tmem_slot = reinterpret_cast<volatile uint32_t *>(smem + L::BAR_OFF + L::NBAR * 8);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -180,14 +166,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             mbar_init(tempty_bar(a), EPI_WARPS * CG);  // one arrival per epilogue warp of the pair
             for (int q = 0; q < 4; q++) mbar_init(pair_bar(a, q), 128);
         }
-        if constexpr (EPI == E2C_EPI_NORMADD)
-            for (int r = 0; r < 2; r++)
-                for (int q = 0; q < 4; q++) {
-                    mbar_init(lbar(r, q), 128);             // the 4 warps of a lane quadrant
-                    mbar_init(xbar(r, q), 1);               // this CTA's expect_tx; the bytes come by st.async
-                }
-        if constexpr (EPI == E2C_EPI_NORMADD)
-            for (int w = 0; w < EPI_WARPS; w++) mbar_init(rbar(w), 1);
         fence_mbar_init();
         tma_prefetch_desc(&tmA);
         tma_prefetch_desc(&tmB);
@@ -203,8 +181,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         }
     }
     tc_fence_before();
-    // a pair (or a NORMADD cluster): every CTA's barriers are initialised before another signals them
-    if constexpr (CG == 2 || EPI == E2C_EPI_NORMADD) cluster_sync();
+    // a pair: the leader's barriers are initialised before the other CTA signals them
+    if constexpr (CG == 2) cluster_sync();
     else __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
@@ -371,7 +349,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             if (PERBLOCK || t >= ntiles) return r;
             const int m = (t / tiles_n) * (BM * CG) + (int)rank * BM + row, c0 = p.n0 + (t % tiles_n) * BN;
             if (m < M) r.as = __ldg(p.a_scale + (size_t)m * nb);
-            if constexpr (EPI == E2C_EPI_F32 || EPI == E2C_EPI_RESID || EPI == E2C_EPI_NORMADD) {
+            if constexpr (EPI == E2C_EPI_F32 || EPI == E2C_EPI_RESID) {
                 const int cw = c0 + part * QCOLS;
                 if (lane < QCOLS && cw + lane < p.n1) r.w0 = __ldg(p.w_scale + cw + lane);
                 if (32 + lane < QCOLS && cw + 32 + lane < p.n1) r.w1 = __ldg(p.w_scale + cw + 32 + lane);
@@ -390,7 +368,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             }
             return r;
         };
-        float *cst = reinterpret_cast<float *>(smem + L::CST_OFF) + (warp - 2) * L::CST_FLOATS;
+        float *cst = reinterpret_cast<float *>(smem + L::CST_OFF) + (warp - 2) * 128;
         // 16 consecutive floats of cst from `off` (a broadcast: every lane reads the same address)
         auto cst16 = [&](int off, float (&o)[16]) {
 #pragma unroll
@@ -399,545 +377,287 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 o[4 * k] = w.x, o[4 * k + 1] = w.y, o[4 * k + 2] = w.z, o[4 * k + 3] = w.w;
             }
         };
-        if constexpr (EPI == E2C_EPI_NORMADD) {
-            // GEMM + residual norms. The CTAs of a cluster hold the column blocks of the same 128 rows
-            // (a CTA's block is fixed for the kernel); this warp owns 32 rows x 48 columns, and the
-            // GEMM output t = acc (as ws) never leaves the SM. Per row (768 columns over the cluster):
-            //   inv1 = 1/sqrt(mean t^2 + eps);  x = t inv1 g1 + res;  inv2 = 1/sqrt(mean x^2 + eps);
-            //   res = x and q = quantise(x inv2 g2) per token, or (the final norm) res = x inv2 gf.
-            // fp32 is reassociated to keep the passes short (the results agree with the two-kernel
-            // path to a few ulp): sum t^2 = as^2 sum (acc ws)^2, x = fma(acc, (as inv1)(ws g1), res),
-            // and q = rint((x g2) 127 / max|x g2|).
-            // The warp's residual block comes by TMA into its three 64-byte-swizzled tiles a tile
-            // ahead, x replaces it in place and leaves by TMA store; the accumulator is read twice
-            // (sum of squares, then x) and released after the second pass. The row's activation
-            // scale arrives a tile ahead by cp.async. Row sums and maxima are exchanged in two
-            // rounds: the quadrant's 4 warps combine their columns in shared memory, one warp sends
-            // the CTA's partial to every CTA of the cluster (st.async, counted on the receiver's
-            // barrier), all wait for all of them.
-            constexpr int NCH = QCOLS / 16;
-            const int ncl = tiles_n;  // CTAs of the cluster = column blocks of a row
-            const int D = p.n1 - p.n0;
-            const int myblk = (int)(blockIdx.x % (unsigned)tiles_n);  // = cluster rank
-            const int cl0 = myblk * BN + part * QCOLS;                  // first column of this warp
-            const bool quant = p.norm_g2 != nullptr;
-            const uint32_t rb = rbar(warp - 2);
-            const uint32_t blk = smem_u32(stg);  // the warp's residual block: NCH tiles of 32 x 16 fp32
-            // column constants, the same for every tile: [0, 48) ws, [64, 112) ws g1, [128, 176) g2
-            // (or gf); [192, 256) the rows' activation scales, two tiles
-            {
-                const float *gb = quant ? p.norm_g2 : p.norm_gf;
-                for (int j = lane; j < QCOLS; j += 32) {
-                    const float w = __ldg(p.w_scale + p.n0 + cl0 + j);
-                    cst[j] = w;
-                    cst[64 + j] = __fmul_rn(w, __ldg(p.norm_g1 + cl0 + j));
-                    cst[128 + j] = __ldg(gb + cl0 + j);
-                }
-                __syncwarp();
-            }
-            const uint32_t as_slot = smem_u32(cst + 192 + lane);
-            auto load_as = [&](int t, int nt) {
-                const int mr = (t / tiles_n) * BM + row;
-                cp_async_4(as_slot + (uint32_t)((nt & 1) * 128), p.a_scale + (mr < M ? (size_t)mr * nb : 0), mr < M ? 4u : 0u);
-                cp_async_commit();
-            };
-            // element (lane, 4 k .. 4 k + 3) of tile c: the 64-byte swizzle of the TMA map
-            auto rp = [&](int c, int k) -> float4 * {
-                return reinterpret_cast<float4 *>(stg + c * STG_WARP + lane * 64 + ((k ^ ((lane >> 1) & 3)) << 4));
-            };
-            bool rpend = false;  // a residual load in flight that nobody waited for
-            uint32_t rpar = 0;
-            auto load_res = [&](int t, int nt) {
-                if (lane == 0) {
-                    mbar_arrive_expect_tx(rb, (uint32_t)(NCH * STG_WARP));
-                    const int y0 = (t / tiles_n) * BM + q * 32;
+        Pre pre = fetch(tfirst);
+        for (int t = tfirst; t < ntiles && ok; t += tstride) {
+            const int mt = (t / tiles_n) * (BM * CG) + (int)rank * BM;
+            const int m = mt + row;
+            const int c0 = p.n0 + (t % tiles_n) * BN;
+            const bool mrow = m < M;
+            const int y0 = mt + q * 32;  // first row of this warp's 32
+            const int cw = c0 + part * QCOLS;  // first column of this warp (F32 / I32 / per-block)
+            if constexpr (PERBLOCK) {
+                float f[QCOLS];
 #pragma unroll
-                    for (int c = 0; c < NCH; c++) tma_load_2d(blk + c * STG_WARP, &tmO0, cl0 + 16 * c, y0, rb);
-                }
-                rpend = true;
-                rpar = (uint32_t)(nt & 1);
-            };
-            auto store_res = [&](int y0) {
-                fence_proxy_async_smem();
-                __syncwarp();
-                if (lane == 0) {
+                for (int j = 0; j < QCOLS; j++) f[j] = 0.f;
+                const int nl = cw + lane;
+                const float wsl = (EPI != E2C_EPI_I32 && nl < p.n1) ? __ldg(p.w_scale + nl) : 0.f;
+                for (int u = 0; u < nunits; u++) {
+                    const float as = mrow ? __ldg(p.a_scale + (size_t)m * nb + u) : 0.f;
+                    // warp-uniform outcome: tcgen05.ld below is .sync.aligned
+                    if (!__all_sync(0xffffffffu, mbar_wait(tfull_bar(acc), acc_phase, p.status, E2C_ERR_WAIT_EPI))) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    uint32_t r[32];
+                    tmem_ld32(tmem_base + lane_addr + (uint32_t)(acc * BN + part * QCOLS), r);
+                    tmem_wait_ld();
+                    release_acc(acc);
+                    if constexpr (EPI == E2C_EPI_I32) {
+                        if (mrow)
+                            for (int j = 0; j < 32; j++)
+                                if (cw + j < p.n1) p.dots[((size_t)m * p.ldd + cw + j) * nb + u] = (int32_t)r[j];
+                    } else {
 #pragma unroll
-                    for (int c = 0; c < NCH; c++) tma_store_2d(&tmO0, blk + c * STG_WARP, cl0 + 16 * c, y0);
-                    bulk_commit();
+                        for (int j = 0; j < 32; j++)
+                            f[j] = __fmaf_rn(__int2float_rn((int)r[j]), __fmul_rn(as, __shfl_sync(0xffffffffu, wsl, j)), f[j]);
+                    }
+                    if (++acc == 2) {
+                        acc = 0;
+                        acc_phase ^= 1u;
+                    }
                 }
-            };
-            float *xl0 = reinterpret_cast<float *>(smem + L::NRM_OFF);                 // [4][BM]
-            float2 *xl1 = reinterpret_cast<float2 *>(smem + L::NRM_OFF + 4 * BM * 4);  // [4][BM]
-            const uint32_t xr0 = sbase + L::NRM_OFF + 4 * BM * 12;                    // [NCL][BM] float
-            const uint32_t xr1 = xr0 + L::NCL * BM * 4;                               // [NCL][BM] float2
-            bool xok = true;
-            // round r of tile parity `par`: this warp's partial (sum in .x, max in .y) combined over the
-            // row's columns
-            auto exchange = [&](int r, uint32_t par, float2 v) -> float2 {
-                if (r == 0) xl0[part * BM + row] = v.x;
-                else xl1[part * BM + row] = v;
-                mbar_arrive(lbar(r, q));
-                if (part == 0) {
-                    xok = xok && __all_sync(0xffffffffu, mbar_wait(lbar(r, q), par, p.status, E2C_ERR_WAIT_EPI));
-                    float2 c = make_float2(0.f, 0.f);
-                    if (xok) {
+                if (!ok) break;
+                if constexpr (EPI != E2C_EPI_I32) {
 #pragma unroll
-                        for (int w = 0; w < 4; w++) {
-                            if (r == 0) {
-                                c.x = __fadd_rn(c.x, xl0[w * BM + row]);
-                            } else {
-                                const float2 o = xl1[w * BM + row];
-                                c.x = __fadd_rn(c.x, o.x);
-                                c.y = fmaxf(c.y, o.y);
-                            }
+                    for (int h2 = 0; h2 < 2; h2++) {
+                        float v[16];
+#pragma unroll
+                        for (int j = 0; j < 16; j++) {
+                            const int n = cw + 16 * h2 + j;
+                            v[j] = fminf(fmaxf(f[16 * h2 + j], p.out_min), p.out_max);
+                            if constexpr (EPI == E2C_EPI_RESID)
+                                if (mrow && n < p.n1) v[j] = __fadd_rn(v[j], p.resid[(size_t)m * p.ldr + n]);
+                        }
+                        if (tma_out) {
+                            put16(v, cw + 16 * h2 - p.n0, y0);
+                        } else if (mrow) {
+                            for (int j = 0; j < 16; j++)
+                                if (cw + 16 * h2 + j < p.n1) p.y[(size_t)m * p.ldy + cw + 16 * h2 + j] = v[j];
                         }
                     }
-                    // this CTA expects one partial per row of the quadrant from every CTA
-                    if (lane == 0) mbar_arrive_expect_tx(xbar(r, q), (uint32_t)(ncl * 32 * (r == 0 ? 4 : 8)));
-                    for (int d = 0; d < ncl; d++) {
-                        const uint32_t slot = (r == 0 ? xr0 + (uint32_t)((myblk * BM + row) * 4)
-                                                      : xr1 + (uint32_t)((myblk * BM + row) * 8));
-                        const uint32_t rbd = mapa_shared(xbar(r, q), (uint32_t)d);
-                        if (r == 0) st_async_f32(mapa_shared(slot, (uint32_t)d), c.x, rbd);
-                        else st_async_f32x2(mapa_shared(slot, (uint32_t)d), c.x, c.y, rbd);
-                    }
                 }
-                xok = xok && __all_sync(0xffffffffu, mbar_wait(xbar(r, q), par, p.status, E2C_ERR_WAIT_EPI));
-                float2 tot = make_float2(0.f, 0.f);
-                for (int d = 0; d < ncl; d++) {
-                    if (r == 0) {
-                        tot.x = __fadd_rn(tot.x, *reinterpret_cast<const float *>(smem + (xr0 - sbase) + (d * BM + row) * 4));
-                    } else {
-                        const float2 o = *reinterpret_cast<const float2 *>(smem + (xr1 - sbase) + (d * BM + row) * 8);
-                        tot.x = __fadd_rn(tot.x, o.x);
-                        tot.y = fmaxf(tot.y, o.y);
-                    }
+            } else {
+                const Pre cur = pre;
+                pre = fetch(t + tstride);
+                const float as = cur.as;
+                __syncwarp();  // every lane is done reading the previous tile's cst
+                if constexpr (EPI == E2C_EPI_F32 || EPI == E2C_EPI_RESID) {
+                    if (lane < QCOLS) cst[lane] = cur.w0;
+                    if (32 + lane < QCOLS) cst[32 + lane] = cur.w1;
+                } else if constexpr (EPI == E2C_EPI_GELU) {
+                    cst[lane] = cur.w0;
+                    cst[32 + lane] = cur.w1;
+                } else if constexpr (EPI == E2C_EPI_QKV) {
+                    cst[lane] = cur.w0;
+                    cst[32 + lane] = cur.w1;
+                    cst[64 + lane] = __fmul_rn(cur.w0, cur.g0);
+                    cst[96 + lane] = __fmul_rn(cur.w1, cur.g1);
                 }
-                return tot;
-            };
-            if (tfirst < ntiles) {
-                load_res(tfirst, 0);
-                load_as(tfirst, 0);
-            }
-            int nt = 0;  // tiles this warp finished
-            for (int t = tfirst; t < ntiles && ok; t += tstride, nt++) {
-                const int mt = (t / tiles_n) * BM;
-                const int y0 = mt + q * 32;
-                const uint32_t par = (uint32_t)(nt & 1);
-                // this tile's activation scale (landed a tile ago); the next one's starts
-                cp_async_wait_all();
-                const float as = cst[192 + (nt & 1) * 32 + lane];
-                if (t + tstride < ntiles) load_as(t + tstride, nt + 1);
-                // pass 1: sum over the warp's columns of (acc ws)^2
+                __syncwarp();
                 if (!__all_sync(0xffffffffu, mbar_wait(tfull_bar(acc), acc_phase, p.status, E2C_ERR_WAIT_EPI))) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
-                const uint32_t tb = tmem_base + lane_addr + (uint32_t)(acc * BN + part * QCOLS);
-                float ss = 0.f;
-#pragma unroll
-                for (int c = 0; c < NCH; c++) {
-                    uint32_t r[16];
-                    tmem_ld16(tb + 16 * c, r);
-                    tmem_wait_ld();
-#pragma unroll
-                    for (int k = 0; k < 4; k++) {
-                        const float4 w4 = *reinterpret_cast<const float4 *>(cst + 16 * c + 4 * k);
-                        const float u0 = __fmul_rn(__int2float_rn((int)r[4 * k]), w4.x);
-                        const float u1 = __fmul_rn(__int2float_rn((int)r[4 * k + 1]), w4.y);
-                        const float u2 = __fmul_rn(__int2float_rn((int)r[4 * k + 2]), w4.z);
-                        const float u3 = __fmul_rn(__int2float_rn((int)r[4 * k + 3]), w4.w);
-                        ss = __fmaf_rn(u3, u3, __fmaf_rn(u2, u2, __fmaf_rn(u1, u1, __fmaf_rn(u0, u0, ss))));
+                const uint32_t tbase = tmem_base + lane_addr + (uint32_t)(acc * BN);
+                if constexpr (EPI == E2C_EPI_I32) {
+#pragma unroll 1
+                    for (int c = 0; c < QCOLS / 16; c++) {
+                        uint32_t r[16];
+                        tmem_ld16(tbase + part * QCOLS + 16 * c, r);
+                        tmem_wait_ld();
+                        const int nbase = cw + 16 * c;
+                        if (mrow)
+                            for (int j = 0; j < 16; j++)
+                                if (nbase + j < p.n1) p.dots[(size_t)m * p.ldd + nbase + j] = (int32_t)r[j];
                     }
-                }
-                const float s1 = exchange(0, par, make_float2(__fmul_rn(__fmul_rn(as, as), ss), 0.f)).x;
-                if (!xok) {
-                    ok = false;
-                    break;
-                }
-                const float inv1 = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(s1, (float)D), p.eps)));
-                const float sr = __fmul_rn(as, inv1);
-                // pass 2: x = fma(acc, sr (ws g1), res) in place of res; sum of x^2 and max |x g2|
-                if (!__all_sync(0xffffffffu, mbar_wait(rb, rpar, p.status, E2C_ERR_WAIT_EPI))) {
-                    ok = false;
-                    break;
-                }
-                rpend = false;
-                float ss2 = 0.f, mx = 0.f;
+                } else if constexpr (EPI == E2C_EPI_F32 || EPI == E2C_EPI_RESID) {
+                    // y = float(acc) * (as * ws), the reference's single-block fold; the clamp only
+                    // when the weight carries one (the defaults +-1e31 bound no finite output)
+                    constexpr int NCH = QCOLS / 16;
+                    const bool clamp = p.out_min > -1e30f || p.out_max < 1e30f;
 #pragma unroll
-                for (int c = 0; c < NCH; c++) {
-                    uint32_t r[16];
-                    tmem_ld16(tb + 16 * c, r);
-                    tmem_wait_ld();
+                    for (int c2 = 0; c2 < NCH; c2 += 2) {
+                        uint32_t r[2][16];
+                        tmem_ld16(tbase + part * QCOLS + 16 * c2, r[0]);
+                        if (c2 + 1 < NCH) tmem_ld16(tbase + part * QCOLS + 16 * (c2 + 1), r[1]);
+                        tmem_wait_ld();
 #pragma unroll
-                    for (int k = 0; k < 4; k++) {
-                        float4 *p4 = rp(c, k);
-                        const float4 r4 = *p4;
-                        const float4 c4 = *reinterpret_cast<const float4 *>(cst + 64 + 16 * c + 4 * k);
-                        const float4 x4 = make_float4(__fmaf_rn(__int2float_rn((int)r[4 * k]), __fmul_rn(sr, c4.x), r4.x),
-                                                      __fmaf_rn(__int2float_rn((int)r[4 * k + 1]), __fmul_rn(sr, c4.y), r4.y),
-                                                      __fmaf_rn(__int2float_rn((int)r[4 * k + 2]), __fmul_rn(sr, c4.z), r4.z),
-                                                      __fmaf_rn(__int2float_rn((int)r[4 * k + 3]), __fmul_rn(sr, c4.w), r4.w));
-                        *p4 = x4;
-                        ss2 = __fmaf_rn(x4.w, x4.w, __fmaf_rn(x4.z, x4.z, __fmaf_rn(x4.y, x4.y, __fmaf_rn(x4.x, x4.x, ss2))));
-                        if (quant) {
-                            const float4 g4 = *reinterpret_cast<const float4 *>(cst + 128 + 16 * c + 4 * k);
-                            mx = fmaxf(fmaxf(fmaxf(fmaxf(mx, fabsf(__fmul_rn(x4.x, g4.x))), fabsf(__fmul_rn(x4.y, g4.y))),
-                                             fabsf(__fmul_rn(x4.z, g4.z))),
-                                       fabsf(__fmul_rn(x4.w, g4.w)));
+                        for (int h = 0; h < 2; h++) {
+                            if (c2 + h < NCH) {
+                                const int nbase = cw + 16 * (c2 + h);
+                                float w[16], v[16];
+                                cst16(16 * (c2 + h), w);
+#pragma unroll
+                                for (int j = 0; j < 16; j++) v[j] = dq(r[h][j], __fmul_rn(as, w[j]));
+                                if (clamp)
+#pragma unroll
+                                    for (int j = 0; j < 16; j++) v[j] = fminf(fmaxf(v[j], p.out_min), p.out_max);
+                                if constexpr (EPI == E2C_EPI_RESID) {
+                                    if (mrow) {
+                                        const float *rr = p.resid + (size_t)m * p.ldr + nbase;
+                                        for (int j = 0; j < 16; j++)
+                                            if (nbase + j < p.n1) v[j] = __fadd_rn(v[j], rr[j]);
+                                    }
+                                }
+                                if (tma_out) {
+                                    put16(v, nbase - p.n0, y0);
+                                } else if (mrow && nbase < p.n1) {
+                                    float *yr = p.y + (size_t)m * p.ldy + nbase;
+                                    for (int j = 0; j < 16; j++)
+                                        if (nbase + j < p.n1) yr[j] = v[j];
+                                }
+                            }
                         }
+                    }
+                } else if constexpr (EPI == E2C_EPI_GELU) {
+                    // weight rows are interleaved per 128: [gate c0/2 .. +128 | up c0/2 .. +128];
+                    // this warp produces outputs [32 part, 32 part + 32) of the tile's 128, 16 at a time
+                    const int h0 = (c0 - p.n0) / 2;
+#pragma unroll
+                    for (int h2 = 0; h2 < 2; h2++) {
+                        const int oc = 32 * part + 16 * h2;
+                        uint32_t rg[16], ru[16];
+                        tmem_ld16(tbase + oc, rg);
+                        tmem_ld16(tbase + 128 + oc, ru);
+                        tmem_wait_ld();
+                        float wg[16], wu[16], h[16];
+                        cst16(16 * h2, wg);
+                        cst16(32 + 16 * h2, wu);
+#pragma unroll
+                        for (int j = 0; j < 16; j++) {
+                            const float g = dq(rg[j], __fmul_rn(as, wg[j]));
+                            const float u = dq(ru[j], __fmul_rn(as, wu[j]));
+                            h[j] = __fmul_rn(gelu_tanh(g), u);
+                        }
+                        if (tma_out) {
+                            put16(h, h0 + oc, y0);
+                        } else if (mrow) {
+                            float4 *y4 = reinterpret_cast<float4 *>(p.y + (size_t)m * p.ldy + h0 + oc);
+#pragma unroll
+                            for (int j = 0; j < 4; j++) y4[j] = make_float4(h[4 * j], h[4 * j + 1], h[4 * j + 2], h[4 * j + 3]);
+                        }
+                    }
+                } else if constexpr (EPI == E2C_EPI_QKV) {
+                    // one 256-column tile = one head (q heads, then k, then v). This warp owns
+                    // rotate-half pairs i in [32 part, 32 part + 32) with their partners i + 128.
+                    // x = float(acc) * as * ws;  y = x * inv * gamma with inv = 1/sqrt(mean(x^2) + eps)
+                    // (v: no gamma), computed as float(acc) * (ws * gamma) * (as * inv); then RoPE.
+                    const int head = (c0 - p.n0) / 256;
+                    const bool is_k = head == p.nq, is_v = head == p.nq + 1;
+                    const int pos = mrow ? m % p.seq_len : 0;
+                    // pass 1: sum over this warp's 64 columns of (float(acc) * ws)^2
+                    float ss = 0.f;
+#pragma unroll
+                    for (int h2 = 0; h2 < 2; h2++) {
+                        uint32_t ra[16], rb[16];
+                        tmem_ld16(tbase + 32 * part + 16 * h2, ra);
+                        tmem_ld16(tbase + 128 + 32 * part + 16 * h2, rb);
+                        tmem_wait_ld();
+                        float wa[16], wb[16];
+                        cst16(16 * h2, wa);
+                        cst16(32 + 16 * h2, wb);
+#pragma unroll
+                        for (int j = 0; j < 16; j++) {
+                            const float a = __fmul_rn(__int2float_rn((int)ra[j]), wa[j]);
+                            const float b = __fmul_rn(__int2float_rn((int)rb[j]), wb[j]);
+                            ss = __fmaf_rn(b, b, __fmaf_rn(a, a, ss));
+                        }
+                    }
+                    // RoPE coefficients of the first 16 pairs load while the row norms are exchanged
+                    float csv[16], snv[16];
+                    auto rope_load = [&](int ia) {
+                        const float4 *cs4 = reinterpret_cast<const float4 *>(p.rope_cos + (size_t)pos * 128 + ia);
+                        const float4 *sn4 = reinterpret_cast<const float4 *>(p.rope_sin + (size_t)pos * 128 + ia);
+#pragma unroll
+                        for (int j = 0; j < 4; j++) {
+                            const float4 c4 = __ldg(cs4 + j), s4 = __ldg(sn4 + j);
+                            csv[4 * j] = c4.x, csv[4 * j + 1] = c4.y, csv[4 * j + 2] = c4.z, csv[4 * j + 3] = c4.w;
+                            snv[4 * j] = s4.x, snv[4 * j + 1] = s4.y, snv[4 * j + 2] = s4.z, snv[4 * j + 3] = s4.w;
+                        }
+                    };
+                    if (!is_v) rope_load(32 * part);
+                    // the row's sum of squares over the four warps of this quadrant (same rows)
+                    float *ssq = reinterpret_cast<float *>(smem + L::SSQ_OFF) + acc * 4 * BM;
+                    ssq[part * BM + row] = ss;
+                    mbar_arrive(pair_bar(acc, q));  // release: the partial is visible to the others
+                    if (!__all_sync(0xffffffffu, mbar_wait(pair_bar(acc, q), acc_phase, p.status, E2C_ERR_WAIT_EPI))) {
+                        ok = false;
+                        break;
+                    }
+                    const float sst = __fadd_rn(__fadd_rn(ssq[row], ssq[BM + row]), __fadd_rn(ssq[2 * BM + row], ssq[3 * BM + row]));
+                    const float ms = __fmul_rn(__fmul_rn(as, as), __fdiv_rn(sst, 256.0f));
+                    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, p.eps)));
+                    const float rs = __fmul_rn(as, inv);
+                    if (!is_v && tma_out && nst > 0) {
+                        // the previous tile's stores have read both staging halves
+                        if (lane == 0) bulk_wait_read0();
+                        __syncwarp();
+                    }
+#pragma unroll
+                    for (int h2 = 0; h2 < 2; h2++) {
+                        const int ia = 32 * part + 16 * h2;  // rotate-half index of these 16 pairs
+                        uint32_t ra[16], rb[16];
+                        tmem_ld16(tbase + ia, ra);
+                        tmem_ld16(tbase + 128 + ia, rb);
+                        if (h2 == 1 && !is_v) rope_load(ia);
+                        tmem_wait_ld();
+                        float ca[16], cb[16], va[16], vb[16];
+                        cst16(64 + 16 * h2, ca);
+                        cst16(96 + 16 * h2, cb);
+#pragma unroll
+                        for (int j = 0; j < 16; j++) {
+                            const float a = __fmul_rn(__fmul_rn(__int2float_rn((int)ra[j]), ca[j]), rs);
+                            const float b = __fmul_rn(__fmul_rn(__int2float_rn((int)rb[j]), cb[j]), rs);
+                            if (!is_v) {
+                                va[j] = __fmaf_rn(a, csv[j], -__fmul_rn(b, snv[j]));
+                                vb[j] = __fmaf_rn(a, snv[j], __fmul_rn(b, csv[j]));
+                            } else {
+                                va[j] = a;
+                                vb[j] = b;
+                            }
+                        }
+                        if (is_v) {
+                            if (mrow) {
+                                __nv_bfloat16 *vt = reinterpret_cast<__nv_bfloat16 *>(p.vt_out) +
+                                                    (size_t)(m / p.seq_len) * 256 * p.ldvt + pos;
+#pragma unroll
+                                for (int j = 0; j < 16; j++) {
+                                    vt[(size_t)(ia + j) * p.ldvt] = __float2bfloat16_rn(va[j]);
+                                    vt[(size_t)(128 + ia + j) * p.ldvt] = __float2bfloat16_rn(vb[j]);
+                                }
+                            }
+                        } else if (tma_out) {
+                            stage_bf16x16(stg, lane, 2 * h2, va);
+                            stage_bf16x16(stg + STG_WARP, lane, 2 * h2, vb);
+                        } else if (mrow) {
+                            __nv_bfloat16 *dst = is_k ? reinterpret_cast<__nv_bfloat16 *>(p.k_out) + (size_t)m * 256
+                                                      : reinterpret_cast<__nv_bfloat16 *>(p.q_out) +
+                                                            (size_t)m * (256 * p.nq) + head * 256;
+                            for (int j = 0; j < 16; j++) {
+                                dst[ia + j] = __float2bfloat16_rn(va[j]);
+                                dst[128 + ia + j] = __float2bfloat16_rn(vb[j]);
+                            }
+                        }
+                    }
+                    if (!is_v && tma_out) {
+                        const CUtensorMap *tm = is_k ? &tmO1 : &tmO0;
+                        const int xb = is_k ? 0 : head * 256;
+                        fence_proxy_async_smem();
+                        __syncwarp();
+                        if (lane == 0) {
+                            tma_store_2d(tm, smem_u32(stg), xb + 32 * part, y0);
+                            tma_store_2d(tm, smem_u32(stg + STG_WARP), xb + 128 + 32 * part, y0);
+                            bulk_commit();
+                        }
+                        ++nst;
                     }
                 }
                 release_acc(acc);
                 if (++acc == 2) {
                     acc = 0;
                     acc_phase ^= 1u;
-                }
-                if (quant) store_res(y0);  // the new residual is x: out while the sums travel
-                const float2 t2 = exchange(1, par, make_float2(ss2, mx));
-                if (!xok) {
-                    ok = false;
-                    break;
-                }
-                const float inv2 = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t2.x, (float)D), p.eps)));
-                // pass 3
-                if (quant) {
-                    // the quantiser of src/int8.c:178-209 on z = x inv2 g2: amax = max |z| = inv2 max|x g2|,
-                    // scale = amax / 127, q = rint(z 127 / amax) = rint((x g2) 127 / max|x g2|). |x g2| <= max,
-                    // so |q| <= 127 needs no clamp; rint is the round-to-nearest-even of adding 1.5 2^23,
-                    // whose low byte is q.
-                    const float amax = __fmul_rn(t2.y, inv2);
-                    const float s = t2.y > 0.f ? __fdiv_rn(127.0f, t2.y) : 0.f;
-                    const int m = mt + row;
-                    const bool mrow = m < M;
-                    if (myblk == 0 && part == 0 && mrow) p.q8_scale[m] = amax > 0.f ? __fmul_rn(amax, 0x1.020408p-7f) : 1.0f;
-#pragma unroll
-                    for (int c = 0; c < NCH; c++) {
-                        uint32_t pk[4];
-#pragma unroll
-                        for (int k = 0; k < 4; k++) {
-                            const float4 x4 = *rp(c, k);
-                            const float4 g4 = *reinterpret_cast<const float4 *>(cst + 128 + 16 * c + 4 * k);
-                            const uint32_t b0 = __float_as_uint(__fmaf_rn(__fmul_rn(x4.x, g4.x), s, 12582912.0f));
-                            const uint32_t b1 = __float_as_uint(__fmaf_rn(__fmul_rn(x4.y, g4.y), s, 12582912.0f));
-                            const uint32_t b2 = __float_as_uint(__fmaf_rn(__fmul_rn(x4.z, g4.z), s, 12582912.0f));
-                            const uint32_t b3 = __float_as_uint(__fmaf_rn(__fmul_rn(x4.w, g4.w), s, 12582912.0f));
-                            pk[k] = __byte_perm(__byte_perm(b0, b1, 0x0040), __byte_perm(b2, b3, 0x0040), 0x5410);
-                        }
-                        if (mrow)
-                            *reinterpret_cast<uint4 *>(p.q8 + (size_t)m * p.ldq + cl0 + 16 * c) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-                    }
-                } else {
-#pragma unroll
-                    for (int c = 0; c < NCH; c++) {
-#pragma unroll
-                        for (int k = 0; k < 4; k++) {
-                            float4 *p4 = rp(c, k);
-                            const float4 x4 = *p4;
-                            const float4 g4 = *reinterpret_cast<const float4 *>(cst + 128 + 16 * c + 4 * k);
-                            *p4 = make_float4(__fmul_rn(__fmul_rn(x4.x, inv2), g4.x), __fmul_rn(__fmul_rn(x4.y, inv2), g4.y),
-                                              __fmul_rn(__fmul_rn(x4.z, inv2), g4.z), __fmul_rn(__fmul_rn(x4.w, inv2), g4.w));
-                        }
-                    }
-                    store_res(y0);
-                }
-                // the block's tiles take the next tile's residual once the store has read them
-                if (t + tstride < ntiles) {
-                    if (lane == 0) bulk_wait_read0();
-                    __syncwarp();
-                    load_res(t + tstride, nt + 1);
-                }
-            }
-            // copies into this warp's shared memory land before the CTA's shared memory goes away
-            cp_async_wait_all();
-            if (rpend) {
-                if (lane == 0) mbar_wait(rb, rpar, nullptr, E2C_ERR_WAIT_DRAIN);
-                __syncwarp();
-            }
-        } else {
-            Pre pre = fetch(tfirst);
-            for (int t = tfirst; t < ntiles && ok; t += tstride) {
-                const int mt = (t / tiles_n) * (BM * CG) + (int)rank * BM;
-                const int m = mt + row;
-                const int c0 = p.n0 + (t % tiles_n) * BN;
-                const bool mrow = m < M;
-                const int y0 = mt + q * 32;  // first row of this warp's 32
-                const int cw = c0 + part * QCOLS;  // first column of this warp (F32 / I32 / per-block)
-                if constexpr (PERBLOCK) {
-                    float f[QCOLS];
-    #pragma unroll
-                    for (int j = 0; j < QCOLS; j++) f[j] = 0.f;
-                    const int nl = cw + lane;
-                    const float wsl = (EPI != E2C_EPI_I32 && nl < p.n1) ? __ldg(p.w_scale + nl) : 0.f;
-                    for (int u = 0; u < nunits; u++) {
-                        const float as = mrow ? __ldg(p.a_scale + (size_t)m * nb + u) : 0.f;
-                        // warp-uniform outcome: tcgen05.ld below is .sync.aligned
-                        if (!__all_sync(0xffffffffu, mbar_wait(tfull_bar(acc), acc_phase, p.status, E2C_ERR_WAIT_EPI))) {
-                            ok = false;
-                            break;
-                        }
-                        tc_fence_after();
-                        uint32_t r[32];
-                        tmem_ld32(tmem_base + lane_addr + (uint32_t)(acc * BN + part * QCOLS), r);
-                        tmem_wait_ld();
-                        release_acc(acc);
-                        if constexpr (EPI == E2C_EPI_I32) {
-                            if (mrow)
-                                for (int j = 0; j < 32; j++)
-                                    if (cw + j < p.n1) p.dots[((size_t)m * p.ldd + cw + j) * nb + u] = (int32_t)r[j];
-                        } else {
-    #pragma unroll
-                            for (int j = 0; j < 32; j++)
-                                f[j] = __fmaf_rn(__int2float_rn((int)r[j]), __fmul_rn(as, __shfl_sync(0xffffffffu, wsl, j)), f[j]);
-                        }
-                        if (++acc == 2) {
-                            acc = 0;
-                            acc_phase ^= 1u;
-                        }
-                    }
-                    if (!ok) break;
-                    if constexpr (EPI != E2C_EPI_I32) {
-    #pragma unroll
-                        for (int h2 = 0; h2 < 2; h2++) {
-                            float v[16];
-    #pragma unroll
-                            for (int j = 0; j < 16; j++) {
-                                const int n = cw + 16 * h2 + j;
-                                v[j] = fminf(fmaxf(f[16 * h2 + j], p.out_min), p.out_max);
-                                if constexpr (EPI == E2C_EPI_RESID)
-                                    if (mrow && n < p.n1) v[j] = __fadd_rn(v[j], p.resid[(size_t)m * p.ldr + n]);
-                            }
-                            if (tma_out) {
-                                put16(v, cw + 16 * h2 - p.n0, y0);
-                            } else if (mrow) {
-                                for (int j = 0; j < 16; j++)
-                                    if (cw + 16 * h2 + j < p.n1) p.y[(size_t)m * p.ldy + cw + 16 * h2 + j] = v[j];
-                            }
-                        }
-                    }
-                } else {
-                    const Pre cur = pre;
-                    pre = fetch(t + tstride);
-                    const float as = cur.as;
-                    __syncwarp();  // every lane is done reading the previous tile's cst
-                    if constexpr (EPI == E2C_EPI_F32 || EPI == E2C_EPI_RESID) {
-                        if (lane < QCOLS) cst[lane] = cur.w0;
-                        if (32 + lane < QCOLS) cst[32 + lane] = cur.w1;
-                    } else if constexpr (EPI == E2C_EPI_GELU) {
-                        cst[lane] = cur.w0;
-                        cst[32 + lane] = cur.w1;
-                    } else if constexpr (EPI == E2C_EPI_QKV) {
-                        cst[lane] = cur.w0;
-                        cst[32 + lane] = cur.w1;
-                        cst[64 + lane] = __fmul_rn(cur.w0, cur.g0);
-                        cst[96 + lane] = __fmul_rn(cur.w1, cur.g1);
-                    }
-                    __syncwarp();
-                    if (!__all_sync(0xffffffffu, mbar_wait(tfull_bar(acc), acc_phase, p.status, E2C_ERR_WAIT_EPI))) {
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after();
-                    const uint32_t tbase = tmem_base + lane_addr + (uint32_t)(acc * BN);
-                    if constexpr (EPI == E2C_EPI_I32) {
-    #pragma unroll 1
-                        for (int c = 0; c < QCOLS / 16; c++) {
-                            uint32_t r[16];
-                            tmem_ld16(tbase + part * QCOLS + 16 * c, r);
-                            tmem_wait_ld();
-                            const int nbase = cw + 16 * c;
-                            if (mrow)
-                                for (int j = 0; j < 16; j++)
-                                    if (nbase + j < p.n1) p.dots[(size_t)m * p.ldd + nbase + j] = (int32_t)r[j];
-                        }
-                    } else if constexpr (EPI == E2C_EPI_F32 || EPI == E2C_EPI_RESID) {
-                        // y = float(acc) * (as * ws), the reference's single-block fold; the clamp only
-                        // when the weight carries one (the defaults +-1e31 bound no finite output)
-                        constexpr int NCH = QCOLS / 16;
-                        const bool clamp = p.out_min > -1e30f || p.out_max < 1e30f;
-    #pragma unroll
-                        for (int c2 = 0; c2 < NCH; c2 += 2) {
-                            uint32_t r[2][16];
-                            tmem_ld16(tbase + part * QCOLS + 16 * c2, r[0]);
-                            if (c2 + 1 < NCH) tmem_ld16(tbase + part * QCOLS + 16 * (c2 + 1), r[1]);
-                            tmem_wait_ld();
-    #pragma unroll
-                            for (int h = 0; h < 2; h++) {
-                                if (c2 + h < NCH) {
-                                    const int nbase = cw + 16 * (c2 + h);
-                                    float w[16], v[16];
-                                    cst16(16 * (c2 + h), w);
-    #pragma unroll
-                                    for (int j = 0; j < 16; j++) v[j] = dq(r[h][j], __fmul_rn(as, w[j]));
-                                    if (clamp)
-    #pragma unroll
-                                        for (int j = 0; j < 16; j++) v[j] = fminf(fmaxf(v[j], p.out_min), p.out_max);
-                                    if constexpr (EPI == E2C_EPI_RESID) {
-                                        if (mrow) {
-                                            const float *rr = p.resid + (size_t)m * p.ldr + nbase;
-                                            for (int j = 0; j < 16; j++)
-                                                if (nbase + j < p.n1) v[j] = __fadd_rn(v[j], rr[j]);
-                                        }
-                                    }
-                                    if (tma_out) {
-                                        put16(v, nbase - p.n0, y0);
-                                    } else if (mrow && nbase < p.n1) {
-                                        float *yr = p.y + (size_t)m * p.ldy + nbase;
-                                        for (int j = 0; j < 16; j++)
-                                            if (nbase + j < p.n1) yr[j] = v[j];
-                                    }
-                                }
-                            }
-                        }
-                    } else if constexpr (EPI == E2C_EPI_GELU) {
-                        // weight rows are interleaved per 128: [gate c0/2 .. +128 | up c0/2 .. +128];
-                        // this warp produces outputs [32 part, 32 part + 32) of the tile's 128, 16 at a time
-                        const int h0 = (c0 - p.n0) / 2;
-    #pragma unroll
-                        for (int h2 = 0; h2 < 2; h2++) {
-                            const int oc = 32 * part + 16 * h2;
-                            uint32_t rg[16], ru[16];
-                            tmem_ld16(tbase + oc, rg);
-                            tmem_ld16(tbase + 128 + oc, ru);
-                            tmem_wait_ld();
-                            float wg[16], wu[16], h[16];
-                            cst16(16 * h2, wg);
-                            cst16(32 + 16 * h2, wu);
-    #pragma unroll
-                            for (int j = 0; j < 16; j++) {
-                                const float g = dq(rg[j], __fmul_rn(as, wg[j]));
-                                const float u = dq(ru[j], __fmul_rn(as, wu[j]));
-                                h[j] = __fmul_rn(gelu_tanh(g), u);
-                            }
-                            if (tma_out) {
-                                put16(h, h0 + oc, y0);
-                            } else if (mrow) {
-                                float4 *y4 = reinterpret_cast<float4 *>(p.y + (size_t)m * p.ldy + h0 + oc);
-    #pragma unroll
-                                for (int j = 0; j < 4; j++) y4[j] = make_float4(h[4 * j], h[4 * j + 1], h[4 * j + 2], h[4 * j + 3]);
-                            }
-                        }
-                    } else if constexpr (EPI == E2C_EPI_QKV) {
-                        // one 256-column tile = one head (q heads, then k, then v). This warp owns
-                        // rotate-half pairs i in [32 part, 32 part + 32) with their partners i + 128.
-                        // x = float(acc) * as * ws;  y = x * inv * gamma with inv = 1/sqrt(mean(x^2) + eps)
-                        // (v: no gamma), computed as float(acc) * (ws * gamma) * (as * inv); then RoPE.
-                        const int head = (c0 - p.n0) / 256;
-                        const bool is_k = head == p.nq, is_v = head == p.nq + 1;
-                        const int pos = mrow ? m % p.seq_len : 0;
-                        // pass 1: sum over this warp's 64 columns of (float(acc) * ws)^2
-                        float ss = 0.f;
-    #pragma unroll
-                        for (int h2 = 0; h2 < 2; h2++) {
-                            uint32_t ra[16], rb[16];
-                            tmem_ld16(tbase + 32 * part + 16 * h2, ra);
-                            tmem_ld16(tbase + 128 + 32 * part + 16 * h2, rb);
-                            tmem_wait_ld();
-                            float wa[16], wb[16];
-                            cst16(16 * h2, wa);
-                            cst16(32 + 16 * h2, wb);
-    #pragma unroll
-                            for (int j = 0; j < 16; j++) {
-                                const float a = __fmul_rn(__int2float_rn((int)ra[j]), wa[j]);
-                                const float b = __fmul_rn(__int2float_rn((int)rb[j]), wb[j]);
-                                ss = __fmaf_rn(b, b, __fmaf_rn(a, a, ss));
-                            }
-                        }
-                        // RoPE coefficients of the first 16 pairs load while the row norms are exchanged
-                        float csv[16], snv[16];
-                        auto rope_load = [&](int ia) {
-                            const float4 *cs4 = reinterpret_cast<const float4 *>(p.rope_cos + (size_t)pos * 128 + ia);
-                            const float4 *sn4 = reinterpret_cast<const float4 *>(p.rope_sin + (size_t)pos * 128 + ia);
-    #pragma unroll
-                            for (int j = 0; j < 4; j++) {
-                                const float4 c4 = __ldg(cs4 + j), s4 = __ldg(sn4 + j);
-                                csv[4 * j] = c4.x, csv[4 * j + 1] = c4.y, csv[4 * j + 2] = c4.z, csv[4 * j + 3] = c4.w;
-                                snv[4 * j] = s4.x, snv[4 * j + 1] = s4.y, snv[4 * j + 2] = s4.z, snv[4 * j + 3] = s4.w;
-                            }
-                        };
-                        if (!is_v) rope_load(32 * part);
-                        // the row's sum of squares over the four warps of this quadrant (same rows)
-                        float *ssq = reinterpret_cast<float *>(smem + L::SSQ_OFF) + acc * 4 * BM;
-                        ssq[part * BM + row] = ss;
-                        mbar_arrive(pair_bar(acc, q));  // release: the partial is visible to the others
-                        if (!__all_sync(0xffffffffu, mbar_wait(pair_bar(acc, q), acc_phase, p.status, E2C_ERR_WAIT_EPI))) {
-                            ok = false;
-                            break;
-                        }
-                        const float sst = __fadd_rn(__fadd_rn(ssq[row], ssq[BM + row]), __fadd_rn(ssq[2 * BM + row], ssq[3 * BM + row]));
-                        const float ms = __fmul_rn(__fmul_rn(as, as), __fdiv_rn(sst, 256.0f));
-                        const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, p.eps)));
-                        const float rs = __fmul_rn(as, inv);
-                        if (!is_v && tma_out && nst > 0) {
-                            // the previous tile's stores have read both staging halves
-                            if (lane == 0) bulk_wait_read0();
-                            __syncwarp();
-                        }
-    #pragma unroll
-                        for (int h2 = 0; h2 < 2; h2++) {
-                            const int ia = 32 * part + 16 * h2;  // rotate-half index of these 16 pairs
-                            uint32_t ra[16], rb[16];
-                            tmem_ld16(tbase + ia, ra);
-                            tmem_ld16(tbase + 128 + ia, rb);
-                            if (h2 == 1 && !is_v) rope_load(ia);
-                            tmem_wait_ld();
-                            float ca[16], cb[16], va[16], vb[16];
-                            cst16(64 + 16 * h2, ca);
-                            cst16(96 + 16 * h2, cb);
-    #pragma unroll
-                            for (int j = 0; j < 16; j++) {
-                                const float a = __fmul_rn(__fmul_rn(__int2float_rn((int)ra[j]), ca[j]), rs);
-                                const float b = __fmul_rn(__fmul_rn(__int2float_rn((int)rb[j]), cb[j]), rs);
-                                if (!is_v) {
-                                    va[j] = __fmaf_rn(a, csv[j], -__fmul_rn(b, snv[j]));
-                                    vb[j] = __fmaf_rn(a, snv[j], __fmul_rn(b, csv[j]));
-                                } else {
-                                    va[j] = a;
-                                    vb[j] = b;
-                                }
-                            }
-                            if (is_v) {
-                                if (mrow) {
-                                    __nv_bfloat16 *vt = reinterpret_cast<__nv_bfloat16 *>(p.vt_out) +
-                                                        (size_t)(m / p.seq_len) * 256 * p.ldvt + pos;
-    #pragma unroll
-                                    for (int j = 0; j < 16; j++) {
-                                        vt[(size_t)(ia + j) * p.ldvt] = __float2bfloat16_rn(va[j]);
-                                        vt[(size_t)(128 + ia + j) * p.ldvt] = __float2bfloat16_rn(vb[j]);
-                                    }
-                                }
-                            } else if (tma_out) {
-                                stage_bf16x16(stg, lane, 2 * h2, va);
-                                stage_bf16x16(stg + STG_WARP, lane, 2 * h2, vb);
-                            } else if (mrow) {
-                                __nv_bfloat16 *dst = is_k ? reinterpret_cast<__nv_bfloat16 *>(p.k_out) + (size_t)m * 256
-                                                          : reinterpret_cast<__nv_bfloat16 *>(p.q_out) +
-                                                                (size_t)m * (256 * p.nq) + head * 256;
-                                for (int j = 0; j < 16; j++) {
-                                    dst[ia + j] = __float2bfloat16_rn(va[j]);
-                                    dst[128 + ia + j] = __float2bfloat16_rn(vb[j]);
-                                }
-                            }
-                        }
-                        if (!is_v && tma_out) {
-                            const CUtensorMap *tm = is_k ? &tmO1 : &tmO0;
-                            const int xb = is_k ? 0 : head * 256;
-                            fence_proxy_async_smem();
-                            __syncwarp();
-                            if (lane == 0) {
-                                tma_store_2d(tm, smem_u32(stg), xb + 32 * part, y0);
-                                tma_store_2d(tm, smem_u32(stg + STG_WARP), xb + 128 + 32 * part, y0);
-                                bulk_commit();
-                            }
-                            ++nst;
-                        }
-                    }
-                    release_acc(acc);
-                    if (++acc == 2) {
-                        acc = 0;
-                        acc_phase ^= 1u;
-                    }
                 }
             }
         }
@@ -947,9 +667,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
 
     tc_fence_before();
-    // a pair (or a NORMADD cluster): no CTA leaves while another may still signal its barriers or
-    // write its shared memory
-    if constexpr (CG == 2 || EPI == E2C_EPI_NORMADD) cluster_sync();
+    // a pair: neither CTA leaves while the other may still signal its barriers
+    if constexpr (CG == 2) cluster_sync();
     else __syncthreads();
     if (warp == 1) {
         __syncwarp();
@@ -966,7 +685,7 @@ int launch(const e2c_gemm_args *a, cudaStream_t st) {
     using L = GemmSmem<BN, STAGES, PERBLOCK, EPI, CG>;
     auto kern = k_gemm_i8<BN, STAGES, PERBLOCK, EPI, CG>;
     static bool attr_set = false;
-    static int max_clusters[9] = {0};  // clusters of 2..8 CTAs the device holds at once
+    static int max_pairs = 0;  // CTA pairs the device holds at once (CG = 2)
     if (!attr_set) {
         if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC) != cudaSuccess) {
             e2c_set_msg("gemm: cannot reserve %d bytes of shared memory", L::ALLOC);
@@ -994,24 +713,15 @@ int launch(const e2c_gemm_args *a, cudaStream_t st) {
         if (a->ldy % 4 == 0 && ((uintptr_t)a->y & 15) == 0)
             tma_out = !e2c_tmap_2d_sw64(&t0, a->y, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)width, (uint64_t)a->M,
                                         (uint64_t)a->ldy * 4, 16, 32);
-    } else if (EPI == E2C_EPI_NORMADD) {
-        // the residual moves by TMA both ways (the dispatcher checked its alignment)
-        if (e2c_tmap_2d_sw64(&t0, a->res, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)(a->n1 - a->n0), (uint64_t)a->M,
-                             (uint64_t)a->ldres * 4, 16, 32))
-            return -3;
-        tma_out = 1;
     } else if (EPI == E2C_EPI_QKV) {
         if ((((uintptr_t)a->q_out | (uintptr_t)a->k_out) & 15) == 0)
             tma_out = !e2c_tmap_2d_sw64(&t0, a->q_out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)256 * a->nq,
                                         (uint64_t)a->M, (uint64_t)512 * a->nq, 32, 32) &&
                       !e2c_tmap_2d_sw64(&t1, a->k_out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 256, (uint64_t)a->M, 512, 32, 32);
     }
-    const int tiles_n = (a->n1 - a->n0 + BN - 1) / BN;
-    const int tiles = ((a->M + BM * CG - 1) / (BM * CG)) * tiles_n;
-    // CTA pairs share 256-row tiles; a NORMADD cluster holds the column blocks of whole rows
-    const int csize = CG == 2 ? 2 : (EPI == E2C_EPI_NORMADD ? tiles_n : 1);
+    const int tiles = ((a->M + BM * CG - 1) / (BM * CG)) * ((a->n1 - a->n0 + BN - 1) / BN);
     cudaError_t e;
-    if (csize == 1) {
+    if constexpr (CG == 1) {
         const int grid = tiles < g_num_sms ? tiles : g_num_sms;
         kern<<<grid, NTHREADS, L::ALLOC, st>>>(ta, tb, t0, t1, *a, tma_out);
         e = cudaGetLastError();
@@ -1020,7 +730,7 @@ int launch(const e2c_gemm_args *a, cudaStream_t st) {
         memset(&cfg, 0, sizeof cfg);
         cudaLaunchAttribute attr[1];
         attr[0].id = cudaLaunchAttributeClusterDimension;
-        attr[0].val.clusterDim.x = (unsigned)csize;
+        attr[0].val.clusterDim.x = 2;
         attr[0].val.clusterDim.y = 1;
         attr[0].val.clusterDim.z = 1;
         cfg.blockDim = dim3(NTHREADS);
@@ -1028,19 +738,16 @@ int launch(const e2c_gemm_args *a, cudaStream_t st) {
         cfg.stream = st;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
-        int &maxc = max_clusters[csize];
-        if (!maxc) {
-            cfg.gridDim = dim3((unsigned)(csize * (g_num_sms / csize)));
-            if (cudaOccupancyMaxActiveClusters(&maxc, kern, &cfg) != cudaSuccess || maxc <= 0) {
+        if (!max_pairs) {
+            cfg.gridDim = dim3(2 * (g_num_sms / 2));
+            if (cudaOccupancyMaxActiveClusters(&max_pairs, kern, &cfg) != cudaSuccess || max_pairs <= 0) {
                 cudaGetLastError();
-                maxc = 0;
-                e2c_set_msg("gemm: the device cannot hold a cluster of %d GEMM CTAs", csize);
+                max_pairs = 0;
+                e2c_set_msg("gemm: the device cannot hold a pair of GEMM CTAs");
                 return -2;
             }
         }
-        // units of work = clusters' worth of tiles (a pair's 256-row tile, a NORMADD row block)
-        const int units = CG == 2 ? tiles : tiles / csize;
-        cfg.gridDim = dim3((unsigned)(csize * (units < maxc ? units : maxc)));
+        cfg.gridDim = dim3(2 * (tiles < max_pairs ? tiles : max_pairs));
         e = cudaLaunchKernelEx(&cfg, kern, ta, tb, t0, t1, *a, tma_out);
     }
     if (e != cudaSuccess) {
@@ -1170,17 +877,17 @@ extern "C" int e2c_gemm(const e2c_gemm_args *a, void *stream) {
         }
         return pair ? launch<256, 4, false, E2C_EPI_QKV, 2>(a, st) : launch<256, 3, false, E2C_EPI_QKV, 1>(a, st);
     case E2C_EPI_NORMADD: {
+        // the residual norms in the epilogue: its own kernel (gemm_i8_norm.cu)
         const int ncols = a->n1 - a->n0;
-        if (perblock || a->n0 != 0 || ncols % 192 || ncols / 192 > 4 || !a->res || !a->norm_g1 ||
+        if (perblock || a->n0 != 0 || ncols % 128 || ncols / 128 > 8 || !a->res || !a->norm_g1 ||
             (!a->norm_g2 && !a->norm_gf) ||
             (a->norm_g2 && (!a->q8 || !a->q8_scale || a->ldq % 16 || ((uintptr_t)a->q8 & 15))) || a->ldres % 4 ||
             ((uintptr_t)a->res & 15)) {
-            e2c_set_msg("gemm: the norm epilogue needs per-row scales, whole rows of 192 x (1..4) columns, a 16-byte "
+            e2c_set_msg("gemm: the norm epilogue needs per-row scales, whole rows of 128 x (1..8) columns, a 16-byte "
                         "aligned res, the norm gains and (with a second gain) 16-byte aligned int8 rows and their scales");
             return -1;
         }
-        // two stages: the residual blocks (96 KB) take the rest of shared memory
-        return launch<192, 2, false, E2C_EPI_NORMADD, 1>(a, st);
+        return e2c_gemm_norm(a, stream);
     }
     default:
         e2c_set_msg("gemm: unknown epilogue %d", a->epi);

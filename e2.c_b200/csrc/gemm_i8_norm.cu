@@ -1,0 +1,574 @@
+// gemm_i8_norm.cu — W8A8 GEMM with an encoder layer's residual norms in its epilogue.
+//
+//   t  = float(acc) * (as[m] * ws[n])                        the projection (o_proj or down)
+//   x  = rmsnorm(t) * g1 + res ;  res <- x                   e2.c src/text.c:947,954 (norm_add)
+//   q8 = quantise(rmsnorm(x) * g2) per token                 the next projection's int8 input
+//   or, after the last layer (g2 NULL):  res <- rmsnorm(x) * gf
+//
+// with rmsnorm(v) = v / sqrt(mean(v^2) + eps) over the D = 128 x (1..8) columns of a row
+// (src/kernels.c:144-171) and the per-token quantiser of src/int8.c:178-209. The GEMM output t
+// never reaches memory: HBM sees the int8 activations, the residual read and written once, and
+// the int8 rows with their scales.
+//
+// Layout: a cluster of D / 128 CTAs owns 128-row blocks, one 128-column block per CTA (the
+// CTA's block is fixed for the kernel), persistent over the row blocks. Per CTA:
+//   warp 0      TMA producer of A [128 x 128] and B [128 x 128] int8 stages (128-byte swizzle);
+//   warp 1      MMA issuer, tcgen05.mma kind::i8 into one of four TMEM accumulators (all 512
+//               columns), so the tensor core runs up to two row blocks ahead of the epilogue;
+//   warps 2-17  epilogue: four per TMEM lane quadrant, each owning 32 rows x 32 columns.
+// A row's statistics span the cluster: each needs a sum over its D columns, reduced in two
+// rounds (sum t^2, then sum x^2 with max |x g2|). In a round the quadrant's four warps combine
+// their columns in shared memory and one of them sends the CTA's partial to every CTA of the
+// cluster by st.async, counted in bytes on the receiver's mbarrier (two slots and barriers,
+// alternating by row block, so a fast CTA's next round never lands on a slot still being read).
+//
+// The epilogue is software-pipelined over row blocks so both rounds' latency hides behind work
+// of a neighbouring block: while block n's second round travels, the warp runs block n+1's first
+// pass; while block n+1's first round travels, it runs block n's last pass. Per block n:
+//   pass 1   acc(n) -> sum (acc ws)^2                     -> round 0 send
+//   pass 2   x = fma(acc, (as inv1)(ws g1), res) into the residual tiles (then TMA store) and
+//            back into acc(n)'s TMEM columns; sum x^2, max |x g2|    -> round 1 send
+//   pass 3   x from TMEM -> q8 = rint((x g2) 127 / max|x g2|), staged and TMA-stored
+// The residual tiles of a warp (32 x 32 fp32, 64-byte swizzle) are reloaded for block n+1 as
+// soon as block n's x store has read them. fp32 is reassociated relative to the two-kernel path
+// (sum t^2 = as^2 sum (acc ws)^2; the products folded per row and column); results agree with it
+// to a few ulp, within the norms' tolerance.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <string.h>
+
+#include "launch.h"
+#include "ptx.cuh"
+#include "tmap.h"
+
+namespace {
+
+constexpr int BM = 128, BN = 128, BK = 128;
+constexpr int STAGES = 3;
+constexpr int NACC = 4;                    // TMEM accumulators of BN columns
+constexpr int EPI_WARPS = 16;
+constexpr int NTHREADS = 64 + 32 * EPI_WARPS;
+constexpr int QCOLS = BN / 4;              // columns per epilogue warp
+constexpr int NCH = QCOLS / 16;            // 16-column chunks per warp
+constexpr int MAXCL = 8;                   // CTAs per cluster: D <= 1024
+constexpr int RES_TILE = 32 * 16 * 4;      // 32 rows x 16 fp32, 64-byte swizzle
+constexpr int Q8_WARP = 32 * QCOLS;        // 32 rows x 32 int8, 32-byte swizzle
+constexpr int C_WG1 = QCOLS, C_G2 = 2 * QCOLS, C_AS = 3 * QCOLS;
+constexpr int CST_FLOATS = C_AS + 4 * 32;  // ws, ws g1, g2 (or gf); four blocks' activation scales
+
+struct Smem {
+    static constexpr int A_BYTES = BM * BK, B_BYTES = BN * BK, STAGE = A_BYTES + B_BYTES;
+    static constexpr int RES_OFF = STAGES * STAGE;
+    static constexpr int Q8_OFF = RES_OFF + EPI_WARPS * NCH * RES_TILE;
+    static constexpr int CST_OFF = Q8_OFF + EPI_WARPS * Q8_WARP;
+    static constexpr int XL0_OFF = CST_OFF + EPI_WARPS * CST_FLOATS * 4;  // [4 parts][BM] float
+    static constexpr int XL1_OFF = XL0_OFF + 4 * BM * 4;                 // [4 parts][BM] float2
+    static constexpr int XR0_OFF = XL1_OFF + 4 * BM * 8;                 // [2][MAXCL][BM] float
+    static constexpr int XR1_OFF = XR0_OFF + 2 * MAXCL * BM * 4;         // [2][MAXCL][BM] float2
+    static constexpr int BAR_OFF = XR1_OFF + 2 * MAXCL * BM * 8;
+    // full[S], empty[S], tfull[NACC], tempty[NACC], lbar[2 rounds][4], xbar[2 rounds][2][4], rbar[16]
+    static constexpr int NBAR = 2 * STAGES + 2 * NACC + 8 + 16 + EPI_WARPS;
+    static constexpr int BYTES = BAR_OFF + NBAR * 8 + 16;
+    static constexpr int ALLOC = BYTES + 1024;  // slack for 1024-byte alignment
+    static_assert(RES_OFF % 1024 == 0 && Q8_OFF % 1024 == 0, "swizzled TMA tiles");
+    static_assert(ALLOC <= 232448, "shared memory");
+};
+
+// QUANT: the next layer's int8 input is produced (g2 given); otherwise the final norm (gf)
+template <bool QUANT>
+__global__ void __launch_bounds__(NTHREADS, 1)
+    k_gemm_norm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                const __grid_constant__ CUtensorMap tmR, const __grid_constant__ CUtensorMap tmQ,
+                const e2c_gemm_args p) {
+    using L = Smem;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    const uint32_t sbase = smem_u32(smem);
+    const uint32_t bar0 = sbase + L::BAR_OFF;
+    auto full_bar = [&](int s) { return bar0 + 8u * s; };
+    auto empty_bar = [&](int s) { return bar0 + 8u * (STAGES + s); };
+    auto tfull_bar = [&](int a) { return bar0 + 8u * (2 * STAGES + a); };
+    auto tempty_bar = [&](int a) { return bar0 + 8u * (2 * STAGES + NACC + a); };
+    auto lbar = [&](int r, int q) { return bar0 + 8u * (2 * STAGES + 2 * NACC + 4 * r + q); };
+    auto xbar = [&](int r, int b, int q) { return bar0 + 8u * (2 * STAGES + 2 * NACC + 8 + 8 * r + 4 * b + q); };
+    auto rbar = [&](int w) { return bar0 + 8u * (2 * STAGES + 2 * NACC + 24 + w); };
+    volatile uint32_t *tmem_slot = reinterpret_cast<volatile uint32_t *>(smem + L::BAR_OFF + L::NBAR * 8);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int M = p.M, K = p.K, D = p.n1 - p.n0;
+    const int ncl = D / BN;                      // CTAs of a cluster (the launch's cluster width)
+    const int rank = (int)(blockIdx.x % (unsigned)ncl);  // = cluster rank = this CTA's column block
+    const int cid = (int)(blockIdx.x / (unsigned)ncl), ncls = (int)(gridDim.x / (unsigned)ncl);
+    const int tiles_m = (M + BM - 1) / BM;
+    const int ntl = cid < tiles_m ? (tiles_m - 1 - cid) / ncls + 1 : 0;  // row blocks of this CTA
+    const int nk = (K + BK - 1) / BK;
+    auto row0 = [&](int n) { return (cid + n * ncls) * BM; };
+
+    if (warp == 0 && lane == 0) {
+        for (int s = 0; s < STAGES; s++) {
+            mbar_init(full_bar(s), 1);
+            mbar_init(empty_bar(s), 1);
+        }
+        for (int a = 0; a < NACC; a++) {
+            mbar_init(tfull_bar(a), 1);
+            mbar_init(tempty_bar(a), EPI_WARPS);
+        }
+        for (int r = 0; r < 2; r++)
+            for (int q = 0; q < 4; q++) {
+                mbar_init(lbar(r, q), 128);  // the quadrant's 4 warps
+                for (int b = 0; b < 2; b++) mbar_init(xbar(r, b, q), 1);  // own expect_tx; bytes by st.async
+            }
+        for (int w = 0; w < EPI_WARPS; w++) mbar_init(rbar(w), 1);
+        fence_mbar_init();
+        tma_prefetch_desc(&tmA);
+        tma_prefetch_desc(&tmB);
+    }
+    if (warp == 1) {
+        __syncwarp();
+        tmem_alloc(sbase + L::BAR_OFF + L::NBAR * 8, NACC * BN);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    cluster_sync();  // every CTA's barriers exist before another CTA signals them
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------------ TMA producer
+        if (elect_one()) {
+            int stage = 0, issued = 0;
+            uint32_t phase = 0;
+            bool ok = true;
+            for (int n = 0; n < ntl && ok; n++) {
+                for (int kb = 0; kb < nk; kb++) {
+                    if (!mbar_wait(empty_bar(stage), phase ^ 1u, p.status, E2C_ERR_WAIT_PRODUCER)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t sa = sbase + stage * L::STAGE, sb = sa + L::A_BYTES;
+                    mbar_arrive_expect_tx(full_bar(stage), L::STAGE);
+                    tma_load_2d(sa, &tmA, kb * BK, row0(n), full_bar(stage));
+                    tma_load_2d(sb, &tmB, kb * BK, p.n0 + rank * BN, full_bar(stage));
+                    issued++;
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+            }
+            if (!ok) {
+                // the copies this thread started land before the CTA's shared memory goes away
+                int s = stage, ph = (int)phase;
+                for (int i = 0; i < (issued < STAGES ? issued : STAGES); i++) {
+                    if (--s < 0) {
+                        s = STAGES - 1;
+                        ph ^= 1;
+                    }
+                    mbar_wait(full_bar(s), (uint32_t)ph, nullptr, E2C_ERR_WAIT_DRAIN);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------------ MMA issuer
+        if (elect_one()) {
+            constexpr uint32_t idesc = idesc_i8(BN, BM);
+            int stage = 0;
+            uint32_t phase = 0;
+            bool ok = true;
+            int n = 0;
+            for (; n < ntl && ok; n++) {
+                const int a = n % NACC;
+                if (!mbar_wait(tempty_bar(a), (uint32_t)((n / NACC) & 1) ^ 1u, p.status, E2C_ERR_WAIT_MMA)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d = tmem_base + (uint32_t)(a * BN);
+                for (int kb = 0; kb < nk; kb++) {
+                    if (!mbar_wait(full_bar(stage), phase, p.status, E2C_ERR_WAIT_MMA)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t sa = sbase + stage * L::STAGE, sb = sa + L::A_BYTES;
+#pragma unroll
+                    for (int k = 0; k < BK / 32; k++)
+                        mma_i8(d, smem_desc_sw128(sa + 32 * k), smem_desc_sw128(sb + 32 * k), idesc, (kb | k) != 0);
+                    mma_commit(empty_bar(stage));
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (!ok) break;
+                mma_commit(tfull_bar(a));
+            }
+            if (!ok) {
+                // every MMA issued so far finishes before the accumulators are released
+                const uint32_t drain = tfull_bar(n % NACC);
+                mma_commit(drain);
+                mbar_wait(drain, (uint32_t)((n / NACC) & 1), nullptr, E2C_ERR_WAIT_DRAIN);
+            }
+        }
+    } else {
+        // ------------------------------------------------------------------ epilogue
+        const int q = warp & 3;             // TMEM lane quadrant this warp may access
+        const int part = (warp - 2) >> 2;   // which 32 of the CTA's 128 columns
+        const int row = q * 32 + lane;      // row of the block = TMEM lane
+        const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
+        const int cl0 = rank * BN + part * QCOLS;  // first column of this warp within the row
+        constexpr bool quant = QUANT;
+        float *cst = reinterpret_cast<float *>(smem + L::CST_OFF) + (warp - 2) * CST_FLOATS;
+        uint8_t *resb = smem + L::RES_OFF + (warp - 2) * NCH * RES_TILE;
+        const uint32_t resb_s = smem_u32(resb);
+        uint8_t *q8s = smem + L::Q8_OFF + (warp - 2) * Q8_WARP;
+        const uint32_t rb = rbar(warp - 2);
+        {
+            const float *gb = quant ? p.norm_g2 : p.norm_gf;
+            for (int j = lane; j < QCOLS; j += 32) {
+                const float w = __ldg(p.w_scale + p.n0 + cl0 + j);
+                cst[j] = w;
+                cst[C_WG1 + j] = __fmul_rn(w, __ldg(p.norm_g1 + cl0 + j));
+                cst[C_G2 + j] = __ldg(gb + cl0 + j);
+            }
+            __syncwarp();
+        }
+        bool ok = true, xok = true;
+        // the rows' activation scales of block n land in slot n & 3 by cp.async (one group per call)
+        const uint32_t as_slot = smem_u32(cst + C_AS + lane);
+        auto load_as = [&](int n) {
+            if (n < ntl) {
+                const int mr = row0(n) + row;
+                cp_async_4(as_slot + (uint32_t)((n & 3) * 128), p.a_scale + (mr < M ? (size_t)mr : 0), mr < M ? 4u : 0u);
+            }
+            cp_async_commit();
+        };
+        // the residual of block n: this warp's 32 rows x 32 columns, two 64-byte-swizzled tiles
+        bool rpend = false;
+        uint32_t rpar = 0;
+        auto load_res = [&](int n) {
+            if (lane == 0) {
+                mbar_arrive_expect_tx(rb, (uint32_t)(NCH * RES_TILE));
+#pragma unroll
+                for (int c = 0; c < NCH; c++) tma_load_2d(resb_s + c * RES_TILE, &tmR, cl0 + 16 * c, row0(n) + q * 32, rb);
+            }
+            rpend = true;
+            rpar = (uint32_t)(n & 1);
+        };
+        auto store_res = [&](int n) {
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+#pragma unroll
+                for (int c = 0; c < NCH; c++) tma_store_2d(&tmR, resb_s + c * RES_TILE, cl0 + 16 * c, row0(n) + q * 32);
+                bulk_commit();
+            }
+        };
+        // element (lane, 4 k .. 4 k + 3) of residual tile c (the TMA map's 64-byte swizzle)
+        auto rp = [&](int c, int k) -> float4 * {
+            return reinterpret_cast<float4 *>(resb + c * RES_TILE + lane * 64 + ((k ^ ((lane >> 1) & 3)) << 4));
+        };
+        float *xl0 = reinterpret_cast<float *>(smem + L::XL0_OFF);
+        float2 *xl1 = reinterpret_cast<float2 *>(smem + L::XL1_OFF);
+        // round r of block n: this warp's partial (sum in .x, max in .y) to the quadrant, and from
+        // part 0 the CTA's partial to every CTA of the cluster
+        auto send = [&](int r, int n, float2 v) {
+            if (r == 0) xl0[part * BM + row] = v.x;
+            else xl1[part * BM + row] = v;
+            mbar_arrive(lbar(r, q));
+            if (part != 0) return;
+            xok = xok && __all_sync(0xffffffffu, mbar_wait(lbar(r, q), (uint32_t)(n & 1), p.status, E2C_ERR_WAIT_EPI));
+            float2 c = make_float2(0.f, 0.f);
+#pragma unroll
+            for (int w = 0; w < 4; w++) {
+                if (r == 0) {
+                    c.x = __fadd_rn(c.x, xl0[w * BM + row]);
+                } else {
+                    const float2 o = xl1[w * BM + row];
+                    c.x = __fadd_rn(c.x, o.x);
+                    c.y = fmaxf(c.y, o.y);
+                }
+            }
+            const int b = n & 1;
+            const uint32_t xb = xbar(r, b, q);
+            if (lane == 0) mbar_arrive_expect_tx(xb, (uint32_t)(ncl * 32 * (r == 0 ? 4 : 8)));
+            const uint32_t slot = r == 0 ? sbase + L::XR0_OFF + (uint32_t)(((b * MAXCL + rank) * BM + row) * 4)
+                                         : sbase + L::XR1_OFF + (uint32_t)(((b * MAXCL + rank) * BM + row) * 8);
+            for (int d = 0; d < ncl; d++) {
+                if (r == 0) st_async_f32(mapa_shared(slot, (uint32_t)d), c.x, mapa_shared(xb, (uint32_t)d));
+                else st_async_f32x2(mapa_shared(slot, (uint32_t)d), c.x, c.y, mapa_shared(xb, (uint32_t)d));
+            }
+        };
+        auto recv = [&](int r, int n) -> float2 {
+            const int b = n & 1;
+            xok = xok && __all_sync(0xffffffffu, mbar_wait(xbar(r, b, q), (uint32_t)((n >> 1) & 1), p.status, E2C_ERR_WAIT_EPI));
+            float2 tot = make_float2(0.f, 0.f);
+            for (int d = 0; d < ncl; d++) {
+                if (r == 0) {
+                    tot.x = __fadd_rn(tot.x, reinterpret_cast<const float *>(smem + L::XR0_OFF)[(b * MAXCL + d) * BM + row]);
+                } else {
+                    const float2 o = reinterpret_cast<const float2 *>(smem + L::XR1_OFF)[(b * MAXCL + d) * BM + row];
+                    tot.x = __fadd_rn(tot.x, o.x);
+                    tot.y = fmaxf(tot.y, o.y);
+                }
+            }
+            return tot;
+        };
+        auto tcols = [&](int n) { return tmem_base + lane_addr + (uint32_t)((n % NACC) * BN + part * QCOLS); };
+        // pass 1: as^2 sum over the warp's columns of (acc ws)^2, once block n's accumulator is full
+        auto pass1 = [&](int n) -> float {
+            if (!__all_sync(0xffffffffu, mbar_wait(tfull_bar(n % NACC), (uint32_t)((n / NACC) & 1), p.status, E2C_ERR_WAIT_EPI))) {
+                ok = false;
+                return 0.f;
+            }
+            tc_fence_after();
+            uint32_t r[NCH][16];
+#pragma unroll
+            for (int c = 0; c < NCH; c++) tmem_ld16(tcols(n) + 16 * c, r[c]);
+            tmem_wait_ld();
+            float ss = 0.f;
+#pragma unroll
+            for (int c = 0; c < NCH; c++)
+#pragma unroll
+                for (int k = 0; k < 4; k++) {
+                    const float4 w4 = *reinterpret_cast<const float4 *>(cst + 16 * c + 4 * k);
+                    const float u0 = __fmul_rn(__int2float_rn((int)r[c][4 * k]), w4.x);
+                    const float u1 = __fmul_rn(__int2float_rn((int)r[c][4 * k + 1]), w4.y);
+                    const float u2 = __fmul_rn(__int2float_rn((int)r[c][4 * k + 2]), w4.z);
+                    const float u3 = __fmul_rn(__int2float_rn((int)r[c][4 * k + 3]), w4.w);
+                    ss = __fmaf_rn(u3, u3, __fmaf_rn(u2, u2, __fmaf_rn(u1, u1, __fmaf_rn(u0, u0, ss))));
+                }
+            const float as = cst[C_AS + (n & 3) * 32 + lane];
+            return __fmul_rn(__fmul_rn(as, as), ss);
+        };
+        auto release = [&](int n) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(tempty_bar(n % NACC));
+        };
+
+        if (ntl > 0) {
+            load_as(0);
+            load_as(1);
+            load_res(0);
+            cp_async_wait_1();
+            const float s0 = pass1(0);
+            if (ok) send(0, 0, make_float2(s0, 0.f));
+        }
+        for (int n = 0; n < ntl && ok && xok; n++) {
+            const int y0 = row0(n) + q * 32;
+            load_as(n + 2);
+            const float s1 = recv(0, n).x;
+            if (!xok) break;
+            const float inv1 = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(s1, (float)D), p.eps)));
+            const float sr = __fmul_rn(cst[C_AS + (n & 3) * 32 + lane], inv1);
+            // pass 2: x = fma(acc, sr (ws g1), res) into the residual tiles and the accumulator
+            if (!__all_sync(0xffffffffu, mbar_wait(rb, rpar, p.status, E2C_ERR_WAIT_EPI))) {
+                ok = false;
+                break;
+            }
+            rpend = false;
+            float ss2 = 0.f, mx = 0.f;
+#pragma unroll
+            for (int c = 0; c < NCH; c++) {
+                uint32_t r[16];
+                tmem_ld16(tcols(n) + 16 * c, r);
+                tmem_wait_ld();
+#pragma unroll
+                for (int k = 0; k < 4; k++) {
+                    float4 *p4 = rp(c, k);
+                    const float4 r4 = *p4;
+                    const float4 c4 = *reinterpret_cast<const float4 *>(cst + C_WG1 + 16 * c + 4 * k);
+                    const float4 x4 = make_float4(__fmaf_rn(__int2float_rn((int)r[4 * k]), __fmul_rn(sr, c4.x), r4.x),
+                                                  __fmaf_rn(__int2float_rn((int)r[4 * k + 1]), __fmul_rn(sr, c4.y), r4.y),
+                                                  __fmaf_rn(__int2float_rn((int)r[4 * k + 2]), __fmul_rn(sr, c4.z), r4.z),
+                                                  __fmaf_rn(__int2float_rn((int)r[4 * k + 3]), __fmul_rn(sr, c4.w), r4.w));
+                    *p4 = x4;
+                    r[4 * k] = __float_as_uint(x4.x);
+                    r[4 * k + 1] = __float_as_uint(x4.y);
+                    r[4 * k + 2] = __float_as_uint(x4.z);
+                    r[4 * k + 3] = __float_as_uint(x4.w);
+                    ss2 = __fmaf_rn(x4.w, x4.w, __fmaf_rn(x4.z, x4.z, __fmaf_rn(x4.y, x4.y, __fmaf_rn(x4.x, x4.x, ss2))));
+                    if constexpr (quant) {
+                        const float4 g4 = *reinterpret_cast<const float4 *>(cst + C_G2 + 16 * c + 4 * k);
+                        mx = fmaxf(fmaxf(fmaxf(fmaxf(mx, fabsf(__fmul_rn(x4.x, g4.x))), fabsf(__fmul_rn(x4.y, g4.y))),
+                                         fabsf(__fmul_rn(x4.z, g4.z))),
+                                   fabsf(__fmul_rn(x4.w, g4.w)));
+                    }
+                }
+                tmem_st16(tcols(n) + 16 * c, r);  // x replaces t in the accumulator for pass 3
+            }
+            tmem_wait_st();
+            if constexpr (quant) store_res(n);  // the new residual is x
+            send(1, n, make_float2(ss2, mx));
+            if constexpr (quant) {
+                // block n+1's first pass and residual load while block n's second round travels
+                if (n + 1 < ntl) {
+                    cp_async_wait_1();
+                    const float s0 = pass1(n + 1);
+                    if (!ok) break;
+                    send(0, n + 1, make_float2(s0, 0.f));
+                    if (lane == 0) bulk_wait_read0();  // block n's x store has read the tiles
+                    __syncwarp();
+                    load_res(n + 1);
+                }
+                const float2 t2 = recv(1, n);
+                if (!xok) break;
+                // pass 3: the quantiser of src/int8.c:178-209 on z = x inv2 g2, amax = inv2 max|x g2|,
+                // scale = amax / 127, q = rint(z 127 / amax) = rint((x g2) 127 / max|x g2|); |q| <= 127
+                // needs no clamp, and rint is the round-to-nearest-even of adding 1.5 2^23, whose low
+                // byte is q
+                const float inv2 = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t2.x, (float)D), p.eps)));
+                const float amax = __fmul_rn(t2.y, inv2);
+                const float s = t2.y > 0.f ? __fdiv_rn(127.0f, t2.y) : 0.f;
+                const int m = row0(n) + row;
+                if (rank == 0 && part == 0 && m < M) p.q8_scale[m] = amax > 0.f ? __fmul_rn(amax, 0x1.020408p-7f) : 1.0f;
+                if (lane == 0) bulk_wait_read1();  // block n-1's int8 store has read the staging rows
+                __syncwarp();
+#pragma unroll
+                for (int c = 0; c < NCH; c++) {
+                    uint32_t r[16];
+                    tmem_ld16(tcols(n) + 16 * c, r);
+                    tmem_wait_ld();
+                    uint32_t pk[4];
+#pragma unroll
+                    for (int k = 0; k < 4; k++) {
+                        const float4 g4 = *reinterpret_cast<const float4 *>(cst + C_G2 + 16 * c + 4 * k);
+                        const uint32_t b0 = __float_as_uint(__fmaf_rn(__fmul_rn(__uint_as_float(r[4 * k]), g4.x), s, 12582912.0f));
+                        const uint32_t b1 = __float_as_uint(__fmaf_rn(__fmul_rn(__uint_as_float(r[4 * k + 1]), g4.y), s, 12582912.0f));
+                        const uint32_t b2 = __float_as_uint(__fmaf_rn(__fmul_rn(__uint_as_float(r[4 * k + 2]), g4.z), s, 12582912.0f));
+                        const uint32_t b3 = __float_as_uint(__fmaf_rn(__fmul_rn(__uint_as_float(r[4 * k + 3]), g4.w), s, 12582912.0f));
+                        pk[k] = __byte_perm(__byte_perm(b0, b1, 0x0040), __byte_perm(b2, b3, 0x0040), 0x5410);
+                    }
+                    // 16-byte chunk c of row `lane` in the 32-byte swizzle of the int8 map
+                    *reinterpret_cast<uint4 *>(q8s + lane * 32 + ((c ^ ((lane >> 2) & 1)) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                }
+                release(n);
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                    tma_store_2d(&tmQ, smem_u32(q8s), cl0, y0);
+                    bulk_commit();
+                }
+            } else {
+                // the final norm: res = x inv2 gf, written over x in the tiles; then block n+1
+                const float2 t2 = recv(1, n);
+                if (!xok) break;
+                const float inv2 = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t2.x, (float)D), p.eps)));
+#pragma unroll
+                for (int c = 0; c < NCH; c++)
+#pragma unroll
+                    for (int k = 0; k < 4; k++) {
+                        float4 *p4 = rp(c, k);
+                        const float4 x4 = *p4;
+                        const float4 g4 = *reinterpret_cast<const float4 *>(cst + C_G2 + 16 * c + 4 * k);
+                        *p4 = make_float4(__fmul_rn(__fmul_rn(x4.x, inv2), g4.x), __fmul_rn(__fmul_rn(x4.y, inv2), g4.y),
+                                          __fmul_rn(__fmul_rn(x4.z, inv2), g4.z), __fmul_rn(__fmul_rn(x4.w, inv2), g4.w));
+                    }
+                release(n);
+                store_res(n);
+                if (n + 1 < ntl) {
+                    cp_async_wait_1();
+                    const float s0 = pass1(n + 1);
+                    if (!ok) break;
+                    send(0, n + 1, make_float2(s0, 0.f));
+                    if (lane == 0) bulk_wait_read0();
+                    __syncwarp();
+                    load_res(n + 1);
+                }
+            }
+        }
+        // copies into this warp's shared memory land, and its stores complete, before the CTA ends
+        cp_async_wait_all();
+        if (rpend) {
+            if (lane == 0) mbar_wait(rb, rpar, nullptr, E2C_ERR_WAIT_DRAIN);
+            __syncwarp();
+        }
+        if (lane == 0) bulk_wait0();
+        __syncwarp();
+    }
+
+    tc_fence_before();
+    // no CTA leaves while another may still signal its barriers or write its shared memory
+    cluster_sync();
+    if (warp == 1) {
+        __syncwarp();
+        tc_fence_after();
+        tmem_dealloc(tmem_base, NACC * BN);
+    }
+}
+
+int g_num_sms = 0;
+
+}  // namespace
+
+// The GEMM + norms launch: geometry checked by e2c_gemm (per-row scales, n0 = 0, D = 128 x (1..8)).
+extern "C" int e2c_gemm_norm(const e2c_gemm_args *a, void *stream) {
+    using L = Smem;
+    static bool attr_set = false;
+    static int max_clusters[2][MAXCL + 1] = { { 0 } };
+    if (!g_num_sms) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        if (cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || g_num_sms <= 0) {
+            e2c_set_msg("gemm_norm: no CUDA device");
+            return -2;
+        }
+    }
+    if (!attr_set) {
+        if (cudaFuncSetAttribute(k_gemm_norm<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC) != cudaSuccess ||
+            cudaFuncSetAttribute(k_gemm_norm<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC) != cudaSuccess) {
+            e2c_set_msg("gemm_norm: cannot reserve %d bytes of shared memory", L::ALLOC);
+            return -2;
+        }
+        attr_set = true;
+    }
+    const int D = a->n1 - a->n0;
+    const int ncl = D / BN;
+    if (a->n0 != 0 || D % BN || ncl < 1 || ncl > MAXCL) {
+        e2c_set_msg("gemm_norm: rows of 128 x (1..8) columns starting at column 0");
+        return -1;
+    }
+    CUtensorMap ta, tb, tr, tq;
+    memset(&tq, 0, sizeof tq);
+    if (e2c_tmap_2d(&ta, a->a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)a->K, (uint64_t)a->M, (uint64_t)a->lda, BK, BM) ||
+        e2c_tmap_2d(&tb, a->w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)a->K, (uint64_t)a->wrows, (uint64_t)a->ldw, BK, BN) ||
+        e2c_tmap_2d_sw64(&tr, a->res, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)D, (uint64_t)a->M,
+                         (uint64_t)a->ldres * 4, 16, 32) ||
+        (a->norm_g2 && e2c_tmap_2d_sw32(&tq, a->q8, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)D, (uint64_t)a->M,
+                                        (uint64_t)a->ldq, QCOLS, 32)))
+        return -3;
+    const int tiles_m = (a->M + BM - 1) / BM;
+    cudaLaunchConfig_t cfg;
+    memset(&cfg, 0, sizeof cfg);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)ncl;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.blockDim = dim3(NTHREADS);
+    cfg.dynamicSmemBytes = L::ALLOC;
+    cfg.stream = (cudaStream_t)stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const bool quant = a->norm_g2 != nullptr;
+    auto kern = quant ? k_gemm_norm<true> : k_gemm_norm<false>;
+    int &maxc = max_clusters[quant][ncl];
+    if (!maxc) {
+        cfg.gridDim = dim3((unsigned)(ncl * (g_num_sms / ncl)));
+        if (cudaOccupancyMaxActiveClusters(&maxc, kern, &cfg) != cudaSuccess || maxc <= 0) {
+            cudaGetLastError();
+            maxc = 0;
+            e2c_set_msg("gemm_norm: the device cannot hold a cluster of %d CTAs", ncl);
+            return -2;
+        }
+    }
+    cfg.gridDim = dim3((unsigned)(ncl * (tiles_m < maxc ? tiles_m : maxc)));
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, tb, tr, tq, *a);
+    if (e != cudaSuccess) {
+        e2c_set_msg("gemm_norm launch: %s", cudaGetErrorString(e));
+        return -2;
+    }
+    return 0;
+}

@@ -38,7 +38,7 @@ enum {
     E2C_EPI_QKV = 4,   /* per-head RMSNorm (+gamma) + RoPE -> bf16 Q, K, V^T               */
     E2C_EPI_NORMADD = 5 /* y = gemm (never stored); x = rmsnorm(y) * g1 + res; res = x;
                           q = quantise(rmsnorm(x) * g2) per token (g2 NULL: res = rmsnorm(x) * gf).
-                          Whole rows per cluster of CTAs (N = 768: 4 x 192 columns) */
+                          Whole rows per cluster of CTAs (N = 768: 6 x 128 columns) */
 };
 
 typedef struct {
@@ -85,6 +85,9 @@ int e2c_gemm(const e2c_gemm_args *a, void *stream);
  * picks it for short activation matrices (few output tiles). Per-row scales, F32 or residual
  * epilogue only. */
 int e2c_gemm_splitk(const e2c_gemm_args *a, int bn, int S, void *stream);
+/* E2C_EPI_NORMADD (gemm_i8_norm.cu): rows of 128 x (1..8) columns over a cluster of CTAs, the
+ * residual norms in the epilogue; called by e2c_gemm after its checks */
+int e2c_gemm_norm(const e2c_gemm_args *a, void *stream);
 /* the split that puts most CTAs to work with every cluster resident at once: returns the CTA count
  * (0 when the split kernel does not apply) and sets *bn, *S */
 int e2c_gemm_splitk_plan(const e2c_gemm_args *a, int num_sms, int *bn, int *S);

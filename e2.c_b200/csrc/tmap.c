@@ -47,8 +47,9 @@ static int tmap_2d(CUtensorMap *m, const void *base, CUtensorMapDataType dt, int
         e2c_set_msg("tensor map: cuTensorMapEncodeTiled unavailable");
         return -1;
     }
-    if (box_inner * (uint32_t)elem_bytes != swz || ((uintptr_t)base & 15) || (row_stride & 15)) {
-        e2c_set_msg("tensor map: %u-byte boxes, 16-byte aligned base and row stride required", swz);
+    if ((swz ? box_inner * (uint32_t)elem_bytes != swz : (box_inner * (uint32_t)elem_bytes) % 16 != 0) ||
+        ((uintptr_t)base & 15) || (row_stride & 15)) {
+        e2c_set_msg("tensor map: %u-byte boxes, 16-byte aligned base and row stride required", swz ? swz : 16);
         return -1;
     }
     const cuuint64_t dims[2] = { inner, outer };
@@ -57,7 +58,10 @@ static int tmap_2d(CUtensorMap *m, const void *base, CUtensorMapDataType dt, int
     const cuuint32_t estr[2] = { 1, 1 };
     memset(m, 0, sizeof *m);
     const CUresult r = enc(m, dt, 2, (void *)base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                           swz == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                           swz == 128  ? CU_TENSOR_MAP_SWIZZLE_128B
+                           : swz == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                           : swz == 32 ? CU_TENSOR_MAP_SWIZZLE_32B
+                                       : CU_TENSOR_MAP_SWIZZLE_NONE,
                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) {
         e2c_set_msg("tensor map: encode failed (%d) for %llu x %llu, stride %llu, box %u x %u", (int)r,
@@ -76,4 +80,14 @@ int e2c_tmap_2d(CUtensorMap *m, const void *base, CUtensorMapDataType dt, int el
 int e2c_tmap_2d_sw64(CUtensorMap *m, const void *base, CUtensorMapDataType dt, int elem_bytes, uint64_t inner,
                      uint64_t outer, uint64_t row_stride, uint32_t box_inner, uint32_t box_outer) {
     return tmap_2d(m, base, dt, elem_bytes, inner, outer, row_stride, box_inner, box_outer, 64);
+}
+
+int e2c_tmap_2d_sw32(CUtensorMap *m, const void *base, CUtensorMapDataType dt, int elem_bytes, uint64_t inner,
+                     uint64_t outer, uint64_t row_stride, uint32_t box_inner, uint32_t box_outer) {
+    return tmap_2d(m, base, dt, elem_bytes, inner, outer, row_stride, box_inner, box_outer, 32);
+}
+
+int e2c_tmap_2d_plain(CUtensorMap *m, const void *base, CUtensorMapDataType dt, int elem_bytes, uint64_t inner,
+                      uint64_t outer, uint64_t row_stride, uint32_t box_inner, uint32_t box_outer) {
+    return tmap_2d(m, base, dt, elem_bytes, inner, outer, row_stride, box_inner, box_outer, 0);
 }

@@ -15,6 +15,12 @@ int e2c_tmap_2d(CUtensorMap *m, const void *base, CUtensorMapDataType dt, int el
 // The same with the 64-byte swizzle (box_inner * elem must be 64 bytes).
 int e2c_tmap_2d_sw64(CUtensorMap *m, const void *base, CUtensorMapDataType dt, int elem_bytes, uint64_t inner,
                      uint64_t outer, uint64_t row_stride, uint32_t box_inner, uint32_t box_outer);
+// The same with the 32-byte swizzle (box_inner * elem must be 32 bytes).
+int e2c_tmap_2d_sw32(CUtensorMap *m, const void *base, CUtensorMapDataType dt, int elem_bytes, uint64_t inner,
+                     uint64_t outer, uint64_t row_stride, uint32_t box_inner, uint32_t box_outer);
+// Without swizzle: row-major boxes (box_inner * elem a multiple of 16 bytes).
+int e2c_tmap_2d_plain(CUtensorMap *m, const void *base, CUtensorMapDataType dt, int elem_bytes, uint64_t inner,
+                      uint64_t outer, uint64_t row_stride, uint32_t box_inner, uint32_t box_outer);
 
 #ifdef __cplusplus
 }

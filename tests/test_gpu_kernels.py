@@ -309,16 +309,17 @@ def test_qkv_epilogue_norm_rope(e2c, of, torch_cuda, B, S):
     assert (diff == 0).mean() > 0.99
 
 
-@pytest.mark.parametrize("M,final", [(300, False), (16384, False), (1000, True)])
-def test_gemm_norm_add_epilogue(e2c, of, torch_cuda, M, final):
+@pytest.mark.parametrize("M,D,final", [(300, 768, False), (16384, 768, False), (1000, 768, True), (700, 256, False),
+                                       (517, 1024, False), (130, 128, False), (4000, 1024, True)])
+def test_gemm_norm_add_epilogue(e2c, of, torch_cuda, M, D, final):
     """o_proj / down with the residual norm fused (e2.c src/text.c:947,950 + :321-339): the GEMM's fp32
     output t stays on chip; x = rmsnorm(t) * g1 + res becomes the residual and the next layer's input
     rmsnorm(x) * g2 is quantised per token (or, after the last layer, rmsnorm(x) * gf is written).
-    Rows span a cluster of four CTAs of 192 columns. Against fp64 of the same formula on the
-    bit-exact t; 16384 rows give every CTA several tiles."""
+    Rows span a cluster of D / 128 CTAs (1 to 8). Against fp64 of the same formula on the bit-exact
+    t; 16384 rows give every CTA several row blocks, so the pipelined epilogue wraps its slots."""
     torch = torch_cuda
     rng = np.random.default_rng(61 + M)
-    N = K = 768
+    N = K = D
     qa, a_s, w, ws = _gemm_inputs(rng, M, N, K, K)
     res0 = rng.standard_normal((M, N)).astype(np.float32)
     g1 = (1 + 0.1 * rng.standard_normal(N)).astype(np.float32)
