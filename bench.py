@@ -400,32 +400,35 @@ def config4(args) -> int:
 # One layer's kernels at the encoder's shape (M = 64 x 512 tokens, hidden 768, FFN 1152, 3 q heads and
 # one KV head of 256), the per-launch algorithmic work each is measured against, and the launches of
 # each per layer. Weights are quantised N(0, 0.02), activations per-token quantised N(0, 1).
-KERNELS = ("gate_up", "qkv", "o_proj", "down", "o_proj_norm", "down_norm", "attention", "quantize", "quantize_ctx",
-           "norm_add")
-# the kernels an encoder layer runs (hidden 768, per-token scales: the residual norms fused into o_proj
-# and down, or with E2C_FUSED_NORM=0 their own row kernel after each)
-LAYER_KERNELS = ("gate_up", "qkv", "o_proj_norm", "down_norm", "attention", "quantize", "quantize_ctx")
+KERNELS = ("gate_up", "gate_up_q", "qkv", "o_proj", "down", "o_proj_norm", "down_norm", "attention", "quantize",
+           "quantize_ctx", "norm_add")
+# the kernels an encoder layer runs (hidden 768, FFN 1152, per-token scales): the residual norms fused
+# into o_proj and down and h's quantiser into gate|up, or with E2C_FUSED_NORM=0 / E2C_FUSED_GELU=0
+# the row kernels after them
+LAYER_KERNELS = ("gate_up_q", "qkv", "o_proj_norm", "down_norm", "attention", "quantize_ctx")
 if os.environ.get("E2C_FUSED_NORM") == "0":
-    LAYER_KERNELS = ("gate_up", "qkv", "o_proj", "down", "attention", "quantize", "quantize_ctx", "norm_add")
+    LAYER_KERNELS = tuple(k for k in LAYER_KERNELS if k not in ("o_proj_norm", "down_norm")) + ("o_proj", "down", "norm_add")
+if os.environ.get("E2C_FUSED_GELU") == "0":
+    LAYER_KERNELS = tuple(k for k in LAYER_KERNELS if k != "gate_up_q") + ("gate_up", "quantize")
 
 
 def kernel_work(name: str, M: int) -> dict:
     D, I, H, Dh = 768, 1152, 3, 256
-    if name in ("gate_up", "qkv", "o_proj", "down", "o_proj_norm", "down_norm"):
-        N, K = {"gate_up": (2 * I, D), "qkv": ((H + 2) * Dh, D), "o_proj": (D, D), "down": (D, I),
-                "o_proj_norm": (D, D), "down_norm": (D, I)}[name]
-        # the fused norm epilogue reads and writes the fp32 residual and writes int8 rows + scales
-        out_bytes = {"gate_up": 4 * M * I, "qkv": 2 * M * N, "o_proj": 4 * M * D, "down": 4 * M * D,
-                     "o_proj_norm": 8 * M * D + M * D + 4 * M, "down_norm": 8 * M * D + M * D + 4 * M}[name]
-        return {"bound": "tensor", "ops": 2.0 * M * N * K, "bytes": M * K + 4 * M + N * K + 4 * N + out_bytes,
-                "per_layer": 1}
+    if name in ("gate_up", "gate_up_q", "qkv", "o_proj", "down", "o_proj_norm", "down_norm"):
+        N, K = {"gate_up": (2 * I, D), "gate_up_q": (2 * I, D), "qkv": ((H + 2) * Dh, D), "o_proj": (D, D),
+                "down": (D, I), "o_proj_norm": (D, D), "down_norm": (D, I)}[name]
+        # the fused norm epilogue reads and writes the fp32 residual and writes int8 rows + scales;
+        # the fused GELU-quantise epilogue writes int8 h + scales
+        out_bytes = {"gate_up": 4 * M * I, "gate_up_q": M * I + 4 * M, "qkv": 2 * M * N, "o_proj": 4 * M * D,
+                     "down": 4 * M * D, "o_proj_norm": 8 * M * D + M * D + 4 * M,
+                     "down_norm": 8 * M * D + M * D + 4 * M}[name]
+        return {"ops": 2.0 * M * N * K, "bytes": M * K + 4 * M + N * K + 4 * N + out_bytes, "per_layer": 1}
     if name == "attention":
-        return {"bound": "tensor", "ops": 4.0 * M * SEQ * Dh * H, "bytes": M * (H + 2) * Dh * 2 + 4 * M * H * Dh,
-                "per_layer": 1}
+        return {"ops": 4.0 * M * SEQ * Dh * H, "bytes": M * (H + 2) * Dh * 2 + 4 * M * H * Dh, "per_layer": 1}
     if name in ("quantize", "quantize_ctx"):
         K = I if name == "quantize" else D
-        return {"bound": "hbm", "ops": 0.0, "bytes": M * (4 * K + K + 4), "per_layer": 1}
-    return {"bound": "hbm", "ops": 0.0, "bytes": M * (3 * 4 * D + D + 4), "per_layer": 2}  # norm_add
+        return {"ops": 0.0, "bytes": M * (4 * K + K + 4), "per_layer": 1}
+    return {"ops": 0.0, "bytes": M * (3 * 4 * D + D + 4), "per_layer": 2}  # norm_add
 
 
 def kernel_runner(name: str, M: int, dev, stream):
@@ -446,9 +449,9 @@ def kernel_runner(name: str, M: int, dev, stream):
         return e2c.quantize_rows(torch.randn((M, K), device=dev, generator=g), K)
 
     keep = []
-    if name in ("gate_up", "qkv", "o_proj", "down", "o_proj_norm", "down_norm"):
-        N, K = {"gate_up": (2 * I, D), "qkv": ((H + 2) * Dh, D), "o_proj": (D, D), "down": (D, I),
-                "o_proj_norm": (D, D), "down_norm": (D, I)}[name]
+    if name in ("gate_up", "gate_up_q", "qkv", "o_proj", "down", "o_proj_norm", "down_norm"):
+        N, K = {"gate_up": (2 * I, D), "gate_up_q": (2 * I, D), "qkv": ((H + 2) * Dh, D), "o_proj": (D, D),
+                "down": (D, I), "o_proj_norm": (D, D), "down_norm": (D, I)}[name]
         wq, ws = syn.quantize_weight_rows((rng.standard_normal((N, K)) * 0.02).astype(np.float32))
         W = e2c.Weight(w=wq, scale=ws)
         qa, qs = qin(K)
@@ -458,6 +461,11 @@ def kernel_runner(name: str, M: int, dev, stream):
             y = torch.empty((M, I), dtype=torch.float32, device=dev)
             a.epi, a.y, a.ldy = e2c.EPI_GELU, y.data_ptr(), I
             keep.append(y)
+        elif name == "gate_up_q":
+            q8 = torch.empty((M, I), dtype=torch.int8, device=dev)
+            q8s = torch.empty((M,), dtype=torch.float32, device=dev)
+            a.epi, a.q8, a.ldq, a.q8_scale = e2c.EPI_GELUQ, q8.data_ptr(), I, q8s.data_ptr()
+            keep += [q8, q8s]
         elif name in ("down", "o_proj"):
             y = torch.empty((M, D), dtype=torch.float32, device=dev)
             a.epi, a.y, a.ldy = e2c.EPI_F32, y.data_ptr(), D
@@ -529,12 +537,14 @@ def kernel_table(dev, stream, M: int = BATCH * SEQ, steps: int = 10) -> dict:
         ms = timed_launches(run, stream, 3, steps)
         e2c.check(stream)
         wk = kernel_work(name, M)
-        if wk["bound"] == "tensor":
-            peak = bf16_peak if name == "attention" else int8_peak
-            achieved, unit = wk["ops"] / (ms / 1e3) / 1e12, "TFLOP/s"
+        # the binding roofline: whichever of the tensor-core time and the HBM time at peak is longer
+        tpeak = bf16_peak if name == "attention" else int8_peak
+        bound = "tensor" if wk["ops"] / (tpeak * 1e12) >= wk["bytes"] / (hbm * 1e9) else "hbm"
+        if bound == "tensor":
+            peak, achieved, unit = tpeak, wk["ops"] / (ms / 1e3) / 1e12, "TFLOP/s"
         else:
             peak, achieved, unit = hbm, wk["bytes"] / (ms / 1e3) / 1e9, "GB/s"
-        table[name] = {"bound": wk["bound"], "achieved": achieved, "peak": peak, "unit": unit, "frac": achieved / peak,
+        table[name] = {"bound": bound, "achieved": achieved, "peak": peak, "unit": unit, "frac": achieved / peak,
                        "avg_ms": ms, "launches_per_layer": wk["per_layer"], "algorithmic_bytes": wk["bytes"],
                        "traffic": traffic.get(name)}
         del run, keep

@@ -82,7 +82,7 @@ class GemmArgs(C.Structure):
                 ("ldq", C.c_int), ("q8_scale", C.c_void_p), ("status", C.c_void_p)]
 
 
-EPI_F32, EPI_RESID, EPI_I32, EPI_GELU, EPI_QKV, EPI_NORMADD = 0, 1, 2, 3, 4, 5
+EPI_F32, EPI_RESID, EPI_I32, EPI_GELU, EPI_QKV, EPI_NORMADD, EPI_GELUQ = 0, 1, 2, 3, 4, 5, 6
 
 
 def gemm_args(w: "Weight", qa, a_scales, M: int) -> GemmArgs:

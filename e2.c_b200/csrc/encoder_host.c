@@ -12,8 +12,9 @@
  *   GEMM down + norm_add(post_ffn) + norm_split(next input_ln) + quant   (last layer: final norm)
  *
  * With per-token scales and a hidden size of 128 x (1..8) the residual norms run in the o_proj and
- * down GEMMs' epilogue (whole rows per cluster of CTAs; 7 kernels per layer); otherwise the GEMM
- * writes fp32 and a row kernel applies them (9 kernels per layer).
+ * down GEMMs' epilogue (whole rows per cluster of CTAs), and with an FFN width of 128 x (1..16) h's
+ * quantiser runs in the gate|up GEMM's epilogue (6 kernels per layer); otherwise the GEMMs write
+ * fp32 and row kernels follow (up to 9 kernels per layer).
  *
  * int8 activations alternate between two buffers: the layer's input (and the fused tails' output)
  * in qb, the quantised ctx and h in qa. A fused tail writes int8 rows of its output while other CTAs
@@ -50,7 +51,7 @@ struct e2cuda_encoder {
     float *out, *res, *tmp, *ctx, *h, *pooled, *h1;
     int8_t *qa, *qb, *pq;
     float *qs, *qsb, *ps;
-    int fused_norm;
+    int fused_norm, fused_gelu;
     void *Q, *K, *Vt;
     size_t vt_bytes;
     int *status;
@@ -263,6 +264,12 @@ e2cuda_encoder *e2cuda_encoder_create(const e2cuda_encoder_desc *d, int max_toke
     {
         const char *fz = getenv("E2C_FUSED_NORM");
         e->fused_norm = !(fz && fz[0] == '0') && e->ablk == D && D % 128 == 0 && D / 128 <= 8;
+        /* gate|up runs with GELU-gate and h's per-token quantiser in its epilogue (h never stored)
+         * where the device holds a cluster of I / 128 CTAs; E2C_FUSED_GELU=0 selects the GELU
+         * epilogue + quantiser kernel pair instead */
+        const char *fg = getenv("E2C_FUSED_GELU");
+        e->fused_gelu = !(fg && fg[0] == '0') && e->ablk == D && e->I % 128 == 0 && e->I / 128 <= 16 &&
+                        e2c_gemm_gelu_quant_supported(e->I / 128);
     }
     e->status = e2cu_status();
     if (!e->status || e2cu_cuda(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking), "stream")) goto fail;
@@ -343,18 +350,27 @@ static int encode(e2cuda_encoder *e, int B, int S, int has_valid, cudaStream_t s
             return -1;
         if (gemm_norms(e, &e->wo[l], M, ab_gd, nrm(e, l, 1), nrm(e, l, 2), NULL, &n, st, "encoder o_proj + norms")) return -1;
         e2cu_gemm_args(&a, &e->wgu[l], e->qb, e->qsb, M, ab_d);
-        a.epi = E2C_EPI_GELU;
-        a.y = e->h;
-        a.ldy = I;
-        if (e2cu_launch(e2c_gemm(&a, st), "encoder gate|up")) return -1;
-        if (e2cu_launch(e2c_quantize(e->h, I, e->qa, I, e->qs, M, I, ab_i, -INFINITY, INFINITY, 0, st),
-                        "encoder h quant"))
-            return -1;
+        if (e->fused_gelu) {
+            a.epi = E2C_EPI_GELUQ;
+            a.q8 = e->qa;
+            a.ldq = I;
+            a.q8_scale = e->qs;
+            if (e2cu_launch(e2c_gemm(&a, st), "encoder gate|up + h quant")) return -1;
+        } else {
+            a.epi = E2C_EPI_GELU;
+            a.y = e->h;
+            a.ldy = I;
+            if (e2cu_launch(e2c_gemm(&a, st), "encoder gate|up")) return -1;
+            if (e2cu_launch(e2c_quantize(e->h, I, e->qa, I, e->qs, M, I, ab_i, -INFINITY, INFINITY, 0, st),
+                            "encoder h quant"))
+                return -1;
+            n += 1;
+        }
         const int last = l + 1 == L;
         if (gemm_norms(e, &e->wd[l], M, ab_i, nrm(e, l, 3), last ? NULL : nrm(e, l + 1, 0), last ? final_norm(e) : NULL,
                        &n, st, "encoder down + norms"))
             return -1;
-        n += 5;
+        n += 4;
     }
     /* head */
     const int ab_dh = e->ablk == D ? e->DH : 128;

@@ -1,0 +1,36 @@
+// epi_math.cuh — element functions shared by the GEMM epilogues (one definition, so fused and
+// unfused paths give the same bits).
+#pragma once
+#include <stdint.h>
+
+// GELU-tanh, the reference's function (src/kernels_avx512.c:46-55,186-203):
+//   0.5 v (1 + tanh(c (v + 0.044715 v^3))),  c = sqrt(2/pi).
+// Evaluated through the identity 0.5 (1 + tanh z) = 1 / (1 + exp(-2z)):
+//   gelu(v) = v / (1 + 2^(k v (1 + 0.044715 v^2))),  k = -2 c log2(e),
+// with the SFU's ex2.approx (<= 2 ulp) and rcp.approx (<= 1 ulp): about 8 instructions, no range
+// clamps (ex2 saturates to 0 or +inf, and v / inf = -0 matches tanh = -1 exactly), and no
+// cancellation in 1 + tanh for negative v. Within ~1e-7 relative of the reference, whose own
+// -ffast-math build divides with rcp14 plus a Newton step.
+__device__ __forceinline__ float ex2_fast(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+__device__ __forceinline__ float rcp_fast(float x) {
+    float y;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+__device__ __forceinline__ float gelu_tanh(float v) {
+    const float t = __fmaf_rn(0.044715f, __fmul_rn(v, v), 1.0f);
+    const float e = ex2_fast(__fmul_rn(__fmul_rn(-2.302208198144325f, v), t));
+    return __fmul_rn(v, rcp_fast(__fadd_rn(1.0f, e)));
+}
+
+// the per-token quantiser's byte: rint(v) for |v| < 2^22 as the low byte of v + 1.5 2^23 (the
+// addition rounds to nearest even at integer spacing), equal to __float2int_rn(v) there
+__device__ __forceinline__ uint32_t rint_low_byte(float v) { return __float_as_uint(__fadd_rn(v, 12582912.0f)); }
+// four such words -> four int8 bytes in memory order
+__device__ __forceinline__ uint32_t pack_low_bytes(uint32_t b0, uint32_t b1, uint32_t b2, uint32_t b3) {
+    return __byte_perm(__byte_perm(b0, b1, 0x0040), __byte_perm(b2, b3, 0x0040), 0x5410);
+}

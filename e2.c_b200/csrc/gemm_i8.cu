@@ -30,6 +30,7 @@
 #include <stdio.h>
 
 #include "launch.h"
+#include "epi_math.cuh"
 #include "ptx.cuh"
 #include "tmap.h"
 
@@ -65,30 +66,6 @@ struct GemmSmem {
 };
 
 // ---------------------------------------------------------------------------------- epilogue math
-// GELU-tanh, the reference's function (src/kernels_avx512.c:46-55,186-203):
-//   0.5 v (1 + tanh(c (v + 0.044715 v^3))),  c = sqrt(2/pi).
-// Evaluated through the identity 0.5 (1 + tanh z) = 1 / (1 + exp(-2z)):
-//   gelu(v) = v / (1 + 2^(k v (1 + 0.044715 v^2))),  k = -2 c log2(e),
-// with the SFU's ex2.approx (<= 2 ulp) and rcp.approx (<= 1 ulp): about 8 instructions, no range
-// clamps (ex2 saturates to 0 or +inf, and v / inf = -0 matches tanh = -1 exactly), and no
-// cancellation in 1 + tanh for negative v. Within ~1e-7 relative of the reference, whose own
-// -ffast-math build divides with rcp14 plus a Newton step.
-__device__ __forceinline__ float ex2_fast(float x) {
-    float y;
-    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-    return y;
-}
-__device__ __forceinline__ float rcp_fast(float x) {
-    float y;
-    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-    return y;
-}
-__device__ __forceinline__ float gelu_tanh(float v) {
-    const float t = __fmaf_rn(0.044715f, __fmul_rn(v, v), 1.0f);
-    const float e = ex2_fast(__fmul_rn(__fmul_rn(-2.302208198144325f, v), t));
-    return __fmul_rn(v, rcp_fast(__fadd_rn(1.0f, e)));
-}
-
 __device__ __forceinline__ float dq(uint32_t acc, float s) { return __fmul_rn(__int2float_rn((int)acc), s); }
 
 // Staging tiles are 32 rows x 64 bytes in the TMA 64-byte-swizzle layout (512-byte aligned): the
@@ -888,6 +865,17 @@ extern "C" int e2c_gemm(const e2c_gemm_args *a, void *stream) {
             return -1;
         }
         return e2c_gemm_norm(a, stream);
+    }
+    case E2C_EPI_GELUQ: {
+        // GELU-gate and the per-token quantiser of h in the epilogue: its own kernel (gemm_i8_gelu.cu)
+        const int ncols = a->n1 - a->n0;
+        if (perblock || a->n0 != 0 || ncols % 256 || ncols / 256 > 16 || !a->q8 || !a->q8_scale || a->ldq % 16 ||
+            ((uintptr_t)a->q8 & 15)) {
+            e2c_set_msg("gemm: the GELU-quantise epilogue needs per-row scales, gate|up rows in groups of 256 "
+                        "(1..16) from row 0 and 16-byte aligned int8 rows with their scales");
+            return -1;
+        }
+        return e2c_gemm_gelu_quant(a, stream);
     }
     default:
         e2c_set_msg("gemm: unknown epilogue %d", a->epi);

@@ -38,7 +38,10 @@ enum {
     E2C_EPI_QKV = 4,   /* per-head RMSNorm (+gamma) + RoPE -> bf16 Q, K, V^T               */
     E2C_EPI_NORMADD = 5 /* y = gemm (never stored); x = rmsnorm(y) * g1 + res; res = x;
                           q = quantise(rmsnorm(x) * g2) per token (g2 NULL: res = rmsnorm(x) * gf).
-                          Whole rows per cluster of CTAs (N = 768: 6 x 128 columns) */
+                          Whole rows per cluster of CTAs (N = 768: 6 x 128 columns) */,
+    E2C_EPI_GELUQ = 6  /* GELU-gate as E2C_EPI_GELU, then the per-token quantiser of h over its
+                          N/2 columns: int8 q8 [M][ldq] and q8_scale [M] (h itself is not stored).
+                          Whole rows per cluster of N/256 CTAs (N = 2304: 9) */
 };
 
 typedef struct {
@@ -88,6 +91,10 @@ int e2c_gemm_splitk(const e2c_gemm_args *a, int bn, int S, void *stream);
 /* E2C_EPI_NORMADD (gemm_i8_norm.cu): rows of 128 x (1..8) columns over a cluster of CTAs, the
  * residual norms in the epilogue; called by e2c_gemm after its checks */
 int e2c_gemm_norm(const e2c_gemm_args *a, void *stream);
+/* E2C_EPI_GELUQ (gemm_i8_gelu.cu), called by e2c_gemm after its checks; _supported(ncl) is 1 when
+ * the device holds clusters of ncl such CTAs */
+int e2c_gemm_gelu_quant(const e2c_gemm_args *a, void *stream);
+int e2c_gemm_gelu_quant_supported(int ncl);
 /* the split that puts most CTAs to work with every cluster resident at once: returns the CTA count
  * (0 when the split kernel does not apply) and sets *bn, *S */
 int e2c_gemm_splitk_plan(const e2c_gemm_args *a, int num_sms, int *bn, int *S);

@@ -72,9 +72,14 @@ def test_encoder_matches_cpu_reference(e2c, of, syn, torch_cuda):
     assert cos.min() >= 0.9999, cos
     assert np.allclose(np.linalg.norm(got[:3], axis=1), 1.0, atol=1e-5)
     calls, kernels, _ = enc.stats()
-    # 7 kernels per layer with the residual norms fused into o_proj / down (hidden 128 x 1..8,
-    # per-token scales), else 9; plus the embed pass and the 6 head kernels
-    per_layer = 7 if (w.cfg.hidden % 128 == 0 and w.cfg.hidden // 128 <= 8) else 9
+    # 9 kernels per layer; 2 fewer with the residual norms fused into o_proj / down (hidden 128 x 1..8,
+    # per-token scales), 1 fewer with h's quantiser fused into gate|up (ffn 128 x 1..16, a device
+    # that holds the cluster); plus the embed pass and the 6 head kernels
+    per_layer = 9
+    if w.cfg.hidden % 128 == 0 and w.cfg.hidden // 128 <= 8:
+        per_layer -= 2
+    if w.cfg.ffn % 128 == 0 and w.cfg.ffn // 128 <= 16 and e2c.lib().e2c_gemm_gelu_quant_supported(w.cfg.ffn // 128):
+        per_layer -= 1
     assert calls == 1 and kernels == 1 + per_layer * w.cfg.n_layers + 6
 
 

@@ -257,6 +257,46 @@ def test_gelu_gate_epilogue(e2c, of, torch_cuda, M):
     tie_tolerant_bytes(gq, wq, want * (np.float32(127.0) / np.abs(want).max(axis=1, keepdims=True)))
 
 
+def _gate_up_weight(e2c, rng, M, D, I):
+    """Inputs and the interleaved gate|up weight (groups of 128 gate rows, then 128 up rows)."""
+    qa, a_s, wg, sg = _gemm_inputs(rng, M, I, D, D)
+    _, _, wu, su = _gemm_inputs(rng, M, I, D, D)
+    wi = np.empty((2 * I, D), np.int8)
+    si = np.empty(2 * I, np.float32)
+    for t in range(I // 128):
+        wi[256 * t:256 * t + 128], si[256 * t:256 * t + 128] = wg[128 * t:128 * t + 128], sg[128 * t:128 * t + 128]
+        wi[256 * t + 128:256 * t + 256], si[256 * t + 128:256 * t + 256] = wu[128 * t:128 * t + 128], su[128 * t:128 * t + 128]
+    return qa, a_s, e2c.Weight(w=wi, scale=si)
+
+
+@pytest.mark.parametrize("M,I", [(300, 1152), (16384, 1152), (1000, 128), (517, 2048), (129, 1024)])
+def test_gelu_quant_epilogue(e2c, of, torch_cuda, M, I):
+    """gate|up GEMM with GELU-gate and the per-token quantiser of h in the epilogue (h never stored):
+    the int8 rows and scales are bit-identical to the GELU epilogue followed by the quantiser kernel
+    (both already checked against the reference above). Rows span a cluster of I / 128 CTAs (1 to 16,
+    9 for the encoder's I = 1152); 16384 rows give every CTA several row blocks."""
+    torch = torch_cuda
+    rng = np.random.default_rng(91 + M + I)
+    D = 768
+    qa, a_s, W = _gate_up_weight(e2c, rng, M, D, I)
+    qd, sd = dev(torch, qa), dev(torch, a_s)
+    lib = e2c.lib()
+    if not lib.e2c_gemm_gelu_quant_supported(I // 128):
+        pytest.skip(f"the device holds no cluster of {I // 128} CTAs")
+    h = torch.zeros((M, I), dtype=torch.float32, device="cuda")
+    a = _args_for(W, qd, sd, M, D)
+    a.epi, a.y, a.ldy = e2c.EPI_GELU, h.data_ptr(), I
+    _launch(e2c, a, torch)
+    want_q, want_s = e2c.quantize_rows(h, I)
+    q = torch.full((M, I), 99, dtype=torch.int8, device="cuda")
+    s = torch.zeros((M,), dtype=torch.float32, device="cuda")
+    a = _args_for(W, qd, sd, M, D)
+    a.epi, a.q8, a.ldq, a.q8_scale = e2c.EPI_GELUQ, q.data_ptr(), I, s.data_ptr()
+    _launch(e2c, a, torch)
+    assert np.array_equal(q.cpu().numpy(), want_q.cpu().numpy())
+    assert f32_bits_equal(s.cpu().numpy(), want_s.cpu().numpy()[:, 0])
+
+
 @pytest.mark.parametrize("B,S", [(2, 200), (16, 240)])  # 16 x 240 rows: CTA pairs
 def test_qkv_epilogue_norm_rope(e2c, of, torch_cuda, B, S):
     """q|k|v GEMM with per-head RMSNorm (+gamma) and RoPE in the epilogue (e2.c src/text.c:836-854),
