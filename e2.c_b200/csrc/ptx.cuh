@@ -62,20 +62,36 @@ E2C_DEV bool mbar_try_wait(uint32_t bar, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
+// The same, but the thread may sleep in the instruction until the phase completes or `ns`
+// nanoseconds have passed: a waiting warp issues nothing meanwhile, so the warps that are working
+// keep the issue slots.
+E2C_DEV bool mbar_try_wait_sleep(uint32_t bar, uint32_t parity, uint32_t ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity), "r"(ns)
+        : "memory");
+    return ok != 0;
+}
+// Longest sleep of one wait step; the failure checks below run between steps.
+#ifndef E2C_WAIT_STEP_NS
+#define E2C_WAIT_STEP_NS 100000u
+#endif
 // Wait until the phase with parity `parity` has completed. Bounded: returns false (and records
 // `code`) after E2C_WAIT_NS, or at once if another role of this kernel already failed.
 E2C_DEV bool mbar_wait(uint32_t bar, uint32_t parity, int *status, int code) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer();
-    for (uint32_t it = 0;; ++it) {
-        if (mbar_try_wait(bar, parity)) return true;
-        if ((it & 63) == 63) {
-            if (globaltimer() - t0 > E2C_WAIT_NS) {
-                record_status(status, code);
-                return false;
-            }
-            if (status && *(volatile int *)status != 0) return false;
+    for (;;) {
+        if (mbar_try_wait_sleep(bar, parity, E2C_WAIT_STEP_NS)) return true;
+        if (globaltimer() - t0 > E2C_WAIT_NS) {
+            record_status(status, code);
+            return false;
         }
+        if (status && *(volatile int *)status != 0) return false;
     }
 }
 
@@ -223,15 +239,21 @@ E2C_DEV bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
 E2C_DEV bool mbar_wait_cluster(uint32_t bar, uint32_t parity, int *status, int code) {
     if (mbar_try_wait_cluster(bar, parity)) return true;
     const uint64_t t0 = globaltimer();
-    for (uint32_t it = 0;; ++it) {
-        if (mbar_try_wait_cluster(bar, parity)) return true;
-        if ((it & 63) == 63) {
-            if (globaltimer() - t0 > E2C_WAIT_NS) {
-                record_status(status, code);
-                return false;
-            }
-            if (status && *(volatile int *)status != 0) return false;
+    for (;;) {
+        uint32_t ok;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(ok)
+            : "r"(bar), "r"(parity), "r"(E2C_WAIT_STEP_NS)
+            : "memory");
+        if (ok) return true;
+        if (globaltimer() - t0 > E2C_WAIT_NS) {
+            record_status(status, code);
+            return false;
         }
+        if (status && *(volatile int *)status != 0) return false;
     }
 }
 // Asynchronous stores into another CTA's shared memory whose bytes complete on an mbarrier of that
