@@ -115,6 +115,42 @@ __global__ void __launch_bounds__(256) k_quant_wide(const float *__restrict__ x,
     }
 }
 
+// Per-token mode, K = 128 NV: lane l holds the float4s l, l + 32, ... of a row (every lane busy, one
+// coalesced 4-byte store per float4), and each warp walks rows with the next row's loads in flight
+// while it quantises the current one. Bit-identical to k_quant_wide (the maximum does not depend on
+// the order it is taken in; each element's arithmetic is the same).
+template <int NV>
+__global__ void __launch_bounds__(256) k_quant_rows(const float *__restrict__ x, int ldx, int8_t *__restrict__ q, int ldq,
+                                                    float *__restrict__ scales, int M, uint32_t bias) {
+    const int lane = threadIdx.x & 31;
+    const int nw = (int)((gridDim.x * blockDim.x) >> 5);
+    int r = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
+    float4 v[NV], nx[NV];
+    auto load = [&](int row, float4 (&d)[NV]) {
+        const float4 *src = reinterpret_cast<const float4 *>(x + (size_t)row * ldx);
+#pragma unroll
+        for (int i = 0; i < NV; i++) d[i] = __ldcs(src + lane + 32 * i);
+    };
+    if (r < M) load(r, v);
+    for (; r < M; r += nw) {
+        if (r + nw < M) load(r + nw, nx);
+        float amax = 0.f;
+#pragma unroll
+        for (int i = 0; i < NV; i++)
+            amax = fmaxf(fmaxf(fmaxf(amax, fabsf(v[i].x)), fmaxf(fabsf(v[i].y), fabsf(v[i].z))), fabsf(v[i].w));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        const float inv = amax > 0.f ? __fdiv_rn(127.0f, amax) : 1.0f;
+        uint32_t *dst = reinterpret_cast<uint32_t *>(q + (size_t)r * ldq);
+#pragma unroll
+        for (int i = 0; i < NV; i++)
+            dst[lane + 32 * i] = pack4(qround(v[i].x, inv), qround(v[i].y, inv), qround(v[i].z, inv), qround(v[i].w, inv), bias);
+        if (lane == 0) scales[r] = amax > 0.f ? __fmul_rn(amax, kInv127) : 1.0f;
+#pragma unroll
+        for (int i = 0; i < NV; i++) v[i] = nx[i];
+    }
+}
+
 __global__ void k_flip_bias(uint32_t *q, size_t n4) {
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x)
         q[i] ^= 0x80808080u;
@@ -155,7 +191,36 @@ extern "C" int e2c_quantize(const float *x, int ldx, int8_t *q, int ldq, float *
     cudaStream_t st = (cudaStream_t)stream;
     const dim3 block(256), grid((unsigned)((M + 7) / 8));
     const int g = ablk / 16;
-    if (ablk <= 512 && (g & (g - 1)) == 0) {
+    if (ablk == K && K % 128 == 0 && K / 128 <= 9 && !clamp) {
+        // per-token rows of 128 NV: persistent warps, as many CTAs as the SMs hold at once
+        static int sms = 0, resident[10] = { 0 };
+        if (!sms && (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, 0) != cudaSuccess || sms <= 0)) sms = 148;
+        const int nv = K / 128;
+        if (!resident[nv]) {
+            const void *fn = nv == 1 ? (const void *)k_quant_rows<1> : nv == 2 ? (const void *)k_quant_rows<2>
+                           : nv == 3 ? (const void *)k_quant_rows<3> : nv == 4 ? (const void *)k_quant_rows<4>
+                           : nv == 5 ? (const void *)k_quant_rows<5> : nv == 6 ? (const void *)k_quant_rows<6>
+                           : nv == 7 ? (const void *)k_quant_rows<7> : nv == 8 ? (const void *)k_quant_rows<8>
+                                     : (const void *)k_quant_rows<9>;
+            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&resident[nv], fn, 256, 0) != cudaSuccess || resident[nv] <= 0)
+                resident[nv] = 1;
+        }
+        const long cap = (long)resident[nv] * sms;
+        const unsigned rg = (unsigned)((M + 7) / 8 < cap ? (M + 7) / 8 : cap);
+#define E2C_QR(NV) k_quant_rows<NV><<<rg, block, 0, st>>>(x, ldx, q, ldq, scales, M, bias)
+        switch (K / 128) {
+        case 1: E2C_QR(1); break;
+        case 2: E2C_QR(2); break;
+        case 3: E2C_QR(3); break;
+        case 4: E2C_QR(4); break;
+        case 5: E2C_QR(5); break;
+        case 6: E2C_QR(6); break;
+        case 7: E2C_QR(7); break;
+        case 8: E2C_QR(8); break;
+        default: E2C_QR(9); break;
+        }
+#undef E2C_QR
+    } else if (ablk <= 512 && (g & (g - 1)) == 0) {
         switch (g) {
         case 1: k_quant_small<1><<<grid, block, 0, st>>>(x, ldx, q, ldq, scales, M, K, lo, hi, clamp, bias); break;
         case 2: k_quant_small<2><<<grid, block, 0, st>>>(x, ldx, q, ldq, scales, M, K, lo, hi, clamp, bias); break;

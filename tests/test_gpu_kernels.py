@@ -27,6 +27,7 @@ def f32_bits_equal(a: np.ndarray, b: np.ndarray) -> bool:
 
 # ------------------------------------------------------------------------------------------ A1 quantiser
 QUANT_CASES = [(1, 768, 768), (7, 768, 768), (512, 768, 768), (333, 1152, 1152), (5, 8192, 8192), (17, 2048, 2048),
+               (40000, 768, 768), (3001, 1152, 1152), (2500, 1024, 1024), (777, 128, 128),
                (9, 208, 208), (3, 3072, 3072), (64, 768, 128), (31, 1152, 128), (8, 512, 32), (8, 512, 64),
                (8, 1024, 256), (8, 1024, 512), (0, 768, 768)]
 
