@@ -34,6 +34,7 @@
 #include <stdint.h>
 
 #include "launch.h"
+#include "pdl.h"
 #include "ptx.cuh"
 #include "tmap.h"
 
@@ -111,7 +112,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     k_attention(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                 const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO, const AttnArgs p) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
+    griddep_launch_dependents();
     if (smem_u32(smem_raw) & 1023) {  // never expected; refuse rather than misplace the swizzled tiles
+        griddep_wait();
         if (threadIdx.x == 0) record_status(p.status, E2C_ERR_SMEM_ALIGN);
         return;
     }
@@ -153,6 +156,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
+    griddep_wait();  // the previous kernel's Q, K, V (and its reads of ctx) are done
     const uint32_t tmem = *tmem_slot;  // S buffer i: cols 64 i .. +63 (i < 4), O: 256..511
 
     if (warp == 0) {
@@ -505,7 +509,7 @@ extern "C" int e2c_attention(const void *q, const void *k, const void *vt, int l
     a.scale_log2 = scale * 1.4426950408889634f;
     a.status = status;
     const int grid = a.units < g_attn_sms ? a.units : g_attn_sms;
-    k_attention<<<grid, NTHREADS, SMEM_ALLOC, (cudaStream_t)stream>>>(tq, tk, tv, to, a);
+    e2c_launch(k_attention, dim3(grid), dim3(NTHREADS), SMEM_ALLOC, (cudaStream_t)stream, tq, tk, tv, to, a);
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
         e2c_set_msg("attention launch: %s", cudaGetErrorString(e));

@@ -31,6 +31,7 @@
 
 #include "launch.h"
 #include "epi_math.cuh"
+#include "pdl.h"
 #include "ptx.cuh"
 #include "tmap.h"
 
@@ -108,6 +109,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
               const int tma_out) {
     using L = GemmSmem<BN, STAGES, PERBLOCK, EPI, CG>;
     extern __shared__ uint8_t smem_raw[];
+    griddep_launch_dependents();
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     const uint32_t sbase = smem_u32(smem);
     const uint32_t bar0 = sbase + L::BAR_OFF;
@@ -162,6 +164,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     if constexpr (CG == 2) cluster_sync();
     else __syncthreads();
     tc_fence_after();
+    griddep_wait();  // the stream's earlier kernels are done with what this one reads and writes
     const uint32_t tmem_base = *tmem_slot;
     // the accumulator is free again: one arrival per warp on the leader's barrier
     auto release_acc = [&](int a) {
@@ -700,12 +703,11 @@ int launch(const e2c_gemm_args *a, cudaStream_t st) {
     cudaError_t e;
     if constexpr (CG == 1) {
         const int grid = tiles < g_num_sms ? tiles : g_num_sms;
-        kern<<<grid, NTHREADS, L::ALLOC, st>>>(ta, tb, t0, t1, *a, tma_out);
-        e = cudaGetLastError();
+        e = e2c_launch(kern, dim3(grid), dim3(NTHREADS), L::ALLOC, st, ta, tb, t0, t1, *a, tma_out);
     } else {
         cudaLaunchConfig_t cfg;
         memset(&cfg, 0, sizeof cfg);
-        cudaLaunchAttribute attr[1];
+        cudaLaunchAttribute attr[2];
         attr[0].id = cudaLaunchAttributeClusterDimension;
         attr[0].val.clusterDim.x = 2;
         attr[0].val.clusterDim.y = 1;
@@ -725,6 +727,7 @@ int launch(const e2c_gemm_args *a, cudaStream_t st) {
             }
         }
         cfg.gridDim = dim3(2 * (tiles < max_pairs ? tiles : max_pairs));
+        cfg.numAttrs = e2c_pdl_attr(attr, 1);
         e = cudaLaunchKernelEx(&cfg, kern, ta, tb, t0, t1, *a, tma_out);
     }
     if (e != cudaSuccess) {

@@ -29,6 +29,7 @@
 
 #include "epi_math.cuh"
 #include "launch.h"
+#include "pdl.h"
 #include "ptx.cuh"
 #include "tmap.h"
 
@@ -67,6 +68,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                       const __grid_constant__ CUtensorMap tmQ, const e2c_gemm_args p) {
     using L = Smem;
     extern __shared__ uint8_t smem_raw[];
+    griddep_launch_dependents();
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     const uint32_t sbase = smem_u32(smem);
     const uint32_t bar0 = sbase + L::BAR_OFF;
@@ -113,6 +115,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     tc_fence_before();
     cluster_sync();
     tc_fence_after();
+    griddep_wait();  // the stream's earlier kernels are done with what this one reads and writes
     const uint32_t tmem_base = *tmem_slot;
 
     if (warp == 0) {
@@ -389,7 +392,7 @@ extern "C" int e2c_gemm_gelu_quant(const e2c_gemm_args *a, void *stream) {
         return -1;
     }
     cudaLaunchConfig_t cfg;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     const int rc = prepare(ncl, &cfg, attr, (cudaStream_t)stream);
     if (rc) return rc;
     CUtensorMap ta, tb, tq;
@@ -401,6 +404,7 @@ extern "C" int e2c_gemm_gelu_quant(const e2c_gemm_args *a, void *stream) {
     const int tiles_m = (a->M + BM - 1) / BM;
     const int maxc = g_max_clusters[ncl];
     cfg.gridDim = dim3((unsigned)(ncl * (tiles_m < maxc ? tiles_m : maxc)));
+    cfg.numAttrs = e2c_pdl_attr(attr, 1);
     const cudaError_t e = cudaLaunchKernelEx(&cfg, k_gemm_gelu_quant, ta, tb, tq, *a);
     if (e != cudaSuccess) {
         e2c_set_msg("gemm_gelu_quant launch: %s", cudaGetErrorString(e));

@@ -39,6 +39,7 @@
 #include <string.h>
 
 #include "launch.h"
+#include "pdl.h"
 #include "ptx.cuh"
 #include "tmap.h"
 
@@ -83,6 +84,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 const e2c_gemm_args p) {
     using L = Smem;
     extern __shared__ uint8_t smem_raw[];
+    griddep_launch_dependents();
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     const uint32_t sbase = smem_u32(smem);
     const uint32_t bar0 = sbase + L::BAR_OFF;
@@ -132,6 +134,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     tc_fence_before();
     cluster_sync();  // every CTA's barriers exist before another CTA signals them
     tc_fence_after();
+    griddep_wait();  // the stream's earlier kernels are done with what this one reads and writes
     const uint32_t tmem_base = *tmem_slot;
 
     if (warp == 0) {
@@ -542,7 +545,7 @@ extern "C" int e2c_gemm_norm(const e2c_gemm_args *a, void *stream) {
     const int tiles_m = (a->M + BM - 1) / BM;
     cudaLaunchConfig_t cfg;
     memset(&cfg, 0, sizeof cfg);
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = (unsigned)ncl;
     attr[0].val.clusterDim.y = 1;
@@ -565,6 +568,7 @@ extern "C" int e2c_gemm_norm(const e2c_gemm_args *a, void *stream) {
         }
     }
     cfg.gridDim = dim3((unsigned)(ncl * (tiles_m < maxc ? tiles_m : maxc)));
+    cfg.numAttrs = e2c_pdl_attr(attr, 1);
     const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, tb, tr, tq, *a);
     if (e != cudaSuccess) {
         e2c_set_msg("gemm_norm launch: %s", cudaGetErrorString(e));

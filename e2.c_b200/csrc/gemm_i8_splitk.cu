@@ -23,6 +23,7 @@
 #include <string.h>
 
 #include "launch.h"
+#include "pdl.h"
 #include "ptx.cuh"
 #include "tmap.h"
 
@@ -71,6 +72,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                   const e2c_gemm_args p, const int a_rows) {
     static_assert(BM * BN * 4 <= POOL, "partials fit in the pool");
     extern __shared__ uint8_t smem_raw[];
+    griddep_launch_dependents();
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     const uint32_t sbase = smem_u32(smem);
     const uint32_t bar0 = sbase + BAR_OFF;
@@ -111,6 +113,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
+    griddep_wait();  // the stream's earlier kernels are done with what this one reads and writes
     const uint32_t tmem = *tmem_slot;
     bool ok = true;
 
@@ -286,7 +289,7 @@ int launch_bn(const e2c_gemm_args *a, int S, cudaStream_t st) {
     const int tiles = ((a->M + BM - 1) / BM) * ((a->n1 - a->n0 + BN - 1) / BN);
     cudaLaunchConfig_t cfg;
     memset(&cfg, 0, sizeof cfg);
-    cudaLaunchAttribute attr_c[1];
+    cudaLaunchAttribute attr_c[2];
     attr_c[0].id = cudaLaunchAttributeClusterDimension;
     attr_c[0].val.clusterDim.x = (unsigned)S;
     attr_c[0].val.clusterDim.y = 1;
@@ -296,7 +299,7 @@ int launch_bn(const e2c_gemm_args *a, int S, cudaStream_t st) {
     cfg.dynamicSmemBytes = SMEM_ALLOC;
     cfg.stream = st;
     cfg.attrs = attr_c;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = e2c_pdl_attr(attr_c, 1);
     const cudaError_t e = cudaLaunchKernelEx(&cfg, k_gemm_splitk<BN>, ta, tb, *a, a_rows);
     if (e != cudaSuccess) {
         e2c_set_msg("gemm_splitk launch: %s", cudaGetErrorString(e));

@@ -33,6 +33,15 @@ E2C_DEV uint64_t globaltimer() {
     return t;
 }
 
+// Programmatic dependent launch. A kernel launched with the programmatic-serialization attribute
+// may start while the previous kernel of its stream is still running: it must pass griddep_wait(),
+// which returns once that kernel (and so every earlier one) has finished and its writes are
+// visible, before it reads or writes global memory the stream's earlier kernels touch. For a kernel
+// launched without the attribute both calls do nothing. griddep_launch_dependents() lets the next
+// kernel of the stream be scheduled as soon as SMs free up.
+E2C_DEV void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+E2C_DEV void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 E2C_DEV void record_status(int *status, int code) {
     if (status) atomicCAS(status, 0, code);
 }

@@ -9,6 +9,7 @@
 #include <stdint.h>
 
 #include "launch.h"
+#include "pdl.h"
 #include "ptx.cuh"
 
 namespace {
@@ -60,6 +61,8 @@ template <int G>
 __global__ void __launch_bounds__(256) k_quant_small(const float *__restrict__ x, int ldx, int8_t *__restrict__ q,
                                                      int ldq, float *__restrict__ scales, int M, int K,
                                                      float lo, float hi, int clamp, uint32_t bias) {
+    griddep_launch_dependents();
+    griddep_wait();
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (warp >= M) return;
     const float *xr = x + (size_t)warp * ldx;
@@ -89,6 +92,8 @@ template <int REG, bool CLAMP>
 __global__ void __launch_bounds__(256) k_quant_wide(const float *__restrict__ x, int ldx, int8_t *__restrict__ q,
                                                     int ldq, float *__restrict__ scales, int M, int K, int ablk,
                                                     float lo, float hi, uint32_t bias) {
+    griddep_launch_dependents();
+    griddep_wait();
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (warp >= M) return;
     const float *xr = x + (size_t)warp * ldx;
@@ -122,6 +127,8 @@ __global__ void __launch_bounds__(256) k_quant_wide(const float *__restrict__ x,
 template <int NV>
 __global__ void __launch_bounds__(256) k_quant_rows(const float *__restrict__ x, int ldx, int8_t *__restrict__ q, int ldq,
                                                     float *__restrict__ scales, int M, uint32_t bias) {
+    griddep_launch_dependents();
+    griddep_wait();
     const int lane = threadIdx.x & 31;
     const int nw = (int)((gridDim.x * blockDim.x) >> 5);
     int r = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
@@ -152,6 +159,8 @@ __global__ void __launch_bounds__(256) k_quant_rows(const float *__restrict__ x,
 }
 
 __global__ void k_flip_bias(uint32_t *q, size_t n4) {
+    griddep_launch_dependents();
+    griddep_wait();
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x)
         q[i] ^= 0x80808080u;
 }
@@ -166,7 +175,7 @@ extern "C" int e2c_flip_bias(int8_t *q, size_t n, void *stream) {
     if (!n) return 0;
     const size_t n4 = n / 4;
     const unsigned grid = (unsigned)((n4 + 255) / 256 < 4096 ? (n4 + 255) / 256 : 4096);
-    k_flip_bias<<<grid, 256, 0, (cudaStream_t)stream>>>(reinterpret_cast<uint32_t *>(q), n4);
+    e2c_launch(k_flip_bias, dim3(grid), dim3(256), 0, (cudaStream_t)stream, reinterpret_cast<uint32_t *>(q), n4);
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
         e2c_set_msg("flip_bias launch: %s", cudaGetErrorString(e));
@@ -207,7 +216,7 @@ extern "C" int e2c_quantize(const float *x, int ldx, int8_t *q, int ldq, float *
         }
         const long cap = (long)resident[nv] * sms;
         const unsigned rg = (unsigned)((M + 7) / 8 < cap ? (M + 7) / 8 : cap);
-#define E2C_QR(NV) k_quant_rows<NV><<<rg, block, 0, st>>>(x, ldx, q, ldq, scales, M, bias)
+#define E2C_QR(NV) e2c_launch(k_quant_rows<NV>, dim3(rg), block, 0, st, x, ldx, q, ldq, scales, M, bias)
         switch (K / 128) {
         case 1: E2C_QR(1); break;
         case 2: E2C_QR(2); break;
@@ -222,12 +231,12 @@ extern "C" int e2c_quantize(const float *x, int ldx, int8_t *q, int ldq, float *
 #undef E2C_QR
     } else if (ablk <= 512 && (g & (g - 1)) == 0) {
         switch (g) {
-        case 1: k_quant_small<1><<<grid, block, 0, st>>>(x, ldx, q, ldq, scales, M, K, lo, hi, clamp, bias); break;
-        case 2: k_quant_small<2><<<grid, block, 0, st>>>(x, ldx, q, ldq, scales, M, K, lo, hi, clamp, bias); break;
-        case 4: k_quant_small<4><<<grid, block, 0, st>>>(x, ldx, q, ldq, scales, M, K, lo, hi, clamp, bias); break;
-        case 8: k_quant_small<8><<<grid, block, 0, st>>>(x, ldx, q, ldq, scales, M, K, lo, hi, clamp, bias); break;
-        case 16: k_quant_small<16><<<grid, block, 0, st>>>(x, ldx, q, ldq, scales, M, K, lo, hi, clamp, bias); break;
-        default: k_quant_small<32><<<grid, block, 0, st>>>(x, ldx, q, ldq, scales, M, K, lo, hi, clamp, bias); break;
+        case 1: e2c_launch(k_quant_small<1>, grid, block, 0, st, x, ldx, q, ldq, scales, M, K, lo, hi, clamp, bias); break;
+        case 2: e2c_launch(k_quant_small<2>, grid, block, 0, st, x, ldx, q, ldq, scales, M, K, lo, hi, clamp, bias); break;
+        case 4: e2c_launch(k_quant_small<4>, grid, block, 0, st, x, ldx, q, ldq, scales, M, K, lo, hi, clamp, bias); break;
+        case 8: e2c_launch(k_quant_small<8>, grid, block, 0, st, x, ldx, q, ldq, scales, M, K, lo, hi, clamp, bias); break;
+        case 16: e2c_launch(k_quant_small<16>, grid, block, 0, st, x, ldx, q, ldq, scales, M, K, lo, hi, clamp, bias); break;
+        default: e2c_launch(k_quant_small<32>, grid, block, 0, st, x, ldx, q, ldq, scales, M, K, lo, hi, clamp, bias); break;
         }
     } else {
         const int reg = (ablk / 16 + 31) / 32;  // groups of 16 per lane
@@ -236,8 +245,8 @@ extern "C" int e2c_quantize(const float *x, int ldx, int8_t *q, int ldq, float *
             return -1;
         }
 #define E2C_QW(R)                                                                                            \
-    (clamp ? k_quant_wide<R, true><<<grid, block, 0, st>>>(x, ldx, q, ldq, scales, M, K, ablk, lo, hi, bias)   \
-           : k_quant_wide<R, false><<<grid, block, 0, st>>>(x, ldx, q, ldq, scales, M, K, ablk, lo, hi, bias))
+    (clamp ? e2c_launch(k_quant_wide<R, true>, grid, block, 0, st, x, ldx, q, ldq, scales, M, K, ablk, lo, hi, bias)   \
+           : e2c_launch(k_quant_wide<R, false>, grid, block, 0, st, x, ldx, q, ldq, scales, M, K, ablk, lo, hi, bias))
         switch (reg) {
         case 1: E2C_QW(1); break;
         case 2: E2C_QW(2); break;

@@ -12,6 +12,8 @@
 #include <stdint.h>
 
 #include "launch.h"
+#include "pdl.h"
+#include "ptx.cuh"
 
 namespace {
 
@@ -90,6 +92,8 @@ __global__ void __launch_bounds__(256) k_embed_norm_quant(const int32_t *__restr
                                                           const float *__restrict__ gamma, float eps, float *__restrict__ res,
                                                           int8_t *__restrict__ q, float *__restrict__ qs, int M, int ablk,
                                                           int vocab, int *status) {
+    griddep_launch_dependents();
+    griddep_wait();
     const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (row >= M) return;
     constexpr int D = NV * 128;
@@ -120,6 +124,8 @@ __global__ void __launch_bounds__(256) k_norm_add_norm_quant(const float *__rest
                                                              const float *__restrict__ g1, const float *__restrict__ g2,
                                                              const float *__restrict__ gf, float eps, int8_t *__restrict__ q,
                                                              float *__restrict__ qs, int M, int ablk) {
+    griddep_launch_dependents();
+    griddep_wait();
     const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (row >= M) return;
     constexpr int D = NV * 128;
@@ -155,6 +161,8 @@ __global__ void __launch_bounds__(256) k_norm_add_norm_quant(const float *__rest
 template <int NV>
 __global__ void __launch_bounds__(256) k_norm_quant(const float *__restrict__ x, const float *__restrict__ gamma, float eps,
                                                     int8_t *__restrict__ q, float *__restrict__ qs, int M, int ablk) {
+    griddep_launch_dependents();
+    griddep_wait();
     const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (row >= M) return;
     constexpr int D = NV * 128;
@@ -171,6 +179,8 @@ __global__ void __launch_bounds__(256) k_norm_quant(const float *__restrict__ x,
 
 __global__ void k_meanpool(const float *__restrict__ x, const uint8_t *__restrict__ valid, float *__restrict__ out,
                            int S, int D) {
+    griddep_launch_dependents();
+    griddep_wait();
     const int b = blockIdx.y, d = blockIdx.x * blockDim.x + threadIdx.x;
     if (d >= D) return;
     float s = 0.f;
@@ -184,6 +194,8 @@ __global__ void k_meanpool(const float *__restrict__ x, const uint8_t *__restric
 }
 
 __global__ void k_l2norm_rows(float *__restrict__ y, const uint8_t *__restrict__ valid, int B, int S, int D) {
+    griddep_launch_dependents();
+    griddep_wait();
     const int b = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (b >= B) return;
     float *r = y + (size_t)b * D;
@@ -231,8 +243,8 @@ extern "C" int e2c_embed_norm_quant(const int32_t *ids, const int8_t *table, con
     if (M <= 0) return 0;
     const dim3 grid((M + 7) / 8), block(256);
     cudaStream_t st = (cudaStream_t)stream;
-    E2C_NV_SWITCH(D / 128, (k_embed_norm_quant<V><<<grid, block, 0, st>>>(ids, table, table_scale, embed_scale, gamma, eps,
-                                                                          res, q, qs, M, ablk, vocab, status)));
+    E2C_NV_SWITCH(D / 128, (e2c_launch(k_embed_norm_quant<V>, grid, block, 0, st, ids, table, table_scale, embed_scale, gamma, eps,
+                                                      res, q, qs, M, ablk, vocab, status)));
     return check("embed_norm_quant");
 }
 
@@ -245,7 +257,7 @@ extern "C" int e2c_norm_add_norm_quant(const float *t, float *res, const float *
     if (M <= 0) return 0;
     const dim3 grid((M + 7) / 8), block(256);
     cudaStream_t st = (cudaStream_t)stream;
-    E2C_NV_SWITCH(D / 128, (k_norm_add_norm_quant<V><<<grid, block, 0, st>>>(t, res, g1, g2, gfinal, eps, q, qs, M, ablk)));
+    E2C_NV_SWITCH(D / 128, (e2c_launch(k_norm_add_norm_quant<V>, grid, block, 0, st, t, res, g1, g2, gfinal, eps, q, qs, M, ablk)));
     return check("norm_add_norm_quant");
 }
 
@@ -258,19 +270,19 @@ extern "C" int e2c_norm_quant(const float *x, const float *gamma, float eps, int
     if (M <= 0) return 0;
     const dim3 grid((M + 7) / 8), block(256);
     cudaStream_t st = (cudaStream_t)stream;
-    E2C_NV_SWITCH(D / 128, (k_norm_quant<V><<<grid, block, 0, st>>>(x, gamma, eps, q, qs, M, ablk)));
+    E2C_NV_SWITCH(D / 128, (e2c_launch(k_norm_quant<V>, grid, block, 0, st, x, gamma, eps, q, qs, M, ablk)));
     return check("norm_quant");
 }
 
 extern "C" int e2c_meanpool(const float *x, const uint8_t *valid, float *pooled, int B, int S, int D, void *stream) {
     if (B <= 0) return 0;
     const dim3 grid((D + 127) / 128, B), block(128);
-    k_meanpool<<<grid, block, 0, (cudaStream_t)stream>>>(x, valid, pooled, S, D);
+    e2c_launch(k_meanpool, grid, block, 0, (cudaStream_t)stream, x, valid, pooled, S, D);
     return check("meanpool");
 }
 
 extern "C" int e2c_l2norm_rows(float *y, const uint8_t *valid, int B, int S, int D, void *stream) {
     if (B <= 0) return 0;
-    k_l2norm_rows<<<(B + 7) / 8, 256, 0, (cudaStream_t)stream>>>(y, valid, B, S, D);
+    e2c_launch(k_l2norm_rows, dim3((B + 7) / 8), dim3(256), 0, (cudaStream_t)stream, y, valid, B, S, D);
     return check("l2norm_rows");
 }
