@@ -53,11 +53,12 @@ struct GemmSmem {
     static constexpr int STG_BUFS = (EPI == E2C_EPI_QKV || (!PERBLOCK && EPI != E2C_EPI_I32 && CG == 1)) ? 2 : 1;
     static constexpr int STG_PER_WARP = STG_BUFS * STG_WARP;
     static constexpr int STG_OFF = STAGES * STAGE_BYTES;
-    // per-warp column constants (weight scales, norm gains): 128 floats
+    // per-warp column constants (weight scales, norm gains): 128 floats (QKV: 256, 64 pairs a warp)
+    static constexpr int CST_FLOATS = EPI == E2C_EPI_QKV ? 256 : 128;
     static constexpr int CST_OFF = STG_OFF + EPI_WARPS * STG_PER_WARP;
-    static constexpr int CST_BYTES = (PERBLOCK || EPI == E2C_EPI_I32) ? 0 : EPI_WARPS * 128 * 4;
+    static constexpr int CST_BYTES = (PERBLOCK || EPI == E2C_EPI_I32) ? 0 : EPI_WARPS * CST_FLOATS * 4;
     static constexpr int SSQ_OFF = CST_OFF + CST_BYTES;
-    static constexpr int SSQ_BYTES = EPI == E2C_EPI_QKV ? 2 * 4 * BM * 4 : 0;  // [acc][part][row]
+    static constexpr int SSQ_BYTES = EPI == E2C_EPI_QKV ? 2 * 2 * BM * 4 : 0;  // [group][part2][row]
     static constexpr int BAR_OFF = SSQ_OFF + SSQ_BYTES;
     // full[S], empty[S], tfull[2], tempty[2], pair[2][4] (QKV row-norm exchange), tmem slot
     static constexpr int NBAR = 2 * STAGES + 4 + 8;
@@ -142,8 +143,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         }
         for (int a = 0; a < 2; a++) {
             mbar_init(tfull_bar(a), 1);
-            mbar_init(tempty_bar(a), EPI_WARPS * CG);  // one arrival per epilogue warp of the pair
-            for (int q = 0; q < 4; q++) mbar_init(pair_bar(a, q), 128);
+            // one arrival per epilogue warp of the pair (QKV: per warp of the group that owns it)
+            mbar_init(tempty_bar(a), (EPI == E2C_EPI_QKV ? EPI_WARPS / 2 : EPI_WARPS) * CG);
+            for (int q = 0; q < 4; q++) mbar_init(pair_bar(a, q), 64);  // QKV: the quadrant's 2 warps of a group
         }
         fence_mbar_init();
         tma_prefetch_desc(&tmA);
@@ -333,22 +335,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 const int cw = c0 + part * QCOLS;
                 if (lane < QCOLS && cw + lane < p.n1) r.w0 = __ldg(p.w_scale + cw + lane);
                 if (32 + lane < QCOLS && cw + 32 + lane < p.n1) r.w1 = __ldg(p.w_scale + cw + 32 + lane);
-            } else if constexpr (EPI == E2C_EPI_GELU || EPI == E2C_EPI_QKV) {
-                // gate | up (GELU) or the rotate-half pair i, i + 128 (QKV) of this warp's 32 columns
+            } else if constexpr (EPI == E2C_EPI_GELU) {
+                // gate | up of this warp's 32 columns
                 r.w0 = __ldg(p.w_scale + c0 + 32 * part + lane);
                 r.w1 = __ldg(p.w_scale + c0 + 128 + 32 * part + lane);
-                if constexpr (EPI == E2C_EPI_QKV) {
-                    const int head = (c0 - p.n0) / 256;
-                    const float *gamma = head == p.nq + 1 ? nullptr : (head == p.nq ? p.k_gamma : p.q_gamma);
-                    if (gamma) {
-                        r.g0 = __ldg(gamma + 32 * part + lane);
-                        r.g1 = __ldg(gamma + 128 + 32 * part + lane);
-                    }
-                }
             }
             return r;
         };
-        float *cst = reinterpret_cast<float *>(smem + L::CST_OFF) + (warp - 2) * 128;
+        float *cst = reinterpret_cast<float *>(smem + L::CST_OFF) + (warp - 2) * L::CST_FLOATS;
         // 16 consecutive floats of cst from `off` (a broadcast: every lane reads the same address)
         auto cst16 = [&](int off, float (&o)[16]) {
 #pragma unroll
@@ -357,287 +351,359 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 o[4 * k] = w.x, o[4 * k + 1] = w.y, o[4 * k + 2] = w.z, o[4 * k + 3] = w.w;
             }
         };
-        Pre pre = fetch(tfirst);
-        for (int t = tfirst; t < ntiles && ok; t += tstride) {
-            const int mt = (t / tiles_n) * (BM * CG) + (int)rank * BM;
-            const int m = mt + row;
-            const int c0 = p.n0 + (t % tiles_n) * BN;
-            const bool mrow = m < M;
-            const int y0 = mt + q * 32;  // first row of this warp's 32
-            const int cw = c0 + part * QCOLS;  // first column of this warp (F32 / I32 / per-block)
-            if constexpr (PERBLOCK) {
-                float f[QCOLS];
+        if constexpr (EPI == E2C_EPI_QKV) {
+            // One 256-column tile = one head (q heads, then k, then v):
+            //   x = float(acc) * as * ws;  y = x * inv * gamma, inv = 1/sqrt(mean(x^2) + eps) (v: no
+            //   gamma), computed as float(acc) * (ws * gamma) * (as * inv); then RoPE and bf16.
+            // Two groups of eight warps take alternate tiles of this CTA (group g: its tiles g, g + 2,
+            // ..., accumulator g), so one group's waits (the row-norm exchange, the RoPE loads, TMEM)
+            // overlap the other group's arithmetic. In a group, two warps per TMEM lane quadrant:
+            // warp part2 owns rotate-half pairs i in [64 part2, 64 part2 + 64) with partners i + 128.
+            const int grp = (warp - 2) >> 3;
+            const int part2 = ((warp - 2) >> 2) & 1;
+            float *cst2 = reinterpret_cast<float *>(smem + L::CST_OFF) + (warp - 2) * L::CST_FLOATS;
+            // [0, 64) ws of pairs i, [64, 128) ws of partners, [128, 192) and [192, 256) ws * gamma
+            auto c16 = [&](int off, float (&o)[16]) {
 #pragma unroll
-                for (int j = 0; j < QCOLS; j++) f[j] = 0.f;
-                const int nl = cw + lane;
-                const float wsl = (EPI != E2C_EPI_I32 && nl < p.n1) ? __ldg(p.w_scale + nl) : 0.f;
-                for (int u = 0; u < nunits; u++) {
-                    const float as = mrow ? __ldg(p.a_scale + (size_t)m * nb + u) : 0.f;
-                    // warp-uniform outcome: tcgen05.ld below is .sync.aligned
+                for (int k = 0; k < 4; k++) {
+                    const float4 w = *reinterpret_cast<const float4 *>(cst2 + off + 4 * k);
+                    o[4 * k] = w.x, o[4 * k + 1] = w.y, o[4 * k + 2] = w.z, o[4 * k + 3] = w.w;
+                }
+            };
+            // the row's activation scale, fetched a tile of this group ahead
+            auto fetch_as = [&](int t) -> float {
+                if (t >= ntiles) return 0.f;
+                const int m = (t / tiles_n) * (BM * CG) + (int)rank * BM + row;
+                return m < M ? __ldg(p.a_scale + (size_t)m * nb) : 0.f;
+            };
+            float *ssq = reinterpret_cast<float *>(smem + L::SSQ_OFF);  // [group][part2][row]
+            int nst2 = 0;  // store groups this warp committed
+            int j = 0;     // tiles this group finished
+            float as_next = fetch_as(tfirst + grp * tstride);
+            for (int t = tfirst + grp * tstride; t < ntiles && ok; t += 2 * tstride, j++) {
+                const float as = as_next;
+                as_next = fetch_as(t + 2 * tstride);
+                const uint32_t aph = (uint32_t)(j & 1);
+                const int mt = (t / tiles_n) * (BM * CG) + (int)rank * BM;
+                const int m = mt + row;
+                const int c0 = p.n0 + (t % tiles_n) * BN;
+                const bool mrow = m < M;
+                const int y0 = mt + q * 32;
+                const int head = (c0 - p.n0) / 256;
+                const bool is_k = head == p.nq, is_v = head == p.nq + 1;
+                const int pos = mrow ? m % p.seq_len : 0;
+                // the column constants of the head (per lane: columns lane and lane + 32 of the
+                // warp's pairs and of their partners)
+                {
+                    const float *gamma = is_v ? nullptr : (is_k ? p.k_gamma : p.q_gamma);
+                    float wv[4], gv[4];
+#pragma unroll
+                    for (int k = 0; k < 4; k++) {
+                        const int col = (k >> 1) * 128 + 64 * part2 + 32 * (k & 1) + lane;
+                        wv[k] = __ldg(p.w_scale + c0 + col);
+                        gv[k] = gamma ? __ldg(gamma + col) : 1.f;
+                    }
+                    __syncwarp();  // every lane is done reading the previous tile's constants
+#pragma unroll
+                    for (int k = 0; k < 4; k++) {
+                        const int o = (k >> 1) * 64 + 32 * (k & 1) + lane;
+                        cst2[o] = wv[k];
+                        cst2[128 + o] = __fmul_rn(wv[k], gv[k]);
+                    }
+                    __syncwarp();
+                }
+                if (!__all_sync(0xffffffffu, mbar_wait(tfull_bar(grp), aph, p.status, E2C_ERR_WAIT_EPI))) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t tbase = tmem_base + lane_addr + (uint32_t)(grp * BN);
+                // pass 1: sum over this warp's 128 columns of (float(acc) * ws)^2, in four independent
+                // partial sums (a single fma chain would issue one step per fma latency)
+                float ssp[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                for (int c = 0; c < 4; c++) {
+                    uint32_t ra[16], rb[16];
+                    tmem_ld16(tbase + 64 * part2 + 16 * c, ra);
+                    tmem_ld16(tbase + 128 + 64 * part2 + 16 * c, rb);
+                    tmem_wait_ld();
+                    float wa[16], wb[16];
+                    c16(16 * c, wa);
+                    c16(64 + 16 * c, wb);
+#pragma unroll
+                    for (int e = 0; e < 16; e++) {
+                        const float a = __fmul_rn(__int2float_rn((int)ra[e]), wa[e]);
+                        const float b = __fmul_rn(__int2float_rn((int)rb[e]), wb[e]);
+                        ssp[e & 3] = __fmaf_rn(b, b, __fmaf_rn(a, a, ssp[e & 3]));
+                    }
+                }
+                const float ss = __fadd_rn(__fadd_rn(ssp[0], ssp[1]), __fadd_rn(ssp[2], ssp[3]));
+                // the row's sum of squares over the two warps of this quadrant in the group
+                ssq[(grp * 2 + part2) * BM + row] = ss;
+                mbar_arrive(pair_bar(grp, q));
+                if (!__all_sync(0xffffffffu, mbar_wait(pair_bar(grp, q), aph, p.status, E2C_ERR_WAIT_EPI))) {
+                    ok = false;
+                    break;
+                }
+                const float sst = __fadd_rn(ssq[(grp * 2) * BM + row], ssq[(grp * 2 + 1) * BM + row]);
+                const float ms = __fmul_rn(__fmul_rn(as, as), __fdiv_rn(sst, 256.0f));
+                const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, p.eps)));
+                const float rs = __fmul_rn(as, inv);
+                // pass 2: eight steps of 8 pairs (8-column TMEM loads, constants four at a time, outputs
+                // packed to bf16 pairs at once: few registers live). The two staging tiles (pairs |
+                // partners) take 32 pairs each and leave by TMA.
+#pragma unroll 1
+                for (int c8 = 0; c8 < 8; c8++) {
+                    const int ia = 64 * part2 + 8 * c8;  // rotate-half index of these 8 pairs
+                    if (!is_v && tma_out && (c8 & 3) == 0 && nst2 > 0) {
+                        // the stores that last read the staging tiles have finished reading them
+                        if (lane == 0) bulk_wait_read0();
+                        __syncwarp();
+                    }
+                    uint32_t ra[8], rb[8];
+                    tmem_ld8(tbase + ia, ra);
+                    tmem_ld8(tbase + 128 + ia, rb);
+                    float cs[8], sn[8];
+                    if (!is_v) {
+                        const float4 *cs4 = reinterpret_cast<const float4 *>(p.rope_cos + (size_t)pos * 128 + ia);
+                        const float4 *sn4 = reinterpret_cast<const float4 *>(p.rope_sin + (size_t)pos * 128 + ia);
+#pragma unroll
+                        for (int k = 0; k < 2; k++) {
+                            const float4 c4 = __ldg(cs4 + k), s4 = __ldg(sn4 + k);
+                            cs[4 * k] = c4.x, cs[4 * k + 1] = c4.y, cs[4 * k + 2] = c4.z, cs[4 * k + 3] = c4.w;
+                            sn[4 * k] = s4.x, sn[4 * k + 1] = s4.y, sn[4 * k + 2] = s4.z, sn[4 * k + 3] = s4.w;
+                        }
+                    }
+                    tmem_wait_ld();
+                    if (c8 == 7) release_acc(grp);  // every TMEM column this warp reads has been read
+                    uint32_t pa[4], pb[4];  // bf16 pairs of the 8 outputs of each side
+                    float va[8], vb[8];
+#pragma unroll
+                    for (int k = 0; k < 2; k++) {
+                        const float4 ca = *reinterpret_cast<const float4 *>(cst2 + 128 + 8 * c8 + 4 * k);
+                        const float4 cb = *reinterpret_cast<const float4 *>(cst2 + 192 + 8 * c8 + 4 * k);
+                        const float cav[4] = {ca.x, ca.y, ca.z, ca.w}, cbv[4] = {cb.x, cb.y, cb.z, cb.w};
+#pragma unroll
+                        for (int e = 0; e < 4; e++) {
+                            const int i = 4 * k + e;
+                            const float a = __fmul_rn(__fmul_rn(__int2float_rn((int)ra[i]), cav[e]), rs);
+                            const float b = __fmul_rn(__fmul_rn(__int2float_rn((int)rb[i]), cbv[e]), rs);
+                            if (!is_v) {
+                                va[i] = __fmaf_rn(a, cs[i], -__fmul_rn(b, sn[i]));
+                                vb[i] = __fmaf_rn(a, sn[i], __fmul_rn(b, cs[i]));
+                            } else {
+                                va[i] = a;
+                                vb[i] = b;
+                            }
+                        }
+                    }
+#pragma unroll
+                    for (int k = 0; k < 4; k++) {
+                        const __nv_bfloat162 ha = __floats2bfloat162_rn(va[2 * k], va[2 * k + 1]);
+                        const __nv_bfloat162 hb = __floats2bfloat162_rn(vb[2 * k], vb[2 * k + 1]);
+                        pa[k] = *reinterpret_cast<const uint32_t *>(&ha);
+                        pb[k] = *reinterpret_cast<const uint32_t *>(&hb);
+                    }
+                    if (is_v) {
+                        if (mrow) {
+                            __nv_bfloat16 *vt = reinterpret_cast<__nv_bfloat16 *>(p.vt_out) +
+                                                (size_t)(m / p.seq_len) * 256 * p.ldvt + pos;
+#pragma unroll
+                            for (int i = 0; i < 8; i++) {
+                                vt[(size_t)(ia + i) * p.ldvt] = reinterpret_cast<const __nv_bfloat16 *>(pa)[i];
+                                vt[(size_t)(128 + ia + i) * p.ldvt] = reinterpret_cast<const __nv_bfloat16 *>(pb)[i];
+                            }
+                        }
+                    } else if (tma_out) {
+                        // 16-byte chunk (c8 & 3) of the row's 64 bytes, in the 64-byte swizzle
+                        const int ch = ((c8 & 3) ^ ((lane >> 1) & 3)) << 4;
+                        *reinterpret_cast<uint4 *>(stg + lane * 64 + ch) = make_uint4(pa[0], pa[1], pa[2], pa[3]);
+                        *reinterpret_cast<uint4 *>(stg + STG_WARP + lane * 64 + ch) = make_uint4(pb[0], pb[1], pb[2], pb[3]);
+                        if ((c8 & 3) == 3) {
+                            const CUtensorMap *tm = is_k ? &tmO1 : &tmO0;
+                            const int xb = (is_k ? 0 : head * 256) + 64 * part2 + 32 * (c8 >> 2);
+                            fence_proxy_async_smem();
+                            __syncwarp();
+                            if (lane == 0) {
+                                tma_store_2d(tm, smem_u32(stg), xb, y0);
+                                tma_store_2d(tm, smem_u32(stg + STG_WARP), xb + 128, y0);
+                                bulk_commit();
+                            }
+                            ++nst2;
+                        }
+                    } else if (mrow) {
+                        __nv_bfloat16 *dst = is_k ? reinterpret_cast<__nv_bfloat16 *>(p.k_out) + (size_t)m * 256
+                                                  : reinterpret_cast<__nv_bfloat16 *>(p.q_out) +
+                                                        (size_t)m * (256 * p.nq) + head * 256;
+                        *reinterpret_cast<uint4 *>(dst + ia) = make_uint4(pa[0], pa[1], pa[2], pa[3]);
+                        *reinterpret_cast<uint4 *>(dst + 128 + ia) = make_uint4(pb[0], pb[1], pb[2], pb[3]);
+                    }
+                }
+            }
+        } else {
+            Pre pre = fetch(tfirst);
+            for (int t = tfirst; t < ntiles && ok; t += tstride) {
+                const int mt = (t / tiles_n) * (BM * CG) + (int)rank * BM;
+                const int m = mt + row;
+                const int c0 = p.n0 + (t % tiles_n) * BN;
+                const bool mrow = m < M;
+                const int y0 = mt + q * 32;  // first row of this warp's 32
+                const int cw = c0 + part * QCOLS;  // first column of this warp (F32 / I32 / per-block)
+                if constexpr (PERBLOCK) {
+                    float f[QCOLS];
+    #pragma unroll
+                    for (int j = 0; j < QCOLS; j++) f[j] = 0.f;
+                    const int nl = cw + lane;
+                    const float wsl = (EPI != E2C_EPI_I32 && nl < p.n1) ? __ldg(p.w_scale + nl) : 0.f;
+                    for (int u = 0; u < nunits; u++) {
+                        const float as = mrow ? __ldg(p.a_scale + (size_t)m * nb + u) : 0.f;
+                        // warp-uniform outcome: tcgen05.ld below is .sync.aligned
+                        if (!__all_sync(0xffffffffu, mbar_wait(tfull_bar(acc), acc_phase, p.status, E2C_ERR_WAIT_EPI))) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        uint32_t r[32];
+                        tmem_ld32(tmem_base + lane_addr + (uint32_t)(acc * BN + part * QCOLS), r);
+                        tmem_wait_ld();
+                        release_acc(acc);
+                        if constexpr (EPI == E2C_EPI_I32) {
+                            if (mrow)
+                                for (int j = 0; j < 32; j++)
+                                    if (cw + j < p.n1) p.dots[((size_t)m * p.ldd + cw + j) * nb + u] = (int32_t)r[j];
+                        } else {
+    #pragma unroll
+                            for (int j = 0; j < 32; j++)
+                                f[j] = __fmaf_rn(__int2float_rn((int)r[j]), __fmul_rn(as, __shfl_sync(0xffffffffu, wsl, j)), f[j]);
+                        }
+                        if (++acc == 2) {
+                            acc = 0;
+                            acc_phase ^= 1u;
+                        }
+                    }
+                    if (!ok) break;
+                    if constexpr (EPI != E2C_EPI_I32) {
+    #pragma unroll
+                        for (int h2 = 0; h2 < 2; h2++) {
+                            float v[16];
+    #pragma unroll
+                            for (int j = 0; j < 16; j++) {
+                                const int n = cw + 16 * h2 + j;
+                                v[j] = fminf(fmaxf(f[16 * h2 + j], p.out_min), p.out_max);
+                                if constexpr (EPI == E2C_EPI_RESID)
+                                    if (mrow && n < p.n1) v[j] = __fadd_rn(v[j], p.resid[(size_t)m * p.ldr + n]);
+                            }
+                            if (tma_out) {
+                                put16(v, cw + 16 * h2 - p.n0, y0);
+                            } else if (mrow) {
+                                for (int j = 0; j < 16; j++)
+                                    if (cw + 16 * h2 + j < p.n1) p.y[(size_t)m * p.ldy + cw + 16 * h2 + j] = v[j];
+                            }
+                        }
+                    }
+                } else {
+                    const Pre cur = pre;
+                    pre = fetch(t + tstride);
+                    const float as = cur.as;
+                    __syncwarp();  // every lane is done reading the previous tile's cst
+                    if constexpr (EPI == E2C_EPI_F32 || EPI == E2C_EPI_RESID) {
+                        if (lane < QCOLS) cst[lane] = cur.w0;
+                        if (32 + lane < QCOLS) cst[32 + lane] = cur.w1;
+                    } else if constexpr (EPI == E2C_EPI_GELU) {
+                        cst[lane] = cur.w0;
+                        cst[32 + lane] = cur.w1;
+                    }
+                    __syncwarp();
                     if (!__all_sync(0xffffffffu, mbar_wait(tfull_bar(acc), acc_phase, p.status, E2C_ERR_WAIT_EPI))) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    uint32_t r[32];
-                    tmem_ld32(tmem_base + lane_addr + (uint32_t)(acc * BN + part * QCOLS), r);
-                    tmem_wait_ld();
-                    release_acc(acc);
+                    const uint32_t tbase = tmem_base + lane_addr + (uint32_t)(acc * BN);
                     if constexpr (EPI == E2C_EPI_I32) {
-                        if (mrow)
-                            for (int j = 0; j < 32; j++)
-                                if (cw + j < p.n1) p.dots[((size_t)m * p.ldd + cw + j) * nb + u] = (int32_t)r[j];
-                    } else {
-#pragma unroll
-                        for (int j = 0; j < 32; j++)
-                            f[j] = __fmaf_rn(__int2float_rn((int)r[j]), __fmul_rn(as, __shfl_sync(0xffffffffu, wsl, j)), f[j]);
+    #pragma unroll 1
+                        for (int c = 0; c < QCOLS / 16; c++) {
+                            uint32_t r[16];
+                            tmem_ld16(tbase + part * QCOLS + 16 * c, r);
+                            tmem_wait_ld();
+                            const int nbase = cw + 16 * c;
+                            if (mrow)
+                                for (int j = 0; j < 16; j++)
+                                    if (nbase + j < p.n1) p.dots[(size_t)m * p.ldd + nbase + j] = (int32_t)r[j];
+                        }
+                    } else if constexpr (EPI == E2C_EPI_F32 || EPI == E2C_EPI_RESID) {
+                        // y = float(acc) * (as * ws), the reference's single-block fold; the clamp only
+                        // when the weight carries one (the defaults +-1e31 bound no finite output)
+                        constexpr int NCH = QCOLS / 16;
+                        const bool clamp = p.out_min > -1e30f || p.out_max < 1e30f;
+    #pragma unroll
+                        for (int c2 = 0; c2 < NCH; c2 += 2) {
+                            uint32_t r[2][16];
+                            tmem_ld16(tbase + part * QCOLS + 16 * c2, r[0]);
+                            if (c2 + 1 < NCH) tmem_ld16(tbase + part * QCOLS + 16 * (c2 + 1), r[1]);
+                            tmem_wait_ld();
+    #pragma unroll
+                            for (int h = 0; h < 2; h++) {
+                                if (c2 + h < NCH) {
+                                    const int nbase = cw + 16 * (c2 + h);
+                                    float w[16], v[16];
+                                    cst16(16 * (c2 + h), w);
+    #pragma unroll
+                                    for (int j = 0; j < 16; j++) v[j] = dq(r[h][j], __fmul_rn(as, w[j]));
+                                    if (clamp)
+    #pragma unroll
+                                        for (int j = 0; j < 16; j++) v[j] = fminf(fmaxf(v[j], p.out_min), p.out_max);
+                                    if constexpr (EPI == E2C_EPI_RESID) {
+                                        if (mrow) {
+                                            const float *rr = p.resid + (size_t)m * p.ldr + nbase;
+                                            for (int j = 0; j < 16; j++)
+                                                if (nbase + j < p.n1) v[j] = __fadd_rn(v[j], rr[j]);
+                                        }
+                                    }
+                                    if (tma_out) {
+                                        put16(v, nbase - p.n0, y0);
+                                    } else if (mrow && nbase < p.n1) {
+                                        float *yr = p.y + (size_t)m * p.ldy + nbase;
+                                        for (int j = 0; j < 16; j++)
+                                            if (nbase + j < p.n1) yr[j] = v[j];
+                                    }
+                                }
+                            }
+                        }
+                    } else if constexpr (EPI == E2C_EPI_GELU) {
+                        // weight rows are interleaved per 128: [gate c0/2 .. +128 | up c0/2 .. +128];
+                        // this warp produces outputs [32 part, 32 part + 32) of the tile's 128, 16 at a time
+                        const int h0 = (c0 - p.n0) / 2;
+    #pragma unroll
+                        for (int h2 = 0; h2 < 2; h2++) {
+                            const int oc = 32 * part + 16 * h2;
+                            uint32_t rg[16], ru[16];
+                            tmem_ld16(tbase + oc, rg);
+                            tmem_ld16(tbase + 128 + oc, ru);
+                            tmem_wait_ld();
+                            float wg[16], wu[16], h[16];
+                            cst16(16 * h2, wg);
+                            cst16(32 + 16 * h2, wu);
+    #pragma unroll
+                            for (int j = 0; j < 16; j++) {
+                                const float g = dq(rg[j], __fmul_rn(as, wg[j]));
+                                const float u = dq(ru[j], __fmul_rn(as, wu[j]));
+                                h[j] = __fmul_rn(gelu_tanh(g), u);
+                            }
+                            if (tma_out) {
+                                put16(h, h0 + oc, y0);
+                            } else if (mrow) {
+                                float4 *y4 = reinterpret_cast<float4 *>(p.y + (size_t)m * p.ldy + h0 + oc);
+    #pragma unroll
+                                for (int j = 0; j < 4; j++) y4[j] = make_float4(h[4 * j], h[4 * j + 1], h[4 * j + 2], h[4 * j + 3]);
+                            }
+                        }
                     }
+                    release_acc(acc);
                     if (++acc == 2) {
                         acc = 0;
                         acc_phase ^= 1u;
                     }
-                }
-                if (!ok) break;
-                if constexpr (EPI != E2C_EPI_I32) {
-#pragma unroll
-                    for (int h2 = 0; h2 < 2; h2++) {
-                        float v[16];
-#pragma unroll
-                        for (int j = 0; j < 16; j++) {
-                            const int n = cw + 16 * h2 + j;
-                            v[j] = fminf(fmaxf(f[16 * h2 + j], p.out_min), p.out_max);
-                            if constexpr (EPI == E2C_EPI_RESID)
-                                if (mrow && n < p.n1) v[j] = __fadd_rn(v[j], p.resid[(size_t)m * p.ldr + n]);
-                        }
-                        if (tma_out) {
-                            put16(v, cw + 16 * h2 - p.n0, y0);
-                        } else if (mrow) {
-                            for (int j = 0; j < 16; j++)
-                                if (cw + 16 * h2 + j < p.n1) p.y[(size_t)m * p.ldy + cw + 16 * h2 + j] = v[j];
-                        }
-                    }
-                }
-            } else {
-                const Pre cur = pre;
-                pre = fetch(t + tstride);
-                const float as = cur.as;
-                __syncwarp();  // every lane is done reading the previous tile's cst
-                if constexpr (EPI == E2C_EPI_F32 || EPI == E2C_EPI_RESID) {
-                    if (lane < QCOLS) cst[lane] = cur.w0;
-                    if (32 + lane < QCOLS) cst[32 + lane] = cur.w1;
-                } else if constexpr (EPI == E2C_EPI_GELU) {
-                    cst[lane] = cur.w0;
-                    cst[32 + lane] = cur.w1;
-                } else if constexpr (EPI == E2C_EPI_QKV) {
-                    cst[lane] = cur.w0;
-                    cst[32 + lane] = cur.w1;
-                    cst[64 + lane] = __fmul_rn(cur.w0, cur.g0);
-                    cst[96 + lane] = __fmul_rn(cur.w1, cur.g1);
-                }
-                __syncwarp();
-                if (!__all_sync(0xffffffffu, mbar_wait(tfull_bar(acc), acc_phase, p.status, E2C_ERR_WAIT_EPI))) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
-                const uint32_t tbase = tmem_base + lane_addr + (uint32_t)(acc * BN);
-                if constexpr (EPI == E2C_EPI_I32) {
-#pragma unroll 1
-                    for (int c = 0; c < QCOLS / 16; c++) {
-                        uint32_t r[16];
-                        tmem_ld16(tbase + part * QCOLS + 16 * c, r);
-                        tmem_wait_ld();
-                        const int nbase = cw + 16 * c;
-                        if (mrow)
-                            for (int j = 0; j < 16; j++)
-                                if (nbase + j < p.n1) p.dots[(size_t)m * p.ldd + nbase + j] = (int32_t)r[j];
-                    }
-                } else if constexpr (EPI == E2C_EPI_F32 || EPI == E2C_EPI_RESID) {
-                    // y = float(acc) * (as * ws), the reference's single-block fold; the clamp only
-                    // when the weight carries one (the defaults +-1e31 bound no finite output)
-                    constexpr int NCH = QCOLS / 16;
-                    const bool clamp = p.out_min > -1e30f || p.out_max < 1e30f;
-#pragma unroll
-                    for (int c2 = 0; c2 < NCH; c2 += 2) {
-                        uint32_t r[2][16];
-                        tmem_ld16(tbase + part * QCOLS + 16 * c2, r[0]);
-                        if (c2 + 1 < NCH) tmem_ld16(tbase + part * QCOLS + 16 * (c2 + 1), r[1]);
-                        tmem_wait_ld();
-#pragma unroll
-                        for (int h = 0; h < 2; h++) {
-                            if (c2 + h < NCH) {
-                                const int nbase = cw + 16 * (c2 + h);
-                                float w[16], v[16];
-                                cst16(16 * (c2 + h), w);
-#pragma unroll
-                                for (int j = 0; j < 16; j++) v[j] = dq(r[h][j], __fmul_rn(as, w[j]));
-                                if (clamp)
-#pragma unroll
-                                    for (int j = 0; j < 16; j++) v[j] = fminf(fmaxf(v[j], p.out_min), p.out_max);
-                                if constexpr (EPI == E2C_EPI_RESID) {
-                                    if (mrow) {
-                                        const float *rr = p.resid + (size_t)m * p.ldr + nbase;
-                                        for (int j = 0; j < 16; j++)
-                                            if (nbase + j < p.n1) v[j] = __fadd_rn(v[j], rr[j]);
-                                    }
-                                }
-                                if (tma_out) {
-                                    put16(v, nbase - p.n0, y0);
-                                } else if (mrow && nbase < p.n1) {
-                                    float *yr = p.y + (size_t)m * p.ldy + nbase;
-                                    for (int j = 0; j < 16; j++)
-                                        if (nbase + j < p.n1) yr[j] = v[j];
-                                }
-                            }
-                        }
-                    }
-                } else if constexpr (EPI == E2C_EPI_GELU) {
-                    // weight rows are interleaved per 128: [gate c0/2 .. +128 | up c0/2 .. +128];
-                    // this warp produces outputs [32 part, 32 part + 32) of the tile's 128, 16 at a time
-                    const int h0 = (c0 - p.n0) / 2;
-#pragma unroll
-                    for (int h2 = 0; h2 < 2; h2++) {
-                        const int oc = 32 * part + 16 * h2;
-                        uint32_t rg[16], ru[16];
-                        tmem_ld16(tbase + oc, rg);
-                        tmem_ld16(tbase + 128 + oc, ru);
-                        tmem_wait_ld();
-                        float wg[16], wu[16], h[16];
-                        cst16(16 * h2, wg);
-                        cst16(32 + 16 * h2, wu);
-#pragma unroll
-                        for (int j = 0; j < 16; j++) {
-                            const float g = dq(rg[j], __fmul_rn(as, wg[j]));
-                            const float u = dq(ru[j], __fmul_rn(as, wu[j]));
-                            h[j] = __fmul_rn(gelu_tanh(g), u);
-                        }
-                        if (tma_out) {
-                            put16(h, h0 + oc, y0);
-                        } else if (mrow) {
-                            float4 *y4 = reinterpret_cast<float4 *>(p.y + (size_t)m * p.ldy + h0 + oc);
-#pragma unroll
-                            for (int j = 0; j < 4; j++) y4[j] = make_float4(h[4 * j], h[4 * j + 1], h[4 * j + 2], h[4 * j + 3]);
-                        }
-                    }
-                } else if constexpr (EPI == E2C_EPI_QKV) {
-                    // one 256-column tile = one head (q heads, then k, then v). This warp owns
-                    // rotate-half pairs i in [32 part, 32 part + 32) with their partners i + 128.
-                    // x = float(acc) * as * ws;  y = x * inv * gamma with inv = 1/sqrt(mean(x^2) + eps)
-                    // (v: no gamma), computed as float(acc) * (ws * gamma) * (as * inv); then RoPE.
-                    const int head = (c0 - p.n0) / 256;
-                    const bool is_k = head == p.nq, is_v = head == p.nq + 1;
-                    const int pos = mrow ? m % p.seq_len : 0;
-                    // pass 1: sum over this warp's 64 columns of (float(acc) * ws)^2
-                    float ss = 0.f;
-#pragma unroll
-                    for (int h2 = 0; h2 < 2; h2++) {
-                        uint32_t ra[16], rb[16];
-                        tmem_ld16(tbase + 32 * part + 16 * h2, ra);
-                        tmem_ld16(tbase + 128 + 32 * part + 16 * h2, rb);
-                        tmem_wait_ld();
-                        float wa[16], wb[16];
-                        cst16(16 * h2, wa);
-                        cst16(32 + 16 * h2, wb);
-#pragma unroll
-                        for (int j = 0; j < 16; j++) {
-                            const float a = __fmul_rn(__int2float_rn((int)ra[j]), wa[j]);
-                            const float b = __fmul_rn(__int2float_rn((int)rb[j]), wb[j]);
-                            ss = __fmaf_rn(b, b, __fmaf_rn(a, a, ss));
-                        }
-                    }
-                    // RoPE coefficients of the first 16 pairs load while the row norms are exchanged
-                    float csv[16], snv[16];
-                    auto rope_load = [&](int ia) {
-                        const float4 *cs4 = reinterpret_cast<const float4 *>(p.rope_cos + (size_t)pos * 128 + ia);
-                        const float4 *sn4 = reinterpret_cast<const float4 *>(p.rope_sin + (size_t)pos * 128 + ia);
-#pragma unroll
-                        for (int j = 0; j < 4; j++) {
-                            const float4 c4 = __ldg(cs4 + j), s4 = __ldg(sn4 + j);
-                            csv[4 * j] = c4.x, csv[4 * j + 1] = c4.y, csv[4 * j + 2] = c4.z, csv[4 * j + 3] = c4.w;
-                            snv[4 * j] = s4.x, snv[4 * j + 1] = s4.y, snv[4 * j + 2] = s4.z, snv[4 * j + 3] = s4.w;
-                        }
-                    };
-                    if (!is_v) rope_load(32 * part);
-                    // the row's sum of squares over the four warps of this quadrant (same rows)
-                    float *ssq = reinterpret_cast<float *>(smem + L::SSQ_OFF) + acc * 4 * BM;
-                    ssq[part * BM + row] = ss;
-                    mbar_arrive(pair_bar(acc, q));  // release: the partial is visible to the others
-                    if (!__all_sync(0xffffffffu, mbar_wait(pair_bar(acc, q), acc_phase, p.status, E2C_ERR_WAIT_EPI))) {
-                        ok = false;
-                        break;
-                    }
-                    const float sst = __fadd_rn(__fadd_rn(ssq[row], ssq[BM + row]), __fadd_rn(ssq[2 * BM + row], ssq[3 * BM + row]));
-                    const float ms = __fmul_rn(__fmul_rn(as, as), __fdiv_rn(sst, 256.0f));
-                    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, p.eps)));
-                    const float rs = __fmul_rn(as, inv);
-                    if (!is_v && tma_out && nst > 0) {
-                        // the previous tile's stores have read both staging halves
-                        if (lane == 0) bulk_wait_read0();
-                        __syncwarp();
-                    }
-#pragma unroll
-                    for (int h2 = 0; h2 < 2; h2++) {
-                        const int ia = 32 * part + 16 * h2;  // rotate-half index of these 16 pairs
-                        uint32_t ra[16], rb[16];
-                        tmem_ld16(tbase + ia, ra);
-                        tmem_ld16(tbase + 128 + ia, rb);
-                        if (h2 == 1 && !is_v) rope_load(ia);
-                        tmem_wait_ld();
-                        float ca[16], cb[16], va[16], vb[16];
-                        cst16(64 + 16 * h2, ca);
-                        cst16(96 + 16 * h2, cb);
-#pragma unroll
-                        for (int j = 0; j < 16; j++) {
-                            const float a = __fmul_rn(__fmul_rn(__int2float_rn((int)ra[j]), ca[j]), rs);
-                            const float b = __fmul_rn(__fmul_rn(__int2float_rn((int)rb[j]), cb[j]), rs);
-                            if (!is_v) {
-                                va[j] = __fmaf_rn(a, csv[j], -__fmul_rn(b, snv[j]));
-                                vb[j] = __fmaf_rn(a, snv[j], __fmul_rn(b, csv[j]));
-                            } else {
-                                va[j] = a;
-                                vb[j] = b;
-                            }
-                        }
-                        if (is_v) {
-                            if (mrow) {
-                                __nv_bfloat16 *vt = reinterpret_cast<__nv_bfloat16 *>(p.vt_out) +
-                                                    (size_t)(m / p.seq_len) * 256 * p.ldvt + pos;
-#pragma unroll
-                                for (int j = 0; j < 16; j++) {
-                                    vt[(size_t)(ia + j) * p.ldvt] = __float2bfloat16_rn(va[j]);
-                                    vt[(size_t)(128 + ia + j) * p.ldvt] = __float2bfloat16_rn(vb[j]);
-                                }
-                            }
-                        } else if (tma_out) {
-                            stage_bf16x16(stg, lane, 2 * h2, va);
-                            stage_bf16x16(stg + STG_WARP, lane, 2 * h2, vb);
-                        } else if (mrow) {
-                            __nv_bfloat16 *dst = is_k ? reinterpret_cast<__nv_bfloat16 *>(p.k_out) + (size_t)m * 256
-                                                      : reinterpret_cast<__nv_bfloat16 *>(p.q_out) +
-                                                            (size_t)m * (256 * p.nq) + head * 256;
-                            for (int j = 0; j < 16; j++) {
-                                dst[ia + j] = __float2bfloat16_rn(va[j]);
-                                dst[128 + ia + j] = __float2bfloat16_rn(vb[j]);
-                            }
-                        }
-                    }
-                    if (!is_v && tma_out) {
-                        const CUtensorMap *tm = is_k ? &tmO1 : &tmO0;
-                        const int xb = is_k ? 0 : head * 256;
-                        fence_proxy_async_smem();
-                        __syncwarp();
-                        if (lane == 0) {
-                            tma_store_2d(tm, smem_u32(stg), xb + 32 * part, y0);
-                            tma_store_2d(tm, smem_u32(stg + STG_WARP), xb + 128 + 32 * part, y0);
-                            bulk_commit();
-                        }
-                        ++nst;
-                    }
-                }
-                release_acc(acc);
-                if (++acc == 2) {
-                    acc = 0;
-                    acc_phase ^= 1u;
                 }
             }
         }
@@ -855,7 +921,8 @@ extern "C" int e2c_gemm(const e2c_gemm_args *a, void *stream) {
             e2c_set_msg("gemm: the QKV epilogue needs per-row scales, whole heads of 256 and M a multiple of seq_len");
             return -1;
         }
-        return pair ? launch<256, 4, false, E2C_EPI_QKV, 2>(a, st) : launch<256, 3, false, E2C_EPI_QKV, 1>(a, st);
+        // (single CTAs only for short activation matrices: two stages leave room for the constants)
+        return pair ? launch<256, 4, false, E2C_EPI_QKV, 2>(a, st) : launch<256, 2, false, E2C_EPI_QKV, 1>(a, st);
     case E2C_EPI_NORMADD: {
         // the residual norms in the epilogue: its own kernel (gemm_i8_norm.cu)
         const int ncols = a->n1 - a->n0;

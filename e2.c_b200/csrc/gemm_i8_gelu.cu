@@ -234,8 +234,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             }
             tc_fence_after();
             const uint32_t tg = tmem_base + lane_addr + (uint32_t)(a * BN + part * QH);  // gate columns; up at + HC
-            // pass 1: h = gelu(g) u (the GELU epilogue's bits), back over the gate columns; max |h|
-            float amax = 0.f;
+            // pass 1: h = gelu(g) u (the GELU epilogue's bits), back over the gate columns; max |h| in
+            // four independent partial maxima
+            float amp[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
             for (int c = 0; c < QH / 16; c++) {
                 uint32_t rg[16], ru[16];
@@ -253,13 +254,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                         const float g = __fmul_rn(__int2float_rn((int)rg[j]), __fmul_rn(as, wgv[e]));
                         const float u = __fmul_rn(__int2float_rn((int)ru[j]), __fmul_rn(as, wuv[e]));
                         const float h = __fmul_rn(gelu_tanh(g), u);
-                        amax = fmaxf(amax, fabsf(h));
+                        amp[e] = fmaxf(amp[e], fabsf(h));
                         rg[j] = __float_as_uint(h);
                     }
                 }
                 tmem_st16(tg + 16 * c, rg);
             }
             tmem_wait_st();
+            const float amax = fmaxf(fmaxf(amp[0], amp[1]), fmaxf(amp[2], amp[3]));
             // the row's maximum over the cluster
             xl[part * BM + row] = amax;
             mbar_arrive(lbar(q));

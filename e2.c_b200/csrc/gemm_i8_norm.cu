@@ -330,7 +330,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 #pragma unroll
             for (int c = 0; c < NCH; c++) tmem_ld16(tcols(n) + 16 * c, r[c]);
             tmem_wait_ld();
-            float ss = 0.f;
+            // four independent partial sums: a single fma chain would issue one step per fma latency
+            float ssp[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
             for (int c = 0; c < NCH; c++)
 #pragma unroll
@@ -340,8 +341,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     const float u1 = __fmul_rn(__int2float_rn((int)r[c][4 * k + 1]), w4.y);
                     const float u2 = __fmul_rn(__int2float_rn((int)r[c][4 * k + 2]), w4.z);
                     const float u3 = __fmul_rn(__int2float_rn((int)r[c][4 * k + 3]), w4.w);
-                    ss = __fmaf_rn(u3, u3, __fmaf_rn(u2, u2, __fmaf_rn(u1, u1, __fmaf_rn(u0, u0, ss))));
+                    ssp[0] = __fmaf_rn(u0, u0, ssp[0]);
+                    ssp[1] = __fmaf_rn(u1, u1, ssp[1]);
+                    ssp[2] = __fmaf_rn(u2, u2, ssp[2]);
+                    ssp[3] = __fmaf_rn(u3, u3, ssp[3]);
                 }
+            const float ss = __fadd_rn(__fadd_rn(ssp[0], ssp[1]), __fadd_rn(ssp[2], ssp[3]));
             const float as = cst[C_AS + (n & 3) * 32 + lane];
             return __fmul_rn(__fmul_rn(as, as), ss);
         };
@@ -372,7 +377,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 break;
             }
             rpend = false;
-            float ss2 = 0.f, mx = 0.f;
+            float s2p[4] = {0.f, 0.f, 0.f, 0.f}, mxp[4] = {0.f, 0.f, 0.f, 0.f};  // independent partials
 #pragma unroll
             for (int c = 0; c < NCH; c++) {
                 uint32_t r[16];
@@ -392,17 +397,23 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     r[4 * k + 1] = __float_as_uint(x4.y);
                     r[4 * k + 2] = __float_as_uint(x4.z);
                     r[4 * k + 3] = __float_as_uint(x4.w);
-                    ss2 = __fmaf_rn(x4.w, x4.w, __fmaf_rn(x4.z, x4.z, __fmaf_rn(x4.y, x4.y, __fmaf_rn(x4.x, x4.x, ss2))));
+                    s2p[0] = __fmaf_rn(x4.x, x4.x, s2p[0]);
+                    s2p[1] = __fmaf_rn(x4.y, x4.y, s2p[1]);
+                    s2p[2] = __fmaf_rn(x4.z, x4.z, s2p[2]);
+                    s2p[3] = __fmaf_rn(x4.w, x4.w, s2p[3]);
                     if constexpr (quant) {
                         const float4 g4 = *reinterpret_cast<const float4 *>(cst + C_G2 + 16 * c + 4 * k);
-                        mx = fmaxf(fmaxf(fmaxf(fmaxf(mx, fabsf(__fmul_rn(x4.x, g4.x))), fabsf(__fmul_rn(x4.y, g4.y))),
-                                         fabsf(__fmul_rn(x4.z, g4.z))),
-                                   fabsf(__fmul_rn(x4.w, g4.w)));
+                        mxp[0] = fmaxf(mxp[0], fabsf(__fmul_rn(x4.x, g4.x)));
+                        mxp[1] = fmaxf(mxp[1], fabsf(__fmul_rn(x4.y, g4.y)));
+                        mxp[2] = fmaxf(mxp[2], fabsf(__fmul_rn(x4.z, g4.z)));
+                        mxp[3] = fmaxf(mxp[3], fabsf(__fmul_rn(x4.w, g4.w)));
                     }
                 }
                 tmem_st16(tcols(n) + 16 * c, r);  // x replaces t in the accumulator for pass 3
             }
             tmem_wait_st();
+            const float ss2 = __fadd_rn(__fadd_rn(s2p[0], s2p[1]), __fadd_rn(s2p[2], s2p[3]));
+            const float mx = fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3]));
             if constexpr (quant) store_res(n);  // the new residual is x
             send(1, n, make_float2(ss2, mx));
             if constexpr (quant) {
