@@ -301,14 +301,15 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 #pragma unroll
                     for (int i = 0; i < 32; i++) s[i] = __uint_as_float(rr[i]);
                 }
-                // masking only where a tile runs past the sequence or a valid mask is given
+                // masking only where a tile runs past the sequence or a valid mask is given: lane i
+                // reads key k0 + i's flag, a ballot gives every lane the 32 keys' bits
                 const int k0 = j * TKV + 32 * kh;
                 if (p.valid || k0 + 32 > S) {
+                    const int key = k0 + lane;
+                    const uint32_t keep = __ballot_sync(0xffffffffu, key < S && (!p.valid || p.valid[row0 + key]));
 #pragma unroll
-                    for (int i = 0; i < 32; i++) {
-                        const int key = k0 + i;
-                        if (!(key < S && (!p.valid || p.valid[row0 + key]))) s[i] = -INFINITY;
-                    }
+                    for (int i = 0; i < 32; i++)
+                        if (!((keep >> i) & 1u)) s[i] = -INFINITY;
                 }
                 float mx = -INFINITY;
 #pragma unroll
