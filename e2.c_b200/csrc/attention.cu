@@ -18,9 +18,10 @@
 // Operands: Q [B*S][H*256] and K [B*S][256] bf16 row-major (head dim contiguous, K-major for QK^T),
 // V^T [B][256][ldvt] bf16 (keys contiguous, K-major for PV) — the QKV GEMM epilogue writes them so.
 //
-// Warps: 0 = TMA for Q and K, 1 = TMA for V^T, 2 = MMA issuer (+TMEM owner), 3..10 = softmax,
-// rescale and epilogue: warp w owns TMEM lanes 32*(w%4) .. +31 and, with its partner of the same
-// quadrant, half of every key tile (keys 32*kh .. +31) and half of the output columns.
+// Warps: 0 = TMA for Q and K, 1 = TMA for V^T, 2 = MMA issuer (+TMEM owner), 3..10 = softmax and
+// rescale: warp w owns TMEM lanes 32*(w%4) .. +31 and, with its partner of the same quadrant, half
+// of every key tile (keys 32*kh .. +31); 11..14 = epilogue, one per lane quadrant: ctx = O / rowsum
+// for its 32 rows and all 256 columns, stored while the softmax warps run the next unit.
 //
 // Every per-tile barrier is indexed by a tile counter that runs across units (g): the S, P and PV
 // barriers come four to a set (index g & 3, phase parity (g >> 2) & 1), the K and V buffers two to
@@ -44,7 +45,8 @@ constexpr int HD = 256;        // head dim
 constexpr int TQ = 128;        // queries per unit
 constexpr int TKV = 64;        // keys per tile
 constexpr int SM_WARPS = 8;    // softmax warps
-constexpr int NTHREADS = 96 + 32 * SM_WARPS;
+constexpr int EP_WARPS = 4;    // epilogue warps
+constexpr int NTHREADS = 96 + 32 * SM_WARPS + 32 * EP_WARPS;
 constexpr float kRescaleLog2 = 8.0f;
 
 // shared memory map (bytes, from a 1024-aligned base)
@@ -53,12 +55,14 @@ constexpr int K_TILE = TKV * HD * 2;               // 4 x [64 k][64 d]    (8 KB 
 constexpr int V_TILE = HD * TKV * 2;               // [256 d][64 k]       (32 KB)
 constexpr int K_OFF = Q_OFF + TQ * HD * 2;         // 2 buffers
 constexpr int V_OFF = K_OFF + 2 * K_TILE;          // 2 buffers
-// per softmax warp, two 32-row x 16-column fp32 staging tiles for the ctx TMA stores (64-byte
-// swizzle: 16-byte chunk c of row r at chunk c ^ ((r >> 1) & 3)), used alternately
+// per epilogue warp, three 32-row x 16-column fp32 staging tiles for the ctx TMA stores (64-byte
+// swizzle: 16-byte chunk c of row r at chunk c ^ ((r >> 1) & 3)), used in turn
 constexpr int STG = 32 * 16 * 4;
+constexpr int NSTG = 3;
 constexpr int STG_OFF = V_OFF + 2 * V_TILE;
-constexpr int X_OFF = STG_OFF + SM_WARPS * 2 * STG;  // row-max exchange [2 tile parities][2 halves][128]
-constexpr int BAR_OFF = X_OFF + 2 * 2 * TQ * 4;
+constexpr int X_OFF = STG_OFF + EP_WARPS * NSTG * STG;  // row-max exchange [2 tile parities][2 halves][128]
+constexpr int INV_OFF = X_OFF + 2 * 2 * TQ * 4;        // 1 / rowsum of a unit's rows [2 unit parities][128]
+constexpr int BAR_OFF = INV_OFF + 2 * TQ * 4;
 // Q full / Q free / O free; K full x2, K empty x2, V full x2, V empty x2, PV done x4, S full x4,
 // P full x4, pair [2][4], final [4], drain
 enum {
@@ -75,7 +79,8 @@ enum {
     B_PAIR = B_PF + 4,
     B_FIN = B_PAIR + 8,
     B_DRAIN = B_FIN + 4,
-    B_NUM
+    B_UD,  // [2 unit parities][4]: a unit's 1/rowsum of a lane quadrant is ready for its epilogue warp
+    B_NUM = B_UD + 8
 };
 constexpr int SMEM_BYTES = BAR_OFF + B_NUM * 8 + 16;
 // No alignment slack: the dynamic shared memory of a kernel without static shared variables starts
@@ -129,7 +134,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     if (warp == 0 && lane == 0) {
         mbar_init(bar(B_Q), 1);
         mbar_init(bar(B_QE), 1);
-        mbar_init(bar(B_OE), 32 * SM_WARPS);
+        mbar_init(bar(B_OE), 32 * EP_WARPS);
         for (int i = 0; i < 2; i++) {
             mbar_init(bar(B_KF + i), 1);
             mbar_init(bar(B_KE + i), 1);
@@ -144,6 +149,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         mbar_init(bar(B_DRAIN), 1);
         for (int i = 0; i < 8; i++) mbar_init(bar(B_PAIR + i), 64);
         for (int i = 0; i < 4; i++) mbar_init(bar(B_FIN + i), 64);
+        for (int i = 0; i < 8; i++) mbar_init(bar(B_UD + i), 32);
         fence_mbar_init();
         tma_prefetch_desc(&tmQ);
         tma_prefetch_desc(&tmK);
@@ -269,15 +275,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 mbar_wait(bar(B_DRAIN), 0, nullptr, E2C_ERR_WAIT_DRAIN);
             }
         }
-    } else {
-        // ---------------------------------------------------------------- softmax / epilogue
+    } else if (warp < 3 + SM_WARPS) {
+        // ---------------------------------------------------------------- softmax
         const int quad = warp & 3;
-        const int kh = (warp - 3) >> 2;   // key half of every tile (and output-column half) this warp owns
+        const int kh = (warp - 3) >> 2;   // key half of every tile this warp owns
         const int r = quad * 32 + lane;   // query row within the tile = TMEM lane
         const uint32_t lane_addr = (uint32_t)(quad * 32) << 16;
         float *xch = reinterpret_cast<float *>(smem + X_OFF);  // [2][2][TQ] row maxima
-        uint8_t *stg = smem + STG_OFF + (warp - 3) * 2 * STG;
-        int nst = 0;  // ctx stores this warp committed
+        float *invs = reinterpret_cast<float *>(smem + INV_OFF);  // [2][TQ]
         bool ok = true;
         int g0 = 0, nu = 0;
         for (int u = blockIdx.x; u < p.units && ok; u += gridDim.x, nu++, g0 += nkt) {
@@ -380,19 +385,16 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 mbar_arrive(bar(B_PF + s4));
             }
             if (!ok) break;
-            // ------------------------------------------------------------ epilogue of the unit
-            // PV of the last tile completes after every earlier product (tcgen05.commit tracks all
-            // prior MMAs)
+            // ------------------------------------------------------------ end of the unit
+            // The row sum over both key halves, exchanged in the row-max slots of the last tile's
+            // parity: both warps of the pair have published P of that tile (so read its maxima) once
+            // that tile's P-full barrier completed, and neither writes those slots again before both
+            // have passed the next unit's first exchange, which follows the reads below.
             const int gl = g0 + nkt - 1;
-            if (!__all_sync(0xffffffffu, mbar_wait(bar(B_PV + (gl & 3)), (uint32_t)((gl >> 2) & 1), p.status, E2C_ERR_WAIT_ATTN))) {
+            if (!__all_sync(0xffffffffu, mbar_wait(bar(B_PF + (gl & 3)), (uint32_t)((gl >> 2) & 1), p.status, E2C_ERR_WAIT_ATTN))) {
                 ok = false;
                 break;
             }
-            tc_fence_after();
-            // The row sum over both key halves, exchanged in the row-max slots of the last tile's
-            // parity: both warps of the pair published P of that tile (so read its maxima) before
-            // PV(gl) could complete, and neither writes those slots again before both have passed the
-            // next unit's first exchange, which follows the reads below.
             float *xfin = xch + (gl & 1) * 2 * TQ;
             xfin[kh * TQ + r] = l;
             mbar_arrive(bar(B_FIN + quad));
@@ -402,35 +404,70 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             }
             const float lt = xfin[r] + xfin[TQ + r];
             const bool keep = row_in && (!p.valid || p.valid[row0 + qrow]) && lt > 0.f;
-            const float inv = keep ? __fdiv_rn(1.0f, lt) : 0.f;
-            // ctx leaves 16 columns at a time through TMA stores from the warp's two staging tiles;
-            // the stores drain while the warp moves on to the next unit. A 32-row group running past
-            // the sequence end stores row by row instead, so the next sequence's rows stay untouched.
+            // ctx = O / rowsum is the epilogue warp's. Slot and barrier alternate by unit: both are
+            // used again two units on, and unit nu+2's S tiles come from QK products the MMA issues
+            // after unit nu+1's first PV, which waited for that warp to release O of unit nu+1, after
+            // it had waited for and read unit nu's.
+            if (kh == 0) {
+                invs[(nu & 1) * TQ + r] = keep ? __fdiv_rn(1.0f, lt) : 0.f;
+                mbar_arrive(bar(B_UD + (nu & 1) * 4 + quad));
+            }
+        }
+    } else {
+        // ---------------------------------------------------------------- epilogue
+        // ctx = O / rowsum for this quadrant's 32 rows, 16 columns at a time through three staging
+        // tiles and TMA stores that drain while the next unit runs. A 32-row group running past the
+        // sequence end stores row by row instead, so the next sequence's rows stay untouched.
+        const int quad = warp & 3;
+        const int r = quad * 32 + lane;
+        const uint32_t lane_addr = (uint32_t)(quad * 32) << 16;
+        const float *invs = reinterpret_cast<const float *>(smem + INV_OFF);
+        uint8_t *stg = smem + STG_OFF + (warp - 3 - SM_WARPS) * NSTG * STG;
+        int nst = 0;  // ctx stores this warp committed
+        bool ok = true;
+        int g0 = 0, nu = 0;
+        for (int u = blockIdx.x; u < p.units && ok; u += gridDim.x, nu++, g0 += nkt) {
+            const Unit w = unit_of(u, p);
+            const int row0 = w.b * S, q0 = w.qt * TQ;
+            const int qrow = q0 + r;
+            const bool row_in = qrow < S;
+            if (!__all_sync(0xffffffffu, mbar_wait(bar(B_UD + (nu & 1) * 4 + quad), (uint32_t)((nu >> 1) & 1), p.status,
+                                                   E2C_ERR_WAIT_ATTN))) {
+                ok = false;
+                break;
+            }
+            const float inv = invs[(nu & 1) * TQ + r];
+            // PV of the last tile completes after every earlier product (tcgen05.commit tracks all
+            // prior MMAs): O is final
+            const int gl = g0 + nkt - 1;
+            if (!__all_sync(0xffffffffu, mbar_wait(bar(B_PV + (gl & 3)), (uint32_t)((gl >> 2) & 1), p.status, E2C_ERR_WAIT_ATTN))) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
             const int gq0 = q0 + quad * 32;  // first query row of this warp
             const bool tma = gq0 + 32 <= S;
-            float *out = p.ctx + ((size_t)row0 + qrow) * (size_t)(p.H * HD) + w.h * HD + 128 * kh;
-#pragma unroll
-            for (int cp = 0; cp < 2; cp++) {
-                uint32_t o[2][32];
-                tmem_ld32(tmem + lane_addr + (uint32_t)(256 + 128 * kh + 64 * cp), o[0]);
-                tmem_ld32(tmem + lane_addr + (uint32_t)(256 + 128 * kh + 64 * cp + 32), o[1]);
+            float *out = p.ctx + ((size_t)row0 + qrow) * (size_t)(p.H * HD) + w.h * HD;
+#pragma unroll 1
+            for (int cp = 0; cp < HD / 32; cp++) {
+                uint32_t o[32];
+                tmem_ld32(tmem + lane_addr + (uint32_t)(256 + 32 * cp), o);
                 tmem_wait_ld();
-                if (cp == 1) {
+                if (cp == HD / 32 - 1) {
                     // every O column this warp reads has been read: the next unit's PV may write O
                     tc_fence_before();
                     mbar_arrive(bar(B_OE));
                 }
 #pragma unroll
-                for (int c16 = 0; c16 < 4; c16++) {
-                    const uint32_t *src = &o[c16 >> 1][16 * (c16 & 1)];
+                for (int h = 0; h < 2; h++) {
                     float v[16];
 #pragma unroll
-                    for (int i = 0; i < 16; i++) v[i] = __uint_as_float(src[i]) * inv;
-                    const int col = 64 * cp + 16 * c16;
+                    for (int i = 0; i < 16; i++) v[i] = __uint_as_float(o[16 * h + i]) * inv;
+                    const int col = 32 * cp + 16 * h;
                     if (tma) {
-                        uint8_t *buf = stg + (nst & 1) * STG;
-                        if (nst >= 2) {  // the store that last read this tile has finished reading it
-                            if (lane == 0) bulk_wait_read1();
+                        uint8_t *buf = stg + (nst % NSTG) * STG;
+                        if (nst >= NSTG) {  // the store that last read this tile has finished reading it
+                            if (lane == 0) bulk_wait_read2();
                             __syncwarp();
                         }
                         uint8_t *rowp = buf + lane * 64;
@@ -441,7 +478,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                         fence_proxy_async_smem();
                         __syncwarp();
                         if (lane == 0) {
-                            tma_store_2d(&tmO, smem_u32(buf), w.h * HD + 128 * kh + col, row0 + gq0);
+                            tma_store_2d(&tmO, smem_u32(buf), w.h * HD + col, row0 + gq0);
                             bulk_commit();
                         }
                         ++nst;

@@ -130,6 +130,7 @@ E2C_DEV void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "mem
 E2C_DEV void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 // the same for all but the most recently committed group
 E2C_DEV void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+E2C_DEV void bulk_wait_read2() { asm volatile("cp.async.bulk.wait_group.read 2;" ::: "memory"); }
 // every committed store has completed
 E2C_DEV void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 // 4 bytes global -> shared without a register round trip; src_bytes 0 writes a zero and reads
