@@ -25,13 +25,14 @@
 // The epilogue is software-pipelined over row blocks so both rounds' latency hides behind work
 // of a neighbouring block: while block n's second round travels, the warp runs block n+1's first
 // pass; while block n+1's first round travels, it runs block n's last pass. Per block n:
-//   pass 1   acc(n) -> sum (acc ws)^2                     -> round 0 send
-//   pass 2   x = fma(acc, (as inv1)(ws g1), res) into the residual tiles (then TMA store) and
-//            back into acc(n)'s TMEM columns; sum x^2, max |x g2|    -> round 1 send
-//   pass 3   x from TMEM -> q8 = rint((x g2) 127 / max|x g2|), staged and TMA-stored
+//   pass 1   acc(n) -> sum (acc ws)^2, and v = acc (ws g1) back into acc(n)'s TMEM columns
+//                                                                    -> round 0 send
+//   pass 2   x = fma(v, as inv1, res) into the residual tiles (then TMA store); sum x^2, and
+//            y = x g2 back into TMEM with max |y|                   -> round 1 send
+//   pass 3   y from TMEM -> q8 = rint(y 127 / max|y|), staged and TMA-stored
 // The residual tiles of a warp (32 x 32 fp32, 64-byte swizzle) are reloaded for block n+1 as
 // soon as block n's x store has read them. fp32 is reassociated relative to the two-kernel path
-// (sum t^2 = as^2 sum (acc ws)^2; the products folded per row and column); results agree with it
+// (sum t^2 = as^2 sum (acc ws)^2, x = (acc (ws g1)) (as inv1) + res); results agree with it
 // to a few ulp, within the norms' tolerance.
 #include <cuda.h>
 #include <cuda_runtime.h>
@@ -319,7 +320,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             return tot;
         };
         auto tcols = [&](int n) { return tmem_base + lane_addr + (uint32_t)((n % NACC) * BN + part * QCOLS); };
-        // pass 1: as^2 sum over the warp's columns of (acc ws)^2, once block n's accumulator is full
+        // pass 1: as^2 sum over the warp's columns of (acc ws)^2, once block n's accumulator is full;
+        // v = acc (ws g1) replaces the accumulator for pass 2
         auto pass1 = [&](int n) -> float {
             if (!__all_sync(0xffffffffu, mbar_wait(tfull_bar(n % NACC), (uint32_t)((n / NACC) & 1), p.status, E2C_ERR_WAIT_EPI))) {
                 ok = false;
@@ -333,19 +335,23 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             // four independent partial sums: a single fma chain would issue one step per fma latency
             float ssp[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-            for (int c = 0; c < NCH; c++)
+            for (int c = 0; c < NCH; c++) {
 #pragma unroll
                 for (int k = 0; k < 4; k++) {
                     const float4 w4 = *reinterpret_cast<const float4 *>(cst + 16 * c + 4 * k);
-                    const float u0 = __fmul_rn(__int2float_rn((int)r[c][4 * k]), w4.x);
-                    const float u1 = __fmul_rn(__int2float_rn((int)r[c][4 * k + 1]), w4.y);
-                    const float u2 = __fmul_rn(__int2float_rn((int)r[c][4 * k + 2]), w4.z);
-                    const float u3 = __fmul_rn(__int2float_rn((int)r[c][4 * k + 3]), w4.w);
-                    ssp[0] = __fmaf_rn(u0, u0, ssp[0]);
-                    ssp[1] = __fmaf_rn(u1, u1, ssp[1]);
-                    ssp[2] = __fmaf_rn(u2, u2, ssp[2]);
-                    ssp[3] = __fmaf_rn(u3, u3, ssp[3]);
+                    const float4 c4 = *reinterpret_cast<const float4 *>(cst + C_WG1 + 16 * c + 4 * k);
+                    const float wv[4] = {w4.x, w4.y, w4.z, w4.w}, cv[4] = {c4.x, c4.y, c4.z, c4.w};
+#pragma unroll
+                    for (int e = 0; e < 4; e++) {
+                        const float f = __int2float_rn((int)r[c][4 * k + e]);
+                        const float u = __fmul_rn(f, wv[e]);
+                        ssp[e] = __fmaf_rn(u, u, ssp[e]);
+                        r[c][4 * k + e] = __float_as_uint(__fmul_rn(f, cv[e]));  // v = acc (ws g1), for pass 2
+                    }
                 }
+                tmem_st16(tcols(n) + 16 * c, r[c]);
+            }
+            tmem_wait_st();
             const float ss = __fadd_rn(__fadd_rn(ssp[0], ssp[1]), __fadd_rn(ssp[2], ssp[3]));
             const float as = cst[C_AS + (n & 3) * 32 + lane];
             return __fmul_rn(__fmul_rn(as, as), ss);
@@ -371,7 +377,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             if (!xok) break;
             const float inv1 = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(s1, (float)D), p.eps)));
             const float sr = __fmul_rn(cst[C_AS + (n & 3) * 32 + lane], inv1);
-            // pass 2: x = fma(acc, sr (ws g1), res) into the residual tiles and the accumulator
+            // pass 2: x = fma(v, as inv1, res) into the residual tiles; y = x g2 into the accumulator
             if (!__all_sync(0xffffffffu, mbar_wait(rb, rpar, p.status, E2C_ERR_WAIT_EPI))) {
                 ok = false;
                 break;
@@ -387,29 +393,27 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 for (int k = 0; k < 4; k++) {
                     float4 *p4 = rp(c, k);
                     const float4 r4 = *p4;
-                    const float4 c4 = *reinterpret_cast<const float4 *>(cst + C_WG1 + 16 * c + 4 * k);
-                    const float4 x4 = make_float4(__fmaf_rn(__int2float_rn((int)r[4 * k]), __fmul_rn(sr, c4.x), r4.x),
-                                                  __fmaf_rn(__int2float_rn((int)r[4 * k + 1]), __fmul_rn(sr, c4.y), r4.y),
-                                                  __fmaf_rn(__int2float_rn((int)r[4 * k + 2]), __fmul_rn(sr, c4.z), r4.z),
-                                                  __fmaf_rn(__int2float_rn((int)r[4 * k + 3]), __fmul_rn(sr, c4.w), r4.w));
+                    const float4 x4 = make_float4(__fmaf_rn(__uint_as_float(r[4 * k]), sr, r4.x),
+                                                  __fmaf_rn(__uint_as_float(r[4 * k + 1]), sr, r4.y),
+                                                  __fmaf_rn(__uint_as_float(r[4 * k + 2]), sr, r4.z),
+                                                  __fmaf_rn(__uint_as_float(r[4 * k + 3]), sr, r4.w));
                     *p4 = x4;
-                    r[4 * k] = __float_as_uint(x4.x);
-                    r[4 * k + 1] = __float_as_uint(x4.y);
-                    r[4 * k + 2] = __float_as_uint(x4.z);
-                    r[4 * k + 3] = __float_as_uint(x4.w);
                     s2p[0] = __fmaf_rn(x4.x, x4.x, s2p[0]);
                     s2p[1] = __fmaf_rn(x4.y, x4.y, s2p[1]);
                     s2p[2] = __fmaf_rn(x4.z, x4.z, s2p[2]);
                     s2p[3] = __fmaf_rn(x4.w, x4.w, s2p[3]);
                     if constexpr (quant) {
+                        // y = x g2 goes back to TMEM for the int8 pass
                         const float4 g4 = *reinterpret_cast<const float4 *>(cst + C_G2 + 16 * c + 4 * k);
-                        mxp[0] = fmaxf(mxp[0], fabsf(__fmul_rn(x4.x, g4.x)));
-                        mxp[1] = fmaxf(mxp[1], fabsf(__fmul_rn(x4.y, g4.y)));
-                        mxp[2] = fmaxf(mxp[2], fabsf(__fmul_rn(x4.z, g4.z)));
-                        mxp[3] = fmaxf(mxp[3], fabsf(__fmul_rn(x4.w, g4.w)));
+                        const float y[4] = {__fmul_rn(x4.x, g4.x), __fmul_rn(x4.y, g4.y), __fmul_rn(x4.z, g4.z), __fmul_rn(x4.w, g4.w)};
+#pragma unroll
+                        for (int e = 0; e < 4; e++) {
+                            mxp[e] = fmaxf(mxp[e], fabsf(y[e]));
+                            r[4 * k + e] = __float_as_uint(y[e]);
+                        }
                     }
                 }
-                tmem_st16(tcols(n) + 16 * c, r);  // x replaces t in the accumulator for pass 3
+                if constexpr (quant) tmem_st16(tcols(n) + 16 * c, r);
             }
             tmem_wait_st();
             const float ss2 = __fadd_rn(__fadd_rn(s2p[0], s2p[1]), __fadd_rn(s2p[2], s2p[3]));
@@ -429,8 +433,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 }
                 const float2 t2 = recv(1, n);
                 if (!xok) break;
-                // pass 3: the quantiser of src/int8.c:178-209 on z = x inv2 g2, amax = inv2 max|x g2|,
-                // scale = amax / 127, q = rint(z 127 / amax) = rint((x g2) 127 / max|x g2|); |q| <= 127
+                // pass 3: the quantiser of src/int8.c:178-209 on z = x inv2 g2, amax = inv2 max|y| with
+                // y = x g2, scale = amax / 127, q = rint(z 127 / amax) = rint(y 127 / max|y|); |q| <= 127
                 // needs no clamp, and rint is the round-to-nearest-even of adding 1.5 2^23, whose low
                 // byte is q
                 const float inv2 = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t2.x, (float)D), p.eps)));
@@ -448,11 +452,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     uint32_t pk[4];
 #pragma unroll
                     for (int k = 0; k < 4; k++) {
-                        const float4 g4 = *reinterpret_cast<const float4 *>(cst + C_G2 + 16 * c + 4 * k);
-                        const uint32_t b0 = __float_as_uint(__fmaf_rn(__fmul_rn(__uint_as_float(r[4 * k]), g4.x), s, 12582912.0f));
-                        const uint32_t b1 = __float_as_uint(__fmaf_rn(__fmul_rn(__uint_as_float(r[4 * k + 1]), g4.y), s, 12582912.0f));
-                        const uint32_t b2 = __float_as_uint(__fmaf_rn(__fmul_rn(__uint_as_float(r[4 * k + 2]), g4.z), s, 12582912.0f));
-                        const uint32_t b3 = __float_as_uint(__fmaf_rn(__fmul_rn(__uint_as_float(r[4 * k + 3]), g4.w), s, 12582912.0f));
+                        const uint32_t b0 = __float_as_uint(__fmaf_rn(__uint_as_float(r[4 * k]), s, 12582912.0f));
+                        const uint32_t b1 = __float_as_uint(__fmaf_rn(__uint_as_float(r[4 * k + 1]), s, 12582912.0f));
+                        const uint32_t b2 = __float_as_uint(__fmaf_rn(__uint_as_float(r[4 * k + 2]), s, 12582912.0f));
+                        const uint32_t b3 = __float_as_uint(__fmaf_rn(__uint_as_float(r[4 * k + 3]), s, 12582912.0f));
                         pk[k] = __byte_perm(__byte_perm(b0, b1, 0x0040), __byte_perm(b2, b3, 0x0040), 0x5410);
                     }
                     // 16-byte chunk c of row `lane` in the 32-byte swizzle of the int8 map
