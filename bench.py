@@ -484,11 +484,12 @@ def kernel_runner(name: str, M: int, dev, stream):
             Kt = torch.empty((M, Dh), dtype=torch.bfloat16, device=dev)
             Vt = torch.empty((M // SEQ, Dh, SEQ), dtype=torch.bfloat16, device=dev)
             gam = torch.ones(Dh, device=dev)
-            cs = torch.rand((SEQ, Dh // 2), device=dev)
+            cs = torch.rand((Dh // 2, SEQ), device=dev)  # pair-major RoPE table
             keep += [Q, Kt, Vt, gam, cs]
             a.epi, a.nq, a.q_out, a.k_out, a.vt_out, a.ldvt, a.seq_len = e2c.EPI_QKV, H, Q.data_ptr(), Kt.data_ptr(), Vt.data_ptr(), SEQ, SEQ
             a.q_gamma = a.k_gamma = gam.data_ptr()
             a.rope_cos = a.rope_sin = cs.data_ptr()
+            a.ldrope = SEQ
             a.eps = 1e-6
         return (lambda: e2c.gemm_raw(a, stream)), keep
     if name == "attention":

@@ -77,7 +77,7 @@ class GemmArgs(C.Structure):
                 ("out_min", C.c_float), ("out_max", C.c_float), ("nq", C.c_int), ("q_out", C.c_void_p),
                 ("k_out", C.c_void_p), ("vt_out", C.c_void_p), ("ldvt", C.c_int), ("seq_len", C.c_int),
                 ("q_gamma", C.c_void_p), ("k_gamma", C.c_void_p), ("rope_cos", C.c_void_p),
-                ("rope_sin", C.c_void_p), ("eps", C.c_float), ("res", C.c_void_p), ("ldres", C.c_int),
+                ("rope_sin", C.c_void_p), ("ldrope", C.c_int), ("eps", C.c_float), ("res", C.c_void_p), ("ldres", C.c_int),
                 ("norm_g1", C.c_void_p), ("norm_g2", C.c_void_p), ("norm_gf", C.c_void_p), ("q8", C.c_void_p),
                 ("ldq", C.c_int), ("q8_scale", C.c_void_p), ("status", C.c_void_p)]
 

@@ -218,7 +218,8 @@ e2cuda_encoder *e2cuda_encoder_create(const e2cuda_encoder_desc *d, int max_toke
     }
     {
         /* e2.c src/text.c:483-506: inv = 1/theta^(2i/D), angle = pos * inv; halves duplicated there,
-         * stored once here ([pos][Dh/2]) */
+         * stored once here, pair-major ([Dh/2][max_seq]) so the QKV epilogue reads a warp's 32
+         * positions of one pair in one line */
         const int half = e->Dh / 2;
         float *c = malloc(sizeof(float) * (size_t)e->max_seq * half), *s = malloc(sizeof(float) * (size_t)e->max_seq * half);
         if (!c || !s) {
@@ -231,8 +232,8 @@ e2cuda_encoder *e2cuda_encoder_create(const e2cuda_encoder_desc *d, int max_toke
             for (int i = 0; i < half; i++) {
                 const float inv = 1.0f / powf(d->rope_theta, (float)(2 * i) / (float)e->Dh);
                 const float f = (float)p * inv;
-                c[(size_t)p * half + i] = cosf(f);
-                s[(size_t)p * half + i] = sinf(f);
+                c[(size_t)i * e->max_seq + p] = cosf(f);
+                s[(size_t)i * e->max_seq + p] = sinf(f);
             }
         const size_t nb = sizeof(float) * (size_t)e->max_seq * half;
         const int rc = DALLOC(e->rope_cos, nb) || DALLOC(e->rope_sin, nb) ||
@@ -340,6 +341,7 @@ static int encode(e2cuda_encoder *e, int B, int S, int has_valid, cudaStream_t s
         a.k_gamma = nrm(e, l, 5);
         a.rope_cos = e->rope_cos;
         a.rope_sin = e->rope_sin;
+        a.ldrope = e->max_seq;
         a.eps = e->eps;
         if (e2cu_launch(e2c_gemm(&a, st), "encoder qkv")) return -1;
         if (e2cu_launch(e2c_attention(e->Q, e->K, e->Vt, ldvt, valid, e->ctx, B, S, e->H, e->attn_scale, e->status, st),

@@ -441,6 +441,19 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 // the row's sum of squares over the two warps of this quadrant in the group
                 ssq[(grp * 2 + part2) * BM + row] = ss;
                 mbar_arrive(pair_bar(grp, q));
+                // RoPE cos / sin come from pair-major tables ([128][ldrope]: a warp's 32 consecutive
+                // positions of one pair are one coalesced 128-byte read), each step's 8 pairs loaded a
+                // step ahead, the first step's before the row-norm exchange
+                float csn[8], snn[8];
+                if (!is_v) {
+                    const float *cp = p.rope_cos + (size_t)(64 * part2) * p.ldrope + pos;
+                    const float *sp = p.rope_sin + (size_t)(64 * part2) * p.ldrope + pos;
+#pragma unroll
+                    for (int k = 0; k < 8; k++) {
+                        csn[k] = __ldg(cp + (size_t)k * p.ldrope);
+                        snn[k] = __ldg(sp + (size_t)k * p.ldrope);
+                    }
+                }
                 if (!__all_sync(0xffffffffu, mbar_wait(pair_bar(grp, q), aph, p.status, E2C_ERR_WAIT_EPI))) {
                     ok = false;
                     break;
@@ -464,14 +477,15 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     tmem_ld8(tbase + ia, ra);
                     tmem_ld8(tbase + 128 + ia, rb);
                     float cs[8], sn[8];
-                    if (!is_v) {
-                        const float4 *cs4 = reinterpret_cast<const float4 *>(p.rope_cos + (size_t)pos * 128 + ia);
-                        const float4 *sn4 = reinterpret_cast<const float4 *>(p.rope_sin + (size_t)pos * 128 + ia);
 #pragma unroll
-                        for (int k = 0; k < 2; k++) {
-                            const float4 c4 = __ldg(cs4 + k), s4 = __ldg(sn4 + k);
-                            cs[4 * k] = c4.x, cs[4 * k + 1] = c4.y, cs[4 * k + 2] = c4.z, cs[4 * k + 3] = c4.w;
-                            sn[4 * k] = s4.x, sn[4 * k + 1] = s4.y, sn[4 * k + 2] = s4.z, sn[4 * k + 3] = s4.w;
+                    for (int k = 0; k < 8; k++) cs[k] = csn[k], sn[k] = snn[k];
+                    if (!is_v && c8 < 7) {
+                        const float *cp = p.rope_cos + (size_t)(ia + 8) * p.ldrope + pos;
+                        const float *sp = p.rope_sin + (size_t)(ia + 8) * p.ldrope + pos;
+#pragma unroll
+                        for (int k = 0; k < 8; k++) {
+                            csn[k] = __ldg(cp + (size_t)k * p.ldrope);
+                            snn[k] = __ldg(sp + (size_t)k * p.ldrope);
                         }
                     }
                     tmem_wait_ld();
@@ -917,8 +931,10 @@ extern "C" int e2c_gemm(const e2c_gemm_args *a, void *stream) {
         }
         return pair ? launch<256, 5, false, E2C_EPI_GELU, 2>(a, st) : launch<256, 3, false, E2C_EPI_GELU, 1>(a, st);
     case E2C_EPI_QKV:
-        if (perblock || a->n0 != 0 || a->n1 != 256 * (a->nq + 2) || a->seq_len <= 0 || a->M % a->seq_len) {
-            e2c_set_msg("gemm: the QKV epilogue needs per-row scales, whole heads of 256 and M a multiple of seq_len");
+        if (perblock || a->n0 != 0 || a->n1 != 256 * (a->nq + 2) || a->seq_len <= 0 || a->M % a->seq_len ||
+            a->ldrope < a->seq_len) {
+            e2c_set_msg("gemm: the QKV epilogue needs per-row scales, whole heads of 256, M a multiple of seq_len "
+                        "and RoPE tables of ldrope >= seq_len positions");
             return -1;
         }
         // (single CTAs only for short activation matrices: two stages leave room for the constants)

@@ -68,7 +68,8 @@ typedef struct {
     void *q_out, *k_out, *vt_out; /* bf16: Q [M][256*nq], K [M][256], V^T [B][256][ldvt]  */
     int ldvt, seq_len;     /* position of row m = m % seq_len; V^T row block = m / seq_len  */
     const float *q_gamma, *k_gamma; /* [256] */
-    const float *rope_cos, *rope_sin; /* [seq_len][128] */
+    const float *rope_cos, *rope_sin; /* pair-major [128][ldrope]: (i, pos) at i * ldrope + pos */
+    int ldrope;            /* >= seq_len                                                    */
     float eps;
     /* NORMADD epilogue: the residual stream res [M][ldres] (read and written), the two norm gains,
      * the final norm's gain (used when norm_g2 is NULL), the quantised rows q8 [M][ldq] and their

@@ -319,11 +319,17 @@ def test_qkv_epilogue_norm_rope(e2c, of, torch_cuda, B, S):
     K = torch.zeros((M, Dh), dtype=torch.bfloat16, device="cuda")
     Vt = torch.zeros((B, Dh, ldvt), dtype=torch.bfloat16, device="cuda")
     gq, gk = dev(torch, qg), dev(torch, kg)
-    cd, sdn = dev(torch, np.ascontiguousarray(cs[:, :128])), dev(torch, np.ascontiguousarray(sn[:, :128]))
+    # the kernel's tables are pair-major: [128][ldrope], ldrope >= S (padded here to check the stride)
+    ldrope = S + 5
+    cT = np.zeros((128, ldrope), np.float32)
+    sT = np.zeros((128, ldrope), np.float32)
+    cT[:, :S], sT[:, :S] = cs[:, :128].T, sn[:, :128].T
+    cd, sdn = dev(torch, cT), dev(torch, sT)
     a = _args_for(W, qd, sd, M, D)
     a.epi, a.nq = 4, H
     a.q_out, a.k_out, a.vt_out, a.ldvt, a.seq_len = Q.data_ptr(), K.data_ptr(), Vt.data_ptr(), ldvt, S
     a.q_gamma, a.k_gamma, a.rope_cos, a.rope_sin, a.eps = gq.data_ptr(), gk.data_ptr(), cd.data_ptr(), sdn.data_ptr(), 1e-6
+    a.ldrope = ldrope
     _launch(e2c, a, torch)
     y = of.gemm_plain(qa, a_s, w, ws, D).reshape(M, H + 2, Dh)
     port = of.port()
