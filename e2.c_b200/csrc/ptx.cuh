@@ -89,18 +89,25 @@ E2C_DEV bool mbar_try_wait_sleep(uint32_t bar, uint32_t parity, uint32_t ns) {
 #ifndef E2C_WAIT_STEP_NS
 #define E2C_WAIT_STEP_NS 100000u
 #endif
+// A wait reads the kernel's status word (another role's failure) only once it has lasted this
+// long: the read is a global load, and a barrier that completes while it is in flight would wake
+// the waiter a memory round trip late. Waits of a working pipeline end well before this.
+#ifndef E2C_WAIT_POLL_NS
+#define E2C_WAIT_POLL_NS 20000ull
+#endif
 // Wait until the phase with parity `parity` has completed. Bounded: returns false (and records
-// `code`) after E2C_WAIT_NS, or at once if another role of this kernel already failed.
+// `code`) after E2C_WAIT_NS, or soon after another role of this kernel has failed.
 E2C_DEV bool mbar_wait(uint32_t bar, uint32_t parity, int *status, int code) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer();
     for (;;) {
         if (mbar_try_wait_sleep(bar, parity, E2C_WAIT_STEP_NS)) return true;
-        if (globaltimer() - t0 > E2C_WAIT_NS) {
+        const uint64_t dt = globaltimer() - t0;
+        if (dt > E2C_WAIT_NS) {
             record_status(status, code);
             return false;
         }
-        if (status && *(volatile int *)status != 0) return false;
+        if (dt > E2C_WAIT_POLL_NS && status && *(volatile int *)status != 0) return false;
     }
 }
 
@@ -259,11 +266,12 @@ E2C_DEV bool mbar_wait_cluster(uint32_t bar, uint32_t parity, int *status, int c
             : "r"(bar), "r"(parity), "r"(E2C_WAIT_STEP_NS)
             : "memory");
         if (ok) return true;
-        if (globaltimer() - t0 > E2C_WAIT_NS) {
+        const uint64_t dt = globaltimer() - t0;
+        if (dt > E2C_WAIT_NS) {
             record_status(status, code);
             return false;
         }
-        if (status && *(volatile int *)status != 0) return false;
+        if (dt > E2C_WAIT_POLL_NS && status && *(volatile int *)status != 0) return false;
     }
 }
 // Asynchronous stores into another CTA's shared memory whose bytes complete on an mbarrier of that
