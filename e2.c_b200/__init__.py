@@ -125,7 +125,25 @@ API = [
     ("e2cuda_encoder_embed_batch", C.c_int, [vp, i32p, u8p, C.c_int, C.c_int, f32p]),
     ("e2cuda_encoder_embed_batch_device", C.c_int, [vp, vp, vp, C.c_int, C.c_int, vp, vp]),
     ("e2cuda_encoder_stats", C.c_int, [vp, C.POINTER(C.c_long), C.POINTER(C.c_long), C.POINTER(C.c_double)]),
+    ("e2cuda_q8c_open", vp, [C.c_char_p]),
+    ("e2cuda_q8c_close", None, [vp]),
+    ("e2cuda_q8c_version", C.c_int, [vp]),
+    ("e2cuda_q8c_count", C.c_int, [vp]),
+    ("e2cuda_q8c_entry", C.c_int, [vp, C.c_int, C.POINTER(C.c_char_p), C.POINTER(C.c_int), C.POINTER(C.c_int),
+                                   C.POINTER(C.c_int64), C.POINTER(C.c_uint64)]),
+    ("e2cuda_q8c_get", vp, [vp, C.c_char_p, C.c_int, C.POINTER(C.c_size_t)]),
+    ("e2cuda_q8c_get_q8w", C.c_int, [vp, C.c_char_p, C.POINTER(Q8W)]),
+    ("e2cuda_q8c_upload_w8", C.c_int, [vp, C.c_char_p, C.POINTER(W8)]),
+    ("e2cuda_q8c_create", vp, [C.c_char_p]),
+    ("e2cuda_q8c_put", C.c_int, [vp, C.c_char_p, C.c_int, C.c_int, C.POINTER(C.c_int64), vp, C.c_size_t]),
+    ("e2cuda_q8c_put_q8w", C.c_int, [vp, C.c_char_p, C.POINTER(Q8W)]),
+    ("e2cuda_q8c_put_w8", C.c_int, [vp, C.c_char_p, C.POINTER(Q8W)]),
+    ("e2cuda_q8c_commit", C.c_int, [vp]),
+    ("e2cuda_q8c_abort", None, [vp]),
+    ("e2cuda_q8c_convert", C.c_int, [C.c_char_p, C.c_char_p]),
 ]
+
+Q8C_BF16, Q8C_F32, Q8C_Q8W, Q8C_W8 = 1, 2, 3, 4
 
 _lib: C.CDLL | None = None
 
@@ -292,6 +310,96 @@ class FFN:
                 self.h = None
         except Exception:
             pass
+
+
+class Q8Cache:
+    """A mapped .e8cq model cache (e2cuda_q8c_*): the reference's kinds 1-3 and kind 4, an int8
+    weight in the device layout. Pointers it hands out live until close()."""
+
+    def __init__(self, path):
+        self.h = lib().e2cuda_q8c_open(str(path).encode())
+        if not self.h:
+            raise E2CudaError(f"q8c_open: {last_error()}")
+
+    @property
+    def version(self) -> int:
+        return lib().e2cuda_q8c_version(self.h)
+
+    def entries(self) -> list[tuple[str, int, tuple[int, ...], int]]:
+        """(name, kind, dims, nbytes) of every index entry, in file order."""
+        out = []
+        for i in range(lib().e2cuda_q8c_count(self.h)):
+            name, kind, ndim = C.c_char_p(), C.c_int(), C.c_int()
+            dims, nb = (C.c_int64 * 4)(), C.c_uint64()
+            _ok(lib().e2cuda_q8c_entry(self.h, i, C.byref(name), C.byref(kind), C.byref(ndim), dims, C.byref(nb)),
+                "q8c_entry")
+            out.append((name.value.decode(), kind.value, tuple(dims[:ndim.value]), nb.value))
+        return out
+
+    def blob(self, name: str, kind: int) -> np.ndarray:
+        """The raw bytes stored under `name` (a copy)."""
+        n = C.c_size_t()
+        p = lib().e2cuda_q8c_get(self.h, name.encode(), kind, C.byref(n))
+        if not p:
+            raise E2CudaError(f"q8c_get: {last_error()}")
+        return np.ctypeslib.as_array(C.cast(p, u8p), (n.value,)).copy() if n.value else np.zeros(0, np.uint8)
+
+    def q8w(self, name: str) -> Q8W:
+        q = Q8W()
+        _ok(lib().e2cuda_q8c_get_q8w(self.h, name.encode(), C.byref(q)), "q8c_get_q8w")
+        return q
+
+    def upload_w8(self, name: str) -> "Weight":
+        """A kind-4 entry copied to the device as is (a kind-3 one repacked on the way)."""
+        wt = Weight.__new__(Weight)
+        wt.w8 = W8()
+        _ok(lib().e2cuda_q8c_upload_w8(self.h, name.encode(), C.byref(wt.w8)), "q8c_upload_w8")
+        return wt
+
+    def close(self) -> None:
+        if getattr(self, "h", None):
+            lib().e2cuda_q8c_close(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.close()
+
+
+class Q8CacheWriter:
+    """e2cuda_q8c_create / put / commit: a new .e8cq file, renamed into place by commit()."""
+
+    def __init__(self, path):
+        self.h = lib().e2cuda_q8c_create(str(path).encode())
+        if not self.h:
+            raise E2CudaError(f"q8c_create: {last_error()}")
+
+    def put(self, name: str, kind: int, arr: np.ndarray) -> None:
+        a = np.array(arr, order="C", copy=None)  # keeps rank 0 (np.ascontiguousarray would not)
+        dims = (C.c_int64 * 4)(*a.shape)
+        _ok(lib().e2cuda_q8c_put(self.h, name.encode(), kind, a.ndim, dims, a.ctypes.data_as(vp), a.nbytes), "q8c_put")
+
+    def put_q8w(self, name: str, q) -> None:
+        _ok(lib().e2cuda_q8c_put_q8w(self.h, name.encode(), C.cast(C.byref(q), C.POINTER(Q8W))), "q8c_put_q8w")
+
+    def put_w8(self, name: str, q) -> None:
+        _ok(lib().e2cuda_q8c_put_w8(self.h, name.encode(), C.cast(C.byref(q), C.POINTER(Q8W))), "q8c_put_w8")
+
+    def commit(self) -> None:
+        h, self.h = self.h, None
+        _ok(lib().e2cuda_q8c_commit(h), "q8c_commit")
+
+    def abort(self) -> None:
+        if self.h:
+            lib().e2cuda_q8c_abort(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.abort()
+
+
+def q8c_convert(src, dst) -> None:
+    """Rewrite cache `src` as `dst` with every kind-3 weight in kind 4 (the device layout)."""
+    _ok(lib().e2cuda_q8c_convert(str(src).encode(), str(dst).encode()), "q8c_convert")
 
 
 class Encoder:

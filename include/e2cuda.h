@@ -75,6 +75,44 @@ int e2cuda_w8_from_q8w(const e2cuda_q8w *q, e2cuda_w8 *out);
 int e2cuda_w8_from_int8(const int8_t *w, const float *scale, int N, int K, e2cuda_w8 *out);
 void e2cuda_w8_free(e2cuda_w8 *w);
 
+/* ---- q8cache (.e8cq) model-cache files (A11). The reference's format (e2.c src/q8cache.c:1-12) is
+ * read and written byte-compatibly for kinds 1-3 (bf16, f32, e2_q8w). Kind 4 is an int8 weight in the
+ * e2cuda_w8 device layout (int8 [rows][ld], then fp32 scale [rows]; dims N, K, rows, ld), loaded with
+ * one host-to-device copy and no repack. A file holding a kind-4 entry is version 2; one without is
+ * version 1, which the reference's reader accepts. Calls return 0 / -1 (NULL) with e2cuda_last_error(). */
+enum { E2CUDA_Q8C_BF16 = 1, E2CUDA_Q8C_F32 = 2, E2CUDA_Q8C_Q8W = 3, E2CUDA_Q8C_W8 = 4 };
+typedef struct e2cuda_q8c e2cuda_q8c;
+typedef struct e2cuda_q8c_writer e2cuda_q8c_writer;
+/* Map a cache and check every index entry before any is used (q8c_read_open, src/q8cache.c:242-317). */
+e2cuda_q8c *e2cuda_q8c_open(const char *path);
+void e2cuda_q8c_close(e2cuda_q8c *c); /* q8c_read_close, src/q8cache.c:319 */
+int e2cuda_q8c_version(const e2cuda_q8c *c);
+int e2cuda_q8c_count(const e2cuda_q8c *c);
+/* entry i's name (valid until close), kind, rank, dims (zero past the rank) and blob size */
+int e2cuda_q8c_entry(const e2cuda_q8c *c, int i, const char **name, int *kind, int *ndim, int64_t dims[4],
+                     uint64_t *nbytes);
+/* the blob stored under `name` as `kind`, pointing into the mapping (q8c_get, src/q8cache.c:329-349) */
+const void *e2cuda_q8c_get(const e2cuda_q8c *c, const char *name, int kind, size_t *nbytes);
+/* a kind-3 entry as a borrowed e2_q8w pointing into the mapping, unclamped (q8c_get_q8w,
+ * src/q8cache.c:357-385) */
+int e2cuda_q8c_get_q8w(const e2cuda_q8c *c, const char *name, e2cuda_q8w *q);
+/* a kind-4 entry copied to the device as is; a kind-3 entry repacked as e2cuda_w8_from_q8w does */
+int e2cuda_q8c_upload_w8(const e2cuda_q8c *c, const char *name, e2cuda_w8 *out);
+/* Writer: blobs stream to a temporary file beside `path`; the commit appends the index, rewrites the
+ * header and renames the file into place; abort (or a failed commit) leaves an existing file
+ * untouched (q8c_write_open / q8c_write_close / q8c_write_abort, src/q8cache.c:61-80,183-221). */
+e2cuda_q8c_writer *e2cuda_q8c_create(const char *path);
+/* a dense kind-1/2 tensor; nbytes must be its element count times 2 or 4 */
+int e2cuda_q8c_put(e2cuda_q8c_writer *w, const char *name, int kind, int ndim, const int64_t *dims, const void *p,
+                   size_t nbytes);
+int e2cuda_q8c_put_q8w(e2cuda_q8c_writer *w, const char *name, const e2cuda_q8w *q); /* kind 3, q8c_put_q8w :163-181 */
+int e2cuda_q8c_put_w8(e2cuda_q8c_writer *w, const char *name, const e2cuda_q8w *q);  /* kind 4, repacked on the host */
+int e2cuda_q8c_commit(e2cuda_q8c_writer *w); /* frees the writer */
+void e2cuda_q8c_abort(e2cuda_q8c_writer *w); /* frees the writer */
+/* Copy a cache with every kind-3 weight rewritten as kind 4 and every other entry byte for byte:
+ * the step an exporter (e2.c tools/export_cache.c) adds to write a cache that loads without repack. */
+int e2cuda_q8c_convert(const char *in, const char *out);
+
 /* ------------------------------------------------------------------ op API (device pointers) */
 /* Activation quantiser (A1), e2.c src/int8.c:178-209 / src/kernels_i8_avx512_vnni.c:312-366:
  * per block of `ablk` elements (ablk = K: per-token scales), amax of the input clamped to [lo, hi]

@@ -140,6 +140,37 @@ def port() -> C.CDLL:
     return _port
 
 
+_q8c: list = []
+
+
+def ref_q8cache() -> C.CDLL | None:
+    """The reference's .e8cq writer and reader (src/q8cache.c, built by oracle/Makefile), or None
+    when the reference was not built here. Its state is global: one file open at a time."""
+    if not _q8c:
+        p = REF_DIR / "libe2ref_q8c.so"
+        lib = None
+        if p.exists():
+            lib = C.CDLL(str(p))
+            i64p = C.POINTER(C.c_int64)
+            for name, res, args in [
+                ("q8c_write_open", C.c_int, [C.c_char_p]),
+                ("q8c_defer", C.c_int, [C.c_char_p, C.c_int, C.c_int, i64p, C.c_void_p, C.c_size_t]),
+                ("q8c_put_q8w", C.c_int, [C.c_char_p, C.POINTER(Q8W)]),
+                ("q8c_write_close", C.c_int, []),
+                ("q8c_write_abort", None, []),
+                ("q8c_read_open", C.c_int, [C.c_char_p]),
+                ("q8c_read_close", None, []),
+                ("q8c_get", C.c_void_p, [C.c_char_p, C.c_int, C.c_int, i64p, C.POINTER(C.c_size_t)]),
+                ("q8c_get_q8w", C.c_int, [C.c_char_p, C.POINTER(Q8W)]),
+                ("q8c_kind_of", C.c_int, [C.c_char_p]),
+                ("q8c_error", C.c_char_p, []),
+            ]:
+                fn = getattr(lib, name)
+                fn.restype, fn.argtypes = res, args
+        _q8c.append(lib)
+    return _q8c[0]
+
+
 def ref_available(block: int) -> bool:
     return (REF_DIR / f"libe2ref_b{block}.so").exists()
 

@@ -101,6 +101,33 @@ def test_gemm_bitexact(e2c, of, torch_cuda, M, N, K, ablk):
     assert f32_bits_equal(y, ey), f"fp32 outputs differ: max abs {np.abs(y - ey).max()}"
 
 
+@pytest.mark.parametrize("N,K,ablk", [(200, 768, 768), (77, 256, 128), (1152, 768, 768)])
+def test_q8cache_upload_matches_the_repack(e2c, of, torch_cuda, tmp_path, N, K, ablk):
+    """A11: a kind-4 cache entry (the device layout) goes to the GPU with one copy, a kind-3 entry
+    through the repack; both compute bit-for-bit what e2cuda_w8_from_q8w's weight computes, and
+    what the port computes."""
+    rng = np.random.default_rng(N + K)
+    w = of.Weight(rng.standard_normal((N, K)).astype(np.float32) * 0.05, ablk)
+    wr = e2c.Q8CacheWriter(tmp_path / "c.e8cq")
+    wr.put_w8("w4", w.q)
+    wr.put_q8w("w3", w.q)
+    wr.commit()
+    c = e2c.Q8Cache(tmp_path / "c.e8cq")
+    W4, W3 = c.upload_w8("w4"), c.upload_w8("w3")
+    c.close()  # the device copies do not depend on the mapping
+    Wr = e2c.Weight(q8w=C.cast(C.byref(w.q), C.POINTER(e2c.Q8W)).contents)
+    assert (W4.w8.N, W4.w8.K, W4.w8.rows, W4.w8.ld) == (Wr.w8.N, Wr.w8.K, Wr.w8.rows, Wr.w8.ld)
+    M = 300
+    qa = rng.integers(-127, 128, size=(M, K), dtype=np.int8)
+    a_s = rng.uniform(1e-3, 0.05, size=(M, K // ablk)).astype(np.float32)
+    qd, sd = dev(torch_cuda, qa), dev(torch_cuda, a_s)
+    ys = [e2c.i8_gemm(W, qd, sd, ablk).cpu().numpy() for W in (W4, W3, Wr)]
+    e2c.check()
+    ey = of.gemm_plain(qa, a_s, w.plain(), w.scales(), ablk)
+    for y in ys:
+        assert f32_bits_equal(y, ey)
+
+
 def test_gemm_column_range_residual(e2c, of, torch_cuda):
     rng = np.random.default_rng(11)
     M, N, K = 45, 40, 768
