@@ -401,7 +401,8 @@ def config4(args) -> int:
 # one KV head of 256), the per-launch algorithmic work each is measured against, and the launches of
 # each per layer. Weights are quantised N(0, 0.02), activations per-token quantised N(0, 1).
 KERNELS = ("gate_up", "gate_up_q", "qkv", "o_proj", "down", "o_proj_norm", "down_norm", "attention", "quantize",
-           "quantize_ctx", "norm_add")
+           "quantize_ctx", "norm_add", "o_proj_pb", "down_pb")
+# *_pb: the same GEMMs with per-128-block activation scales (the reference engine's own recipe)
 # the kernels an encoder layer runs (hidden 768, FFN 1152, per-token scales): the residual norms fused
 # into o_proj and down and h's quantiser into gate|up, or with E2C_FUSED_NORM=0 / E2C_FUSED_GELU=0
 # the row kernels after them
@@ -414,15 +415,16 @@ if os.environ.get("E2C_FUSED_GELU") == "0":
 
 def kernel_work(name: str, M: int) -> dict:
     D, I, H, Dh = 768, 1152, 3, 256
-    if name in ("gate_up", "gate_up_q", "qkv", "o_proj", "down", "o_proj_norm", "down_norm"):
+    if name in ("gate_up", "gate_up_q", "qkv", "o_proj", "down", "o_proj_norm", "down_norm", "o_proj_pb", "down_pb"):
         N, K = {"gate_up": (2 * I, D), "gate_up_q": (2 * I, D), "qkv": ((H + 2) * Dh, D), "o_proj": (D, D),
-                "down": (D, I), "o_proj_norm": (D, D), "down_norm": (D, I)}[name]
+                "down": (D, I), "o_proj_norm": (D, D), "down_norm": (D, I), "o_proj_pb": (D, D), "down_pb": (D, I)}[name]
         # the fused norm epilogue reads and writes the fp32 residual and writes int8 rows + scales;
         # the fused GELU-quantise epilogue writes int8 h + scales
         out_bytes = {"gate_up": 4 * M * I, "gate_up_q": M * I + 4 * M, "qkv": 2 * M * N, "o_proj": 4 * M * D,
                      "down": 4 * M * D, "o_proj_norm": 8 * M * D + M * D + 4 * M,
-                     "down_norm": 8 * M * D + M * D + 4 * M}[name]
-        return {"ops": 2.0 * M * N * K, "bytes": M * K + 4 * M + N * K + 4 * N + out_bytes, "per_layer": 1}
+                     "down_norm": 8 * M * D + M * D + 4 * M, "o_proj_pb": 4 * M * D, "down_pb": 4 * M * D}[name]
+        a_scales = 4 * M * (K // 128) if name.endswith("_pb") else 4 * M
+        return {"ops": 2.0 * M * N * K, "bytes": M * K + a_scales + N * K + 4 * N + out_bytes, "per_layer": 1}
     if name == "attention":
         return {"ops": 4.0 * M * SEQ * Dh * H, "bytes": M * (H + 2) * Dh * 2 + 4 * M * H * Dh, "per_layer": 1}
     if name in ("quantize", "quantize_ctx"):
@@ -449,13 +451,16 @@ def kernel_runner(name: str, M: int, dev, stream):
         return e2c.quantize_rows(torch.randn((M, K), device=dev, generator=g), K)
 
     keep = []
-    if name in ("gate_up", "gate_up_q", "qkv", "o_proj", "down", "o_proj_norm", "down_norm"):
+    if name in ("gate_up", "gate_up_q", "qkv", "o_proj", "down", "o_proj_norm", "down_norm", "o_proj_pb", "down_pb"):
         N, K = {"gate_up": (2 * I, D), "gate_up_q": (2 * I, D), "qkv": ((H + 2) * Dh, D), "o_proj": (D, D),
-                "down": (D, I), "o_proj_norm": (D, D), "down_norm": (D, I)}[name]
+                "down": (D, I), "o_proj_norm": (D, D), "down_norm": (D, I), "o_proj_pb": (D, D), "down_pb": (D, I)}[name]
         wq, ws = syn.quantize_weight_rows((rng.standard_normal((N, K)) * 0.02).astype(np.float32))
         W = e2c.Weight(w=wq, scale=ws)
-        qa, qs = qin(K)
+        pb = name.endswith("_pb")
+        qa, qs = e2c.quantize_rows(torch.randn((M, K), device=dev, generator=g), 128) if pb else qin(K)
         a = e2c.gemm_args(W, qa, qs, M)
+        if pb:
+            a.ablk = 128
         keep = [W, qa, qs]
         if name == "gate_up":
             y = torch.empty((M, I), dtype=torch.float32, device=dev)
@@ -466,7 +471,7 @@ def kernel_runner(name: str, M: int, dev, stream):
             q8s = torch.empty((M,), dtype=torch.float32, device=dev)
             a.epi, a.q8, a.ldq, a.q8_scale = e2c.EPI_GELUQ, q8.data_ptr(), I, q8s.data_ptr()
             keep += [q8, q8s]
-        elif name in ("down", "o_proj"):
+        elif name in ("down", "o_proj", "down_pb", "o_proj_pb"):
             y = torch.empty((M, D), dtype=torch.float32, device=dev)
             a.epi, a.y, a.ldy = e2c.EPI_F32, y.data_ptr(), D
             keep.append(y)
@@ -526,8 +531,6 @@ def kernel_table(dev, stream, M: int = BATCH * SEQ, steps: int = 10) -> dict:
     """CUDA-event time of every encoder kernel at the encoder's shape (L2 flushed before each launch)
     with its roofline fraction against the measured peaks."""
     e2c = load_pkg()
-    p = peaks()
-    int8_peak, bf16_peak, hbm = 2.0 * p["bf16_tflops"], p["bf16_tflops"], p["hbm_gbs"]
     traffic = {}
     tf = ROOT / "profiles" / "traffic.json"
     if tf.exists():
@@ -537,19 +540,24 @@ def kernel_table(dev, stream, M: int = BATCH * SEQ, steps: int = 10) -> dict:
         run, keep = kernel_runner(name, M, dev, stream)
         ms = timed_launches(run, stream, 3, steps)
         e2c.check(stream)
-        wk = kernel_work(name, M)
-        # the binding roofline: whichever of the tensor-core time and the HBM time at peak is longer
-        tpeak = bf16_peak if name == "attention" else int8_peak
-        bound = "tensor" if wk["ops"] / (tpeak * 1e12) >= wk["bytes"] / (hbm * 1e9) else "hbm"
-        if bound == "tensor":
-            peak, achieved, unit = tpeak, wk["ops"] / (ms / 1e3) / 1e12, "TFLOP/s"
-        else:
-            peak, achieved, unit = hbm, wk["bytes"] / (ms / 1e3) / 1e9, "GB/s"
-        table[name] = {"bound": bound, "achieved": achieved, "peak": peak, "unit": unit, "frac": achieved / peak,
-                       "avg_ms": ms, "launches_per_layer": wk["per_layer"], "algorithmic_bytes": wk["bytes"],
-                       "traffic": traffic.get(name)}
+        table[name] = dict(binding_roofline(name, M, ms), traffic=traffic.get(name))
         del run, keep
     return table
+
+
+def binding_roofline(name: str, M: int, ms: float) -> dict:
+    """Kernel `name` at M tokens taking `ms`: the binding roofline (whichever of the tensor-core time
+    and the HBM time at the measured peaks is longer) and the fraction of it achieved."""
+    p = peaks()
+    wk = kernel_work(name, M)
+    tpeak, hbm = (p["bf16_tflops"] if name == "attention" else 2.0 * p["bf16_tflops"]), p["hbm_gbs"]
+    bound = "tensor" if wk["ops"] / (tpeak * 1e12) >= wk["bytes"] / (hbm * 1e9) else "hbm"
+    if bound == "tensor":
+        peak, achieved, unit = tpeak, wk["ops"] / (ms / 1e3) / 1e12, "TFLOP/s"
+    else:
+        peak, achieved, unit = hbm, wk["bytes"] / (ms / 1e3) / 1e9, "GB/s"
+    return {"bound": bound, "achieved": achieved, "peak": peak, "unit": unit, "frac": achieved / peak, "avg_ms": ms,
+            "launches_per_layer": wk["per_layer"], "algorithmic_bytes": wk["bytes"]}
 
 
 def dominant_roofline(table: dict) -> dict:
@@ -578,7 +586,9 @@ def kernel_only(args) -> int:
     run, keep = kernel_runner(args.kernel, args.tokens, dev, stream)
     avg_ms = timed_launches(run, stream, args.warmup, args.steps)
     e2c.check(stream)
-    print(json.dumps({"kernel": args.kernel, "tokens": args.tokens, "avg_ms": avg_ms, "l2": "flushed between launches"}))
+    r = binding_roofline(args.kernel, args.tokens, avg_ms)
+    print(json.dumps({"kernel": args.kernel, "tokens": args.tokens, "avg_ms": avg_ms, "l2": "flushed between launches",
+                      "bound": r["bound"], "achieved": r["achieved"], "unit": r["unit"], "frac": r["frac"]}))
     return 0
 
 

@@ -53,15 +53,19 @@ struct GemmSmem {
     static constexpr int STG_BUFS = (EPI == E2C_EPI_QKV || (!PERBLOCK && EPI != E2C_EPI_I32 && CG == 1)) ? 2 : 1;
     static constexpr int STG_PER_WARP = STG_BUFS * STG_WARP;
     static constexpr int STG_OFF = STAGES * STAGE_BYTES;
-    // per-warp column constants (weight scales, norm gains): 128 floats (QKV: 256, 64 pairs a warp)
-    static constexpr int CST_FLOATS = EPI == E2C_EPI_QKV ? 256 : 128;
+    // per-warp column constants (weight scales, norm gains): 128 floats (QKV: 256, 64 pairs a warp;
+    // per-block mode: the 32 weight scales of the warp)
+    static constexpr int CST_FLOATS = EPI == E2C_EPI_QKV ? 256 : PERBLOCK ? 32 : 128;
     static constexpr int CST_OFF = STG_OFF + EPI_WARPS * STG_PER_WARP;
-    static constexpr int CST_BYTES = (PERBLOCK || EPI == E2C_EPI_I32) ? 0 : EPI_WARPS * CST_FLOATS * 4;
+    static constexpr int CST_BYTES = EPI == E2C_EPI_I32 ? 0 : EPI_WARPS * CST_FLOATS * 4;
     static constexpr int SSQ_OFF = CST_OFF + CST_BYTES;
     static constexpr int SSQ_BYTES = EPI == E2C_EPI_QKV ? 2 * 2 * BM * 4 : 0;  // [group][part2][row]
     static constexpr int BAR_OFF = SSQ_OFF + SSQ_BYTES;
-    // full[S], empty[S], tfull[2], tempty[2], pair[2][4] (QKV row-norm exchange), tmem slot
-    static constexpr int NBAR = 2 * STAGES + 4 + 8;
+    // TMEM accumulators: per-block mode keeps four (the tensor core runs up to three 128-deep blocks
+    // ahead of the drain), the others two
+    static constexpr int NACC = PERBLOCK ? 4 : 2;
+    // full[S], empty[S], tfull[NACC], tempty[NACC], pair[2][4] (QKV row-norm exchange), tmem slot
+    static constexpr int NBAR = 2 * STAGES + 2 * NACC + 8;
     static constexpr int BYTES = BAR_OFF + NBAR * 8 + 16;
     static constexpr int ALLOC = BYTES + 1024;  // slack for 1024-byte alignment
     static_assert(ALLOC <= 232448, "shared memory");
@@ -116,9 +120,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     const uint32_t bar0 = sbase + L::BAR_OFF;
     auto full_bar = [&](int s) { return bar0 + 8u * s; };
     auto empty_bar = [&](int s) { return bar0 + 8u * (STAGES + s); };
+    constexpr int NACC = L::NACC;
     auto tfull_bar = [&](int a) { return bar0 + 8u * (2 * STAGES + a); };
-    auto tempty_bar = [&](int a) { return bar0 + 8u * (2 * STAGES + 2 + a); };
-    auto pair_bar = [&](int a, int q) { return bar0 + 8u * (2 * STAGES + 4 + 4 * a + q); };
+    auto tempty_bar = [&](int a) { return bar0 + 8u * (2 * STAGES + NACC + a); };
+    auto pair_bar = [&](int a, int q) { return bar0 + 8u * (2 * STAGES + 2 * NACC + 4 * a + q); };
     volatile uint32_t *tmem_slot = reinterpret_cast<volatile uint32_t *>(smem + L::BAR_OFF + L::NBAR * 8);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -134,19 +139,21 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     const int kpu = PERBLOCK ? p.ablk / BK : nk;         // stages per accumulation unit
     const int nunits = PERBLOCK ? K / p.ablk : 1;
     const int nb = K / p.ablk;                           // scale blocks per row
-    constexpr uint32_t TMEM_COLS = BN == 192 ? 512 : 2 * BN;  // a power of two, two accumulators
+    static_assert(!PERBLOCK || BN == 128, "per-block mode: four 128-column accumulators");
+    constexpr uint32_t TMEM_COLS = PERBLOCK ? 512 : BN == 192 ? 512 : 2 * BN;  // a power of two
 
     if (warp == 0 && lane == 0) {
         for (int s = 0; s < STAGES; s++) {
             mbar_init(full_bar(s), 1);
             mbar_init(empty_bar(s), 1);
         }
-        for (int a = 0; a < 2; a++) {
+        for (int a = 0; a < NACC; a++) {
             mbar_init(tfull_bar(a), 1);
             // one arrival per epilogue warp of the pair (QKV: per warp of the group that owns it)
             mbar_init(tempty_bar(a), (EPI == E2C_EPI_QKV ? EPI_WARPS / 2 : EPI_WARPS) * CG);
-            for (int q = 0; q < 4; q++) mbar_init(pair_bar(a, q), 64);  // QKV: the quadrant's 2 warps of a group
         }
+        for (int a = 0; a < 2; a++)
+            for (int q = 0; q < 4; q++) mbar_init(pair_bar(a, q), 64);  // QKV: the quadrant's 2 warps of a group
         fence_mbar_init();
         tma_prefetch_desc(&tmA);
         tma_prefetch_desc(&tmB);
@@ -273,7 +280,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                         }
                     }
                     commit(tfull_bar(acc));
-                    if (++acc == 2) {
+                    if (++acc == NACC) {
                         acc = 0;
                         acc_phase ^= 1u;
                     }
@@ -567,10 +574,18 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     float f[QCOLS];
     #pragma unroll
                     for (int j = 0; j < QCOLS; j++) f[j] = 0.f;
-                    const int nl = cw + lane;
-                    const float wsl = (EPI != E2C_EPI_I32 && nl < p.n1) ? __ldg(p.w_scale + nl) : 0.f;
+                    if constexpr (EPI != E2C_EPI_I32) {
+                        // the warp's 32 weight scales, read back by broadcast loads four at a time
+                        const int nl = cw + lane;
+                        __syncwarp();  // every lane is done with the previous tile's
+                        cst[lane] = nl < p.n1 ? __ldg(p.w_scale + nl) : 0.f;
+                        __syncwarp();
+                    }
+                    // the row's activation scale of block u, loaded a block ahead
+                    float as_next = mrow ? __ldg(p.a_scale + (size_t)m * nb) : 0.f;
                     for (int u = 0; u < nunits; u++) {
-                        const float as = mrow ? __ldg(p.a_scale + (size_t)m * nb + u) : 0.f;
+                        const float as = as_next;
+                        if (u + 1 < nunits) as_next = mrow ? __ldg(p.a_scale + (size_t)m * nb + u + 1) : 0.f;
                         // warp-uniform outcome: tcgen05.ld below is .sync.aligned
                         if (!__all_sync(0xffffffffu, mbar_wait(tfull_bar(acc), acc_phase, p.status, E2C_ERR_WAIT_EPI))) {
                             ok = false;
@@ -587,10 +602,17 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                                     if (cw + j < p.n1) p.dots[((size_t)m * p.ldd + cw + j) * nb + u] = (int32_t)r[j];
                         } else {
     #pragma unroll
-                            for (int j = 0; j < 32; j++)
-                                f[j] = __fmaf_rn(__int2float_rn((int)r[j]), __fmul_rn(as, __shfl_sync(0xffffffffu, wsl, j)), f[j]);
+                            for (int j4 = 0; j4 < 8; j4++) {
+                                const float4 w4 = *reinterpret_cast<const float4 *>(cst + 4 * j4);
+                                const float wv[4] = {w4.x, w4.y, w4.z, w4.w};
+    #pragma unroll
+                                for (int e = 0; e < 4; e++) {
+                                    const int j = 4 * j4 + e;
+                                    f[j] = __fmaf_rn(__int2float_rn((int)r[j]), __fmul_rn(as, wv[e]), f[j]);
+                                }
+                            }
                         }
-                        if (++acc == 2) {
+                        if (++acc == NACC) {
                             acc = 0;
                             acc_phase ^= 1u;
                         }
@@ -714,7 +736,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                         }
                     }
                     release_acc(acc);
-                    if (++acc == 2) {
+                    if (++acc == NACC) {
                         acc = 0;
                         acc_phase ^= 1u;
                     }
@@ -898,7 +920,7 @@ extern "C" int e2c_gemm(const e2c_gemm_args *a, void *stream) {
     const bool pair = pl.cg == 2;
     switch (a->epi) {
     case E2C_EPI_F32:
-        if (perblock) return launch<128, 6, true, E2C_EPI_F32, 1>(a, st);
+        if (perblock) return launch<128, 5, true, E2C_EPI_F32, 1>(a, st);
         if (pair)
             return pl.bn == 128   ? launch<128, 6, false, E2C_EPI_F32, 2>(a, st)
                    : pl.bn == 192 ? launch<192, 6, false, E2C_EPI_F32, 2>(a, st)
@@ -907,7 +929,7 @@ extern "C" int e2c_gemm(const e2c_gemm_args *a, void *stream) {
                : pl.bn == 192 ? launch<192, 3, false, E2C_EPI_F32, 1>(a, st)
                               : launch<256, 3, false, E2C_EPI_F32, 1>(a, st);
     case E2C_EPI_RESID:
-        if (perblock) return launch<128, 6, true, E2C_EPI_RESID, 1>(a, st);
+        if (perblock) return launch<128, 5, true, E2C_EPI_RESID, 1>(a, st);
         if (pair)
             return pl.bn == 128   ? launch<128, 6, false, E2C_EPI_RESID, 2>(a, st)
                    : pl.bn == 192 ? launch<192, 6, false, E2C_EPI_RESID, 2>(a, st)
