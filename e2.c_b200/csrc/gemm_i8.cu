@@ -601,14 +601,20 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                                 for (int j = 0; j < 32; j++)
                                     if (cw + j < p.n1) p.dots[((size_t)m * p.ldd + cw + j) * nb + u] = (int32_t)r[j];
                         } else {
+                            // f = fma(float(dot), as * ws, f) per column, two columns per packed
+                            // f32x2 multiply and fma
+                            const float2 as2 = make_float2(as, as);
     #pragma unroll
                             for (int j4 = 0; j4 < 8; j4++) {
                                 const float4 w4 = *reinterpret_cast<const float4 *>(cst + 4 * j4);
-                                const float wv[4] = {w4.x, w4.y, w4.z, w4.w};
     #pragma unroll
-                                for (int e = 0; e < 4; e++) {
-                                    const int j = 4 * j4 + e;
-                                    f[j] = __fmaf_rn(__int2float_rn((int)r[j]), __fmul_rn(as, wv[e]), f[j]);
+                                for (int h = 0; h < 2; h++) {
+                                    const int j = 4 * j4 + 2 * h;
+                                    const float2 s2 = mul2_rn(as2, h ? make_float2(w4.z, w4.w) : make_float2(w4.x, w4.y));
+                                    const float2 d2 = make_float2(__int2float_rn((int)r[j]), __int2float_rn((int)r[j + 1]));
+                                    const float2 o = fma2_rn(d2, s2, make_float2(f[j], f[j + 1]));
+                                    f[j] = o.x;
+                                    f[j + 1] = o.y;
                                 }
                             }
                         }
