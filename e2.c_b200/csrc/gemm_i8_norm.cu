@@ -39,6 +39,7 @@
 #include <stdint.h>
 #include <string.h>
 
+#include "epi_math.cuh"
 #include "launch.h"
 #include "pdl.h"
 #include "ptx.cuh"
@@ -332,27 +333,31 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 #pragma unroll
             for (int c = 0; c < NCH; c++) tmem_ld16(tcols(n) + 16 * c, r[c]);
             tmem_wait_ld();
-            // four independent partial sums: a single fma chain would issue one step per fma latency
-            float ssp[4] = {0.f, 0.f, 0.f, 0.f};
+            // four independent partial sums (a single fma chain would issue one step per fma latency),
+            // two per packed f32x2 register: ssp[h] = (sum of columns 4i + 2h, of columns 4i + 2h + 1)
+            float2 ssp[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
             for (int c = 0; c < NCH; c++) {
 #pragma unroll
                 for (int k = 0; k < 4; k++) {
                     const float4 w4 = *reinterpret_cast<const float4 *>(cst + 16 * c + 4 * k);
                     const float4 c4 = *reinterpret_cast<const float4 *>(cst + C_WG1 + 16 * c + 4 * k);
-                    const float wv[4] = {w4.x, w4.y, w4.z, w4.w}, cv[4] = {c4.x, c4.y, c4.z, c4.w};
 #pragma unroll
-                    for (int e = 0; e < 4; e++) {
-                        const float f = __int2float_rn((int)r[c][4 * k + e]);
-                        const float u = __fmul_rn(f, wv[e]);
-                        ssp[e] = __fmaf_rn(u, u, ssp[e]);
-                        r[c][4 * k + e] = __float_as_uint(__fmul_rn(f, cv[e]));  // v = acc (ws g1), for pass 2
+                    for (int h = 0; h < 2; h++) {
+                        const int e = 4 * k + 2 * h;
+                        const float2 f = make_float2(__int2float_rn((int)r[c][e]), __int2float_rn((int)r[c][e + 1]));
+                        const float2 u = mul2_rn(f, h ? make_float2(w4.z, w4.w) : make_float2(w4.x, w4.y));
+                        ssp[h] = fma2_rn(u, u, ssp[h]);
+                        // v = acc (ws g1), for pass 2
+                        const float2 v = mul2_rn(f, h ? make_float2(c4.z, c4.w) : make_float2(c4.x, c4.y));
+                        r[c][e] = __float_as_uint(v.x);
+                        r[c][e + 1] = __float_as_uint(v.y);
                     }
                 }
                 tmem_st16(tcols(n) + 16 * c, r[c]);
             }
             tmem_wait_st();
-            const float ss = __fadd_rn(__fadd_rn(ssp[0], ssp[1]), __fadd_rn(ssp[2], ssp[3]));
+            const float ss = __fadd_rn(__fadd_rn(ssp[0].x, ssp[0].y), __fadd_rn(ssp[1].x, ssp[1].y));
             const float as = cst[C_AS + (n & 3) * 32 + lane];
             return __fmul_rn(__fmul_rn(as, as), ss);
         };
@@ -383,7 +388,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 break;
             }
             rpend = false;
-            float s2p[4] = {0.f, 0.f, 0.f, 0.f}, mxp[4] = {0.f, 0.f, 0.f, 0.f};  // independent partials
+            // independent partials, the sums two per packed f32x2 register (as in pass 1)
+            float2 s2p[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+            float mxp[4] = {0.f, 0.f, 0.f, 0.f};
+            const float2 sr2 = make_float2(sr, sr);
 #pragma unroll
             for (int c = 0; c < NCH; c++) {
                 uint32_t r[16];
@@ -393,19 +401,18 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 for (int k = 0; k < 4; k++) {
                     float4 *p4 = rp(c, k);
                     const float4 r4 = *p4;
-                    const float4 x4 = make_float4(__fmaf_rn(__uint_as_float(r[4 * k]), sr, r4.x),
-                                                  __fmaf_rn(__uint_as_float(r[4 * k + 1]), sr, r4.y),
-                                                  __fmaf_rn(__uint_as_float(r[4 * k + 2]), sr, r4.z),
-                                                  __fmaf_rn(__uint_as_float(r[4 * k + 3]), sr, r4.w));
-                    *p4 = x4;
-                    s2p[0] = __fmaf_rn(x4.x, x4.x, s2p[0]);
-                    s2p[1] = __fmaf_rn(x4.y, x4.y, s2p[1]);
-                    s2p[2] = __fmaf_rn(x4.z, x4.z, s2p[2]);
-                    s2p[3] = __fmaf_rn(x4.w, x4.w, s2p[3]);
+                    const float2 xa = fma2_rn(make_float2(__uint_as_float(r[4 * k]), __uint_as_float(r[4 * k + 1])), sr2,
+                                              make_float2(r4.x, r4.y));
+                    const float2 xb = fma2_rn(make_float2(__uint_as_float(r[4 * k + 2]), __uint_as_float(r[4 * k + 3])), sr2,
+                                              make_float2(r4.z, r4.w));
+                    *p4 = make_float4(xa.x, xa.y, xb.x, xb.y);
+                    s2p[0] = fma2_rn(xa, xa, s2p[0]);
+                    s2p[1] = fma2_rn(xb, xb, s2p[1]);
                     if constexpr (quant) {
                         // y = x g2 goes back to TMEM for the int8 pass
                         const float4 g4 = *reinterpret_cast<const float4 *>(cst + C_G2 + 16 * c + 4 * k);
-                        const float y[4] = {__fmul_rn(x4.x, g4.x), __fmul_rn(x4.y, g4.y), __fmul_rn(x4.z, g4.z), __fmul_rn(x4.w, g4.w)};
+                        const float2 ya = mul2_rn(xa, make_float2(g4.x, g4.y)), yb = mul2_rn(xb, make_float2(g4.z, g4.w));
+                        const float y[4] = {ya.x, ya.y, yb.x, yb.y};
 #pragma unroll
                         for (int e = 0; e < 4; e++) {
                             mxp[e] = fmaxf(mxp[e], fabsf(y[e]));
@@ -416,7 +423,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 if constexpr (quant) tmem_st16(tcols(n) + 16 * c, r);
             }
             tmem_wait_st();
-            const float ss2 = __fadd_rn(__fadd_rn(s2p[0], s2p[1]), __fadd_rn(s2p[2], s2p[3]));
+            const float ss2 = __fadd_rn(__fadd_rn(s2p[0].x, s2p[0].y), __fadd_rn(s2p[1].x, s2p[1].y));
             const float mx = fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3]));
             if constexpr (quant) store_res(n);  // the new residual is x
             send(1, n, make_float2(ss2, mx));
@@ -450,13 +457,13 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     tmem_ld16(tcols(n) + 16 * c, r);
                     tmem_wait_ld();
                     uint32_t pk[4];
+                    const float2 s2 = make_float2(s, s), mg = make_float2(12582912.0f, 12582912.0f);
 #pragma unroll
                     for (int k = 0; k < 4; k++) {
-                        const uint32_t b0 = __float_as_uint(__fmaf_rn(__uint_as_float(r[4 * k]), s, 12582912.0f));
-                        const uint32_t b1 = __float_as_uint(__fmaf_rn(__uint_as_float(r[4 * k + 1]), s, 12582912.0f));
-                        const uint32_t b2 = __float_as_uint(__fmaf_rn(__uint_as_float(r[4 * k + 2]), s, 12582912.0f));
-                        const uint32_t b3 = __float_as_uint(__fmaf_rn(__uint_as_float(r[4 * k + 3]), s, 12582912.0f));
-                        pk[k] = __byte_perm(__byte_perm(b0, b1, 0x0040), __byte_perm(b2, b3, 0x0040), 0x5410);
+                        const float2 ba = fma2_rn(make_float2(__uint_as_float(r[4 * k]), __uint_as_float(r[4 * k + 1])), s2, mg);
+                        const float2 bb = fma2_rn(make_float2(__uint_as_float(r[4 * k + 2]), __uint_as_float(r[4 * k + 3])), s2, mg);
+                        pk[k] = __byte_perm(__byte_perm(__float_as_uint(ba.x), __float_as_uint(ba.y), 0x0040),
+                                            __byte_perm(__float_as_uint(bb.x), __float_as_uint(bb.y), 0x0040), 0x5410);
                     }
                     // 16-byte chunk c of row `lane` in the 32-byte swizzle of the int8 map
                     *reinterpret_cast<uint4 *>(q8s + lane * 32 + ((c ^ ((lane >> 2) & 1)) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
