@@ -63,3 +63,10 @@ __device__ __forceinline__ float2 add2_rn(float2 a, float2 b) {
     asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)));
     return f2_from(d);
 }
+// gelu_tanh of two values: lane for lane the same operations, so the same bits, as gelu_tanh
+__device__ __forceinline__ float2 gelu_tanh2(float2 v) {
+    const float2 t = fma2_rn(make_float2(0.044715f, 0.044715f), mul2_rn(v, v), make_float2(1.0f, 1.0f));
+    const float2 a = mul2_rn(mul2_rn(make_float2(-2.302208198144325f, -2.302208198144325f), v), t);
+    const float2 d = add2_rn(make_float2(1.0f, 1.0f), make_float2(ex2_fast(a.x), ex2_fast(a.y)));
+    return mul2_rn(v, make_float2(rcp_fast(d.x), rcp_fast(d.y)));
+}

@@ -244,19 +244,22 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 tmem_ld16(tg + HC + 16 * c, ru);
                 tmem_wait_ld();
 #pragma unroll
-                for (int k = 0; k < 4; k++) {
-                    const float4 wg = *reinterpret_cast<const float4 *>(cst + 16 * c + 4 * k);
-                    const float4 wu = *reinterpret_cast<const float4 *>(cst + C_WU + 16 * c + 4 * k);
-                    const float wgv[4] = {wg.x, wg.y, wg.z, wg.w}, wuv[4] = {wu.x, wu.y, wu.z, wu.w};
-#pragma unroll
-                    for (int e = 0; e < 4; e++) {
-                        const int j = 4 * k + e;
-                        const float g = __fmul_rn(__int2float_rn((int)rg[j]), __fmul_rn(as, wgv[e]));
-                        const float u = __fmul_rn(__int2float_rn((int)ru[j]), __fmul_rn(as, wuv[e]));
-                        const float h = __fmul_rn(gelu_tanh(g), u);
-                        amp[e] = fmaxf(amp[e], fabsf(h));
-                        rg[j] = __float_as_uint(h);
-                    }
+                for (int k = 0; k < 8; k++) {
+                    // columns j, j + 1 per packed f32x2 operation (lane for lane the scalar epilogue's
+                    // operations: the same bits)
+                    const int j = 2 * k;
+                    const float2 wg = *reinterpret_cast<const float2 *>(cst + 16 * c + j);
+                    const float2 wu = *reinterpret_cast<const float2 *>(cst + C_WU + 16 * c + j);
+                    const float2 as2 = make_float2(as, as);
+                    const float2 g = mul2_rn(make_float2(__int2float_rn((int)rg[j]), __int2float_rn((int)rg[j + 1])),
+                                             mul2_rn(as2, wg));
+                    const float2 u = mul2_rn(make_float2(__int2float_rn((int)ru[j]), __int2float_rn((int)ru[j + 1])),
+                                             mul2_rn(as2, wu));
+                    const float2 h = mul2_rn(gelu_tanh2(g), u);
+                    amp[j & 3] = fmaxf(amp[j & 3], fabsf(h.x));
+                    amp[(j + 1) & 3] = fmaxf(amp[(j + 1) & 3], fabsf(h.y));
+                    rg[j] = __float_as_uint(h.x);
+                    rg[j + 1] = __float_as_uint(h.y);
                 }
                 tmem_st16(tg + 16 * c, rg);
             }
