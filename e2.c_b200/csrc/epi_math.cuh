@@ -37,7 +37,9 @@ __device__ __forceinline__ uint32_t pack_low_bytes(uint32_t b0, uint32_t b1, uin
 
 // Two fp32 lanes per instruction (sm_100's packed f32x2 FMA pipe): each lane is the IEEE
 // round-to-nearest result of the scalar operation, so these give the same bits as two __fmul_rn /
-// __fmaf_rn / __fadd_rn while issuing half the instructions.
+// __fmaf_rn / __fadd_rn while issuing half the instructions. A mul2_rn whose result feeds an
+// add2_rn has been seen to round like one fused operation (an exact .5 tie came out 1 ulp apart),
+// so no kernel here feeds a packed product into a packed add where the bits matter.
 __device__ __forceinline__ unsigned long long f2_bits(float2 v) {
     unsigned long long r;
     asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(v.x), "f"(v.y));
