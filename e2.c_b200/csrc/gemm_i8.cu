@@ -83,20 +83,6 @@ __device__ __forceinline__ void stage_f32x16(uint8_t *buf, int lane, const float
         *reinterpret_cast<float4 *>(row + ((c ^ ((lane >> 1) & 3)) << 4)) =
             make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
 }
-// 16 bf16 values into chunks [c0, c0 + 2) of the row
-__device__ __forceinline__ void stage_bf16x16(uint8_t *buf, int lane, int c0, const float (&v)[16]) {
-    uint8_t *row = buf + lane * 64;
-#pragma unroll
-    for (int c = 0; c < 2; c++) {
-        uint32_t w[4];
-#pragma unroll
-        for (int j = 0; j < 4; j++) {
-            const __nv_bfloat162 h = __floats2bfloat162_rn(v[8 * c + 2 * j], v[8 * c + 2 * j + 1]);
-            w[j] = *reinterpret_cast<const uint32_t *>(&h);
-        }
-        *reinterpret_cast<uint4 *>(row + (((c0 + c) ^ ((lane >> 1) & 3)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
-    }
-}
 // hand a staged tile to the TMA engine (one lane), after every lane's writes are visible to it
 __device__ __forceinline__ void stage_store(const CUtensorMap *m, uint8_t *buf, int x, int y, int lane) {
     fence_proxy_async_smem();
