@@ -56,7 +56,9 @@ def peaks() -> dict:
 
 # ------------------------------------------------------------------------------------ clocks
 class ClockSampler:
-    """nvidia-smi sampled every 200 ms while the timed region runs (read-only queries)."""
+    """nvidia-smi sampled every 100 ms (read-only queries). Started before the warm-up; the host marks
+    the timed region with mark_start() / mark_end() and the summary covers the samples taken inside
+    it, or, when the region is shorter than a few sampling periods, those of warm-up and region."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -65,7 +67,9 @@ class ClockSampler:
     def __init__(self, index: int):
         self.index = index
         self.proc = None
-        self.lines: list[str] = []
+        self.lines: list[tuple[float, str]] = []
+        self.t0 = self.t1 = None
+        self.started = threading.Event()
 
     def __enter__(self):
         try:
@@ -74,16 +78,25 @@ class ClockSampler:
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
+            self.started.wait(timeout=5.0)  # the first sample is in before anything is timed
         except OSError:
             self.proc = None
         return self
 
     def _read(self):
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            self.lines.append((time.perf_counter(), line.strip()))
+            self.started.set()
+
+    def mark_start(self):
+        self.t0 = time.perf_counter()
+
+    def mark_end(self):
+        self.t1 = time.perf_counter()
 
     def __exit__(self, *a):
         if self.proc:
+            time.sleep(0.25)  # one more sample after the region
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
@@ -91,9 +104,14 @@ class ClockSampler:
                 self.proc.kill()
 
     def summary(self) -> dict:
-        sm, smax, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        window = "timed region"
+        rows = [ln for t, ln in self.lines if self.t0 is not None and self.t0 <= t <= (self.t1 or t)]
+        if len(rows) < 3:
+            window = "warm-up and timed region (region shorter than 3 sampling periods)"
+            rows = [ln for t, ln in self.lines if self.t1 is None or t <= self.t1 + 0.15]
+        sm, smax, reasons = [], None, set()
+        for ln in rows:
             f = [x.strip() for x in ln.split(",")]
             if len(f) < 9:
                 continue
@@ -106,7 +124,30 @@ class ClockSampler:
                 if v.lower().startswith("active"):
                     reasons.add(n)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax, "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "samples": len(sm), "window": window}
+
+
+def cpu_info(threads: int) -> dict:
+    """The host CPU the baseline ran on: model, ISA flags the reference kernels use, logical CPUs,
+    the threads used and their pinning (the process's CPU affinity)."""
+    model, flags = None, set()
+    try:
+        for ln in open("/proc/cpuinfo"):
+            if model is None and ln.startswith("model name"):
+                model = ln.split(":", 1)[1].strip()
+            if ln.startswith("flags"):
+                for f in ln.split(":", 1)[1].split():
+                    if f.startswith(("avx512", "amx")) or f in ("avx_vnni", "avx2", "fma"):
+                        flags.add(f)
+    except OSError:
+        pass
+    try:
+        aff = sorted(os.sched_getaffinity(0))
+    except (AttributeError, OSError):
+        aff = []
+    return {"cpu_model": model, "isa": sorted(flags), "nproc": os.cpu_count(), "threads": threads,
+            "pinning": f"process affinity {len(aff)} CPUs ({aff[0]}-{aff[-1]})" if aff else "unknown",
+            "pool": "reference thread pool (src/threads.c), one worker per thread, capped at 64"}
 
 
 # ------------------------------------------------------------------------------------ distributed
@@ -161,10 +202,12 @@ def cpu_reference(seqs: int, seq_len: int, steps: int, warmup: int, weights, rng
         if budget_s is not None and time.perf_counter() - t_start > budget_s and len(times) >= 1:
             break
     total = sum(times)
-    info = {"kind": kind, "cores": nthreads if kind == "reference" else 1,
+    cores = nthreads if kind == "reference" else 1
+    info = {"kind": kind, "cores": cores,
             "sample": f"{len(times)} x {seqs} sequences x {seq_len} tokens of the 24-layer encoder "
                       f"({'reference e2.c AVX512-VNNI kernels + thread pool' if kind == 'reference' else 'plain-C port'}), "
                       f"host {os.cpu_count()} logical CPUs"}
+    info.update(cpu_info(cores))
     return done / total, info
 
 
@@ -186,6 +229,10 @@ def main() -> int:
     ap.add_argument("--config4", action="store_true",
                     help="benchmark config 4: log-uniform lengths, length-bucketed, LPT-sharded over the GPUs")
     ap.add_argument("--sequences", type=int, default=65536, help="sequences of the config-4 job")
+    ap.add_argument("--cpu-subsample", type=int, default=64,
+                    help="config 4: time the reference CPU path on every n-th sequence by length (0: skip)")
+    ap.add_argument("--config0", action="store_true", help="benchmark config 0: one quantised linear layer")
+    ap.add_argument("--config1", action="store_true", help="benchmark config 1: the int8 gated FFN block")
     args = ap.parse_args()
     if args.kernel:
         return kernel_only(args)
@@ -193,6 +240,10 @@ def main() -> int:
         return gemm_sweep(args)
     if args.config4:
         return config4(args)
+    if args.config0:
+        return config0(args)
+    if args.config1:
+        return config1(args)
 
     import torch
 
@@ -249,21 +300,23 @@ def main() -> int:
             with torch.cuda.stream(stream):
                 dist.all_gather_into_tensor(gathered, out)
 
-    with torch.cuda.stream(stream):
-        for _ in range(max(args.warmup, 3)):
-            step()
-    e2c.check(stream)
-    if dist:
-        dist.barrier()
-    torch.cuda.synchronize()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
+        with torch.cuda.stream(stream):
+            for _ in range(max(args.warmup, 3)):
+                step()
+        e2c.check(stream)
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+        clk.mark_start()
         with torch.cuda.stream(stream):
             ev0.record(stream)
             for _ in range(args.steps):
                 step()
             ev1.record(stream)
         torch.cuda.synchronize()
+        clk.mark_end()
     e2c.check(stream)
     ms = ev0.elapsed_time(ev1)
     ms = max_over_ranks(dist, ms, dev)
@@ -292,7 +345,11 @@ def main() -> int:
         table = kernel_table(dev, stream)
         roof = dominant_roofline(table)
     cpu = None
-    if rank == 0 and not args.no_cpu_baseline:
+    if world > 1:
+        # timed on rank 0 at N = 1 only: with N > 1 the other ranks' NCCL progress threads poll on the
+        # same host cores and the sample would measure that contention
+        cpu = {"value": None, "unit": UNIT, "note": "the CPU baseline is timed at N=1 only (bench.py --gpus 1)"}
+    elif not args.no_cpu_baseline:
         try:
             v, info = cpu_reference(2, SEQ, 3, 1, w, np.random.default_rng(9), budget_s=30.0)
             cpu = dict(info, value=v, unit=UNIT)
@@ -341,7 +398,8 @@ def config4(args) -> int:
     rng = np.random.default_rng(44)  # the same job on every rank
     lengths = shard.log_uniform_lengths(rng, args.sequences)
     padded = shard.bucket_length(lengths, 64)
-    mine = shard.lpt_assign(shard.sequence_cost(padded, cfg.n_layers), world)[rank]
+    shares = shard.lpt_assign(shard.sequence_cost(padded, cfg.n_layers), world)
+    mine = shares[rank]
     passes = shard.plan_passes(mine, padded, args.chunk)
     tok_rng = np.random.default_rng(45 + rank)
     dev_passes = []
@@ -362,26 +420,53 @@ def config4(args) -> int:
                 enc.embed_batch_device(ids, valid, out, stream)
                 emb.index_copy_(0, r, out)
             if dist:
-                return shard.gather_embeddings(dist, mine, emb, args.sequences, device=dev)
+                return shard.gather_embeddings(dist, shares, emb, args.sequences, device=dev)
         return emb
 
-    for _ in range(2):  # every pass shape runs eagerly once, then is captured as a CUDA graph
-        run()
-    e2c.check(stream)
-    if dist:
-        dist.barrier()
-    torch.cuda.synchronize()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    mids = []  # per step: this rank's passes done, before the gather
     with ClockSampler(local) as clk:
+        for _ in range(2):  # every pass shape runs eagerly once, then is captured as a CUDA graph
+            run()
+        e2c.check(stream)
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+        clk.mark_start()
         ev0.record(stream)
         for _ in range(args.steps):
-            run()
+            with torch.cuda.stream(stream):
+                st = torch.cuda.Event(enable_timing=True)
+                st.record(stream)
+                for (ids, valid, out, _), r in zip(dev_passes, rows):
+                    enc.embed_batch_device(ids, valid, out, stream)
+                    emb.index_copy_(0, r, out)
+                m = torch.cuda.Event(enable_timing=True)
+                m.record(stream)
+                mids.append((st, m))
+                if dist:
+                    shard.gather_embeddings(dist, shares, emb, args.sequences, device=dev)
         ev1.record(stream)
         torch.cuda.synchronize()
+        clk.mark_end()
     e2c.check(stream)
-    ms = max_over_ranks(dist, ev0.elapsed_time(ev1), dev) / args.steps
+    total = ev0.elapsed_time(ev1)
+    # this rank's own share of the step (its passes) and the gather's, averaged over the steps
+    compute = sum(a.elapsed_time(b) for a, b in mids) / args.steps
+    per_rank = torch.tensor([total / args.steps, compute], dtype=torch.float64, device=dev)
+    if dist:
+        allr = torch.zeros((world, 2), dtype=torch.float64, device=dev)
+        dist.all_gather_into_tensor(allr, per_rank[None, :])
+        per_rank_list = allr.cpu().numpy()
+    else:
+        per_rank_list = per_rank.cpu().numpy()[None, :]
+    ms = float(per_rank_list[:, 0].max())
+    cpu = None
+    if rank == 0 and world == 1 and args.cpu_subsample > 0:
+        cpu = config4_cpu(w, lengths, args.cpu_subsample)
     if rank == 0:
         tokens = int(lengths.sum())
+        fin = per_rank_list[:, 1]
         print(json.dumps({"metric": "config-4 embeddings/sec (log-uniform lengths, length-bucketed, LPT-sharded)",
                           "value": args.sequences / (ms / 1e3), "unit": "embeddings/s", "n_gpus": world,
                           "steps": args.steps, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
@@ -389,11 +474,236 @@ def config4(args) -> int:
                           "dtype": "int8", "data": "synthetic (seeded lengths and token ids, random-init weights)",
                           "config": {"workload": "config 4", "sequences": args.sequences, "tokens": tokens,
                                      "bucket": 64, "tokens_per_pass": args.chunk, "passes_rank0": len(passes)},
-                          "clocks": clk.summary()}))
+                          "per_rank_passes_ms": [round(float(v), 3) for v in fin],
+                          "rank_spread": {"min_ms": float(fin.min()), "max_ms": float(fin.max()),
+                                          "imbalance": float(fin.max() / fin.mean()) if fin.mean() > 0 else None,
+                                          "gather_and_rest_ms": float(ms - fin.max())},
+                          "clocks": clk.summary(), "cpu_baseline": cpu}))
     enc.close()
     if dist:
         dist.barrier()
         dist.destroy_process_group()
+    return 0
+
+
+def config4_cpu(w, lengths: np.ndarray, every: int, budget_s: float = 240.0) -> dict:
+    """The reference CPU path on a stratified 1/`every` subsample of the config-4 job (every n-th
+    sequence in length order, each at its own length, in a seeded random order), extrapolated to the
+    whole job. If the budget runs out first, the part done (a random subset of the subsample) is
+    extrapolated instead, and the fraction is stated."""
+    sys.path.insert(0, str(ROOT))
+    from oracle import oracle_ffi as of
+
+    kind = "reference" if of.mux() is not None else "port"
+    nthreads = of.mux().e2refmux_init(str(of.REF_DIR).encode(), 0) if kind == "reference" else 1
+    order = np.argsort(lengths, kind="stable")
+    sub = order[every // 2::every]
+    rng = np.random.default_rng(46)
+    sub = sub[rng.permutation(len(sub))]
+    done_tok, done_seq, t_used = 0, 0, 0.0
+    for i in sub:
+        n = int(lengths[i])
+        ids = rng.integers(2, w.cfg.vocab, size=(1, n), dtype=np.int32)
+        t0 = time.perf_counter()
+        of.encoder_forward(kind, w, ids)
+        t_used += time.perf_counter() - t0
+        done_tok += n
+        done_seq += 1
+        if t_used > budget_s:
+            break
+    frac = done_seq / len(sub)
+    scale = len(lengths) / done_seq
+    est_s = t_used * scale
+    return dict({"kind": kind, "cores": nthreads, "value": len(lengths) / est_s, "unit": "embeddings/s",
+                 "tokens_per_s": done_tok / t_used, "extrapolated_job_s": est_s,
+                 "sample": f"{done_seq} of a stratified 1/{every} subsample ({len(sub)} sequences; "
+                           f"{frac:.0%} done within the {budget_s:.0f} s budget), each sequence at its own length, "
+                           f"extrapolated x{scale:.1f} to the {len(lengths)}-sequence job"}, **cpu_info(nthreads))
+
+
+def _roof(ops: float, nbytes: float, ms: float) -> dict:
+    """Both fractions of a run of `ops` int8 operations over `nbytes` algorithmic bytes in `ms`,
+    against the measured peaks (int8 dense = 2 x measured bf16)."""
+    p = peaks()
+    t = ms / 1e3
+    tops, gbs = ops / t / 1e12, nbytes / t / 1e9
+    int8_peak = 2.0 * p["bf16_tflops"]
+    bound = "tensor" if ops / (int8_peak * 1e12) >= nbytes / (p["hbm_gbs"] * 1e9) else "hbm"
+    return {"us": ms * 1e3, "tops": tops, "gbs": gbs, "frac_int8_peak": tops / int8_peak,
+            "frac_hbm": gbs / p["hbm_gbs"], "bound": bound,
+            "frac_of_roofline": (tops / int8_peak) if bound == "tensor" else (gbs / p["hbm_gbs"]),
+            "peak_src": f"{p['src']}: HBM {p['hbm_gbs']} GB/s, int8 2 x {p['bf16_tflops']} TFLOP/s"}
+
+
+def _best_cpu(fn, warmup: int = 2, reps: int = 5, budget_s: float = 20.0) -> float:
+    """Best wall time (s) of `fn` after warm-ups (the reference's own rule, PERFORMANCE.md:19-24)."""
+    for _ in range(warmup):
+        fn()
+    best, t_end = math.inf, time.perf_counter() + budget_s
+    for i in range(reps):
+        t0 = time.perf_counter()
+        fn()
+        best = min(best, time.perf_counter() - t0)
+        if time.perf_counter() > t_end and i >= 1:
+            break
+    return best
+
+
+def config0(args) -> int:
+    """Benchmark config 0: y = int8 GEMM(quantise(X)) for X [512][768] N(0,1) with four outlier
+    channels x20 and W [1152][768] N(0,0.02) quantised per row by the reference's own weight
+    quantiser. Device: the quantiser + GEMM kernels over resident X (L2 flushed before every step);
+    e2e: the reference-signature host drop-ins (e2cuda_i8_quantize_host then e2cuda_i8_gemm_host,
+    host buffers, copies inside). Beside them the reference's quantise + N-split GEMM region
+    (e2ref_linear over its pool) on the host cores."""
+    import ctypes as C
+
+    import torch
+
+    sys.path.insert(0, str(ROOT))
+    from oracle import oracle_ffi as of
+
+    e2c = load_pkg()
+    import e2c_b200.synthetic as syn
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    stream = torch.cuda.Stream(device=dev)
+    M, K, N = 512, 768, 1152
+    rng = np.random.default_rng(0xE2C0DE + 0)
+    x = syn.activations(rng, M, K)
+    wf = (rng.standard_normal((N, K), dtype=np.float32) * np.float32(0.02)).astype(np.float32)
+    ref = of.ref(K)
+    wq = of.Weight(wf, K, lib=ref) if ref is not None else of.Weight(wf, K)
+    W = e2c.Weight(q8w=C.cast(C.byref(wq.q), C.POINTER(e2c.Q8W)).contents)
+    xd = torch.from_numpy(x).to(dev)
+    q = torch.empty((M, K), dtype=torch.int8, device=dev)
+    qs = torch.empty((M, 1), dtype=torch.float32, device=dev)
+    y = torch.empty((M, N), dtype=torch.float32, device=dev)
+    lib = e2c.lib()
+    ep = e2c.Epilogue()
+
+    def run():
+        e2c._ok(lib.e2cuda_quantize_rows(xd.data_ptr(), q.data_ptr(), qs.data_ptr(), M, K, K, -math.inf, math.inf,
+                                         stream.cuda_stream), "quantize")
+        e2c._ok(lib.e2cuda_i8_gemm(C.byref(W.w8), q.data_ptr(), qs.data_ptr(), M, K, 0, N, C.byref(ep), y.data_ptr(),
+                                   N, stream.cuda_stream), "gemm")
+
+    ms = timed_launches(run, stream, max(args.warmup, 3), args.steps)
+    e2c.check(stream)
+    ops = 2.0 * M * N * K
+    nbytes = 4 * M * K + N * K + 4 * N + 4 * M * N  # x in, W + scales, y out (q stays on chip / in L2)
+    # e2e through the reference-signature host drop-ins
+    lib.e2cuda_set_act_block(K)
+    qa_h = np.empty((M, K), np.int8)
+    as_h = np.empty((M, 1), np.float32)
+    y_h = np.empty((M, N), np.float32)
+
+    def host_call():
+        lib.e2cuda_i8_quantize_host(qa_h.ctypes.data_as(e2c.i8p), as_h.ctypes.data_as(e2c.f32p),
+                                    x.ctypes.data_as(e2c.f32p), M, K, -math.inf, math.inf)
+        lib.e2cuda_i8_gemm_host(y_h.ctypes.data_as(e2c.f32p), qa_h.ctypes.data_as(e2c.i8p), as_h.ctypes.data_as(e2c.f32p),
+                                C.cast(C.byref(wq.q), C.POINTER(e2c.Q8W)), M, N, 0, N)
+
+    for _ in range(3):
+        host_call()
+    if e2c.last_error():
+        raise RuntimeError(e2c.last_error())
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        host_call()
+    e2e_ms = (time.perf_counter() - t0) * 1e3 / args.steps
+    cpu = None
+    if ref is not None:
+        qa_c = np.empty((M, K), np.int8)
+        as_c = np.empty((M, 1), np.float32)
+        y_c = np.empty((M, N), np.float32)
+        nthreads = ref.e2ref_init(0)
+        t = _best_cpu(lambda: ref.e2ref_linear(x.ctypes.data_as(of.f32p), M, K, C.byref(wq.q), qa_c.ctypes.data_as(of.i8p),
+                                               as_c.ctypes.data_as(of.f32p), y_c.ctypes.data_as(of.f32p)))
+        cpu = dict(_roof(ops, nbytes, t * 1e3), kind="reference", cores=nthreads,
+                   sample="quantise + N-split int8 GEMM region of e2.c (e2_quantize_blocks_avx512 + e2_i8_gemm_avx512, "
+                          "E2_I8_BLOCK=768) over its pool, best of 5 after 2 warm-ups", **cpu_info(nthreads))
+    print(json.dumps({"metric": "config-0 quantised linear layer time", "value": ms * 1e3, "unit": "us",
+                      "higher_is_better": False, "steps": args.steps, "dtype": "int8",
+                      "data": "synthetic (seeded, BASELINE config 0)",
+                      "config": {"workload": "config 0: quantise X [512][768] + W8A8 GEMM -> fp32 [512][1152], per-row scales",
+                                 "l2": "flushed before every step", "kernels_per_step": 2},
+                      "roofline": _roof(ops, nbytes, ms), "algorithmic_bytes": nbytes, "ops": ops,
+                      "e2e": {"value": e2e_ms * 1e3, "unit": "us", "api": "e2cuda_i8_quantize_host + e2cuda_i8_gemm_host",
+                              "h2d_bytes_per_step": 4 * M * K + M * K + 4 * M, "d2h_bytes_per_step": M * K + 4 * M + 4 * M * N},
+                      "cpu_baseline": cpu}))
+    return 0
+
+
+def config1(args) -> int:
+    """Benchmark config 1: the int8 gated FFN block at M = 4096 tokens (RMSNorm -> quantise -> gate|up
+    768->2x1152 -> GELU-tanh(gate)*up -> quantise -> down 1152->768 + residual) through
+    e2cuda_ffn_forward (3 kernels). Device time over resident x (L2 flushed before every step); e2e
+    with pinned host x / y and the copies inside; beside them the reference's own kernels running the
+    same block over its pool on the host cores."""
+    import torch
+
+    sys.path.insert(0, str(ROOT))
+    from oracle import oracle_ffi as of
+
+    e2c = load_pkg()
+    import e2c_b200.synthetic as syn
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    stream = torch.cuda.Stream(device=dev)
+    rng = np.random.default_rng(0xE2C0DE + 1)
+    M, D, I = 4096, 768, 1152
+    x = rng.standard_normal((M, D), dtype=np.float32)
+    g = (1 + 0.1 * rng.standard_normal(D)).astype(np.float32)
+    wg, wu = syn.packed_weight(rng, I, D, 0.02, D), syn.packed_weight(rng, I, D, 0.02, D)
+    wd = syn.packed_weight(rng, D, I, 0.02, I)
+    qs = [e2c.Q8W() for _ in range(3)]
+    for qq, ww in zip(qs, (wg, wu, wd)):
+        ww.fill(qq)
+    ffn = e2c.FFN(qs[0], qs[1], qs[2], g, 1e-6, M)
+    xd = torch.from_numpy(x).to(dev)
+    yd = torch.empty_like(xd)
+    ms = timed_launches(lambda: ffn.forward(xd, yd, stream), stream, max(args.warmup, 3), args.steps)
+    e2c.check(stream)
+    ops = 2.0 * M * (D * 2 * I + I * D)
+    nbytes = 4 * M * D + (2 * I * D + D * I) + 4 * (2 * I + D) + 4 * M * D + 4 * D  # x in, weights, y out, gamma
+    x_pin = torch.from_numpy(x).pin_memory()
+    y_pin = torch.empty((M, D), dtype=torch.float32).pin_memory()
+
+    def e2e_step():
+        with torch.cuda.stream(stream):
+            xd.copy_(x_pin, non_blocking=True)
+            ffn.forward(xd, yd, stream)
+            y_pin.copy_(yd, non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / args.steps
+    cpu = None
+    if of.mux() is not None:
+        nthreads = of.mux().e2refmux_init(str(of.REF_DIR).encode(), 0)
+        t = _best_cpu(lambda: of.ffn_block("reference", x, g, 1e-6, wg, wu, wd, ablk=0))
+        cpu = dict(_roof(ops, nbytes, t * 1e3), kind="reference", cores=nthreads,
+                   sample="the same block on e2.c's own kernels (per-row builds) over its pool, best of 5 after 2 warm-ups",
+                   **cpu_info(nthreads))
+    print(json.dumps({"metric": "config-1 int8 FFN block time", "value": ms * 1e3, "unit": "us",
+                      "higher_is_better": False, "steps": args.steps, "dtype": "int8",
+                      "data": "synthetic (seeded, BASELINE config 1)",
+                      "config": {"workload": "config 1: FFN block, M=4096, D=768, I=1152, per-token scales",
+                                 "l2": "flushed before every step", "kernels_per_step": 3},
+                      "roofline": _roof(ops, nbytes, ms), "algorithmic_bytes": nbytes, "ops": ops,
+                      "e2e": {"value": e2e_ms * 1e3, "unit": "us", "api": "e2cuda_ffn_forward, pinned host x/y",
+                              "h2d_bytes_per_step": 4 * M * D, "d2h_bytes_per_step": 4 * M * D},
+                      "cpu_baseline": cpu}))
     return 0
 
 

@@ -2,7 +2,7 @@
 
 The product is ``libe2cuda.so`` in this directory: sm_100a kernels plus a C11 host library. This
 module binds it with ctypes so tests and ``bench.py`` call the same entry points an e2.c build would
-bind (see INTEGRATION.md). Device buffers are torch CUDA tensors, used only as memory and streams.
+bind. Device buffers are torch CUDA tensors, used only as memory and streams.
 
 The directory name contains a dot, so import it by path::
 

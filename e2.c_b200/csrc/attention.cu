@@ -35,6 +35,7 @@
 #include <stdint.h>
 
 #include "launch.h"
+#include "devstate.cuh"
 #include "pdl.h"
 #include "ptx.cuh"
 #include "tmap.h"
@@ -503,8 +504,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
 }
 
-int g_attn_sms = 0;
-
 }  // namespace
 
 extern "C" int e2c_attention(const void *q, const void *k, const void *vt, int ldvt, const uint8_t *valid, float *ctx,
@@ -518,16 +517,19 @@ extern "C" int e2c_attention(const void *q, const void *k, const void *vt, int l
         e2c_set_msg("attention: ctx must be 16-byte aligned");
         return -1;
     }
-    static bool attr = false;
-    if (!attr) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        if (cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_ALLOC) != cudaSuccess ||
-            cudaDeviceGetAttribute(&g_attn_sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || g_attn_sms <= 0) {
+    static E2cPerDev attr;  // the shared-memory opt-in, per device
+    const int dev = e2c_device();
+    const int num_sms = e2c_sm_count(dev);
+    if (!num_sms) {
+        e2c_set_msg("attention: no CUDA device");
+        return -2;
+    }
+    if (!attr.get(dev)) {
+        if (cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_ALLOC) != cudaSuccess) {
             e2c_set_msg("attention: cannot reserve %d bytes of shared memory", SMEM_ALLOC);
             return -2;
         }
-        attr = true;
+        attr.set(dev, 1);
     }
     CUtensorMap tq, tk, tv, to;
     const uint64_t rows = (uint64_t)B * S;
@@ -546,7 +548,7 @@ extern "C" int e2c_attention(const void *q, const void *k, const void *vt, int l
     a.units = B * H * a.nqt;
     a.scale_log2 = scale * 1.4426950408889634f;
     a.status = status;
-    const int grid = a.units < g_attn_sms ? a.units : g_attn_sms;
+    const int grid = a.units < num_sms ? a.units : num_sms;
     e2c_launch(k_attention, dim3(grid), dim3(NTHREADS), SMEM_ALLOC, (cudaStream_t)stream, tq, tk, tv, to, a);
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {

@@ -255,11 +255,12 @@ int e2cuda_attention(const void *q, const void *k, const void *vt, int ldvt, con
 /* ------------------------------------------------------------------ fused FFN (config 1) */
 struct e2cuda_ffn {
     int D, I, max_tokens;
+    int fused; /* gate|up + GELU + h's quantiser in one kernel (E2C_EPI_GELUQ), h never stored */
     float eps;
     e2cuda_w8 wgu, wd; /* gate|up interleaved per 128 rows */
     float *gamma;
-    int8_t *qa;
-    float *qs, *h;
+    int8_t *qa, *qh;   /* quantised normed x [M][D]; quantised h [M][I] */
+    float *qs, *qhs, *h;
 };
 
 /* gate|up interleaved per 128 rows: [g0..127 | u0..127 | g128..255 | u128..255 | ...] so one
@@ -313,11 +314,16 @@ e2cuda_ffn *e2cuda_ffn_create(const e2cuda_q8w *gate, const e2cuda_q8w *up, cons
     f->eps = eps;
     f->max_tokens = max_tokens;
     const size_t M = (size_t)max_tokens;
+    const char *env = getenv("E2C_FUSED_GELU");
+    f->fused = f->I % 128 == 0 && f->I / 128 <= 16 && !(env && env[0] == '0') &&
+               e2c_gemm_gelu_quant_supported(f->I / 128);
     if (e2cu_upload_gate_up(gate, up, &f->wgu) || e2cuda_w8_from_q8w(down, &f->wd) ||
         e2cu_cuda(cudaMalloc((void **)&f->gamma, sizeof(float) * f->D), "ffn alloc") ||
         e2cu_cuda(cudaMalloc((void **)&f->qa, M * (size_t)(f->I > f->D ? f->I : f->D)), "ffn alloc") ||
         e2cu_cuda(cudaMalloc((void **)&f->qs, M * sizeof(float)), "ffn alloc") ||
-        e2cu_cuda(cudaMalloc((void **)&f->h, M * (size_t)f->I * sizeof(float)), "ffn alloc") ||
+        (f->fused ? (e2cu_cuda(cudaMalloc((void **)&f->qh, M * (size_t)f->I), "ffn alloc") ||
+                     e2cu_cuda(cudaMalloc((void **)&f->qhs, M * sizeof(float)), "ffn alloc"))
+                  : e2cu_cuda(cudaMalloc((void **)&f->h, M * (size_t)f->I * sizeof(float)), "ffn alloc")) ||
         e2cu_cuda(cudaMemcpy(f->gamma, gamma, sizeof(float) * f->D, cudaMemcpyHostToDevice), "ffn upload")) {
         e2cuda_ffn_destroy(f);
         return NULL;
@@ -332,6 +338,8 @@ void e2cuda_ffn_destroy(e2cuda_ffn *f) {
     cudaFree(f->gamma);
     cudaFree(f->qa);
     cudaFree(f->qs);
+    cudaFree(f->qh);
+    cudaFree(f->qhs);
     cudaFree(f->h);
     free(f);
 }
@@ -346,14 +354,25 @@ int e2cuda_ffn_forward(e2cuda_ffn *f, const float *x, int M, float *y, void *str
         return -1;
     e2c_gemm_args a;
     e2cu_gemm_args(&a, &f->wgu, f->qa, f->qs, M, f->D);
-    a.epi = E2C_EPI_GELU;
-    a.y = f->h;
-    a.ldy = f->I;
-    if (e2cu_launch(e2c_gemm(&a, stream), "ffn gate|up")) return -1;
-    if (e2cu_launch(e2c_quantize(f->h, f->I, f->qa, f->I, f->qs, M, f->I, f->I, -INFINITY, INFINITY, 0, stream),
-                    "ffn quantize"))
-        return -1;
-    e2cu_gemm_args(&a, &f->wd, f->qa, f->qs, M, f->I);
+    if (f->fused) {
+        /* gate_quant (src/text.c:424-468) in the gate|up GEMM's epilogue: bit-identical to the
+         * GELU epilogue followed by the quantiser */
+        a.epi = E2C_EPI_GELUQ;
+        a.q8 = f->qh;
+        a.ldq = f->I;
+        a.q8_scale = f->qhs;
+        if (e2cu_launch(e2c_gemm(&a, stream), "ffn gate|up + quantise")) return -1;
+        e2cu_gemm_args(&a, &f->wd, f->qh, f->qhs, M, f->I);
+    } else {
+        a.epi = E2C_EPI_GELU;
+        a.y = f->h;
+        a.ldy = f->I;
+        if (e2cu_launch(e2c_gemm(&a, stream), "ffn gate|up")) return -1;
+        if (e2cu_launch(e2c_quantize(f->h, f->I, f->qa, f->I, f->qs, M, f->I, f->I, -INFINITY, INFINITY, 0, stream),
+                        "ffn quantize"))
+            return -1;
+        e2cu_gemm_args(&a, &f->wd, f->qa, f->qs, M, f->I);
+    }
     a.epi = E2C_EPI_RESID;
     a.y = y;
     a.ldy = f->D;

@@ -31,6 +31,7 @@
 
 #include "launch.h"
 #include "epi_math.cuh"
+#include "devstate.cuh"
 #include "pdl.h"
 #include "ptx.cuh"
 #include "tmap.h"
@@ -752,20 +753,18 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
 }
 
-int g_num_sms = 0;
-
 template <int BN, int STAGES, bool PERBLOCK, int EPI, int CG>
-int launch(const e2c_gemm_args *a, cudaStream_t st) {
+int launch(const e2c_gemm_args *a, cudaStream_t st, int dev, int num_sms) {
     using L = GemmSmem<BN, STAGES, PERBLOCK, EPI, CG>;
     auto kern = k_gemm_i8<BN, STAGES, PERBLOCK, EPI, CG>;
-    static bool attr_set = false;
-    static int max_pairs = 0;  // CTA pairs the device holds at once (CG = 2)
-    if (!attr_set) {
+    static E2cPerDev attr_set;   // the shared-memory opt-in, per device
+    static E2cPerDev max_pairs;  // CTA pairs the device holds at once (CG = 2)
+    if (!attr_set.get(dev)) {
         if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC) != cudaSuccess) {
             e2c_set_msg("gemm: cannot reserve %d bytes of shared memory", L::ALLOC);
             return -2;
         }
-        attr_set = true;
+        attr_set.set(dev, 1);
     }
     CUtensorMap ta, tb, t0, t1;
     if (e2c_tmap_2d(&ta, a->a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)a->K, (uint64_t)a->M, (uint64_t)a->lda,
@@ -796,7 +795,7 @@ int launch(const e2c_gemm_args *a, cudaStream_t st) {
     const int tiles = ((a->M + BM * CG - 1) / (BM * CG)) * ((a->n1 - a->n0 + BN - 1) / BN);
     cudaError_t e;
     if constexpr (CG == 1) {
-        const int grid = tiles < g_num_sms ? tiles : g_num_sms;
+        const int grid = tiles < num_sms ? tiles : num_sms;
         e = e2c_launch(kern, dim3(grid), dim3(NTHREADS), L::ALLOC, st, ta, tb, t0, t1, *a, tma_out);
     } else {
         cudaLaunchConfig_t cfg;
@@ -811,16 +810,17 @@ int launch(const e2c_gemm_args *a, cudaStream_t st) {
         cfg.stream = st;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
-        if (!max_pairs) {
-            cfg.gridDim = dim3(2 * (g_num_sms / 2));
-            if (cudaOccupancyMaxActiveClusters(&max_pairs, kern, &cfg) != cudaSuccess || max_pairs <= 0) {
+        int pairs = max_pairs.get(dev);
+        if (!pairs) {
+            cfg.gridDim = dim3(2 * (num_sms / 2));
+            if (cudaOccupancyMaxActiveClusters(&pairs, kern, &cfg) != cudaSuccess || pairs <= 0) {
                 cudaGetLastError();
-                max_pairs = 0;
                 e2c_set_msg("gemm: the device cannot hold a pair of GEMM CTAs");
                 return -2;
             }
+            max_pairs.set(dev, pairs);
         }
-        cfg.gridDim = dim3(2 * (tiles < max_pairs ? tiles : max_pairs));
+        cfg.gridDim = dim3(2 * (tiles < pairs ? tiles : pairs));
         cfg.numAttrs = e2c_pdl_attr(attr, 1);
         e = cudaLaunchKernelEx(&cfg, kern, ta, tb, t0, t1, *a, tma_out);
     }
@@ -837,16 +837,16 @@ struct Plan {
     int bn, cg;
 };
 
-Plan pick_plan(const e2c_gemm_args *a) {
+Plan pick_plan(const e2c_gemm_args *a, int num_sms) {
     if (a->ablk != a->K) return {128, 1};                    // per-block fold keeps BN/4 floats per thread
     const int ncols = a->n1 - a->n0;
     const long pairs256 = (long)((a->M + 2 * BM - 1) / (2 * BM)) * ((ncols + 255) / 256);
     // pairs pay off once they fill the device (a full wave of 256-row tiles) and both CTAs of a
     // pair have rows of their own: with M <= 256 the second one would only multiply zeros
-    const int cg = (pairs256 >= g_num_sms / 2 && a->M > 2 * BM) ? 2 : 1;
+    const int cg = (pairs256 >= num_sms / 2 && a->M > 2 * BM) ? 2 : 1;
     if (a->epi == E2C_EPI_GELU || a->epi == E2C_EPI_QKV) return {256, cg};
     // the width whose waves of persistent tiles cost least: a tile's time ~ BN + a fixed 32
-    const int slots = cg == 2 ? g_num_sms / 2 : g_num_sms;
+    const int slots = cg == 2 ? num_sms / 2 : num_sms;
     const long tm = (a->M + BM * cg - 1) / (BM * cg);
     int best = 256;
     long best_cost = -1;
@@ -864,20 +864,19 @@ Plan pick_plan(const e2c_gemm_args *a) {
 }  // namespace
 
 extern "C" void e2c_gemm_tile(const e2c_gemm_args *a, int *bm, int *bn) {
-    if (!g_num_sms) cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, 0);
-    const Plan pl = pick_plan(a);
+    int num_sms = e2c_sm_count(e2c_device());
+    if (!num_sms) num_sms = 148;
+    const Plan pl = pick_plan(a, num_sms);
     *bm = BM * pl.cg;
     *bn = pl.bn;
 }
 
 extern "C" int e2c_gemm(const e2c_gemm_args *a, void *stream) {
-    if (!g_num_sms) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        if (cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || g_num_sms <= 0) {
-            e2c_set_msg("gemm: no CUDA device");
-            return -2;
-        }
+    const int dev = e2c_device();
+    const int num_sms = e2c_sm_count(dev);
+    if (!num_sms) {
+        e2c_set_msg("gemm: no CUDA device");
+        return -2;
     }
     if (a->M < 0 || a->K <= 0 || a->K % 16 || a->lda % 16 || a->ldw % 16 || a->n0 < 0 || a->n1 > a->wrows ||
         a->n0 > a->n1) {
@@ -900,50 +899,50 @@ extern "C" int e2c_gemm(const e2c_gemm_args *a, void *stream) {
         // short activation matrices: when the persistent kernel would leave most SMs idle, split K
         // over a cluster so every SM streams a slice of the weight
         int sbn = 0, S = 1;
-        const int split_ctas = e2c_gemm_splitk_plan(a, g_num_sms, &sbn, &S);
+        const int split_ctas = e2c_gemm_splitk_plan(a, num_sms, &sbn, &S);
         if (split_ctas) {
-            const Plan pp = pick_plan(a);
+            const Plan pp = pick_plan(a, num_sms);
             const long ptiles = (long)((a->M + BM * pp.cg - 1) / (BM * pp.cg)) * ((a->n1 - a->n0 + pp.bn - 1) / pp.bn);
-            const long pctas = (ptiles < g_num_sms / pp.cg ? ptiles : g_num_sms / pp.cg) * pp.cg;
+            const long pctas = (ptiles < num_sms / pp.cg ? ptiles : num_sms / pp.cg) * pp.cg;
             if (split_ctas >= 2 * pctas) return e2c_gemm_splitk(a, sbn, S, stream);
         }
     }
-    const Plan pl = pick_plan(a);
+    const Plan pl = pick_plan(a, num_sms);
     const bool pair = pl.cg == 2;
     switch (a->epi) {
     case E2C_EPI_F32:
-        if (perblock) return launch<128, 5, true, E2C_EPI_F32, 1>(a, st);
+        if (perblock) return launch<128, 5, true, E2C_EPI_F32, 1>(a, st, dev, num_sms);
         if (pair)
-            return pl.bn == 128   ? launch<128, 6, false, E2C_EPI_F32, 2>(a, st)
-                   : pl.bn == 192 ? launch<192, 6, false, E2C_EPI_F32, 2>(a, st)
-                                  : launch<256, 5, false, E2C_EPI_F32, 2>(a, st);
-        return pl.bn == 128   ? launch<128, 4, false, E2C_EPI_F32, 1>(a, st)
-               : pl.bn == 192 ? launch<192, 3, false, E2C_EPI_F32, 1>(a, st)
-                              : launch<256, 3, false, E2C_EPI_F32, 1>(a, st);
+            return pl.bn == 128   ? launch<128, 6, false, E2C_EPI_F32, 2>(a, st, dev, num_sms)
+                   : pl.bn == 192 ? launch<192, 6, false, E2C_EPI_F32, 2>(a, st, dev, num_sms)
+                                  : launch<256, 5, false, E2C_EPI_F32, 2>(a, st, dev, num_sms);
+        return pl.bn == 128   ? launch<128, 4, false, E2C_EPI_F32, 1>(a, st, dev, num_sms)
+               : pl.bn == 192 ? launch<192, 3, false, E2C_EPI_F32, 1>(a, st, dev, num_sms)
+                              : launch<256, 3, false, E2C_EPI_F32, 1>(a, st, dev, num_sms);
     case E2C_EPI_RESID:
-        if (perblock) return launch<128, 5, true, E2C_EPI_RESID, 1>(a, st);
+        if (perblock) return launch<128, 5, true, E2C_EPI_RESID, 1>(a, st, dev, num_sms);
         if (pair)
-            return pl.bn == 128   ? launch<128, 6, false, E2C_EPI_RESID, 2>(a, st)
-                   : pl.bn == 192 ? launch<192, 6, false, E2C_EPI_RESID, 2>(a, st)
-                                  : launch<256, 5, false, E2C_EPI_RESID, 2>(a, st);
-        return pl.bn == 128   ? launch<128, 4, false, E2C_EPI_RESID, 1>(a, st)
-               : pl.bn == 192 ? launch<192, 3, false, E2C_EPI_RESID, 1>(a, st)
-                              : launch<256, 3, false, E2C_EPI_RESID, 1>(a, st);
+            return pl.bn == 128   ? launch<128, 6, false, E2C_EPI_RESID, 2>(a, st, dev, num_sms)
+                   : pl.bn == 192 ? launch<192, 6, false, E2C_EPI_RESID, 2>(a, st, dev, num_sms)
+                                  : launch<256, 5, false, E2C_EPI_RESID, 2>(a, st, dev, num_sms);
+        return pl.bn == 128   ? launch<128, 4, false, E2C_EPI_RESID, 1>(a, st, dev, num_sms)
+               : pl.bn == 192 ? launch<192, 3, false, E2C_EPI_RESID, 1>(a, st, dev, num_sms)
+                              : launch<256, 3, false, E2C_EPI_RESID, 1>(a, st, dev, num_sms);
     case E2C_EPI_I32:
-        if (perblock) return launch<128, 6, true, E2C_EPI_I32, 1>(a, st);
+        if (perblock) return launch<128, 6, true, E2C_EPI_I32, 1>(a, st, dev, num_sms);
         if (pair)
-            return pl.bn == 128   ? launch<128, 6, false, E2C_EPI_I32, 2>(a, st)
-                   : pl.bn == 192 ? launch<192, 6, false, E2C_EPI_I32, 2>(a, st)
-                                  : launch<256, 6, false, E2C_EPI_I32, 2>(a, st);
-        return pl.bn == 128   ? launch<128, 6, false, E2C_EPI_I32, 1>(a, st)
-               : pl.bn == 192 ? launch<192, 4, false, E2C_EPI_I32, 1>(a, st)
-                              : launch<256, 4, false, E2C_EPI_I32, 1>(a, st);
+            return pl.bn == 128   ? launch<128, 6, false, E2C_EPI_I32, 2>(a, st, dev, num_sms)
+                   : pl.bn == 192 ? launch<192, 6, false, E2C_EPI_I32, 2>(a, st, dev, num_sms)
+                                  : launch<256, 6, false, E2C_EPI_I32, 2>(a, st, dev, num_sms);
+        return pl.bn == 128   ? launch<128, 6, false, E2C_EPI_I32, 1>(a, st, dev, num_sms)
+               : pl.bn == 192 ? launch<192, 4, false, E2C_EPI_I32, 1>(a, st, dev, num_sms)
+                              : launch<256, 4, false, E2C_EPI_I32, 1>(a, st, dev, num_sms);
     case E2C_EPI_GELU:
         if (perblock || (a->n1 - a->n0) % 256 || a->n0 % 256 || a->ldy % 4) {
             e2c_set_msg("gemm: the GELU-gate epilogue needs per-row scales and 256-column (gate|up) groups");
             return -1;
         }
-        return pair ? launch<256, 5, false, E2C_EPI_GELU, 2>(a, st) : launch<256, 3, false, E2C_EPI_GELU, 1>(a, st);
+        return pair ? launch<256, 5, false, E2C_EPI_GELU, 2>(a, st, dev, num_sms) : launch<256, 3, false, E2C_EPI_GELU, 1>(a, st, dev, num_sms);
     case E2C_EPI_QKV:
         if (perblock || a->n0 != 0 || a->n1 != 256 * (a->nq + 2) || a->seq_len <= 0 || a->M % a->seq_len ||
             a->ldrope < a->seq_len) {
@@ -952,7 +951,7 @@ extern "C" int e2c_gemm(const e2c_gemm_args *a, void *stream) {
             return -1;
         }
         // (single CTAs only for short activation matrices: two stages leave room for the constants)
-        return pair ? launch<256, 4, false, E2C_EPI_QKV, 2>(a, st) : launch<256, 2, false, E2C_EPI_QKV, 1>(a, st);
+        return pair ? launch<256, 4, false, E2C_EPI_QKV, 2>(a, st, dev, num_sms) : launch<256, 2, false, E2C_EPI_QKV, 1>(a, st, dev, num_sms);
     case E2C_EPI_NORMADD: {
         // the residual norms in the epilogue: its own kernel (gemm_i8_norm.cu)
         const int ncols = a->n1 - a->n0;

@@ -29,6 +29,7 @@
 
 #include "epi_math.cuh"
 #include "launch.h"
+#include "devstate.cuh"
 #include "pdl.h"
 #include "ptx.cuh"
 #include "tmap.h"
@@ -331,28 +332,26 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
 }
 
-int g_num_sms = 0;
-int g_max_clusters[MAXCL + 1] = { 0 };
+E2cPerDev g_max_clusters[MAXCL + 1];  // resident clusters per width, per device (-1: none)
 
-int prepare(int ncl, cudaLaunchConfig_t *cfg, cudaLaunchAttribute *attr, cudaStream_t st) {
+// Per-device set-up and the launch configuration; *maxc_out is the clusters the device holds.
+int prepare(int ncl, cudaLaunchConfig_t *cfg, cudaLaunchAttribute *attr, cudaStream_t st, int *maxc_out) {
     using L = Smem;
-    static bool attr_set = false;
-    if (!g_num_sms) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        if (cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || g_num_sms <= 0) {
-            e2c_set_msg("gemm_gelu_quant: no CUDA device");
-            return -2;
-        }
+    static E2cPerDev attr_set;  // the shared-memory and cluster-size opt-ins, per device
+    const int dev = e2c_device();
+    const int num_sms = e2c_sm_count(dev);
+    if (!num_sms) {
+        e2c_set_msg("gemm_gelu_quant: no CUDA device");
+        return -2;
     }
-    if (!attr_set) {
+    if (!attr_set.get(dev)) {
         if (cudaFuncSetAttribute(k_gemm_gelu_quant, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC) != cudaSuccess ||
             cudaFuncSetAttribute(k_gemm_gelu_quant, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess) {
             cudaGetLastError();
             e2c_set_msg("gemm_gelu_quant: cannot reserve %d bytes of shared memory or clusters above 8", L::ALLOC);
             return -2;
         }
-        attr_set = true;
+        attr_set.set(dev, 1);
     }
     memset(cfg, 0, sizeof *cfg);
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -364,18 +363,20 @@ int prepare(int ncl, cudaLaunchConfig_t *cfg, cudaLaunchAttribute *attr, cudaStr
     cfg->stream = st;
     cfg->attrs = attr;
     cfg->numAttrs = 1;
-    int &maxc = g_max_clusters[ncl];
+    int maxc = g_max_clusters[ncl].get(dev);
     if (!maxc) {
-        cfg->gridDim = dim3((unsigned)(ncl * (g_num_sms / ncl)));
+        cfg->gridDim = dim3((unsigned)(ncl * (num_sms / ncl)));
         if (cudaOccupancyMaxActiveClusters(&maxc, k_gemm_gelu_quant, cfg) != cudaSuccess || maxc <= 0) {
             cudaGetLastError();
             maxc = -1;
         }
+        g_max_clusters[ncl].set(dev, maxc);
     }
     if (maxc < 0) {
         e2c_set_msg("gemm_gelu_quant: the device cannot hold a cluster of %d CTAs", ncl);
         return -2;
     }
+    *maxc_out = maxc;
     return 0;
 }
 
@@ -386,7 +387,8 @@ extern "C" int e2c_gemm_gelu_quant_supported(int ncl) {
     if (ncl < 1 || ncl > MAXCL) return 0;
     cudaLaunchConfig_t cfg;
     cudaLaunchAttribute attr[1];
-    return prepare(ncl, &cfg, attr, 0) == 0;
+    int maxc = 0;
+    return prepare(ncl, &cfg, attr, 0, &maxc) == 0;
 }
 
 // The launch: geometry checked by e2c_gemm (per-row scales, n0 = 0, N = 256 x (1..16)).
@@ -398,7 +400,8 @@ extern "C" int e2c_gemm_gelu_quant(const e2c_gemm_args *a, void *stream) {
     }
     cudaLaunchConfig_t cfg;
     cudaLaunchAttribute attr[2];
-    const int rc = prepare(ncl, &cfg, attr, (cudaStream_t)stream);
+    int maxc = 0;
+    const int rc = prepare(ncl, &cfg, attr, (cudaStream_t)stream, &maxc);
     if (rc) return rc;
     CUtensorMap ta, tb, tq;
     if (e2c_tmap_2d(&ta, a->a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)a->K, (uint64_t)a->M, (uint64_t)a->lda, BK, BM) ||
@@ -407,7 +410,6 @@ extern "C" int e2c_gemm_gelu_quant(const e2c_gemm_args *a, void *stream) {
                          QH, 32))
         return -3;
     const int tiles_m = (a->M + BM - 1) / BM;
-    const int maxc = g_max_clusters[ncl];
     cfg.gridDim = dim3((unsigned)(ncl * (tiles_m < maxc ? tiles_m : maxc)));
     cfg.numAttrs = e2c_pdl_attr(attr, 1);
     const cudaError_t e = cudaLaunchKernelEx(&cfg, k_gemm_gelu_quant, ta, tb, tq, *a);

@@ -41,6 +41,7 @@
 
 #include "epi_math.cuh"
 #include "launch.h"
+#include "devstate.cuh"
 #include "pdl.h"
 #include "ptx.cuh"
 #include "tmap.h"
@@ -523,30 +524,26 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
 }
 
-int g_num_sms = 0;
-
 }  // namespace
 
 // The GEMM + norms launch: geometry checked by e2c_gemm (per-row scales, n0 = 0, D = 128 x (1..8)).
 extern "C" int e2c_gemm_norm(const e2c_gemm_args *a, void *stream) {
     using L = Smem;
-    static bool attr_set = false;
-    static int max_clusters[2][MAXCL + 1] = { { 0 } };
-    if (!g_num_sms) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        if (cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || g_num_sms <= 0) {
-            e2c_set_msg("gemm_norm: no CUDA device");
-            return -2;
-        }
+    static E2cPerDev attr_set;                  // the shared-memory opt-in, per device
+    static E2cPerDev max_clusters[2][MAXCL + 1];  // resident clusters per (quantise, width), per device
+    const int dev = e2c_device();
+    const int num_sms = e2c_sm_count(dev);
+    if (!num_sms) {
+        e2c_set_msg("gemm_norm: no CUDA device");
+        return -2;
     }
-    if (!attr_set) {
+    if (!attr_set.get(dev)) {
         if (cudaFuncSetAttribute(k_gemm_norm<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC) != cudaSuccess ||
             cudaFuncSetAttribute(k_gemm_norm<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC) != cudaSuccess) {
             e2c_set_msg("gemm_norm: cannot reserve %d bytes of shared memory", L::ALLOC);
             return -2;
         }
-        attr_set = true;
+        attr_set.set(dev, 1);
     }
     const int D = a->n1 - a->n0;
     const int ncl = D / BN;
@@ -578,15 +575,15 @@ extern "C" int e2c_gemm_norm(const e2c_gemm_args *a, void *stream) {
     cfg.numAttrs = 1;
     const bool quant = a->norm_g2 != nullptr;
     auto kern = quant ? k_gemm_norm<true> : k_gemm_norm<false>;
-    int &maxc = max_clusters[quant][ncl];
+    int maxc = max_clusters[quant][ncl].get(dev);
     if (!maxc) {
-        cfg.gridDim = dim3((unsigned)(ncl * (g_num_sms / ncl)));
+        cfg.gridDim = dim3((unsigned)(ncl * (num_sms / ncl)));
         if (cudaOccupancyMaxActiveClusters(&maxc, kern, &cfg) != cudaSuccess || maxc <= 0) {
             cudaGetLastError();
-            maxc = 0;
             e2c_set_msg("gemm_norm: the device cannot hold a cluster of %d CTAs", ncl);
             return -2;
         }
+        max_clusters[quant][ncl].set(dev, maxc);
     }
     cfg.gridDim = dim3((unsigned)(ncl * (tiles_m < maxc ? tiles_m : maxc)));
     cfg.numAttrs = e2c_pdl_attr(attr, 1);

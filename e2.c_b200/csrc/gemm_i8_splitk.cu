@@ -23,6 +23,7 @@
 #include <string.h>
 
 #include "launch.h"
+#include "devstate.cuh"
 #include "pdl.h"
 #include "ptx.cuh"
 #include "tmap.h"
@@ -233,27 +234,34 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
 }
 
+// the shared-memory and cluster-size opt-ins on the current device: 0 unset, 1 ok, -1 failed
 template <int BN>
 bool configure() {
-    static int state = 0;  // 0 unset, 1 ok, -1 failed
-    if (!state) {
-        state = (cudaFuncSetAttribute(k_gemm_splitk<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_ALLOC) == cudaSuccess &&
-                 cudaFuncSetAttribute(k_gemm_splitk<BN>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess)
-                    ? 1
-                    : -1;
-        if (state < 0) cudaGetLastError();
+    static E2cPerDev state;
+    const int dev = e2c_device();
+    if (dev < 0) return false;
+    int s = state.get(dev);
+    if (!s) {
+        s = (cudaFuncSetAttribute(k_gemm_splitk<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_ALLOC) == cudaSuccess &&
+             cudaFuncSetAttribute(k_gemm_splitk<BN>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess)
+                ? 1
+                : -1;
+        if (s < 0) cudaGetLastError();
+        state.set(dev, s);
     }
-    return state > 0;
+    return s > 0;
 }
 
+// clusters of S CTAs the current device holds at once (0: none), per device and S
 template <int BN>
 int clusters(int S) {
-    static int cache[5] = {-1, -1, -1, -1, -1};
+    static E2cPerDev cache[5];  // value + 1; 0 = not yet asked
     int i = 0;
     while ((2 << i) < S && i < 4) i++;
     if (S < 2 || S > 16 || (2 << i) != S || !configure<BN>()) return 0;
-    if (cache[i] >= 0) return cache[i];
-    cache[i] = 0;
+    const int dev = e2c_device();
+    const int c = cache[i].get(dev);
+    if (c > 0) return c - 1;
     cudaLaunchConfig_t cfg;
     memset(&cfg, 0, sizeof cfg);
     cudaLaunchAttribute at[1];
@@ -267,9 +275,12 @@ int clusters(int S) {
     cfg.attrs = at;
     cfg.numAttrs = 1;
     int n = 0;
-    if (cudaOccupancyMaxActiveClusters(&n, k_gemm_splitk<BN>, &cfg) == cudaSuccess && n > 0) cache[i] = n;
-    else cudaGetLastError();
-    return cache[i];
+    if (cudaOccupancyMaxActiveClusters(&n, k_gemm_splitk<BN>, &cfg) != cudaSuccess || n < 0) {
+        cudaGetLastError();
+        n = 0;
+    }
+    cache[i].set(dev, n + 1);
+    return n;
 }
 
 template <int BN>

@@ -126,6 +126,11 @@ int e2c_l2norm_rows(float *y, const uint8_t *valid, int B, int S, int D, void *s
 int e2c_attention(const void *q, const void *k, const void *vt, int ldvt, const uint8_t *valid,
                   float *ctx, int B, int S, int H, float scale, int *status, void *stream);
 
+/* ---- self-test of the bounded wait (selftest.cu): one warp waits on an mbarrier that receives
+ * its arrival first (arrive != 0) or never (arrive == 0). *completed is 1 if the wait completed, 0
+ * if it gave up after its bound (~2 s) and recorded `code` (0x101..0x105) in *status. */
+int e2c_wait_selftest(int *status, int code, int arrive, int *completed, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -70,8 +70,12 @@ extern "C" int e2cuda_i8_linear_noalloc(const e2cuda_w8 *w, const float *x, int 
         return -1;
     }
     const int K = w->K;
-    if (K % 16 || w->ld != K) {
+    if (K % 16) {
         e2cu_err("i8_linear_noalloc: K (%d) must be a multiple of 16", K);
+        return -1;
+    }
+    if (w->ld != K) {
+        e2cu_err("i8_linear_noalloc: the weight's row stride (%d bytes) must equal K (%d)", w->ld, K);
         return -1;
     }
     if (ablk != K && (ablk <= 0 || ablk % 128 || K % ablk)) {
@@ -92,6 +96,15 @@ extern "C" int e2cuda_i8_linear_noalloc(const e2cuda_w8 *w, const float *x, int 
     if (M == 0) return 0;
 
     cudaStream_t st = (cudaStream_t)stream;
+    // The call ends by synchronising `stream` to read its status word. On a capturing stream that
+    // would invalidate the caller's capture, so such a call is refused before anything is queued.
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    if (e2cu_cuda(cudaStreamIsCapturing(st, &cap), "i8_linear_noalloc: capture query")) return -1;
+    if (cap != cudaStreamCaptureStatusNone) {
+        e2cu_err("i8_linear_noalloc: `stream` is being captured; this call synchronises its stream to read its "
+                 "status, so it runs on a stream that is not capturing");
+        return -1;
+    }
     int *status = reinterpret_cast<int *>(scratch);
     int8_t *q = reinterpret_cast<int8_t *>(scratch + kHeader);
     float *qs = reinterpret_cast<float *>(scratch + s_off);

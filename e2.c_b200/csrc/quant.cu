@@ -9,6 +9,7 @@
 #include <stdint.h>
 
 #include "launch.h"
+#include "devstate.cuh"
 #include "pdl.h"
 #include "ptx.cuh"
 
@@ -202,8 +203,11 @@ extern "C" int e2c_quantize(const float *x, int ldx, int8_t *q, int ldq, float *
     const int g = ablk / 16;
     if (ablk == K && K % 128 == 0 && K / 128 <= 9 && !clamp) {
         // per-token rows of 128 NV: persistent warps, as many CTAs as the SMs hold at once
-        static int sms = 0, resident[10] = { 0 };
-        if (!sms && (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, 0) != cudaSuccess || sms <= 0)) sms = 148;
+        // blocks per SM depend only on the kernel's resources and the architecture (this library
+        // holds sm_100a code only), so they are kept once; the SM count is the current device's
+        static int resident[10] = { 0 };
+        int sms = e2c_sm_count(e2c_device());
+        if (sms <= 0) sms = 148;
         const int nv = K / 128;
         if (!resident[nv]) {
             const void *fn = nv == 1 ? (const void *)k_quant_rows<1> : nv == 2 ? (const void *)k_quant_rows<2>

@@ -93,27 +93,28 @@ def pack_batch(ids_of, lengths: np.ndarray, p: Pass) -> tuple[np.ndarray, np.nda
     return ids, valid
 
 
-def gather_embeddings(dist, local_idx: np.ndarray, local_emb, n_total: int, device=None):
-    """All-gather every rank's (sequence index, embedding) rows and return the [n_total][dim]
-    matrix in original sequence order (on every rank). One collective for the rows and one for the
-    indices, each padded to the largest share."""
+def gather_embeddings(dist, shares: list, local_emb, n_total: int, device=None):
+    """All-gather every rank's embedding rows and return the [n_total][dim] matrix in original
+    sequence order (on every rank). `shares` is lpt_assign's result, which every rank computes
+    identically from the same job, so the row counts and the sequence index of every gathered row
+    are known without exchanging them: the only collective is one all-gather of each rank's rows,
+    padded to the largest share."""
     import torch
 
+    rank, world = dist.get_rank(), dist.get_world_size()
+    if len(shares) != world:
+        raise ValueError(f"{len(shares)} shares for a world of {world}")
     dim = local_emb.shape[1]
-    world = dist.get_world_size()
-    counts = torch.tensor([len(local_idx)], dtype=torch.int64, device=device)
-    all_counts = [torch.zeros_like(counts) for _ in range(world)]
-    dist.all_gather(all_counts, counts)
-    cmax = int(max(int(c.item()) for c in all_counts))
+    mine = len(shares[rank])
+    if local_emb.shape[0] != mine:
+        raise ValueError(f"rank {rank} holds {local_emb.shape[0]} rows for a share of {mine}")
+    cmax = max(len(s) for s in shares)
     emb = torch.zeros((cmax, dim), dtype=local_emb.dtype, device=device)
-    emb[: len(local_idx)] = local_emb
-    idx = torch.full((cmax,), -1, dtype=torch.int64, device=device)
-    idx[: len(local_idx)] = torch.as_tensor(local_idx, dtype=torch.int64, device=device)
+    emb[:mine] = local_emb
     g_emb = torch.empty((world * cmax, dim), dtype=local_emb.dtype, device=device)
-    g_idx = torch.empty((world * cmax,), dtype=torch.int64, device=device)
     dist.all_gather_into_tensor(g_emb, emb)
-    dist.all_gather_into_tensor(g_idx, idx)
-    keep = g_idx >= 0
+    src = np.concatenate([r * cmax + np.arange(len(s)) for r, s in enumerate(shares)]).astype(np.int64)
+    dst = np.concatenate([np.asarray(s, np.int64) for s in shares])
     out = torch.empty((n_total, dim), dtype=local_emb.dtype, device=device)
-    out[g_idx[keep]] = g_emb[keep]
+    out[torch.as_tensor(dst, device=device)] = g_emb[torch.as_tensor(src, device=device)]
     return out

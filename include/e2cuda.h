@@ -161,7 +161,9 @@ int e2cuda_i8_gemm(const e2cuda_w8 *w, const int8_t *qa, const float *a_scales, 
  *     Make that first call before any stream capture.
  *
  * The call is queued on `stream`, then synchronises `stream` to read its device status; it returns
- * once y is written. Calls no cudaMalloc, cudaFree or allocating library routine. */
+ * once y is written. A stream that is being captured is refused with an error before anything is
+ * queued, since the synchronisation would invalidate the capture. Calls no cudaMalloc, cudaFree or
+ * allocating library routine. */
 #define E2CUDA_NOALLOC_SCRATCH_BYTES ((size_t)8 << 20)
 int e2cuda_i8_linear_noalloc(const e2cuda_w8 *w, const float *x, int M, int ablk, float *y, int ldy,
                              void *stream);

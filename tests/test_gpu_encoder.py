@@ -18,10 +18,11 @@ def _which(of):
     return "reference" if of.mux() is not None else "port"
 
 
-def test_ffn_block_config1_shape(e2c, of, syn, torch_cuda):
+@pytest.mark.parametrize("M", [1024, 4096])  # 4096 tokens: benchmark config 1 itself
+def test_ffn_block_config1_shape(e2c, of, syn, torch_cuda, M):
     torch = torch_cuda
     rng = np.random.default_rng(0xE2C0DE + 1)
-    M, D, I = 1024, 768, 1152
+    D, I = 768, 1152
     x = rng.standard_normal((M, D), dtype=np.float32)
     g = (1 + 0.1 * rng.standard_normal(D)).astype(np.float32)
     wg, wu = syn.packed_weight(rng, I, D, 0.02, D), syn.packed_weight(rng, I, D, 0.02, D)

@@ -513,3 +513,37 @@ def test_attention_vs_fp64(e2c, torch_cuda, B, S, H, scale, masked):
             err = np.linalg.norm(g[live] - w[live], axis=1) / np.linalg.norm(w[live], axis=1)
             assert err.max() < 1e-2, f"b={b} h={h} worst row rel err {err.max()}"
             assert cosine_rows(g[live], w[live]).min() > 0.9999
+
+
+# ------------------------------------------------------------------------------------------ failure detection
+def test_bounded_wait_expires_and_reports(e2c, torch_cuda):
+    """The bounded mbarrier wait every kernel uses (ptx.cuh mbar_wait): with its arrival withheld it
+    gives up after its ~2 s bound, records the code in the device status word and returns, so
+    e2cuda_check reports the failure and the context keeps working. With the arrival it completes
+    at once and records nothing."""
+    import time
+
+    torch = torch_cuda
+    lib = e2c.lib()
+    lib.e2c_wait_selftest.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p]
+    lib.e2c_wait_selftest.restype = C.c_int
+    lib.e2cu_status.restype = C.c_void_p
+    e2c.check()  # start from a clean status word
+    status = lib.e2cu_status()
+    done = torch.full((1,), -1, dtype=torch.int32, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    assert lib.e2c_wait_selftest(status, 0x102, 1, done.data_ptr(), stream) == 0
+    e2c.check()
+    assert int(done.item()) == 1
+    t0 = time.perf_counter()
+    assert lib.e2c_wait_selftest(status, 0x102, 0, done.data_ptr(), stream) == 0
+    with pytest.raises(e2c.E2CudaError, match="0x102"):
+        e2c.check()
+    waited = time.perf_counter() - t0
+    assert int(done.item()) == 0
+    assert 1.5 < waited < 30, waited
+    # the status was cleared by the check and the device still runs kernels
+    x = torch.randn((64, 768), device="cuda")
+    q, s = e2c.quantize_rows(x, 768)
+    e2c.check()
+    assert q.shape == (64, 768)

@@ -76,11 +76,12 @@ def _gather_worker(rank: int, world: int, port: int, n: int, q):
     try:
         rng = np.random.default_rng(5)  # the same plan on every rank
         lens = shard.bucket_length(shard.log_uniform_lengths(rng, n), 64)
-        mine = shard.lpt_assign(shard.sequence_cost(lens), world)[rank]
+        shares = shard.lpt_assign(shard.sequence_cost(lens), world)
+        mine = shares[rank]
         # stand-in embeddings: row i is a function of the sequence index only
         emb = torch.stack([torch.full((8,), float(i)) + torch.arange(8.0) for i in mine]) if len(mine) else \
             torch.zeros((0, 8))
-        out = shard.gather_embeddings(dist, mine, emb, n)
+        out = shard.gather_embeddings(dist, shares, emb, n)
         want = torch.arange(n, dtype=torch.float32)[:, None] + torch.arange(8.0)[None, :]
         q.put((rank, bool(torch.equal(out, want)), len(mine)))
     finally:
