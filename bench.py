@@ -931,42 +931,113 @@ SWEEP_KN = ((2048, 8192), (8192, 2048), (2048, 2048), (768, 262144))
 
 def gemm_sweep(args) -> int:
     """Benchmark config 3: the W8A8 GEMM (per-token activation scales, fp32 output) over
-    M x (K, N), one JSON line per point with its time against the roofline that bounds it: int8
-    tensor throughput (2 x measured bf16) or HBM bandwidth over the algorithmic bytes
-    M*K + 4*M (activations) + N*K + 4*N (weights) + 4*M*N (output)."""
+    M x (K, N), one JSON line per point against the roofline that bounds it: int8 tensor throughput
+    (2 x measured bf16) or HBM bandwidth over the algorithmic bytes M*K + 4*M (activations) + N*K +
+    4*N (weights) + 4*M*N (output). Two device timings per point, both CUDA events:
+      - "isolated": one launch after a 256 MB L2 flush (cold L2, launch ramp and tail exposed);
+      - "chain": back-to-back launches over R copies of the weight whose total exceeds twice the
+        L2, captured as one CUDA graph, per-launch average (the decode pattern: one GEMM after
+        another, every weight from HBM).
+    Beside them the reference's quantise + GEMM region (e2ref_linear, E2_I8_BLOCK = K) on the host
+    cores, best of 3, as GMAC/s and GB/s. E2C_SWEEP_M=1,16 restricts the token counts."""
+    import ctypes as C
+
     import torch
 
+    sys.path.insert(0, str(ROOT))
+    from oracle import oracle_ffi as of
+
     e2c = load_pkg()
+    import e2c_b200.synthetic as syn
+
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     stream = torch.cuda.Stream(device=dev)
     p = peaks()
     int8_peak, hbm = 2.0 * p["bf16_tflops"] * 1e12, p["hbm_gbs"] * 1e9
-    g = torch.Generator(device=dev).manual_seed(3)
-    rng = np.random.default_rng(3)
+    lib = e2c.lib()
+    lib.e2c_gemm_last_kernel.restype = C.c_char_p
+    lib.e2c_gemm_ws_bytes.argtypes = [C.c_int]
+    lib.e2c_gemm_ws_bytes.restype = C.c_size_t
+    lib.e2cu_status.restype = C.c_void_p
+    ms_only = [int(v) for v in os.environ.get("E2C_SWEEP_M", "").split(",") if v] or list(SWEEP_M)
     for K, N in SWEEP_KN:
-        W = e2c.Weight(w=rng.integers(-127, 128, size=(N, K), dtype=np.int8),
-                       scale=rng.uniform(1e-4, 0.02, size=N).astype(np.float32))
-        for M in SWEEP_M:
-            qa = torch.randint(-127, 128, (M, K), dtype=torch.int8, device=dev, generator=g)
-            qs = torch.rand((M, 1), device=dev, generator=g) * 0.05 + 1e-3
+        rng = np.random.default_rng(0xE2C0DE + 3 + K + N)
+        wf = (rng.standard_normal((N, K), dtype=np.float32) * np.float32(0.02)).astype(np.float32)
+        wq, wsc = syn.quantize_weight_rows(wf)
+        ref = of.ref(K) if not args.no_cpu_baseline else None
+        wref = of.Weight(wf, K, lib=ref) if ref is not None else None
+        del wf
+        copies = max(1, min(64, -(-(2 * 128 << 20) // (N * K))))
+        Ws = [e2c.Weight(w=wq, scale=wsc) for _ in range(copies)]
+        for M in ms_only:
+            x = syn.activations(np.random.default_rng(M + K + N), M, K)
+            qa, qs = e2c.quantize_rows(torch.from_numpy(x).to(dev), K)
             y = torch.empty((M, N), dtype=torch.float32, device=dev)
-            a = e2c.gemm_args(W, qa, qs, M)
-            a.epi, a.y, a.ldy = e2c.EPI_F32, y.data_ptr(), N
-            run = lambda: e2c.gemm_raw(a, stream)
-            ms = timed_launches(run, stream, args.warmup, args.steps)
+            wsb = lib.e2c_gemm_ws_bytes(M)
+            wsp = torch.zeros(max(wsb // 4, 1) + 32, dtype=torch.int32, device=dev)
+            argl = []
+            for W in Ws:
+                a = e2c.gemm_args(W, qa, qs, M)
+                a.epi, a.y, a.ldy = e2c.EPI_F32, y.data_ptr(), N
+                a.status = lib.e2cu_status()
+                if wsb:
+                    a.ws, a.ws_bytes = wsp.data_ptr(), wsb
+                argl.append(a)
+            ms = timed_launches(lambda: e2c.gemm_raw(argl[0], stream), stream, args.warmup, args.steps)
+            kernel = lib.e2c_gemm_last_kernel().decode()
             e2c.check(stream)
+            # the chain is captured as one CUDA graph, so host launch overhead never paces it
+            reps = max(2, min(64, (4 * args.steps) // len(argl)))
+            with torch.cuda.stream(stream):
+                for a in argl:
+                    e2c.gemm_raw(a, stream)
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=stream):
+                for _ in range(reps):
+                    for a in argl:
+                        e2c.gemm_raw(a, stream)
+            with torch.cuda.stream(stream):
+                graph.replay()
+                torch.cuda._sleep(100_000)
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                graph.replay()
+                e1.record(stream)
+            torch.cuda.synchronize()
+            e2c.check(stream)
+            ms_chain = e0.elapsed_time(e1) / (reps * len(argl))
+            del graph
             ops = 2.0 * M * N * K
             nbytes = M * K + 4 * M + N * K + 4 * N + 4 * M * N
             t_tc, t_hbm = ops / int8_peak, nbytes / hbm
-            t = ms / 1e3
-            print(json.dumps({"sweep": "config 3", "M": M, "K": K, "N": N, "us": round(ms * 1e3, 2),
-                              "tops": round(ops / t / 1e12, 1), "gbs": round(nbytes / t / 1e9, 1),
-                              "bound": "tensor" if t_tc > t_hbm else "hbm",
-                              "frac_of_roofline": round(max(t_tc, t_hbm) / t, 3),
-                              "peak_src": p["src"]}), flush=True)
-            del qa, qs, y
-        W.free()
+
+            def fr(ms_):
+                t = ms_ / 1e3
+                return {"us": round(ms_ * 1e3, 2), "tops": round(ops / t / 1e12, 1), "gbs": round(nbytes / t / 1e9, 1),
+                        "frac_of_roofline": round(max(t_tc, t_hbm) / t, 3)}
+
+            cpu = None
+            if wref is not None:
+                qa_c = np.empty((M, K), np.int8)
+                as_c = np.empty((M, 1), np.float32)
+                y_c = np.empty((M, N), np.float32)
+                nthreads = ref.e2ref_init(0)
+                t = _best_cpu(lambda: ref.e2ref_linear(x.ctypes.data_as(of.f32p), M, K, C.byref(wref.q),
+                                                       qa_c.ctypes.data_as(of.i8p), as_c.ctypes.data_as(of.f32p),
+                                                       y_c.ctypes.data_as(of.f32p)), warmup=1, reps=3, budget_s=15.0)
+                cpu = {"us": round(t * 1e6, 1), "gmacs": round(M * N * K / t / 1e9, 1),
+                       "gbs": round(nbytes / t / 1e9, 1), "threads": nthreads,
+                       "what": "e2ref_linear: e2_quantize_blocks_avx512 + e2_i8_gemm_avx512 over the reference pool"}
+            print(json.dumps({"sweep": "config 3", "M": M, "K": K, "N": N, "kernel": kernel,
+                              "bound": "tensor" if t_tc > t_hbm else "hbm", "isolated": fr(ms), "chain": fr(ms_chain),
+                              "chain_weights": len(argl), "pdl": os.environ.get("E2C_PDL") == "1",
+                              "peak_src": p["src"], "cpu_reference": cpu}), flush=True)
+            del qa, qs, y, wsp, argl
+        for W in Ws:
+            W.free()
+        del wref
     return 0
 
 

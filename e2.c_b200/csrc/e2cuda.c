@@ -70,6 +70,22 @@ static const char *status_name(int s) {
     }
 }
 
+/* ------------------------------------------------------------------ workspace generations */
+/* The weight-streaming GEMM leaves its workspace zero after every launch that completes; one that
+ * failed may leave partial sums behind. Every reported device failure bumps this count, and a
+ * workspace cleared at an older count is cleared again before its next use. */
+static int g_fail_gen;
+
+void e2cu_note_failure(void) { __atomic_add_fetch(&g_fail_gen, 1, __ATOMIC_RELEASE); }
+
+int e2cu_ws_refresh(int *ws, size_t bytes, int *gen, cudaStream_t st) {
+    const int now = __atomic_load_n(&g_fail_gen, __ATOMIC_ACQUIRE);
+    if (*gen == now) return 0;
+    if (e2cu_cuda(cudaMemsetAsync(ws, 0, bytes, st), "workspace clear")) return -1;
+    *gen = now;
+    return 0;
+}
+
 int e2cuda_check(void *stream) {
     if (e2cu_cuda(cudaStreamSynchronize((cudaStream_t)stream), "synchronize")) return -1;
     int *st = e2cu_status();
@@ -81,6 +97,7 @@ int e2cuda_check(void *stream) {
     if (e2cu_cuda(cudaMemcpy(&h, st, sizeof h, cudaMemcpyDeviceToHost), "status read")) return -1;
     if (h) {
         cudaMemset(st, 0, sizeof(int));
+        e2cu_note_failure();
         e2cu_err("device kernel failure 0x%x: %s", h, status_name(h));
         return -1;
     }
@@ -210,6 +227,71 @@ void e2cu_gemm_args(e2c_gemm_args *a, const e2cuda_w8 *w, const int8_t *qa, cons
     a->status = e2cu_status();
 }
 
+/* ------------------------------------------------------------------ per-stream GEMM workspace */
+/* The op API's GEMM keeps one weight-streaming workspace per (device, stream), grown on demand: a
+ * workspace serves one stream at a time, and calls on one stream are ordered. A stream that is
+ * being captured never allocates (it uses what it has, or the other GEMM kernels). */
+#define E2CU_WS_SLOTS 32
+static pthread_mutex_t g_ws_mu = PTHREAD_MUTEX_INITIALIZER;
+static struct {
+    int used, dev, gen;
+    cudaStream_t st;
+    int *p;
+    size_t n;
+} g_ws[E2CU_WS_SLOTS];
+
+/* a ready (zeroed, stream-ordered) workspace of at least `need` bytes for `st`, or NULL */
+static int *stream_ws(cudaStream_t st, size_t need, size_t *got) {
+    int dev = 0;
+    if (!need || cudaGetDevice(&dev) != cudaSuccess) return NULL;
+    enum cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(st, &cap) != cudaSuccess) {
+        cudaGetLastError();
+        return NULL;
+    }
+    int *out = NULL;
+    pthread_mutex_lock(&g_ws_mu);
+    int slot = -1, free_slot = -1;
+    for (int i = 0; i < E2CU_WS_SLOTS; i++) {
+        if (g_ws[i].used && g_ws[i].dev == dev && g_ws[i].st == st) slot = i;
+        if (!g_ws[i].used && free_slot < 0) free_slot = i;
+    }
+    if (slot < 0 && free_slot >= 0 && cap == cudaStreamCaptureStatusNone) {
+        slot = free_slot;
+        g_ws[slot].used = 1;
+        g_ws[slot].dev = dev;
+        g_ws[slot].st = st;
+        g_ws[slot].p = NULL;
+        g_ws[slot].n = 0;
+    }
+    if (slot >= 0) {
+        if (g_ws[slot].n < need && cap == cudaStreamCaptureStatusNone) {
+            /* grow: the old buffer may still be in use by queued work on this stream */
+            if (g_ws[slot].p) {
+                cudaStreamSynchronize(st);
+                cudaFree(g_ws[slot].p);
+            }
+            g_ws[slot].p = NULL;
+            g_ws[slot].n = 0;
+            int *p = NULL;
+            if (cudaMalloc((void **)&p, need) == cudaSuccess) {
+                g_ws[slot].p = p;
+                g_ws[slot].n = need;
+                g_ws[slot].gen = __atomic_load_n(&g_fail_gen, __ATOMIC_ACQUIRE) - 1; /* cleared below */
+            } else {
+                cudaGetLastError();
+            }
+        }
+        if (g_ws[slot].p && g_ws[slot].n >= need &&
+            e2cu_ws_refresh(g_ws[slot].p, g_ws[slot].n, &g_ws[slot].gen, st) == 0) {
+            out = g_ws[slot].p;
+            *got = g_ws[slot].n;
+        }
+    }
+    pthread_mutex_unlock(&g_ws_mu);
+    return out;
+}
+
 int e2cuda_i8_gemm(const e2cuda_w8 *w, const int8_t *qa, const float *a_scales, int M, int ablk, int n0, int n1,
                    const e2cuda_epilogue *ep, float *y, int ldy, void *stream) {
     if (!w || !w->w || M < 0 || (M > 0 && (!qa || !a_scales)) || n0 < 0 || n1 > w->N || n0 > n1) {
@@ -239,6 +321,10 @@ int e2cuda_i8_gemm(const e2cuda_w8 *w, const int8_t *qa, const float *a_scales, 
     if (a.epi != E2C_EPI_I32 && !y) {
         e2cu_err("i8_gemm: no output");
         return -1;
+    }
+    if (a.epi != E2C_EPI_I32 && ablk == w->K) {
+        const size_t need = e2c_gemm_ws_bytes(M);
+        if (need) a.ws = stream_ws((cudaStream_t)stream, need, &a.ws_bytes);
     }
     return e2cu_launch(e2c_gemm(&a, stream), "i8_gemm");
 }
@@ -506,6 +592,10 @@ static void gemm_host_locked(float *y, const int8_t *qa, const float *a_scales, 
     a.y = dy - n0; /* column n lands at dy[m * (n1-n0) + n - n0] */
     a.ldy = n1 - n0;
     a.epi = E2C_EPI_F32;
+    if (ablk == K) {
+        const size_t need = e2c_gemm_ws_bytes(M);
+        if (need) a.ws = stream_ws(NULL, need, &a.ws_bytes);
+    }
     if (e2cu_launch(e2c_gemm(&a, NULL), "i8_gemm_host") || e2cuda_check(NULL) ||
         e2cu_cuda(cudaMemcpy2D(y + n0, sizeof(float) * (size_t)N, dy, sizeof(float) * (size_t)(n1 - n0),
                                sizeof(float) * (size_t)(n1 - n0), (size_t)M, cudaMemcpyDeviceToHost),

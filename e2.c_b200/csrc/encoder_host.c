@@ -55,6 +55,9 @@ struct e2cuda_encoder {
     void *Q, *K, *Vt;
     size_t vt_bytes;
     int *status;
+    int *gws;          /* workspace of the weight-streaming GEMM (the head's short GEMMs) */
+    size_t gws_bytes;
+    int gws_rows, gws_gen;
     cudaStream_t stream;
     float *host_out;
     graph_slot graphs[MAX_GRAPHS];
@@ -118,7 +121,7 @@ void e2cuda_encoder_destroy(e2cuda_encoder *e) {
     e2cuda_w8_free(&e->dense2);
     void *dev[] = { e->table, e->table_scale, e->norms, e->rope_cos, e->rope_sin, e->ids, e->valid, e->out, e->res,
                     e->tmp, e->ctx, e->h, e->pooled, e->h1, e->qa, e->qb, e->pq, e->qs, e->qsb, e->ps, e->Q, e->K,
-                    e->Vt };
+                    e->Vt, e->gws };
     for (size_t i = 0; i < sizeof dev / sizeof dev[0]; i++)
         if (dev[i]) cudaFree(dev[i]);
     if (e->host_out) cudaFreeHost(e->host_out);
@@ -272,6 +275,13 @@ e2cuda_encoder *e2cuda_encoder_create(const e2cuda_encoder_desc *d, int max_toke
         e->fused_gelu = !(fg && fg[0] == '0') && e->ablk == D && e->I % 128 == 0 && e->I / 128 <= 16 &&
                         e2c_gemm_gelu_quant_supported(e->I / 128);
     }
+    /* the head's GEMMs have one row per sequence: up to 256 of them run on the weight-streaming
+     * kernel, whose workspace starts zeroed and is left zeroed by every launch that completes */
+    e->gws_rows = M < 256 ? (int)M : 256;
+    e->gws_bytes = e2c_gemm_ws_bytes(e->gws_rows);
+    if (e->gws_bytes && (DALLOC(e->gws, e->gws_bytes) || e2cu_cuda(cudaMemset(e->gws, 0, e->gws_bytes), "workspace clear")))
+        goto fail;
+    if (!e->gws_bytes) e->gws_rows = 0;
     e->status = e2cu_status();
     if (!e->status || e2cu_cuda(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking), "stream")) goto fail;
     return e;
@@ -382,6 +392,10 @@ static int encode(e2cuda_encoder *e, int B, int S, int has_valid, cudaStream_t s
     e2cu_gemm_args(&a, &e->dense1, e->pq, e->ps, B, ab_d);
     a.y = e->h1;
     a.ldy = e->DH;
+    if (B <= e->gws_rows) {
+        a.ws = e->gws;
+        a.ws_bytes = e->gws_bytes;
+    }
     if (e2cu_launch(e2c_gemm(&a, st), "encoder dense1") ||
         e2cu_launch(e2c_quantize(e->h1, e->DH, e->pq, e->DH, e->ps, B, e->DH, ab_dh, -INFINITY, INFINITY, 0, st),
                     "encoder head quant"))
@@ -389,6 +403,10 @@ static int encode(e2cuda_encoder *e, int B, int S, int has_valid, cudaStream_t s
     e2cu_gemm_args(&a, &e->dense2, e->pq, e->ps, B, ab_dh);
     a.y = e->out;
     a.ldy = e->DO;
+    if (B <= e->gws_rows) {
+        a.ws = e->gws;
+        a.ws_bytes = e->gws_bytes;
+    }
     if (e2cu_launch(e2c_gemm(&a, st), "encoder dense2") ||
         e2cu_launch(e2c_l2norm_rows(e->out, valid, B, S, e->DO, st), "encoder l2"))
         return -1;
@@ -412,6 +430,7 @@ static int ensure_vt(e2cuda_encoder *e, int B, int S) {
 /* one pass, inputs already in e->ids / e->valid, result in e->out */
 static int pass(e2cuda_encoder *e, int B, int S, int has_valid, cudaStream_t st) {
     if (ensure_vt(e, B, S)) return -1;
+    if (e->gws && e2cu_ws_refresh(e->gws, e->gws_bytes, &e->gws_gen, st)) return -1;
     graph_slot *g = NULL;
     for (int i = 0; i < e->ngraphs; i++)
         if (e->graphs[i].B == B && e->graphs[i].S == S && e->graphs[i].has_valid == has_valid) g = &e->graphs[i];

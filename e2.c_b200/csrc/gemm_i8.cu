@@ -28,6 +28,7 @@
 #include <math.h>
 #include <stdint.h>
 #include <stdio.h>
+#include <stdlib.h>
 
 #include "launch.h"
 #include "epi_math.cuh"
@@ -831,6 +832,20 @@ int launch(const e2c_gemm_args *a, cudaStream_t st, int dev, int num_sms) {
     return 0;
 }
 
+// the kernel family e2c_gemm last chose on this thread (for benchmark reports)
+thread_local const char *g_last_kernel = "";
+
+// E2C_GEMM_STREAM=0 turns the weight-streaming path off (the split-K and persistent kernels then
+// take short activation matrices), for comparisons
+bool stream_path_on() {
+    static int on = -1;
+    if (on < 0) {
+        const char *v = getenv("E2C_GEMM_STREAM");
+        on = !(v && v[0] == '0');
+    }
+    return on != 0;
+}
+
 // Tile plan: width BN and whether CTA pairs (M = 256 per pair, each SM loading half of the weight
 // tile: a third less operand traffic per MAC) share tiles.
 struct Plan {
@@ -862,6 +877,13 @@ Plan pick_plan(const e2c_gemm_args *a, int num_sms) {
 }
 
 }  // namespace
+
+extern "C" const char *e2c_gemm_last_kernel(void) { return g_last_kernel; }
+
+extern "C" size_t e2c_gemm_ws_bytes(int M) {
+    const int num_sms = e2c_sm_count(e2c_device());
+    return (num_sms && M >= 1 && M <= 256) ? e2c_gemm_stream_ws_bytes(M, num_sms) : 0;
+}
 
 extern "C" void e2c_gemm_tile(const e2c_gemm_args *a, int *bm, int *bn) {
     int num_sms = e2c_sm_count(e2c_device());
@@ -895,6 +917,17 @@ extern "C" int e2c_gemm(const e2c_gemm_args *a, void *stream) {
     if (a->M == 0 || a->n1 == a->n0) return 0;
     cudaStream_t st = (cudaStream_t)stream;
     const bool perblock = a->ablk != a->K;
+    if (stream_path_on() && a->ws && !perblock && (a->epi == E2C_EPI_F32 || a->epi == E2C_EPI_RESID) && a->M <= 256 &&
+        a->ws_bytes >= e2c_gemm_stream_ws_bytes(a->M, num_sms) && !((uintptr_t)a->ws & 127)) {
+        // short activation matrices: stream the weight over every SM (the weight in the MMA's M
+        // slot) unless the persistent kernel already fills the device
+        const Plan pp = pick_plan(a, num_sms);
+        const long ptiles = (long)((a->M + BM * pp.cg - 1) / (BM * pp.cg)) * ((a->n1 - a->n0 + pp.bn - 1) / pp.bn);
+        if (a->M <= 64 || ptiles * pp.cg < num_sms) {
+            g_last_kernel = "stream";
+            return e2c_gemm_stream(a, stream);
+        }
+    }
     {
         // short activation matrices: when the persistent kernel would leave most SMs idle, split K
         // over a cluster so every SM streams a slice of the weight
@@ -904,11 +937,15 @@ extern "C" int e2c_gemm(const e2c_gemm_args *a, void *stream) {
             const Plan pp = pick_plan(a, num_sms);
             const long ptiles = (long)((a->M + BM * pp.cg - 1) / (BM * pp.cg)) * ((a->n1 - a->n0 + pp.bn - 1) / pp.bn);
             const long pctas = (ptiles < num_sms / pp.cg ? ptiles : num_sms / pp.cg) * pp.cg;
-            if (split_ctas >= 2 * pctas) return e2c_gemm_splitk(a, sbn, S, stream);
+            if (split_ctas >= 2 * pctas) {
+                g_last_kernel = "splitk";
+                return e2c_gemm_splitk(a, sbn, S, stream);
+            }
         }
     }
     const Plan pl = pick_plan(a, num_sms);
     const bool pair = pl.cg == 2;
+    g_last_kernel = pair ? "persistent_pair" : "persistent";
     switch (a->epi) {
     case E2C_EPI_F32:
         if (perblock) return launch<128, 5, true, E2C_EPI_F32, 1>(a, st, dev, num_sms);

@@ -15,6 +15,10 @@ int e2cu_cuda(cudaError_t e, const char *what);
 int e2cu_launch(int rc, const char *what);
 /* the current device's status word (allocated on first use), NULL without a device */
 int *e2cu_status(void);
+/* a device failure was reported: every weight-streaming workspace is cleared before its next use */
+void e2cu_note_failure(void);
+/* clear `ws` (bytes) on `st` if a failure was reported since it was last cleared (*gen) */
+int e2cu_ws_refresh(int *ws, size_t bytes, int *gen, cudaStream_t st);
 
 int e2cu_w8_alloc(e2cuda_w8 *out, int N, int K);
 /* quad-interleaved e2_q8w -> row-major int8 rows of stride ld */

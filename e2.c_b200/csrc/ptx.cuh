@@ -150,6 +150,19 @@ E2C_DEV void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "me
 // every group but the most recently committed one has landed
 E2C_DEV void cp_async_wait_1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
 E2C_DEV void named_barrier(int id, int nthreads) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory"); }
+// named barrier that also returns whether `pred` held in every participating thread
+E2C_DEV bool named_barrier_and(int id, int nthreads, bool pred) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "bar.red.and.pred q, %2, %3, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"((uint32_t)pred), "r"(id), "r"(nthreads)
+        : "memory");
+    return r != 0;
+}
 
 // generic-proxy shared-memory writes become visible to the async proxy (tcgen05.mma operands)
 E2C_DEV void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }

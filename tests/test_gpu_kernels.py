@@ -547,3 +547,94 @@ def test_bounded_wait_expires_and_reports(e2c, torch_cuda):
     q, s = e2c.quantize_rows(x, 768)
     e2c.check()
     assert q.shape == (64, 768)
+
+
+# ------------------------------------------------------------------------------------------ short-M GEMM
+STREAM_CASES = [
+    # (M, N, K): the config-3 weights at M = 1 and 16, token counts around each MMA width, ragged
+    # N and K (partial weight tiles, zero-filled k-blocks), tiny problems (fewer tiles than SMs)
+    (1, 8192, 2048), (16, 8192, 2048), (1, 2048, 8192), (16, 2048, 8192), (1, 2048, 2048), (16, 2048, 2048),
+    (2, 1152, 768), (7, 768, 1152), (17, 1152, 768), (33, 768, 768), (64, 3072, 768), (100, 768, 3072),
+    (128, 8192, 2048), (200, 2048, 2048), (256, 1152, 768), (5, 300, 208), (16, 16, 128), (3, 130, 4096),
+]
+
+
+def _stream_gemm(e2c, torch, W, qd, sd, M, resid=None, n0=0, n1=None):
+    """The weight-streaming kernel itself (e2c_gemm_stream) with a zeroed workspace."""
+    lib = e2c.lib()
+    lib.e2c_gemm_stream.argtypes = [C.POINTER(e2c.GemmArgs), C.c_void_p]
+    lib.e2c_gemm_stream.restype = C.c_int
+    lib.e2c_gemm_ws_bytes.argtypes = [C.c_int]
+    lib.e2c_gemm_ws_bytes.restype = C.c_size_t
+    lib.e2cu_status.restype = C.c_void_p
+    n1 = W.N if n1 is None else n1
+    wsb = lib.e2c_gemm_ws_bytes(M)
+    ws = torch.zeros(wsb // 4 + 32, dtype=torch.int32, device="cuda")
+    y = torch.full((M, W.N), float("nan"), dtype=torch.float32, device="cuda")
+    a = e2c.gemm_args(W, qd, sd, M)
+    a.n0, a.n1 = n0, n1
+    a.epi, a.y, a.ldy = e2c.EPI_F32, y.data_ptr(), W.N
+    if resid is not None:
+        a.epi, a.resid, a.ldr = e2c.EPI_RESID, resid.data_ptr(), W.N
+    a.ws, a.ws_bytes = ws.data_ptr(), wsb
+    a.status = lib.e2cu_status()
+    assert lib.e2c_gemm_stream(C.byref(a), torch.cuda.current_stream().cuda_stream) == 0, lib.e2c_msg().decode()
+    e2c.check()
+    return y, ws
+
+
+@pytest.mark.parametrize("M,N,K", STREAM_CASES)
+def test_stream_gemm_bitexact(e2c, of, torch_cuda, M, N, K):
+    """The weight-streaming kernel (weight rows in the MMA's M slot, stream-K over the SMs, split
+    tiles reduced through the workspace) against the reference fold, bit for bit; the workspace is
+    zero again afterwards; the op API's GEMM (per-stream workspace) gives the same bits."""
+    torch = torch_cuda
+    rng = np.random.default_rng(M * 7 + N + 3 * K)
+    qa, a_s, w, ws = _gemm_inputs(rng, M, N, K, K)
+    W = e2c.Weight(w=w, scale=ws)
+    qd, sd = dev(torch, qa), dev(torch, a_s)
+    y, wsp = _stream_gemm(e2c, torch, W, qd, sd, M)
+    ey = of.gemm_plain(qa, a_s, w, ws, K)
+    assert f32_bits_equal(y.cpu().numpy(), ey), f"max abs diff {np.abs(y.cpu().numpy() - ey).max()}"
+    assert int(wsp.abs().sum().item()) == 0, "workspace not returned to zero"
+    y2 = e2c.i8_gemm(W, qd, sd, K).cpu().numpy()
+    e2c.check()
+    assert f32_bits_equal(y2, ey)
+
+
+def test_stream_gemm_residual_clamp_and_columns(e2c, of, torch_cuda):
+    """Residual epilogue, the e2_q8w output clamp and a column range [n0, n1) on the streaming
+    kernel; columns outside the range stay untouched."""
+    torch = torch_cuda
+    rng = np.random.default_rng(77)
+    M, N, K = 12, 1000, 1536
+    qa, a_s, w, ws = _gemm_inputs(rng, M, N, K, K)
+    W = e2c.Weight(w=w, scale=ws)
+    W.w8.out_min, W.w8.out_max = -0.5, 0.75
+    res = rng.standard_normal((M, N)).astype(np.float32)
+    qd, sd, rd = dev(torch, qa), dev(torch, a_s), dev(torch, res)
+    y, wsp = _stream_gemm(e2c, torch, W, qd, sd, M, resid=rd, n0=136, n1=900)
+    ey = of.gemm_plain(qa, a_s, w, ws, K, out_min=-0.5, out_max=0.75)
+    want = (ey + res).astype(np.float32)
+    got = y.cpu().numpy()
+    assert f32_bits_equal(got[:, 136:900], want[:, 136:900])
+    assert np.isnan(got[:, :136]).all() and np.isnan(got[:, 900:]).all()
+    assert int(wsp.abs().sum().item()) == 0
+
+
+def test_stream_gemm_back_to_back_distinct_weights(e2c, of, torch_cuda):
+    """A chain of launches over different weights on one stream and one workspace, with no
+    synchronisation between them (the decode pattern the kernel exists for): every output
+    bit-exact."""
+    torch = torch_cuda
+    rng = np.random.default_rng(91)
+    M = 16
+    outs = []
+    for N, K in [(8192, 2048), (2048, 8192), (2048, 2048), (3072, 2048)]:
+        qa, a_s, w, ws = _gemm_inputs(rng, M, N, K, K)
+        W = e2c.Weight(w=w, scale=ws)
+        y = e2c.i8_gemm(W, dev(torch, qa), dev(torch, a_s), K)
+        outs.append((y, of.gemm_plain(qa, a_s, w, ws, K), W))
+    e2c.check()
+    for y, ey, _ in outs:
+        assert f32_bits_equal(y.cpu().numpy(), ey)
