@@ -114,6 +114,8 @@ API = [
                                  vp, C.c_int, vp]),
     ("e2cuda_i8_linear_noalloc", C.c_int, [C.POINTER(W8), vp, C.c_int, C.c_int, vp, C.c_int, vp]),
     ("e2cuda_attention", C.c_int, [vp, vp, vp, C.c_int, vp, vp, C.c_int, C.c_int, C.c_int, C.c_float, vp]),
+    ("e2cuda_attention_gqa", C.c_int, [vp, vp, vp, C.c_int, vp, vp, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
+                                       C.c_float, vp]),
     ("e2cuda_ffn_create", vp, [C.POINTER(Q8W), C.POINTER(Q8W), C.POINTER(Q8W), f32p, C.c_float, C.c_int]),
     ("e2cuda_ffn_destroy", None, [vp]),
     ("e2cuda_ffn_forward", C.c_int, [vp, vp, C.c_int, vp, vp]),
@@ -284,6 +286,16 @@ def attention(q, k, vt, valid, B: int, S: int, H: int, scale: float, stream=None
     ctx = torch.empty((B * S, H * 256), dtype=torch.float32, device=q.device)
     _ok(lib().e2cuda_attention(_ptr(q), _ptr(k), _ptr(vt), vt.shape[-1], _ptr(valid), _ptr(ctx), B, S, H, scale,
                                _stream(stream)), "attention")
+    return ctx
+
+
+def attention_gqa(q, k, vt, valid, B: int, S: int, H: int, KV: int, D: int, scale: float, stream=None):
+    """bf16 attention with head dim D (64 or 256) and KV key/value heads: q [B*S][H*D], k [B*S][KV*D],
+    vt [B][KV*D][ldvt] -> ctx fp32 [B*S][H*D]."""
+    torch = _torch()
+    ctx = torch.empty((B * S, H * D), dtype=torch.float32, device=q.device)
+    _ok(lib().e2cuda_attention_gqa(_ptr(q), _ptr(k), _ptr(vt), vt.shape[-1], _ptr(valid), _ptr(ctx), B, S, H, KV, D,
+                                   scale, _stream(stream)), "attention_gqa")
     return ctx
 
 

@@ -42,28 +42,16 @@
 
 namespace {
 
-constexpr int HD = 256;        // head dim
 constexpr int TQ = 128;        // queries per unit
 constexpr int TKV = 64;        // keys per tile
 constexpr int SM_WARPS = 8;    // softmax warps
 constexpr int EP_WARPS = 4;    // epilogue warps
 constexpr int NTHREADS = 96 + 32 * SM_WARPS + 32 * EP_WARPS;
 constexpr float kRescaleLog2 = 8.0f;
-
-// shared memory map (bytes, from a 1024-aligned base)
-constexpr int Q_OFF = 0;                           // 4 x [128 q][64 d]   (16 KB each)
-constexpr int K_TILE = TKV * HD * 2;               // 4 x [64 k][64 d]    (8 KB each)
-constexpr int V_TILE = HD * TKV * 2;               // [256 d][64 k]       (32 KB)
-constexpr int K_OFF = Q_OFF + TQ * HD * 2;         // 2 buffers
-constexpr int V_OFF = K_OFF + 2 * K_TILE;          // 2 buffers
 // per epilogue warp, three 32-row x 16-column fp32 staging tiles for the ctx TMA stores (64-byte
 // swizzle: 16-byte chunk c of row r at chunk c ^ ((r >> 1) & 3)), used in turn
 constexpr int STG = 32 * 16 * 4;
 constexpr int NSTG = 3;
-constexpr int STG_OFF = V_OFF + 2 * V_TILE;
-constexpr int X_OFF = STG_OFF + EP_WARPS * NSTG * STG;  // row-max exchange [2 tile parities][2 halves][128]
-constexpr int INV_OFF = X_OFF + 2 * 2 * TQ * 4;        // 1 / rowsum of a unit's rows [2 unit parities][128]
-constexpr int BAR_OFF = INV_OFF + 2 * TQ * 4;
 // Q full / Q free / O free; K full x2, K empty x2, V full x2, V empty x2, PV done x4, S full x4,
 // P full x4, pair [2][4], final [4], drain
 enum {
@@ -83,16 +71,32 @@ enum {
     B_UD,  // [2 unit parities][4]: a unit's 1/rowsum of a lane quadrant is ready for its epilogue warp
     B_NUM = B_UD + 8
 };
-constexpr int SMEM_BYTES = BAR_OFF + B_NUM * 8 + 16;
-// No alignment slack: the dynamic shared memory of a kernel without static shared variables starts
-// 1024-byte aligned, which the kernel checks before using it (the swizzled tiles need it).
-constexpr int SMEM_ALLOC = SMEM_BYTES;
-static_assert(SMEM_ALLOC <= 232448, "shared memory");
+
+// shared memory map (bytes, from a 1024-aligned base) for head dim HD (64 or 256): Q as HD/64
+// panels of [128 q][64 d], K as HD/64 panels of [64 k][64 d] per buffer, V^T as [HD d][64 k]
+template <int HD>
+struct AttnSmem {
+    static_assert(HD == 64 || HD == 256, "head dim 64 or 256");
+    static constexpr int Q_OFF = 0;
+    static constexpr int K_TILE = TKV * HD * 2;
+    static constexpr int V_TILE = HD * TKV * 2;
+    static constexpr int K_OFF = Q_OFF + TQ * HD * 2;  // 2 buffers
+    static constexpr int V_OFF = K_OFF + 2 * K_TILE;   // 2 buffers
+    static constexpr int STG_OFF = V_OFF + 2 * V_TILE;
+    static constexpr int X_OFF = STG_OFF + EP_WARPS * NSTG * STG;  // row-max exchange [2 tile parities][2 halves][128]
+    static constexpr int INV_OFF = X_OFF + 2 * 2 * TQ * 4;        // 1 / rowsum of a unit's rows [2 unit parities][128]
+    static constexpr int BAR_OFF = INV_OFF + 2 * TQ * 4;
+    static constexpr int SMEM_BYTES = BAR_OFF + B_NUM * 8 + 16;
+    // No alignment slack: the dynamic shared memory of a kernel without static shared variables
+    // starts 1024-byte aligned, which the kernel checks before using it (the swizzled tiles need it).
+    static constexpr int SMEM_ALLOC = SMEM_BYTES;
+    static_assert(SMEM_ALLOC <= 232448, "shared memory");
+};
 
 struct AttnArgs {
     const uint8_t *valid;
     float *ctx;
-    int S, H, nkt, nqt, units;
+    int S, H, KV, nkt, nqt, units;
     float scale_log2;
     int *status;
 };
@@ -114,6 +118,7 @@ E2C_DEV Unit unit_of(int u, const AttnArgs &p) {
     return {b, rem / p.nqt, rem % p.nqt};
 }
 
+template <int HD>
 __global__ void __launch_bounds__(NTHREADS, 1)
     k_attention(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                 const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO, const AttnArgs p) {
@@ -124,6 +129,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         if (threadIdx.x == 0) record_status(p.status, E2C_ERR_SMEM_ALIGN);
         return;
     }
+    using L = AttnSmem<HD>;
+    constexpr int Q_OFF = L::Q_OFF, K_OFF = L::K_OFF, V_OFF = L::V_OFF, K_TILE = L::K_TILE, V_TILE = L::V_TILE;
+    constexpr int STG_OFF = L::STG_OFF, X_OFF = L::X_OFF, INV_OFF = L::INV_OFF, BAR_OFF = L::BAR_OFF;
     uint8_t *smem = smem_raw;
     const uint32_t sbase = smem_u32(smem);
     auto bar = [&](int i) { return sbase + BAR_OFF + 8u * i; };
@@ -174,10 +182,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             for (int u = blockIdx.x; u < p.units && ok; u += gridDim.x, nu++) {
                 const Unit w = unit_of(u, p);
                 const int row0 = w.b * S;
+                const int kvh = w.h / (p.H / p.KV);
                 // Q may be replaced once every QK product of the previous unit completed
                 if (!mbar_wait(bar(B_QE), (uint32_t)((nu & 1) ^ 1), p.status, E2C_ERR_WAIT_PRODUCER)) break;
                 mbar_arrive_expect_tx(bar(B_Q), TQ * HD * 2);
-                for (int i = 0; i < 4; i++)
+                for (int i = 0; i < HD / 64; i++)
                     tma_load_2d(sbase + Q_OFF + i * (TQ * 128), &tmQ, w.h * HD + 64 * i, row0 + w.qt * TQ, bar(B_Q));
                 for (int j = 0; j < nkt; j++, g++) {
                     const int kb = g & 1;
@@ -187,8 +196,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                         break;
                     }
                     mbar_arrive_expect_tx(bar(B_KF + kb), K_TILE);
-                    for (int i = 0; i < 4; i++)
-                        tma_load_2d(sbase + K_OFF + kb * K_TILE + i * (TKV * 128), &tmK, 64 * i, row0 + j * TKV, bar(B_KF + kb));
+                    for (int i = 0; i < HD / 64; i++)
+                        tma_load_2d(sbase + K_OFF + kb * K_TILE + i * (TKV * 128), &tmK, kvh * HD + 64 * i, row0 + j * TKV,
+                                    bar(B_KF + kb));
                 }
             }
             // the last loads must have landed before the CTA may exit
@@ -211,7 +221,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                         break;
                     }
                     mbar_arrive_expect_tx(bar(B_VF + vb), V_TILE);
-                    tma_load_2d(sbase + V_OFF + vb * V_TILE, &tmV, j * TKV, w.b * HD, bar(B_VF + vb));
+                    tma_load_2d(sbase + V_OFF + vb * V_TILE, &tmV, j * TKV, (w.b * p.KV + w.h / (p.H / p.KV)) * HD,
+                                bar(B_VF + vb));
                 }
             }
             for (int i = g - 2 < 0 ? 0 : g - 2; i < g; i++)
@@ -346,9 +357,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     }
                     tc_fence_after();
 #pragma unroll 1
-                    for (int c = 0; c < 4; c++) {
+                    for (int c = 0; c < HD / 64; c++) {  // this warp's half of O's HD columns
                         uint32_t o[32];
-                        const uint32_t ta = tmem + lane_addr + (uint32_t)(256 + 128 * kh + c * 32);
+                        const uint32_t ta = tmem + lane_addr + (uint32_t)(256 + (HD / 2) * kh + c * 32);
                         tmem_ld32(ta, o);
                         tmem_wait_ld();
 #pragma unroll
@@ -504,29 +515,15 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
 }
 
-}  // namespace
-
-extern "C" int e2c_attention(const void *q, const void *k, const void *vt, int ldvt, const uint8_t *valid, float *ctx,
-                             int B, int S, int H, float scale, int *status, void *stream) {
-    if (B <= 0 || S <= 0) return 0;
-    if (H <= 0 || ldvt < S || ldvt % 8 || (((uintptr_t)q | (uintptr_t)k | (uintptr_t)vt) & 15)) {
-        e2c_set_msg("attention: bad arguments (H=%d S=%d ldvt=%d; ldvt >= S, multiple of 8; 16-byte aligned)", H, S, ldvt);
-        return -1;
-    }
-    if ((uintptr_t)ctx & 15) {
-        e2c_set_msg("attention: ctx must be 16-byte aligned");
-        return -1;
-    }
+template <int HD>
+int launch_hd(const void *q, const void *k, const void *vt, int ldvt, const uint8_t *valid, float *ctx, int B, int S,
+              int H, int KV, float scale, int *status, cudaStream_t st, int dev, int num_sms) {
+    using L = AttnSmem<HD>;
     static E2cPerDev attr;  // the shared-memory opt-in, per device
-    const int dev = e2c_device();
-    const int num_sms = e2c_sm_count(dev);
-    if (!num_sms) {
-        e2c_set_msg("attention: no CUDA device");
-        return -2;
-    }
     if (!attr.get(dev)) {
-        if (cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_ALLOC) != cudaSuccess) {
-            e2c_set_msg("attention: cannot reserve %d bytes of shared memory", SMEM_ALLOC);
+        if (cudaFuncSetAttribute(k_attention<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM_ALLOC) != cudaSuccess) {
+            cudaGetLastError();
+            e2c_set_msg("attention: cannot reserve %d bytes of shared memory", L::SMEM_ALLOC);
             return -2;
         }
         attr.set(dev, 1);
@@ -534,8 +531,9 @@ extern "C" int e2c_attention(const void *q, const void *k, const void *vt, int l
     CUtensorMap tq, tk, tv, to;
     const uint64_t rows = (uint64_t)B * S;
     if (e2c_tmap_2d(&tq, q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)H * HD, rows, (uint64_t)H * HD * 2, 64, TQ) ||
-        e2c_tmap_2d(&tk, k, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, HD, rows, HD * 2, 64, TKV) ||
-        e2c_tmap_2d(&tv, vt, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)S, (uint64_t)B * HD, (uint64_t)ldvt * 2, 64, HD) ||
+        e2c_tmap_2d(&tk, k, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)KV * HD, rows, (uint64_t)KV * HD * 2, 64, TKV) ||
+        e2c_tmap_2d(&tv, vt, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)S, (uint64_t)B * KV * HD, (uint64_t)ldvt * 2, 64,
+                    HD) ||
         e2c_tmap_2d_sw64(&to, ctx, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)H * HD, rows, (uint64_t)H * HD * 4, 16, 32))
         return -3;
     AttnArgs a;
@@ -543,17 +541,49 @@ extern "C" int e2c_attention(const void *q, const void *k, const void *vt, int l
     a.ctx = ctx;
     a.S = S;
     a.H = H;
+    a.KV = KV;
     a.nkt = (S + TKV - 1) / TKV;
     a.nqt = (S + TQ - 1) / TQ;
     a.units = B * H * a.nqt;
     a.scale_log2 = scale * 1.4426950408889634f;
     a.status = status;
     const int grid = a.units < num_sms ? a.units : num_sms;
-    e2c_launch(k_attention, dim3(grid), dim3(NTHREADS), SMEM_ALLOC, (cudaStream_t)stream, tq, tk, tv, to, a);
+    e2c_launch(k_attention<HD>, dim3(grid), dim3(NTHREADS), L::SMEM_ALLOC, st, tq, tk, tv, to, a);
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
         e2c_set_msg("attention launch: %s", cudaGetErrorString(e));
         return -2;
     }
     return 0;
+}
+
+}  // namespace
+
+extern "C" int e2c_attention_gqa(const void *q, const void *k, const void *vt, int ldvt, const uint8_t *valid, float *ctx,
+                                 int B, int S, int H, int KV, int D, float scale, int *status, void *stream) {
+    if (B <= 0 || S <= 0) return 0;
+    if (H <= 0 || KV <= 0 || H % KV || (D != 64 && D != 256) || ldvt < S || ldvt % 8 ||
+        (((uintptr_t)q | (uintptr_t)k | (uintptr_t)vt) & 15)) {
+        e2c_set_msg("attention: bad arguments (H=%d KV=%d D=%d S=%d ldvt=%d; KV divides H, D 64 or 256, ldvt >= S and "
+                    "a multiple of 8, 16-byte aligned operands)", H, KV, D, S, ldvt);
+        return -1;
+    }
+    if ((uintptr_t)ctx & 15) {
+        e2c_set_msg("attention: ctx must be 16-byte aligned");
+        return -1;
+    }
+    const int dev = e2c_device();
+    const int num_sms = e2c_sm_count(dev);
+    if (!num_sms) {
+        e2c_set_msg("attention: no CUDA device");
+        return -2;
+    }
+    cudaStream_t st = (cudaStream_t)stream;
+    return D == 256 ? launch_hd<256>(q, k, vt, ldvt, valid, ctx, B, S, H, KV, scale, status, st, dev, num_sms)
+                    : launch_hd<64>(q, k, vt, ldvt, valid, ctx, B, S, H, KV, scale, status, st, dev, num_sms);
+}
+
+extern "C" int e2c_attention(const void *q, const void *k, const void *vt, int ldvt, const uint8_t *valid, float *ctx,
+                             int B, int S, int H, float scale, int *status, void *stream) {
+    return e2c_attention_gqa(q, k, vt, ldvt, valid, ctx, B, S, H, 1, 256, scale, status, stream);
 }

@@ -338,6 +338,16 @@ int e2cuda_attention(const void *q, const void *k, const void *vt, int ldvt, con
     return e2cu_launch(e2c_attention(q, k, vt, ldvt, valid, ctx, B, S, H, scale, e2cu_status(), stream), "attention");
 }
 
+int e2cuda_attention_gqa(const void *q, const void *k, const void *vt, int ldvt, const uint8_t *valid, float *ctx,
+                         int B, int S, int H, int KV, int D, float scale, void *stream) {
+    if (!q || !k || !vt || !ctx) {
+        e2cu_err("attention_gqa: bad arguments");
+        return -1;
+    }
+    return e2cu_launch(e2c_attention_gqa(q, k, vt, ldvt, valid, ctx, B, S, H, KV, D, scale, e2cu_status(), stream),
+                       "attention_gqa");
+}
+
 /* ------------------------------------------------------------------ fused FFN (config 1) */
 struct e2cuda_ffn {
     int D, I, max_tokens;

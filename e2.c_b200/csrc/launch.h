@@ -144,6 +144,10 @@ int e2c_l2norm_rows(float *y, const uint8_t *valid, int B, int S, int D, void *s
 /* ---- attention: bf16 Q [B*S][H*256], K [B*S][256], V^T [B][256][ldvt] -> ctx fp32 [B*S][H*256] */
 int e2c_attention(const void *q, const void *k, const void *vt, int ldvt, const uint8_t *valid,
                   float *ctx, int B, int S, int H, float scale, int *status, void *stream);
+/* the same for head dim D (64 or 256) and KV key/value heads (KV divides H; query head h reads KV
+ * head h / (H / KV)): Q [B*S][H*D], K [B*S][KV*D], V^T [B][KV*D][ldvt] -> ctx [B*S][H*D] */
+int e2c_attention_gqa(const void *q, const void *k, const void *vt, int ldvt, const uint8_t *valid, float *ctx,
+                      int B, int S, int H, int KV, int D, float scale, int *status, void *stream);
 
 /* ---- self-test of the bounded wait (selftest.cu): one warp waits on an mbarrier that receives
  * its arrival first (arrive != 0) or never (arrive == 0). *completed is 1 if the wait completed, 0

@@ -173,6 +173,12 @@ int e2cuda_i8_linear_noalloc(const e2cuda_w8 *w, const float *x, int M, int ablk
  * valid [B*S] or NULL -> ctx fp32 [B*S][H*256]. scale multiplies the logits. */
 int e2cuda_attention(const void *q, const void *k, const void *vt, int ldvt, const uint8_t *valid,
                      float *ctx, int B, int S, int H, float scale, void *stream);
+/* The same for head dim D = 64 or 256 and KV key/value heads (KV divides H; query head h attends with
+ * KV head h / (H / KV)): q [B*S][H*D], k [B*S][KV*D], vt [B][KV*D][ldvt] -> ctx fp32 [B*S][H*D]. D = 64
+ * with KV = H is the vision tower's attention (e2.c src/vision.c:540-571: 12 heads of 64, scale 1,
+ * up to 2520 patches); D = 256 with KV = 1 is e2cuda_attention. */
+int e2cuda_attention_gqa(const void *q, const void *k, const void *vt, int ldvt, const uint8_t *valid,
+                         float *ctx, int B, int S, int H, int KV, int D, float scale, void *stream);
 
 /* ------------------------------------------------------------------ fused FFN block (config 1) */
 typedef struct e2cuda_ffn e2cuda_ffn;

@@ -638,3 +638,79 @@ def test_stream_gemm_back_to_back_distinct_weights(e2c, of, torch_cuda):
     e2c.check()
     for y, ey, _ in outs:
         assert f32_bits_equal(y.cpu().numpy(), ey)
+
+
+# ------------------------------------------------------------------------------------------ GQA / vision attention
+def _attn_ref_gqa(q, k, v, valid, B, S, H, KV, D, scale):
+    """fp64 attention with KV heads (query head h reads KV head h // (H // KV)); invalid query rows 0."""
+    out = np.zeros((B * S, H * D), np.float64)
+    for b in range(B):
+        keys = np.arange(S) if valid is None else np.nonzero(valid[b])[0]
+        for h in range(H):
+            kvh = h // (H // KV)
+            if len(keys) == 0:
+                continue
+            qh = q[b * S:(b + 1) * S, h * D:(h + 1) * D].astype(np.float64)
+            kb = k[b * S + keys, kvh * D:(kvh + 1) * D].astype(np.float64)
+            vb = v[b * S + keys, kvh * D:(kvh + 1) * D].astype(np.float64)
+            lg = qh @ kb.T * scale
+            lg -= lg.max(axis=1, keepdims=True)
+            pr = np.exp(lg)
+            pr /= pr.sum(axis=1, keepdims=True)
+            o = pr @ vb
+            if valid is not None:
+                o[valid[b] == 0] = 0
+            out[b * S:(b + 1) * S, h * D:(h + 1) * D] = o
+    return out
+
+
+@pytest.mark.parametrize("B,S,H,KV,D,scale,masked", [
+    (1, 2520, 12, 12, 64, 1.0, False),     # the vision tower: 2520 patches, 12 heads of 64, scale 1
+    (2, 1000, 12, 12, 64, 0.125, True),    # fewer patches, masks, 1/sqrt(64)
+    (3, 300, 12, 4, 64, 0.125, True),      # grouped KV heads at D = 64
+    (2, 512, 4, 2, 256, 1 / 16, True),     # two KV heads at D = 256
+    (1, 77, 2, 1, 64, 1.0, False),         # one partial tile
+])
+def test_attention_gqa_vs_fp64(e2c, of, torch_cuda, B, S, H, KV, D, scale, masked):
+    """The attention kernel at head dim 64 (the vision tower's) and with several KV heads, against fp64
+    of the same bf16 inputs, and against the checker's fp32 attention (e2o_attention_f32, restating
+    e2.c src/text.c:702-741 and src/vision.c:540-571) for the first sequence."""
+    torch = torch_cuda
+    rng = np.random.default_rng(S * 13 + H + KV + D)
+    qf = torch.from_numpy(rng.standard_normal((B * S, H * D)).astype(np.float32)).to(torch.bfloat16)
+    kf = torch.from_numpy(rng.standard_normal((B * S, KV * D)).astype(np.float32)).to(torch.bfloat16)
+    vf = torch.from_numpy(rng.standard_normal((B * S, KV * D)).astype(np.float32)).to(torch.bfloat16)
+    valid = None
+    if masked:
+        valid = np.ones((B, S), np.uint8)
+        valid[-1, S - S // 5:] = 0
+        valid[0, 3:11] = 0
+    ldvt = (S + 7) // 8 * 8
+    vt = torch.zeros((B, KV * D, ldvt), dtype=torch.bfloat16)
+    vt[:, :, :S] = vf.reshape(B, S, KV * D).transpose(1, 2)
+    vd = None if valid is None else dev(torch, valid.reshape(-1))
+    ctx = e2c.attention_gqa(qf.cuda(), kf.cuda(), vt.cuda(), vd, B, S, H, KV, D, scale)
+    e2c.check()
+    got = ctx.cpu().numpy()
+    q32, k32, v32 = (t.float().numpy() for t in (qf, kf, vf))
+    want = _attn_ref_gqa(q32, k32, v32, valid, B, S, H, KV, D, scale)
+    for b in range(B):
+        for h in range(H):
+            rows = slice(b * S, (b + 1) * S)
+            g = got[rows, h * D:(h + 1) * D]
+            w = want[rows, h * D:(h + 1) * D]
+            live = np.linalg.norm(w, axis=1) > 0
+            if valid is not None:
+                assert np.all(g[valid[b] == 0] == 0)
+            err = np.linalg.norm(g[live] - w[live], axis=1) / np.linalg.norm(w[live], axis=1)
+            assert err.max() < 1e-2, f"b={b} h={h} worst row rel err {err.max()}"
+            assert cosine_rows(g[live], w[live]).min() > 0.9999
+    # the checker's own fp32 attention on sequence 0
+    want0 = np.zeros((S, H * D), np.float32)
+    vb0 = None if valid is None else np.ascontiguousarray(valid[0])
+    qb, kb, vb = (np.ascontiguousarray(t[:S]) for t in (q32, k32, v32))
+    of.port().e2o_attention_f32(of.port().e2o_port_kernels(0), qb.ctypes.data_as(of.f32p), kb.ctypes.data_as(of.f32p),
+                                vb.ctypes.data_as(of.f32p), want0.ctypes.data_as(of.f32p),
+                                None if vb0 is None else vb0.ctypes.data_as(of.u8p), S, H, KV, D, scale)
+    live = np.linalg.norm(want0, axis=1) > 0
+    assert cosine_rows(got[:S][live], want0[live]).min() > 0.9999
