@@ -711,7 +711,9 @@ def config1(args) -> int:
 # one KV head of 256), the per-launch algorithmic work each is measured against, and the launches of
 # each per layer. Weights are quantised N(0, 0.02), activations per-token quantised N(0, 1).
 KERNELS = ("gate_up", "gate_up_q", "qkv", "o_proj", "down", "o_proj_norm", "down_norm", "attention", "quantize",
-           "quantize_ctx", "norm_add", "o_proj_pb", "down_pb")
+           "quantize_ctx", "norm_add", "o_proj_pb", "down_pb", "attention_vision")
+# attention_vision: the vision tower's attention (e2.c src/vision.c:540-571), 2520 patches per image,
+# 12 heads of 64 with their own K and V, scale 1; M tokens = M // 2520 images
 # *_pb: the same GEMMs with per-128-block activation scales (the reference engine's own recipe)
 # the kernels an encoder layer runs (hidden 768, FFN 1152, per-token scales): the residual norms fused
 # into o_proj and down and h's quantiser into gate|up, or with E2C_FUSED_NORM=0 / E2C_FUSED_GELU=0
@@ -737,6 +739,10 @@ def kernel_work(name: str, M: int) -> dict:
         return {"ops": 2.0 * M * N * K, "bytes": M * K + a_scales + N * K + 4 * N + out_bytes, "per_layer": 1}
     if name == "attention":
         return {"ops": 4.0 * M * SEQ * Dh * H, "bytes": M * (H + 2) * Dh * 2 + 4 * M * H * Dh, "per_layer": 1}
+    if name == "attention_vision":
+        P, Hv, Dv = 2520, 12, 64
+        Mv = max(1, M // P) * P
+        return {"ops": 4.0 * Mv * P * Dv * Hv, "bytes": Mv * 3 * Hv * Dv * 2 + 4 * Mv * Hv * Dv, "per_layer": 1}
     if name in ("quantize", "quantize_ctx"):
         K = I if name == "quantize" else D
         return {"ops": 0.0, "bytes": M * (4 * K + K + 4), "per_layer": 1}
@@ -813,6 +819,13 @@ def kernel_runner(name: str, M: int, dev, stream):
         k = torch.randn((M, Dh), device=dev, generator=g).to(torch.bfloat16)
         vt = torch.randn((B, Dh, SEQ), device=dev, generator=g).to(torch.bfloat16)
         return (lambda: e2c.attention(q, k, vt, None, B, SEQ, H, 1.0 / 16, stream)), [q, k, vt]
+    if name == "attention_vision":
+        P, Hv, Dv = 2520, 12, 64
+        B = max(1, M // P)
+        q = torch.randn((B * P, Hv * Dv), device=dev, generator=g).to(torch.bfloat16)
+        k = torch.randn((B * P, Hv * Dv), device=dev, generator=g).to(torch.bfloat16)
+        vt = torch.randn((B, Hv * Dv, P), device=dev, generator=g).to(torch.bfloat16)
+        return (lambda: e2c.attention_gqa(q, k, vt, None, B, P, Hv, Hv, Dv, 1.0, stream)), [q, k, vt]
     if name in ("quantize", "quantize_ctx"):
         K = I if name == "quantize" else D
         x = torch.randn((M, K), device=dev, generator=g)
@@ -860,7 +873,7 @@ def binding_roofline(name: str, M: int, ms: float) -> dict:
     and the HBM time at the measured peaks is longer) and the fraction of it achieved."""
     p = peaks()
     wk = kernel_work(name, M)
-    tpeak, hbm = (p["bf16_tflops"] if name == "attention" else 2.0 * p["bf16_tflops"]), p["hbm_gbs"]
+    tpeak, hbm = (p["bf16_tflops"] if name.startswith("attention") else 2.0 * p["bf16_tflops"]), p["hbm_gbs"]
     bound = "tensor" if wk["ops"] / (tpeak * 1e12) >= wk["bytes"] / (hbm * 1e9) else "hbm"
     if bound == "tensor":
         peak, achieved, unit = tpeak, wk["ops"] / (ms / 1e3) / 1e12, "TFLOP/s"

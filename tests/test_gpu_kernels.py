@@ -714,3 +714,21 @@ def test_attention_gqa_vs_fp64(e2c, of, torch_cuda, B, S, H, KV, D, scale, maske
                                 None if vb0 is None else vb0.ctypes.data_as(of.u8p), S, H, KV, D, scale)
     live = np.linalg.norm(want0, axis=1) > 0
     assert cosine_rows(got[:S][live], want0[live]).min() > 0.9999
+
+
+@pytest.mark.parametrize("N,K", [(768, 768), (3072, 768), (768, 3072), (2304, 768)])
+def test_gemm_vision_tower_shapes(e2c, of, syn, torch_cuda, N, K):
+    """The vision tower's projections (e2.c src/vision.c: 2520 patches, hidden 768, MLP 3072; q|k|v
+    concatenated) on the GEMM kernels, per-token scales, bit-exact to the reference fold."""
+    torch = torch_cuda
+    M = 2520
+    rng = np.random.default_rng(N + K)
+    x = syn.activations(rng, M, K)
+    q, s = e2c.quantize_rows(dev(torch, x), K)
+    wq, ws = syn.quantize_weight_rows((rng.standard_normal((N, K), dtype=np.float32) * np.float32(0.02)))
+    W = e2c.Weight(w=wq, scale=ws)
+    y = e2c.i8_gemm(W, q, s, K).cpu().numpy()
+    e2c.check()
+    eq, es = of.quantize_signed(x, K)
+    assert np.array_equal(q.cpu().numpy(), eq)
+    assert f32_bits_equal(y, of.gemm_plain(eq, es, wq, ws, K))
