@@ -711,7 +711,9 @@ def config1(args) -> int:
 # one KV head of 256), the per-launch algorithmic work each is measured against, and the launches of
 # each per layer. Weights are quantised N(0, 0.02), activations per-token quantised N(0, 1).
 KERNELS = ("gate_up", "gate_up_q", "qkv", "o_proj", "down", "o_proj_norm", "down_norm", "attention", "quantize",
-           "quantize_ctx", "norm_add", "o_proj_pb", "down_pb", "attention_vision")
+           "quantize_ctx", "norm_add", "o_proj_pb", "down_pb", "attention_vision", "gemm_small")
+# gemm_small: the config-3 GEMM (K, N) = (2048, 8192) at M = --tokens rows (1..256: the weight-streaming
+# kernel), per-token scales, fp32 output
 # attention_vision: the vision tower's attention (e2.c src/vision.c:540-571), 2520 patches per image,
 # 12 heads of 64 with their own K and V, scale 1; M tokens = M // 2520 images
 # *_pb: the same GEMMs with per-128-block activation scales (the reference engine's own recipe)
@@ -739,6 +741,9 @@ def kernel_work(name: str, M: int) -> dict:
         return {"ops": 2.0 * M * N * K, "bytes": M * K + a_scales + N * K + 4 * N + out_bytes, "per_layer": 1}
     if name == "attention":
         return {"ops": 4.0 * M * SEQ * Dh * H, "bytes": M * (H + 2) * Dh * 2 + 4 * M * H * Dh, "per_layer": 1}
+    if name == "gemm_small":
+        K, N = 2048, 8192
+        return {"ops": 2.0 * M * N * K, "bytes": M * K + 4 * M + N * K + 4 * N + 4 * M * N, "per_layer": 1}
     if name == "attention_vision":
         P, Hv, Dv = 2520, 12, 64
         Mv = max(1, M // P) * P
@@ -819,6 +824,24 @@ def kernel_runner(name: str, M: int, dev, stream):
         k = torch.randn((M, Dh), device=dev, generator=g).to(torch.bfloat16)
         vt = torch.randn((B, Dh, SEQ), device=dev, generator=g).to(torch.bfloat16)
         return (lambda: e2c.attention(q, k, vt, None, B, SEQ, H, 1.0 / 16, stream)), [q, k, vt]
+    if name == "gemm_small":
+        K, N = 2048, 8192
+        lib = e2c.lib()
+        lib.e2c_gemm_ws_bytes.argtypes = [C.c_int]
+        lib.e2c_gemm_ws_bytes.restype = C.c_size_t
+        lib.e2cu_status.restype = C.c_void_p
+        wq, ws_ = syn.quantize_weight_rows((rng.standard_normal((N, K)) * 0.02).astype(np.float32))
+        W = e2c.Weight(w=wq, scale=ws_)
+        qa, qs = qin(K)
+        y = torch.empty((M, N), dtype=torch.float32, device=dev)
+        wsb = lib.e2c_gemm_ws_bytes(M)
+        wsp = torch.zeros(max(wsb // 4, 1) + 32, dtype=torch.int32, device=dev)
+        a = e2c.gemm_args(W, qa, qs, M)
+        a.epi, a.y, a.ldy = e2c.EPI_F32, y.data_ptr(), N
+        a.status = lib.e2cu_status()
+        if wsb:
+            a.ws, a.ws_bytes = wsp.data_ptr(), wsb
+        return (lambda: e2c.gemm_raw(a, stream)), [W, qa, qs, y, wsp]
     if name == "attention_vision":
         P, Hv, Dv = 2520, 12, 64
         B = max(1, M // P)

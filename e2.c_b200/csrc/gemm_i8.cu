@@ -919,11 +919,14 @@ extern "C" int e2c_gemm(const e2c_gemm_args *a, void *stream) {
     const bool perblock = a->ablk != a->K;
     if (stream_path_on() && a->ws && !perblock && (a->epi == E2C_EPI_F32 || a->epi == E2C_EPI_RESID) && a->M <= 256 &&
         a->ws_bytes >= e2c_gemm_stream_ws_bytes(a->M, num_sms) && !((uintptr_t)a->ws & 127)) {
-        // short activation matrices: stream the weight over every SM (the weight in the MMA's M
-        // slot) unless the persistent kernel already fills the device
+        // short activation matrices against a long weight: stream the weight over every SM (the
+        // weight in the MMA's M slot). It pays where each CTA streams at least 8 of the 16 KB weight
+        // tiles, so its fixed costs (launch ramp, the split tiles' reductions) amortise; shorter
+        // weights go to the split-K kernel below, which measured faster there (4-17 MB at M <= 128).
         const Plan pp = pick_plan(a, num_sms);
         const long ptiles = (long)((a->M + BM * pp.cg - 1) / (BM * pp.cg)) * ((a->n1 - a->n0 + pp.bn - 1) / pp.bn);
-        if (a->M <= 64 || ptiles * pp.cg < num_sms) {
+        const long wtiles = (long)((a->n1 - a->n0 + 127) / 128) * ((a->K + 127) / 128);
+        if (wtiles >= 8L * num_sms && (a->M <= 64 || ptiles * pp.cg < num_sms)) {
             g_last_kernel = "stream";
             return e2c_gemm_stream(a, stream);
         }

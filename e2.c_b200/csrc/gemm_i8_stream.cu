@@ -26,9 +26,7 @@
 // behind: the owner of the workspace clears it before reusing it.
 //
 // Warps: 0 TMA producer, 1 TMEM owner + MMA issuer, 2..5 epilogue (warp w drains TMEM lanes
-// 32 (w % 4) .. +31). Shared memory stays near 100 KB for MT <= 128 so that two CTAs fit on an SM:
-// with programmatic dependent launch the next GEMM's CTAs start streaming their weights beside this
-// one's tail. Every wait is bounded; no TMA load uses multicast.
+// 32 (w % 4) .. +31). Every wait is bounded; no TMA load uses multicast.
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <math.h>
@@ -53,7 +51,9 @@ struct StreamSmem {
     static constexpr int W_BYTES = BW * BK;
     static constexpr int X_BYTES = MT * BK;
     static constexpr int STAGE = W_BYTES + X_BYTES;
-    static constexpr int STAGES = MT <= 32 ? 5 : MT <= 64 ? 4 : MT <= 128 ? 3 : 4;
+    // deep rings (180-200 KB in flight per SM): a CTA's whole range of a 4-17 MB weight is requested
+    // at once, and a long stream keeps enough bytes in flight to cover HBM latency
+    static constexpr int STAGES = MT <= 16 ? 10 : MT <= 32 ? 9 : MT <= 64 ? 8 : MT <= 128 ? 6 : 4;
     static constexpr int BAR_OFF = STAGES * STAGE;
     static constexpr int NBAR = 2 * STAGES + 5;  // full[S], empty[S], tfull[2], tempty[2], mma_done
     static constexpr int SLOT_OFF = BAR_OFF + NBAR * 8;  // TMEM address, then the "last" flag
@@ -248,12 +248,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 }
                 if (whole) {
                     if (nok) {
+                        // the chunk's scales first: loads issued back to back, not one per store
+                        float as16[16];
+#pragma unroll
+                        for (int u = 0; u < 16; u++) as16[u] = c + u < M ? __ldg(p.a_scale + (size_t)(c + u) * nbs) : 0.f;
 #pragma unroll
                         for (int u = 0; u < 16; u++) {
                             const int m = c + u;
-                            if (m < M)
-                                p.y[(size_t)m * p.ldy + n] =
-                                    fold((int)v[u], __ldg(p.a_scale + (size_t)m * nbs), wsn, p, clamp, m, n);
+                            if (m < M) p.y[(size_t)m * p.ldy + n] = fold((int)v[u], as16[u], wsn, p, clamp, m, n);
                         }
                     }
                 } else {
@@ -275,11 +277,25 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 named_barrier(1, EPI_THREADS);  // the flag is read before the next run rewrites it
                 if (last) {
                     __threadfence();
-                    for (int m = 0; m < M; m++) {
-                        int *src = part + (size_t)m * BW;
-                        const int sum = __ldcg(src);
-                        __stcg(src, 0);
-                        if (nok) p.y[(size_t)m * p.ldy + n] = fold(sum, __ldg(p.a_scale + (size_t)m * nbs), wsn, p, clamp, m, n);
+                    // 16 rows at a time: the sums and scales are loaded back to back before any of
+                    // the stores (which could alias them as far as the compiler knows) is issued
+#pragma unroll 1
+                    for (int m0 = 0; m0 < M; m0 += 16) {
+                        int sum[16];
+                        float as16[16];
+#pragma unroll
+                        for (int u = 0; u < 16; u++) {
+                            sum[u] = m0 + u < M ? __ldcg(part + (size_t)(m0 + u) * BW) : 0;
+                            as16[u] = m0 + u < M ? __ldg(p.a_scale + (size_t)(m0 + u) * nbs) : 0.f;
+                        }
+#pragma unroll
+                        for (int u = 0; u < 16; u++) {
+                            const int m = m0 + u;
+                            if (m < M) {
+                                __stcg(part + (size_t)m * BW, 0);
+                                if (nok) p.y[(size_t)m * p.ldy + n] = fold(sum[u], as16[u], wsn, p, clamp, m, n);
+                            }
+                        }
                     }
                     if (leader) atomicExch(cnt + slot, 0);
                 }
