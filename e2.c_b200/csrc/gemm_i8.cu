@@ -492,17 +492,28 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                         const float4 ca = *reinterpret_cast<const float4 *>(cst2 + 128 + 8 * c8 + 4 * k);
                         const float4 cb = *reinterpret_cast<const float4 *>(cst2 + 192 + 8 * c8 + 4 * k);
                         const float cav[4] = {ca.x, ca.y, ca.z, ca.w}, cbv[4] = {cb.x, cb.y, cb.z, cb.w};
+                        // two pairs per packed f32x2 operation; lane for lane the scalar operations
+                        // (a = float(acc) (ws g) rs; va = fma(a, cos, -(b sin)), vb = fma(a, sin, b cos)),
+                        // no packed product feeding a packed add
+                        const float2 rs2 = make_float2(rs, rs);
 #pragma unroll
-                        for (int e = 0; e < 4; e++) {
+                        for (int e = 0; e < 4; e += 2) {
                             const int i = 4 * k + e;
-                            const float a = __fmul_rn(__fmul_rn(__int2float_rn((int)ra[i]), cav[e]), rs);
-                            const float b = __fmul_rn(__fmul_rn(__int2float_rn((int)rb[i]), cbv[e]), rs);
+                            const float2 a = mul2_rn(mul2_rn(make_float2(__int2float_rn((int)ra[i]), __int2float_rn((int)ra[i + 1])),
+                                                             make_float2(cav[e], cav[e + 1])),
+                                                     rs2);
+                            const float2 b = mul2_rn(mul2_rn(make_float2(__int2float_rn((int)rb[i]), __int2float_rn((int)rb[i + 1])),
+                                                             make_float2(cbv[e], cbv[e + 1])),
+                                                     rs2);
                             if (!is_v) {
-                                va[i] = __fmaf_rn(a, cs[i], -__fmul_rn(b, sn[i]));
-                                vb[i] = __fmaf_rn(a, sn[i], __fmul_rn(b, cs[i]));
+                                const float2 c2 = make_float2(cs[i], cs[i + 1]), s2 = make_float2(sn[i], sn[i + 1]);
+                                const float2 x = fma2_rn(a, c2, mul2_rn(b, make_float2(-s2.x, -s2.y)));
+                                const float2 y = fma2_rn(a, s2, mul2_rn(b, c2));
+                                va[i] = x.x, va[i + 1] = x.y;
+                                vb[i] = y.x, vb[i + 1] = y.y;
                             } else {
-                                va[i] = a;
-                                vb[i] = b;
+                                va[i] = a.x, va[i + 1] = a.y;
+                                vb[i] = b.x, vb[i + 1] = b.y;
                             }
                         }
                     }
