@@ -712,8 +712,8 @@ def config1(args) -> int:
 # each per layer. Weights are quantised N(0, 0.02), activations per-token quantised N(0, 1).
 KERNELS = ("gate_up", "gate_up_q", "qkv", "o_proj", "down", "o_proj_norm", "down_norm", "attention", "quantize",
            "quantize_ctx", "norm_add", "o_proj_pb", "down_pb", "attention_vision", "gemm_small")
-# gemm_small: the config-3 GEMM (K, N) = (2048, 8192) at M = --tokens rows (1..256: the weight-streaming
-# kernel), per-token scales, fp32 output
+# gemm_small: the config-3 GEMM (K, N) = (2048, 8192) at M = --tokens rows (1..256) on the
+# weight-streaming kernel itself (e2c_gemm_stream), per-token scales, fp32 output
 # attention_vision: the vision tower's attention (e2.c src/vision.c:540-571), 2520 patches per image,
 # 12 heads of 64 with their own K and V, scale 1; M tokens = M // 2520 images
 # *_pb: the same GEMMs with per-128-block activation scales (the reference engine's own recipe)
@@ -839,9 +839,11 @@ def kernel_runner(name: str, M: int, dev, stream):
         a = e2c.gemm_args(W, qa, qs, M)
         a.epi, a.y, a.ldy = e2c.EPI_F32, y.data_ptr(), N
         a.status = lib.e2cu_status()
-        if wsb:
-            a.ws, a.ws_bytes = wsp.data_ptr(), wsb
-        return (lambda: e2c.gemm_raw(a, stream)), [W, qa, qs, y, wsp]
+        a.ws, a.ws_bytes = wsp.data_ptr(), wsb
+        lib.e2c_gemm_stream.argtypes = [C.POINTER(e2c.GemmArgs), C.c_void_p]
+        lib.e2c_gemm_stream.restype = C.c_int
+        run = lambda: e2c._ok(lib.e2c_gemm_stream(C.byref(a), e2c._stream(stream)), "gemm_stream")
+        return run, [W, qa, qs, y, wsp, a]
     if name == "attention_vision":
         P, Hv, Dv = 2520, 12, 64
         B = max(1, M // P)
