@@ -49,6 +49,7 @@ struct e2cuda_encoder {
     int32_t *ids;
     uint8_t *valid;
     float *out, *res, *tmp, *ctx, *h, *pooled, *h1;
+    float *qkvf, *guf; /* per-128-block mode only: the q|k|v and gate|up GEMMs' fp32 outputs */
     int8_t *qa, *qb, *pq;
     float *qs, *qsb, *ps;
     int fused_norm, fused_gelu;
@@ -121,7 +122,7 @@ void e2cuda_encoder_destroy(e2cuda_encoder *e) {
     e2cuda_w8_free(&e->dense2);
     void *dev[] = { e->table, e->table_scale, e->norms, e->rope_cos, e->rope_sin, e->ids, e->valid, e->out, e->res,
                     e->tmp, e->ctx, e->h, e->pooled, e->h1, e->qa, e->qb, e->pq, e->qs, e->qsb, e->ps, e->Q, e->K,
-                    e->Vt, e->gws };
+                    e->Vt, e->gws, e->qkvf, e->guf };
     for (size_t i = 0; i < sizeof dev / sizeof dev[0]; i++)
         if (dev[i]) cudaFree(dev[i]);
     if (e->host_out) cudaFreeHost(e->host_out);
@@ -261,6 +262,11 @@ e2cuda_encoder *e2cuda_encoder_create(const e2cuda_encoder_desc *d, int max_toke
             DALLOC(e->pq, MB * (size_t)(e->DH > D ? e->DH : D)) ||
             DALLOC(e->ps, sizeof(float) * MB * (size_t)((e->DH > D ? e->DH : D) / 128 + 1)))
             goto fail;
+        /* per-128-block activation scales: the QKV and GELU epilogues need whole-row (per-token)
+         * scales, so those GEMMs write fp32 and row kernels finish them */
+        if (e->ablk != D && (DALLOC(e->qkvf, sizeof(float) * M * (size_t)(GD + 2 * e->Dh)) ||
+                             DALLOC(e->guf, sizeof(float) * M * (size_t)(2 * e->I))))
+            goto fail;
     }
     /* o_proj / down run with the residual norms in their epilogue (one launch instead of two, the
      * GEMM output never written) where the shape allows; E2C_FUSED_NORM=0 selects the GEMM + row
@@ -340,6 +346,18 @@ static int encode(e2cuda_encoder *e, int B, int S, int has_valid, cudaStream_t s
     for (int l = 0; l < L; l++) {
         /* q|k|v with per-head RMSNorm + RoPE */
         e2cu_gemm_args(&a, &e->wqkv[l], e->qb, e->qsb, M, ab_d);
+        if (e->ablk != D) {
+            /* per-block scales: the GEMM folds block by block into fp32, a row kernel does the rest */
+            a.epi = E2C_EPI_F32;
+            a.y = e->qkvf;
+            a.ldy = GD + 2 * e->Dh;
+            if (e2cu_launch(e2c_gemm(&a, st), "encoder qkv") ||
+                e2cu_launch(e2c_qkv_post(e->qkvf, GD + 2 * e->Dh, e->H, nrm(e, l, 4), nrm(e, l, 5), e->eps, e->rope_cos,
+                                         e->rope_sin, e->max_seq, S, e->Q, e->K, e->Vt, ldvt, M, st),
+                            "encoder qkv post"))
+                return -1;
+            n += 1;
+        } else {
         a.epi = E2C_EPI_QKV;
         a.nq = e->H;
         a.q_out = e->Q;
@@ -354,6 +372,7 @@ static int encode(e2cuda_encoder *e, int B, int S, int has_valid, cudaStream_t s
         a.ldrope = e->max_seq;
         a.eps = e->eps;
         if (e2cu_launch(e2c_gemm(&a, st), "encoder qkv")) return -1;
+        }
         if (e2cu_launch(e2c_attention(e->Q, e->K, e->Vt, ldvt, valid, e->ctx, B, S, e->H, e->attn_scale, e->status, st),
                         "encoder attention"))
             return -1;
@@ -368,6 +387,14 @@ static int encode(e2cuda_encoder *e, int B, int S, int has_valid, cudaStream_t s
             a.ldq = I;
             a.q8_scale = e->qs;
             if (e2cu_launch(e2c_gemm(&a, st), "encoder gate|up + h quant")) return -1;
+        } else if (e->ablk != D) {
+            a.epi = E2C_EPI_F32;
+            a.y = e->guf;
+            a.ldy = 2 * I;
+            if (e2cu_launch(e2c_gemm(&a, st), "encoder gate|up") ||
+                e2cu_launch(e2c_gelu_mul_quant(e->guf, 2 * I, I, e->qa, e->qs, M, ab_i, st), "encoder gelu quant"))
+                return -1;
+            n += 1;
         } else {
             a.epi = E2C_EPI_GELU;
             a.y = e->h;

@@ -136,6 +136,16 @@ int e2c_norm_add_norm_quant(const float *t, float *res, const float *g1, const f
 /* quantise(rmsnorm(x) * gamma) per row (config-1 FFN prologue; the residual is x itself) */
 int e2c_norm_quant(const float *x, const float *gamma, float eps, int8_t *q, float *qs, int M, int D,
                    int ablk, void *stream);
+/* Per-128-block activation mode (the reference's default recipe), where the fused epilogues that
+ * need per-token scales cannot run. q|k|v fp32 y [M][ldy] (heads of 256: nq q heads, then k, then v)
+ * -> per-head RMSNorm (q_gamma, k_gamma; v without) -> RoPE on q and k -> bf16 Q [M][256 nq],
+ * K [M][256], V^T [M / seq_len][256][ldvt]; the same arithmetic as the QKV epilogue. */
+int e2c_qkv_post(const float *y, int ldy, int nq, const float *q_gamma, const float *k_gamma, float eps,
+                 const float *rope_cos, const float *rope_sin, int ldrope, int seq_len, void *q_out, void *k_out,
+                 void *vt_out, int ldvt, int M, void *stream);
+/* gate|up fp32 y [M][ldy], columns interleaved per 128 -> h = gelu_tanh(gate) * up -> q [M][I] int8
+ * and scales [M][I / ablk] (ablk 128 or I) */
+int e2c_gelu_mul_quant(const float *y, int ldy, int I, int8_t *q, float *qs, int M, int ablk, void *stream);
 /* pooled[b][d] = mean over valid rows of x[b*S + s][d] (all-invalid -> 0) */
 int e2c_meanpool(const float *x, const uint8_t *valid, float *pooled, int B, int S, int D, void *stream);
 /* rows of y [B][D] L2-normalised in place; rows whose sequence has no valid token become 0 */

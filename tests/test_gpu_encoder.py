@@ -84,6 +84,28 @@ def test_encoder_matches_cpu_reference(e2c, of, syn, torch_cuda):
     assert calls == 1 and kernels == 1 + per_layer * w.cfg.n_layers + 6
 
 
+def test_encoder_per_block_scales_matches_cpu_reference(e2c, of, syn, torch_cuda):
+    """The reference engine's default recipe: activations quantised per 128-element block
+    (E2_I8_BLOCK = 128, src/int8.h:61-70) in every layer. The GEMMs fold block by block, bit-exact;
+    the q|k|v and gate|up GEMMs write fp32 that row kernels finish (norm, RoPE / GELU, quantise)."""
+    cfg = syn.EncoderConfig(n_layers=2, vocab=4096, max_seq=512)
+    w = syn.encoder_weights(cfg, seed=79, ablk=128)
+    rng = np.random.default_rng(5)
+    B, S = 3, 256
+    ids = syn.token_batch(rng, B, S, w.cfg.vocab)
+    valid = np.ones((B, S), np.uint8)
+    valid[1, 200:] = 0
+    valid[2, 17:40] = 0
+    enc = _device_encoder(e2c, syn, w, B * S)
+    got = enc.embed_batch(ids, valid)
+    want = of.encoder_forward(_which(of), w, ids, valid)
+    cos = cosine_rows(got, want)
+    assert cos.min() >= 0.9999, cos
+    calls, kernels, _ = enc.stats()
+    assert kernels == 1 + 10 * w.cfg.n_layers + 6  # q|k|v + finish, attention, ctx quant, o_proj + norms,
+    # gate|up + finish, down + norms (two kernels each), then the head
+
+
 def test_encoder_graph_replay_and_device_api(e2c, syn, torch_cuda):
     """Second call of a shape replays the captured graph: identical bits to the eager first call;
     the device API gives the same bits as the host API; chunking by whole sequences is invisible."""

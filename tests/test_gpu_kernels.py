@@ -732,3 +732,95 @@ def test_gemm_vision_tower_shapes(e2c, of, syn, torch_cuda, N, K):
     eq, es = of.quantize_signed(x, K)
     assert np.array_equal(q.cpu().numpy(), eq)
     assert f32_bits_equal(y, of.gemm_plain(eq, es, wq, ws, K))
+
+
+# ------------------------------------------------------------------------------------------ per-128-block mode
+def test_qkv_post_matches_port(e2c, of, torch_cuda):
+    """Per-block mode's q|k|v finish (e2c_qkv_post): per-head RMSNorm, RoPE and bf16 out from the GEMM's
+    fp32 output, against the port's e2o_rmsnorm + e2o_rope_rows (src/kernels.c:76-87,112-126)."""
+    torch = torch_cuda
+    rng = np.random.default_rng(33)
+    B, S, H, Dh = 3, 200, 3, 256
+    M = B * S
+    y = rng.standard_normal((M, (H + 2) * Dh)).astype(np.float32) * 3
+    qg = (1 + 0.1 * rng.standard_normal(Dh)).astype(np.float32)
+    kg = (1 + 0.1 * rng.standard_normal(Dh)).astype(np.float32)
+    cs = np.empty((S, Dh), np.float32)
+    sn = np.empty((S, Dh), np.float32)
+    of.port().e2o_rope_tables(cs.ctypes.data_as(of.f32p), sn.ctypes.data_as(of.f32p), S, Dh, 10000.0)
+    ldrope, ldvt = S + 3, (S + 7) // 8 * 8
+    cT = np.zeros((128, ldrope), np.float32)
+    sT = np.zeros((128, ldrope), np.float32)
+    cT[:, :S], sT[:, :S] = cs[:, :128].T, sn[:, :128].T
+    Q = torch.zeros((M, H * Dh), dtype=torch.bfloat16, device="cuda")
+    K = torch.zeros((M, Dh), dtype=torch.bfloat16, device="cuda")
+    Vt = torch.zeros((B, Dh, ldvt), dtype=torch.bfloat16, device="cuda")
+    yd, gq, gk, cd, sdn = (dev(torch, t) for t in (y, qg, kg, cT, sT))
+    lib = e2c.lib()
+    lib.e2c_qkv_post.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_float, C.c_void_p, C.c_void_p,
+                                 C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p]
+    assert lib.e2c_qkv_post(yd.data_ptr(), (H + 2) * Dh, H, gq.data_ptr(), gk.data_ptr(), 1e-6, cd.data_ptr(),
+                            sdn.data_ptr(), ldrope, S, Q.data_ptr(), K.data_ptr(), Vt.data_ptr(), ldvt, M,
+                            torch.cuda.current_stream().cuda_stream) == 0, lib.e2c_msg().decode()
+    e2c.check()
+    port = of.port()
+    yy = y.reshape(M, H + 2, Dh)
+    exp = np.empty_like(yy)
+    for hd in range(H + 2):
+        blk = np.ascontiguousarray(yy[:, hd])
+        gamma = qg if hd < H else (kg if hd == H else None)
+        port.e2o_rmsnorm(blk.ctypes.data_as(of.f32p), M, Dh, None if gamma is None else gamma.ctypes.data_as(of.f32p), 1e-6)
+        if hd <= H:
+            port.e2o_rope_rows(blk.ctypes.data_as(of.f32p), 0, M, 1, Dh, Dh,
+                               np.ascontiguousarray(np.tile(cs, (B, 1))).ctypes.data_as(of.f32p),
+                               np.ascontiguousarray(np.tile(sn, (B, 1))).ctypes.data_as(of.f32p))
+        exp[:, hd] = blk
+    to_bf = lambda t: t.float().cpu().numpy()
+    got = np.concatenate([to_bf(Q).reshape(M, H, Dh), to_bf(K).reshape(M, 1, Dh),
+                          to_bf(Vt)[:, :, :S].transpose(0, 2, 1).reshape(M, 1, Dh)], axis=1)
+    want = torch.from_numpy(exp).to(torch.bfloat16).float().numpy()
+    diff = np.abs(got - want)
+    tol = np.abs(want) * 2.0 ** -7 + 4e-6  # one bf16 ulp (the norm's sum order differs from the port's)
+    assert np.all(diff <= tol), f"beyond one bf16 ulp: {int((diff > tol).sum())}, worst {diff.max()}"
+    assert (diff == 0).mean() > 0.99
+
+
+@pytest.mark.parametrize("ablk", [1152, 128])
+def test_gelu_mul_quant(e2c, of, torch_cuda, ablk):
+    """Per-block mode's gate|up finish (e2c_gelu_mul_quant): h = gelu_tanh(g) * u from the GEMM's fp32
+    output (columns interleaved per 128), quantised per token or per 128-block. Per token it must give
+    the bytes and scales of the fused gate|up + GELU + quantise kernel bit for bit; per block, the
+    port's GELU and quantiser within the tie rule."""
+    torch = torch_cuda
+    rng = np.random.default_rng(35)
+    M, D, I = 300, 768, 1152
+    qa, a_s, w, ws = _gemm_inputs(rng, M, 2 * I, D, D)
+    W = e2c.Weight(w=w, scale=ws)
+    qd, sd = dev(torch, qa), dev(torch, a_s)
+    y = torch.empty((M, 2 * I), dtype=torch.float32, device="cuda")
+    a = _args_for(W, qd, sd, M, D)
+    a.epi, a.y, a.ldy = e2c.EPI_F32, y.data_ptr(), 2 * I
+    _launch(e2c, a, torch)
+    q = torch.zeros((M, I), dtype=torch.int8, device="cuda")
+    qs = torch.zeros((M, I // ablk), dtype=torch.float32, device="cuda")
+    lib = e2c.lib()
+    lib.e2c_gelu_mul_quant.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p]
+    assert lib.e2c_gelu_mul_quant(y.data_ptr(), 2 * I, I, q.data_ptr(), qs.data_ptr(), M, ablk,
+                                  torch.cuda.current_stream().cuda_stream) == 0, lib.e2c_msg().decode()
+    e2c.check()
+    if ablk == I and lib.e2c_gemm_gelu_quant_supported(I // 128):
+        qf = torch.zeros((M, I), dtype=torch.int8, device="cuda")
+        qsf = torch.zeros((M,), dtype=torch.float32, device="cuda")
+        a2 = _args_for(W, qd, sd, M, D)
+        a2.epi, a2.q8, a2.ldq, a2.q8_scale = e2c.EPI_GELUQ, qf.data_ptr(), I, qsf.data_ptr()
+        _launch(e2c, a2, torch)
+        assert torch.equal(q, qf), "bytes differ from the fused gate|up + GELU + quantise kernel"
+        assert np.array_equal(qs.cpu().numpy()[:, 0].view(np.int32), qsf.cpu().numpy().view(np.int32))
+    yh = y.cpu().numpy().reshape(M, I // 128, 2, 128)
+    g, u = np.ascontiguousarray(yh[:, :, 0].reshape(M, I)), np.ascontiguousarray(yh[:, :, 1].reshape(M, I))
+    of.port().e2o_gelu_tanh(g.ctypes.data_as(of.f32p), g.size)
+    h = (g * u).astype(np.float32)
+    eq, es = of.quantize_signed(h, ablk)
+    np.testing.assert_allclose(qs.cpu().numpy(), es, rtol=1e-5)
+    pre = h.reshape(M, I // ablk, ablk) * (np.float32(127.0) / np.abs(h.reshape(M, I // ablk, ablk)).max(axis=2, keepdims=True))
+    tie_tolerant_bytes(q.cpu().numpy(), eq, pre.reshape(M, I))
