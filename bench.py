@@ -220,6 +220,8 @@ def main() -> int:
     ap.add_argument("--impl", default="e2cuda", choices=["e2cuda", "reference"])
     ap.add_argument("--layers", type=int, default=24, help=argparse.SUPPRESS)  # debugging only; headline uses 24
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ablk", type=int, default=0, choices=[0, 128],
+                    help="activation block: 0 = per token (the headline), 128 = the reference engine's default recipe")
     ap.add_argument("--kernel", default=None, choices=list(KERNELS),
                     help="run one encoder kernel --steps times at the encoder's shapes (for ncu captures)")
     ap.add_argument("--tokens", type=int, default=BATCH * SEQ, help="tokens for --kernel (a multiple of 512)")
@@ -256,7 +258,8 @@ def main() -> int:
     config = {"workload": f"config 2: synthetic encoder, {cfg.n_layers} layers, hidden {cfg.hidden}, "
                           f"{cfg.n_heads}q/{cfg.n_kv_heads}kv heads x {cfg.head_dim}, ffn {cfg.ffn}, int8 table "
                           f"[{cfg.vocab}][{cfg.hidden}], head {cfg.hidden}->{cfg.dense_hidden}->{cfg.out_dim}",
-              "batch_per_gpu": BATCH, "seq_len": SEQ, "global_batch": BATCH * n, "act_scales": "per-token",
+              "batch_per_gpu": BATCH, "seq_len": SEQ, "global_batch": BATCH * n,
+              "act_scales": "per-token" if not args.ablk else "per-128-block",
               "parallelism": f"dp{n} (batch-sharded, weights replicated, one all-gather)",
               "l2": "inputs larger than L2: each step streams ~0.1 GB of layer weights per pass and ~0.6 GB of ids, "
                     "table rows and activations",
@@ -267,7 +270,7 @@ def main() -> int:
             if dist:
                 dist.destroy_process_group()
             return 0
-        w = syn.encoder_weights(cfg)
+        w = syn.encoder_weights(cfg, ablk=args.ablk or None)
         rng = np.random.default_rng(7)
         seqs = 2
         v, info = cpu_reference(seqs, SEQ, args.steps, args.warmup, w, rng)
@@ -284,7 +287,7 @@ def main() -> int:
     e2c = load_pkg()
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    w = syn.encoder_weights(cfg)
+    w = syn.encoder_weights(cfg, ablk=args.ablk or None)
     desc, keep = syn.fill_desc(w, e2c.Q8W, e2c.EncoderDesc)
     enc = e2c.Encoder(desc, keep, args.chunk)
     rng = np.random.default_rng(1000 + rank)
@@ -342,8 +345,8 @@ def main() -> int:
     # every kernel of a layer in isolation; the roofline object is the dominant one's
     roof, table = None, None
     if rank == 0:
-        table = kernel_table(dev, stream)
-        roof = dominant_roofline(table)
+        table = kernel_table(dev, stream) if not args.ablk else None
+        roof = dominant_roofline(table) if table else None
     cpu = None
     if world > 1:
         # timed on rank 0 at N = 1 only: with N > 1 the other ranks' NCCL progress threads poll on the
