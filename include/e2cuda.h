@@ -131,7 +131,10 @@ typedef struct e2cuda_epilogue {
 /* W8A8 GEMM (A3), e2.c src/kernels_i8_avx512_vnni.c:276-307: for n in [n0, n1),
  *   y[m * ldy + n] = clamp(sum_b fma-fold float(dot_b(qa[m], w[n])) * (a_scales[m][b] * w.scale[n]))
  * bit-identical to the reference kernel. ablk = K (per-token scales, the fast path) or a multiple of
- * 128 dividing K. */
+ * 128 dividing K. For short activation matrices (M <= 256) against long weights the call may use a
+ * weight-streaming kernel that keeps a small zeroed device workspace per (device, stream): it is
+ * allocated by the first such call on a stream that is not being captured (make one before
+ * capturing a graph on that stream) and held until the process exits. */
 int e2cuda_i8_gemm(const e2cuda_w8 *w, const int8_t *qa, const float *a_scales, int M, int ablk,
                    int n0, int n1, const e2cuda_epilogue *ep, float *y, int ldy, void *stream);
 
