@@ -49,46 +49,57 @@
 namespace {
 
 constexpr int BM = 128, BN = 128, BK = 128;
-constexpr int STAGES = 3;
 constexpr int NACC = 4;                    // TMEM accumulators of BN columns
 constexpr int EPI_WARPS = 16;
 constexpr int NTHREADS = 64 + 32 * EPI_WARPS;
 constexpr int QCOLS = BN / 4;              // columns per epilogue warp
 constexpr int NCH = QCOLS / 16;            // 16-column chunks per warp
 constexpr int MAXCL = 8;                   // CTAs per cluster: D <= 1024
+// Column constants per column part (the quadrants' four warps of a part share them): ws, ws g1, g2
+// (or gf); then per warp the activation scales of four row blocks (rows differ by quadrant)
+constexpr int CSTC_FLOATS = 3 * QCOLS;
+constexpr int CSTA_FLOATS = 4 * 32;
 constexpr int RES_TILE = 32 * 16 * 4;      // 32 rows x 16 fp32, 64-byte swizzle
-constexpr int Q8_WARP = 32 * QCOLS;        // 32 rows x 32 int8, 32-byte swizzle
-constexpr int C_WG1 = QCOLS, C_G2 = 2 * QCOLS, C_AS = 3 * QCOLS;
-constexpr int CST_FLOATS = C_AS + 4 * 32;  // ws, ws g1, g2 (or gf); four blocks' activation scales
+constexpr int C_WG1 = QCOLS, C_G2 = 2 * QCOLS;
 
+// STG mainloop stages; exchange slots for clusters of up to XMAX CTAs. Four stages fit beside the
+// epilogue's buffers for clusters of up to 6 (D <= 768); wider clusters keep three.
+template <int STG, int XMAX>
 struct Smem {
     static constexpr int A_BYTES = BM * BK, B_BYTES = BN * BK, STAGE = A_BYTES + B_BYTES;
-    static constexpr int RES_OFF = STAGES * STAGE;
-    static constexpr int Q8_OFF = RES_OFF + EPI_WARPS * NCH * RES_TILE;
-    static constexpr int CST_OFF = Q8_OFF + EPI_WARPS * Q8_WARP;
-    static constexpr int XL0_OFF = CST_OFF + EPI_WARPS * CST_FLOATS * 4;  // [4 parts][BM] float
-    static constexpr int XL1_OFF = XL0_OFF + 4 * BM * 4;                 // [4 parts][BM] float2
-    static constexpr int XR0_OFF = XL1_OFF + 4 * BM * 8;                 // [2][MAXCL][BM] float
-    static constexpr int XR1_OFF = XR0_OFF + 2 * MAXCL * BM * 4;         // [2][MAXCL][BM] float2
-    static constexpr int BAR_OFF = XR1_OFF + 2 * MAXCL * BM * 8;
+    static constexpr int RES_OFF = STG * STAGE;
+    static constexpr int CSTC_OFF = RES_OFF + EPI_WARPS * NCH * RES_TILE;  // [4 parts][3 x 32] float
+    static constexpr int CSTA_OFF = CSTC_OFF + 4 * CSTC_FLOATS * 4;        // [16 warps][4 x 32] float
+    static constexpr int XL0_OFF = CSTA_OFF + EPI_WARPS * CSTA_FLOATS * 4;  // [4 parts][BM] float
+    static constexpr int XL1_OFF = XL0_OFF + 4 * BM * 4;                   // [4 parts][BM] float2
+    static constexpr int XR0_OFF = XL1_OFF + 4 * BM * 8;                   // [2][XMAX][BM] float
+    static constexpr int XR1_OFF = XR0_OFF + 2 * XMAX * BM * 4;            // [2][XMAX][BM] float2
+    static constexpr int BAR_OFF = XR1_OFF + 2 * XMAX * BM * 8;
     // full[S], empty[S], tfull[NACC], tempty[NACC], lbar[2 rounds][4], xbar[2 rounds][2][4], rbar[16]
-    static constexpr int NBAR = 2 * STAGES + 2 * NACC + 8 + 16 + EPI_WARPS;
+    static constexpr int NBAR = 2 * STG + 2 * NACC + 8 + 16 + EPI_WARPS;
     static constexpr int BYTES = BAR_OFF + NBAR * 8 + 16;
-    static constexpr int ALLOC = BYTES + 1024;  // slack for 1024-byte alignment
-    static_assert(RES_OFF % 1024 == 0 && Q8_OFF % 1024 == 0, "swizzled TMA tiles");
+    // No alignment slack: the dynamic shared memory of a kernel without static shared variables
+    // starts 1024-byte aligned, which the kernel checks before using it (the swizzled tiles need it).
+    static constexpr int ALLOC = BYTES;
+    static_assert(RES_OFF % 1024 == 0, "swizzled TMA tiles");
     static_assert(ALLOC <= 232448, "shared memory");
 };
 
 // QUANT: the next layer's int8 input is produced (g2 given); otherwise the final norm (gf)
-template <bool QUANT>
+template <bool QUANT, int STAGES, int XMAX>
 __global__ void __launch_bounds__(NTHREADS, 1)
     k_gemm_norm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                const __grid_constant__ CUtensorMap tmR, const __grid_constant__ CUtensorMap tmQ,
+                const __grid_constant__ CUtensorMap tmR,
                 const e2c_gemm_args p) {
-    using L = Smem;
-    extern __shared__ uint8_t smem_raw[];
+    using L = Smem<STAGES, XMAX>;
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
     griddep_launch_dependents();
-    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    if (smem_u32(smem_raw) & 1023) {  // never expected; every CTA of the launch sees the same base
+        griddep_wait();
+        if (threadIdx.x == 0) record_status(p.status, E2C_ERR_SMEM_ALIGN);
+        return;
+    }
+    uint8_t *smem = smem_raw;
     const uint32_t sbase = smem_u32(smem);
     const uint32_t bar0 = sbase + L::BAR_OFF;
     auto full_bar = [&](int s) { return bar0 + 8u * s; };
@@ -225,10 +236,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
         const int cl0 = rank * BN + part * QCOLS;  // first column of this warp within the row
         constexpr bool quant = QUANT;
-        float *cst = reinterpret_cast<float *>(smem + L::CST_OFF) + (warp - 2) * CST_FLOATS;
+        float *cst = reinterpret_cast<float *>(smem + L::CSTC_OFF) + part * CSTC_FLOATS;   // shared by the part's warps
+        float *csta = reinterpret_cast<float *>(smem + L::CSTA_OFF) + (warp - 2) * CSTA_FLOATS;
         uint8_t *resb = smem + L::RES_OFF + (warp - 2) * NCH * RES_TILE;
         const uint32_t resb_s = smem_u32(resb);
-        uint8_t *q8s = smem + L::Q8_OFF + (warp - 2) * Q8_WARP;
         const uint32_t rb = rbar(warp - 2);
         {
             const float *gb = quant ? p.norm_g2 : p.norm_gf;
@@ -242,7 +253,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         }
         bool ok = true, xok = true;
         // the rows' activation scales of block n land in slot n & 3 by cp.async (one group per call)
-        const uint32_t as_slot = smem_u32(cst + C_AS + lane);
+        const uint32_t as_slot = smem_u32(csta + lane);
         auto load_as = [&](int n) {
             if (n < ntl) {
                 const int mr = row0(n) + row;
@@ -299,8 +310,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             const int b = n & 1;
             const uint32_t xb = xbar(r, b, q);
             if (lane == 0) mbar_arrive_expect_tx(xb, (uint32_t)(ncl * 32 * (r == 0 ? 4 : 8)));
-            const uint32_t slot = r == 0 ? sbase + L::XR0_OFF + (uint32_t)(((b * MAXCL + rank) * BM + row) * 4)
-                                         : sbase + L::XR1_OFF + (uint32_t)(((b * MAXCL + rank) * BM + row) * 8);
+            const uint32_t slot = r == 0 ? sbase + L::XR0_OFF + (uint32_t)(((b * XMAX + rank) * BM + row) * 4)
+                                         : sbase + L::XR1_OFF + (uint32_t)(((b * XMAX + rank) * BM + row) * 8);
             for (int d = 0; d < ncl; d++) {
                 if (r == 0) st_async_f32(mapa_shared(slot, (uint32_t)d), c.x, mapa_shared(xb, (uint32_t)d));
                 else st_async_f32x2(mapa_shared(slot, (uint32_t)d), c.x, c.y, mapa_shared(xb, (uint32_t)d));
@@ -312,9 +323,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             float2 tot = make_float2(0.f, 0.f);
             for (int d = 0; d < ncl; d++) {
                 if (r == 0) {
-                    tot.x = __fadd_rn(tot.x, reinterpret_cast<const float *>(smem + L::XR0_OFF)[(b * MAXCL + d) * BM + row]);
+                    tot.x = __fadd_rn(tot.x, reinterpret_cast<const float *>(smem + L::XR0_OFF)[(b * XMAX + d) * BM + row]);
                 } else {
-                    const float2 o = reinterpret_cast<const float2 *>(smem + L::XR1_OFF)[(b * MAXCL + d) * BM + row];
+                    const float2 o = reinterpret_cast<const float2 *>(smem + L::XR1_OFF)[(b * XMAX + d) * BM + row];
                     tot.x = __fadd_rn(tot.x, o.x);
                     tot.y = fmaxf(tot.y, o.y);
                 }
@@ -359,7 +370,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             }
             tmem_wait_st();
             const float ss = __fadd_rn(__fadd_rn(ssp[0].x, ssp[0].y), __fadd_rn(ssp[1].x, ssp[1].y));
-            const float as = cst[C_AS + (n & 3) * 32 + lane];
+            const float as = csta[(n & 3) * 32 + lane];
             return __fmul_rn(__fmul_rn(as, as), ss);
         };
         auto release = [&](int n) {
@@ -377,12 +388,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             if (ok) send(0, 0, make_float2(s0, 0.f));
         }
         for (int n = 0; n < ntl && ok && xok; n++) {
-            const int y0 = row0(n) + q * 32;
             load_as(n + 2);
             const float s1 = recv(0, n).x;
             if (!xok) break;
             const float inv1 = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(s1, (float)D), p.eps)));
-            const float sr = __fmul_rn(cst[C_AS + (n & 3) * 32 + lane], inv1);
+            const float sr = __fmul_rn(csta[(n & 3) * 32 + lane], inv1);
             // pass 2: x = fma(v, as inv1, res) into the residual tiles; y = x g2 into the accumulator
             if (!__all_sync(0xffffffffu, mbar_wait(rb, rpar, p.status, E2C_ERR_WAIT_EPI))) {
                 ok = false;
@@ -450,8 +460,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 const float s = t2.y > 0.f ? __fdiv_rn(127.0f, t2.y) : 0.f;
                 const int m = row0(n) + row;
                 if (rank == 0 && part == 0 && m < M) p.q8_scale[m] = amax > 0.f ? __fmul_rn(amax, 0x1.020408p-7f) : 1.0f;
-                if (lane == 0) bulk_wait_read1();  // block n-1's int8 store has read the staging rows
-                __syncwarp();
+                uint4 *qrow = reinterpret_cast<uint4 *>(p.q8 + (size_t)(m < M ? m : 0) * p.ldq + cl0);
 #pragma unroll
                 for (int c = 0; c < NCH; c++) {
                     uint32_t r[16];
@@ -466,16 +475,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                         pk[k] = __byte_perm(__byte_perm(__float_as_uint(ba.x), __float_as_uint(ba.y), 0x0040),
                                             __byte_perm(__float_as_uint(bb.x), __float_as_uint(bb.y), 0x0040), 0x5410);
                     }
-                    // 16-byte chunk c of row `lane` in the 32-byte swizzle of the int8 map
-                    *reinterpret_cast<uint4 *>(q8s + lane * 32 + ((c ^ ((lane >> 2) & 1)) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                    // 16 bytes of row m straight from registers (chunks 0 and 1 fill the row's 32-byte sector)
+                    if (m < M) qrow[c] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
                 }
                 release(n);
-                fence_proxy_async_smem();
-                __syncwarp();
-                if (lane == 0) {
-                    tma_store_2d(&tmQ, smem_u32(q8s), cl0, y0);
-                    bulk_commit();
-                }
             } else {
                 // the final norm: res = x inv2 gf, written over x in the tiles; then block n+1
                 const float2 t2 = recv(1, n);
@@ -524,41 +527,28 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
 }
 
-}  // namespace
-
-// The GEMM + norms launch: geometry checked by e2c_gemm (per-row scales, n0 = 0, D = 128 x (1..8)).
-extern "C" int e2c_gemm_norm(const e2c_gemm_args *a, void *stream) {
-    using L = Smem;
-    static E2cPerDev attr_set;                  // the shared-memory opt-in, per device
+template <int STG, int XMAX>
+int launch_norm(const e2c_gemm_args *a, int ncl, bool quant, cudaStream_t st, int dev, int num_sms) {
+    using L = Smem<STG, XMAX>;
+    static E2cPerDev attr_set;                    // the shared-memory opt-in, per device
     static E2cPerDev max_clusters[2][MAXCL + 1];  // resident clusters per (quantise, width), per device
-    const int dev = e2c_device();
-    const int num_sms = e2c_sm_count(dev);
-    if (!num_sms) {
-        e2c_set_msg("gemm_norm: no CUDA device");
-        return -2;
-    }
     if (!attr_set.get(dev)) {
-        if (cudaFuncSetAttribute(k_gemm_norm<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC) != cudaSuccess ||
-            cudaFuncSetAttribute(k_gemm_norm<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC) != cudaSuccess) {
+        if (cudaFuncSetAttribute(k_gemm_norm<true, STG, XMAX>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC) !=
+                cudaSuccess ||
+            cudaFuncSetAttribute(k_gemm_norm<false, STG, XMAX>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC) !=
+                cudaSuccess) {
+            cudaGetLastError();
             e2c_set_msg("gemm_norm: cannot reserve %d bytes of shared memory", L::ALLOC);
             return -2;
         }
         attr_set.set(dev, 1);
     }
     const int D = a->n1 - a->n0;
-    const int ncl = D / BN;
-    if (a->n0 != 0 || D % BN || ncl < 1 || ncl > MAXCL) {
-        e2c_set_msg("gemm_norm: rows of 128 x (1..8) columns starting at column 0");
-        return -1;
-    }
-    CUtensorMap ta, tb, tr, tq;
-    memset(&tq, 0, sizeof tq);
+    CUtensorMap ta, tb, tr;
     if (e2c_tmap_2d(&ta, a->a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)a->K, (uint64_t)a->M, (uint64_t)a->lda, BK, BM) ||
         e2c_tmap_2d(&tb, a->w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)a->K, (uint64_t)a->wrows, (uint64_t)a->ldw, BK, BN) ||
         e2c_tmap_2d_sw64(&tr, a->res, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)D, (uint64_t)a->M,
-                         (uint64_t)a->ldres * 4, 16, 32) ||
-        (a->norm_g2 && e2c_tmap_2d_sw32(&tq, a->q8, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)D, (uint64_t)a->M,
-                                        (uint64_t)a->ldq, QCOLS, 32)))
+                         (uint64_t)a->ldres * 4, 16, 32))
         return -3;
     const int tiles_m = (a->M + BM - 1) / BM;
     cudaLaunchConfig_t cfg;
@@ -570,11 +560,10 @@ extern "C" int e2c_gemm_norm(const e2c_gemm_args *a, void *stream) {
     attr[0].val.clusterDim.z = 1;
     cfg.blockDim = dim3(NTHREADS);
     cfg.dynamicSmemBytes = L::ALLOC;
-    cfg.stream = (cudaStream_t)stream;
+    cfg.stream = st;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    const bool quant = a->norm_g2 != nullptr;
-    auto kern = quant ? k_gemm_norm<true> : k_gemm_norm<false>;
+    auto kern = quant ? k_gemm_norm<true, STG, XMAX> : k_gemm_norm<false, STG, XMAX>;
     int maxc = max_clusters[quant][ncl].get(dev);
     if (!maxc) {
         cfg.gridDim = dim3((unsigned)(ncl * (num_sms / ncl)));
@@ -587,10 +576,31 @@ extern "C" int e2c_gemm_norm(const e2c_gemm_args *a, void *stream) {
     }
     cfg.gridDim = dim3((unsigned)(ncl * (tiles_m < maxc ? tiles_m : maxc)));
     cfg.numAttrs = e2c_pdl_attr(attr, 1);
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, tb, tr, tq, *a);
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, tb, tr, *a);
     if (e != cudaSuccess) {
         e2c_set_msg("gemm_norm launch: %s", cudaGetErrorString(e));
         return -2;
     }
     return 0;
+}
+
+}  // namespace
+
+// The GEMM + norms launch: geometry checked by e2c_gemm (per-row scales, n0 = 0, D = 128 x (1..8)).
+extern "C" int e2c_gemm_norm(const e2c_gemm_args *a, void *stream) {
+    const int dev = e2c_device();
+    const int num_sms = e2c_sm_count(dev);
+    if (!num_sms) {
+        e2c_set_msg("gemm_norm: no CUDA device");
+        return -2;
+    }
+    const int D = a->n1 - a->n0;
+    const int ncl = D / BN;
+    if (a->n0 != 0 || D % BN || ncl < 1 || ncl > MAXCL) {
+        e2c_set_msg("gemm_norm: rows of 128 x (1..8) columns starting at column 0");
+        return -1;
+    }
+    const bool quant = a->norm_g2 != nullptr;
+    cudaStream_t st = (cudaStream_t)stream;
+    return ncl <= 6 ? launch_norm<4, 6>(a, ncl, quant, st, dev, num_sms) : launch_norm<3, MAXCL>(a, ncl, quant, st, dev, num_sms);
 }
