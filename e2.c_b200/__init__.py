@@ -116,6 +116,8 @@ API = [
     ("e2cuda_attention", C.c_int, [vp, vp, vp, C.c_int, vp, vp, C.c_int, C.c_int, C.c_int, C.c_float, vp]),
     ("e2cuda_attention_gqa", C.c_int, [vp, vp, vp, C.c_int, vp, vp, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
                                        C.c_float, vp]),
+    ("e2cuda_attention_window", C.c_int, [vp, vp, vp, C.c_int, vp, vp, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
+                                          C.c_float, C.c_int, vp]),
     ("e2cuda_ffn_create", vp, [C.POINTER(Q8W), C.POINTER(Q8W), C.POINTER(Q8W), f32p, C.c_float, C.c_int]),
     ("e2cuda_ffn_destroy", None, [vp]),
     ("e2cuda_ffn_forward", C.c_int, [vp, vp, C.c_int, vp, vp]),
@@ -144,6 +146,12 @@ API = [
     ("e2cuda_q8c_commit", C.c_int, [vp]),
     ("e2cuda_q8c_abort", None, [vp]),
     ("e2cuda_q8c_convert", C.c_int, [C.c_char_p, C.c_char_p]),
+    ("e2cuda_text_create", vp, [vp, C.c_int]),
+    ("e2cuda_text_destroy", None, [vp]),
+    ("e2cuda_text_embed", C.c_int, [vp, i32p, C.c_int, f32p]),
+    ("e2cuda_text_embed_batch", C.c_int, [vp, i32p, u8p, C.c_int, C.c_int, f32p]),
+    ("e2cuda_text_embed_batch_device", C.c_int, [vp, vp, vp, C.c_int, C.c_int, vp, vp]),
+    ("e2cuda_text_stats", C.c_int, [vp, C.POINTER(C.c_long), C.POINTER(C.c_long), C.POINTER(C.c_double)]),
 ]
 
 Q8C_BF16, Q8C_F32, Q8C_Q8W, Q8C_W8 = 1, 2, 3, 4
@@ -296,6 +304,16 @@ def attention_gqa(q, k, vt, valid, B: int, S: int, H: int, KV: int, D: int, scal
     ctx = torch.empty((B * S, H * D), dtype=torch.float32, device=q.device)
     _ok(lib().e2cuda_attention_gqa(_ptr(q), _ptr(k), _ptr(vt), vt.shape[-1], _ptr(valid), _ptr(ctx), B, S, H, KV, D,
                                    scale, _stream(stream)), "attention_gqa")
+    return ctx
+
+
+def attention_window(q, k, vt, valid, B: int, S: int, H: int, KV: int, D: int, scale: float, window: int = -1,
+                     stream=None):
+    """attention_gqa with a sliding window (|i - j| <= window; -1: none) and head dims 64, 256 or 512."""
+    torch = _torch()
+    ctx = torch.empty((B * S, H * D), dtype=torch.float32, device=q.device)
+    _ok(lib().e2cuda_attention_window(_ptr(q), _ptr(k), _ptr(vt), vt.shape[-1], _ptr(valid), _ptr(ctx), B, S, H, KV, D,
+                                      scale, window, _stream(stream)), "attention_window")
     return ctx
 
 
@@ -458,6 +476,64 @@ class Encoder:
     def close(self) -> None:
         if getattr(self, "h", None):
             lib().e2cuda_encoder_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class TextTower:
+    """e2.c's own EmbeddingGemma-2 text tower on the device (e2cuda_text_*). `desc` is an
+    e2cuda_text_desc (text_model.TextDesc, from text_model.TextWeights or filled by e2.c's loader);
+    the library copies everything at create time."""
+
+    def __init__(self, desc, max_tokens: int, keepalive=None):
+        self._keep = keepalive
+        h = lib().e2cuda_text_create(C.addressof(desc), max_tokens)
+        if not h:
+            raise E2CudaError(f"text_create: {last_error()}")
+        self.h = h
+        self.out_dim = desc.out_dim
+
+    def embed_batch(self, ids: np.ndarray, valid: np.ndarray | None = None) -> np.ndarray:
+        """Host buffers in and out (e2_hip_text_embed_batch's contract)."""
+        ids = np.ascontiguousarray(ids, np.int32)
+        B, S = ids.shape
+        out = np.empty((B, self.out_dim), np.float32)
+        v = None if valid is None else np.ascontiguousarray(valid, np.uint8)
+        _ok(lib().e2cuda_text_embed_batch(self.h, ids.ctypes.data_as(i32p), None if v is None else v.ctypes.data_as(u8p),
+                                          B, S, out.ctypes.data_as(f32p)), "text_embed_batch")
+        return out
+
+    def embed(self, ids: np.ndarray) -> np.ndarray:
+        ids = np.ascontiguousarray(ids, np.int32).reshape(-1)
+        out = np.empty(self.out_dim, np.float32)
+        _ok(lib().e2cuda_text_embed(self.h, ids.ctypes.data_as(i32p), ids.size, out.ctypes.data_as(f32p)), "text_embed")
+        return out
+
+    def embed_batch_into(self, ids, valid, out) -> None:
+        """Host (pinned) torch tensors in and out, without extra copies."""
+        B, S = ids.shape
+        _ok(lib().e2cuda_text_embed_batch(self.h, C.cast(ids.data_ptr(), i32p),
+                                          None if valid is None else C.cast(valid.data_ptr(), u8p), B, S,
+                                          C.cast(out.data_ptr(), f32p)), "text_embed_batch")
+
+    def embed_batch_device(self, ids, valid, out, stream=None) -> None:
+        B, S = ids.shape
+        _ok(lib().e2cuda_text_embed_batch_device(self.h, _ptr(ids), _ptr(valid), B, S, _ptr(out), _stream(stream)),
+            "text_embed_batch_device")
+
+    def stats(self):
+        calls, kern, ms = C.c_long(), C.c_long(), C.c_double()
+        _ok(lib().e2cuda_text_stats(self.h, C.byref(calls), C.byref(kern), C.byref(ms)), "text_stats")
+        return calls.value, kern.value, ms.value
+
+    def close(self) -> None:
+        if getattr(self, "h", None):
+            lib().e2cuda_text_destroy(self.h)
             self.h = None
 
     def __del__(self):

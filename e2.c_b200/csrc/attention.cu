@@ -97,6 +97,7 @@ struct AttnArgs {
     const uint8_t *valid;
     float *ctx;
     int S, H, KV, nkt, nqt, units;
+    int window;  // keys j with |i - j| <= window attend to query i; < 0: every key
     float scale_log2;
     int *status;
 };
@@ -116,6 +117,19 @@ E2C_DEV Unit unit_of(int u, const AttnArgs &p) {
     const int per_seq = p.H * p.nqt;
     const int b = u / per_seq, rem = u - b * per_seq;
     return {b, rem / p.nqt, rem % p.nqt};
+}
+
+// the key tiles a unit visits: all of them, or those a sliding window reaches from its queries
+E2C_DEV void tile_range(const Unit &w, const AttnArgs &p, int &j0, int &nt) {
+    if (p.window < 0) {
+        j0 = 0;
+        nt = p.nkt;
+        return;
+    }
+    const int q0 = w.qt * TQ, q1 = min(q0 + TQ, p.S) - 1;
+    const int lo = max(0, q0 - p.window), hi = min(p.S - 1, q1 + p.window);
+    j0 = lo / TKV;
+    nt = hi / TKV + 1 - j0;
 }
 
 template <int HD>
@@ -138,7 +152,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     volatile uint32_t *tmem_slot = reinterpret_cast<volatile uint32_t *>(smem + BAR_OFF + B_NUM * 8);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int S = p.S, nkt = p.nkt;
+    const int S = p.S;
 
     if (warp == 0 && lane == 0) {
         mbar_init(bar(B_Q), 1);
@@ -183,12 +197,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 const Unit w = unit_of(u, p);
                 const int row0 = w.b * S;
                 const int kvh = w.h / (p.H / p.KV);
+                int j0, nt;
+                tile_range(w, p, j0, nt);
                 // Q may be replaced once every QK product of the previous unit completed
                 if (!mbar_wait(bar(B_QE), (uint32_t)((nu & 1) ^ 1), p.status, E2C_ERR_WAIT_PRODUCER)) break;
                 mbar_arrive_expect_tx(bar(B_Q), TQ * HD * 2);
                 for (int i = 0; i < HD / 64; i++)
                     tma_load_2d(sbase + Q_OFF + i * (TQ * 128), &tmQ, w.h * HD + 64 * i, row0 + w.qt * TQ, bar(B_Q));
-                for (int j = 0; j < nkt; j++, g++) {
+                for (int j = j0; j < j0 + nt; j++, g++) {
                     const int kb = g & 1;
                     // buffer kb is free once QK of tile g-2 completed
                     if (!mbar_wait(bar(B_KE + kb), (uint32_t)(((g >> 1) & 1) ^ 1), p.status, E2C_ERR_WAIT_PRODUCER)) {
@@ -213,7 +229,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             bool ok = true;
             for (int u = blockIdx.x; u < p.units && ok; u += gridDim.x) {
                 const Unit w = unit_of(u, p);
-                for (int j = 0; j < nkt; j++, g++) {
+                int j0, nt;
+                tile_range(w, p, j0, nt);
+                for (int j = j0; j < j0 + nt; j++, g++) {
                     const int vb = g & 1;
                     // buffer vb is free once PV of tile g-2 completed
                     if (!mbar_wait(bar(B_VE + vb), (uint32_t)(((g >> 1) & 1) ^ 1), p.status, E2C_ERR_WAIT_PRODUCER)) {
@@ -252,18 +270,21 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 if (last) mma_commit(bar(B_QE));  // the unit's last read of Q
                 return true;
             };
-            for (int u = blockIdx.x; u < p.units && ok; u += gridDim.x, nu++, g0 += nkt) {
+            int nt = 0;
+            for (int u = blockIdx.x; u < p.units && ok; u += gridDim.x, nu++, g0 += nt) {
+                int j0;
+                tile_range(unit_of(u, p), p, j0, nt);
                 if (!mbar_wait(bar(B_Q), (uint32_t)(nu & 1), p.status, E2C_ERR_WAIT_MMA)) {
                     ok = false;
                     break;
                 }
-                if (!issue_qk(g0, nkt == 1) || (nkt > 1 && !issue_qk(g0 + 1, nkt == 2))) {
+                if (!issue_qk(g0, nt == 1) || (nt > 1 && !issue_qk(g0 + 1, nt == 2))) {
                     ok = false;
                     break;
                 }
-                for (int j = 0; j < nkt; j++) {
+                for (int j = 0; j < nt; j++) {
                     const int g = g0 + j, vb = g & 1, s4 = g & 3;
-                    if (j + 2 < nkt && !(ok = issue_qk(g + 2, j + 2 == nkt - 1))) break;
+                    if (j + 2 < nt && !(ok = issue_qk(g + 2, j + 2 == nt - 1))) break;
                     if (!mbar_wait(bar(B_PF + s4), (uint32_t)((g >> 2) & 1), p.status, E2C_ERR_WAIT_MMA) ||
                         !mbar_wait(bar(B_VF + vb), (uint32_t)((g >> 1) & 1), p.status, E2C_ERR_WAIT_MMA) ||
                         // the first PV of a unit overwrites O: the previous unit's epilogue has read it
@@ -296,15 +317,20 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         float *xch = reinterpret_cast<float *>(smem + X_OFF);  // [2][2][TQ] row maxima
         float *invs = reinterpret_cast<float *>(smem + INV_OFF);  // [2][TQ]
         bool ok = true;
-        int g0 = 0, nu = 0;
-        for (int u = blockIdx.x; u < p.units && ok; u += gridDim.x, nu++, g0 += nkt) {
+        int g0 = 0, nu = 0, nt = 0;
+        for (int u = blockIdx.x; u < p.units && ok; u += gridDim.x, nu++, g0 += nt) {
             const Unit w = unit_of(u, p);
             const int row0 = w.b * S, q0 = w.qt * TQ;
             const int qrow = q0 + r;
             const bool row_in = qrow < S;
+            int j0;
+            tile_range(w, p, j0, nt);
+            // the warp's 32 query rows start at wq0
+            const int wq0 = q0 + quad * 32;
             float m_used = -INFINITY, l = 0.f;
-            for (int j = 0; j < nkt; j++) {
-                const int g = g0 + j, sb = g & 1, s4 = g & 3;
+            for (int jj = 0; jj < nt; jj++) {
+                const int j = j0 + jj;
+                const int g = g0 + jj, sb = g & 1, s4 = g & 3;
                 if (!__all_sync(0xffffffffu, mbar_wait(bar(B_SF + s4), (uint32_t)((g >> 2) & 1), p.status, E2C_ERR_WAIT_ATTN))) {
                     ok = false;
                     break;
@@ -328,6 +354,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     for (int i = 0; i < 32; i++)
                         if (!((keep >> i) & 1u)) s[i] = -INFINITY;
                 }
+                // the window's edge runs through this warp's 32 x 32 block: per element
+                if (p.window >= 0 && (k0 < wq0 + 31 - p.window || k0 + 31 > wq0 + p.window)) {
+#pragma unroll
+                    for (int i = 0; i < 32; i++)
+                        if (k0 + i < qrow - p.window || k0 + i > qrow + p.window) s[i] = -INFINITY;
+                }
                 float mx = -INFINITY;
 #pragma unroll
                 for (int i = 0; i < 32; i++) mx = fmaxf(mx, s[i]);
@@ -348,7 +380,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     l *= alpha;
                     m_used = mx;
                 }
-                if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+                if (jj > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
                     // O may be touched only once PV of tile g-1 completed
                     if (!__all_sync(0xffffffffu, mbar_wait(bar(B_PV + ((g - 1) & 3)), (uint32_t)(((g - 1) >> 2) & 1),
                                                            p.status, E2C_ERR_WAIT_ATTN))) {
@@ -402,7 +434,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             // parity: both warps of the pair have published P of that tile (so read its maxima) once
             // that tile's P-full barrier completed, and neither writes those slots again before both
             // have passed the next unit's first exchange, which follows the reads below.
-            const int gl = g0 + nkt - 1;
+            const int gl = g0 + nt - 1;
             if (!__all_sync(0xffffffffu, mbar_wait(bar(B_PF + (gl & 3)), (uint32_t)((gl >> 2) & 1), p.status, E2C_ERR_WAIT_ATTN))) {
                 ok = false;
                 break;
@@ -437,12 +469,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         uint8_t *stg = smem + STG_OFF + (warp - 3 - SM_WARPS) * NSTG * STG;
         int nst = 0;  // ctx stores this warp committed
         bool ok = true;
-        int g0 = 0, nu = 0;
-        for (int u = blockIdx.x; u < p.units && ok; u += gridDim.x, nu++, g0 += nkt) {
+        int g0 = 0, nu = 0, nt = 0;
+        for (int u = blockIdx.x; u < p.units && ok; u += gridDim.x, nu++, g0 += nt) {
             const Unit w = unit_of(u, p);
             const int row0 = w.b * S, q0 = w.qt * TQ;
             const int qrow = q0 + r;
             const bool row_in = qrow < S;
+            int j0;
+            tile_range(w, p, j0, nt);
             if (!__all_sync(0xffffffffu, mbar_wait(bar(B_UD + (nu & 1) * 4 + quad), (uint32_t)((nu >> 1) & 1), p.status,
                                                    E2C_ERR_WAIT_ATTN))) {
                 ok = false;
@@ -451,7 +485,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             const float inv = invs[(nu & 1) * TQ + r];
             // PV of the last tile completes after every earlier product (tcgen05.commit tracks all
             // prior MMAs): O is final
-            const int gl = g0 + nkt - 1;
+            const int gl = g0 + nt - 1;
             if (!__all_sync(0xffffffffu, mbar_wait(bar(B_PV + (gl & 3)), (uint32_t)((gl >> 2) & 1), p.status, E2C_ERR_WAIT_ATTN))) {
                 ok = false;
                 break;
@@ -517,7 +551,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 
 template <int HD>
 int launch_hd(const void *q, const void *k, const void *vt, int ldvt, const uint8_t *valid, float *ctx, int B, int S,
-              int H, int KV, float scale, int *status, cudaStream_t st, int dev, int num_sms) {
+              int H, int KV, float scale, int window, int *status, cudaStream_t st, int dev, int num_sms) {
     using L = AttnSmem<HD>;
     static E2cPerDev attr;  // the shared-memory opt-in, per device
     if (!attr.get(dev)) {
@@ -545,6 +579,7 @@ int launch_hd(const void *q, const void *k, const void *vt, int ldvt, const uint
     a.nkt = (S + TKV - 1) / TKV;
     a.nqt = (S + TQ - 1) / TQ;
     a.units = B * H * a.nqt;
+    a.window = window;
     a.scale_log2 = scale * 1.4426950408889634f;
     a.status = status;
     const int grid = a.units < num_sms ? a.units : num_sms;
@@ -559,19 +594,20 @@ int launch_hd(const void *q, const void *k, const void *vt, int ldvt, const uint
 
 }  // namespace
 
-extern "C" int e2c_attention_gqa(const void *q, const void *k, const void *vt, int ldvt, const uint8_t *valid, float *ctx,
-                                 int B, int S, int H, int KV, int D, float scale, int *status, void *stream) {
+extern "C" int e2c_attention_win(const void *q, const void *k, const void *vt, int ldvt, const uint8_t *valid, float *ctx,
+                                 int B, int S, int H, int KV, int D, float scale, int window, int *status, void *stream) {
     if (B <= 0 || S <= 0) return 0;
-    if (H <= 0 || KV <= 0 || H % KV || (D != 64 && D != 256) || ldvt < S || ldvt % 8 ||
+    if (H <= 0 || KV <= 0 || H % KV || (D != 64 && D != 256 && D != 512) || ldvt < S || ldvt % 8 ||
         (((uintptr_t)q | (uintptr_t)k | (uintptr_t)vt) & 15)) {
-        e2c_set_msg("attention: bad arguments (H=%d KV=%d D=%d S=%d ldvt=%d; KV divides H, D 64 or 256, ldvt >= S and "
-                    "a multiple of 8, 16-byte aligned operands)", H, KV, D, S, ldvt);
+        e2c_set_msg("attention: bad arguments (H=%d KV=%d D=%d S=%d ldvt=%d; KV divides H, D 64, 256 or 512, ldvt >= S "
+                    "and a multiple of 8, 16-byte aligned operands)", H, KV, D, S, ldvt);
         return -1;
     }
     if ((uintptr_t)ctx & 15) {
         e2c_set_msg("attention: ctx must be 16-byte aligned");
         return -1;
     }
+    if (D == 512) return e2c_attention_wide(q, k, vt, ldvt, valid, ctx, B, S, H, KV, scale, window, status, stream);
     const int dev = e2c_device();
     const int num_sms = e2c_sm_count(dev);
     if (!num_sms) {
@@ -579,8 +615,17 @@ extern "C" int e2c_attention_gqa(const void *q, const void *k, const void *vt, i
         return -2;
     }
     cudaStream_t st = (cudaStream_t)stream;
-    return D == 256 ? launch_hd<256>(q, k, vt, ldvt, valid, ctx, B, S, H, KV, scale, status, st, dev, num_sms)
-                    : launch_hd<64>(q, k, vt, ldvt, valid, ctx, B, S, H, KV, scale, status, st, dev, num_sms);
+    return D == 256 ? launch_hd<256>(q, k, vt, ldvt, valid, ctx, B, S, H, KV, scale, window, status, st, dev, num_sms)
+                    : launch_hd<64>(q, k, vt, ldvt, valid, ctx, B, S, H, KV, scale, window, status, st, dev, num_sms);
+}
+
+extern "C" int e2c_attention_gqa(const void *q, const void *k, const void *vt, int ldvt, const uint8_t *valid, float *ctx,
+                                 int B, int S, int H, int KV, int D, float scale, int *status, void *stream) {
+    if (D == 512) {
+        e2c_set_msg("attention: D=%d; head dim 512 runs through e2c_attention_win", D);
+        return -1;
+    }
+    return e2c_attention_win(q, k, vt, ldvt, valid, ctx, B, S, H, KV, D, scale, -1, status, stream);
 }
 
 extern "C" int e2c_attention(const void *q, const void *k, const void *vt, int ldvt, const uint8_t *valid, float *ctx,

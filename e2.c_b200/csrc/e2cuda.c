@@ -348,6 +348,16 @@ int e2cuda_attention_gqa(const void *q, const void *k, const void *vt, int ldvt,
                        "attention_gqa");
 }
 
+int e2cuda_attention_window(const void *q, const void *k, const void *vt, int ldvt, const uint8_t *valid, float *ctx,
+                            int B, int S, int H, int KV, int D, float scale, int window, void *stream) {
+    if (!q || !k || !vt || !ctx) {
+        e2cu_err("attention_window: bad arguments");
+        return -1;
+    }
+    return e2cu_launch(e2c_attention_win(q, k, vt, ldvt, valid, ctx, B, S, H, KV, D, scale, window, e2cu_status(), stream),
+                       "attention_window");
+}
+
 /* ------------------------------------------------------------------ fused FFN (config 1) */
 struct e2cuda_ffn {
     int D, I, max_tokens;

@@ -151,6 +151,31 @@ int e2c_meanpool(const float *x, const uint8_t *valid, float *pooled, int B, int
 /* rows of y [B][D] L2-normalised in place; rows whose sequence has no valid token become 0 */
 int e2c_l2norm_rows(float *y, const uint8_t *valid, int B, int S, int D, void *stream);
 
+/* ---- row kernels of e2.c's own text tower (text_rows.cu); D, P, I multiples of 128, ablk 128 or
+ * the row width */
+/* x = bf16 table[id] * embed_scale -> res; quantise(x) -> qx, qxs; quantise(rmsnorm(x) * gamma) -> qn,
+ * qns. An id outside [0, vocab) reads row 0 and records status 0x106. */
+int e2c_tt_embed(const int32_t *ids, const uint16_t *table, float embed_scale, const float *gamma, float eps,
+                 float *res, int8_t *qx, float *qxs, int8_t *qn, float *qns, int M, int D, int ablk, int vocab,
+                 int *status, void *stream);
+/* per row and slice of P columns (nslices slices, rows ld floats apart): v = ple * scale, then
+ * rmsnorm(v) * gamma, in place */
+int e2c_tt_ple_norm(float *ple, int ld, int nslices, int P, float scale, const float *gamma, float eps, int M,
+                    void *stream);
+/* q|k|v fp32 y [M][ldy] as [H q heads | KV k heads | KV v heads] of D (256 or 512) -> per-head
+ * RMSNorm (q_gamma, k_gamma [D]; v without) -> RoPE on q and k (pair-major tables [D/2][ldrope]) ->
+ * bf16 Q [M][H D], K [M][KV D], V^T [M / seq_len][KV D][ldvt] */
+int e2c_tt_qkv_post(const float *y, int ldy, int H, int KV, int D, const float *q_gamma, const float *k_gamma,
+                    float eps, const float *rope_cos, const float *rope_sin, int ldrope, int seq_len, void *q_out,
+                    void *k_out, void *vt_out, int ldvt, int M, void *stream);
+/* x = (rmsnorm(t) * g1 + res) * layer_scalar -> res; quantise(rmsnorm(x) * g2) -> q, qs, or
+ * quantise(x) when g2 is NULL */
+int e2c_tt_norm_add(const float *t, float *res, const float *g1, float layer_scalar, const float *g2, float eps,
+                    int8_t *q, float *qs, int M, int D, int ablk, void *stream);
+/* h = gelu_tanh(g) * u over I columns (g rows ldg floats apart, u rows ldu apart) -> quantise -> q, qs */
+int e2c_tt_gate_quant(const float *g, int ldg, const float *u, int ldu, int I, int8_t *q, float *qs, int M,
+                      int ablk, void *stream);
+
 /* ---- attention: bf16 Q [B*S][H*256], K [B*S][256], V^T [B][256][ldvt] -> ctx fp32 [B*S][H*256] */
 int e2c_attention(const void *q, const void *k, const void *vt, int ldvt, const uint8_t *valid,
                   float *ctx, int B, int S, int H, float scale, int *status, void *stream);
@@ -158,6 +183,13 @@ int e2c_attention(const void *q, const void *k, const void *vt, int ldvt, const 
  * head h / (H / KV)): Q [B*S][H*D], K [B*S][KV*D], V^T [B][KV*D][ldvt] -> ctx [B*S][H*D] */
 int e2c_attention_gqa(const void *q, const void *k, const void *vt, int ldvt, const uint8_t *valid, float *ctx,
                       int B, int S, int H, int KV, int D, float scale, int *status, void *stream);
+/* the same with a sliding window: query i attends to keys j with |i - j| <= window (window < 0: all
+ * keys), e2.c src/text.c:656-661; D 64, 256 or 512 (512: attention_wide.cu) */
+int e2c_attention_win(const void *q, const void *k, const void *vt, int ldvt, const uint8_t *valid, float *ctx,
+                      int B, int S, int H, int KV, int D, float scale, int window, int *status, void *stream);
+/* head dim 512 (attention_wide.cu), called by e2c_attention_win after its checks */
+int e2c_attention_wide(const void *q, const void *k, const void *vt, int ldvt, const uint8_t *valid, float *ctx,
+                       int B, int S, int H, int KV, float scale, int window, int *status, void *stream);
 
 /* ---- self-test of the bounded wait (selftest.cu): one warp waits on an mbarrier that receives
  * its arrival first (arrive != 0) or never (arrive == 0). *completed is 1 if the wait completed, 0

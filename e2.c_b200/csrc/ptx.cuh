@@ -343,6 +343,17 @@ E2C_DEV uint64_t smem_desc_sw128(uint32_t addr) {
     return d;
 }
 
+// The same for K-major tiles whose rows are 64 bytes, stored with the 64-byte swizzle (8-row groups
+// 512 bytes apart; layout type 4 = SWIZZLE_64B).
+E2C_DEV uint64_t smem_desc_sw64(uint32_t addr) {
+    uint64_t d = 0;
+    d |= (uint64_t)((addr >> 4) & 0x3FFFu);
+    d |= (uint64_t)(512u >> 4) << 32;  // stride byte offset
+    d |= (uint64_t)1 << 46;             // descriptor version (sm_100)
+    d |= (uint64_t)4 << 61;             // SWIZZLE_64B
+    return d;
+}
+
 // Instruction descriptors (M = 128, K-major A and B, dense).
 __host__ __device__ constexpr uint32_t idesc_i8(int n, int m = 128) {
     return (2u << 4)            // D = s32

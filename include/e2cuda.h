@@ -182,6 +182,12 @@ int e2cuda_attention(const void *q, const void *k, const void *vt, int ldvt, con
  * up to 2520 patches); D = 256 with KV = 1 is e2cuda_attention. */
 int e2cuda_attention_gqa(const void *q, const void *k, const void *vt, int ldvt, const uint8_t *valid,
                          float *ctx, int B, int S, int H, int KV, int D, float scale, void *stream);
+/* The same with a sliding window (e2.c's attention_blocked / attn_rows with L->sliding, src/text.c:
+ * 656-661,723-729): query i attends to keys j with |i - j| <= window; window < 0 attends to every key.
+ * D is 64, 256 or 512 (512: e2.c's full-attention layers; each 128-query tile runs as two halves of
+ * the value dimensions). */
+int e2cuda_attention_window(const void *q, const void *k, const void *vt, int ldvt, const uint8_t *valid,
+                            float *ctx, int B, int S, int H, int KV, int D, float scale, int window, void *stream);
 
 /* ------------------------------------------------------------------ fused FFN block (config 1) */
 typedef struct e2cuda_ffn e2cuda_ffn;
@@ -242,6 +248,56 @@ int e2cuda_encoder_embed_batch_device(e2cuda_encoder *e, const int32_t *d_ids, c
                                       int batch, int seq_len, float *d_out, void *stream);
 /* Calls served, kernels in the last pass, wall time of the last host call (e2hip.h:62-64). */
 int e2cuda_encoder_stats(e2cuda_encoder *e, long *calls, long *kernels_last, double *last_ms);
+
+/* ------------------------------------------------------------------ e2.c's own text tower */
+/* EmbeddingGemma-2's text tower as e2.c runs it (src/text.c:924-984): per layer RMSNorm ->
+ * attention (q/k/v projections, q/k/v RMSNorm, RoPE, 4 query heads, head dim 256 with 2 KV heads and
+ * a 512-key sliding window, or head dim 512 with 1 KV head and full attention; scale 1.0) ->
+ * residual norms -> gated GELU-tanh MLP -> residual norms -> per-layer-embedding (PLE) block ->
+ * layer scalar; PLE projection of the input embeddings; final norm, embed_proj to out_dim, masked
+ * mean pool, L2. This is the device half of the backend e2hip.h gives AMD GPUs (e2hip.h:32-64):
+ * e2.c's loader fills the description from its e2_model (the e2_q8w weights it built, the bf16 token
+ * table it mapped, the fp32 norm vectors), the library uploads it once. */
+typedef struct e2cuda_text e2cuda_text;
+
+typedef struct e2cuda_text_layer {
+    const e2cuda_q8w *q, *k, *v, *o, *gate, *up, *down, *ple_gate, *ple_proj; /* e2_layer.q8_*      */
+    const float *input_ln, *post_attn_ln, *pre_ffn_ln, *post_ffn_ln, *ple_norm; /* [hidden]        */
+    const float *q_norm, *k_norm;                                               /* [head_dim]      */
+    float layer_scalar;
+    int head_dim, n_kv_heads; /* 256 / 2 (sliding) or 512 / 1 (full) in EmbeddingGemma-2        */
+    int window;               /* keys with |i - j| <= window attend; < 0: full attention          */
+    float rope_theta;
+} e2cuda_text_layer;
+
+typedef struct e2cuda_text_desc {
+    int n_layers, hidden, intermediate, ple_dim, n_heads, vocab, out_dim;
+    int max_seq;  /* longest sequence a call may pass (RoPE table size; e2.c: 2048)               */
+    int ablk;     /* activation block: 128 (e2.c's E2_I8_BLOCK; the default when 0) or hidden    */
+    float eps, embed_scale, ple_scale;
+    const uint16_t *embed_tokens;     /* bf16 [vocab][hidden], copied at create time              */
+    const e2cuda_q8w *ple_model_proj; /* [n_layers * ple_dim][hidden]                             */
+    const e2cuda_q8w *embed_proj;     /* [out_dim][hidden]                                        */
+    const float *ple_proj_norm;       /* [ple_dim]                                                */
+    const float *final_norm;          /* [hidden]                                                 */
+    const e2cuda_text_layer *layers;  /* [n_layers]                                               */
+} e2cuda_text_desc;
+
+/* Uploads everything once (e2_hip_create, e2hip.h:32). max_tokens bounds batch * seq_len of one
+ * device pass (larger batches are chunked by whole sequences). NULL on failure. */
+e2cuda_text *e2cuda_text_create(const e2cuda_text_desc *d, int max_tokens);
+void e2cuda_text_destroy(e2cuda_text *t);
+/* One sequence of n_ids tokens -> one out_dim unit vector (e2_hip_text_embed, e2hip.h:39). */
+int e2cuda_text_embed(e2cuda_text *t, const int32_t *ids, int n_ids, float *out);
+/* batch x seq_len tokens, valid NULL or nonzero-keeps, positions restart per sequence; all-invalid
+ * sequences give zeros (e2_hip_text_embed_batch, e2hip.h:44-50). Host buffers. */
+int e2cuda_text_embed_batch(e2cuda_text *t, const int32_t *ids, const uint8_t *valid, int batch, int seq_len,
+                            float *out);
+/* The same on device buffers, stream-ordered (e2cuda_check before reading d_out). */
+int e2cuda_text_embed_batch_device(e2cuda_text *t, const int32_t *d_ids, const uint8_t *d_valid, int batch,
+                                   int seq_len, float *d_out, void *stream);
+/* Calls served, kernels in the last pass, wall time of the last host call (e2_hip_stats, e2hip.h:62). */
+int e2cuda_text_stats(e2cuda_text *t, long *calls, long *kernels_last, double *last_ms);
 
 #ifdef __cplusplus
 }

@@ -5,7 +5,9 @@ module. It wraps two kinds of library built by ``oracle/Makefile``:
 
 * ``oracle/liboracle.so`` -- the plain-C restatement of the reference kernels (the "port");
 * ``oracle/_ref/libe2ref_b<B>.so`` -- the reference's own kernel sources compiled with their own
-  flags and ``-DE2_I8_BLOCK=<B>`` (absent where the reference sources were not available to build).
+  flags and ``-DE2_I8_BLOCK=<B>`` (absent where the reference sources were not available to build);
+* ``oracle/_ref/libe2ref_text.so`` -- the reference's whole engine (loader + text tower), the
+  checker of the device text tower (``RefText``).
 
 Arrays are numpy; every wrapper checks dtype/contiguity and returns fresh outputs.
 """
@@ -363,3 +365,74 @@ def gemm_ref(lib, qa_biased: np.ndarray, as_: np.ndarray, w: Weight, fn="e2_i8_g
     getattr(lib, fn)(_ptr(y, f32p), _ptr(np.ascontiguousarray(qa_biased).view(np.int8), i8p),
                      _ptr(np.ascontiguousarray(as_, np.float32), f32p), C.byref(w.q), M, w.N, 0, w.N)
     return y
+
+
+# ------------------------------------------------------------------------------ e2.c's own text tower
+REF_TEXT_LIB = REF_DIR / "libe2ref_text.so"
+ATTN_TABLE, ATTN_F32, ATTN_I8 = -1, 0, 2  # e2_attn_kind (src/dispatch.h:26), -1: the dispatch table
+
+
+class RefText:
+    """e2.c's loader and text tower (oracle/ref_text.c over the reference's sources). One model per
+    process (e2.c's own rule): `load` once, `embed_batch` any number of times."""
+
+    def __init__(self):
+        if not REF_TEXT_LIB.exists():
+            raise FileNotFoundError(f"{REF_TEXT_LIB} was not built (make -C oracle needs the reference sources)")
+        lib = C.CDLL(str(REF_TEXT_LIB))
+        lib.ref_text_load.argtypes = [C.c_char_p, C.c_char_p]
+        lib.ref_text_error.restype = C.c_char_p
+        lib.ref_text_embed_batch.argtypes = [i32p, u8p, C.c_int, C.c_int, f32p]
+        lib.ref_text_attention.argtypes = [C.c_int]
+        lib.ref_text_describe.argtypes = [C.c_void_p, C.c_void_p]
+        lib.ref_text_cuda_create.restype = C.c_void_p
+        lib.e2_cuda_text_embed_batch.argtypes = [C.c_void_p, i32p, u8p, C.c_int, C.c_int, f32p]
+        lib.e2_cuda_destroy.argtypes = [C.c_void_p]
+        self.lib = lib
+
+    def load(self, model_dir, cache_path) -> None:
+        if self.lib.ref_text_load(str(model_dir).encode(), str(cache_path).encode()) != 0:
+            raise RuntimeError(f"e2_load: {self.lib.ref_text_error().decode()}")
+
+    def threads(self) -> int:
+        return self.lib.ref_text_threads()
+
+    def embed_batch(self, ids: np.ndarray, valid: np.ndarray | None = None, attention: int = ATTN_TABLE) -> np.ndarray:
+        ids = np.ascontiguousarray(ids, np.int32)
+        B, S = ids.shape
+        v = None if valid is None else np.ascontiguousarray(valid, np.uint8)
+        out = np.zeros((B, 768), np.float32)
+        self.lib.ref_text_attention(attention)
+        try:
+            rc = self.lib.ref_text_embed_batch(_ptr(ids, i32p), None if v is None else _ptr(v, u8p), B, S, _ptr(out, f32p))
+        finally:
+            self.lib.ref_text_attention(ATTN_TABLE)
+        if rc != 0:
+            raise RuntimeError(f"e2_text_embed_batch: {self.lib.ref_text_error().decode()}")
+        return out
+
+    def describe(self, desc, layers) -> None:
+        """Fill an e2cuda_text_desc (and its layer array) from the loaded e2_model: what the
+        binding e2_cuda_create hands the library."""
+        if self.lib.ref_text_describe(C.addressof(desc), C.addressof(layers)) != 0:
+            raise RuntimeError("e2_cuda_describe: no int8 model loaded")
+
+    def cuda_embed_batch(self, ids: np.ndarray, valid: np.ndarray | None = None) -> np.ndarray:
+        """Through the binding as e2.c would call it: e2_cuda_create(m), e2_cuda_text_embed_batch."""
+        g = self.lib.ref_text_cuda_create()
+        if not g:
+            raise RuntimeError("e2_cuda_create failed")
+        try:
+            ids = np.ascontiguousarray(ids, np.int32)
+            B, S = ids.shape
+            v = None if valid is None else np.ascontiguousarray(valid, np.uint8)
+            out = np.zeros((B, 768), np.float32)
+            if self.lib.e2_cuda_text_embed_batch(g, _ptr(ids, i32p), None if v is None else _ptr(v, u8p), B, S,
+                                                 _ptr(out, f32p)) != 0:
+                raise RuntimeError("e2_cuda_text_embed_batch failed")
+            return out
+        finally:
+            self.lib.e2_cuda_destroy(g)
+
+    def free(self) -> None:
+        self.lib.ref_text_free()

@@ -77,3 +77,32 @@ def tie_tolerant_bytes(got: np.ndarray, want: np.ndarray, pre_round: np.ndarray,
     near = np.abs(np.abs(pre_round - np.floor(pre_round)) - 0.5) < band
     bad = (d > 1) | ((d == 1) & ~near)
     assert not bad.any(), f"{int(bad.sum())} bytes differ beyond the tie rule (of {d.size}); max delta {int(d.max())}"
+
+
+# ------------------------------------------------------------------------------ e2.c's own text tower
+@pytest.fixture(scope="session")
+def text_tensors():
+    """The seeded random-init text-tower checkpoint (bf16 bit patterns by tensor name)."""
+    load_e2c()
+    import e2c_b200.text_model as tm
+
+    return tm.random_tensors()
+
+
+@pytest.fixture(scope="session")
+def text_model_dir(tmp_path_factory, text_tensors):
+    """<dir>/model.safetensors of text_tensors, as e2.c's loader reads it."""
+    import e2c_b200.text_model as tm
+
+    d = tmp_path_factory.mktemp("text_model")
+    tm.write_safetensors(d / "model.safetensors", text_tensors)
+    return d
+
+
+@pytest.fixture(scope="session")
+def ref_text(of, text_model_dir):
+    """e2.c's own engine with the checkpoint loaded (one model per process, e2.c's rule)."""
+    r = of.RefText()
+    r.load(text_model_dir, text_model_dir / "text.e8cq")
+    yield r
+    r.free()
