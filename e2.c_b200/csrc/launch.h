@@ -162,12 +162,13 @@ int e2c_tt_embed(const int32_t *ids, const uint16_t *table, float embed_scale, c
  * rmsnorm(v) * gamma, in place */
 int e2c_tt_ple_norm(float *ple, int ld, int nslices, int P, float scale, const float *gamma, float eps, int M,
                     void *stream);
-/* q|k|v fp32 y [M][ldy] as [H q heads | KV k heads | KV v heads] of D (256 or 512) -> per-head
- * RMSNorm (q_gamma, k_gamma [D]; v without) -> RoPE on q and k (pair-major tables [D/2][ldrope]) ->
- * bf16 Q [M][H D], K [M][KV D], V^T [M / seq_len][KV D][ldvt] */
+/* q|k|v fp32 y [M][ldy] as [H q heads | KV k heads | KV v heads] of D (256 or 512, KV D <= 512) -> per-head
+ * RMSNorm (q_gamma, k_gamma [D]; v without) -> RoPE on q and k -> bf16 Q [M][H D], K [M][KV D],
+ * V^T [M / seq_len][KV D][ldvt]. RoPE tables position-major ([pos][ldrope], rope_pos_major != 0) or
+ * pair-major ([D/2][ldrope]). */
 int e2c_tt_qkv_post(const float *y, int ldy, int H, int KV, int D, const float *q_gamma, const float *k_gamma,
-                    float eps, const float *rope_cos, const float *rope_sin, int ldrope, int seq_len, void *q_out,
-                    void *k_out, void *vt_out, int ldvt, int M, void *stream);
+                    float eps, const float *rope_cos, const float *rope_sin, int ldrope, int rope_pos_major,
+                    int seq_len, void *q_out, void *k_out, void *vt_out, int ldvt, int M, void *stream);
 /* x = (rmsnorm(t) * g1 + res) * layer_scalar -> res; quantise(rmsnorm(x) * g2) -> q, qs, or
  * quantise(x) when g2 is NULL */
 int e2c_tt_norm_add(const float *t, float *res, const float *g1, float layer_scalar, const float *g2, float eps,

@@ -150,66 +150,6 @@ __global__ void k_l2norm_rows(float *__restrict__ y, const uint8_t *__restrict__
     for (int d = lane; d < D; d += 32) r[d] = any ? __fmul_rn(r[d], inv) : 0.f;
 }
 
-// One warp per (token row, head of 256): lane l holds elements 4l..4l+3 (a) and their rotate-half
-// partners 128+4l.. (b). RMSNorm over the head (q heads with q_gamma, the k head with k_gamma, the v
-// head without a learned scale), RoPE on q and k (pair-major tables [128][ldrope], pos = row %
-// seq_len, the AVX-512 form of src/kernels_avx512.c:246-250 as the fused QKV epilogue computes it),
-// bf16 out: Q [M][256 nq], K [M][256], V^T [M / seq_len][256][ldvt].
-__global__ void __launch_bounds__(256) k_qkv_post(const float *__restrict__ y, int ldy, int nq, const float *__restrict__ qg,
-                                                  const float *__restrict__ kg, float eps, const float *__restrict__ rcos,
-                                                  const float *__restrict__ rsin, int ldrope, int seq_len,
-                                                  __nv_bfloat16 *__restrict__ Q, __nv_bfloat16 *__restrict__ Kout,
-                                                  __nv_bfloat16 *__restrict__ Vt, int ldvt, int M) {
-    griddep_launch_dependents();
-    griddep_wait();
-    const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-    const int nh = nq + 2;
-    if (w >= M * nh) return;
-    const int row = w / nh, head = w - row * nh;
-    const float4 *src = reinterpret_cast<const float4 *>(y + (size_t)row * ldy + head * 256);
-    float4 a[1] = {src[lane]}, b[1] = {src[32 + lane]};
-    const float inv = rms_inv(__fadd_rn(sumsq(a), sumsq(b)), 256, eps);
-    const float *g = head < nq ? qg : head == nq ? kg : nullptr;
-    const float4 ga = g ? __ldg(reinterpret_cast<const float4 *>(g) + lane) : make_float4(1.f, 1.f, 1.f, 1.f);
-    const float4 gb = g ? __ldg(reinterpret_cast<const float4 *>(g) + 32 + lane) : make_float4(1.f, 1.f, 1.f, 1.f);
-    float va[4], vb[4];
-    {
-        const float4 na = g ? norm4(a[0], inv, ga) : make_float4(__fmul_rn(a[0].x, inv), __fmul_rn(a[0].y, inv),
-                                                                 __fmul_rn(a[0].z, inv), __fmul_rn(a[0].w, inv));
-        const float4 nb = g ? norm4(b[0], inv, gb) : make_float4(__fmul_rn(b[0].x, inv), __fmul_rn(b[0].y, inv),
-                                                                 __fmul_rn(b[0].z, inv), __fmul_rn(b[0].w, inv));
-        va[0] = na.x, va[1] = na.y, va[2] = na.z, va[3] = na.w;
-        vb[0] = nb.x, vb[1] = nb.y, vb[2] = nb.z, vb[3] = nb.w;
-    }
-    const int pos = row % seq_len;
-    if (head <= nq) {
-#pragma unroll
-        for (int j = 0; j < 4; j++) {
-            const int i = 4 * lane + j;
-            const float c = __ldg(rcos + (size_t)i * ldrope + pos), sn = __ldg(rsin + (size_t)i * ldrope + pos);
-            const float x = va[j], z = vb[j];
-            va[j] = __fmaf_rn(x, c, -__fmul_rn(z, sn));
-            vb[j] = __fmaf_rn(x, sn, __fmul_rn(z, c));
-        }
-    }
-    if (head < nq || head == nq) {
-        __nv_bfloat16 *dst = head < nq ? Q + (size_t)row * (256 * nq) + head * 256 : Kout + (size_t)row * 256;
-        const __nv_bfloat162 p0 = __floats2bfloat162_rn(va[0], va[1]), p1 = __floats2bfloat162_rn(va[2], va[3]);
-        const __nv_bfloat162 p2 = __floats2bfloat162_rn(vb[0], vb[1]), p3 = __floats2bfloat162_rn(vb[2], vb[3]);
-        *reinterpret_cast<uint2 *>(dst + 4 * lane) =
-            make_uint2(*reinterpret_cast<const uint32_t *>(&p0), *reinterpret_cast<const uint32_t *>(&p1));
-        *reinterpret_cast<uint2 *>(dst + 128 + 4 * lane) =
-            make_uint2(*reinterpret_cast<const uint32_t *>(&p2), *reinterpret_cast<const uint32_t *>(&p3));
-    } else {
-        __nv_bfloat16 *vt = Vt + (size_t)(row / seq_len) * 256 * ldvt + pos;
-#pragma unroll
-        for (int j = 0; j < 4; j++) {
-            vt[(size_t)(4 * lane + j) * ldvt] = __float2bfloat16_rn(va[j]);
-            vt[(size_t)(128 + 4 * lane + j) * ldvt] = __float2bfloat16_rn(vb[j]);
-        }
-    }
-}
-
 // One warp per token row of the gate|up GEMM's fp32 output, columns interleaved per 128
 // ([g 0..127 | u 0..127 | g 128..255 | ...]): h = gelu_tanh(g) * u with the GELU epilogue's element
 // function, then the per-row quantiser of h (per 128-block or per token).
@@ -310,16 +250,9 @@ extern "C" int e2c_l2norm_rows(float *y, const uint8_t *valid, int B, int S, int
 extern "C" int e2c_qkv_post(const float *y, int ldy, int nq, const float *q_gamma, const float *k_gamma, float eps,
                             const float *rope_cos, const float *rope_sin, int ldrope, int seq_len, void *q_out,
                             void *k_out, void *vt_out, int ldvt, int M, void *stream) {
-    if (nq <= 0 || ldy % 4 || ldy < 256 * (nq + 2) || seq_len <= 0 || M % seq_len || ldrope < seq_len || ldvt < seq_len) {
-        e2c_set_msg("qkv_post: bad geometry (nq=%d ldy=%d seq_len=%d ldrope=%d ldvt=%d M=%d)", nq, ldy, seq_len, ldrope, ldvt, M);
-        return -1;
-    }
-    if (M <= 0) return 0;
-    const long warps = (long)M * (nq + 2);
-    e2c_launch(k_qkv_post, dim3((unsigned)((warps + 7) / 8)), dim3(256), 0, (cudaStream_t)stream, y, ldy, nq, q_gamma,
-               k_gamma, eps, rope_cos, rope_sin, ldrope, seq_len, (__nv_bfloat16 *)q_out, (__nv_bfloat16 *)k_out,
-               (__nv_bfloat16 *)vt_out, ldvt, M);
-    return check("qkv_post");
+    // nq q heads, one k and one v head of 256: the text tower's finish with KV = 1 (text_rows.cu)
+    return e2c_tt_qkv_post(y, ldy, nq, 1, 256, q_gamma, k_gamma, eps, rope_cos, rope_sin, ldrope, 0, seq_len, q_out,
+                           k_out, vt_out, ldvt, M, stream);
 }
 
 extern "C" int e2c_gelu_mul_quant(const float *y, int ldy, int I, int8_t *q, float *qs, int M, int ablk, void *stream) {

@@ -89,84 +89,121 @@ __global__ void __launch_bounds__(256) k_tt_ple_norm(float *__restrict__ ple, in
     for (int i = 0; i < NV; i++) src[lane + 32 * i] = norm4(v[i], inv, __ldg(g4 + lane + 32 * i));
 }
 
-// One warp per (token row, head) over q|k|v fp32 [M][ldy] laid out [H q heads | KV k heads | KV v
-// heads] of D = 256 NVH: lane l holds float4s l + 32 i of the head's first half (a) and their
-// rotate-half partners in the second half (b). RMSNorm over the head, RoPE on q and k with the
-// pair-major tables [D/2][ldrope] (pos = row % seq_len; the AVX-512 form of src/kernels_avx512.c:
-// 309-331, a' = fma(a, c, -(y s)), y' = fma(a, s, y c)), bf16 out: Q [M][H D], K [M][KV D],
-// V^T [M / seq_len][KV D][ldvt].
+// q|k|v fp32 [M][ldy] laid out [H q heads | KV k heads | KV v heads] of D = 256 NVH. One CTA per
+// (sequence, tile of 32 positions); its 8 warps take (position, head) items in turn. Per item, lane l
+// holds float4s l + 32 i of the head's first half (a) and their rotate-half partners in the second
+// half (b): RMSNorm over the head, RoPE on q and k (the AVX-512 form of src/kernels_avx512.c:309-331, a' = fma(a, c, -(y s)), y' = fma(a, s, y c)); Q
+// [M][H D] and K [M][KV D] are stored in bf16 straight from the warp, 512 contiguous bytes per
+// instruction. V is staged in shared memory and leaves transposed, V^T [B][KV D][ldvt]: each of its
+// rows gets the tile's 32 positions as 64 contiguous bytes (a position-major store would write one
+// 2-byte element per 32-byte sector). The RoPE tables are position-major ([pos][ldrope], pair e of
+// position p at p * ldrope + e: a lane's four pairs in one 16-byte load) or pair-major ([D/2][ldrope],
+// at e * ldrope + p: the layout the fused QKV GEMM epilogue reads, where a warp's lanes are positions).
+constexpr int QKV_TILE = 32;
+
 template <int NVH>
 __global__ void __launch_bounds__(256) k_tt_qkv_post(const float *__restrict__ y, int ldy, int H, int KV,
                                                      const float *__restrict__ qg, const float *__restrict__ kg, float eps,
                                                      const float *__restrict__ rcos, const float *__restrict__ rsin,
-                                                     int ldrope, int seq_len, __nv_bfloat16 *__restrict__ Q,
+                                                     int ldrope, int pos_major, int S, int ntiles,
+                                                     __nv_bfloat16 *__restrict__ Q,
                                                      __nv_bfloat16 *__restrict__ Kout, __nv_bfloat16 *__restrict__ Vt,
-                                                     int ldvt, int M) {
+                                                     int ldvt) {
     griddep_launch_dependents();
     griddep_wait();
     constexpr int D = 256 * NVH, HALF4 = D / 8;  // float4s in half a head
-    const long w = ((long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    const int lane = threadIdx.x & 31;
+    extern __shared__ __nv_bfloat16 vs[];         // [QKV_TILE][KV D + 2]
+    const int ldv = KV * D + 2;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int b = blockIdx.x / ntiles, p0 = (blockIdx.x - b * ntiles) * QKV_TILE;
+    const int npos = min(QKV_TILE, S - p0);
     const int nh = H + 2 * KV;
-    if (w >= (long)M * nh) return;
-    const int row = (int)(w / nh), head = (int)(w - (long)row * nh);
-    const int kind = head < H ? 0 : head < H + KV ? 1 : 2;  // q, k, v
-    const float4 *src = reinterpret_cast<const float4 *>(y + (size_t)row * ldy + (size_t)head * D);
-    float4 a[NVH], b[NVH];
+    for (int it = warp; it < npos * nh; it += 8) {
+        const int r = it / nh, head = it - r * nh;
+        const int pos = p0 + r;
+        const size_t row = (size_t)b * S + pos;
+        const int kind = head < H ? 0 : head < H + KV ? 1 : 2;  // q, k, v
+        const float4 *src = reinterpret_cast<const float4 *>(y + row * ldy + (size_t)head * D);
+        float4 a[NVH], bb[NVH];
 #pragma unroll
-    for (int i = 0; i < NVH; i++) {
-        a[i] = src[lane + 32 * i];
-        b[i] = src[HALF4 + lane + 32 * i];
-    }
-    const float inv = rms_inv(__fadd_rn(sumsq(a), sumsq(b)), D, eps);
-    const float *g = kind == 0 ? qg : kind == 1 ? kg : nullptr;
+        for (int i = 0; i < NVH; i++) {
+            a[i] = src[lane + 32 * i];
+            bb[i] = src[HALF4 + lane + 32 * i];
+        }
+        const float inv = rms_inv(__fadd_rn(sumsq(a), sumsq(bb)), D, eps);
+        const float *g = kind == 0 ? qg : kind == 1 ? kg : nullptr;
 #pragma unroll
-    for (int i = 0; i < NVH; i++) {
-        if (g) {
-            a[i] = norm4(a[i], inv, __ldg(reinterpret_cast<const float4 *>(g) + lane + 32 * i));
-            b[i] = norm4(b[i], inv, __ldg(reinterpret_cast<const float4 *>(g) + HALF4 + lane + 32 * i));
+        for (int i = 0; i < NVH; i++) {
+            if (g) {
+                a[i] = norm4(a[i], inv, __ldg(reinterpret_cast<const float4 *>(g) + lane + 32 * i));
+                bb[i] = norm4(bb[i], inv, __ldg(reinterpret_cast<const float4 *>(g) + HALF4 + lane + 32 * i));
+            } else {
+                a[i] = mul4(a[i], inv);
+                bb[i] = mul4(bb[i], inv);
+            }
+        }
+        if (kind < 2) {
+#pragma unroll
+            for (int i = 0; i < NVH; i++) {
+                float *pa = reinterpret_cast<float *>(&a[i]), *pb = reinterpret_cast<float *>(&bb[i]);
+                const int e0 = 4 * (lane + 32 * i);
+                float cc[4], ss[4];
+                if (pos_major) {
+                    const float4 c4 = __ldg(reinterpret_cast<const float4 *>(rcos + (size_t)pos * ldrope + e0));
+                    const float4 s4 = __ldg(reinterpret_cast<const float4 *>(rsin + (size_t)pos * ldrope + e0));
+                    cc[0] = c4.x, cc[1] = c4.y, cc[2] = c4.z, cc[3] = c4.w;
+                    ss[0] = s4.x, ss[1] = s4.y, ss[2] = s4.z, ss[3] = s4.w;
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 4; j++) {
+                        cc[j] = __ldg(rcos + (size_t)(e0 + j) * ldrope + pos);
+                        ss[j] = __ldg(rsin + (size_t)(e0 + j) * ldrope + pos);
+                    }
+                }
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    const float x = pa[j], z = pb[j];
+                    pa[j] = __fmaf_rn(x, cc[j], -__fmul_rn(z, ss[j]));
+                    pb[j] = __fmaf_rn(x, ss[j], __fmul_rn(z, cc[j]));
+                }
+            }
+            __nv_bfloat16 *dst = kind == 0 ? Q + row * H * D + (size_t)head * D : Kout + row * KV * D + (size_t)(head - H) * D;
+#pragma unroll
+            for (int i = 0; i < NVH; i++) {
+                const __nv_bfloat162 q0 = __floats2bfloat162_rn(a[i].x, a[i].y), q1 = __floats2bfloat162_rn(a[i].z, a[i].w);
+                const __nv_bfloat162 q2 = __floats2bfloat162_rn(bb[i].x, bb[i].y), q3 = __floats2bfloat162_rn(bb[i].z, bb[i].w);
+                *reinterpret_cast<uint2 *>(dst + 4 * (lane + 32 * i)) =
+                    make_uint2(*reinterpret_cast<const uint32_t *>(&q0), *reinterpret_cast<const uint32_t *>(&q1));
+                *reinterpret_cast<uint2 *>(dst + D / 2 + 4 * (lane + 32 * i)) =
+                    make_uint2(*reinterpret_cast<const uint32_t *>(&q2), *reinterpret_cast<const uint32_t *>(&q3));
+            }
         } else {
-            a[i] = mul4(a[i], inv);
-            b[i] = mul4(b[i], inv);
+            __nv_bfloat16 *vr = vs + (size_t)r * ldv + (size_t)(head - H - KV) * D;
+#pragma unroll
+            for (int i = 0; i < NVH; i++) {
+                const float *pa = reinterpret_cast<const float *>(&a[i]), *pb = reinterpret_cast<const float *>(&bb[i]);
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    const int e = 4 * (lane + 32 * i) + j;
+                    vr[e] = __float2bfloat16_rn(pa[j]);
+                    vr[D / 2 + e] = __float2bfloat16_rn(pb[j]);
+                }
+            }
         }
     }
-    const int pos = row % seq_len;
-    if (kind < 2) {
-#pragma unroll
-        for (int i = 0; i < NVH; i++) {
-            float *pa = reinterpret_cast<float *>(&a[i]), *pb = reinterpret_cast<float *>(&b[i]);
-#pragma unroll
-            for (int j = 0; j < 4; j++) {
-                const int e = 4 * (lane + 32 * i) + j;
-                const float c = __ldg(rcos + (size_t)e * ldrope + pos), sn = __ldg(rsin + (size_t)e * ldrope + pos);
-                const float x = pa[j], z = pb[j];
-                pa[j] = __fmaf_rn(x, c, -__fmul_rn(z, sn));
-                pb[j] = __fmaf_rn(x, sn, __fmul_rn(z, c));
-            }
-        }
-        __nv_bfloat16 *dst = kind == 0 ? Q + (size_t)row * H * D + (size_t)head * D
-                                       : Kout + (size_t)row * KV * D + (size_t)(head - H) * D;
-#pragma unroll
-        for (int i = 0; i < NVH; i++) {
-            const __nv_bfloat162 p0 = __floats2bfloat162_rn(a[i].x, a[i].y), p1 = __floats2bfloat162_rn(a[i].z, a[i].w);
-            const __nv_bfloat162 p2 = __floats2bfloat162_rn(b[i].x, b[i].y), p3 = __floats2bfloat162_rn(b[i].z, b[i].w);
-            *reinterpret_cast<uint2 *>(dst + 4 * (lane + 32 * i)) =
-                make_uint2(*reinterpret_cast<const uint32_t *>(&p0), *reinterpret_cast<const uint32_t *>(&p1));
-            *reinterpret_cast<uint2 *>(dst + D / 2 + 4 * (lane + 32 * i)) =
-                make_uint2(*reinterpret_cast<const uint32_t *>(&p2), *reinterpret_cast<const uint32_t *>(&p3));
-        }
-    } else {
-        const int kvh = head - H - KV;
-        __nv_bfloat16 *vt = Vt + ((size_t)(row / seq_len) * KV + kvh) * D * (size_t)ldvt + pos;
-#pragma unroll
-        for (int i = 0; i < NVH; i++) {
-            const float *pa = reinterpret_cast<const float *>(&a[i]), *pb = reinterpret_cast<const float *>(&b[i]);
-#pragma unroll
-            for (int j = 0; j < 4; j++) {
-                const int e = 4 * (lane + 32 * i) + j;
-                vt[(size_t)e * ldvt] = __float2bfloat16_rn(pa[j]);
-                vt[(size_t)(D / 2 + e) * ldvt] = __float2bfloat16_rn(pb[j]);
-            }
+    __syncthreads();
+    // V^T rows (kv head, dim) x the tile's positions, two positions per thread and word
+    const int rows = KV * D;
+    __nv_bfloat16 *vt = Vt + (size_t)b * rows * ldvt + p0;
+    for (int w = threadIdx.x; w < rows * (QKV_TILE / 2); w += blockDim.x) {
+        const int d = w / (QKV_TILE / 2), pp = 2 * (w - d * (QKV_TILE / 2));
+        if (pp + 1 < npos) {
+            __nv_bfloat162 v2;
+            v2.x = vs[(size_t)pp * ldv + d];
+            v2.y = vs[(size_t)(pp + 1) * ldv + d];
+            *reinterpret_cast<__nv_bfloat162 *>(vt + (size_t)d * ldvt + pp) = v2;
+        } else if (pp < npos) {
+            vt[(size_t)d * ldvt + pp] = vs[(size_t)pp * ldv + d];
         }
     }
 }
@@ -284,24 +321,26 @@ extern "C" int e2c_tt_ple_norm(float *ple, int ld, int nslices, int P, float sca
 }
 
 extern "C" int e2c_tt_qkv_post(const float *y, int ldy, int H, int KV, int D, const float *q_gamma, const float *k_gamma,
-                               float eps, const float *rope_cos, const float *rope_sin, int ldrope, int seq_len, void *q_out,
+                               float eps, const float *rope_cos, const float *rope_sin, int ldrope, int rope_pos_major,
+                               int seq_len, void *q_out,
                                void *k_out, void *vt_out, int ldvt, int M, void *stream) {
-    if ((D != 256 && D != 512) || H <= 0 || KV <= 0 || ldy % 4 || ldy < D * (H + 2 * KV) || seq_len <= 0 || M % seq_len ||
-        ldrope < seq_len || ldvt < seq_len) {
-        e2c_set_msg("tt_qkv_post: bad geometry (D=%d H=%d KV=%d ldy=%d seq_len=%d ldrope=%d ldvt=%d M=%d)", D, H, KV, ldy,
-                    seq_len, ldrope, ldvt, M);
+    if ((D != 256 && D != 512) || H <= 0 || KV <= 0 || KV * D > 512 || ldy % 4 || ldy < D * (H + 2 * KV) || seq_len <= 0 ||
+        M % seq_len || ldvt < seq_len || ldvt % 8 || (rope_pos_major ? ldrope < D / 2 || ldrope % 4 : ldrope < seq_len)) {
+        e2c_set_msg("tt_qkv_post: bad geometry (D=%d H=%d KV=%d ldy=%d seq_len=%d ldrope=%d ldvt=%d M=%d; KV D <= 512, "
+                    "ldvt a multiple of 8)", D, H, KV, ldy, seq_len, ldrope, ldvt, M);
         return -1;
     }
     if (M <= 0) return 0;
-    const long warps = (long)M * (H + 2 * KV);
-    const dim3 grid((unsigned)((warps + 7) / 8)), block(256);
+    const int ntiles = (seq_len + QKV_TILE - 1) / QKV_TILE;
+    const dim3 grid((unsigned)((M / seq_len) * ntiles)), block(256);
+    const size_t smem = (size_t)QKV_TILE * (KV * D + 2) * 2;
     cudaStream_t st = (cudaStream_t)stream;
     if (D == 256)
-        e2c_launch(k_tt_qkv_post<1>, grid, block, 0, st, y, ldy, H, KV, q_gamma, k_gamma, eps, rope_cos, rope_sin, ldrope,
-                   seq_len, (__nv_bfloat16 *)q_out, (__nv_bfloat16 *)k_out, (__nv_bfloat16 *)vt_out, ldvt, M);
+        e2c_launch(k_tt_qkv_post<1>, grid, block, smem, st, y, ldy, H, KV, q_gamma, k_gamma, eps, rope_cos, rope_sin, ldrope,
+                   rope_pos_major, seq_len, ntiles, (__nv_bfloat16 *)q_out, (__nv_bfloat16 *)k_out, (__nv_bfloat16 *)vt_out, ldvt);
     else
-        e2c_launch(k_tt_qkv_post<2>, grid, block, 0, st, y, ldy, H, KV, q_gamma, k_gamma, eps, rope_cos, rope_sin, ldrope,
-                   seq_len, (__nv_bfloat16 *)q_out, (__nv_bfloat16 *)k_out, (__nv_bfloat16 *)vt_out, ldvt, M);
+        e2c_launch(k_tt_qkv_post<2>, grid, block, smem, st, y, ldy, H, KV, q_gamma, k_gamma, eps, rope_cos, rope_sin, ldrope,
+                   rope_pos_major, seq_len, ntiles, (__nv_bfloat16 *)q_out, (__nv_bfloat16 *)k_out, (__nv_bfloat16 *)vt_out, ldvt);
     return check("tt_qkv_post");
 }
 

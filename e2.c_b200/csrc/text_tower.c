@@ -138,7 +138,7 @@ static int upload_stack(const e2cuda_q8w *const *parts, int nparts, e2cuda_w8 *o
 }
 
 /* e2.c src/text.c:483-506: inv = 1 / theta^(2i / hd), angle = pos * inv; e2.c duplicates the halves,
- * here they are stored once, pair-major ([hd/2][max_seq]) */
+ * here they are stored once, position-major ([max_seq][hd/2]) for the q|k|v finish's warp per position */
 static int rope_table(e2cuda_text *t, int slot, int hd, float theta) {
     const int half = hd / 2;
     const size_t n = (size_t)t->max_seq * half;
@@ -153,8 +153,8 @@ static int rope_table(e2cuda_text *t, int slot, int hd, float theta) {
         for (int i = 0; i < half; i++) {
             const float inv = 1.0f / powf(theta, (float)(2 * i) / (float)hd);
             const float f = (float)p * inv;
-            c[(size_t)i * t->max_seq + p] = cosf(f);
-            s[(size_t)i * t->max_seq + p] = sinf(f);
+            c[(size_t)p * half + i] = cosf(f);
+            s[(size_t)p * half + i] = sinf(f);
         }
     const int rc = upload_floats(&t->rope_cos[slot], c, n, "rope upload") || upload_floats(&t->rope_sin[slot], s, n, "rope upload");
     free(c);
@@ -321,7 +321,7 @@ static int forward(e2cuda_text *t, int B, int S, int has_valid, cudaStream_t st)
         const int ldy = qd + 2 * kv * hd;
         Q(gemm_f32(&y->qkv, t->qa, t->qas, M, ab, t->yf, ldy, st), "text qkv");
         Q(e2c_tt_qkv_post(t->yf, ldy, H, kv, hd, lnorm(t, l, 5), lnorm(t, l, 6), t->eps, t->rope_cos[y->rope],
-                          t->rope_sin[y->rope], t->max_seq, S, t->Q, t->K, t->Vt, ldvt, M, st),
+                          t->rope_sin[y->rope], hd / 2, 1, S, t->Q, t->K, t->Vt, ldvt, M, st),
           "text qkv post");
         Q(e2c_attention_win(t->Q, t->K, t->Vt, ldvt, valid, t->ctx, B, S, H, kv, hd, 1.0f, y->window, t->status, st),
           "text attention");

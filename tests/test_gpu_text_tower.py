@@ -214,20 +214,21 @@ def test_tt_qkv_post_matches_port(e2c, of, torch_cuda, D, KV):
     sn = np.empty((S, D), np.float32)
     theta = 1e6 if D == 512 else 1e4
     of.port().e2o_rope_tables(cs.ctypes.data_as(of.f32p), sn.ctypes.data_as(of.f32p), S, D, theta)
-    ldrope, ldvt = S + 5, (S + 7) // 8 * 8
-    cT = np.zeros((D // 2, ldrope), np.float32)
-    sT = np.zeros((D // 2, ldrope), np.float32)
-    cT[:, :S], sT[:, :S] = cs[:, :D // 2].T, sn[:, :D // 2].T
+    # the tower's position-major tables [pos][ldrope] (row padding 4 floats)
+    ldrope, ldvt = D // 2 + 4, (S + 7) // 8 * 8
+    cT = np.zeros((S, ldrope), np.float32)
+    sT = np.zeros((S, ldrope), np.float32)
+    cT[:, :D // 2], sT[:, :D // 2] = cs[:, :D // 2], sn[:, :D // 2]
     Q = torch.zeros((M, H * D), dtype=torch.bfloat16, device="cuda")
     K = torch.zeros((M, KV * D), dtype=torch.bfloat16, device="cuda")
     Vt = torch.zeros((B, KV * D, ldvt), dtype=torch.bfloat16, device="cuda")
     yd, gq, gk, cd, sdn = (torch.from_numpy(t).cuda() for t in (y, qg, kg, cT, sT))
     lib = e2c.lib()
     lib.e2c_tt_qkv_post.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_float,
-                                    C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int,
-                                    C.c_int, C.c_void_p]
+                                    C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p,
+                                    C.c_int, C.c_int, C.c_void_p]
     assert lib.e2c_tt_qkv_post(yd.data_ptr(), nh * D, H, KV, D, gq.data_ptr(), gk.data_ptr(), 1e-6, cd.data_ptr(),
-                               sdn.data_ptr(), ldrope, S, Q.data_ptr(), K.data_ptr(), Vt.data_ptr(), ldvt, M,
+                               sdn.data_ptr(), ldrope, 1, S, Q.data_ptr(), K.data_ptr(), Vt.data_ptr(), ldvt, M,
                                torch.cuda.current_stream().cuda_stream) == 0, lib.e2c_msg().decode()
     e2c.check()
     port = of.port()
