@@ -723,8 +723,7 @@ def text_pass_work(B: int, S: int, cfg) -> list:
     def gemm(name, K, N):
         return (name, 2.0 * M * K * N, 0.0, M * K + 4 * M * K / 128 + N * K + 4 * N + 4 * M * N)
 
-    w = [("embed", 0, 0, 4 * M + 2 * M * D + 4 * M * D + 2 * (M * D + 4 * M * D / 128)), gemm("ple_proj_model", D, L * P),
-         ("ple_norm", 0, 0, 8 * M * L * P)]
+    w = [("embed", 0, 0, 4 * M + 2 * M * D + 4 * M * D + 2 * (M * D + 4 * M * D / 128)), gemm("ple_proj_model", D, L * P)]
     for l in range(L):
         hd, kv, qd = cfg.head_dim(l), cfg.n_kv(l), cfg.q_dim(l)
         nqkv = qd + 2 * kv * hd

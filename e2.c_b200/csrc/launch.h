@@ -158,10 +158,6 @@ int e2c_l2norm_rows(float *y, const uint8_t *valid, int B, int S, int D, void *s
 int e2c_tt_embed(const int32_t *ids, const uint16_t *table, float embed_scale, const float *gamma, float eps,
                  float *res, int8_t *qx, float *qxs, int8_t *qn, float *qns, int M, int D, int ablk, int vocab,
                  int *status, void *stream);
-/* per row and slice of P columns (nslices slices, rows ld floats apart): v = ple * scale, then
- * rmsnorm(v) * gamma, in place */
-int e2c_tt_ple_norm(float *ple, int ld, int nslices, int P, float scale, const float *gamma, float eps, int M,
-                    void *stream);
 /* q|k|v fp32 y [M][ldy] as [H q heads | KV k heads | KV v heads] of D (256 or 512, KV D <= 512) -> per-head
  * RMSNorm (q_gamma, k_gamma [D]; v without) -> RoPE on q and k -> bf16 Q [M][H D], K [M][KV D],
  * V^T [M / seq_len][KV D][ldvt]. RoPE tables position-major ([pos][ldrope], rope_pos_major != 0) or
@@ -173,9 +169,10 @@ int e2c_tt_qkv_post(const float *y, int ldy, int H, int KV, int D, const float *
  * quantise(x) when g2 is NULL */
 int e2c_tt_norm_add(const float *t, float *res, const float *g1, float layer_scalar, const float *g2, float eps,
                     int8_t *q, float *qs, int M, int D, int ablk, void *stream);
-/* h = gelu_tanh(g) * u over I columns (g rows ldg floats apart, u rows ldu apart) -> quantise -> q, qs */
-int e2c_tt_gate_quant(const float *g, int ldg, const float *u, int ldu, int I, int8_t *q, float *qs, int M,
-                      int ablk, void *stream);
+/* h = gelu_tanh(g) * u over I columns (g rows ldg floats apart, u rows ldu apart) -> quantise -> q, qs.
+ * ugamma given: u is first rmsnorm(u * uscale) * ugamma over its I values (the PLE slice's norm). */
+int e2c_tt_gate_quant(const float *g, int ldg, const float *u, int ldu, float uscale, const float *ugamma, float eps,
+                      int I, int8_t *q, float *qs, int M, int ablk, void *stream);
 
 /* ---- attention: bf16 Q [B*S][H*256], K [B*S][256], V^T [B][256][ldvt] -> ctx fp32 [B*S][H*256] */
 int e2c_attention(const void *q, const void *k, const void *vt, int ldvt, const uint8_t *valid,

@@ -4,7 +4,8 @@
 //   token gather: bf16 table row * embed_scale      e2_embed_token, src/text.c:917-921
 //     -> x (the residual stream), quantise(x) for the PLE projection, and
 //        quantise(rmsnorm(x) * input_ln[0]) for layer 0's q|k|v        src/text.c:929,944
-//   PLE: ple * ple_scale, RMSNorm of each 512 slice with ple_proj_norm   src/text.c:930-931
+//   PLE gate: h = gelu_tanh(gate) * rmsnorm(ple slice * ple_scale) * ple_proj_norm, quantised: the
+//     per-layer input's scale and norm (src/text.c:930-931) applied where each slice is read
 //   q|k|v: per-head RMSNorm (q_norm, k_norm; v without a scale), RoPE on q and k, bf16 Q, K, V^T
 //     for head dims 256 and 512 and any number of KV heads                src/text.c:842-857
 //   x = (rmsnorm(t) * g1 + res) * layer_scalar, stored as the residual, then quantise either
@@ -66,27 +67,6 @@ __global__ void __launch_bounds__(256) k_tt_embed(const int32_t *__restrict__ id
 #pragma unroll
     for (int i = 0; i < NV; i++) x[i] = norm4(x[i], inv, __ldg(g4 + lane + 32 * i));
     quantize_row(x, ablk, D, qn + (size_t)row * D, qns + (size_t)row * nb, lane);
-}
-
-// one warp per (row, slice of P = 128 NV): v = p * scale, then v * inv(v) * gamma, in place
-template <int NV>
-__global__ void __launch_bounds__(256) k_tt_ple_norm(float *__restrict__ ple, int ld, int nslices, float scale,
-                                                     const float *__restrict__ gamma, float eps, int M) {
-    griddep_launch_dependents();
-    griddep_wait();
-    const long w = ((long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    const int lane = threadIdx.x & 31;
-    if (w >= (long)M * nslices) return;
-    const int row = (int)(w / nslices), sl = (int)(w - (long)row * nslices);
-    constexpr int P = NV * 128;
-    float4 *src = reinterpret_cast<float4 *>(ple + (size_t)row * ld + (size_t)sl * P);
-    float4 v[NV];
-#pragma unroll
-    for (int i = 0; i < NV; i++) v[i] = mul4(src[lane + 32 * i], scale);
-    const float inv = rms_inv(sumsq(v), P, eps);
-    const float4 *g4 = reinterpret_cast<const float4 *>(gamma);
-#pragma unroll
-    for (int i = 0; i < NV; i++) src[lane + 32 * i] = norm4(v[i], inv, __ldg(g4 + lane + 32 * i));
 }
 
 // q|k|v fp32 [M][ldy] laid out [H q heads | KV k heads | KV v heads] of D = 256 NVH. One CTA per
@@ -242,11 +222,13 @@ __global__ void __launch_bounds__(256) k_tt_norm_add(const float *__restrict__ t
     quantize_row(v, ablk, D, q + (size_t)row * D, qs + (size_t)row * (D / ablk), lane);
 }
 
-// h = gelu_tanh(g) * u (u's rows ldu apart: the PLE slice of this layer), quantised per row
+// h = gelu_tanh(g) * u (u's rows ldu apart: the PLE slice of this layer), quantised per row. With
+// ugamma given, u is first taken as rmsnorm(u * uscale) * ugamma over its I values: the PLE slice's
+// scale and norm, the arithmetic of a separate pass over the slice (u * scale, then x * inv * gamma).
 template <int NV>
 __global__ void __launch_bounds__(256) k_tt_gate_quant(const float *__restrict__ g, int ldg, const float *__restrict__ u,
-                                                       int ldu, int8_t *__restrict__ q, float *__restrict__ qs, int M,
-                                                       int ablk) {
+                                                       int ldu, float uscale, const float *__restrict__ ugamma, float eps,
+                                                       int8_t *__restrict__ q, float *__restrict__ qs, int M, int ablk) {
     griddep_launch_dependents();
     griddep_wait();
     const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
@@ -254,12 +236,23 @@ __global__ void __launch_bounds__(256) k_tt_gate_quant(const float *__restrict__
     constexpr int I = NV * 128;
     const float4 *g4 = reinterpret_cast<const float4 *>(g + (size_t)row * ldg);
     const float4 *u4 = reinterpret_cast<const float4 *>(u + (size_t)row * ldu);
+    float4 b[NV];
+#pragma unroll
+    for (int i = 0; i < NV; i++) b[i] = u4[lane + 32 * i];
+    if (ugamma) {
+#pragma unroll
+        for (int i = 0; i < NV; i++) b[i] = mul4(b[i], uscale);
+        const float inv = rms_inv(sumsq(b), I, eps);
+        const float4 *gm4 = reinterpret_cast<const float4 *>(ugamma);
+#pragma unroll
+        for (int i = 0; i < NV; i++) b[i] = norm4(b[i], inv, __ldg(gm4 + lane + 32 * i));
+    }
     float4 h[NV];
 #pragma unroll
     for (int i = 0; i < NV; i++) {
-        const float4 a = g4[lane + 32 * i], b = u4[lane + 32 * i];
-        h[i] = make_float4(__fmul_rn(gelu_tanh(a.x), b.x), __fmul_rn(gelu_tanh(a.y), b.y), __fmul_rn(gelu_tanh(a.z), b.z),
-                           __fmul_rn(gelu_tanh(a.w), b.w));
+        const float4 a = g4[lane + 32 * i];
+        h[i] = make_float4(__fmul_rn(gelu_tanh(a.x), b[i].x), __fmul_rn(gelu_tanh(a.y), b[i].y),
+                           __fmul_rn(gelu_tanh(a.z), b[i].z), __fmul_rn(gelu_tanh(a.w), b[i].w));
     }
     quantize_row(h, ablk, I, q + (size_t)row * I, qs + (size_t)row * (I / ablk), lane);
 }
@@ -304,22 +297,6 @@ extern "C" int e2c_tt_embed(const int32_t *ids, const uint16_t *table, float emb
     return check("tt_embed");
 }
 
-extern "C" int e2c_tt_ple_norm(float *ple, int ld, int nslices, int P, float scale, const float *gamma, float eps, int M,
-                               void *stream) {
-    if (P % 128 || P > 1024 || ld % 4 || ld < nslices * P) {
-        e2c_set_msg("tt_ple_norm: slice %d must be a multiple of 128 up to 1024 (ld %d >= %d slices)", P, ld, nslices);
-        return -1;
-    }
-    if (M <= 0 || nslices <= 0) return 0;
-    const long warps = (long)M * nslices;
-    const dim3 grid((unsigned)((warps + 7) / 8)), block(256);
-    cudaStream_t st = (cudaStream_t)stream;
-    const int D = P;
-    E2C_TT_SWITCH(D / 128, (e2c_launch(k_tt_ple_norm<V>, grid, block, 0, st, ple, ld, nslices, scale, gamma, eps, M)),
-                  "tt_ple_norm");
-    return check("tt_ple_norm");
-}
-
 extern "C" int e2c_tt_qkv_post(const float *y, int ldy, int H, int KV, int D, const float *q_gamma, const float *k_gamma,
                                float eps, const float *rope_cos, const float *rope_sin, int ldrope, int rope_pos_major,
                                int seq_len, void *q_out,
@@ -358,8 +335,8 @@ extern "C" int e2c_tt_norm_add(const float *t, float *res, const float *g1, floa
     return check("tt_norm_add");
 }
 
-extern "C" int e2c_tt_gate_quant(const float *g, int ldg, const float *u, int ldu, int I, int8_t *q, float *qs, int M,
-                                 int ablk, void *stream) {
+extern "C" int e2c_tt_gate_quant(const float *g, int ldg, const float *u, int ldu, float uscale, const float *ugamma,
+                                 float eps, int I, int8_t *q, float *qs, int M, int ablk, void *stream) {
     if (I % 128 || I > 2048 || ldg % 4 || ldu % 4 || ldg < I || !ablk_ok(ablk, I)) {
         e2c_set_msg("tt_gate_quant: I=%d must be a multiple of 128 up to 2048 (ldg %d, ldu %d), ablk 128 or I", I, ldg, ldu);
         return -1;
@@ -368,7 +345,8 @@ extern "C" int e2c_tt_gate_quant(const float *g, int ldg, const float *u, int ld
     const dim3 grid((M + 7) / 8), block(256);
     cudaStream_t st = (cudaStream_t)stream;
     const int D = I;
-    E2C_TT_SWITCH(D / 128, (e2c_launch(k_tt_gate_quant<V>, grid, block, 0, st, g, ldg, u, ldu, q, qs, M, ablk)),
+    E2C_TT_SWITCH(D / 128, (e2c_launch(k_tt_gate_quant<V>, grid, block, 0, st, g, ldg, u, ldu, uscale, ugamma, eps, q, qs,
+                                       M, ablk)),
                   "tt_gate_quant");
     return check("tt_gate_quant");
 }

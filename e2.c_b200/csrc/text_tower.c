@@ -5,19 +5,20 @@
  * default build does; every GEMM writes fp32):
  *
  *   gather: x = bf16 table[id] * embed_scale; quantise(x); quantise(rmsnorm(x) * input_ln[0])
- *   PLE:    ple = GEMM(x) [M][L * P]; * ple_scale; RMSNorm per P slice (ple_proj_norm)
+ *   PLE:    ple = GEMM(x) [M][L * P] (its scale and per-slice RMSNorm with ple_proj_norm are applied
+ *           where layer l's PLE gate reads slice l)
  *   per layer l:
  *     GEMM q|k|v -> per-head RMSNorm + RoPE -> bf16 Q, K, V^T
  *     attention (sliding window or full, head dim 256 or 512) -> ctx; quantise(ctx)
  *     GEMM o_proj -> x = rmsnorm(.) * post_attn_ln + x; quantise(rmsnorm(x) * pre_ffn_ln)
  *     GEMM gate|up -> quantise(gelu_tanh(gate) * up)
  *     GEMM down -> x = rmsnorm(.) * post_ffn_ln + x; quantise(x)
- *     GEMM ple_gate -> quantise(gelu_tanh(.) * ple[:, l P .. +P])
+ *     GEMM ple_gate -> quantise(gelu_tanh(.) * rmsnorm(ple[:, l P .. +P] * ple_scale) * ple_proj_norm)
  *     GEMM ple_proj -> x = (rmsnorm(.) * ple_norm + x) * layer_scalar;
  *                      quantise(rmsnorm(x) * input_ln[l + 1]), after the last layer final_norm
  *   GEMM embed_proj -> masked mean pool -> L2
  *
- * 14 kernels per layer, 6 around them. int8 activations alternate between qa (inputs of the
+ * 14 kernels per layer, 5 around them. int8 activations alternate between qa (inputs of the
  * hidden-wide GEMMs) and qb (ctx, h and the PLE gate's output), so a row kernel never writes the
  * buffer the GEMM before it still reads.
  */
@@ -314,7 +315,6 @@ static int forward(e2cuda_text *t, int B, int S, int has_valid, cudaStream_t st)
                    t->V, t->status, st),
       "text embed");
     Q(gemm_f32(&t->ple_model, t->qp, t->qps, M, ab, t->ple, L * P, st), "text PLE projection");
-    Q(e2c_tt_ple_norm(t->ple, L * P, L, P, t->ple_scale, t->ple_norm, t->eps, M, st), "text PLE norm");
     for (int l = 0; l < L; l++) {
         const tt_layer *y = &t->layer[l];
         const int hd = y->hd, kv = y->kv, qd = y->qdim, ab_q = ab == 128 ? 128 : qd;
@@ -335,7 +335,9 @@ static int forward(e2cuda_text *t, int B, int S, int has_valid, cudaStream_t st)
         Q(e2c_tt_norm_add(t->tmp, t->res, lnorm(t, l, 3), 1.0f, NULL, t->eps, t->qa, t->qas, M, D, ab, st),
           "text post-ffn norm");
         Q(gemm_f32(&y->pg, t->qa, t->qas, M, ab, t->yf, P, st), "text PLE gate");
-        Q(e2c_tt_gate_quant(t->yf, P, t->ple + (size_t)l * P, L * P, P, t->qb, t->qbs, M, ab_p, st), "text PLE gate quant");
+        Q(e2c_tt_gate_quant(t->yf, P, t->ple + (size_t)l * P, L * P, t->ple_scale, t->ple_norm, t->eps, P, t->qb, t->qbs, M,
+                            ab_p, st),
+          "text PLE gate quant");
         Q(gemm_f32(&y->pp, t->qb, t->qbs, M, ab_p, t->tmp, D, st), "text PLE projection");
         Q(e2c_tt_norm_add(t->tmp, t->res, lnorm(t, l, 4), y->ls, l + 1 < L ? lnorm(t, l + 1, 0) : t->final_norm, t->eps,
                           t->qa, t->qas, M, D, ab, st),
