@@ -864,8 +864,12 @@ struct Plan {
 };
 
 Plan pick_plan(const e2c_gemm_args *a, int num_sms) {
-    if (a->ablk != a->K) return {128, 1};                    // per-block fold keeps BN/4 floats per thread
     const int ncols = a->n1 - a->n0;
+    if (a->ablk != a->K) {
+        // per-block fold: BN 128 (four 128-column accumulators); CTA pairs on the same rule
+        const long pairs128 = (long)((a->M + 2 * BM - 1) / (2 * BM)) * ((ncols + 127) / 128);
+        return {128, (pairs128 >= num_sms / 2 && a->M > 2 * BM) ? 2 : 1};
+    }
     const long pairs256 = (long)((a->M + 2 * BM - 1) / (2 * BM)) * ((ncols + 255) / 256);
     // pairs pay off once they fill the device (a full wave of 256-row tiles) and both CTAs of a
     // pair have rows of their own: with M <= 256 the second one would only multiply zeros
@@ -962,7 +966,9 @@ extern "C" int e2c_gemm(const e2c_gemm_args *a, void *stream) {
     g_last_kernel = pair ? "persistent_pair" : "persistent";
     switch (a->epi) {
     case E2C_EPI_F32:
-        if (perblock) return launch<128, 5, true, E2C_EPI_F32, 1>(a, st, dev, num_sms);
+        if (perblock)
+            return pair ? launch<128, 6, true, E2C_EPI_F32, 2>(a, st, dev, num_sms)
+                        : launch<128, 5, true, E2C_EPI_F32, 1>(a, st, dev, num_sms);
         if (pair)
             return pl.bn == 128   ? launch<128, 6, false, E2C_EPI_F32, 2>(a, st, dev, num_sms)
                    : pl.bn == 192 ? launch<192, 6, false, E2C_EPI_F32, 2>(a, st, dev, num_sms)
@@ -971,7 +977,9 @@ extern "C" int e2c_gemm(const e2c_gemm_args *a, void *stream) {
                : pl.bn == 192 ? launch<192, 3, false, E2C_EPI_F32, 1>(a, st, dev, num_sms)
                               : launch<256, 3, false, E2C_EPI_F32, 1>(a, st, dev, num_sms);
     case E2C_EPI_RESID:
-        if (perblock) return launch<128, 5, true, E2C_EPI_RESID, 1>(a, st, dev, num_sms);
+        if (perblock)
+            return pair ? launch<128, 6, true, E2C_EPI_RESID, 2>(a, st, dev, num_sms)
+                        : launch<128, 5, true, E2C_EPI_RESID, 1>(a, st, dev, num_sms);
         if (pair)
             return pl.bn == 128   ? launch<128, 6, false, E2C_EPI_RESID, 2>(a, st, dev, num_sms)
                    : pl.bn == 192 ? launch<192, 6, false, E2C_EPI_RESID, 2>(a, st, dev, num_sms)
@@ -980,7 +988,9 @@ extern "C" int e2c_gemm(const e2c_gemm_args *a, void *stream) {
                : pl.bn == 192 ? launch<192, 3, false, E2C_EPI_RESID, 1>(a, st, dev, num_sms)
                               : launch<256, 3, false, E2C_EPI_RESID, 1>(a, st, dev, num_sms);
     case E2C_EPI_I32:
-        if (perblock) return launch<128, 6, true, E2C_EPI_I32, 1>(a, st, dev, num_sms);
+        if (perblock)
+            return pair ? launch<128, 6, true, E2C_EPI_I32, 2>(a, st, dev, num_sms)
+                        : launch<128, 6, true, E2C_EPI_I32, 1>(a, st, dev, num_sms);
         if (pair)
             return pl.bn == 128   ? launch<128, 6, false, E2C_EPI_I32, 2>(a, st, dev, num_sms)
                    : pl.bn == 192 ? launch<192, 6, false, E2C_EPI_I32, 2>(a, st, dev, num_sms)

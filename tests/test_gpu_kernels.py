@@ -75,6 +75,8 @@ GEMM_CASES = [
     (8, 64, 512, 128), (130, 256, 1024, 128), (17, 48, 384, 128), (256, 384, 2048, 256),
     # large enough for CTA pairs (256-row tiles over two SMs): 192-, 128- and 256-column tiles
     (2048, 2560, 256, 256), (4096, 1152, 768, 768), (9472, 512, 256, 256),
+    # per-128-block scales on CTA pairs (M > 256, a wave of 256 x 128 pair tiles), incl. a ragged M
+    (4096, 1152, 768, 128), (5000, 2048, 512, 128),
 ]
 
 
