@@ -202,17 +202,28 @@ e2cuda_text *e2cuda_text_create(const e2cuda_text_desc *d, int max_tokens) {
     t->ple_scale = d->ple_scale;
     const int L = t->L, D = t->D, I = t->I, P = t->P;
     int qdim_max = 0, yw = 2 * I > P ? 2 * I : P;
+    /* the whole description is checked before any device work */
+    for (int l = 0; l < L; l++) {
+        const e2cuda_text_layer *x = &d->layers[l];
+        const int hd = x->head_dim, kv = x->n_kv_heads, qd = t->H * hd;
+        if ((hd != 256 && hd != 512) || kv <= 0 || t->H % kv || kv * hd > 512 || !q8w_is(x->q, qd, D) ||
+            !q8w_is(x->k, kv * hd, D) || !q8w_is(x->v, kv * hd, D) || !q8w_is(x->o, D, qd) || !q8w_is(x->gate, I, D) ||
+            !q8w_is(x->up, I, D) || !q8w_is(x->down, D, I) || !q8w_is(x->ple_gate, P, D) || !q8w_is(x->ple_proj, D, P) ||
+            !x->input_ln || !x->post_attn_ln || !x->pre_ffn_ln || !x->post_ffn_ln || !x->ple_norm || !x->q_norm ||
+            !x->k_norm) {
+            e2cu_err("text_create: layer %d: shapes do not match (head_dim 256 or 512, KV heads dividing %d heads, "
+                     "KV heads x head_dim <= 512)", l, t->H);
+            goto fail;
+        }
+    }
+    if (!q8w_is(d->ple_model_proj, L * P, D) || !q8w_is(d->embed_proj, t->DO, D)) {
+        e2cu_err("text_create: PLE projection or embed_proj shapes do not match");
+        goto fail;
+    }
     for (int l = 0; l < L; l++) {
         const e2cuda_text_layer *x = &d->layers[l];
         tt_layer *y = &t->layer[l];
         const int hd = x->head_dim, kv = x->n_kv_heads, qd = t->H * hd;
-        if ((hd != 256 && hd != 512) || kv <= 0 || t->H % kv || !q8w_is(x->q, qd, D) || !q8w_is(x->k, kv * hd, D) ||
-            !q8w_is(x->v, kv * hd, D) || !q8w_is(x->o, D, qd) || !q8w_is(x->gate, I, D) || !q8w_is(x->up, I, D) ||
-            !q8w_is(x->down, D, I) || !q8w_is(x->ple_gate, P, D) || !q8w_is(x->ple_proj, D, P) || !x->input_ln ||
-            !x->post_attn_ln || !x->pre_ffn_ln || !x->post_ffn_ln || !x->ple_norm || !x->q_norm || !x->k_norm) {
-            e2cu_err("text_create: layer %d: shapes do not match (head_dim 256 or 512, KV heads dividing %d heads)", l, t->H);
-            goto fail;
-        }
         y->hd = hd;
         y->kv = kv;
         y->qdim = qd;
@@ -250,10 +261,6 @@ e2cuda_text *e2cuda_text_create(const e2cuda_text_desc *d, int max_tokens) {
         const int rc = upload_floats(&y->norms, hn, nn, "norm upload");
         free(hn);
         if (rc) goto fail;
-    }
-    if (!q8w_is(d->ple_model_proj, L * P, D) || !q8w_is(d->embed_proj, t->DO, D)) {
-        e2cu_err("text_create: PLE projection or embed_proj shapes do not match");
-        goto fail;
     }
     if (e2cuda_w8_from_q8w(d->ple_model_proj, &t->ple_model) || e2cuda_w8_from_q8w(d->embed_proj, &t->embed_proj) ||
         upload_floats(&t->ple_norm, d->ple_proj_norm, (size_t)P, "norm upload") ||

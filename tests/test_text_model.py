@@ -85,3 +85,34 @@ def test_reference_text_tower_embeds(tm, ref_text):
     short = ref_text.embed_batch(ids[2:3, :40])
     cos = float(out[2] @ short[0])
     assert cos > 0.9999, cos
+
+
+def test_text_create_rejects_bad_descriptions(e2c, tm, text_tensors):
+    """Geometry is checked before any device work: a hidden size off the 128 grid, a layer whose
+    head dim is neither 256 nor 512, a projection whose shape disagrees with the description, and an
+    activation block other than 128 or hidden all fail with a message (no GPU needed)."""
+    w = tm.TextWeights(text_tensors)
+    lib = e2c.lib()
+
+    def create(d):
+        return lib.e2cuda_text_create(C.addressof(d), 1024)
+
+    d = w.desc()
+    d.hidden = 500
+    assert create(d) is None and "unsupported geometry" in e2c.last_error()
+    d = w.desc()
+    d.ablk = 64
+    assert create(d) is None and "ablk" in e2c.last_error()
+    d = w.desc()
+    saved = w.layers[3].head_dim
+    w.layers[3].head_dim = 384
+    try:
+        assert create(d) is None and "layer 3" in e2c.last_error()
+    finally:
+        w.layers[3].head_dim = saved
+    saved = w.layers[7].o
+    w.layers[7].o = w.layers[7].q  # q is [1024][512], o must be [512][1024]
+    try:
+        assert create(w.desc()) is None and "layer 7" in e2c.last_error()
+    finally:
+        w.layers[7].o = saved
