@@ -945,6 +945,13 @@ extern "C" int e2c_gemm(const e2c_gemm_args *a, void *stream) {
             g_last_kernel = "stream";
             return e2c_gemm_stream(a, stream);
         }
+        // Under programmatic dependent launch the short weights at a few tokens stream too, two
+        // CTAs per SM: the next launch's weight tiles are requested while this one finishes,
+        // which hides the fixed costs a chain of short launches pays one after another.
+        if (e2c_pdl_on() && a->M <= 32) {
+            g_last_kernel = "stream_coresident";
+            return e2c_gemm_stream(a, stream);
+        }
     }
     {
         // short activation matrices: when the persistent kernel would leave most SMs idle, split K

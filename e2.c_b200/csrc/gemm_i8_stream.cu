@@ -46,21 +46,26 @@ constexpr int BK = 128;  // K bytes per k-block (one 128-byte swizzle row)
 constexpr int NTHREADS = 192;
 constexpr int EPI_THREADS = 128;
 
-template <int MT>
+// CO = 1: a ring short enough (about 110 KB) for two CTAs per SM, so that under programmatic
+// dependent launch the next launch's CTAs are resident, and stream their first weight tiles, while
+// this launch finishes (short weights at a few tokens, where a launch's fixed costs exceed its
+// streaming time)
+template <int MT, int CO = 0>
 struct StreamSmem {
     static constexpr int W_BYTES = BW * BK;
     static constexpr int X_BYTES = MT * BK;
     static constexpr int STAGE = W_BYTES + X_BYTES;
     // deep rings (180-200 KB in flight per SM): a CTA's whole range of a 4-17 MB weight is requested
     // at once, and a long stream keeps enough bytes in flight to cover HBM latency
-    static constexpr int STAGES = MT <= 16 ? 10 : MT <= 32 ? 9 : MT <= 64 ? 8 : MT <= 128 ? 6 : 4;
+    static constexpr int STAGES = CO ? (MT <= 16 ? 6 : MT <= 32 ? 5 : 4)
+                                     : MT <= 16 ? 10 : MT <= 32 ? 9 : MT <= 64 ? 8 : MT <= 128 ? 6 : 4;
     static constexpr int BAR_OFF = STAGES * STAGE;
     static constexpr int NBAR = 2 * STAGES + 5;  // full[S], empty[S], tfull[2], tempty[2], mma_done
     static constexpr int SLOT_OFF = BAR_OFF + NBAR * 8;  // TMEM address, then the "last" flag
     static constexpr int BYTES = SLOT_OFF + 16;
     static constexpr int ALLOC = BYTES + 1024;  // slack for 1024-byte alignment
     static constexpr uint32_t TMEM_COLS = 2 * MT < 32 ? 32 : 2 * MT;
-    static_assert(ALLOC <= 232448, "shared memory");
+    static_assert(ALLOC <= (CO ? 232448 / 2 - 1024 : 232448), "shared memory");
     static_assert(STAGE % 1024 == 0, "stages stay 1024-byte aligned");
 };
 
@@ -84,11 +89,11 @@ __device__ __forceinline__ float fold(int acc, float as, float wsn, const e2c_ge
     return o;
 }
 
-template <int MT>
-__global__ void __launch_bounds__(NTHREADS, 1)
+template <int MT, int CO>
+__global__ void __launch_bounds__(NTHREADS, CO ? 2 : 1)
     k_gemm_stream(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
                   const e2c_gemm_args p) {
-    using L = StreamSmem<MT>;
+    using L = StreamSmem<MT, CO>;
     constexpr int ST = L::STAGES;
     extern __shared__ uint8_t smem_raw[];
     griddep_launch_dependents();
@@ -313,12 +318,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
 }
 
-template <int MT>
+template <int MT, int CO = 0>
 int launch_mt(const e2c_gemm_args *a, int G, cudaStream_t st, int dev) {
-    using L = StreamSmem<MT>;
+    using L = StreamSmem<MT, CO>;
     static E2cPerDev attr_set;
     if (!attr_set.get(dev)) {
-        if (cudaFuncSetAttribute(k_gemm_stream<MT>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC) != cudaSuccess) {
+        if (cudaFuncSetAttribute(k_gemm_stream<MT, CO>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC) != cudaSuccess) {
             cudaGetLastError();
             e2c_set_msg("gemm_stream: cannot reserve %d bytes of shared memory", L::ALLOC);
             return -2;
@@ -331,7 +336,7 @@ int launch_mt(const e2c_gemm_args *a, int G, cudaStream_t st, int dev) {
         e2c_tmap_2d(&tx, a->a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)a->K, (uint64_t)a->M, (uint64_t)a->lda, BK,
                     (uint32_t)MT))
         return -3;
-    const cudaError_t e = e2c_launch(k_gemm_stream<MT>, dim3((unsigned)G), dim3(NTHREADS), L::ALLOC, st, tw, tx, *a);
+    const cudaError_t e = e2c_launch(k_gemm_stream<MT, CO>, dim3((unsigned)G), dim3(NTHREADS), L::ALLOC, st, tw, tx, *a);
     if (e != cudaSuccess) {
         e2c_set_msg("gemm_stream launch: %s", cudaGetErrorString(e));
         return -2;
@@ -369,6 +374,10 @@ extern "C" int e2c_gemm_stream(const e2c_gemm_args *a, void *stream) {
     }
     const int G = e2c_gemm_stream_ctas(a, num_sms);
     cudaStream_t st = (cudaStream_t)stream;
+    // under programmatic dependent launch, short weights at a few tokens take the co-resident ring
+    const long long T = (long long)((a->n1 - a->n0 + BW - 1) / BW) * ((a->K + BK - 1) / BK);
+    if (e2c_pdl_on() && a->M <= 32 && T < 8LL * num_sms)
+        return a->M <= 16 ? launch_mt<16, 1>(a, G, st, dev) : launch_mt<32, 1>(a, G, st, dev);
     if (a->M <= 16) return launch_mt<16>(a, G, st, dev);
     if (a->M <= 32) return launch_mt<32>(a, G, st, dev);
     if (a->M <= 64) return launch_mt<64>(a, G, st, dev);
