@@ -717,7 +717,8 @@ def config1(args) -> int:
 
 def text_pass_work(B: int, S: int, cfg) -> list:
     """(kernel, int8 ops, bf16 flops, algorithmic bytes) of every launch of one text-tower pass over
-    B sequences of S tokens (activations per 128-block; every GEMM writes fp32)."""
+    B sequences of S tokens (activations per 128-block; every GEMM writes fp32 except gate|up, which
+    writes h quantised per 128-block)."""
     M, D, I, P, L, H, DO = B * S, cfg.hidden, cfg.intermediate, cfg.ple_dim, cfg.n_layers, cfg.n_heads, cfg.out_dim
 
     def gemm(name, K, N):
@@ -731,8 +732,9 @@ def text_pass_work(B: int, S: int, cfg) -> list:
         w += [gemm("qkv", D, nqkv), ("qkv_post", 0, 0, 4 * M * nqkv + 2 * M * nqkv),
               ("attention", 0, 4.0 * M * keys * hd * H, 2 * M * nqkv + 4 * M * qd),
               ("quantize_ctx", 0, 0, 4 * M * qd + M * qd + 4 * M * qd / 128), gemm("o_proj", qd, D),
-              ("norm_add", 0, 0, 13 * M * D + 4 * M * D / 128), gemm("gate_up", D, 2 * I),
-              ("gelu_quant", 0, 0, 8 * M * I + M * I + 4 * M * I / 128), gemm("down", I, D),
+              ("norm_add", 0, 0, 13 * M * D + 4 * M * D / 128),
+              ("gate_up_gelu_quant", 2.0 * M * D * 2 * I, 0.0,
+               M * D + 4 * M * D / 128 + 2 * I * D + 8 * I + M * I + 4 * M * I / 128), gemm("down", I, D),
               ("norm_add", 0, 0, 13 * M * D + 4 * M * D / 128), gemm("ple_gate", D, P),
               ("ple_gate_quant", 0, 0, 8 * M * P + M * P + 4 * M * P / 128), gemm("ple_proj", P, D),
               ("norm_add", 0, 0, 13 * M * D + 4 * M * D / 128)]
@@ -845,12 +847,14 @@ def text_tower(args) -> int:
 # one KV head of 256), the per-launch algorithmic work each is measured against, and the launches of
 # each per layer. Weights are quantised N(0, 0.02), activations per-token quantised N(0, 1).
 KERNELS = ("gate_up", "gate_up_q", "qkv", "o_proj", "down", "o_proj_norm", "down_norm", "attention", "quantize",
-           "quantize_ctx", "norm_add", "o_proj_pb", "down_pb", "attention_vision", "gemm_small")
+           "quantize_ctx", "norm_add", "o_proj_pb", "down_pb", "gate_up_pb", "gate_up_q_pb", "attention_vision",
+           "gemm_small")
 # gemm_small: the config-3 GEMM (K, N) = (2048, 8192) at M = --tokens rows (1..256) on the
 # weight-streaming kernel itself (e2c_gemm_stream), per-token scales, fp32 output
 # attention_vision: the vision tower's attention (e2.c src/vision.c:540-571), 2520 patches per image,
 # 12 heads of 64 with their own K and V, scale 1; M tokens = M // 2520 images
-# *_pb: the same GEMMs with per-128-block activation scales (the reference engine's own recipe)
+# *_pb: the same GEMMs with per-128-block activation scales (the reference engine's own recipe);
+# gate_up_pb writes g|u in fp32, gate_up_q_pb applies GELU-gate and h's per-block quantiser
 # the kernels an encoder layer runs (hidden 768, FFN 1152, per-token scales): the residual norms fused
 # into o_proj and down and h's quantiser into gate|up, or with E2C_FUSED_NORM=0 / E2C_FUSED_GELU=0
 # the row kernels after them
@@ -861,16 +865,22 @@ if os.environ.get("E2C_FUSED_GELU") == "0":
     LAYER_KERNELS = tuple(k for k in LAYER_KERNELS if k != "gate_up_q") + ("gate_up", "quantize")
 
 
+GEMM_KERNELS = ("gate_up", "gate_up_q", "qkv", "o_proj", "down", "o_proj_norm", "down_norm", "o_proj_pb", "down_pb",
+                "gate_up_pb", "gate_up_q_pb")
+
+
 def kernel_work(name: str, M: int) -> dict:
     D, I, H, Dh = 768, 1152, 3, 256
-    if name in ("gate_up", "gate_up_q", "qkv", "o_proj", "down", "o_proj_norm", "down_norm", "o_proj_pb", "down_pb"):
+    if name in GEMM_KERNELS:
         N, K = {"gate_up": (2 * I, D), "gate_up_q": (2 * I, D), "qkv": ((H + 2) * Dh, D), "o_proj": (D, D),
-                "down": (D, I), "o_proj_norm": (D, D), "down_norm": (D, I), "o_proj_pb": (D, D), "down_pb": (D, I)}[name]
+                "down": (D, I), "o_proj_norm": (D, D), "down_norm": (D, I), "o_proj_pb": (D, D), "down_pb": (D, I),
+                "gate_up_pb": (2 * I, D), "gate_up_q_pb": (2 * I, D)}[name]
         # the fused norm epilogue reads and writes the fp32 residual and writes int8 rows + scales;
         # the fused GELU-quantise epilogue writes int8 h + scales
         out_bytes = {"gate_up": 4 * M * I, "gate_up_q": M * I + 4 * M, "qkv": 2 * M * N, "o_proj": 4 * M * D,
                      "down": 4 * M * D, "o_proj_norm": 8 * M * D + M * D + 4 * M,
-                     "down_norm": 8 * M * D + M * D + 4 * M, "o_proj_pb": 4 * M * D, "down_pb": 4 * M * D}[name]
+                     "down_norm": 8 * M * D + M * D + 4 * M, "o_proj_pb": 4 * M * D, "down_pb": 4 * M * D,
+                     "gate_up_pb": 8 * M * I, "gate_up_q_pb": M * I + 4 * M * (I // 128)}[name]
         a_scales = 4 * M * (K // 128) if name.endswith("_pb") else 4 * M
         return {"ops": 2.0 * M * N * K, "bytes": M * K + a_scales + N * K + 4 * N + out_bytes, "per_layer": 1}
     if name == "attention":
@@ -906,9 +916,10 @@ def kernel_runner(name: str, M: int, dev, stream):
         return e2c.quantize_rows(torch.randn((M, K), device=dev, generator=g), K)
 
     keep = []
-    if name in ("gate_up", "gate_up_q", "qkv", "o_proj", "down", "o_proj_norm", "down_norm", "o_proj_pb", "down_pb"):
+    if name in GEMM_KERNELS:
         N, K = {"gate_up": (2 * I, D), "gate_up_q": (2 * I, D), "qkv": ((H + 2) * Dh, D), "o_proj": (D, D),
-                "down": (D, I), "o_proj_norm": (D, D), "down_norm": (D, I), "o_proj_pb": (D, D), "down_pb": (D, I)}[name]
+                "down": (D, I), "o_proj_norm": (D, D), "down_norm": (D, I), "o_proj_pb": (D, D), "down_pb": (D, I),
+                "gate_up_pb": (2 * I, D), "gate_up_q_pb": (2 * I, D)}[name]
         wq, ws = syn.quantize_weight_rows((rng.standard_normal((N, K)) * 0.02).astype(np.float32))
         W = e2c.Weight(w=wq, scale=ws)
         pb = name.endswith("_pb")
@@ -921,11 +932,15 @@ def kernel_runner(name: str, M: int, dev, stream):
             y = torch.empty((M, I), dtype=torch.float32, device=dev)
             a.epi, a.y, a.ldy = e2c.EPI_GELU, y.data_ptr(), I
             keep.append(y)
-        elif name == "gate_up_q":
+        elif name in ("gate_up_q", "gate_up_q_pb"):
             q8 = torch.empty((M, I), dtype=torch.int8, device=dev)
-            q8s = torch.empty((M,), dtype=torch.float32, device=dev)
+            q8s = torch.empty((M, I // 128 if pb else 1), dtype=torch.float32, device=dev)
             a.epi, a.q8, a.ldq, a.q8_scale = e2c.EPI_GELUQ, q8.data_ptr(), I, q8s.data_ptr()
             keep += [q8, q8s]
+        elif name == "gate_up_pb":
+            y = torch.empty((M, 2 * I), dtype=torch.float32, device=dev)
+            a.epi, a.y, a.ldy = e2c.EPI_F32, y.data_ptr(), 2 * I
+            keep.append(y)
         elif name in ("down", "o_proj", "down_pb", "o_proj_pb"):
             y = torch.empty((M, D), dtype=torch.float32, device=dev)
             a.epi, a.y, a.ldy = e2c.EPI_F32, y.data_ptr(), D

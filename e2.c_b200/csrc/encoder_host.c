@@ -262,8 +262,9 @@ e2cuda_encoder *e2cuda_encoder_create(const e2cuda_encoder_desc *d, int max_toke
             DALLOC(e->pq, MB * (size_t)(e->DH > D ? e->DH : D)) ||
             DALLOC(e->ps, sizeof(float) * MB * (size_t)((e->DH > D ? e->DH : D) / 128 + 1)))
             goto fail;
-        /* per-128-block activation scales: the QKV and GELU epilogues need whole-row (per-token)
-         * scales, so those GEMMs write fp32 and row kernels finish them */
+        /* per-128-block activation scales: the QKV epilogue needs whole-row (per-token) scales, so
+         * that GEMM writes fp32 and a row kernel finishes it; the gate|up fp32 buffer serves the
+         * two-kernel path (E2C_FUSED_GELU=0) */
         if (e->ablk != D && (DALLOC(e->qkvf, sizeof(float) * M * (size_t)(GD + 2 * e->Dh)) ||
                              DALLOC(e->guf, sizeof(float) * M * (size_t)(2 * e->I))))
             goto fail;
@@ -274,12 +275,13 @@ e2cuda_encoder *e2cuda_encoder_create(const e2cuda_encoder_desc *d, int max_toke
     {
         const char *fz = getenv("E2C_FUSED_NORM");
         e->fused_norm = !(fz && fz[0] == '0') && e->ablk == D && D % 128 == 0 && D / 128 <= 8;
-        /* gate|up runs with GELU-gate and h's per-token quantiser in its epilogue (h never stored)
-         * where the device holds a cluster of I / 128 CTAs; E2C_FUSED_GELU=0 selects the GELU
-         * epilogue + quantiser kernel pair instead */
+        /* gate|up runs with GELU-gate and h's quantiser in its epilogue (h never stored): per token
+         * where the device holds a cluster of I / 128 CTAs, per 128-block in the per-block GEMM;
+         * E2C_FUSED_GELU=0 selects the two-kernel paths instead */
         const char *fg = getenv("E2C_FUSED_GELU");
-        e->fused_gelu = !(fg && fg[0] == '0') && e->ablk == D && e->I % 128 == 0 && e->I / 128 <= 16 &&
-                        e2c_gemm_gelu_quant_supported(e->I / 128);
+        e->fused_gelu = !(fg && fg[0] == '0') && e->I % 128 == 0 &&
+                        (e->ablk == D ? e->I / 128 <= 16 && e2c_gemm_gelu_quant_supported(e->I / 128)
+                                      : e->ablk == 128);
     }
     /* the head's GEMMs have one row per sequence: up to 256 of them run on the weight-streaming
      * kernel, whose workspace starts zeroed and is left zeroed by every launch that completes */

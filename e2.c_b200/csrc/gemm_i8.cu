@@ -53,20 +53,26 @@ struct GemmSmem {
     // staging tiles per epilogue warp: QKV stages the two halves of a head; the other epilogues
     // without the per-block fold alternate between two, so a store overlaps the next chunk's math
     static constexpr int STG_BUFS = (EPI == E2C_EPI_QKV || (!PERBLOCK && EPI != E2C_EPI_I32 && CG == 1)) ? 2 : 1;
-    static constexpr int STG_PER_WARP = STG_BUFS * STG_WARP;
+    // (the per-block GELU-quantise epilogue stores its int8 rows from registers)
+    static constexpr int STG_PER_WARP = EPI == E2C_EPI_GELUQ ? 0 : STG_BUFS * STG_WARP;
     static constexpr int STG_OFF = STAGES * STAGE_BYTES;
     // per-warp column constants (weight scales, norm gains): 128 floats (QKV: 256, 64 pairs a warp;
-    // per-block mode: the 32 weight scales of the warp)
-    static constexpr int CST_FLOATS = EPI == E2C_EPI_QKV ? 256 : PERBLOCK ? 32 : 128;
+    // per-block mode: the 32 weight scales of the warp; per-block GELU-quantise: its 16 gate and 16
+    // up weight scales of each of the two sub-tiles)
+    static constexpr int CST_FLOATS = EPI == E2C_EPI_QKV ? 256 : EPI == E2C_EPI_GELUQ ? 64 : PERBLOCK ? 32 : 128;
     static constexpr int CST_OFF = STG_OFF + EPI_WARPS * STG_PER_WARP;
     static constexpr int CST_BYTES = EPI == E2C_EPI_I32 ? 0 : EPI_WARPS * CST_FLOATS * 4;
     static constexpr int SSQ_OFF = CST_OFF + CST_BYTES;
-    static constexpr int SSQ_BYTES = EPI == E2C_EPI_QKV ? 2 * 2 * BM * 4 : 0;  // [group][part2][row]
+    // QKV: [group][part2][row] row sums of squares; per-block GELU-quantise: [tile parity][part][row]
+    // row maxima of |h|
+    static constexpr int SSQ_BYTES = EPI == E2C_EPI_QKV ? 2 * 2 * BM * 4 : EPI == E2C_EPI_GELUQ ? 2 * 4 * BM * 4 : 0;
     static constexpr int BAR_OFF = SSQ_OFF + SSQ_BYTES;
     // TMEM accumulators: per-block mode keeps four (the tensor core runs up to three 128-deep blocks
-    // ahead of the drain), the others two
-    static constexpr int NACC = PERBLOCK ? 4 : 2;
-    // full[S], empty[S], tfull[NACC], tempty[NACC], pair[2][4] (QKV row-norm exchange), tmem slot
+    // ahead of the drain; the GELU-quantise epilogue three, its columns 384.. holding the first
+    // sub-tile's h), the others two
+    static constexpr int NACC = EPI == E2C_EPI_GELUQ ? 3 : PERBLOCK ? 4 : 2;
+    // full[S], empty[S], tfull[NACC], tempty[NACC], pair[2][4] (the QKV row-norm and per-block
+    // GELU-quantise row-maximum exchanges), tmem slot
     static constexpr int NBAR = 2 * STAGES + 2 * NACC + 8;
     static constexpr int BYTES = BAR_OFF + NBAR * 8 + 16;
     static constexpr int ALLOC = BYTES + 1024;  // slack for 1024-byte alignment
@@ -121,9 +127,15 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     const uint32_t rank = CG == 2 ? cluster_ctarank() : 0u;
     const int tfirst = CG == 2 ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
     const int tstride = CG == 2 ? (int)(gridDim.x >> 1) : (int)gridDim.x;
-    const int tiles_m = (M + BM * CG - 1) / (BM * CG), tiles_n = (ncols + BN - 1) / BN;
+    // Per-block GELU-quantise: a tile is 256 weight rows (128 gate + 128 up = one 128-column block
+    // of h) taken as two sub-tiles of 128 columns, each the gate and up rows of 64 h columns.
+    constexpr bool GQ = EPI == E2C_EPI_GELUQ;
+    constexpr int NSUB = GQ ? 2 : 1;
+    constexpr int TW = BN * NSUB;                        // weight rows per tile
+    static_assert(!GQ || (PERBLOCK && BN == 128), "the GELU-quantise epilogue here is the per-block one");
+    const int tiles_m = (M + BM * CG - 1) / (BM * CG), tiles_n = (ncols + TW - 1) / TW;
     const int ntiles = tiles_m * tiles_n;
-    const int nk = (K + BK - 1) / BK;                    // stages per tile
+    const int nk = (K + BK - 1) / BK;                    // stages per (sub-)tile
     const int kpu = PERBLOCK ? p.ablk / BK : nk;         // stages per accumulation unit
     const int nunits = PERBLOCK ? K / p.ablk : 1;
     const int nb = K / p.ablk;                           // scale blocks per row
@@ -140,8 +152,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             // one arrival per epilogue warp of the pair (QKV: per warp of the group that owns it)
             mbar_init(tempty_bar(a), (EPI == E2C_EPI_QKV ? EPI_WARPS / 2 : EPI_WARPS) * CG);
         }
+        // QKV: the quadrant's 2 warps of a group; GELU-quantise: the quadrant's 4 warps
         for (int a = 0; a < 2; a++)
-            for (int q = 0; q < 4; q++) mbar_init(pair_bar(a, q), 64);  // QKV: the quadrant's 2 warps of a group
+            for (int q = 0; q < 4; q++) mbar_init(pair_bar(a, q), GQ ? 128 : 64);
         fence_mbar_init();
         tma_prefetch_desc(&tmA);
         tma_prefetch_desc(&tmB);
@@ -181,8 +194,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             int issued = 0;  // loads in flight that nobody consumed (drained on failure)
             bool ok = true;
             for (int t = tfirst; t < ntiles && ok; t += tstride) {
-                const int m0 = (t / tiles_n) * (BM * CG) + (int)rank * BM, c0 = p.n0 + (t % tiles_n) * BN;
-                for (int kb = 0; kb < nk; kb++) {
+                const int m0 = (t / tiles_n) * (BM * CG) + (int)rank * BM, c0 = p.n0 + (t % tiles_n) * TW;
+                for (int kb2 = 0; kb2 < NSUB * nk; kb2++) {
+                    const int kb = GQ ? kb2 % nk : kb2, sub = GQ ? kb2 / nk : 0;
                     if (!mbar_wait(empty_bar(stage), phase ^ 1u, p.status, E2C_ERR_WAIT_PRODUCER)) {
                         ok = false;
                         break;
@@ -193,11 +207,19 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                         const uint32_t fb = mapa_shared(full_bar(stage), 0);
                         if (rank == 0) mbar_arrive_expect_tx(full_bar(stage), 2 * L::STAGE_BYTES);
                         tma_load_2d_pair(sa, &tmA, kb * BK, m0, fb);
-                        tma_load_2d_pair(sb, &tmB, kb * BK, c0 + (int)rank * (BN / 2), fb);
+                        // GELU-quantise: the first CTA holds the sub-tile's 64 gate rows, the second
+                        // its 64 up rows
+                        tma_load_2d_pair(sb, &tmB, kb * BK, GQ ? c0 + 128 * (int)rank + 64 * sub : c0 + (int)rank * (BN / 2), fb);
                     } else {
                         mbar_arrive_expect_tx(full_bar(stage), L::STAGE_BYTES);
                         tma_load_2d(sa, &tmA, kb * BK, m0, full_bar(stage));
-                        tma_load_2d(sb, &tmB, kb * BK, c0, full_bar(stage));
+                        if constexpr (GQ) {
+                            // 64 gate rows, then their 64 up rows (boxes of 64 rows)
+                            tma_load_2d(sb, &tmB, kb * BK, c0 + 64 * sub, full_bar(stage));
+                            tma_load_2d(sb + 64 * BK, &tmB, kb * BK, c0 + 128 + 64 * sub, full_bar(stage));
+                        } else {
+                            tma_load_2d(sb, &tmB, kb * BK, c0, full_bar(stage));
+                        }
                     }
                     issued++;
                     if (++stage == STAGES) {
@@ -238,7 +260,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             uint32_t acc_phase = 0;
             bool ok = true;
             for (int t = tfirst; t < ntiles && ok; t += tstride) {
-                for (int u = 0; u < nunits && ok; u++) {
+                for (int u = 0; u < NSUB * nunits && ok; u++) {
                     if (!mbar_wait(tempty_bar(acc), acc_phase ^ 1u, p.status, E2C_ERR_WAIT_MMA)) {
                         ok = false;
                         break;
@@ -324,7 +346,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         auto fetch = [&](int t) -> Pre {
             Pre r{0.f, 0.f, 1.f, 1.f, 0.f};
             if (PERBLOCK || t >= ntiles) return r;
-            const int m = (t / tiles_n) * (BM * CG) + (int)rank * BM + row, c0 = p.n0 + (t % tiles_n) * BN;
+            const int m = (t / tiles_n) * (BM * CG) + (int)rank * BM + row, c0 = p.n0 + (t % tiles_n) * TW;
             if (m < M) r.as = __ldg(p.a_scale + (size_t)m * nb);
             if constexpr (EPI == E2C_EPI_F32 || EPI == E2C_EPI_RESID) {
                 const int cw = c0 + part * QCOLS;
@@ -381,7 +403,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 const uint32_t aph = (uint32_t)(j & 1);
                 const int mt = (t / tiles_n) * (BM * CG) + (int)rank * BM;
                 const int m = mt + row;
-                const int c0 = p.n0 + (t % tiles_n) * BN;
+                const int c0 = p.n0 + (t % tiles_n) * TW;
                 const bool mrow = m < M;
                 const int y0 = mt + q * 32;
                 const int head = (c0 - p.n0) / 256;
@@ -562,14 +584,126 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             }
         } else {
             Pre pre = fetch(tfirst);
-            for (int t = tfirst; t < ntiles && ok; t += tstride) {
+            int jt = 0;  // tiles this CTA finished (GELU-quantise: the row-maximum slot and phase)
+            for (int t = tfirst; t < ntiles && ok; t += tstride, jt++) {
                 const int mt = (t / tiles_n) * (BM * CG) + (int)rank * BM;
                 const int m = mt + row;
-                const int c0 = p.n0 + (t % tiles_n) * BN;
+                const int c0 = p.n0 + (t % tiles_n) * TW;
                 const bool mrow = m < M;
                 const int y0 = mt + q * 32;  // first row of this warp's 32
                 const int cw = c0 + part * QCOLS;  // first column of this warp (F32 / I32 / per-block)
-                if constexpr (PERBLOCK) {
+                if constexpr (GQ) {
+                    // Sub-tile s holds h columns [64 s, 64 s + 64) of the tile's block of 128: TMEM
+                    // columns 0..63 their gate rows, 64..127 their up rows. This warp folds h columns
+                    // 16 part .. 16 part + 15 of each sub-tile, g and u as the F32 epilogue does
+                    // (f = fma(float(dot), as * ws, f) per 128-deep block, then the clamp), then
+                    // h = gelu(g) * u; the block's quantiser follows the row maximum over the
+                    // quadrant's four warps.
+                    const int hb = (c0 - p.n0) / TW;  // the tile's block of 128 h columns
+                    __syncwarp();  // every lane is done with the previous tile's weight scales
+                    {
+                        const int s = lane >> 4, j = lane & 15;
+                        cst[32 * s + j] = __ldg(p.w_scale + c0 + 64 * s + 16 * part + j);
+                        cst[32 * s + 16 + j] = __ldg(p.w_scale + c0 + 128 + 64 * s + 16 * part + j);
+                    }
+                    __syncwarp();
+                    // h of the first sub-tile waits in TMEM columns 384 + 16 part .. (registers hold
+                    // the second's)
+                    const uint32_t park = tmem_base + lane_addr + (uint32_t)(3 * BN + 16 * part);
+                    float hv[16];
+#pragma unroll 1
+                    for (int s = 0; s < 2; s++) {
+                        float f[32];
+#pragma unroll
+                        for (int j = 0; j < 32; j++) f[j] = 0.f;
+                        float as_next = mrow ? __ldg(p.a_scale + (size_t)m * nb) : 0.f;
+                        for (int u = 0; u < nunits; u++) {
+                            const float as = as_next;
+                            if (u + 1 < nunits) as_next = mrow ? __ldg(p.a_scale + (size_t)m * nb + u + 1) : 0.f;
+                            if (!__all_sync(0xffffffffu, mbar_wait(tfull_bar(acc), acc_phase, p.status, E2C_ERR_WAIT_EPI))) {
+                                ok = false;
+                                break;
+                            }
+                            tc_fence_after();
+                            const uint32_t ta = tmem_base + lane_addr + (uint32_t)(acc * BN + 16 * part);
+                            const float2 as2 = make_float2(as, as);
+                            // the gate columns, then the up columns (16 loaded values live at a time)
+#pragma unroll
+                            for (int gu = 0; gu < 2; gu++) {
+                                uint32_t r[16];
+                                tmem_ld16(ta + 64 * gu, r);
+                                tmem_wait_ld();
+                                if (gu == 1) release_acc(acc);
+#pragma unroll
+                                for (int j4 = 0; j4 < 4; j4++) {
+                                    const float4 w4 = *reinterpret_cast<const float4 *>(cst + 32 * s + 16 * gu + 4 * j4);
+#pragma unroll
+                                    for (int h = 0; h < 2; h++) {
+                                        const int j = 4 * j4 + 2 * h, jf = 16 * gu + j;
+                                        const float2 s2 = mul2_rn(as2, h ? make_float2(w4.z, w4.w) : make_float2(w4.x, w4.y));
+                                        const float2 d2 = make_float2(__int2float_rn((int)r[j]), __int2float_rn((int)r[j + 1]));
+                                        const float2 o = fma2_rn(d2, s2, make_float2(f[jf], f[jf + 1]));
+                                        f[jf] = o.x;
+                                        f[jf + 1] = o.y;
+                                    }
+                                }
+                            }
+                            if (++acc == NACC) {
+                                acc = 0;
+                                acc_phase ^= 1u;
+                            }
+                        }
+                        if (!ok) break;
+#pragma unroll
+                        for (int j = 0; j < 16; j += 2) {
+                            const float2 g = make_float2(fminf(fmaxf(f[j], p.out_min), p.out_max),
+                                                         fminf(fmaxf(f[j + 1], p.out_min), p.out_max));
+                            const float2 u = make_float2(fminf(fmaxf(f[16 + j], p.out_min), p.out_max),
+                                                         fminf(fmaxf(f[17 + j], p.out_min), p.out_max));
+                            const float2 h = mul2_rn(gelu_tanh2(g), u);
+                            hv[j] = h.x;
+                            hv[j + 1] = h.y;
+                        }
+                        if (s == 0) tmem_st16(park, reinterpret_cast<const uint32_t (&)[16]>(hv));
+                    }
+                    if (!ok) break;
+                    float h0[16];
+                    tmem_wait_st();
+                    tmem_ld16(park, reinterpret_cast<uint32_t (&)[16]>(h0));
+                    tmem_wait_ld();
+                    // the row's max |h| over the block: this warp's 32 columns, then the quadrant's
+                    // four warps through shared memory (two slots, alternating by tile)
+                    float am = 0.f;
+#pragma unroll
+                    for (int j = 0; j < 16; j++) am = fmaxf(am, fmaxf(fabsf(h0[j]), fabsf(hv[j])));
+                    float *xm = reinterpret_cast<float *>(smem + L::SSQ_OFF) + (jt & 1) * 4 * BM;
+                    xm[part * BM + row] = am;
+                    mbar_arrive(pair_bar(0, q));
+                    if (!__all_sync(0xffffffffu, mbar_wait(pair_bar(0, q), (uint32_t)(jt & 1), p.status, E2C_ERR_WAIT_EPI))) {
+                        ok = false;
+                        break;
+                    }
+                    am = fmaxf(fmaxf(xm[row], xm[BM + row]), fmaxf(xm[2 * BM + row], xm[3 * BM + row]));
+                    // the reference quantiser: scale = amax fl(1/127), q = rint(h fl(127 / amax)) (|q| <= 127
+                    // without a clamp: h fl(127 / amax) <= 127 (1 + 2^-24))
+                    const float inv = am > 0.f ? __fdiv_rn(127.0f, am) : 1.0f;
+                    if (mrow) {
+                        int8_t *qr = p.q8 + (size_t)m * p.ldq + 128 * hb + 16 * part;
+#pragma unroll
+                        for (int s = 0; s < 2; s++) {
+                            const float *hs = s ? hv : h0;
+                            uint32_t w[4];
+#pragma unroll
+                            for (int k = 0; k < 4; k++)
+                                w[k] = pack_low_bytes(rint_low_byte(__fmul_rn(hs[4 * k], inv)),
+                                                      rint_low_byte(__fmul_rn(hs[4 * k + 1], inv)),
+                                                      rint_low_byte(__fmul_rn(hs[4 * k + 2], inv)),
+                                                      rint_low_byte(__fmul_rn(hs[4 * k + 3], inv)));
+                            *reinterpret_cast<uint4 *>(qr + 64 * s) = make_uint4(w[0], w[1], w[2], w[3]);
+                        }
+                        if (part == 0) p.q8_scale[(size_t)m * tiles_n + hb] = am > 0.f ? __fmul_rn(am, 0x1.020408p-7f) : 1.0f;
+                    }
+                } else if constexpr (PERBLOCK) {
                     float f[QCOLS];
     #pragma unroll
                     for (int j = 0; j < QCOLS; j++) f[j] = 0.f;
@@ -782,7 +916,7 @@ int launch(const e2c_gemm_args *a, cudaStream_t st, int dev, int num_sms) {
     if (e2c_tmap_2d(&ta, a->a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)a->K, (uint64_t)a->M, (uint64_t)a->lda,
                     BK, BM) ||
         e2c_tmap_2d(&tb, a->w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)a->K, (uint64_t)a->wrows,
-                    (uint64_t)a->ldw, BK, BN / CG))
+                    (uint64_t)a->ldw, BK, EPI == E2C_EPI_GELUQ ? 64 : BN / CG))
         return -3;
     memset(&t0, 0, sizeof t0);
     memset(&t1, 0, sizeof t1);
@@ -804,7 +938,8 @@ int launch(const e2c_gemm_args *a, cudaStream_t st, int dev, int num_sms) {
                                         (uint64_t)a->M, (uint64_t)512 * a->nq, 32, 32) &&
                       !e2c_tmap_2d_sw64(&t1, a->k_out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 256, (uint64_t)a->M, 512, 32, 32);
     }
-    const int tiles = ((a->M + BM * CG - 1) / (BM * CG)) * ((a->n1 - a->n0 + BN - 1) / BN);
+    constexpr int TW = EPI == E2C_EPI_GELUQ ? 2 * BN : BN;  // weight rows per tile
+    const int tiles = ((a->M + BM * CG - 1) / (BM * CG)) * ((a->n1 - a->n0 + TW - 1) / TW);
     cudaError_t e;
     if constexpr (CG == 1) {
         const int grid = tiles < num_sms ? tiles : num_sms;
@@ -866,8 +1001,10 @@ struct Plan {
 Plan pick_plan(const e2c_gemm_args *a, int num_sms) {
     const int ncols = a->n1 - a->n0;
     if (a->ablk != a->K) {
-        // per-block fold: BN 128 (four 128-column accumulators); CTA pairs on the same rule
-        const long pairs128 = (long)((a->M + 2 * BM - 1) / (2 * BM)) * ((ncols + 127) / 128);
+        // per-block fold: BN 128 (four 128-column accumulators); CTA pairs on the same rule (the
+        // GELU-quantise epilogue's tiles are 256 weight rows)
+        const int tw = a->epi == E2C_EPI_GELUQ ? 256 : 128;
+        const long pairs128 = (long)((a->M + 2 * BM - 1) / (2 * BM)) * ((ncols + tw - 1) / tw);
         return {128, (pairs128 >= num_sms / 2 && a->M > 2 * BM) ? 2 : 1};
     }
     const long pairs256 = (long)((a->M + 2 * BM - 1) / (2 * BM)) * ((ncols + 255) / 256);
@@ -1034,9 +1171,21 @@ extern "C" int e2c_gemm(const e2c_gemm_args *a, void *stream) {
         return e2c_gemm_norm(a, stream);
     }
     case E2C_EPI_GELUQ: {
-        // GELU-gate and the per-token quantiser of h in the epilogue: its own kernel (gemm_i8_gelu.cu)
         const int ncols = a->n1 - a->n0;
-        if (perblock || a->n0 != 0 || ncols % 256 || ncols / 256 > 16 || !a->q8 || !a->q8_scale || a->ldq % 16 ||
+        if (perblock) {
+            // GELU-gate and h's per-128-block quantiser in the per-block kernel's epilogue: each tile's
+            // 256 weight rows are one block of h
+            if (a->ablk != 128 || a->n0 != 0 || ncols % 256 || !a->q8 || !a->q8_scale || a->ldq % 16 ||
+                a->ldq < ncols / 2 || ((uintptr_t)a->q8 & 15)) {
+                e2c_set_msg("gemm: the per-block GELU-quantise epilogue needs 128-wide activation blocks, gate|up rows "
+                            "in groups of 256 from row 0 and 16-byte aligned int8 rows of ldq >= N/2 with their scales");
+                return -1;
+            }
+            return pair ? launch<128, 8, true, E2C_EPI_GELUQ, 2>(a, st, dev, num_sms)
+                        : launch<128, 6, true, E2C_EPI_GELUQ, 1>(a, st, dev, num_sms);
+        }
+        // GELU-gate and the per-token quantiser of h in the epilogue: its own kernel (gemm_i8_gelu.cu)
+        if ( a->n0 != 0 || ncols % 256 || ncols / 256 > 16 || !a->q8 || !a->q8_scale || a->ldq % 16 ||
             ((uintptr_t)a->q8 & 15)) {
             e2c_set_msg("gemm: the GELU-quantise epilogue needs per-row scales, gate|up rows in groups of 256 "
                         "(1..16) from row 0 and 16-byte aligned int8 rows with their scales");

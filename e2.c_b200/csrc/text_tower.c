@@ -18,7 +18,8 @@
  *                      quantise(rmsnorm(x) * input_ln[l + 1]), after the last layer final_norm
  *   GEMM embed_proj -> masked mean pool -> L2
  *
- * 14 kernels per layer, 5 around them. int8 activations alternate between qa (inputs of the
+ * 14 kernels per layer (13 when gate|up applies GELU-gate and h's per-block quantiser in its
+ * epilogue), 5 around them. int8 activations alternate between qa (inputs of the
  * hidden-wide GEMMs) and qb (ctx, h and the PLE gate's output), so a row kernel never writes the
  * buffer the GEMM before it still reads.
  */
@@ -48,6 +49,7 @@ typedef struct {
 
 struct e2cuda_text {
     int L, D, I, P, H, V, DO, max_seq, ablk, max_tokens;
+    int fused_gelu; /* per-block gate|up GEMM with GELU-gate + quantiser epilogue (E2C_FUSED_GELU=0: off) */
     float eps, embed_scale, ple_scale;
     tt_layer layer[TT_MAX_LAYERS];
     e2cuda_w8 ple_model, embed_proj;
@@ -196,6 +198,10 @@ e2cuda_text *e2cuda_text_create(const e2cuda_text_desc *d, int max_tokens) {
     t->DO = d->out_dim;
     t->max_seq = d->max_seq;
     t->ablk = ablk;
+    {
+        const char *fg = getenv("E2C_FUSED_GELU");
+        t->fused_gelu = ablk == 128 && !(fg && fg[0] == '0');
+    }
     t->max_tokens = max_tokens;
     t->eps = d->eps;
     t->embed_scale = d->embed_scale;
@@ -336,8 +342,18 @@ static int forward(e2cuda_text *t, int B, int S, int has_valid, cudaStream_t st)
         Q(gemm_f32(&y->o, t->qb, t->qbs, M, ab_q, t->tmp, D, st), "text o_proj");
         Q(e2c_tt_norm_add(t->tmp, t->res, lnorm(t, l, 1), 1.0f, lnorm(t, l, 2), t->eps, t->qa, t->qas, M, D, ab, st),
           "text post-attention norms");
-        Q(gemm_f32(&y->gu, t->qa, t->qas, M, ab, t->yf, 2 * I, st), "text gate|up");
-        Q(e2c_gelu_mul_quant(t->yf, 2 * I, I, t->qb, t->qbs, M, ab_i, st), "text gelu quant");
+        if (t->fused_gelu) {
+            e2c_gemm_args a;
+            e2cu_gemm_args(&a, &y->gu, t->qa, t->qas, M, ab);
+            a.epi = E2C_EPI_GELUQ;
+            a.q8 = t->qb;
+            a.ldq = I;
+            a.q8_scale = t->qbs;
+            Q(e2c_gemm(&a, st), "text gate|up + h quant");
+        } else {
+            Q(gemm_f32(&y->gu, t->qa, t->qas, M, ab, t->yf, 2 * I, st), "text gate|up");
+            Q(e2c_gelu_mul_quant(t->yf, 2 * I, I, t->qb, t->qbs, M, ab_i, st), "text gelu quant");
+        }
         Q(gemm_f32(&y->d, t->qb, t->qbs, M, ab_i, t->tmp, D, st), "text down");
         Q(e2c_tt_norm_add(t->tmp, t->res, lnorm(t, l, 3), 1.0f, NULL, t->eps, t->qa, t->qas, M, D, ab, st),
           "text post-ffn norm");

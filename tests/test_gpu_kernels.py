@@ -826,3 +826,39 @@ def test_gelu_mul_quant(e2c, of, torch_cuda, ablk):
     np.testing.assert_allclose(qs.cpu().numpy(), es, rtol=1e-5)
     pre = h.reshape(M, I // ablk, ablk) * (np.float32(127.0) / np.abs(h.reshape(M, I // ablk, ablk)).max(axis=2, keepdims=True))
     tie_tolerant_bytes(q.cpu().numpy(), eq, pre.reshape(M, I))
+
+
+@pytest.mark.parametrize("M,K,I", [(300, 768, 1152), (4096, 512, 2048), (2176, 768, 1152), (129, 1024, 256),
+                                   (1000, 256, 128)])
+def test_gelu_quant_epilogue_per_block(e2c, of, torch_cuda, M, K, I):
+    """Per-block mode's gate|up GEMM with GELU-gate and the per-128-block quantiser of h in its
+    epilogue (the text tower's and the per-block encoder's FFN, e2.c src/text.c:950-953 with
+    src/int8.c:178-209 per block): the int8 rows and scales are bit-identical to the per-block F32
+    GEMM followed by e2c_gelu_mul_quant (both checked against the port above). 4096 and 2176 rows
+    take the CTA-pair kernel (2176: a half-empty last pair), the others single CTAs."""
+    torch = torch_cuda
+    rng = np.random.default_rng(57 + M + K + I)
+    qa, a_s, w, ws = _gemm_inputs(rng, M, 2 * I, K, 128)
+    W = e2c.Weight(w=w, scale=ws)
+    qd, sd = dev(torch, qa), dev(torch, a_s)
+    y = torch.empty((M, 2 * I), dtype=torch.float32, device="cuda")
+    a = _args_for(W, qd, sd, M, K)
+    a.ablk, a.epi, a.y, a.ldy = 128, e2c.EPI_F32, y.data_ptr(), 2 * I
+    _launch(e2c, a, torch)
+    want_q = torch.zeros((M, I), dtype=torch.int8, device="cuda")
+    want_s = torch.zeros((M, I // 128), dtype=torch.float32, device="cuda")
+    lib = e2c.lib()
+    lib.e2c_gelu_mul_quant.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p]
+    assert lib.e2c_gelu_mul_quant(y.data_ptr(), 2 * I, I, want_q.data_ptr(), want_s.data_ptr(), M, 128,
+                                  torch.cuda.current_stream().cuda_stream) == 0, lib.e2c_msg().decode()
+    e2c.check()
+    ldq = I + 16  # a row stride wider than the row
+    q = torch.full((M, ldq), 99, dtype=torch.int8, device="cuda")
+    s = torch.zeros((M, I // 128), dtype=torch.float32, device="cuda")
+    a = _args_for(W, qd, sd, M, K)
+    a.ablk, a.epi, a.q8, a.ldq, a.q8_scale = 128, e2c.EPI_GELUQ, q.data_ptr(), ldq, s.data_ptr()
+    _launch(e2c, a, torch)
+    qn = q.cpu().numpy()
+    assert np.array_equal(qn[:, :I], want_q.cpu().numpy()), "bytes differ from the two-kernel path"
+    assert np.all(qn[:, I:] == 99), "wrote past the row"
+    assert f32_bits_equal(s.cpu().numpy(), want_s.cpu().numpy())

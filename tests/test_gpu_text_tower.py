@@ -174,7 +174,8 @@ def test_text_tower_graph_replay_and_stats(tm, tower):
     b = tower.embed_batch(ids)
     assert np.array_equal(a, b)
     calls, kernels, ms = tower.stats()
-    assert kernels == 5 + 14 * 24 and calls >= 2 and ms > 0
+    # 13 kernels per layer: gate|up applies GELU-gate and h's per-block quantiser in its epilogue
+    assert kernels == 5 + 13 * 24 and calls >= 2 and ms > 0
 
 
 # ------------------------------------------------------------------------------ kernels of the tower
