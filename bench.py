@@ -718,7 +718,8 @@ def config1(args) -> int:
 def text_pass_work(B: int, S: int, cfg) -> list:
     """(kernel, int8 ops, bf16 flops, algorithmic bytes) of every launch of one text-tower pass over
     B sequences of S tokens (activations per 128-block; every GEMM writes fp32 except gate|up, which
-    writes h quantised per 128-block)."""
+    writes h quantised per 128-block, and q|k|v on the layers with heads of 256, which writes bf16
+    Q, K and V^T)."""
     M, D, I, P, L, H, DO = B * S, cfg.hidden, cfg.intermediate, cfg.ple_dim, cfg.n_layers, cfg.n_heads, cfg.out_dim
 
     def gemm(name, K, N):
@@ -729,8 +730,11 @@ def text_pass_work(B: int, S: int, cfg) -> list:
         hd, kv, qd = cfg.head_dim(l), cfg.n_kv(l), cfg.q_dim(l)
         nqkv = qd + 2 * kv * hd
         keys = S if cfg.full(l) else min(S, 2 * cfg.window + 1)
-        w += [gemm("qkv", D, nqkv), ("qkv_post", 0, 0, 4 * M * nqkv + 2 * M * nqkv),
-              ("attention", 0, 4.0 * M * keys * hd * H, 2 * M * nqkv + 4 * M * qd),
+        if hd == 256:  # the q|k|v finish in the GEMM's epilogue: bf16 Q, K, V^T written once
+            w += [("qkv_finish", 2.0 * M * D * nqkv, 0.0, M * D + 4 * M * D / 128 + nqkv * D + 4 * nqkv + 2 * M * nqkv)]
+        else:
+            w += [gemm("qkv", D, nqkv), ("qkv_post", 0, 0, 4 * M * nqkv + 2 * M * nqkv)]
+        w += [("attention", 0, 4.0 * M * keys * hd * H, 2 * M * nqkv + 4 * M * qd),
               ("quantize_ctx", 0, 0, 4 * M * qd + M * qd + 4 * M * qd / 128), gemm("o_proj", qd, D),
               ("norm_add", 0, 0, 13 * M * D + 4 * M * D / 128),
               ("gate_up_gelu_quant", 2.0 * M * D * 2 * I, 0.0,

@@ -83,7 +83,7 @@ class GemmArgs(C.Structure):
                 ("ws_bytes", C.c_size_t)]
 
 
-EPI_F32, EPI_RESID, EPI_I32, EPI_GELU, EPI_QKV, EPI_NORMADD, EPI_GELUQ = 0, 1, 2, 3, 4, 5, 6
+EPI_F32, EPI_RESID, EPI_I32, EPI_GELU, EPI_QKV, EPI_NORMADD, EPI_GELUQ, EPI_QKVPB = 0, 1, 2, 3, 4, 5, 6, 7
 
 
 def gemm_args(w: "Weight", qa, a_scales, M: int) -> GemmArgs:

@@ -53,24 +53,28 @@ struct GemmSmem {
     // staging tiles per epilogue warp: QKV stages the two halves of a head; the other epilogues
     // without the per-block fold alternate between two, so a store overlaps the next chunk's math
     static constexpr int STG_BUFS = (EPI == E2C_EPI_QKV || (!PERBLOCK && EPI != E2C_EPI_I32 && CG == 1)) ? 2 : 1;
-    // (the per-block GELU-quantise epilogue stores its int8 rows from registers)
-    static constexpr int STG_PER_WARP = EPI == E2C_EPI_GELUQ ? 0 : STG_BUFS * STG_WARP;
+    // (the per-block GELU-quantise and q|k|v epilogues store from registers)
+    static constexpr bool SUBT = EPI == E2C_EPI_GELUQ || EPI == E2C_EPI_QKVPB;
+    static constexpr int STG_PER_WARP = SUBT ? 0 : STG_BUFS * STG_WARP;
     static constexpr int STG_OFF = STAGES * STAGE_BYTES;
     // per-warp column constants (weight scales, norm gains): 128 floats (QKV: 256, 64 pairs a warp;
     // per-block mode: the 32 weight scales of the warp; per-block GELU-quantise: its 16 gate and 16
     // up weight scales of each of the two sub-tiles)
-    static constexpr int CST_FLOATS = EPI == E2C_EPI_QKV ? 256 : EPI == E2C_EPI_GELUQ ? 64 : PERBLOCK ? 32 : 128;
+    // per-block q|k|v: the weight scales and norm gains of its 32 columns in each half of the head)
+    static constexpr int CST_FLOATS = EPI == E2C_EPI_QKV ? 256 : EPI == E2C_EPI_GELUQ ? 64 : EPI == E2C_EPI_QKVPB ? 128
+                                    : PERBLOCK ? 32 : 128;
     static constexpr int CST_OFF = STG_OFF + EPI_WARPS * STG_PER_WARP;
     static constexpr int CST_BYTES = EPI == E2C_EPI_I32 ? 0 : EPI_WARPS * CST_FLOATS * 4;
     static constexpr int SSQ_OFF = CST_OFF + CST_BYTES;
-    // QKV: [group][part2][row] row sums of squares; per-block GELU-quantise: [tile parity][part][row]
-    // row maxima of |h|
-    static constexpr int SSQ_BYTES = EPI == E2C_EPI_QKV ? 2 * 2 * BM * 4 : EPI == E2C_EPI_GELUQ ? 2 * 4 * BM * 4 : 0;
+    // QKV: [group][part2][row] row sums of squares; per-block GELU-quantise and q|k|v: [tile
+    // parity][part][row] row maxima of |h| or sums of squares
+    static constexpr int SSQ_BYTES = EPI == E2C_EPI_QKV ? 2 * 2 * BM * 4 : SUBT ? 2 * 4 * BM * 4 : 0;
     static constexpr int BAR_OFF = SSQ_OFF + SSQ_BYTES;
     // TMEM accumulators: per-block mode keeps four (the tensor core runs up to three 128-deep blocks
-    // ahead of the drain; the GELU-quantise epilogue three, its columns 384.. holding the first
-    // sub-tile's h), the others two
-    static constexpr int NACC = EPI == E2C_EPI_GELUQ ? 3 : PERBLOCK ? 4 : 2;
+    // ahead of the drain; the GELU-quantise epilogue three, columns 384.. holding the first
+    // sub-tile's h; the q|k|v epilogue two, columns 256.. holding both halves of the head), the
+    // others two
+    static constexpr int NACC = EPI == E2C_EPI_QKVPB ? 2 : SUBT ? 3 : PERBLOCK ? 4 : 2;
     // full[S], empty[S], tfull[NACC], tempty[NACC], pair[2][4] (the QKV row-norm and per-block
     // GELU-quantise row-maximum exchanges), tmem slot
     static constexpr int NBAR = 2 * STAGES + 2 * NACC + 8;
@@ -129,10 +133,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     const int tstride = CG == 2 ? (int)(gridDim.x >> 1) : (int)gridDim.x;
     // Per-block GELU-quantise: a tile is 256 weight rows (128 gate + 128 up = one 128-column block
     // of h) taken as two sub-tiles of 128 columns, each the gate and up rows of 64 h columns.
+    // Per-block q|k|v: a tile is one head of 256 weight rows, taken as its two halves.
     constexpr bool GQ = EPI == E2C_EPI_GELUQ;
-    constexpr int NSUB = GQ ? 2 : 1;
+    constexpr bool QP = EPI == E2C_EPI_QKVPB;
+    constexpr int NSUB = (GQ || QP) ? 2 : 1;
     constexpr int TW = BN * NSUB;                        // weight rows per tile
-    static_assert(!GQ || (PERBLOCK && BN == 128), "the GELU-quantise epilogue here is the per-block one");
+    static_assert(!(GQ || QP) || (PERBLOCK && BN == 128), "sub-tiled epilogues are per-block ones");
     const int tiles_m = (M + BM * CG - 1) / (BM * CG), tiles_n = (ncols + TW - 1) / TW;
     const int ntiles = tiles_m * tiles_n;
     const int nk = (K + BK - 1) / BK;                    // stages per (sub-)tile
@@ -154,7 +160,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         }
         // QKV: the quadrant's 2 warps of a group; GELU-quantise: the quadrant's 4 warps
         for (int a = 0; a < 2; a++)
-            for (int q = 0; q < 4; q++) mbar_init(pair_bar(a, q), GQ ? 128 : 64);
+            for (int q = 0; q < 4; q++) mbar_init(pair_bar(a, q), (GQ || QP) ? 128 : 64);
         fence_mbar_init();
         tma_prefetch_desc(&tmA);
         tma_prefetch_desc(&tmB);
@@ -196,7 +202,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             for (int t = tfirst; t < ntiles && ok; t += tstride) {
                 const int m0 = (t / tiles_n) * (BM * CG) + (int)rank * BM, c0 = p.n0 + (t % tiles_n) * TW;
                 for (int kb2 = 0; kb2 < NSUB * nk; kb2++) {
-                    const int kb = GQ ? kb2 % nk : kb2, sub = GQ ? kb2 / nk : 0;
+                    const int kb = NSUB > 1 ? kb2 % nk : kb2, sub = NSUB > 1 ? kb2 / nk : 0;
                     if (!mbar_wait(empty_bar(stage), phase ^ 1u, p.status, E2C_ERR_WAIT_PRODUCER)) {
                         ok = false;
                         break;
@@ -209,7 +215,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                         tma_load_2d_pair(sa, &tmA, kb * BK, m0, fb);
                         // GELU-quantise: the first CTA holds the sub-tile's 64 gate rows, the second
                         // its 64 up rows
-                        tma_load_2d_pair(sb, &tmB, kb * BK, GQ ? c0 + 128 * (int)rank + 64 * sub : c0 + (int)rank * (BN / 2), fb);
+                        tma_load_2d_pair(sb, &tmB, kb * BK,
+                                         GQ ? c0 + 128 * (int)rank + 64 * sub : c0 + BN * sub + (int)rank * (BN / 2), fb);
                     } else {
                         mbar_arrive_expect_tx(full_bar(stage), L::STAGE_BYTES);
                         tma_load_2d(sa, &tmA, kb * BK, m0, full_bar(stage));
@@ -218,7 +225,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                             tma_load_2d(sb, &tmB, kb * BK, c0 + 64 * sub, full_bar(stage));
                             tma_load_2d(sb + 64 * BK, &tmB, kb * BK, c0 + 128 + 64 * sub, full_bar(stage));
                         } else {
-                            tma_load_2d(sb, &tmB, kb * BK, c0, full_bar(stage));
+                            tma_load_2d(sb, &tmB, kb * BK, c0 + BN * sub, full_bar(stage));
                         }
                     }
                     issued++;
@@ -703,6 +710,158 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                         }
                         if (part == 0) p.q8_scale[(size_t)m * tiles_n + hb] = am > 0.f ? __fmul_rn(am, 0x1.020408p-7f) : 1.0f;
                     }
+                } else if constexpr (QP) {
+                    // One tile = one head of 256 columns, its halves [0, 128) and [128, 256) the two
+                    // sub-tiles. This warp folds columns 32 part .. 32 part + 31 of each half, so the
+                    // rotate-half pairs (i, i + 128) of RoPE meet in one thread; both folded halves
+                    // wait in TMEM columns 256 + 64 part .. + 63 for the norm. The row's sum of
+                    // squares over the head combines the quadrant's four warps through shared memory.
+                    // Arithmetic per element as the per-block F32 GEMM followed by the q|k|v finish
+                    // (x = float(acc) fold, clamp; y = (x * inv) * gain; RoPE; bf16), the norm's sum
+                    // of squares in its own order.
+                    const int head = (c0 - p.n0) / TW;
+                    const int nkv = (ncols / 256 - p.nq) / 2;
+                    const int kind = head < p.nq ? 0 : head < p.nq + nkv ? 1 : 2;  // q, k, v
+                    __syncwarp();  // every lane is done with the previous tile's constants
+                    {
+                        const float *gam = kind == 0 ? p.q_gamma : kind == 1 ? p.k_gamma : nullptr;
+#pragma unroll
+                        for (int s = 0; s < 2; s++) {
+                            cst[32 * s + lane] = __ldg(p.w_scale + c0 + 128 * s + 32 * part + lane);
+                            cst[64 + 32 * s + lane] = gam ? __ldg(gam + 128 * s + 32 * part + lane) : 1.f;
+                        }
+                    }
+                    __syncwarp();
+                    const uint32_t park = tmem_base + lane_addr + (uint32_t)(2 * BN + 64 * part);
+                    float ssh = 0.f;  // the warp's sum of squares over the halves folded so far
+#pragma unroll 1
+                    for (int s = 0; s < 2; s++) {
+                        float f[32];
+#pragma unroll
+                        for (int j = 0; j < 32; j++) f[j] = 0.f;
+                        float as_next = mrow ? __ldg(p.a_scale + (size_t)m * nb) : 0.f;
+                        for (int u = 0; u < nunits; u++) {
+                            const float as = as_next;
+                            if (u + 1 < nunits) as_next = mrow ? __ldg(p.a_scale + (size_t)m * nb + u + 1) : 0.f;
+                            if (!__all_sync(0xffffffffu, mbar_wait(tfull_bar(acc), acc_phase, p.status, E2C_ERR_WAIT_EPI))) {
+                                ok = false;
+                                break;
+                            }
+                            tc_fence_after();
+                            const uint32_t ta = tmem_base + lane_addr + (uint32_t)(acc * BN + 32 * part);
+                            const float2 as2 = make_float2(as, as);
+                            // 16 columns at a time (16 loaded values live)
+#pragma unroll
+                            for (int hh = 0; hh < 2; hh++) {
+                                uint32_t r[16];
+                                tmem_ld16(ta + 16 * hh, r);
+                                tmem_wait_ld();
+                                if (hh == 1) release_acc(acc);
+#pragma unroll
+                                for (int j4 = 0; j4 < 4; j4++) {
+                                    const float4 w4 = *reinterpret_cast<const float4 *>(cst + 32 * s + 16 * hh + 4 * j4);
+#pragma unroll
+                                    for (int h = 0; h < 2; h++) {
+                                        const int j = 4 * j4 + 2 * h, jf = 16 * hh + j;
+                                        const float2 s2 = mul2_rn(as2, h ? make_float2(w4.z, w4.w) : make_float2(w4.x, w4.y));
+                                        const float2 d2 = make_float2(__int2float_rn((int)r[j]), __int2float_rn((int)r[j + 1]));
+                                        const float2 o = fma2_rn(d2, s2, make_float2(f[jf], f[jf + 1]));
+                                        f[jf] = o.x;
+                                        f[jf + 1] = o.y;
+                                    }
+                                }
+                            }
+                            if (++acc == NACC) {
+                                acc = 0;
+                                acc_phase ^= 1u;
+                            }
+                        }
+                        if (!ok) break;
+                        float ssp[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                        for (int j = 0; j < 32; j++) {
+                            f[j] = fminf(fmaxf(f[j], p.out_min), p.out_max);
+                            ssp[j & 3] = __fmaf_rn(f[j], f[j], ssp[j & 3]);
+                        }
+                        ssh = __fadd_rn(ssh, __fadd_rn(__fadd_rn(ssp[0], ssp[1]), __fadd_rn(ssp[2], ssp[3])));
+                        tmem_st32(park + 32 * s, reinterpret_cast<const uint32_t (&)[32]>(f));
+                    }
+                    if (!ok) break;
+                    float *xs = reinterpret_cast<float *>(smem + L::SSQ_OFF) + (jt & 1) * 4 * BM;
+                    xs[part * BM + row] = ssh;
+                    mbar_arrive(pair_bar(0, q));
+                    if (!__all_sync(0xffffffffu, mbar_wait(pair_bar(0, q), (uint32_t)(jt & 1), p.status, E2C_ERR_WAIT_EPI))) {
+                        ok = false;
+                        break;
+                    }
+                    const float ss = __fadd_rn(__fadd_rn(xs[row], xs[BM + row]), __fadd_rn(xs[2 * BM + row], xs[3 * BM + row]));
+                    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, 256.0f), p.eps)));
+                    tmem_wait_st();
+                    const int bseq = mrow ? m / p.seq_len : 0, pos = mrow ? m - bseq * p.seq_len : 0;
+                    if (kind < 2) {
+                        // q, k: 8 pairs a step from TMEM, RoPE on 4 at a time; 16-byte bf16 runs of
+                        // each half
+                        __nv_bfloat16 *dst = kind == 0
+                            ? reinterpret_cast<__nv_bfloat16 *>(p.q_out) + (size_t)m * (256 * p.nq) + head * 256
+                            : reinterpret_cast<__nv_bfloat16 *>(p.k_out) + (size_t)m * (256 * nkv) + (head - p.nq) * 256;
+                        const float *rc = p.rope_cos + (size_t)pos * p.ldrope, *rs = p.rope_sin + (size_t)pos * p.ldrope;
+#pragma unroll 1
+                        for (int c = 0; c < 4; c++) {
+                            uint32_t r0[8], r1[8];
+                            tmem_ld8(park + 8 * c, r0);
+                            tmem_ld8(park + 32 + 8 * c, r1);
+                            tmem_wait_ld();
+                            const int i0 = 32 * part + 8 * c;  // rotate-half index of the first pair
+                            uint32_t px[4], pz[4];
+#pragma unroll
+                            for (int h4 = 0; h4 < 2; h4++) {
+                                const float4 c4 = __ldg(reinterpret_cast<const float4 *>(rc + i0 + 4 * h4));
+                                const float4 s4 = __ldg(reinterpret_cast<const float4 *>(rs + i0 + 4 * h4));
+                                const float cs[4] = {c4.x, c4.y, c4.z, c4.w}, sn[4] = {s4.x, s4.y, s4.z, s4.w};
+                                float xo[4], zo[4];
+#pragma unroll
+                                for (int jj = 0; jj < 4; jj++) {
+                                    const int j = 4 * h4 + jj;
+                                    const float x = __fmul_rn(__fmul_rn(__uint_as_float(r0[j]), inv), cst[64 + 8 * c + j]);
+                                    const float z = __fmul_rn(__fmul_rn(__uint_as_float(r1[j]), inv), cst[96 + 8 * c + j]);
+                                    xo[jj] = __fmaf_rn(x, cs[jj], -__fmul_rn(z, sn[jj]));
+                                    zo[jj] = __fmaf_rn(x, sn[jj], __fmul_rn(z, cs[jj]));
+                                }
+#pragma unroll
+                                for (int k = 0; k < 2; k++) {
+                                    const __nv_bfloat162 hx = __floats2bfloat162_rn(xo[2 * k], xo[2 * k + 1]);
+                                    const __nv_bfloat162 hz = __floats2bfloat162_rn(zo[2 * k], zo[2 * k + 1]);
+                                    px[2 * h4 + k] = *reinterpret_cast<const uint32_t *>(&hx);
+                                    pz[2 * h4 + k] = *reinterpret_cast<const uint32_t *>(&hz);
+                                }
+                            }
+                            if (mrow) {
+                                *reinterpret_cast<uint4 *>(dst + i0) = make_uint4(px[0], px[1], px[2], px[3]);
+                                *reinterpret_cast<uint4 *>(dst + 128 + i0) = make_uint4(pz[0], pz[1], pz[2], pz[3]);
+                            }
+                        }
+                    } else {
+                        // v: V^T [B][256 nkv][ldvt]; the warp's 32 consecutive positions of one dimension
+                        // are one contiguous run
+                        __nv_bfloat16 *vt = reinterpret_cast<__nv_bfloat16 *>(p.vt_out) +
+                                            ((size_t)bseq * 256 * nkv + (size_t)(head - p.nq - nkv) * 256) * p.ldvt + pos;
+#pragma unroll 1
+                        for (int c = 0; c < 4; c++) {
+                            uint32_t r0[8], r1[8];
+                            tmem_ld8(park + 8 * c, r0);
+                            tmem_ld8(park + 32 + 8 * c, r1);
+                            tmem_wait_ld();
+                            const int i0 = 32 * part + 8 * c;
+                            if (mrow)
+#pragma unroll
+                                for (int j = 0; j < 8; j++) {
+                                    vt[(size_t)(i0 + j) * p.ldvt] =
+                                        __float2bfloat16_rn(__fmul_rn(__fmul_rn(__uint_as_float(r0[j]), inv), cst[64 + 8 * c + j]));
+                                    vt[(size_t)(128 + i0 + j) * p.ldvt] =
+                                        __float2bfloat16_rn(__fmul_rn(__fmul_rn(__uint_as_float(r1[j]), inv), cst[96 + 8 * c + j]));
+                                }
+                        }
+                    }
                 } else if constexpr (PERBLOCK) {
                     float f[QCOLS];
     #pragma unroll
@@ -938,7 +1097,7 @@ int launch(const e2c_gemm_args *a, cudaStream_t st, int dev, int num_sms) {
                                         (uint64_t)a->M, (uint64_t)512 * a->nq, 32, 32) &&
                       !e2c_tmap_2d_sw64(&t1, a->k_out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 256, (uint64_t)a->M, 512, 32, 32);
     }
-    constexpr int TW = EPI == E2C_EPI_GELUQ ? 2 * BN : BN;  // weight rows per tile
+    constexpr int TW = (EPI == E2C_EPI_GELUQ || EPI == E2C_EPI_QKVPB) ? 2 * BN : BN;  // weight rows per tile
     const int tiles = ((a->M + BM * CG - 1) / (BM * CG)) * ((a->n1 - a->n0 + TW - 1) / TW);
     cudaError_t e;
     if constexpr (CG == 1) {
@@ -1003,7 +1162,7 @@ Plan pick_plan(const e2c_gemm_args *a, int num_sms) {
     if (a->ablk != a->K) {
         // per-block fold: BN 128 (four 128-column accumulators); CTA pairs on the same rule (the
         // GELU-quantise epilogue's tiles are 256 weight rows)
-        const int tw = a->epi == E2C_EPI_GELUQ ? 256 : 128;
+        const int tw = (a->epi == E2C_EPI_GELUQ || a->epi == E2C_EPI_QKVPB) ? 256 : 128;
         const long pairs128 = (long)((a->M + 2 * BM - 1) / (2 * BM)) * ((ncols + tw - 1) / tw);
         return {128, (pairs128 >= num_sms / 2 && a->M > 2 * BM) ? 2 : 1};
     }
@@ -1192,6 +1351,21 @@ extern "C" int e2c_gemm(const e2c_gemm_args *a, void *stream) {
             return -1;
         }
         return e2c_gemm_gelu_quant(a, stream);
+    }
+    case E2C_EPI_QKVPB: {
+        // the per-block q|k|v finish of heads of 256 in the per-block kernel's epilogue
+        const int ncols = a->n1 - a->n0, heads = ncols / 256, nkv2 = heads - a->nq;
+        if (!perblock || a->n0 != 0 || ncols % 256 || a->nq < 1 || nkv2 < 2 || nkv2 % 2 || a->seq_len <= 0 ||
+            a->M % a->seq_len || a->ldvt < a->seq_len || a->ldrope < 128 || a->ldrope % 4 || !a->q_out || !a->k_out ||
+            !a->vt_out || !a->rope_cos || !a->rope_sin ||
+            (((uintptr_t)a->q_out | (uintptr_t)a->k_out | (uintptr_t)a->rope_cos | (uintptr_t)a->rope_sin) & 15)) {
+            e2c_set_msg("gemm: the per-block q|k|v epilogue needs per-block scales, whole heads of 256 (nq q heads, then "
+                        "as many k as v heads), M a multiple of seq_len, ldvt >= seq_len, position-major RoPE tables "
+                        "of ldrope >= 128 (a multiple of 4) and 16-byte aligned Q, K and tables");
+            return -1;
+        }
+        return pair ? launch<128, 8, true, E2C_EPI_QKVPB, 2>(a, st, dev, num_sms)
+                    : launch<128, 6, true, E2C_EPI_QKVPB, 1>(a, st, dev, num_sms);
     }
     default:
         e2c_set_msg("gemm: unknown epilogue %d", a->epi);

@@ -39,9 +39,16 @@ enum {
     E2C_EPI_NORMADD = 5 /* y = gemm (never stored); x = rmsnorm(y) * g1 + res; res = x;
                           q = quantise(rmsnorm(x) * g2) per token (g2 NULL: res = rmsnorm(x) * gf).
                           Whole rows per cluster of CTAs (N = 768: 6 x 128 columns) */,
-    E2C_EPI_GELUQ = 6  /* GELU-gate as E2C_EPI_GELU, then the per-token quantiser of h over its
+    E2C_EPI_GELUQ = 6, /* GELU-gate as E2C_EPI_GELU, then the per-token quantiser of h over its
                           N/2 columns: int8 q8 [M][ldq] and q8_scale [M] (h itself is not stored).
-                          Whole rows per cluster of N/256 CTAs (N = 2304: 9) */
+                          Whole rows per cluster of N/256 CTAs (N = 2304: 9). With per-128-block
+                          activation scales: h's per-block quantiser, q8_scale [M][N/256] */
+    E2C_EPI_QKVPB = 7  /* per-128-block activation scales: the q|k|v finish of heads of 256.
+                          Columns [0, 256 nq) are q heads, then nkv k heads, then nkv v heads
+                          (nkv = (N/256 - nq) / 2): per-head RMSNorm (q_gamma, k_gamma; v without a
+                          gain), RoPE on q and k from position-major tables (cos of pair i at
+                          position p: rope_cos[p * ldrope + i]), bf16 Q [M][256 nq], K [M][256 nkv]
+                          and V^T [B][256 nkv][ldvt] */
 };
 
 typedef struct {

@@ -18,8 +18,9 @@
  *                      quantise(rmsnorm(x) * input_ln[l + 1]), after the last layer final_norm
  *   GEMM embed_proj -> masked mean pool -> L2
  *
- * 14 kernels per layer (13 when gate|up applies GELU-gate and h's per-block quantiser in its
- * epilogue), 5 around them. int8 activations alternate between qa (inputs of the
+ * 14 kernels per layer, 5 around them; one fewer each where gate|up applies GELU-gate and h's
+ * per-block quantiser in its epilogue, and where the q|k|v GEMM finishes its heads of 256 in its
+ * epilogue. int8 activations alternate between qa (inputs of the
  * hidden-wide GEMMs) and qb (ctx, h and the PLE gate's output), so a row kernel never writes the
  * buffer the GEMM before it still reads.
  */
@@ -50,6 +51,7 @@ typedef struct {
 struct e2cuda_text {
     int L, D, I, P, H, V, DO, max_seq, ablk, max_tokens;
     int fused_gelu; /* per-block gate|up GEMM with GELU-gate + quantiser epilogue (E2C_FUSED_GELU=0: off) */
+    int fused_qkv;  /* per-block q|k|v GEMM with the finish in its epilogue, heads of 256 (E2C_FUSED_QKV=0: off) */
     float eps, embed_scale, ple_scale;
     tt_layer layer[TT_MAX_LAYERS];
     e2cuda_w8 ple_model, embed_proj;
@@ -199,8 +201,9 @@ e2cuda_text *e2cuda_text_create(const e2cuda_text_desc *d, int max_tokens) {
     t->max_seq = d->max_seq;
     t->ablk = ablk;
     {
-        const char *fg = getenv("E2C_FUSED_GELU");
+        const char *fg = getenv("E2C_FUSED_GELU"), *fq = getenv("E2C_FUSED_QKV");
         t->fused_gelu = ablk == 128 && !(fg && fg[0] == '0');
+        t->fused_qkv = ablk == 128 && !(fq && fq[0] == '0');
     }
     t->max_tokens = max_tokens;
     t->eps = d->eps;
@@ -332,10 +335,29 @@ static int forward(e2cuda_text *t, int B, int S, int has_valid, cudaStream_t st)
         const tt_layer *y = &t->layer[l];
         const int hd = y->hd, kv = y->kv, qd = y->qdim, ab_q = ab == 128 ? 128 : qd;
         const int ldy = qd + 2 * kv * hd;
-        Q(gemm_f32(&y->qkv, t->qa, t->qas, M, ab, t->yf, ldy, st), "text qkv");
-        Q(e2c_tt_qkv_post(t->yf, ldy, H, kv, hd, lnorm(t, l, 5), lnorm(t, l, 6), t->eps, t->rope_cos[y->rope],
-                          t->rope_sin[y->rope], hd / 2, 1, S, t->Q, t->K, t->Vt, ldvt, M, st),
-          "text qkv post");
+        if (t->fused_qkv && hd == 256) {
+            e2c_gemm_args a;
+            e2cu_gemm_args(&a, &y->qkv, t->qa, t->qas, M, ab);
+            a.epi = E2C_EPI_QKVPB;
+            a.nq = H;
+            a.q_out = t->Q;
+            a.k_out = t->K;
+            a.vt_out = t->Vt;
+            a.ldvt = ldvt;
+            a.seq_len = S;
+            a.q_gamma = lnorm(t, l, 5);
+            a.k_gamma = lnorm(t, l, 6);
+            a.rope_cos = t->rope_cos[y->rope];
+            a.rope_sin = t->rope_sin[y->rope];
+            a.ldrope = hd / 2;
+            a.eps = t->eps;
+            Q(e2c_gemm(&a, st), "text qkv + finish");
+        } else {
+            Q(gemm_f32(&y->qkv, t->qa, t->qas, M, ab, t->yf, ldy, st), "text qkv");
+            Q(e2c_tt_qkv_post(t->yf, ldy, H, kv, hd, lnorm(t, l, 5), lnorm(t, l, 6), t->eps, t->rope_cos[y->rope],
+                              t->rope_sin[y->rope], hd / 2, 1, S, t->Q, t->K, t->Vt, ldvt, M, st),
+              "text qkv post");
+        }
         Q(e2c_attention_win(t->Q, t->K, t->Vt, ldvt, valid, t->ctx, B, S, H, kv, hd, 1.0f, y->window, t->status, st),
           "text attention");
         Q(e2c_quantize(t->ctx, qd, t->qb, qd, t->qbs, M, qd, ab_q, -INFINITY, INFINITY, 0, st), "text ctx quant");

@@ -174,8 +174,9 @@ def test_text_tower_graph_replay_and_stats(tm, tower):
     b = tower.embed_batch(ids)
     assert np.array_equal(a, b)
     calls, kernels, ms = tower.stats()
-    # 13 kernels per layer: gate|up applies GELU-gate and h's per-block quantiser in its epilogue
-    assert kernels == 5 + 13 * 24 and calls >= 2 and ms > 0
+    # 14 kernels per layer, less gate|up's GELU-quantise epilogue (every layer) and the q|k|v
+    # finish in the q|k|v GEMM's epilogue (the 20 sliding layers, heads of 256)
+    assert kernels == 5 + 12 * 20 + 13 * 4 and calls >= 2 and ms > 0
 
 
 # ------------------------------------------------------------------------------ kernels of the tower
@@ -289,3 +290,72 @@ def test_tt_qkv_post_matches_port(e2c, of, torch_cuda, D, KV):
     tol = np.abs(want) * 2.0 ** -7 + 4e-6
     assert np.all(diff <= tol), f"beyond one bf16 ulp: {int((diff > tol).sum())}, worst {diff.max()}"
     assert (diff == 0).mean() > 0.99
+
+
+@pytest.mark.parametrize("B,S,H,KV,K", [(2, 512, 4, 2, 512), (16, 256, 4, 2, 512), (3, 77, 4, 2, 512),
+                                        (4, 200, 3, 1, 768)])
+def test_qkv_per_block_epilogue_matches_two_kernel_path(e2c, of, torch_cuda, B, S, H, KV, K):
+    """The per-block q|k|v GEMM with the finish in its epilogue (E2C_EPI_QKVPB: per-head RMSNorm, v
+    without a gain, RoPE from position-major tables, bf16 Q, K, V^T) against the per-block F32 GEMM
+    followed by e2c_tt_qkv_post (checked against the port above). The fold and every element
+    operation are the same; the norm's sum of squares is taken in another order, so values agree
+    within one bf16 ulp and nearly all bit for bit. 16 x 256 rows take CTA pairs, 3 x 77 a ragged
+    last tile; 4 x 200 is the synthetic encoder's 3 q heads and one KV head at K = 768."""
+    torch = torch_cuda
+    rng = np.random.default_rng(B * S + H + 7 * KV)
+    D = 256
+    M, nh = B * S, H + 2 * KV
+    N = nh * D
+    qa = rng.integers(-127, 128, size=(M, K), dtype=np.int8)
+    a_s = rng.uniform(1e-3, 0.05, size=(M, K // 128)).astype(np.float32)
+    w = rng.integers(-127, 128, size=(N, K), dtype=np.int8)
+    ws = rng.uniform(1e-4, 0.02, size=N).astype(np.float32)
+    W = e2c.Weight(w=w, scale=ws)
+    qd, sd = torch.from_numpy(qa).cuda(), torch.from_numpy(a_s).cuda()
+    qg = (1 + 0.1 * rng.standard_normal(D)).astype(np.float32)
+    kg = (1 + 0.1 * rng.standard_normal(D)).astype(np.float32)
+    cs = np.empty((S, D), np.float32)
+    sn = np.empty((S, D), np.float32)
+    of.port().e2o_rope_tables(cs.ctypes.data_as(of.f32p), sn.ctypes.data_as(of.f32p), S, D, 1e4)
+    ldrope, ldvt = D // 2 + 4, (S + 7) // 8 * 8
+    cT = np.zeros((S, ldrope), np.float32)
+    sT = np.zeros((S, ldrope), np.float32)
+    cT[:, :D // 2], sT[:, :D // 2] = cs[:, :D // 2], sn[:, :D // 2]
+    gq, gk, cd, sdn = (torch.from_numpy(t).cuda() for t in (qg, kg, cT, sT))
+    stream = torch.cuda.current_stream().cuda_stream
+
+    def outputs():
+        return (torch.zeros((M, H * D), dtype=torch.bfloat16, device="cuda"),
+                torch.zeros((M, KV * D), dtype=torch.bfloat16, device="cuda"),
+                torch.zeros((B, KV * D, ldvt), dtype=torch.bfloat16, device="cuda"))
+
+    # two kernels: the per-block F32 GEMM, then the finish
+    y = torch.empty((M, N), dtype=torch.float32, device="cuda")
+    a = e2c.gemm_args(W, qd, sd, M)
+    a.ablk, a.epi, a.y, a.ldy = 128, e2c.EPI_F32, y.data_ptr(), N
+    e2c.gemm_raw(a)
+    Q0, K0, V0 = outputs()
+    lib = e2c.lib()
+    lib.e2c_tt_qkv_post.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_float,
+                                    C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p,
+                                    C.c_int, C.c_int, C.c_void_p]
+    assert lib.e2c_tt_qkv_post(y.data_ptr(), N, H, KV, D, gq.data_ptr(), gk.data_ptr(), 1e-6, cd.data_ptr(),
+                               sdn.data_ptr(), ldrope, 1, S, Q0.data_ptr(), K0.data_ptr(), V0.data_ptr(), ldvt, M,
+                               stream) == 0, lib.e2c_msg().decode()
+    # one kernel
+    Q1, K1, V1 = outputs()
+    a = e2c.gemm_args(W, qd, sd, M)
+    a.ablk, a.epi, a.nq = 128, e2c.EPI_QKVPB, H
+    a.q_out, a.k_out, a.vt_out, a.ldvt, a.seq_len = Q1.data_ptr(), K1.data_ptr(), V1.data_ptr(), ldvt, S
+    a.q_gamma, a.k_gamma, a.rope_cos, a.rope_sin = gq.data_ptr(), gk.data_ptr(), cd.data_ptr(), sdn.data_ptr()
+    a.ldrope, a.eps = ldrope, 1e-6
+    e2c.gemm_raw(a)
+    e2c.check()
+    f = lambda t: t.float().cpu().numpy()
+    for got, want, what in ((Q1, Q0, "Q"), (K1, K0, "K"), (V1[:, :, :S], V0[:, :, :S], "V^T")):
+        g, w_ = f(got), f(want)
+        diff = np.abs(g - w_)
+        tol = np.maximum(np.abs(g), np.abs(w_)) * 2.0 ** -7 + 1e-6
+        assert np.all(diff <= tol), f"{what}: beyond one bf16 ulp: {int((diff > tol).sum())}, worst {diff.max()}"
+        assert (diff == 0).mean() > 0.98, f"{what}: {(diff == 0).mean()} identical"
+    assert torch.count_nonzero(V1[:, :, S:]) == 0, "V^T written past seq_len"
