@@ -13,8 +13,9 @@
  *
  * With per-token scales and a hidden size of 128 x (1..8) the residual norms run in the o_proj and
  * down GEMMs' epilogue (whole rows per cluster of CTAs), and with an FFN width of 128 x (1..16) h's
- * quantiser runs in the gate|up GEMM's epilogue (6 kernels per layer); otherwise the GEMMs write
- * fp32 and row kernels follow (up to 9 kernels per layer).
+ * quantiser runs in the gate|up GEMM's epilogue (6 kernels per layer). With per-128-block scales
+ * the q|k|v finish and h's per-block quantiser run in those GEMMs' epilogues and the residual norms
+ * follow o_proj and down as row kernels (8 kernels per layer).
  *
  * int8 activations alternate between two buffers: the layer's input (and the fused tails' output)
  * in qb, the quantised ctx and h in qa. A fused tail writes int8 rows of its output while other CTAs
@@ -45,6 +46,7 @@ struct e2cuda_encoder {
     float *table_scale;
     float *norms; /* per layer: input, post_attn, pre_ffn, post_ffn [D] + q_norm, k_norm [Dh]; then final [D] */
     float *rope_cos, *rope_sin;
+    float *rope_cos_pm, *rope_sin_pm; /* per-128-block mode: the same tables position-major [max_seq][Dh/2] */
     /* workspace */
     int32_t *ids;
     uint8_t *valid;
@@ -52,7 +54,7 @@ struct e2cuda_encoder {
     float *qkvf, *guf; /* per-128-block mode only: the q|k|v and gate|up GEMMs' fp32 outputs */
     int8_t *qa, *qb, *pq;
     float *qs, *qsb, *ps;
-    int fused_norm, fused_gelu;
+    int fused_norm, fused_gelu, fused_qkv;
     void *Q, *K, *Vt;
     size_t vt_bytes;
     int *status;
@@ -122,7 +124,7 @@ void e2cuda_encoder_destroy(e2cuda_encoder *e) {
     e2cuda_w8_free(&e->dense2);
     void *dev[] = { e->table, e->table_scale, e->norms, e->rope_cos, e->rope_sin, e->ids, e->valid, e->out, e->res,
                     e->tmp, e->ctx, e->h, e->pooled, e->h1, e->qa, e->qb, e->pq, e->qs, e->qsb, e->ps, e->Q, e->K,
-                    e->Vt, e->gws, e->qkvf, e->guf };
+                    e->Vt, e->gws, e->qkvf, e->guf, e->rope_cos_pm, e->rope_sin_pm };
     for (size_t i = 0; i < sizeof dev / sizeof dev[0]; i++)
         if (dev[i]) cudaFree(dev[i]);
     if (e->host_out) cudaFreeHost(e->host_out);
@@ -240,9 +242,28 @@ e2cuda_encoder *e2cuda_encoder_create(const e2cuda_encoder_desc *d, int max_toke
                 s[(size_t)i * e->max_seq + p] = sinf(f);
             }
         const size_t nb = sizeof(float) * (size_t)e->max_seq * half;
-        const int rc = DALLOC(e->rope_cos, nb) || DALLOC(e->rope_sin, nb) ||
-                       e2cu_cuda(cudaMemcpy(e->rope_cos, c, nb, cudaMemcpyHostToDevice), "rope upload") ||
-                       e2cu_cuda(cudaMemcpy(e->rope_sin, s, nb, cudaMemcpyHostToDevice), "rope upload");
+        int rc = DALLOC(e->rope_cos, nb) || DALLOC(e->rope_sin, nb) ||
+                 e2cu_cuda(cudaMemcpy(e->rope_cos, c, nb, cudaMemcpyHostToDevice), "rope upload") ||
+                 e2cu_cuda(cudaMemcpy(e->rope_sin, s, nb, cudaMemcpyHostToDevice), "rope upload");
+        if (!rc && e->ablk != D) {
+            /* per-block mode's q|k|v epilogue reads a lane's (one position's) pairs in 16-byte runs */
+            float *ct = malloc(nb), *st = malloc(nb);
+            if (!ct || !st) {
+                e2cu_err("encoder_create: out of host memory");
+                rc = 1;
+            } else {
+                for (int p = 0; p < e->max_seq; p++)
+                    for (int i = 0; i < half; i++) {
+                        ct[(size_t)p * half + i] = c[(size_t)i * e->max_seq + p];
+                        st[(size_t)p * half + i] = s[(size_t)i * e->max_seq + p];
+                    }
+                rc = DALLOC(e->rope_cos_pm, nb) || DALLOC(e->rope_sin_pm, nb) ||
+                     e2cu_cuda(cudaMemcpy(e->rope_cos_pm, ct, nb, cudaMemcpyHostToDevice), "rope upload") ||
+                     e2cu_cuda(cudaMemcpy(e->rope_sin_pm, st, nb, cudaMemcpyHostToDevice), "rope upload");
+            }
+            free(ct);
+            free(st);
+        }
         free(c);
         free(s);
         if (rc) goto fail;
@@ -282,6 +303,10 @@ e2cuda_encoder *e2cuda_encoder_create(const e2cuda_encoder_desc *d, int max_toke
         e->fused_gelu = !(fg && fg[0] == '0') && e->I % 128 == 0 &&
                         (e->ablk == D ? e->I / 128 <= 16 && e2c_gemm_gelu_quant_supported(e->I / 128)
                                       : e->ablk == 128);
+        /* per-block mode: q|k|v with the head finish in its epilogue (heads of 256);
+         * E2C_FUSED_QKV=0 selects the GEMM + row kernel pair */
+        const char *fq = getenv("E2C_FUSED_QKV");
+        e->fused_qkv = !(fq && fq[0] == '0') && e->ablk != D && e->Dh == 256;
     }
     /* the head's GEMMs have one row per sequence: up to 256 of them run on the weight-streaming
      * kernel, whose workspace starts zeroed and is left zeroed by every launch that completes */
@@ -348,7 +373,22 @@ static int encode(e2cuda_encoder *e, int B, int S, int has_valid, cudaStream_t s
     for (int l = 0; l < L; l++) {
         /* q|k|v with per-head RMSNorm + RoPE */
         e2cu_gemm_args(&a, &e->wqkv[l], e->qb, e->qsb, M, ab_d);
-        if (e->ablk != D) {
+        if (e->fused_qkv) {
+            a.epi = E2C_EPI_QKVPB;
+            a.nq = e->H;
+            a.q_out = e->Q;
+            a.k_out = e->K;
+            a.vt_out = e->Vt;
+            a.ldvt = ldvt;
+            a.seq_len = S;
+            a.q_gamma = nrm(e, l, 4);
+            a.k_gamma = nrm(e, l, 5);
+            a.rope_cos = e->rope_cos_pm;
+            a.rope_sin = e->rope_sin_pm;
+            a.ldrope = e->Dh / 2;
+            a.eps = e->eps;
+            if (e2cu_launch(e2c_gemm(&a, st), "encoder qkv + finish")) return -1;
+        } else if (e->ablk != D) {
             /* per-block scales: the GEMM folds block by block into fp32, a row kernel does the rest */
             a.epi = E2C_EPI_F32;
             a.y = e->qkvf;
