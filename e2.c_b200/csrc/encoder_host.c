@@ -14,8 +14,8 @@
  * With per-token scales and a hidden size of 128 x (1..8) the residual norms run in the o_proj and
  * down GEMMs' epilogue (whole rows per cluster of CTAs), and with an FFN width of 128 x (1..16) h's
  * quantiser runs in the gate|up GEMM's epilogue (6 kernels per layer). With per-128-block scales
- * the q|k|v finish and h's per-block quantiser run in those GEMMs' epilogues and the residual norms
- * follow o_proj and down as row kernels (8 kernels per layer).
+ * the same six: the q|k|v finish, the residual norms and h's quantiser run in the GEMMs'
+ * epilogues with the per-block fold, the int8 outputs quantised per 128-column block.
  *
  * int8 activations alternate between two buffers: the layer's input (and the fused tails' output)
  * in qb, the quantised ctx and h in qa. A fused tail writes int8 rows of its output while other CTAs
@@ -291,11 +291,12 @@ e2cuda_encoder *e2cuda_encoder_create(const e2cuda_encoder_desc *d, int max_toke
             goto fail;
     }
     /* o_proj / down run with the residual norms in their epilogue (one launch instead of two, the
-     * GEMM output never written) where the shape allows; E2C_FUSED_NORM=0 selects the GEMM + row
+     * GEMM output never written; per-128-block scales: the per-block fold and a per-block quantiser)
+     * where the shape allows; E2C_FUSED_NORM=0 selects the GEMM + row
      * kernel pair instead. */
     {
         const char *fz = getenv("E2C_FUSED_NORM");
-        e->fused_norm = !(fz && fz[0] == '0') && e->ablk == D && D % 128 == 0 && D / 128 <= 8;
+        e->fused_norm = !(fz && fz[0] == '0') && D % 128 == 0 && D / 128 <= 8;
         /* gate|up runs with GELU-gate and h's quantiser in its epilogue (h never stored): per token
          * where the device holds a cluster of I / 128 CTAs, per 128-block in the per-block GEMM;
          * E2C_FUSED_GELU=0 selects the two-kernel paths instead */

@@ -1317,13 +1317,14 @@ extern "C" int e2c_gemm(const e2c_gemm_args *a, void *stream) {
         // (single CTAs only for short activation matrices: two stages leave room for the constants)
         return pair ? launch<256, 4, false, E2C_EPI_QKV, 2>(a, st, dev, num_sms) : launch<256, 2, false, E2C_EPI_QKV, 1>(a, st, dev, num_sms);
     case E2C_EPI_NORMADD: {
-        // the residual norms in the epilogue: its own kernel (gemm_i8_norm.cu)
+        // the residual norms in the epilogue: its own kernel (gemm_i8_norm.cu); with per-128-block
+        // activation scales the int8 output is quantised per 128-column block (q8_scale [M][N/128])
         const int ncols = a->n1 - a->n0;
-        if (perblock || a->n0 != 0 || ncols % 128 || ncols / 128 > 8 || !a->res || !a->norm_g1 ||
+        if ((perblock && a->ablk != 128) || a->n0 != 0 || ncols % 128 || ncols / 128 > 8 || !a->res || !a->norm_g1 ||
             (!a->norm_g2 && !a->norm_gf) ||
             (a->norm_g2 && (!a->q8 || !a->q8_scale || a->ldq % 16 || ((uintptr_t)a->q8 & 15))) || a->ldres % 4 ||
             ((uintptr_t)a->res & 15)) {
-            e2c_set_msg("gemm: the norm epilogue needs per-row scales, whole rows of 128 x (1..8) columns, a 16-byte "
+            e2c_set_msg("gemm: the norm epilogue needs per-row or 128-wide block scales, whole rows of 128 x (1..8) columns, a 16-byte "
                         "aligned res, the norm gains and (with a second gain) 16-byte aligned int8 rows and their scales");
             return -1;
         }

@@ -85,8 +85,14 @@ struct Smem {
     static_assert(ALLOC <= 232448, "shared memory");
 };
 
-// QUANT: the next layer's int8 input is produced (g2 given); otherwise the final norm (gf)
-template <bool QUANT, int STAGES, int XMAX>
+// QUANT: the next layer's int8 input is produced (g2 given); otherwise the final norm (gf).
+// PB: activations with per-128-block scales (the per-block fold, e2.c's default recipe): the MMA
+// fills a ring of two 128-deep-block accumulators (TMEM columns 0..255), the first pass folds a
+// row block's blocks into t = sum fl(as ws) float(dot) (then the F32 epilogue's clamp) and keeps
+// v = t g1 in one of two row-block slots (columns 256..511), and the int8 output is quantised per
+// 128-column block, the CTA's own: its maximum comes from the quadrant's four warps, not the
+// cluster. The second pass's factor is inv1 alone.
+template <bool QUANT, int STAGES, int XMAX, bool PB>
 __global__ void __launch_bounds__(NTHREADS, 1)
     k_gemm_norm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const __grid_constant__ CUtensorMap tmR,
@@ -119,6 +125,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     const int tiles_m = (M + BM - 1) / BM;
     const int ntl = cid < tiles_m ? (tiles_m - 1 - cid) / ncls + 1 : 0;  // row blocks of this CTA
     const int nk = (K + BK - 1) / BK;
+    const int kpu = PB ? p.ablk / BK : nk;  // k-blocks per accumulation unit
+    const int nb = PB ? K / p.ablk : 1;     // units (activation scale blocks) per row block
     auto row0 = [&](int n) { return (cid + n * ncls) * BM; };
 
     if (warp == 0 && lane == 0) {
@@ -188,7 +196,49 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         }
     } else if (warp == 1) {
         // ------------------------------------------------------------------ MMA issuer
-        if (elect_one()) {
+        if (PB && elect_one()) {
+            // a ring of two accumulators of one 128-deep block each, drained by the first pass
+            constexpr uint32_t idesc = idesc_i8(BN, BM);
+            int stage = 0, ua = 0;
+            uint32_t phase = 0, uph = 0;
+            bool ok = true;
+            for (int n = 0; n < ntl && ok; n++) {
+                for (int u = 0; u < nb && ok; u++) {
+                    if (!mbar_wait(tempty_bar(ua), uph ^ 1u, p.status, E2C_ERR_WAIT_MMA)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t d = tmem_base + (uint32_t)(ua * BN);
+                    for (int kk = 0; kk < kpu; kk++) {
+                        if (!mbar_wait(full_bar(stage), phase, p.status, E2C_ERR_WAIT_MMA)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        const uint32_t sa = sbase + stage * L::STAGE, sb = sa + L::A_BYTES;
+#pragma unroll
+                        for (int k = 0; k < BK / 32; k++)
+                            mma_i8(d, smem_desc_sw128(sa + 32 * k), smem_desc_sw128(sb + 32 * k), idesc, (kk | k) != 0);
+                        mma_commit(empty_bar(stage));
+                        if (++stage == STAGES) {
+                            stage = 0;
+                            phase ^= 1u;
+                        }
+                    }
+                    if (!ok) break;
+                    mma_commit(tfull_bar(ua));
+                    ua ^= 1;
+                    if (ua == 0) uph ^= 1u;
+                }
+            }
+            if (!ok) {
+                // every MMA issued so far finishes before the accumulators are released
+                const uint32_t drain = tfull_bar(ua);
+                mma_commit(drain);
+                mbar_wait(drain, uph, nullptr, E2C_ERR_WAIT_DRAIN);
+            }
+        } else if (!PB && elect_one()) {
             constexpr uint32_t idesc = idesc_i8(BN, BM);
             int stage = 0;
             uint32_t phase = 0;
@@ -246,7 +296,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             for (int j = lane; j < QCOLS; j += 32) {
                 const float w = __ldg(p.w_scale + p.n0 + cl0 + j);
                 cst[j] = w;
-                cst[C_WG1 + j] = __fmul_rn(w, __ldg(p.norm_g1 + cl0 + j));
+                // per-block: the gain alone (t is scaled by the fold)
+                cst[C_WG1 + j] = PB ? __ldg(p.norm_g1 + cl0 + j) : __fmul_rn(w, __ldg(p.norm_g1 + cl0 + j));
                 cst[C_G2 + j] = __ldg(gb + cl0 + j);
             }
             __syncwarp();
@@ -255,7 +306,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         // the rows' activation scales of block n land in slot n & 3 by cp.async (one group per call)
         const uint32_t as_slot = smem_u32(csta + lane);
         auto load_as = [&](int n) {
-            if (n < ntl) {
+            if (!PB && n < ntl) {  // (per-block: the fold reads its scales itself; an empty group)
                 const int mr = row0(n) + row;
                 cp_async_4(as_slot + (uint32_t)((n & 3) * 128), p.a_scale + (mr < M ? (size_t)mr : 0), mr < M ? 4u : 0u);
             }
@@ -287,10 +338,15 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             return reinterpret_cast<float4 *>(resb + c * RES_TILE + lane * 64 + ((k ^ ((lane >> 1) & 3)) << 4));
         };
         float *xl0 = reinterpret_cast<float *>(smem + L::XL0_OFF);
-        float2 *xl1 = reinterpret_cast<float2 *>(smem + L::XL1_OFF);
+        // round 1's per-warp partials; per-block mode reads them again for the block maximum in
+        // pass 3, so they alternate by row block (odd blocks in the row-scale area it does not use)
+        auto xl1b = [&](int n) {
+            return reinterpret_cast<float2 *>(smem + ((PB && (n & 1)) ? L::CSTA_OFF : L::XL1_OFF));
+        };
         // round r of block n: this warp's partial (sum in .x, max in .y) to the quadrant, and from
         // part 0 the CTA's partial to every CTA of the cluster
         auto send = [&](int r, int n, float2 v) {
+            float2 *xl1 = xl1b(n);
             if (r == 0) xl0[part * BM + row] = v.x;
             else xl1[part * BM + row] = v;
             mbar_arrive(lbar(r, q));
@@ -332,7 +388,83 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             }
             return tot;
         };
-        auto tcols = [&](int n) { return tmem_base + lane_addr + (uint32_t)((n % NACC) * BN + part * QCOLS); };
+        // the block's TMEM columns: its accumulator, or per-block its slot (columns 256..511)
+        auto tcols = [&](int n) {
+            return tmem_base + lane_addr + (uint32_t)((PB ? 2 + (n & 1) : n % NACC) * BN + part * QCOLS);
+        };
+        int ua = 0;  // per-block: the accumulator ring, in step with the MMA issuer
+        uint32_t uph = 0;
+        // per-block pass 1: block n's 128-deep blocks folded in registers, f = fma(float(dot),
+        // fl(as ws), f) block by block (the per-block F32 epilogue's arithmetic) and clamped to t;
+        // returns sum t^2 over the warp's columns and leaves v = t g1 in the block's slot
+        auto pass1_pb = [&](int n) -> float {
+            const int m = row0(n) + row;
+            const bool mrow = m < M;
+            float f[QCOLS];
+#pragma unroll
+            for (int j = 0; j < QCOLS; j++) f[j] = 0.f;
+            float as_next = mrow ? __ldg(p.a_scale + (size_t)m * nb) : 0.f;
+            for (int u = 0; u < nb; u++) {
+                const float as = as_next;
+                if (u + 1 < nb) as_next = mrow ? __ldg(p.a_scale + (size_t)m * nb + u + 1) : 0.f;
+                if (!__all_sync(0xffffffffu, mbar_wait(tfull_bar(ua), uph, p.status, E2C_ERR_WAIT_EPI))) {
+                    ok = false;
+                    return 0.f;
+                }
+                tc_fence_after();
+                const uint32_t ta = tmem_base + lane_addr + (uint32_t)(ua * BN + part * QCOLS);
+                const float2 as2 = make_float2(as, as);
+#pragma unroll
+                for (int c = 0; c < NCH; c++) {
+                    uint32_t r[16];
+                    tmem_ld16(ta + 16 * c, r);
+                    tmem_wait_ld();
+                    if (c == NCH - 1) {
+                        // every column of the accumulator this warp reads has been read
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(tempty_bar(ua));
+                    }
+#pragma unroll
+                    for (int k = 0; k < 4; k++) {
+                        const float4 w4 = *reinterpret_cast<const float4 *>(cst + 16 * c + 4 * k);
+#pragma unroll
+                        for (int h = 0; h < 2; h++) {
+                            const int e = 4 * k + 2 * h, j = 16 * c + e;
+                            const float2 s2 = mul2_rn(as2, h ? make_float2(w4.z, w4.w) : make_float2(w4.x, w4.y));
+                            const float2 d2 = make_float2(__int2float_rn((int)r[e]), __int2float_rn((int)r[e + 1]));
+                            const float2 o = fma2_rn(d2, s2, make_float2(f[j], f[j + 1]));
+                            f[j] = o.x;
+                            f[j + 1] = o.y;
+                        }
+                    }
+                }
+                ua ^= 1;
+                if (ua == 0) uph ^= 1u;
+            }
+            float2 ssp[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+#pragma unroll
+            for (int c = 0; c < NCH; c++) {
+                uint32_t r[16];
+#pragma unroll
+                for (int k = 0; k < 4; k++) {
+                    const float4 g4 = *reinterpret_cast<const float4 *>(cst + C_WG1 + 16 * c + 4 * k);
+#pragma unroll
+                    for (int h = 0; h < 2; h++) {
+                        const int e = 4 * k + 2 * h, j = 16 * c + e;
+                        const float2 t = make_float2(fminf(fmaxf(f[j], p.out_min), p.out_max),
+                                                     fminf(fmaxf(f[j + 1], p.out_min), p.out_max));
+                        ssp[h] = fma2_rn(t, t, ssp[h]);
+                        const float2 v = mul2_rn(t, h ? make_float2(g4.z, g4.w) : make_float2(g4.x, g4.y));
+                        r[e] = __float_as_uint(v.x);
+                        r[e + 1] = __float_as_uint(v.y);
+                    }
+                }
+                tmem_st16(tcols(n) + 16 * c, r);
+            }
+            tmem_wait_st();
+            return __fadd_rn(__fadd_rn(ssp[0].x, ssp[0].y), __fadd_rn(ssp[1].x, ssp[1].y));
+        };
         // pass 1: as^2 sum over the warp's columns of (acc ws)^2, once block n's accumulator is full;
         // v = acc (ws g1) replaces the accumulator for pass 2
         auto pass1 = [&](int n) -> float {
@@ -373,7 +505,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             const float as = csta[(n & 3) * 32 + lane];
             return __fmul_rn(__fmul_rn(as, as), ss);
         };
+        auto pass1x = [&](int n) -> float {
+            if constexpr (PB) return pass1_pb(n);
+            else return pass1(n);
+        };
         auto release = [&](int n) {
+            if (PB) return;  // (per-block: the slots belong to the epilogue; the ring is released by pass 1)
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(tempty_bar(n % NACC));
@@ -384,7 +521,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             load_as(1);
             load_res(0);
             cp_async_wait_1();
-            const float s0 = pass1(0);
+            const float s0 = pass1x(0);
             if (ok) send(0, 0, make_float2(s0, 0.f));
         }
         for (int n = 0; n < ntl && ok && xok; n++) {
@@ -392,7 +529,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             const float s1 = recv(0, n).x;
             if (!xok) break;
             const float inv1 = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(s1, (float)D), p.eps)));
-            const float sr = __fmul_rn(csta[(n & 3) * 32 + lane], inv1);
+            const float sr = PB ? inv1 : __fmul_rn(csta[(n & 3) * 32 + lane], inv1);
             // pass 2: x = fma(v, as inv1, res) into the residual tiles; y = x g2 into the accumulator
             if (!__all_sync(0xffffffffu, mbar_wait(rb, rpar, p.status, E2C_ERR_WAIT_EPI))) {
                 ok = false;
@@ -442,7 +579,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 // block n+1's first pass and residual load while block n's second round travels
                 if (n + 1 < ntl) {
                     cp_async_wait_1();
-                    const float s0 = pass1(n + 1);
+                    const float s0 = pass1x(n + 1);
                     if (!ok) break;
                     send(0, n + 1, make_float2(s0, 0.f));
                     if (lane == 0) bulk_wait_read0();  // block n's x store has read the tiles
@@ -456,10 +593,20 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 // needs no clamp, and rint is the round-to-nearest-even of adding 1.5 2^23, whose low
                 // byte is q
                 const float inv2 = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t2.x, (float)D), p.eps)));
-                const float amax = __fmul_rn(t2.y, inv2);
-                const float s = t2.y > 0.f ? __fdiv_rn(127.0f, t2.y) : 0.f;
+                // the quantiser's max|y|: the row's (cluster), or per-block the CTA's 128 columns (the
+                // quadrant's four warps, whose round-1 partials this warp waits for too)
+                float mxy = t2.y;
+                if constexpr (PB) {
+                    xok = xok && __all_sync(0xffffffffu, mbar_wait(lbar(1, q), (uint32_t)(n & 1), p.status, E2C_ERR_WAIT_EPI));
+                    if (!xok) break;
+                    const float2 *xb = xl1b(n);
+                    mxy = fmaxf(fmaxf(xb[row].y, xb[BM + row].y), fmaxf(xb[2 * BM + row].y, xb[3 * BM + row].y));
+                }
+                const float amax = __fmul_rn(mxy, inv2);
+                const float s = mxy > 0.f ? __fdiv_rn(127.0f, mxy) : 0.f;
                 const int m = row0(n) + row;
-                if (rank == 0 && part == 0 && m < M) p.q8_scale[m] = amax > 0.f ? __fmul_rn(amax, 0x1.020408p-7f) : 1.0f;
+                if ((PB || rank == 0) && part == 0 && m < M)
+                    p.q8_scale[PB ? (size_t)m * ncl + rank : (size_t)m] = amax > 0.f ? __fmul_rn(amax, 0x1.020408p-7f) : 1.0f;
                 uint4 *qrow = reinterpret_cast<uint4 *>(p.q8 + (size_t)(m < M ? m : 0) * p.ldq + cl0);
 #pragma unroll
                 for (int c = 0; c < NCH; c++) {
@@ -498,7 +645,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 store_res(n);
                 if (n + 1 < ntl) {
                     cp_async_wait_1();
-                    const float s0 = pass1(n + 1);
+                    const float s0 = pass1x(n + 1);
                     if (!ok) break;
                     send(0, n + 1, make_float2(s0, 0.f));
                     if (lane == 0) bulk_wait_read0();
@@ -527,15 +674,15 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
 }
 
-template <int STG, int XMAX>
+template <int STG, int XMAX, bool PB>
 int launch_norm(const e2c_gemm_args *a, int ncl, bool quant, cudaStream_t st, int dev, int num_sms) {
     using L = Smem<STG, XMAX>;
     static E2cPerDev attr_set;                    // the shared-memory opt-in, per device
     static E2cPerDev max_clusters[2][MAXCL + 1];  // resident clusters per (quantise, width), per device
     if (!attr_set.get(dev)) {
-        if (cudaFuncSetAttribute(k_gemm_norm<true, STG, XMAX>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC) !=
+        if (cudaFuncSetAttribute(k_gemm_norm<true, STG, XMAX, PB>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC) !=
                 cudaSuccess ||
-            cudaFuncSetAttribute(k_gemm_norm<false, STG, XMAX>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC) !=
+            cudaFuncSetAttribute(k_gemm_norm<false, STG, XMAX, PB>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC) !=
                 cudaSuccess) {
             cudaGetLastError();
             e2c_set_msg("gemm_norm: cannot reserve %d bytes of shared memory", L::ALLOC);
@@ -563,7 +710,7 @@ int launch_norm(const e2c_gemm_args *a, int ncl, bool quant, cudaStream_t st, in
     cfg.stream = st;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    auto kern = quant ? k_gemm_norm<true, STG, XMAX> : k_gemm_norm<false, STG, XMAX>;
+    auto kern = quant ? k_gemm_norm<true, STG, XMAX, PB> : k_gemm_norm<false, STG, XMAX, PB>;
     int maxc = max_clusters[quant][ncl].get(dev);
     if (!maxc) {
         cfg.gridDim = dim3((unsigned)(ncl * (num_sms / ncl)));
@@ -602,5 +749,9 @@ extern "C" int e2c_gemm_norm(const e2c_gemm_args *a, void *stream) {
     }
     const bool quant = a->norm_g2 != nullptr;
     cudaStream_t st = (cudaStream_t)stream;
-    return ncl <= 6 ? launch_norm<4, 6>(a, ncl, quant, st, dev, num_sms) : launch_norm<3, MAXCL>(a, ncl, quant, st, dev, num_sms);
+    if (a->ablk != a->K)  // per-128-block activation scales
+        return ncl <= 6 ? launch_norm<4, 6, true>(a, ncl, quant, st, dev, num_sms)
+                        : launch_norm<3, MAXCL, true>(a, ncl, quant, st, dev, num_sms);
+    return ncl <= 6 ? launch_norm<4, 6, false>(a, ncl, quant, st, dev, num_sms)
+                    : launch_norm<3, MAXCL, false>(a, ncl, quant, st, dev, num_sms);
 }

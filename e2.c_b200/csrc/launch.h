@@ -38,7 +38,9 @@ enum {
     E2C_EPI_QKV = 4,   /* per-head RMSNorm (+gamma) + RoPE -> bf16 Q, K, V^T               */
     E2C_EPI_NORMADD = 5 /* y = gemm (never stored); x = rmsnorm(y) * g1 + res; res = x;
                           q = quantise(rmsnorm(x) * g2) per token (g2 NULL: res = rmsnorm(x) * gf).
-                          Whole rows per cluster of CTAs (N = 768: 6 x 128 columns) */,
+                          Whole rows per cluster of CTAs (N = 768: 6 x 128 columns). With 128-wide
+                          activation blocks: the per-block fold, and q per 128-column block with
+                          q8_scale [M][N/128] */,
     E2C_EPI_GELUQ = 6, /* GELU-gate as E2C_EPI_GELU, then the per-token quantiser of h over its
                           N/2 columns: int8 q8 [M][ldq] and q8_scale [M] (h itself is not stored).
                           Whole rows per cluster of N/256 CTAs (N = 2304: 9). With per-128-block

@@ -87,8 +87,8 @@ def test_encoder_matches_cpu_reference(e2c, of, syn, torch_cuda):
 def test_encoder_per_block_scales_matches_cpu_reference(e2c, of, syn, torch_cuda):
     """The reference engine's default recipe: activations quantised per 128-element block
     (E2_I8_BLOCK = 128, src/int8.h:61-70) in every layer. The GEMMs fold block by block, bit-exact;
-    the q|k|v GEMM finishes its heads (norm, RoPE) and the gate|up GEMM applies GELU-gate and h's
-    per-block quantiser in their epilogues."""
+    the q|k|v GEMM finishes its heads (norm, RoPE), o_proj and down apply the residual norms and
+    gate|up GELU-gate, each with a per-block quantiser, in their epilogues."""
     cfg = syn.EncoderConfig(n_layers=2, vocab=4096, max_seq=512)
     w = syn.encoder_weights(cfg, seed=79, ablk=128)
     rng = np.random.default_rng(5)
@@ -103,9 +103,9 @@ def test_encoder_per_block_scales_matches_cpu_reference(e2c, of, syn, torch_cuda
     cos = cosine_rows(got, want)
     assert cos.min() >= 0.9999, cos
     calls, kernels, _ = enc.stats()
-    # q|k|v with its finish, attention, ctx quant, o_proj + norms, down + norms (two kernels each),
-    # gate|up with its GELU-quantise epilogue, then the head
-    assert kernels == 1 + 8 * w.cfg.n_layers + 6
+    # q|k|v with its finish, attention, ctx quant, o_proj with the norms, gate|up with its
+    # GELU-quantise epilogue, down with the norms; then the head
+    assert kernels == 1 + 6 * w.cfg.n_layers + 6
 
 
 def test_encoder_graph_replay_and_device_api(e2c, syn, torch_cuda):

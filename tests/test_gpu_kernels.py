@@ -430,6 +430,54 @@ def test_gemm_norm_add_epilogue(e2c, of, torch_cuda, M, D, final):
         tie_tolerant_bytes(q.cpu().numpy(), np.clip(np.rint(pre), -127, 127).astype(np.int8), pre)
 
 
+@pytest.mark.parametrize("M,D,K,final", [(300, 768, 768, False), (4096, 768, 1152, False), (1000, 768, 768, True),
+                                         (517, 1024, 1024, False), (700, 512, 2048, False), (130, 128, 256, False),
+                                         (16384, 512, 512, False)])
+def test_gemm_norm_add_epilogue_per_block(e2c, of, torch_cuda, M, D, K, final):
+    """The residual norms fused into o_proj / down with per-128-block activation scales (e2.c's
+    default recipe): t is the per-block fold (bit-exact to the port's GEMM), x = rmsnorm(t) * g1 + res
+    becomes the residual, and rmsnorm(x) * g2 is quantised per 128-column block (scales [M][D/128]),
+    or rmsnorm(x) * gf is written after the last layer. Against fp64 of the same formula on the
+    bit-exact t; bytes within the tie rule. D = 1024 takes the three-stage kernel, 16384 rows wrap
+    the pipelined epilogue's slots many times."""
+    torch = torch_cuda
+    rng = np.random.default_rng(67 + M + K)
+    N = D
+    qa, a_s, w, ws = _gemm_inputs(rng, M, N, K, 128)
+    res0 = rng.standard_normal((M, N)).astype(np.float32)
+    g1 = (1 + 0.1 * rng.standard_normal(N)).astype(np.float32)
+    g2 = (1 + 0.1 * rng.standard_normal(N)).astype(np.float32)
+    eps = 1e-6
+    W = e2c.Weight(w=w, scale=ws)
+    res = dev(torch, res0)
+    q = torch.zeros((M, N), dtype=torch.int8, device="cuda")
+    qs = torch.zeros((M, N // 128), dtype=torch.float32, device="cuda")
+    gd1, gd2 = dev(torch, g1), dev(torch, g2)
+    a = _args_for(W, dev(torch, qa), dev(torch, a_s), M, K)
+    a.ablk, a.epi, a.eps = 128, e2c.EPI_NORMADD, eps
+    a.res, a.ldres, a.norm_g1 = res.data_ptr(), N, gd1.data_ptr()
+    if final:
+        a.norm_gf = gd2.data_ptr()
+    else:
+        a.norm_g2, a.q8, a.ldq, a.q8_scale = gd2.data_ptr(), q.data_ptr(), N, qs.data_ptr()
+    _launch(e2c, a, torch)
+    t = of.gemm_plain(qa, a_s, w, ws, 128).astype(np.float64)
+    inv1 = 1.0 / np.sqrt((t * t).mean(axis=1, keepdims=True) + eps)
+    x = t * inv1 * g1 + res0
+    inv2 = 1.0 / np.sqrt((x * x).mean(axis=1, keepdims=True) + eps)
+    z = x * inv2 * g2
+    got = res.cpu().numpy()
+    want = z if final else x
+    err = np.abs(got - want).max(axis=1) / np.abs(want).max(axis=1)
+    assert err.max() < 1e-5, f"residual off by {err.max()}"
+    if not final:
+        zb = z.reshape(M, N // 128, 128)
+        amax = np.abs(zb).max(axis=2, keepdims=True)
+        np.testing.assert_allclose(qs.cpu().numpy(), amax[:, :, 0] / 127.0, rtol=1e-5)
+        pre = (zb * (127.0 / amax)).reshape(M, N)
+        tie_tolerant_bytes(q.cpu().numpy(), np.clip(np.rint(pre), -127, 127).astype(np.int8), pre)
+
+
 def test_norm_quant_teacher_forced(e2c, of, torch_cuda):
     """The config-1 prologue (rmsnorm * gamma -> per-row quantise): bytes within the tie rule."""
     torch = torch_cuda
