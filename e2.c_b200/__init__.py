@@ -80,7 +80,7 @@ class GemmArgs(C.Structure):
                 ("rope_sin", C.c_void_p), ("ldrope", C.c_int), ("eps", C.c_float), ("res", C.c_void_p), ("ldres", C.c_int),
                 ("norm_g1", C.c_void_p), ("norm_g2", C.c_void_p), ("norm_gf", C.c_void_p), ("q8", C.c_void_p),
                 ("ldq", C.c_int), ("q8_scale", C.c_void_p), ("status", C.c_void_p), ("ws", C.c_void_p),
-                ("ws_bytes", C.c_size_t)]
+                ("ws_bytes", C.c_size_t), ("norm_ls", C.c_float)]
 
 
 EPI_F32, EPI_RESID, EPI_I32, EPI_GELU, EPI_QKV, EPI_NORMADD, EPI_GELUQ, EPI_QKVPB = 0, 1, 2, 3, 4, 5, 6, 7

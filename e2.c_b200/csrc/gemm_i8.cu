@@ -1319,13 +1319,16 @@ extern "C" int e2c_gemm(const e2c_gemm_args *a, void *stream) {
     case E2C_EPI_NORMADD: {
         // the residual norms in the epilogue: its own kernel (gemm_i8_norm.cu); with per-128-block
         // activation scales the int8 output is quantised per 128-column block (q8_scale [M][N/128])
+        // Three forms: q8 with norm_g2 (quantise rmsnorm(x) g2), q8 alone (quantise x), or norm_gf
+        // without q8 (res = rmsnorm(x) gf after the last layer).
         const int ncols = a->n1 - a->n0;
+        const bool quant = a->q8 != nullptr;
         if ((perblock && a->ablk != 128) || a->n0 != 0 || ncols % 128 || ncols / 128 > 8 || !a->res || !a->norm_g1 ||
-            (!a->norm_g2 && !a->norm_gf) ||
-            (a->norm_g2 && (!a->q8 || !a->q8_scale || a->ldq % 16 || ((uintptr_t)a->q8 & 15))) || a->ldres % 4 ||
-            ((uintptr_t)a->res & 15)) {
+            (quant ? (!a->q8_scale || a->ldq % 16 || ((uintptr_t)a->q8 & 15) || a->norm_gf) : !a->norm_gf || a->norm_g2) ||
+            a->ldres % 4 || ((uintptr_t)a->res & 15)) {
             e2c_set_msg("gemm: the norm epilogue needs per-row or 128-wide block scales, whole rows of 128 x (1..8) columns, a 16-byte "
-                        "aligned res, the norm gains and (with a second gain) 16-byte aligned int8 rows and their scales");
+                        "aligned res, the first gain, and either 16-byte aligned int8 rows with their scales (and "
+                        "optionally a second gain) or a final gain");
             return -1;
         }
         return e2c_gemm_norm(a, stream);

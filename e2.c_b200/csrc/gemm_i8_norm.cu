@@ -4,6 +4,9 @@
 //   x  = rmsnorm(t) * g1 + res ;  res <- x                   e2.c src/text.c:947,954 (norm_add)
 //   q8 = quantise(rmsnorm(x) * g2) per token                 the next projection's int8 input
 //   or, after the last layer (g2 NULL):  res <- rmsnorm(x) * gf
+//   or, with int8 rows but no g2:          q8 = quantise(x)    (e2.c's text tower, after the FFN)
+// with x optionally multiplied by a layer scalar after the residual add (the text tower's
+// per-layer-embedding step, src/text.c:966-975).
 //
 // with rmsnorm(v) = v / sqrt(mean(v^2) + eps) over the D = 128 x (1..8) columns of a row
 // (src/kernels.c:144-171) and the per-token quantiser of src/int8.c:178-209. The GEMM output t
@@ -292,13 +295,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         const uint32_t resb_s = smem_u32(resb);
         const uint32_t rb = rbar(warp - 2);
         {
+            // (quantising x itself: g2 = 1)
             const float *gb = quant ? p.norm_g2 : p.norm_gf;
             for (int j = lane; j < QCOLS; j += 32) {
                 const float w = __ldg(p.w_scale + p.n0 + cl0 + j);
                 cst[j] = w;
                 // per-block: the gain alone (t is scaled by the fold)
                 cst[C_WG1 + j] = PB ? __ldg(p.norm_g1 + cl0 + j) : __fmul_rn(w, __ldg(p.norm_g1 + cl0 + j));
-                cst[C_G2 + j] = __ldg(gb + cl0 + j);
+                cst[C_G2 + j] = gb ? __ldg(gb + cl0 + j) : 1.0f;
             }
             __syncwarp();
         }
@@ -530,6 +534,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             if (!xok) break;
             const float inv1 = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(s1, (float)D), p.eps)));
             const float sr = PB ? inv1 : __fmul_rn(csta[(n & 3) * 32 + lane], inv1);
+            // the layer scalar after the residual add (text tower's per-layer-embedding step)
+            const bool ls_on = p.norm_ls != 0.f && p.norm_ls != 1.f;
+            const float2 ls2 = make_float2(p.norm_ls, p.norm_ls);
             // pass 2: x = fma(v, as inv1, res) into the residual tiles; y = x g2 into the accumulator
             if (!__all_sync(0xffffffffu, mbar_wait(rb, rpar, p.status, E2C_ERR_WAIT_EPI))) {
                 ok = false;
@@ -549,10 +556,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 for (int k = 0; k < 4; k++) {
                     float4 *p4 = rp(c, k);
                     const float4 r4 = *p4;
-                    const float2 xa = fma2_rn(make_float2(__uint_as_float(r[4 * k]), __uint_as_float(r[4 * k + 1])), sr2,
-                                              make_float2(r4.x, r4.y));
-                    const float2 xb = fma2_rn(make_float2(__uint_as_float(r[4 * k + 2]), __uint_as_float(r[4 * k + 3])), sr2,
-                                              make_float2(r4.z, r4.w));
+                    float2 xa = fma2_rn(make_float2(__uint_as_float(r[4 * k]), __uint_as_float(r[4 * k + 1])), sr2,
+                                        make_float2(r4.x, r4.y));
+                    float2 xb = fma2_rn(make_float2(__uint_as_float(r[4 * k + 2]), __uint_as_float(r[4 * k + 3])), sr2,
+                                        make_float2(r4.z, r4.w));
+                    if (ls_on) {
+                        xa = mul2_rn(xa, ls2);
+                        xb = mul2_rn(xb, ls2);
+                    }
                     *p4 = make_float4(xa.x, xa.y, xb.x, xb.y);
                     s2p[0] = fma2_rn(xa, xa, s2p[0]);
                     s2p[1] = fma2_rn(xb, xb, s2p[1]);
@@ -592,7 +603,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 // y = x g2, scale = amax / 127, q = rint(z 127 / amax) = rint(y 127 / max|y|); |q| <= 127
                 // needs no clamp, and rint is the round-to-nearest-even of adding 1.5 2^23, whose low
                 // byte is q
-                const float inv2 = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t2.x, (float)D), p.eps)));
+                // (quantising x itself: no second norm)
+                const float inv2 = p.norm_g2 ? __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t2.x, (float)D), p.eps))) : 1.0f;
                 // the quantiser's max|y|: the row's (cluster), or per-block the CTA's 128 columns (the
                 // quadrant's four warps, whose round-1 partials this warp waits for too)
                 float mxy = t2.y;
@@ -747,7 +759,7 @@ extern "C" int e2c_gemm_norm(const e2c_gemm_args *a, void *stream) {
         e2c_set_msg("gemm_norm: rows of 128 x (1..8) columns starting at column 0");
         return -1;
     }
-    const bool quant = a->norm_g2 != nullptr;
+    const bool quant = a->q8 != nullptr;
     cudaStream_t st = (cudaStream_t)stream;
     if (a->ablk != a->K)  // per-128-block activation scales
         return ncl <= 6 ? launch_norm<4, 6, true>(a, ncl, quant, st, dev, num_sms)

@@ -95,6 +95,9 @@ typedef struct {
      * Every launch that completes leaves it zero. */
     int *ws;
     size_t ws_bytes;
+    /* NORMADD: x is multiplied by norm_ls after the residual add (0: no scaling); with q8 given but
+     * neither norm_g2 nor norm_gf, x itself is quantised (g2 = 1, no second norm) */
+    float norm_ls;
 } e2c_gemm_args;
 
 int e2c_gemm(const e2c_gemm_args *a, void *stream);

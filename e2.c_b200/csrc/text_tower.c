@@ -19,8 +19,9 @@
  *   GEMM embed_proj -> masked mean pool -> L2
  *
  * 14 kernels per layer, 5 around them; one fewer each where gate|up applies GELU-gate and h's
- * per-block quantiser in its epilogue, and where the q|k|v GEMM finishes its heads of 256 in its
- * epilogue. int8 activations alternate between qa (inputs of the
+ * per-block quantiser in its epilogue, where the q|k|v GEMM finishes its heads of 256 in its
+ * epilogue, and for each of o_proj, down and the PLE projection with the residual norms in its
+ * epilogue (per-block mode: 9 on layers with heads of 256, 10 on the others). int8 activations alternate between qa (inputs of the
  * hidden-wide GEMMs) and qb (ctx, h and the PLE gate's output), so a row kernel never writes the
  * buffer the GEMM before it still reads.
  */
@@ -52,6 +53,8 @@ struct e2cuda_text {
     int L, D, I, P, H, V, DO, max_seq, ablk, max_tokens;
     int fused_gelu; /* per-block gate|up GEMM with GELU-gate + quantiser epilogue (E2C_FUSED_GELU=0: off) */
     int fused_qkv;  /* per-block q|k|v GEMM with the finish in its epilogue, heads of 256 (E2C_FUSED_QKV=0: off) */
+    int fused_norm; /* per-block o_proj / down / PLE projection with the residual norms in the epilogue
+                       (E2C_FUSED_NORM=0: off) */
     float eps, embed_scale, ple_scale;
     tt_layer layer[TT_MAX_LAYERS];
     e2cuda_w8 ple_model, embed_proj;
@@ -201,9 +204,10 @@ e2cuda_text *e2cuda_text_create(const e2cuda_text_desc *d, int max_tokens) {
     t->max_seq = d->max_seq;
     t->ablk = ablk;
     {
-        const char *fg = getenv("E2C_FUSED_GELU"), *fq = getenv("E2C_FUSED_QKV");
+        const char *fg = getenv("E2C_FUSED_GELU"), *fq = getenv("E2C_FUSED_QKV"), *fz = getenv("E2C_FUSED_NORM");
         t->fused_gelu = ablk == 128 && !(fg && fg[0] == '0');
         t->fused_qkv = ablk == 128 && !(fq && fq[0] == '0');
+        t->fused_norm = ablk == 128 && d->hidden / 128 <= 8 && !(fz && fz[0] == '0');
     }
     t->max_tokens = max_tokens;
     t->eps = d->eps;
@@ -314,6 +318,25 @@ static int gemm_f32(const e2cuda_w8 *w, const int8_t *qa, const float *qs, int M
     return e2c_gemm(&a, st);
 }
 
+/* the GEMM with the residual norms in its epilogue: x = (rmsnorm(y) g1 + res) ls -> res, then the
+ * int8 rows of rmsnorm(x) g2 (or of x itself, g2 NULL) into qa / qas */
+static int gemm_norm(const e2cuda_text *t, const e2cuda_w8 *w, const int8_t *qin, const float *qsin, int M, int ablk,
+                     const float *g1, float ls, const float *g2, cudaStream_t st) {
+    e2c_gemm_args a;
+    e2cu_gemm_args(&a, w, qin, qsin, M, ablk);
+    a.epi = E2C_EPI_NORMADD;
+    a.res = t->res;
+    a.ldres = t->D;
+    a.norm_g1 = g1;
+    a.norm_g2 = g2;
+    a.norm_ls = ls;
+    a.q8 = t->qa;
+    a.ldq = t->D;
+    a.q8_scale = t->qas;
+    a.eps = t->eps;
+    return e2c_gemm(&a, st);
+}
+
 /* queue one pass over B sequences of S tokens already in t->ids / t->valid; returns kernels queued */
 static int forward(e2cuda_text *t, int B, int S, int has_valid, cudaStream_t st) {
     const int M = B * S, D = t->D, I = t->I, P = t->P, L = t->L, H = t->H;
@@ -361,9 +384,14 @@ static int forward(e2cuda_text *t, int B, int S, int has_valid, cudaStream_t st)
         Q(e2c_attention_win(t->Q, t->K, t->Vt, ldvt, valid, t->ctx, B, S, H, kv, hd, 1.0f, y->window, t->status, st),
           "text attention");
         Q(e2c_quantize(t->ctx, qd, t->qb, qd, t->qbs, M, qd, ab_q, -INFINITY, INFINITY, 0, st), "text ctx quant");
-        Q(gemm_f32(&y->o, t->qb, t->qbs, M, ab_q, t->tmp, D, st), "text o_proj");
-        Q(e2c_tt_norm_add(t->tmp, t->res, lnorm(t, l, 1), 1.0f, lnorm(t, l, 2), t->eps, t->qa, t->qas, M, D, ab, st),
-          "text post-attention norms");
+        if (t->fused_norm) {
+            Q(gemm_norm(t, &y->o, t->qb, t->qbs, M, ab_q, lnorm(t, l, 1), 1.0f, lnorm(t, l, 2), st),
+              "text o_proj + post-attention norms");
+        } else {
+            Q(gemm_f32(&y->o, t->qb, t->qbs, M, ab_q, t->tmp, D, st), "text o_proj");
+            Q(e2c_tt_norm_add(t->tmp, t->res, lnorm(t, l, 1), 1.0f, lnorm(t, l, 2), t->eps, t->qa, t->qas, M, D, ab, st),
+              "text post-attention norms");
+        }
         if (t->fused_gelu) {
             e2c_gemm_args a;
             e2cu_gemm_args(&a, &y->gu, t->qa, t->qas, M, ab);
@@ -376,17 +404,25 @@ static int forward(e2cuda_text *t, int B, int S, int has_valid, cudaStream_t st)
             Q(gemm_f32(&y->gu, t->qa, t->qas, M, ab, t->yf, 2 * I, st), "text gate|up");
             Q(e2c_gelu_mul_quant(t->yf, 2 * I, I, t->qb, t->qbs, M, ab_i, st), "text gelu quant");
         }
-        Q(gemm_f32(&y->d, t->qb, t->qbs, M, ab_i, t->tmp, D, st), "text down");
-        Q(e2c_tt_norm_add(t->tmp, t->res, lnorm(t, l, 3), 1.0f, NULL, t->eps, t->qa, t->qas, M, D, ab, st),
-          "text post-ffn norm");
+        if (t->fused_norm) {
+            Q(gemm_norm(t, &y->d, t->qb, t->qbs, M, ab_i, lnorm(t, l, 3), 1.0f, NULL, st), "text down + post-ffn norm");
+        } else {
+            Q(gemm_f32(&y->d, t->qb, t->qbs, M, ab_i, t->tmp, D, st), "text down");
+            Q(e2c_tt_norm_add(t->tmp, t->res, lnorm(t, l, 3), 1.0f, NULL, t->eps, t->qa, t->qas, M, D, ab, st),
+              "text post-ffn norm");
+        }
         Q(gemm_f32(&y->pg, t->qa, t->qas, M, ab, t->yf, P, st), "text PLE gate");
         Q(e2c_tt_gate_quant(t->yf, P, t->ple + (size_t)l * P, L * P, t->ple_scale, t->ple_norm, t->eps, P, t->qb, t->qbs, M,
                             ab_p, st),
           "text PLE gate quant");
-        Q(gemm_f32(&y->pp, t->qb, t->qbs, M, ab_p, t->tmp, D, st), "text PLE projection");
-        Q(e2c_tt_norm_add(t->tmp, t->res, lnorm(t, l, 4), y->ls, l + 1 < L ? lnorm(t, l + 1, 0) : t->final_norm, t->eps,
-                          t->qa, t->qas, M, D, ab, st),
-          "text PLE norms");
+        const float *gnext = l + 1 < L ? lnorm(t, l + 1, 0) : t->final_norm;
+        if (t->fused_norm) {
+            Q(gemm_norm(t, &y->pp, t->qb, t->qbs, M, ab_p, lnorm(t, l, 4), y->ls, gnext, st), "text PLE projection + norms");
+        } else {
+            Q(gemm_f32(&y->pp, t->qb, t->qbs, M, ab_p, t->tmp, D, st), "text PLE projection");
+            Q(e2c_tt_norm_add(t->tmp, t->res, lnorm(t, l, 4), y->ls, gnext, t->eps, t->qa, t->qas, M, D, ab, st),
+              "text PLE norms");
+        }
     }
     Q(gemm_f32(&t->embed_proj, t->qa, t->qas, M, ab, t->yf, t->DO, st), "text embed_proj");
     Q(e2c_meanpool(t->yf, valid, t->pooled, B, S, t->DO, st), "text pool");

@@ -430,16 +430,19 @@ def test_gemm_norm_add_epilogue(e2c, of, torch_cuda, M, D, final):
         tie_tolerant_bytes(q.cpu().numpy(), np.clip(np.rint(pre), -127, 127).astype(np.int8), pre)
 
 
-@pytest.mark.parametrize("M,D,K,final", [(300, 768, 768, False), (4096, 768, 1152, False), (1000, 768, 768, True),
-                                         (517, 1024, 1024, False), (700, 512, 2048, False), (130, 128, 256, False),
-                                         (16384, 512, 512, False)])
-def test_gemm_norm_add_epilogue_per_block(e2c, of, torch_cuda, M, D, K, final):
+@pytest.mark.parametrize("M,D,K,mode", [(300, 768, 768, "g2"), (4096, 768, 1152, "g2"), (1000, 768, 768, "final"),
+                                        (517, 1024, 1024, "g2"), (700, 512, 2048, "x"), (130, 128, 256, "g2"),
+                                        (16384, 512, 512, "ls"), (1000, 512, 1024, "x")])
+def test_gemm_norm_add_epilogue_per_block(e2c, of, torch_cuda, M, D, K, mode):
     """The residual norms fused into o_proj / down with per-128-block activation scales (e2.c's
     default recipe): t is the per-block fold (bit-exact to the port's GEMM), x = rmsnorm(t) * g1 + res
-    becomes the residual, and rmsnorm(x) * g2 is quantised per 128-column block (scales [M][D/128]),
-    or rmsnorm(x) * gf is written after the last layer. Against fp64 of the same formula on the
-    bit-exact t; bytes within the tie rule. D = 1024 takes the three-stage kernel, 16384 rows wrap
-    the pipelined epilogue's slots many times."""
+    (times the layer scalar in mode "ls", as e2.c's text tower's per-layer-embedding step) becomes the
+    residual, and rmsnorm(x) * g2 is quantised per 128-column block (scales [M][D/128]); mode "x"
+    quantises x itself (the text tower after its FFN), "final" writes rmsnorm(x) * gf. Against fp64
+    of the same formula on the bit-exact t; bytes within the tie rule. D = 1024 takes the three-stage
+    kernel, 16384 rows wrap the pipelined epilogue's slots many times."""
+    final = mode == "final"
+    ls = 0.6875 if mode == "ls" else 1.0
     torch = torch_cuda
     rng = np.random.default_rng(67 + M + K)
     N = D
@@ -454,18 +457,20 @@ def test_gemm_norm_add_epilogue_per_block(e2c, of, torch_cuda, M, D, K, final):
     qs = torch.zeros((M, N // 128), dtype=torch.float32, device="cuda")
     gd1, gd2 = dev(torch, g1), dev(torch, g2)
     a = _args_for(W, dev(torch, qa), dev(torch, a_s), M, K)
-    a.ablk, a.epi, a.eps = 128, e2c.EPI_NORMADD, eps
+    a.ablk, a.epi, a.eps, a.norm_ls = 128, e2c.EPI_NORMADD, eps, ls
     a.res, a.ldres, a.norm_g1 = res.data_ptr(), N, gd1.data_ptr()
     if final:
         a.norm_gf = gd2.data_ptr()
     else:
-        a.norm_g2, a.q8, a.ldq, a.q8_scale = gd2.data_ptr(), q.data_ptr(), N, qs.data_ptr()
+        a.q8, a.ldq, a.q8_scale = q.data_ptr(), N, qs.data_ptr()
+        if mode != "x":
+            a.norm_g2 = gd2.data_ptr()
     _launch(e2c, a, torch)
     t = of.gemm_plain(qa, a_s, w, ws, 128).astype(np.float64)
     inv1 = 1.0 / np.sqrt((t * t).mean(axis=1, keepdims=True) + eps)
-    x = t * inv1 * g1 + res0
+    x = (t * inv1 * g1 + res0) * ls
     inv2 = 1.0 / np.sqrt((x * x).mean(axis=1, keepdims=True) + eps)
-    z = x * inv2 * g2
+    z = x if mode == "x" else x * inv2 * g2
     got = res.cpu().numpy()
     want = z if final else x
     err = np.abs(got - want).max(axis=1) / np.abs(want).max(axis=1)
