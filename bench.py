@@ -717,13 +717,17 @@ def config1(args) -> int:
 
 def text_pass_work(B: int, S: int, cfg) -> list:
     """(kernel, int8 ops, bf16 flops, algorithmic bytes) of every launch of one text-tower pass over
-    B sequences of S tokens (activations per 128-block; every GEMM writes fp32 except gate|up, which
-    writes h quantised per 128-block, and q|k|v on the layers with heads of 256, which writes bf16
-    Q, K and V^T)."""
+    B sequences of S tokens (activations per 128-block; the PLE gate, the PLE projection of the
+    embeddings, q|k|v on the layers with heads of 512 and embed_proj write fp32; gate|up writes h
+    quantised per 128-block, q|k|v on the layers with heads of 256 bf16 Q, K and V^T, and o_proj,
+    down and the PLE projection the residual and the next int8 rows)."""
     M, D, I, P, L, H, DO = B * S, cfg.hidden, cfg.intermediate, cfg.ple_dim, cfg.n_layers, cfg.n_heads, cfg.out_dim
 
     def gemm(name, K, N):
         return (name, 2.0 * M * K * N, 0.0, M * K + 4 * M * K / 128 + N * K + 4 * N + 4 * M * N)
+
+    def gemm_norm(name, K):  # the residual norms in the epilogue: res read and written, int8 rows + scales
+        return (name, 2.0 * M * K * D, 0.0, M * K + 4 * M * K / 128 + D * K + 12 * D + 8 * M * D + M * D + 4 * M * D / 128)
 
     w = [("embed", 0, 0, 4 * M + 2 * M * D + 4 * M * D + 2 * (M * D + 4 * M * D / 128)), gemm("ple_proj_model", D, L * P)]
     for l in range(L):
@@ -735,13 +739,11 @@ def text_pass_work(B: int, S: int, cfg) -> list:
         else:
             w += [gemm("qkv", D, nqkv), ("qkv_post", 0, 0, 4 * M * nqkv + 2 * M * nqkv)]
         w += [("attention", 0, 4.0 * M * keys * hd * H, 2 * M * nqkv + 4 * M * qd),
-              ("quantize_ctx", 0, 0, 4 * M * qd + M * qd + 4 * M * qd / 128), gemm("o_proj", qd, D),
-              ("norm_add", 0, 0, 13 * M * D + 4 * M * D / 128),
+              ("quantize_ctx", 0, 0, 4 * M * qd + M * qd + 4 * M * qd / 128), gemm_norm("o_proj_norm", qd),
               ("gate_up_gelu_quant", 2.0 * M * D * 2 * I, 0.0,
-               M * D + 4 * M * D / 128 + 2 * I * D + 8 * I + M * I + 4 * M * I / 128), gemm("down", I, D),
-              ("norm_add", 0, 0, 13 * M * D + 4 * M * D / 128), gemm("ple_gate", D, P),
-              ("ple_gate_quant", 0, 0, 8 * M * P + M * P + 4 * M * P / 128), gemm("ple_proj", P, D),
-              ("norm_add", 0, 0, 13 * M * D + 4 * M * D / 128)]
+               M * D + 4 * M * D / 128 + 2 * I * D + 8 * I + M * I + 4 * M * I / 128), gemm_norm("down_norm", I),
+              gemm("ple_gate", D, P), ("ple_gate_quant", 0, 0, 8 * M * P + M * P + 4 * M * P / 128),
+              gemm_norm("ple_proj_norm", P)]
     w += [gemm("embed_proj", D, DO), ("meanpool", 0, 0, 4 * M * DO), ("l2norm", 0, 0, 8 * B * DO)]
     return w
 
