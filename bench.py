@@ -634,7 +634,7 @@ def config0(args) -> int:
                           "E2_I8_BLOCK=768) over its pool, best of 5 after 2 warm-ups", **cpu_info(nthreads))
     print(json.dumps({"metric": "config-0 quantised linear layer time", "value": ms * 1e3, "unit": "us",
                       "higher_is_better": False, "steps": args.steps, "dtype": "int8",
-                      "data": "synthetic (seeded, BASELINE config 0)",
+                      "data": "synthetic (seeded, benchmark config 0)",
                       "config": {"workload": "config 0: quantise X [512][768] + W8A8 GEMM -> fp32 [512][1152], per-row scales",
                                  "l2": "flushed before every step", "kernels_per_step": 2},
                       "roofline": _roof(ops, nbytes, ms), "algorithmic_bytes": nbytes, "ops": ops,
@@ -705,7 +705,7 @@ def config1(args) -> int:
                    **cpu_info(nthreads))
     print(json.dumps({"metric": "config-1 int8 FFN block time", "value": ms * 1e3, "unit": "us",
                       "higher_is_better": False, "steps": args.steps, "dtype": "int8",
-                      "data": "synthetic (seeded, BASELINE config 1)",
+                      "data": "synthetic (seeded, benchmark config 1)",
                       "config": {"workload": "config 1: FFN block, M=4096, D=768, I=1152, per-token scales",
                                  "l2": "flushed before every step", "kernels_per_step": 3},
                       "roofline": _roof(ops, nbytes, ms), "algorithmic_bytes": nbytes, "ops": ops,
