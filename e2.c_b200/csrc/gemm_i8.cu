@@ -1245,6 +1245,22 @@ extern "C" int e2c_gemm(const e2c_gemm_args *a, void *stream) {
         // CTAs per SM: the next launch's weight tiles are requested while this one finishes,
         // which hides the fixed costs a chain of short launches pays one after another.
         if (e2c_pdl_on() && a->M <= 32) {
+            // Up to K = 4096 the co-resident split-K kernel, whose partials are reduced in a
+            // cluster's shared memory rather than through the workspace, measured faster in a chain
+            // (2048 x 8192 at M = 1: 6.45 against 6.84 us); deeper K balances better streamed
+            // (8192 x 2048: 7.07 against 8.32 us). E2C_PDL_SPLITK=0 keeps the streaming kernel.
+            static int splitk = -1;
+            if (splitk < 0) {
+                const char *v = getenv("E2C_PDL_SPLITK");
+                splitk = !(v && v[0] == '0');
+            }
+            if (splitk && a->K <= 4096) {
+                const int rc = e2c_gemm_splitk_co(a, stream);
+                if (rc != -1) {
+                    g_last_kernel = "splitk_coresident";
+                    return rc;
+                }
+            }
             g_last_kernel = "stream_coresident";
             return e2c_gemm_stream(a, stream);
         }

@@ -16,6 +16,13 @@
 //
 // Warps: 0 TMA producer, 1 TMEM owner + MMA issuer, 2..5 TMEM -> shared partials and the reduction.
 // Every wait is bounded; no TMA load uses multicast.
+//
+// The co-resident variant (CO, up to 32 rows, BN 128) keeps its stages in under half of an SM's
+// shared memory and is launched with at most one CTA per SM, so under programmatic dependent launch
+// the next GEMM's CTAs become resident beside this one's. Its producer requests the first stages'
+// weight tiles before griddepcontrol.wait (the weight is never written by the stream's kernels):
+// they stream while the previous kernel finishes; the activation tiles, the scales and the output
+// wait for it.
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <math.h>
@@ -36,11 +43,12 @@ constexpr int NTHREADS = 192;
 // shared memory: a pool for the stages (and, once the MMAs are done, the partials), then barriers.
 // The MMA reads 128 rows of A from a stage's A base; past the rows a packed stage holds it reads
 // whatever follows (never used), so the pool keeps 16 KB of slack past the last stage.
-constexpr int POOL = 200 * 1024;
+constexpr int POOL_1 = 200 * 1024, POOL_CO = 108 * 1024;
+constexpr int CO_ROWS = 32;  // rows the co-resident variant takes (its partials: CO_ROWS x BN int32)
 constexpr int A_FULL = BM * BK;
-constexpr int BAR_OFF = POOL;
 constexpr int NBAR = 2 * MAXST + 1;  // full[MAXST], empty[MAXST], tfull; then the TMEM address slot
-constexpr int SMEM_ALLOC = BAR_OFF + NBAR * 8 + 16 + 1024;
+__host__ __device__ constexpr int pool_of(bool co) { return co ? POOL_CO : POOL_1; }
+__host__ __device__ constexpr int smem_alloc(bool co) { return pool_of(co) + NBAR * 8 + 16 + 1024; }
 
 E2C_DEV uint32_t cluster_nctarank() {
     uint32_t r;
@@ -63,15 +71,16 @@ E2C_DEV uint32_t red_off(int row, int chunk) {
 }
 
 // stages that fit for a packed stage of `stage_bytes`
-__host__ __device__ constexpr int stages_for(int stage_bytes) {
-    return (POOL - A_FULL) / stage_bytes < MAXST ? (POOL - A_FULL) / stage_bytes : MAXST;
+__host__ __device__ constexpr int stages_for(int stage_bytes, bool co) {
+    return (pool_of(co) - A_FULL) / stage_bytes < MAXST ? (pool_of(co) - A_FULL) / stage_bytes : MAXST;
 }
 
-template <int BN>
-__global__ void __launch_bounds__(NTHREADS, 1)
+template <int BN, bool CO>
+__global__ void __launch_bounds__(NTHREADS, CO ? 2 : 1)
     k_gemm_splitk(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                   const e2c_gemm_args p, const int a_rows) {
-    static_assert(BM * BN * 4 <= POOL, "partials fit in the pool");
+    constexpr int POOL = pool_of(CO), BAR_OFF = POOL;
+    static_assert((CO ? CO_ROWS : BM) * BN * 4 <= POOL, "partials fit in the pool");
     extern __shared__ uint8_t smem_raw[];
     griddep_launch_dependents();
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
@@ -94,7 +103,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     const int nkb = kb1 > kb0 ? kb1 - kb0 : 0;  // k-blocks of this CTA (the last rank may have none)
     const int a_bytes = a_rows * BK;            // a multiple of 1024: a_rows is a multiple of 8
     const int stage_bytes = a_bytes + BN * BK;
-    const int nst = stages_for(stage_bytes);
+    const int nst = stages_for(stage_bytes, CO);
 
     if (warp == 0 && lane == 0) {
         for (int s = 0; s < MAXST; s++) {
@@ -114,14 +123,30 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    griddep_wait();  // the stream's earlier kernels are done with what this one reads and writes
+    // the stream's earlier kernels are done with what this one reads and writes (co-resident: each
+    // role waits where it first touches the stream's data)
+    if constexpr (!CO) griddep_wait();
     const uint32_t tmem = *tmem_slot;
     bool ok = true;
 
     if (warp == 0) {
         // ---------------------------------------------------------------- TMA producer
         if (elect_one()) {
-            for (int i = 0; i < nkb; i++) {
+            int i0 = 0;
+            if constexpr (CO) {
+                // the first stages' weight tiles before the wait, their activation tiles after it
+                const int pre = nkb < nst ? nkb : nst;
+                for (int i = 0; i < pre; i++) {
+                    const uint32_t sa = sbase + i * stage_bytes, sb = sa + a_bytes;
+                    mbar_arrive_expect_tx(full_bar(i), (uint32_t)stage_bytes);
+                    tma_load_2d(sb, &tmB, (kb0 + i) * BK, c0, full_bar(i));
+                }
+                griddep_wait();
+                for (int i = 0; i < pre; i++)
+                    tma_load_2d(sbase + i * stage_bytes, &tmA, (kb0 + i) * BK, mt, full_bar(i));
+                i0 = pre;
+            }
+            for (int i = i0; i < nkb; i++) {
                 const int s = i % nst;
                 const uint32_t par = (uint32_t)((i / nst) & 1);
                 if (!mbar_wait(empty_bar(s), par ^ 1u, p.status, E2C_ERR_WAIT_PRODUCER)) break;
@@ -150,6 +175,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         }
     } else {
         // ---------------------------------------------------------------- TMEM -> shared partials
+        if constexpr (CO) griddep_wait();  // (the reduction reads the scales and writes y)
         const int q = warp & 3;
         const int row = q * 32 + lane;
         if (mt + q * 32 < p.M) {  // warp-uniform: this quadrant holds rows of the output
@@ -235,15 +261,16 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 }
 
 // the shared-memory and cluster-size opt-ins on the current device: 0 unset, 1 ok, -1 failed
-template <int BN>
+template <int BN, bool CO>
 bool configure() {
     static E2cPerDev state;
     const int dev = e2c_device();
     if (dev < 0) return false;
     int s = state.get(dev);
     if (!s) {
-        s = (cudaFuncSetAttribute(k_gemm_splitk<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_ALLOC) == cudaSuccess &&
-             cudaFuncSetAttribute(k_gemm_splitk<BN>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess)
+        s = (cudaFuncSetAttribute(k_gemm_splitk<BN, CO>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_alloc(CO)) ==
+                 cudaSuccess &&
+             cudaFuncSetAttribute(k_gemm_splitk<BN, CO>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess)
                 ? 1
                 : -1;
         if (s < 0) cudaGetLastError();
@@ -253,12 +280,12 @@ bool configure() {
 }
 
 // clusters of S CTAs the current device holds at once (0: none), per device and S
-template <int BN>
+template <int BN, bool CO>
 int clusters(int S) {
     static E2cPerDev cache[5];  // value + 1; 0 = not yet asked
     int i = 0;
     while ((2 << i) < S && i < 4) i++;
-    if (S < 2 || S > 16 || (2 << i) != S || !configure<BN>()) return 0;
+    if (S < 2 || S > 16 || (2 << i) != S || !configure<BN, CO>()) return 0;
     const int dev = e2c_device();
     const int c = cache[i].get(dev);
     if (c > 0) return c - 1;
@@ -271,11 +298,11 @@ int clusters(int S) {
     at[0].val.clusterDim.z = 1;
     cfg.gridDim = dim3((unsigned)S);
     cfg.blockDim = dim3(NTHREADS);
-    cfg.dynamicSmemBytes = SMEM_ALLOC;
+    cfg.dynamicSmemBytes = smem_alloc(CO);
     cfg.attrs = at;
     cfg.numAttrs = 1;
     int n = 0;
-    if (cudaOccupancyMaxActiveClusters(&n, k_gemm_splitk<BN>, &cfg) != cudaSuccess || n < 0) {
+    if (cudaOccupancyMaxActiveClusters(&n, k_gemm_splitk<BN, CO>, &cfg) != cudaSuccess || n < 0) {
         cudaGetLastError();
         n = 0;
     }
@@ -283,10 +310,10 @@ int clusters(int S) {
     return n;
 }
 
-template <int BN>
+template <int BN, bool CO>
 int launch_bn(const e2c_gemm_args *a, int S, cudaStream_t st) {
-    if (!configure<BN>()) {
-        e2c_set_msg("gemm_splitk: cannot configure the kernel (%d bytes of shared memory, clusters of 16)", SMEM_ALLOC);
+    if (!configure<BN, CO>()) {
+        e2c_set_msg("gemm_splitk: cannot configure the kernel (%d bytes of shared memory, clusters of 16)", smem_alloc(CO));
         return -2;
     }
     // A: as many rows as the output tile has (rounded up to 8); the MMA's other rows are never read
@@ -307,11 +334,11 @@ int launch_bn(const e2c_gemm_args *a, int S, cudaStream_t st) {
     attr_c[0].val.clusterDim.z = 1;
     cfg.gridDim = dim3((unsigned)(tiles * S));
     cfg.blockDim = dim3(NTHREADS);
-    cfg.dynamicSmemBytes = SMEM_ALLOC;
+    cfg.dynamicSmemBytes = smem_alloc(CO);
     cfg.stream = st;
     cfg.attrs = attr_c;
     cfg.numAttrs = e2c_pdl_attr(attr_c, 1);
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, k_gemm_splitk<BN>, ta, tb, *a, a_rows);
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, k_gemm_splitk<BN, CO>, ta, tb, *a, a_rows);
     if (e != cudaSuccess) {
         e2c_set_msg("gemm_splitk launch: %s", cudaGetErrorString(e));
         return -2;
@@ -331,7 +358,7 @@ extern "C" int e2c_gemm_splitk_plan(const e2c_gemm_args *a, int num_sms, int *bn
     for (int w : {256, 128}) {
         const long tiles = mtiles * ((a->n1 - a->n0 + w - 1) / w);
         for (int s2 = 2; s2 <= 16 && s2 <= nk && tiles * s2 <= num_sms; s2 *= 2) {
-            const int c = w == 256 ? clusters<256>(s2) : clusters<128>(s2);
+            const int c = w == 256 ? clusters<256, false>(s2) : clusters<128, false>(s2);
             if (c >= tiles && tiles * s2 > best) {
                 best = (int)(tiles * s2);
                 *bn = w;
@@ -348,5 +375,21 @@ extern "C" int e2c_gemm_splitk(const e2c_gemm_args *a, int bn, int S, void *stre
         e2c_set_msg("gemm_splitk: per-row scales, the F32 or residual epilogue, BN 128 or 256, a cluster of 2..16");
         return -1;
     }
-    return bn == 256 ? launch_bn<256>(a, S, (cudaStream_t)stream) : launch_bn<128>(a, S, (cudaStream_t)stream);
+    return bn == 256 ? launch_bn<256, false>(a, S, (cudaStream_t)stream) : launch_bn<128, false>(a, S, (cudaStream_t)stream);
+}
+
+// The co-resident variant for up to 32 rows: BN 128, the widest power-of-two split with one CTA per
+// SM at most and every cluster resident at once. Returns -1 (nothing launched) where it does not
+// apply.
+extern "C" int e2c_gemm_splitk_co(const e2c_gemm_args *a, void *stream) {
+    if (a->ablk != a->K || (a->epi != E2C_EPI_F32 && a->epi != E2C_EPI_RESID) || a->M < 1 || a->M > CO_ROWS) return -1;
+    const int dev = e2c_device();
+    const int num_sms = e2c_sm_count(dev);
+    const int nk = (a->K + BK - 1) / BK;
+    const long tiles = (a->n1 - a->n0 + 127) / 128;
+    int best = 0;
+    for (int s2 = 2; s2 <= 16 && s2 <= nk && tiles * s2 <= num_sms; s2 *= 2)
+        if (clusters<128, true>(s2) >= tiles) best = s2;
+    if (!best) return -1;
+    return launch_bn<128, true>(a, best, (cudaStream_t)stream);
 }

@@ -106,6 +106,9 @@ int e2c_gemm(const e2c_gemm_args *a, void *stream);
  * picks it for short activation matrices (few output tiles). Per-row scales, F32 or residual
  * epilogue only. */
 int e2c_gemm_splitk(const e2c_gemm_args *a, int bn, int S, void *stream);
+/* Its co-resident variant for 1..32 rows (BN 128, at most one CTA per SM, the weight's first stages
+ * requested before griddepcontrol.wait); -1 without launching where it does not apply */
+int e2c_gemm_splitk_co(const e2c_gemm_args *a, void *stream);
 /* The weight-streaming GEMM for 1..256 rows (gemm_i8_stream.cu): the weight in the MMA's 128-row
  * slot, stream-K over every SM, split weight tiles reduced through the workspace a->ws. Per-row
  * scales, F32 or residual epilogue. e2c_gemm picks it when a workspace is given and the activation
@@ -117,8 +120,9 @@ int e2c_gemm_stream_ctas(const e2c_gemm_args *a, int num_sms);
 /* bytes of workspace e2c_gemm's weight-streaming path needs for M rows on the current device (0
  * without a device, or for M outside 1..256) */
 size_t e2c_gemm_ws_bytes(int M);
-/* the kernel family e2c_gemm last launched on this thread: "stream", "splitk", "persistent" or
- * "persistent_pair" (the fused epilogues: "persistent") */
+/* the kernel family e2c_gemm last launched on this thread: "stream", "splitk", "persistent",
+ * "persistent_pair" (the fused epilogues: "persistent"), or under programmatic dependent launch
+ * "stream_coresident" / "splitk_coresident" */
 const char *e2c_gemm_last_kernel(void);
 /* E2C_EPI_NORMADD (gemm_i8_norm.cu): rows of 128 x (1..8) columns over a cluster of CTAs, the
  * residual norms in the epilogue; called by e2c_gemm after its checks */
