@@ -1241,10 +1241,11 @@ extern "C" int e2c_gemm(const e2c_gemm_args *a, void *stream) {
             g_last_kernel = "stream";
             return e2c_gemm_stream(a, stream);
         }
-        // Under programmatic dependent launch the short weights at a few tokens stream too, two
-        // CTAs per SM: the next launch's weight tiles are requested while this one finishes,
-        // which hides the fixed costs a chain of short launches pays one after another.
-        if (e2c_pdl_on() && a->M <= 32) {
+        // Short weights at a few tokens run co-resident (two CTAs per SM) under programmatic
+        // dependent launch, on by default for these launches (E2C_PDL_SMALL=0: off): the next
+        // launch's weight tiles are requested while this one finishes, which hides the fixed costs
+        // a chain of short launches pays one after another.
+        if (e2c_pdl_small_on() && a->M <= 32) {
             // Up to K = 4096 the co-resident split-K kernel, whose partials are reduced in a
             // cluster's shared memory rather than through the workspace, measured faster in a chain
             // (2048 x 8192 at M = 1: 6.45 against 6.84 us); deeper K balances better streamed

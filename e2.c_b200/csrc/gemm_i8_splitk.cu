@@ -337,7 +337,7 @@ int launch_bn(const e2c_gemm_args *a, int S, cudaStream_t st) {
     cfg.dynamicSmemBytes = smem_alloc(CO);
     cfg.stream = st;
     cfg.attrs = attr_c;
-    cfg.numAttrs = e2c_pdl_attr(attr_c, 1);
+    cfg.numAttrs = e2c_pdl_attr(attr_c, 1, CO);
     const cudaError_t e = cudaLaunchKernelEx(&cfg, k_gemm_splitk<BN, CO>, ta, tb, *a, a_rows);
     if (e != cudaSuccess) {
         e2c_set_msg("gemm_splitk launch: %s", cudaGetErrorString(e));

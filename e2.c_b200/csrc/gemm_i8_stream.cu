@@ -336,7 +336,7 @@ int launch_mt(const e2c_gemm_args *a, int G, cudaStream_t st, int dev) {
         e2c_tmap_2d(&tx, a->a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)a->K, (uint64_t)a->M, (uint64_t)a->lda, BK,
                     (uint32_t)MT))
         return -3;
-    const cudaError_t e = e2c_launch(k_gemm_stream<MT, CO>, dim3((unsigned)G), dim3(NTHREADS), L::ALLOC, st, tw, tx, *a);
+    const cudaError_t e = e2c_launch_as(CO != 0, k_gemm_stream<MT, CO>, dim3((unsigned)G), dim3(NTHREADS), L::ALLOC, st, tw, tx, *a);
     if (e != cudaSuccess) {
         e2c_set_msg("gemm_stream launch: %s", cudaGetErrorString(e));
         return -2;
@@ -376,7 +376,7 @@ extern "C" int e2c_gemm_stream(const e2c_gemm_args *a, void *stream) {
     cudaStream_t st = (cudaStream_t)stream;
     // under programmatic dependent launch, short weights at a few tokens take the co-resident ring
     const long long T = (long long)((a->n1 - a->n0 + BW - 1) / BW) * ((a->K + BK - 1) / BK);
-    if (e2c_pdl_on() && a->M <= 32 && T < 8LL * num_sms)
+    if (e2c_pdl_small_on() && a->M <= 32 && T < 8LL * num_sms)
         return a->M <= 16 ? launch_mt<16, 1>(a, G, st, dev) : launch_mt<32, 1>(a, G, st, dev);
     if (a->M <= 16) return launch_mt<16>(a, G, st, dev);
     if (a->M <= 32) return launch_mt<32>(a, G, st, dev);
