@@ -348,10 +348,13 @@ def main() -> int:
     e2e = n * BATCH * args.steps / (e2e_ms / 1e3)
 
     # every kernel of a layer in isolation; the roofline object is the dominant one's
-    roof, table = None, None
+    roof, table, small_m = None, None, None
     if rank == 0:
         table = kernel_table(dev, stream) if not args.ablk else None
         roof = dominant_roofline(table) if table else None
+        if world == 1 and not args.ablk:
+            # the small-activation GEMMs (benchmark config 3 at M = 1 and 16), timed after the pass
+            small_m = small_m_table(dev, stream)
     cpu = None
     if world > 1:
         # timed on rank 0 at N = 1 only: with N > 1 the other ranks' NCCL progress threads poll on the
@@ -375,6 +378,7 @@ def main() -> int:
                 "gpu_launches": int(kernels * passes * args.steps), "roofline": roof,
                 "kernels": {k: {kk: v[kk] for kk in ("bound", "achieved", "unit", "frac", "avg_ms", "traffic")}
                             for k, v in (table or {}).items()},
+                "small_m": small_m,
                 "cpu_baseline": cpu}
         print(json.dumps(line))
     enc.close()
@@ -1177,31 +1181,7 @@ def gemm_sweep(args) -> int:
                 if wsb:
                     a.ws, a.ws_bytes = wsp.data_ptr(), wsb
                 argl.append(a)
-            ms = timed_launches(lambda: e2c.gemm_raw(argl[0], stream), stream, args.warmup, args.steps)
-            kernel = lib.e2c_gemm_last_kernel().decode()
-            e2c.check(stream)
-            # the chain is captured as one CUDA graph, so host launch overhead never paces it
-            reps = max(2, min(64, (4 * args.steps) // len(argl)))
-            with torch.cuda.stream(stream):
-                for a in argl:
-                    e2c.gemm_raw(a, stream)
-            torch.cuda.synchronize()
-            graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(graph, stream=stream):
-                for _ in range(reps):
-                    for a in argl:
-                        e2c.gemm_raw(a, stream)
-            with torch.cuda.stream(stream):
-                graph.replay()
-                torch.cuda._sleep(100_000)
-                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                e0.record(stream)
-                graph.replay()
-                e1.record(stream)
-            torch.cuda.synchronize()
-            e2c.check(stream)
-            ms_chain = e0.elapsed_time(e1) / (reps * len(argl))
-            del graph
+            ms, ms_chain, kernel = _gemm_point(e2c, lib, argl, stream, args.warmup, args.steps)
             ops = 2.0 * M * N * K
             nbytes = M * K + 4 * M + N * K + 4 * N + 4 * M * N
             t_tc, t_hbm = ops / int8_peak, nbytes / hbm
@@ -1225,13 +1205,95 @@ def gemm_sweep(args) -> int:
                        "what": "e2ref_linear: e2_quantize_blocks_avx512 + e2_i8_gemm_avx512 over the reference pool"}
             print(json.dumps({"sweep": "config 3", "M": M, "K": K, "N": N, "kernel": kernel,
                               "bound": "tensor" if t_tc > t_hbm else "hbm", "isolated": fr(ms), "chain": fr(ms_chain),
-                              "chain_weights": len(argl), "pdl": os.environ.get("E2C_PDL") == "1",
+                              "chain_weights": len(argl), "pdl": os.environ.get("E2C_PDL") == "1" or kernel.endswith("_coresident"),
                               "peak_src": p["src"], "cpu_reference": cpu}), flush=True)
             del qa, qs, y, wsp, argl
         for W in Ws:
             W.free()
         del wref
     return 0
+
+
+def _gemm_point(e2c, lib, argl, stream, warmup: int, steps: int):
+    """(isolated ms, chain ms, kernel family) of one GEMM: the first launch alone after an L2 flush,
+    and the per-launch average of back-to-back launches over every argument block in argl (one per
+    weight copy) captured as one CUDA graph, so host launch overhead never paces the chain."""
+    import torch
+
+    ms = timed_launches(lambda: e2c.gemm_raw(argl[0], stream), stream, warmup, steps)
+    kernel = lib.e2c_gemm_last_kernel().decode()
+    e2c.check(stream)
+    reps = max(2, min(64, (4 * steps) // len(argl)))
+    with torch.cuda.stream(stream):
+        for a in argl:
+            e2c.gemm_raw(a, stream)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for _ in range(reps):
+            for a in argl:
+                e2c.gemm_raw(a, stream)
+    with torch.cuda.stream(stream):
+        graph.replay()
+        torch.cuda._sleep(100_000)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        graph.replay()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    e2c.check(stream)
+    ms_chain = e0.elapsed_time(e1) / (reps * len(argl))
+    del graph
+    return ms, ms_chain, kernel
+
+
+def small_m_table(dev, stream, warmup: int = 3, steps: int = 20) -> dict:
+    """north_star's small-activation GEMMs in the default run: benchmark config 3's three short
+    weights at M = 1 and 16 tokens, per-token scales, fp32 output; per point the kernel family, the
+    isolated and chained launch times and the fraction of the HBM roofline (the weight, read once,
+    is the bound)."""
+    import ctypes as C
+
+    import torch
+
+    e2c = load_pkg()
+    import e2c_b200.synthetic as syn
+
+    lib = e2c.lib()
+    lib.e2c_gemm_last_kernel.restype = C.c_char_p
+    lib.e2c_gemm_ws_bytes.argtypes = [C.c_int]
+    lib.e2c_gemm_ws_bytes.restype = C.c_size_t
+    lib.e2cu_status.restype = C.c_void_p
+    hbm = peaks()["hbm_gbs"] * 1e9
+    out = {}
+    for K, N in ((2048, 8192), (8192, 2048), (2048, 2048)):
+        rng = np.random.default_rng(0xE2C0DE + 3 + K + N)
+        wq, wsc = syn.quantize_weight_rows((rng.standard_normal((N, K), dtype=np.float32) * np.float32(0.02)))
+        copies = max(1, min(64, -(-(2 * 128 << 20) // (N * K))))
+        Ws = [e2c.Weight(w=wq, scale=wsc) for _ in range(copies)]
+        for M in (1, 16):
+            x = syn.activations(np.random.default_rng(M + K + N), M, K)
+            qa, qs = e2c.quantize_rows(torch.from_numpy(x).to(dev), K)
+            y = torch.empty((M, N), dtype=torch.float32, device=dev)
+            wsb = lib.e2c_gemm_ws_bytes(M)
+            wsp = torch.zeros(max(wsb // 4, 1) + 32, dtype=torch.int32, device=dev)
+            argl = []
+            for W in Ws:
+                a = e2c.gemm_args(W, qa, qs, M)
+                a.epi, a.y, a.ldy = e2c.EPI_F32, y.data_ptr(), N
+                a.status = lib.e2cu_status()
+                if wsb:
+                    a.ws, a.ws_bytes = wsp.data_ptr(), wsb
+                argl.append(a)
+            ms, ms_chain, kernel = _gemm_point(e2c, lib, argl, stream, warmup, steps)
+            nbytes = M * K + 4 * M + N * K + 4 * N + 4 * M * N
+            out[f"{K}x{N}_M{M}"] = {"kernel": kernel, "isolated_us": round(ms * 1e3, 2), "chain_us": round(ms_chain * 1e3, 2),
+                                    "chain_frac_hbm": round(nbytes / hbm / (ms_chain / 1e3), 3),
+                                    "isolated_frac_hbm": round(nbytes / hbm / (ms / 1e3), 3)}
+            del qa, qs, y, wsp, argl
+        for W in Ws:
+            W.free()
+    return out
 
 
 if __name__ == "__main__":
