@@ -857,14 +857,15 @@ def text_tower(args) -> int:
 # one KV head of 256), the per-launch algorithmic work each is measured against, and the launches of
 # each per layer. Weights are quantised N(0, 0.02), activations per-token quantised N(0, 1).
 KERNELS = ("gate_up", "gate_up_q", "qkv", "o_proj", "down", "o_proj_norm", "down_norm", "attention", "quantize",
-           "quantize_ctx", "norm_add", "o_proj_pb", "down_pb", "gate_up_pb", "gate_up_q_pb", "attention_vision",
+           "quantize_ctx", "norm_add", "o_proj_pb", "down_pb", "gate_up_pb", "gate_up_q_pb", "qkv_pb", "attention_vision",
            "gemm_small")
 # gemm_small: the config-3 GEMM (K, N) = (2048, 8192) at M = --tokens rows (1..256) on the
 # weight-streaming kernel itself (e2c_gemm_stream), per-token scales, fp32 output
 # attention_vision: the vision tower's attention (e2.c src/vision.c:540-571), 2520 patches per image,
 # 12 heads of 64 with their own K and V, scale 1; M tokens = M // 2520 images
 # *_pb: the same GEMMs with per-128-block activation scales (the reference engine's own recipe);
-# gate_up_pb writes g|u in fp32, gate_up_q_pb applies GELU-gate and h's per-block quantiser
+# gate_up_pb writes g|u in fp32, gate_up_q_pb applies GELU-gate and h's per-block quantiser, qkv_pb
+# finishes the heads (RMSNorm, RoPE from position-major tables, bf16 Q, K, V^T)
 # the kernels an encoder layer runs (hidden 768, FFN 1152, per-token scales): the residual norms fused
 # into o_proj and down and h's quantiser into gate|up, or with E2C_FUSED_NORM=0 / E2C_FUSED_GELU=0
 # the row kernels after them
@@ -876,7 +877,7 @@ if os.environ.get("E2C_FUSED_GELU") == "0":
 
 
 GEMM_KERNELS = ("gate_up", "gate_up_q", "qkv", "o_proj", "down", "o_proj_norm", "down_norm", "o_proj_pb", "down_pb",
-                "gate_up_pb", "gate_up_q_pb")
+                "gate_up_pb", "gate_up_q_pb", "qkv_pb")
 
 
 def kernel_work(name: str, M: int) -> dict:
@@ -884,13 +885,13 @@ def kernel_work(name: str, M: int) -> dict:
     if name in GEMM_KERNELS:
         N, K = {"gate_up": (2 * I, D), "gate_up_q": (2 * I, D), "qkv": ((H + 2) * Dh, D), "o_proj": (D, D),
                 "down": (D, I), "o_proj_norm": (D, D), "down_norm": (D, I), "o_proj_pb": (D, D), "down_pb": (D, I),
-                "gate_up_pb": (2 * I, D), "gate_up_q_pb": (2 * I, D)}[name]
+                "gate_up_pb": (2 * I, D), "gate_up_q_pb": (2 * I, D), "qkv_pb": ((H + 2) * Dh, D)}[name]
         # the fused norm epilogue reads and writes the fp32 residual and writes int8 rows + scales;
         # the fused GELU-quantise epilogue writes int8 h + scales
         out_bytes = {"gate_up": 4 * M * I, "gate_up_q": M * I + 4 * M, "qkv": 2 * M * N, "o_proj": 4 * M * D,
                      "down": 4 * M * D, "o_proj_norm": 8 * M * D + M * D + 4 * M,
                      "down_norm": 8 * M * D + M * D + 4 * M, "o_proj_pb": 4 * M * D, "down_pb": 4 * M * D,
-                     "gate_up_pb": 8 * M * I, "gate_up_q_pb": M * I + 4 * M * (I // 128)}[name]
+                     "gate_up_pb": 8 * M * I, "gate_up_q_pb": M * I + 4 * M * (I // 128), "qkv_pb": 2 * M * N}[name]
         a_scales = 4 * M * (K // 128) if name.endswith("_pb") else 4 * M
         return {"ops": 2.0 * M * N * K, "bytes": M * K + a_scales + N * K + 4 * N + out_bytes, "per_layer": 1}
     if name == "attention":
@@ -929,7 +930,7 @@ def kernel_runner(name: str, M: int, dev, stream):
     if name in GEMM_KERNELS:
         N, K = {"gate_up": (2 * I, D), "gate_up_q": (2 * I, D), "qkv": ((H + 2) * Dh, D), "o_proj": (D, D),
                 "down": (D, I), "o_proj_norm": (D, D), "down_norm": (D, I), "o_proj_pb": (D, D), "down_pb": (D, I),
-                "gate_up_pb": (2 * I, D), "gate_up_q_pb": (2 * I, D)}[name]
+                "gate_up_pb": (2 * I, D), "gate_up_q_pb": (2 * I, D), "qkv_pb": ((H + 2) * Dh, D)}[name]
         wq, ws = syn.quantize_weight_rows((rng.standard_normal((N, K)) * 0.02).astype(np.float32))
         W = e2c.Weight(w=wq, scale=ws)
         pb = name.endswith("_pb")
@@ -969,12 +970,15 @@ def kernel_runner(name: str, M: int, dev, stream):
             Kt = torch.empty((M, Dh), dtype=torch.bfloat16, device=dev)
             Vt = torch.empty((M // SEQ, Dh, SEQ), dtype=torch.bfloat16, device=dev)
             gam = torch.ones(Dh, device=dev)
-            cs = torch.rand((Dh // 2, SEQ), device=dev)  # pair-major RoPE table
+            # RoPE tables: pair-major [Dh/2][SEQ] for the per-token epilogue, position-major
+            # [SEQ][Dh/2] for the per-block one (the same size)
+            cs = torch.rand((Dh // 2, SEQ), device=dev)
             keep += [Q, Kt, Vt, gam, cs]
-            a.epi, a.nq, a.q_out, a.k_out, a.vt_out, a.ldvt, a.seq_len = e2c.EPI_QKV, H, Q.data_ptr(), Kt.data_ptr(), Vt.data_ptr(), SEQ, SEQ
+            a.epi = e2c.EPI_QKVPB if pb else e2c.EPI_QKV
+            a.nq, a.q_out, a.k_out, a.vt_out, a.ldvt, a.seq_len = H, Q.data_ptr(), Kt.data_ptr(), Vt.data_ptr(), SEQ, SEQ
             a.q_gamma = a.k_gamma = gam.data_ptr()
             a.rope_cos = a.rope_sin = cs.data_ptr()
-            a.ldrope = SEQ
+            a.ldrope = Dh // 2 if pb else SEQ
             a.eps = 1e-6
         return (lambda: e2c.gemm_raw(a, stream)), keep
     if name == "attention":
