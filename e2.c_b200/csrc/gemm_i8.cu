@@ -790,6 +790,19 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     float *xs = reinterpret_cast<float *>(smem + L::SSQ_OFF) + (jt & 1) * 4 * BM;
                     xs[part * BM + row] = ssh;
                     mbar_arrive(pair_bar(0, q));
+                    const int bseq = mrow ? m / p.seq_len : 0, pos = mrow ? m - bseq * p.seq_len : 0;
+                    // q, k: the RoPE coefficients of the first step's 8 pairs, requested before the
+                    // row-norm exchange (each later step's one step ahead)
+                    const float *rc = p.rope_cos + (size_t)pos * p.ldrope, *rs = p.rope_sin + (size_t)pos * p.ldrope;
+                    float4 cnx[2] = {make_float4(1.f, 1.f, 1.f, 1.f), make_float4(1.f, 1.f, 1.f, 1.f)};
+                    float4 snx[2] = {make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f)};
+                    if (kind < 2) {
+#pragma unroll
+                        for (int h4 = 0; h4 < 2; h4++) {
+                            cnx[h4] = __ldg(reinterpret_cast<const float4 *>(rc + 32 * part + 4 * h4));
+                            snx[h4] = __ldg(reinterpret_cast<const float4 *>(rs + 32 * part + 4 * h4));
+                        }
+                    }
                     if (!__all_sync(0xffffffffu, mbar_wait(pair_bar(0, q), (uint32_t)(jt & 1), p.status, E2C_ERR_WAIT_EPI))) {
                         ok = false;
                         break;
@@ -797,26 +810,32 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     const float ss = __fadd_rn(__fadd_rn(xs[row], xs[BM + row]), __fadd_rn(xs[2 * BM + row], xs[3 * BM + row]));
                     const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, 256.0f), p.eps)));
                     tmem_wait_st();
-                    const int bseq = mrow ? m / p.seq_len : 0, pos = mrow ? m - bseq * p.seq_len : 0;
                     if (kind < 2) {
                         // q, k: 8 pairs a step from TMEM, RoPE on 4 at a time; 16-byte bf16 runs of
                         // each half
                         __nv_bfloat16 *dst = kind == 0
                             ? reinterpret_cast<__nv_bfloat16 *>(p.q_out) + (size_t)m * (256 * p.nq) + head * 256
                             : reinterpret_cast<__nv_bfloat16 *>(p.k_out) + (size_t)m * (256 * nkv) + (head - p.nq) * 256;
-                        const float *rc = p.rope_cos + (size_t)pos * p.ldrope, *rs = p.rope_sin + (size_t)pos * p.ldrope;
 #pragma unroll 1
                         for (int c = 0; c < 4; c++) {
                             uint32_t r0[8], r1[8];
                             tmem_ld8(park + 8 * c, r0);
                             tmem_ld8(park + 32 + 8 * c, r1);
-                            tmem_wait_ld();
                             const int i0 = 32 * part + 8 * c;  // rotate-half index of the first pair
+                            const float4 cur_c[2] = {cnx[0], cnx[1]}, cur_s[2] = {snx[0], snx[1]};
+                            if (c < 3) {
+#pragma unroll
+                                for (int h4 = 0; h4 < 2; h4++) {
+                                    cnx[h4] = __ldg(reinterpret_cast<const float4 *>(rc + i0 + 8 + 4 * h4));
+                                    snx[h4] = __ldg(reinterpret_cast<const float4 *>(rs + i0 + 8 + 4 * h4));
+                                }
+                            }
+                            tmem_wait_ld();
                             uint32_t px[4], pz[4];
 #pragma unroll
                             for (int h4 = 0; h4 < 2; h4++) {
-                                const float4 c4 = __ldg(reinterpret_cast<const float4 *>(rc + i0 + 4 * h4));
-                                const float4 s4 = __ldg(reinterpret_cast<const float4 *>(rs + i0 + 4 * h4));
+                                const float4 c4 = cur_c[h4];
+                                const float4 s4 = cur_s[h4];
                                 const float cs[4] = {c4.x, c4.y, c4.z, c4.w}, sn[4] = {s4.x, s4.y, s4.z, s4.w};
                                 float xo[4], zo[4];
 #pragma unroll
