@@ -134,7 +134,10 @@ typedef struct e2cuda_epilogue {
  * 128 dividing K. For short activation matrices (M <= 256) against long weights the call may use a
  * weight-streaming kernel that keeps a small zeroed device workspace per (device, stream): it is
  * allocated by the first such call on a stream that is not being captured (make one before
- * capturing a graph on that stream) and held until the process exits. */
+ * capturing a graph on that stream) and held until the process exits. With M <= 32 and a short
+ * weight the call launches with programmatic dependent launch (E2C_PDL_SMALL=0: off) and requests
+ * the weight's first tiles before waiting for the stream's previous kernel: a weight must not be
+ * written by a kernel on the stream that signals its dependents early. */
 int e2cuda_i8_gemm(const e2cuda_w8 *w, const int8_t *qa, const float *a_scales, int M, int ablk,
                    int n0, int n1, const e2cuda_epilogue *ep, float *y, int ldy, void *stream);
 
