@@ -254,7 +254,13 @@ def main() -> int:
 
     import torch
 
-    dist, rank, world, local = dist_setup(args.gpus)
+    if args.impl == "reference":
+        # the reference arm's ranks never communicate (rank 0 times the CPU path, the others exit),
+        # so it joins no process group
+        dist, rank, world = None, int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1"))
+        local = int(os.environ.get("LOCAL_RANK", "0"))
+    else:
+        dist, rank, world, local = dist_setup(args.gpus)
     n = world
     load_pkg()
     import e2c_b200.synthetic as syn
