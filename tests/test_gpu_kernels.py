@@ -915,3 +915,59 @@ def test_gelu_quant_epilogue_per_block(e2c, of, torch_cuda, M, K, I):
     assert np.array_equal(qn[:, :I], want_q.cpu().numpy()), "bytes differ from the two-kernel path"
     assert np.all(qn[:, I:] == 99), "wrote past the row"
     assert f32_bits_equal(s.cpu().numpy(), want_s.cpu().numpy())
+
+
+def test_fused_per_block_epilogues_reject_bad_arguments(e2c, torch_cuda):
+    """The per-block fused epilogues refuse, before anything is launched, what they cannot compute:
+    activation blocks other than 128 (the output quantiser's block is the CTA's 128 columns), gate|up
+    rows not in groups of 256 from row 0, int8 rows not 16-byte aligned, q|k|v columns that are not
+    nq q heads then equal k and v heads of 256, M not a multiple of seq_len, and norm forms without
+    their outputs. Each returns -1 with a message naming the epilogue."""
+    torch = torch_cuda
+    lib = e2c.lib()
+    lib.e2c_msg.restype = C.c_char_p
+    rng = np.random.default_rng(3)
+    M, K = 256, 512
+
+    def args(N, ablk):
+        W = e2c.Weight(w=rng.integers(-127, 128, size=(N, K), dtype=np.int8),
+                       scale=rng.uniform(1e-4, 0.02, size=N).astype(np.float32))
+        qa = torch.zeros((M, K), dtype=torch.int8, device="cuda")
+        qs = torch.ones((M, K // ablk), dtype=torch.float32, device="cuda")
+        a = e2c.gemm_args(W, qa, qs, M)
+        a.ablk = ablk
+        return a, [W, qa, qs]
+
+    def rejected(a, what):
+        rc = lib.e2c_gemm(C.byref(a), torch.cuda.current_stream().cuda_stream)
+        msg = lib.e2c_msg().decode()
+        assert rc == -1 and what in msg, (rc, msg)
+
+    q8 = torch.zeros((M, 1040), dtype=torch.int8, device="cuda")
+    q8s = torch.zeros((M, 8), dtype=torch.float32, device="cuda")
+    # GELU-quantise, per block: a 256-wide activation block; an odd int8 row stride
+    a, keep = args(512, 256)
+    a.epi, a.q8, a.ldq, a.q8_scale = e2c.EPI_GELUQ, q8.data_ptr(), 256, q8s.data_ptr()
+    rejected(a, "GELU-quantise")
+    a, keep = args(512, 128)
+    a.epi, a.q8, a.ldq, a.q8_scale = e2c.EPI_GELUQ, q8.data_ptr(), 264, q8s.data_ptr()
+    rejected(a, "GELU-quantise")
+    # q|k|v, per block: per-token scales; 3 q heads with unequal k and v heads; M not a multiple of S
+    out = torch.zeros((M, 2048), dtype=torch.bfloat16, device="cuda")
+    tab = torch.zeros((512, 128), dtype=torch.float32, device="cuda")
+    for N, ablk, S in ((5 * 256, K, 128), (6 * 256, 128, 128), (5 * 256, 128, 100)):
+        a, keep = args(N, ablk)
+        a.epi, a.nq, a.seq_len, a.ldvt, a.ldrope = e2c.EPI_QKVPB, 3, S, 256, 128
+        a.q_out = a.k_out = a.vt_out = out.data_ptr()
+        a.rope_cos = a.rope_sin = tab.data_ptr()
+        rejected(a, "q|k|v")
+    # residual norms, per block: a 256-wide activation block; neither int8 rows nor a final gain
+    res = torch.zeros((M, 512), dtype=torch.float32, device="cuda")
+    g = torch.ones(512, device="cuda")
+    for ablk, with_q8 in ((256, True), (128, False)):
+        a, keep = args(512, ablk)
+        a.epi, a.res, a.ldres, a.norm_g1, a.eps = e2c.EPI_NORMADD, res.data_ptr(), 512, g.data_ptr(), 1e-6
+        if with_q8:
+            a.q8, a.ldq, a.q8_scale = q8.data_ptr(), 512, q8s.data_ptr()
+        rejected(a, "norm epilogue")
+    e2c.check()
